@@ -1,0 +1,251 @@
+/*
+ * kvr_b200.h — C ABI of the B200-native compressed-KV hot path.
+ *
+ * Plain pointers and sizes only: every pointer named "device" is a CUDA
+ * device pointer on the current device, every call is asynchronous on the
+ * given stream (NULL = legacy default stream) and returns KVR_OK or a KVR_E*
+ * code; kvr_last_error() then holds a one-line message for the calling host
+ * thread.  No entry point allocates device memory: callers own all buffers,
+ * including the workspaces whose sizes the *_workspace_bytes() helpers report.
+ * Workspaces must be zero-filled once before their first use; every
+ * successful call leaves them zero-filled again (their counters self-reset).
+ * A call that returned KVR_ETIMEOUT may leave them dirty: zero them again.
+ *
+ * Reference interfaces replaced (paths inside Misaka477/RINA-1bit-KV):
+ *   modules/kvr_cuda.cu:53-77 / kvr_cuda.py:20-26     -> kvr_compute_scores
+ *   modules/kvr_retrieval.py:95-122  (calibrate)       -> kvr_absmax_scales
+ *   modules/kvr_retrieval.py:162-207 (append/batch)    -> kvr_int4w_encode_k, kvr_int4w_encode_vres
+ *   modules/kvr_retrieval.py:265-289 (all scores)      -> kvr_int4w_token_scores
+ *   modules/kvr_retrieval.py:291-315 (chunk scores)    -> kvr_int4w_chunk_scores
+ *   modules/kvr_retrieval.py:370-392 (top-k)           -> kvr_topk_rows
+ *   modules/kvr_retrieval.py:394-412 (gather, V recon) -> kvr_int4w_gather, kvr_int4w_vres_add
+ *   modules/kvr_window.py:19-41      (ring append)     -> kvr_window_write
+ *   modules/kvr_window.py:43-69, kvr_hook.py:274-282,
+ *   modules/kvr_triton.py:42-104     (attention)       -> kvr_decode_attn
+ *   (no reference counterpart: the 1-bit sd1 codec)    -> kvr_sd1_*, kvr_transform, kvr_lse_merge
+ */
+#ifndef KVR_B200_H
+#define KVR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVR_API __attribute__((visibility("default")))
+#else
+#define KVR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *kvr_stream_t; /* same type as cudaStream_t */
+
+enum kvr_status {
+  KVR_OK = 0,
+  KVR_EINVAL = 1,   /* bad argument (shape, dtype, alignment, null pointer) */
+  KVR_ECUDA = 2,    /* a CUDA runtime call or kernel launch failed */
+  KVR_ENOTSUP = 3,  /* valid but unsupported configuration (e.g. head_dim != 128) */
+  KVR_ETIMEOUT = 4  /* a bounded device-side wait gave up (see kvr_sd1_* notes) */
+};
+
+enum kvr_dtype { KVR_F32 = 0, KVR_F16 = 1, KVR_BF16 = 2 };
+enum kvr_transform_kind { KVR_HADAMARD = 0, KVR_DCT = 1 };
+
+/* One-line description of the last failure on this host thread ("" if none). */
+KVR_API const char *kvr_last_error(void);
+/* ABI version: (major << 16) | minor. */
+KVR_API int kvr_abi_version(void);
+
+/* ---------------------------------------------------------------- int4w ----
+ * The reference-faithful codec: int4 K_pre codes with a per-(head, channel)
+ * absmax scale, V predicted from K through W plus an int2 per-head residual.
+ * Layouts follow modules/kvr_retrieval.py: K (n, n_kv, d), packed K
+ * (n, n_kv, d/2) uint8, packed residual (n, n_kv, d/4) uint8.
+ */
+
+/* calibrate()'s k_scales = clamp(max_t |x[t, c]|, min=clamp_min) over n rows of
+ * `cols` columns (kvr_retrieval.py:99).  x is (n, cols) with row stride `cols`. */
+KVR_API int kvr_absmax_scales(const void *x, int dtype, int64_t n, int64_t cols, float clamp_min,
+                      float *out /* device (cols) */, kvr_stream_t stream);
+
+/* kq = clamp(rint(k / (2*s/16)), -8, 7), packed two per byte, even element in
+ * the high nibble (kvr_retrieval.py:69-72, 167-171, 190-193).  k is
+ * (n, n_kv, d) with token stride `tok_stride` elements. */
+KVR_API int kvr_int4w_encode_k(const void *k, int dtype, int64_t n, int n_kv, int d, int64_t tok_stride,
+                       const float *k_scales /* (n_kv, d) */, uint8_t *k_packed /* (n, n_kv, d/2) */,
+                       kvr_stream_t stream);
+
+/* vrq = clamp(rint((v - v_pred) / (2*vr/4)), -2, 1), packed four per byte,
+ * element 0 in bits 7-6 (kvr_retrieval.py:80-83, 173-180, 196-203).
+ * v (n, n_kv, d) of `dtype`; v_pred (n, n_kv, d) fp32 contiguous. */
+KVR_API int kvr_int4w_encode_vres(const void *v, int dtype, const float *v_pred, int64_t n, int n_kv, int d,
+                          const float *vr_scales /* (n_kv) */, uint8_t *vr_packed /* (n, n_kv, d/4) */,
+                          kvr_stream_t stream);
+
+/* Drop-in for the reference's native score kernel (kvr_cuda.cu:9-49, 53-77):
+ * interleaved-pair RoPE from (n_stored, d/2) cos/sin tables, dot with the
+ * pre-averaged q, divided by sqrt(d).  scores (n_stored, n_kv) fp32. */
+KVR_API int kvr_compute_scores(const float *q_avg /* (n_kv, d) */, const uint8_t *k_pack, const float *k_scales,
+                       const float *cos_tbl, const float *sin_tbl, int n_kv, int d, int64_t n_stored,
+                       float *scores, kvr_stream_t stream);
+
+/* compute_all_scores (kvr_retrieval.py:265-289): cosine between the GQA-group
+ * mean of the post-RoPE query q (n_q, d) fp32 and the rotate_half-RoPE'd
+ * dequantised K of every stored token (position = token index); NaN -> -inf.
+ * cos/sin are (max_pos, d) rows with row stride `rope_stride`; if
+ * `rope_halves_equal` is nonzero the kernel reads only the first d/2 columns
+ * (valid for HF tables, whose halves are duplicated).  Output is HEAD-MAJOR:
+ * scores[h * score_stride + t]. */
+KVR_API int kvr_int4w_token_scores(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                           const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                           int rope_halves_equal, int n_kv, int d, int64_t n_stored, float *scores,
+                           int64_t score_stride, kvr_stream_t stream);
+
+/* compute_chunk_scores (kvr_retrieval.py:291-315): cosine against the mean of
+ * each full chunk of `chunk` RoPE'd tokens (the partial tail is dropped).
+ * Output head-major scores[h * score_stride + c], c < n_stored / chunk. */
+KVR_API int kvr_int4w_chunk_scores(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                           const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                           int rope_halves_equal, int n_kv, int d, int64_t n_stored, int chunk,
+                           float *scores, int64_t score_stride, kvr_stream_t stream);
+
+/* Per-row top-k (kvr_retrieval.py:379, 391-392) over `rows` rows of `n`
+ * contiguous fp32 scores (row r at scores + r * row_stride).  Entries with
+ * index in [ex_start, ex_end) and NaN count as -inf, -0.0 equals +0.0.
+ * Order: score descending, then index ascending (deterministic in place of
+ * torch.topk's unspecified tie order).  k must be <= n and <= 4096.
+ * Writes idx[r * out_row_stride + j * out_elem_stride] (int64) and, if vals is
+ * not NULL, the scores at the same offsets. */
+KVR_API int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t row_stride, int k,
+                  int64_t ex_start, int64_t ex_end, int64_t *idx, float *vals,
+                  int64_t out_row_stride, int64_t out_elem_stride, kvr_stream_t stream);
+
+/* Gather for V reconstruction and K re-rotation (kvr_retrieval.py:394-412).
+ * top (k, n_kv) int64 token indices.  Writes
+ *   ret_k (k, n_kv, d) fp32 : RoPE(deq K[top[i,h], h]) at position top[i,h];
+ *   x     (n_kv, k, n_kv*d) fp32 : deq K_pre of ALL heads of token top[i,h]
+ *                                  minus K_mean (the V-predict GEMM input). */
+KVR_API int kvr_int4w_gather(const uint8_t *k_packed, const float *k_scales, const int64_t *top, int k, int n_kv,
+                     int d, const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                     const float *k_mean /* (n_kv*d) */, float *ret_k, float *x, kvr_stream_t stream);
+
+/* ret_v[i, h, :] = fp16(v_base[h, i, :] + unpack2(vr_packed[top[i,h], h]) * (2*vr[h]/4))
+ * with v_base (n_kv, k, d) fp32 (= x @ W_h^T + V_mean_h) (kvr_retrieval.py:399-402). */
+KVR_API int kvr_int4w_vres_add(const float *v_base, const uint8_t *vr_packed, const float *vr_scales,
+                       const int64_t *top, int k, int n_kv, int d, uint16_t *ret_v /* fp16 */,
+                       kvr_stream_t stream);
+
+/* --------------------------------------------------------------- window ----
+ * Ring write of post-RoPE K and V (kvr_window.py:19-41): token i of the n
+ * new ones goes to slot (pos + i) % cap, converted to fp16.  Only the last
+ * min(n, cap) tokens are written (earlier ones would be overwritten). */
+KVR_API int kvr_window_write(const void *k, const void *v, int dtype, int64_t n, int n_kv, int d,
+                     uint16_t *ring_k, uint16_t *ring_v, int64_t cap, int64_t pos, kvr_stream_t stream);
+
+/* ------------------------------------------------------------ attention ----
+ * Exact decode attention softmax(q k^T / scale) v per Q head (GQA kvh = hq / g)
+ * over the concatenation of two K/V segments (segment 1 may be empty), without
+ * materialising the concatenation (kvr_window.py:43-69, kvr_hook.py:274-282,
+ * kvr_triton.py:42-79).  Segment s is K/V of shape (n_s, n_kv, d) with token
+ * stride tok_stride_s elements and dtypes kdt_s / vdt_s.  scale <= 0 means
+ * sqrt(d).  Split over the tokens across CTAs, merged by log-sum-exp. */
+KVR_API size_t kvr_decode_attn_workspace_bytes(int n_q, int n_kv, int d, int64_t n_tok_total);
+KVR_API int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, int d,
+                    const void *k0, const void *v0, int kdt0, int vdt0, int64_t n0, int64_t tok_stride0,
+                    const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1, int64_t tok_stride1,
+                    float scale, void *out, int out_dtype, void *workspace, size_t workspace_bytes,
+                    kvr_stream_t stream);
+
+/* ------------------------------------------------------------------ sd1 ----
+ * 1-bit codec (no reference counterpart).  head_dim d = 128, tile t in
+ * {32, 64, 128}.  Store of one layer, per (batch b, kv head h, tile i):
+ *   kbits[((b*n_kv + h)*nt_cap + i)*t*4 + j*4 + w]  uint32 (token j, channels 32w..32w+31)
+ *   kscale[((b*n_kv + h)*nt_cap + i)*d + c]          fp16
+ * and vbits / vscale alike.  Inputs K, V are (B, n, n_kv, d)-like with
+ * explicit element strides for batch and token (head stride = d).
+ */
+
+/* Orthonormal transform of `rows` vectors of d = 128 fp32 (y may alias x). */
+KVR_API int kvr_transform(const float *x, float *y, int64_t rows, int kind, int inverse, kvr_stream_t stream);
+
+/* Encode n_tiles full tiles per (b, h) starting at store tile `tile0`.
+ * If cos_tbl != NULL, K is pre-RoPE and is rotated (rotate_half, HF (max_pos, d)
+ * rows of stride rope_stride) at positions pos0 + token index. */
+KVR_API int kvr_sd1_encode(const void *k, const void *v, int dtype, int batch, int n_kv, int64_t n_tiles,
+                   int tile, int64_t batch_stride, int64_t tok_stride, const float *cos_tbl,
+                   const float *sin_tbl, int64_t rope_stride, int64_t pos0, int kind, uint32_t *kbits,
+                   uint16_t *kscale, uint32_t *vbits, uint16_t *vscale, int64_t nt_cap, int64_t tile0,
+                   kvr_stream_t stream);
+
+/* Tile selection scores (B, n_kv, n_tiles) fp32 for q (B, n_q, d) of q_dtype. */
+KVR_API int kvr_sd1_tile_scores(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
+                        float *scores, kvr_stream_t stream);
+
+/* Decode selected tiles to post-RoPE K (fp32) and V (fp16) vectors:
+ * sel (B, n_kv, k) int64 tile indices (entries < 0 are skipped, rows left 0);
+ * out_k / out_v (B, k*t, n_kv, d). */
+KVR_API int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
+                         const uint16_t *vscale, int64_t nt_cap, int batch, int n_kv, int tile, int kind,
+                         const int64_t *sel, int k, float *out_k, uint16_t *out_v, kvr_stream_t stream);
+
+/* Selection for one decode step of one layer: score every full tile
+ * (kvr_sd1_tile_scores) and keep the top k_sel tiles per (b, h) by (score
+ * desc, tile asc), tiles in [ex_t0, ex_t1) excluded.  Writes
+ *   sel        (B, n_kv, k_sel) int32 tile indices + tile_base (-1 past n_tiles),
+ *   sel_scores (B, n_kv, k_sel) fp32 (may be NULL),
+ *   qprime     (B, n_q, d) fp32: the transformed per-head query kvr_sd1_attend needs.
+ * One launch (the last CTA of each (b, h) selects). */
+KVR_API size_t kvr_sd1_select_workspace_bytes(int batch, int n_kv, int64_t n_tiles);
+KVR_API int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                   const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
+                   int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
+                   float *qprime, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
+/* Attention over window + pending tail + the selected tiles (sel entries are
+ * store tile indices; negative entries are skipped), exact log-sum-exp merge.
+ * Window: ring (B, win_cap, n_kv, d) fp16 with n_win valid slots; tail:
+ * (B, t, n_kv, d) fp16 with n_tail valid tokens.  q (B, n_q, d) of q_dtype,
+ * qprime from kvr_sd1_select.  Writes out (B, n_q, d) of out_dtype, or, if
+ * partial_out != NULL, the unnormalised partial rows (B, n_q, d + 2) =
+ * [m, l, o] for kvr_lse_merge instead.  Selected tiles are staged into shared
+ * memory by bulk asynchronous copies; their waits are bounded and report
+ * KVR_ETIMEOUT. */
+KVR_API size_t kvr_sd1_attend_workspace_bytes(int batch, int n_q, int n_kv, int tile, int k_sel, int64_t n_win,
+                                      int64_t n_tail);
+KVR_API int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int batch, int n_q, int n_kv,
+                   const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                   const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
+                   const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
+                   int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out, int out_dtype,
+                   float *partial_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
+/* kvr_sd1_select followed by kvr_sd1_attend on one stream (sel/qprime live in
+ * the workspace; sel_out may be NULL). */
+KVR_API size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,
+                               int64_t n_win, int64_t n_tail);
+KVR_API int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, int n_kv,
+                        const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                        const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail,
+                        const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
+                        const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
+                        int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
+                        int32_t *sel_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
+/* Partial-attention merge for a sequence split across P sources:
+ * partials (P, n_q, d + 2) fp32 rows = [m, l, o_0 .. o_{d-1}] with o
+ * unnormalised (sum_j e^{s_j - m} v_j); out (n_q, d) = sum_p e^{m_p-M} o_p / sum_p e^{m_p-M} l_p. */
+KVR_API int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,
+                  kvr_stream_t stream);
+
+/* Synchronises `stream`, then reads and clears the error word every workspace
+ * starts with: KVR_ETIMEOUT if a bounded device-side wait of an earlier call
+ * using this workspace gave up, else KVR_OK. */
+KVR_API int kvr_workspace_status(const void *workspace, kvr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVR_B200_H */

@@ -1,0 +1,700 @@
+// Decode attention over exact K/V segments and sd1 1-bit tiles (sm_100a).
+//
+// Work decomposition: for every (batch b, KV head h) the tokens are cut into
+// units — 64-token chunks of up to two exact segments (the fp16 window ring,
+// the pending tail, or the retrieved rows of the int4w path) and selected
+// sd1 tiles.  One CTA of 256 threads handles one unit for all g = n_q/n_kv
+// query heads of the group and writes a log-sum-exp partial (m, l, o); the
+// last CTA of each (b, h) to finish merges the partials (no grid-wide wait).
+// sd1 units work in the transformed domain: scores use q' = T q because T is
+// orthonormal, their partial o' is merged first and mapped back with one
+// inverse transform per query head.  Selected tiles are staged into shared
+// memory with bulk asynchronous copies completing on an mbarrier.
+//
+// Reference behaviour replaced: exact softmax over window + retrieved tokens
+// with GQA kvh = hq / g (modules/kvr_window.py:43-69, kvr_hook.py:274-282,
+// kvr_triton.py:42-79, kvr_generator.py:448-450).
+#include "kvr_common.cuh"
+#include "kvr_transform.cuh"
+
+namespace kvr {
+
+constexpr int kChunk = 64;
+constexpr int kMaxG = 8;
+constexpr int kKsStride = kD + 4;  // padded fp32 row of the staged K chunk
+
+struct AttnArgs {
+  const void *q;
+  int q_dt, n_q, n_kv, g;
+  float inv_scale;
+  const float *qprime;  // (B, n_q, d), sd1 units only
+  const void *k[2];
+  const void *v[2];
+  int kdt[2], vdt[2];
+  int64_t n[2], tok_stride[2], batch_stride[2];
+  int nchunk[2];
+  const uint32_t *kbits;
+  const uint16_t *kscale;
+  const uint32_t *vbits;
+  const uint16_t *vscale;
+  int64_t nt_cap;
+  int tile, kind, k_sel;
+  const int32_t *sel;  // (B, n_kv, k_sel)
+  void *out;
+  int out_dt;
+  float *partial_out;  // (B, n_q, d+2) or null
+  float *part;         // (B, n_kv, units, g, d+2)
+  unsigned *counters;  // (B, n_kv)
+  unsigned *err;
+  int units;
+};
+
+// ---- runtime-dtype loads
+__device__ __forceinline__ void load4_rt(const void *p, int64_t i, int dt, float (&x)[4]) {
+  if (dt == KVR_F32) load4<KVR_F32>(p, i, x);
+  else if (dt == KVR_F16) load4<KVR_F16>(p, i, x);
+  else load4<KVR_BF16>(p, i, x);
+}
+
+// ---- mbarrier + bulk copy (PTX)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait; returns false if it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    if (mbar_try_wait(bar, phase)) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+// ---- shared memory plan (bytes)
+struct AttnSmem {
+  static constexpr int kKs = 0;                                      // fp32 [64][132]
+  static constexpr int kVs = kKs + kChunk * kKsStride * 4;           // fp32 [64][128]
+  static constexpr int kExactEnd = kVs + kChunk * kD * 4;
+  // sd1 tile unit reuses the region: bits, scales, LUT
+  static constexpr int kKB = 0;                                      // u32 [128][4]
+  static constexpr int kVB = kKB + 128 * 16;                         // u32 [128][4]
+  static constexpr int kKS = kVB + 128 * 16;                         // fp16 [128]
+  static constexpr int kVS = kKS + kD * 2;                           // fp16 [128]
+  static constexpr int kLUT = kVS + kD * 2;                          // fp32 [g][32][16]
+  static constexpr int kTileEnd = kLUT + kMaxG * 32 * 16 * 4;
+  static constexpr int kUnion = kExactEnd > kTileEnd ? kExactEnd : kTileEnd;
+  static constexpr int kQ = kUnion;                                  // fp32 [8][128]
+  static constexpr int kS = kQ + kMaxG * kD * 4;                     // fp32 [8][128] scores / reduce
+  static constexpr int kP = kS + kMaxG * kD * 4;                     // fp32 [128][8] probabilities
+  static constexpr int kML = kP + 128 * kMaxG * 4;                   // fp32 [8][2]
+  static constexpr int kBar = kML + kMaxG * 2 * 4;                   // u64
+  static constexpr int kFlag = kBar + 16;
+  static constexpr int kTotal = kFlag + 16;
+};
+
+// Softmax over the scores S[hq][0..nt) of every query head; writes P[j][hq],
+// ML[hq] = (m, l).  Rows with no valid token get m = -inf, l = 0.
+__device__ __forceinline__ void softmax_rows(const AttnArgs &a, int nt, const float *S, float *P, float *ML) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int hq = warp; hq < a.g; hq += 8) {
+    float mx = -INFINITY;
+    for (int j = lane; j < nt; j += 32) mx = fmaxf(mx, S[hq * kD + j]);
+    mx = warp_max(mx);
+    float l = 0.0f;
+    for (int j = lane; j < 128; j += 32) {
+      float p = 0.0f;
+      if (j < nt && mx != -INFINITY) p = expf(S[hq * kD + j] - mx);
+      P[j * kMaxG + hq] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      ML[hq * 2] = mx;
+      ML[hq * 2 + 1] = l;
+    }
+  }
+}
+
+__device__ __forceinline__ float *part_row(const AttnArgs &a, int64_t row, int u, int hq) {
+  return a.part + (((row * a.units + u) * a.g) + hq) * (int64_t)(kD + 2);
+}
+
+__device__ void write_empty_partial(const AttnArgs &a, int64_t row, int u) {
+  for (int i = threadIdx.x; i < a.g * (kD + 2); i += blockDim.x) {
+    const int hq = i / (kD + 2), c = i - hq * (kD + 2);
+    part_row(a, row, u, hq)[c] = c == 0 ? -INFINITY : 0.0f;
+  }
+}
+
+// ----------------------------------------------------------- exact unit ----
+__device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h, int seg, int chunk, int u) {
+  float *Ks = reinterpret_cast<float *>(sm + AttnSmem::kKs);
+  float *Vs = reinterpret_cast<float *>(sm + AttnSmem::kVs);
+  float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);
+  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
+  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = b * a.n_kv + h;
+  const int64_t t0 = (int64_t)chunk * kChunk;
+  const int nt = (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk);
+
+  // stage q (scaled) and the K/V chunk as fp32
+  for (int i = tid; i < a.g * 32; i += blockDim.x) {
+    const int hq = i >> 5, qd = i & 31;
+    float x[4];
+    load4_rt(a.q, (b * a.n_q + (int64_t)h * a.g + hq) * kD + qd * 4, a.q_dt, x);
+    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] =
+        make_float4(x[0] * a.inv_scale, x[1] * a.inv_scale, x[2] * a.inv_scale, x[3] * a.inv_scale);
+  }
+  const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD;
+  for (int i = tid; i < kChunk * 32; i += blockDim.x) {
+    const int j = i >> 5, qd = i & 31;
+    float xk[4] = {0.f, 0.f, 0.f, 0.f}, xv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (j < nt) {
+      const int64_t off = base + (t0 + j) * a.tok_stride[seg] + qd * 4;
+      load4_rt(a.k[seg], off, a.kdt[seg], xk);
+      load4_rt(a.v[seg], off, a.vdt[seg], xv);
+    }
+    *reinterpret_cast<float4 *>(Ks + j * kKsStride + qd * 4) = make_float4(xk[0], xk[1], xk[2], xk[3]);
+    *reinterpret_cast<float4 *>(Vs + j * kD + qd * 4) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+  }
+  __syncthreads();
+  // scores: (hq, 32-token block) pairs, lane = token
+  for (int p = warp; p < a.g * 2; p += 8) {
+    const int hq = p >> 1, j = (p & 1) * 32 + lane;
+    const float4 *kr = reinterpret_cast<const float4 *>(Ks + j * kKsStride);
+    const float4 *qr = reinterpret_cast<const float4 *>(Qs + hq * kD);
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < 32; ++c) {
+      const float4 kk = kr[c], qq = qr[c];
+      acc = fmaf(qq.x, kk.x, acc);
+      acc = fmaf(qq.y, kk.y, acc);
+      acc = fmaf(qq.z, kk.z, acc);
+      acc = fmaf(qq.w, kk.w, acc);
+    }
+    S[hq * kD + j] = j < nt ? acc : -INFINITY;
+  }
+  __syncthreads();
+  softmax_rows(a, nt, S, P, ML);
+  __syncthreads();
+  // P.V: thread = (channel, token half)
+  const int c = tid & 127, half = tid >> 7;
+  float o[kMaxG];
+#pragma unroll
+  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
+  for (int j = half * 32; j < half * 32 + 32; ++j) {
+    const float vv = Vs[j * kD + c];
+    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
+    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
+    o[0] = fmaf(p0.x, vv, o[0]); o[1] = fmaf(p0.y, vv, o[1]);
+    o[2] = fmaf(p0.z, vv, o[2]); o[3] = fmaf(p0.w, vv, o[3]);
+    if (a.g > 4) {
+      o[4] = fmaf(p1.x, vv, o[4]); o[5] = fmaf(p1.y, vv, o[5]);
+      o[6] = fmaf(p1.z, vv, o[6]); o[7] = fmaf(p1.w, vv, o[7]);
+    }
+  }
+  if (half == 1)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
+  __syncthreads();
+  if (half == 0) {
+    for (int hq = 0; hq < a.g; ++hq) {
+      float *pr = part_row(a, row, u, hq);
+      pr[2 + c] = o[hq] + S[hq * kD + c];
+      if (c == 0) {
+        pr[0] = ML[hq * 2];
+        pr[1] = ML[hq * 2 + 1];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------- sd1 unit ----
+template <int TILE>
+__device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h, int slot, int u) {
+  uint32_t *KB = reinterpret_cast<uint32_t *>(sm + AttnSmem::kKB);
+  uint32_t *VB = reinterpret_cast<uint32_t *>(sm + AttnSmem::kVB);
+  const uint16_t *KS = reinterpret_cast<const uint16_t *>(sm + AttnSmem::kKS);
+  const uint16_t *VS = reinterpret_cast<const uint16_t *>(sm + AttnSmem::kVS);
+  float *LUT = reinterpret_cast<float *>(sm + AttnSmem::kLUT);
+  float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);
+  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
+  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + AttnSmem::kBar);
+  int *flag = reinterpret_cast<int *>(sm + AttnSmem::kFlag);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = b * a.n_kv + h;
+  const int32_t t = a.sel[row * a.k_sel + slot];
+  if (t < 0) {
+    write_empty_partial(a, row, u);
+    return;
+  }
+  const int64_t tix = row * a.nt_cap + t;
+  constexpr unsigned kBits = TILE * 16, kScale = kD * 2;
+  if (tid == 0) {
+    flag[0] = 1;
+    mbar_init(bar, 1);
+    mbar_expect_tx(bar, 2 * kBits + 2 * kScale);
+    bulk_g2s(KB, a.kbits + tix * TILE * 4, kBits, bar);
+    bulk_g2s(VB, a.vbits + tix * TILE * 4, kBits, bar);
+    bulk_g2s(sm + AttnSmem::kKS, a.kscale + tix * kD, kScale, bar);
+    bulk_g2s(sm + AttnSmem::kVS, a.vscale + tix * kD, kScale, bar);
+  }
+  // transformed queries while the copies fly
+  for (int i = tid; i < a.g * 32; i += blockDim.x) {
+    const int hq = i >> 5, qd = i & 31;
+    const float4 x =
+        __ldg(reinterpret_cast<const float4 *>(a.qprime + (b * a.n_q + (int64_t)h * a.g + hq) * kD) + qd);
+    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] =
+        make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
+  }
+  __syncthreads();  // barrier initialised, Qs staged
+  if (!mbar_wait_bounded(bar, 0)) {
+    atomicOr(a.err, 1u);
+    flag[0] = 0;  // benign race: every thread that fails writes 0
+    mbar_wait_bounded(bar, 0);  // let copies in flight land before smem is reused
+  }
+  __syncthreads();
+  if (!flag[0]) {
+    write_empty_partial(a, row, u);
+    return;
+  }
+  // signed nibble LUT: L[hq][grp][x] = sum_r (bit r of x ? +a : -a)_{4 grp + r}, a_c = q'_c s_c
+  for (int i = tid; i < a.g * 32; i += blockDim.x) {
+    const int hq = i >> 5, grp = i & 31;
+    float av[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      av[r] = Qs[hq * kD + 4 * grp + r] * __half2float(__ushort_as_half(KS[4 * grp + r]));
+    float *L = LUT + (hq * 32 + grp) * 16;
+#pragma unroll
+    for (int x = 0; x < 16; ++x) {
+      float s = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) s += ((x >> r) & 1) ? av[r] : -av[r];
+      L[x] = s;
+    }
+  }
+  __syncthreads();
+  constexpr int NB = TILE / 32;
+  for (int p = warp; p < a.g * NB; p += 8) {
+    const int hq = p / NB, j = (p - hq * NB) * 32 + lane;
+    const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[j];
+    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+    const float *L = LUT + hq * 32 * 16;
+    float acc = 0.0f;
+#pragma unroll
+    for (int grp = 0; grp < 32; ++grp) acc += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
+    S[hq * kD + j] = acc;
+  }
+  __syncthreads();
+  softmax_rows(a, TILE, S, P, ML);
+  __syncthreads();
+  const int c = tid & 127, half = tid >> 7;
+  float o[kMaxG];
+#pragma unroll
+  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
+  const int word = c >> 5, bit = c & 31;
+  for (int j = half * (TILE / 2); j < (half + 1) * (TILE / 2); ++j) {
+    const float bf = (float)((VB[j * 4 + word] >> bit) & 1u);
+    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
+    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
+    o[0] = fmaf(p0.x, bf, o[0]); o[1] = fmaf(p0.y, bf, o[1]);
+    o[2] = fmaf(p0.z, bf, o[2]); o[3] = fmaf(p0.w, bf, o[3]);
+    if (a.g > 4) {
+      o[4] = fmaf(p1.x, bf, o[4]); o[5] = fmaf(p1.y, bf, o[5]);
+      o[6] = fmaf(p1.z, bf, o[6]); o[7] = fmaf(p1.w, bf, o[7]);
+    }
+  }
+  if (half == 1)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
+  __syncthreads();
+  if (half == 0) {
+    const float vs = __half2float(__ushort_as_half(VS[c]));
+    for (int hq = 0; hq < a.g; ++hq) {
+      float *pr = part_row(a, row, u, hq);
+      const float l = ML[hq * 2 + 1];
+      pr[2 + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - l);
+      if (c == 0) {
+        pr[0] = ML[hq * 2];
+        pr[1] = l;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- merge ----
+__device__ void merge_group(const AttnArgs &a, unsigned char *sm, int64_t b, int h) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = b * a.n_kv + h;
+  const int U = a.units;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  // merge layout (all below kML): W [U][8] | Ex [8][128] | Tr [8][128] | buf [8][256] | lee [127]
+  float *W = reinterpret_cast<float *>(sm);
+  float *Ex = W + U * kMaxG;
+  float *Tr = Ex + kMaxG * kD;
+  float *buf = Tr + kMaxG * kD;
+  float *lee = buf + 8 * 2 * kD;
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);  // [g] (M, L)
+  load_lee(lee);
+  for (int hq = warp; hq < a.g; hq += 8) {
+    float mx = -INFINITY;
+    for (int u = lane; u < U; u += 32) mx = fmaxf(mx, __ldcg(part_row(a, row, u, hq)));
+    mx = warp_max(mx);
+    float l = 0.0f;
+    for (int u = lane; u < U; u += 32) {
+      const float *pr = part_row(a, row, u, hq);
+      const float mu = __ldcg(pr);
+      const float w = (mu == -INFINITY) ? 0.0f : expf(mu - mx);
+      W[u * kMaxG + hq] = w;
+      l += w * __ldcg(pr + 1);
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      ML[hq * 2] = mx;
+      ML[hq * 2 + 1] = l;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < a.g * kD; i += blockDim.x) {
+    const int hq = i >> 7, c = i & 127;
+    float ex = 0.0f, tr = 0.0f;
+    for (int u = 0; u < U; ++u) {
+      const float w = W[u * kMaxG + hq];
+      if (w == 0.0f) continue;
+      const float o = __ldcg(part_row(a, row, u, hq) + 2 + c);
+      if (u < n_exact) ex = fmaf(w, o, ex);
+      else tr = fmaf(w, o, tr);
+    }
+    Ex[hq * kD + c] = ex;
+    Tr[hq * kD + c] = tr;
+  }
+  __syncthreads();
+  const bool any_tiles = U > n_exact;
+  for (int hq = warp; hq < a.g; hq += 8) {
+    float x[4];
+    const float4 t4 = reinterpret_cast<const float4 *>(Tr + hq * kD)[lane];
+    x[0] = t4.x; x[1] = t4.y; x[2] = t4.z; x[3] = t4.w;
+    if (any_tiles) transform128(x, lane, a.kind, true, buf + warp * 2 * kD, lee);
+    const float4 e4 = reinterpret_cast<const float4 *>(Ex + hq * kD)[lane];
+    const float y[4] = {e4.x + (any_tiles ? x[0] : 0.f), e4.y + (any_tiles ? x[1] : 0.f),
+                        e4.z + (any_tiles ? x[2] : 0.f), e4.w + (any_tiles ? x[3] : 0.f)};
+    const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
+    const float M = ML[hq * 2], L = ML[hq * 2 + 1];
+    if (a.partial_out) {
+      float *pr = a.partial_out + qh * (kD + 2);
+      if (lane == 0) {
+        pr[0] = M;
+        pr[1] = L;
+      }
+      reinterpret_cast<float2 *>(pr + 2)[2 * lane] = make_float2(y[0], y[1]);
+      reinterpret_cast<float2 *>(pr + 2)[2 * lane + 1] = make_float2(y[2], y[3]);
+    } else {
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int64_t idx = qh * kD + lane * 4 + r;
+        if (a.out_dt == KVR_F32) store_elem<KVR_F32>(a.out, idx, y[r] * inv);
+        else if (a.out_dt == KVR_F16) store_elem<KVR_F16>(a.out, idx, y[r] * inv);
+        else store_elem<KVR_BF16>(a.out, idx, y[r] * inv);
+      }
+    }
+  }
+}
+
+template <int TILE>
+__global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int u = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t row = b * a.n_kv + h;
+  if (u < a.nchunk[0]) {
+    exact_unit(a, sm, b, h, 0, u, u);
+  } else if (u < a.nchunk[0] + a.nchunk[1]) {
+    exact_unit(a, sm, b, h, 1, u - a.nchunk[0], u);
+  } else {
+    tile_unit<TILE>(a, sm, b, h, u - a.nchunk[0] - a.nchunk[1], u);
+  }
+  __syncthreads();
+  int *last = reinterpret_cast<int *>(sm + AttnSmem::kFlag) + 1;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&a.counters[row], 1u);
+    *last = (prev == (unsigned)a.units - 1);
+  }
+  __syncthreads();
+  if (!*last) return;
+  __threadfence();
+  merge_group(a, sm, b, h);
+  if (threadIdx.x == 0) a.counters[row] = 0u;
+}
+
+// Merge kernel for sequence-split partials: one warp per query row.
+__global__ void lse_merge_kernel(const float *__restrict__ part, int P, int n_q, void *out, int out_dt) {
+  const int lane = threadIdx.x & 31;
+  const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (qh >= n_q) return;
+  float mx = -INFINITY;
+  for (int p = 0; p < P; ++p) mx = fmaxf(mx, part[((int64_t)p * n_q + qh) * (kD + 2)]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, l = 0.0f;
+  for (int p = 0; p < P; ++p) {
+    const float *pr = part + ((int64_t)p * n_q + qh) * (kD + 2);
+    const float m = pr[0];
+    if (m == -INFINITY) continue;
+    const float w = expf(m - mx);
+    l = fmaf(w, pr[1], l);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = fmaf(w, pr[2 + lane * 4 + r], acc[r]);
+  }
+  const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t idx = (int64_t)qh * kD + lane * 4 + r;
+    if (out_dt == KVR_F32) store_elem<KVR_F32>(out, idx, acc[r] * inv);
+    else if (out_dt == KVR_F16) store_elem<KVR_F16>(out, idx, acc[r] * inv);
+    else store_elem<KVR_BF16>(out, idx, acc[r] * inv);
+  }
+}
+
+// ------------------------------------------------------------ host side ----
+struct AttnWs {
+  unsigned *err, *counters;
+  float *part;
+  size_t bytes;
+};
+
+static size_t merge_smem_bytes(int units) {
+  return (size_t)units * kMaxG * 4 + 2 * kMaxG * kD * 4 + 8 * 2 * kD * 4 + kD * 4;
+}
+
+static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) {
+  AttnWs w{};
+  char *p = reinterpret_cast<char *>(base);
+  const size_t rows = (size_t)batch * n_kv;
+  size_t off = 0;
+  w.err = reinterpret_cast<unsigned *>(p + off);
+  off += 256;
+  w.counters = reinterpret_cast<unsigned *>(p + off);
+  off += align_up(rows * 4, 256);
+  w.part = reinterpret_cast<float *>(p + off);
+  off += align_up(rows * (size_t)units * g * (kD + 2) * 4, 256);
+  w.bytes = off;
+  return w;
+}
+
+int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what) {
+  if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
+  size_t smem = AttnSmem::kTotal;
+  const size_t ms = merge_smem_bytes(a.units);
+  if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
+  dim3 grid(a.units, a.n_kv, batch);
+  switch (a.tile) {
+#define KVR_AT(T)                                                                                  \
+  case T:                                                                                          \
+    cudaFuncSetAttribute(attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
+    attn_kernel<T><<<grid, 256, smem, st>>>(a);                                                    \
+    break;
+    KVR_AT(32)
+    KVR_AT(64)
+    KVR_AT(128)
+#undef KVR_AT
+    default:
+      return set_error(KVR_ENOTSUP, "%s: tile must be 32, 64 or 128", what);
+  }
+  return check_launch(what);
+}
+
+}  // namespace kvr
+
+using namespace kvr;
+
+extern "C" size_t kvr_decode_attn_workspace_bytes(int n_q, int n_kv, int d, int64_t n_tok_total) {
+  (void)d;
+  if (n_kv <= 0 || n_q <= 0) return 0;
+  const int units = (int)((n_tok_total + kChunk - 1) / kChunk) + 2;
+  return attn_ws_layout(nullptr, 1, n_kv, units, n_q / n_kv).bytes;
+}
+
+extern "C" int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0, const void *v0,
+                               int kdt0, int vdt0, int64_t n0, int64_t tok_stride0, const void *k1, const void *v1,
+                               int kdt1, int vdt1, int64_t n1, int64_t tok_stride1, float scale, void *out,
+                               int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == kD, "kvr_decode_attn: head_dim must be 128 (got %d)", d);
+  KVR_REQUIRE(n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
+              "kvr_decode_attn: need n_q %% n_kv == 0 and n_q/n_kv <= 8 (n_q=%d n_kv=%d)", n_q, n_kv);
+  KVR_REQUIRE(valid_dtype(q_dtype) && valid_dtype(out_dtype), "kvr_decode_attn: bad q/out dtype");
+  KVR_REQUIRE(q && out && workspace, "kvr_decode_attn: null pointer");
+  KVR_REQUIRE(n0 >= 0 && n1 >= 0, "kvr_decode_attn: negative token count");
+  KVR_REQUIRE(n0 == 0 || (k0 && v0 && valid_dtype(kdt0) && valid_dtype(vdt0) && tok_stride0 % 4 == 0),
+              "kvr_decode_attn: bad segment 0");
+  KVR_REQUIRE(n1 == 0 || (k1 && v1 && valid_dtype(kdt1) && valid_dtype(vdt1) && tok_stride1 % 4 == 0),
+              "kvr_decode_attn: bad segment 1");
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_decode_attn: workspace must be 256-byte aligned");
+  AttnArgs a{};
+  a.q = q; a.q_dt = q_dtype; a.n_q = n_q; a.n_kv = n_kv; a.g = n_q / n_kv;
+  a.inv_scale = (float)(1.0 / (scale > 0.f ? (double)scale : sqrt((double)d)));
+  a.k[0] = k0; a.v[0] = v0; a.kdt[0] = kdt0; a.vdt[0] = vdt0; a.n[0] = n0; a.tok_stride[0] = tok_stride0;
+  a.k[1] = k1; a.v[1] = v1; a.kdt[1] = kdt1; a.vdt[1] = vdt1; a.n[1] = n1; a.tok_stride[1] = tok_stride1;
+  a.nchunk[0] = (int)((n0 + kChunk - 1) / kChunk);
+  a.nchunk[1] = (int)((n1 + kChunk - 1) / kChunk);
+  a.units = a.nchunk[0] + a.nchunk[1];
+  a.tile = 64; a.kind = KVR_HADAMARD;
+  a.out = out; a.out_dt = out_dtype;
+  if (a.units == 0) {
+    cudaMemsetAsync(out, 0, (size_t)n_q * d * dtype_size(out_dtype), as_cuda(stream));
+    return check_launch("kvr_decode_attn (empty)");
+  }
+  AttnWs w = attn_ws_layout(workspace, 1, n_kv, a.units, a.g);
+  KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_decode_attn: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  a.err = w.err; a.counters = w.counters; a.part = w.part;
+  return launch_attn(a, 1, as_cuda(stream), "kvr_decode_attn");
+}
+
+static int sd1_units(int64_t n_win, int64_t n_tail, int k_sel) {
+  return (int)((n_win + kChunk - 1) / kChunk + (n_tail + kChunk - 1) / kChunk) + k_sel;
+}
+
+extern "C" size_t kvr_sd1_attend_workspace_bytes(int batch, int n_q, int n_kv, int tile, int k_sel, int64_t n_win,
+                                                 int64_t n_tail) {
+  (void)tile;
+  if (n_kv <= 0 || n_q <= 0 || batch <= 0) return 0;
+  return attn_ws_layout(nullptr, batch, n_kv, sd1_units(n_win, n_tail, k_sel), n_q / n_kv).bytes;
+}
+
+extern "C" int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int batch, int n_q, int n_kv,
+                              const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                              const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
+                              const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
+                              int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out,
+                              int out_dtype, float *partial_out, void *workspace, size_t workspace_bytes,
+                              kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(batch > 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
+              "kvr_sd1_attend: need n_q %% n_kv == 0 and n_q/n_kv <= 8");
+  KVR_REQUIRE(tile == 32 || tile == 64 || tile == 128, "kvr_sd1_attend: tile must be 32, 64 or 128");
+  KVR_REQUIRE(kind == KVR_HADAMARD || kind == KVR_DCT, "kvr_sd1_attend: unknown transform kind");
+  KVR_REQUIRE(valid_dtype(q_dtype) && valid_dtype(out_dtype), "kvr_sd1_attend: bad dtype");
+  KVR_REQUIRE(q && workspace && (out || partial_out), "kvr_sd1_attend: null pointer");
+  KVR_REQUIRE(n_win >= 0 && n_win <= win_cap && (n_win == 0 || (win_k && win_v)), "kvr_sd1_attend: bad window");
+  KVR_REQUIRE(n_tail >= 0 && n_tail <= tile && (n_tail == 0 || (tail_k && tail_v)), "kvr_sd1_attend: bad tail");
+  KVR_REQUIRE(k_sel >= 0 && (k_sel == 0 || (sel && qprime && kbits && kscale && vbits && vscale)),
+              "kvr_sd1_attend: bad selection/store");
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_attend: workspace must be 256-byte aligned");
+  AttnArgs a{};
+  a.q = q; a.q_dt = q_dtype; a.n_q = n_q; a.n_kv = n_kv; a.g = n_q / n_kv;
+  a.inv_scale = (float)(1.0 / (scale > 0.f ? (double)scale : sqrt((double)kD)));
+  a.qprime = qprime;
+  const int64_t tokw = (int64_t)n_kv * kD;
+  a.k[0] = win_k; a.v[0] = win_v; a.kdt[0] = KVR_F16; a.vdt[0] = KVR_F16; a.n[0] = n_win;
+  a.tok_stride[0] = tokw; a.batch_stride[0] = win_cap * tokw;
+  a.k[1] = tail_k; a.v[1] = tail_v; a.kdt[1] = KVR_F16; a.vdt[1] = KVR_F16; a.n[1] = n_tail;
+  a.tok_stride[1] = tokw; a.batch_stride[1] = (int64_t)tile * tokw;
+  a.nchunk[0] = (int)((n_win + kChunk - 1) / kChunk);
+  a.nchunk[1] = (int)((n_tail + kChunk - 1) / kChunk);
+  a.kbits = kbits; a.kscale = kscale; a.vbits = vbits; a.vscale = vscale; a.nt_cap = nt_cap;
+  a.tile = tile; a.kind = kind; a.sel = sel; a.k_sel = k_sel;
+  a.out = out; a.out_dt = out_dtype; a.partial_out = partial_out;
+  a.units = sd1_units(n_win, n_tail, k_sel);
+  if (a.units == 0) {
+    cudaStream_t st = as_cuda(stream);
+    if (partial_out) {
+      // m = -inf rows: fill with a tiny kernel-free pattern via memset is not possible for -inf;
+      // an all-empty step is reported as an error instead.
+      return set_error(KVR_EINVAL, "kvr_sd1_attend: no tokens to attend");
+    }
+    cudaMemsetAsync(out, 0, (size_t)batch * n_q * kD * dtype_size(out_dtype), st);
+    return check_launch("kvr_sd1_attend (empty)");
+  }
+  AttnWs w = attn_ws_layout(workspace, batch, n_kv, a.units, a.g);
+  KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_sd1_attend: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  a.err = w.err; a.counters = w.counters; a.part = w.part;
+  return launch_attn(a, batch, as_cuda(stream), "kvr_sd1_attend");
+}
+
+extern "C" size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,
+                                          int64_t n_win, int64_t n_tail) {
+  const size_t a = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
+  const size_t s = align_up(kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles), 256);
+  const size_t sel = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);
+  const size_t qp = align_up((size_t)batch * n_q * kD * 4, 256);
+  return a + s + sel + qp;
+}
+
+extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint16_t *win_k,
+                                   const uint16_t *win_v, int64_t win_cap, int64_t n_win, const uint16_t *tail_k,
+                                   const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
+                                   const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale,
+                                   int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel, int64_t ex_t0,
+                                   int64_t ex_t1, float scale, void *out, int out_dtype, int32_t *sel_out,
+                                   void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(batch > 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0, "kvr_sd1_decode_step: bad head counts");
+  const size_t need = kvr_sd1_workspace_bytes(batch, n_q, n_kv, n_tiles, tile, k_sel, n_win, n_tail);
+  KVR_REQUIRE(workspace && workspace_bytes >= need, "kvr_sd1_decode_step: workspace %zu < %zu bytes",
+              workspace_bytes, need);
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_decode_step: workspace must be 256-byte aligned");
+  char *p = reinterpret_cast<char *>(workspace);
+  const size_t a_bytes = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
+  const size_t s_bytes = align_up(kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles), 256);
+  const size_t sel_bytes = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);
+  void *ws_attn = p;
+  void *ws_sel = p + a_bytes;
+  int32_t *sel = sel_out ? sel_out : reinterpret_cast<int32_t *>(p + a_bytes + s_bytes);
+  float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
+  int rc = kvr_sd1_select(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
+                          ex_t1, 0, sel, nullptr, qprime, ws_sel, s_bytes, stream);
+  if (rc) return rc;
+  return kvr_sd1_attend(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
+                        kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
+                        ws_attn, a_bytes, stream);
+}
+
+extern "C" int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,
+                             kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == kD, "kvr_lse_merge: head_dim must be 128");
+  KVR_REQUIRE(partials && out && P > 0 && n_q > 0 && valid_dtype(out_dtype), "kvr_lse_merge: bad arguments");
+  lse_merge_kernel<<<(n_q + 7) / 8, 256, 0, as_cuda(stream)>>>(partials, P, n_q, out, out_dtype);
+  return check_launch("kvr_lse_merge");
+}
+
+extern "C" int kvr_workspace_status(const void *workspace, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(workspace, "kvr_workspace_status: null workspace");
+  unsigned flag = 0;
+  cudaStream_t st = as_cuda(stream);
+  if (cudaMemcpyAsync(&flag, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return check_launch("kvr_workspace_status");
+  if (flag) {
+    cudaMemsetAsync(const_cast<void *>(workspace), 0, 4, st);
+    return set_error(KVR_ETIMEOUT, "a bounded device-side wait gave up (flag %u)", flag);
+  }
+  return KVR_OK;
+}

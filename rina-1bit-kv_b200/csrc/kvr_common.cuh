@@ -1,0 +1,119 @@
+// Shared helpers of the kvr_b200 native library (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <climits>
+#include <cstdio>
+
+#include "kvr_b200.h"
+
+namespace kvr {
+
+// ---------------------------------------------------------------- errors ----
+// Sets the calling thread's last-error message and returns `code`.
+int set_error(int code, const char *fmt, ...);
+void clear_error();
+
+#define KVR_REQUIRE(cond, ...)                              \
+  do {                                                      \
+    if (!(cond)) return ::kvr::set_error(KVR_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+// Checks the launch that was just issued.
+int check_launch(const char *what);
+
+inline bool valid_dtype(int dt) { return dt == KVR_F32 || dt == KVR_F16 || dt == KVR_BF16; }
+inline size_t dtype_size(int dt) { return dt == KVR_F32 ? 4 : 2; }
+inline cudaStream_t as_cuda(kvr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---------------------------------------------------------- device utils ----
+template <int DT>
+__device__ __forceinline__ float load_elem(const void *p, int64_t i) {
+  if constexpr (DT == KVR_F32) {
+    return __ldg(reinterpret_cast<const float *>(p) + i);
+  } else if constexpr (DT == KVR_F16) {
+    return __half2float(reinterpret_cast<const __half *>(p)[i]);
+  } else {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+  }
+}
+
+// Loads 4 consecutive elements starting at element i (i must be a multiple of 4
+// and the row 8/16-byte aligned) and widens them to fp32 exactly.
+template <int DT>
+__device__ __forceinline__ void load4(const void *p, int64_t i, float (&x)[4]) {
+  if constexpr (DT == KVR_F32) {
+    float4 v = __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + i));
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+    uint2 u = __ldg(reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(p) + i));
+    uint32_t w[2] = {u.x, u.y};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint16_t lo = w[j] & 0xffff, hi = w[j] >> 16;
+      if constexpr (DT == KVR_F16) {
+        x[2 * j] = __half2float(__ushort_as_half(lo));
+        x[2 * j + 1] = __half2float(__ushort_as_half(hi));
+      } else {
+        x[2 * j] = __bfloat162float(__ushort_as_bfloat16(lo));
+        x[2 * j + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+      }
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void store_elem(void *p, int64_t i, float v) {
+  if constexpr (DT == KVR_F32) {
+    reinterpret_cast<float *>(p)[i] = v;
+  } else if constexpr (DT == KVR_F16) {
+    reinterpret_cast<__half *>(p)[i] = __float2half_rn(v);
+  } else {
+    reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_max_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key).  NaN maps
+// to the key of -inf, -0.0 to the key of +0.0.
+__device__ __forceinline__ uint32_t float_key(float f) {
+  if (f != f) f = -INFINITY;
+  if (f == 0.0f) f = 0.0f;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// Bound on device-side spin iterations (each iteration also sleeps ~64 ns).
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+}  // namespace kvr

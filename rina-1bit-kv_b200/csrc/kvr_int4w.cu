@@ -1,0 +1,512 @@
+// int4w codec kernels (the reference-faithful path), window ring write and
+// the per-row top-k entry point (sm_100a).
+//
+// Reference: modules/kvr_retrieval.py (int4 K + W-predicted V + int2 residual),
+// modules/kvr_window.py (fp16 ring), modules/kvr_cuda.cu (native score kernel).
+// Quantisers use correctly rounded division (__fdiv_rn) and round-half-even
+// (rintf) exactly like torch.round(x / step), so the packed codes are
+// bit-identical to the reference's.
+#include "kvr_common.cuh"
+#include "kvr_topk.cuh"
+
+namespace kvr {
+
+static int blocks_for(int64_t n, int per) {
+  int64_t g = (n + per - 1) / per;
+  if (g > 148 * 32) g = 148 * 32;
+  return (int)(g < 1 ? 1 : g);
+}
+
+// ------------------------------------------------------------- absmax ----
+template <int DT>
+__global__ void absmax_kernel(const void *__restrict__ x, int64_t n, int64_t cols, int64_t rows_per,
+                              unsigned *__restrict__ out_bits) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per, r1 = min(n, r0 + rows_per);
+  float m = 0.0f;
+  for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(load_elem<DT>(x, r * cols + c)));
+  atomicMax(out_bits + c, __float_as_uint(m));  // non-negative floats order like their bits
+}
+__global__ void clamp_min_kernel(float *out, int64_t cols, float lo) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < cols) out[c] = fmaxf(out[c], lo);
+}
+
+// ----------------------------------------------------------- encode K ----
+// One thread per 8 consecutive elements of one (token, head) row -> 4 bytes.
+template <int DT>
+__global__ void encode_k_kernel(const void *__restrict__ k, int64_t n, int n_kv, int d, int64_t tok_stride,
+                                const float *__restrict__ scales, uint8_t *__restrict__ out) {
+  const int groups = d / 8;
+  const int64_t total = n * n_kv * groups;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int gi = (int)(i % groups);
+    const int64_t th = i / groups;
+    const int h = (int)(th % n_kv);
+    const int64_t t = th / n_kv;
+    const int64_t src = t * tok_stride + (int64_t)h * d + gi * 8;
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      int code[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int c = gi * 8 + e + q;
+        const float step = __fdiv_rn(__fmul_rn(2.0f, __ldg(scales + h * d + c)), 16.0f);
+        float r = rintf(__fdiv_rn(load_elem<DT>(k, src + e + q), step));
+        r = fminf(fmaxf(r, -8.0f), 7.0f);
+        code[q] = (int)r + 8;
+      }
+      word |= (uint32_t)((code[0] << 4) | code[1]) << (8 * (e / 2));
+    }
+    *reinterpret_cast<uint32_t *>(out + th * (d / 2) + gi * 4) = word;
+  }
+}
+
+// -------------------------------------------------------- encode V res ----
+// One thread per 16 elements -> 4 bytes.
+template <int DT>
+__global__ void encode_vres_kernel(const void *__restrict__ v, const float *__restrict__ vpred, int64_t n, int n_kv,
+                                   int d, const float *__restrict__ vr, uint8_t *__restrict__ out) {
+  const int groups = d / 16;
+  const int64_t total = n * n_kv * groups;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int gi = (int)(i % groups);
+    const int64_t th = i / groups;
+    const int h = (int)(th % n_kv);
+    const int64_t base = th * d + gi * 16;
+    const float step = __fdiv_rn(__fmul_rn(2.0f, __ldg(vr + h)), 4.0f);
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      uint32_t byte = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float res = __fsub_rn(load_elem<DT>(v, base + e + q), __ldg(vpred + base + e + q));
+        float r = rintf(__fdiv_rn(res, step));
+        r = fminf(fmaxf(r, -2.0f), 1.0f);
+        byte |= (uint32_t)((int)r + 2) << (6 - 2 * q);
+      }
+      word |= byte << (8 * (e / 4));
+    }
+    *reinterpret_cast<uint32_t *>(out + th * (d / 4) + gi * 4) = word;
+  }
+}
+
+// ---------------------------------------- drop-in interleaved scores ----
+// Same arithmetic as the reference kernel (kvr_cuda.cu:25-48): one thread
+// per (token, head), (hi*s)/8, fmaf rotation with (n, d/2) tables, /sqrt(d).
+__global__ void scores_interleaved_kernel(const float *__restrict__ q, const uint8_t *__restrict__ kp,
+                                          const float *__restrict__ sc, const float *__restrict__ cs,
+                                          const float *__restrict__ sn, int n_kv, int d, int64_t n_stored,
+                                          float *__restrict__ scores) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_stored * n_kv) return;
+  const int h = (int)(i % n_kv);
+  const int64_t t = i / n_kv;
+  const int half = d / 2;
+  const uint8_t *p = kp + (t * n_kv + h) * half;
+  const float *s = sc + h * d;
+  const float *c_t = cs + t * half;
+  const float *s_t = sn + t * half;
+  float score = 0.0f;
+  for (int j = 0; j < half; ++j) {
+    const uint8_t b = p[j];
+    const float hi = (float)((b >> 4) - 8), lo = (float)((b & 0x0F) - 8);
+    const float ke = hi * s[2 * j] / 8.0f, ko = lo * s[2 * j + 1] / 8.0f;
+    const float cv = c_t[j], sv = s_t[j];
+    const float k0 = fmaf(ke, cv, -ko * sv), k1 = fmaf(ke, sv, ko * cv);
+    score = fmaf(q[h * d + 2 * j], k0, fmaf(q[h * d + 2 * j + 1], k1, score));
+  }
+  scores[t * n_kv + h] = score / sqrtf((float)d);
+}
+
+// ------------------------------------------------- group-mean queries ----
+__device__ __forceinline__ void stage_qavg(const float *__restrict__ q, int n_q, int n_kv, int d, float *qa) {
+  const int g = n_q / n_kv;
+  for (int i = threadIdx.x; i < n_kv * d; i += blockDim.x) {
+    const int h = i / d, c = i - h * d;
+    float s = 0.0f;
+    for (int j = 0; j < g; ++j) s += q[(int64_t)(h * g + j) * d + c];
+    qa[i] = s / (float)g;
+  }
+}
+
+// --------------------------------------------------- cosine token scores ----
+// 8 lanes per (token, head); lane s of the group owns dims 16s..16s+15.
+// rotate_half partners (i, i +/- 64) sit in lanes s and s ^ 4.
+__global__ void __launch_bounds__(256) token_scores_kernel(
+    const float *__restrict__ q, int n_q, const uint8_t *__restrict__ kp, const float *__restrict__ sc,
+    const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, int halves_equal, int n_kv,
+    int64_t n_stored, float *__restrict__ scores, int64_t score_stride) {
+  constexpr int d = 128;
+  __shared__ float qa[8 * d];  // n_kv <= 8
+  __shared__ float qn_s[8];
+  stage_qavg(q, n_q, n_kv, d, qa);
+  __syncthreads();
+  if (threadIdx.x < n_kv) {
+    float s = 0.0f;
+    for (int c = 0; c < d; ++c) s += qa[threadIdx.x * d + c] * qa[threadIdx.x * d + c];
+    qn_s[threadIdx.x] = sqrtf(s) + 1e-8f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int64_t total = n_stored * n_kv;
+  const int64_t gwarp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // each warp covers 4 (token, head) pairs per iteration; the loop bound is warp-uniform
+  for (int64_t base = gwarp * 4; base < total; base += nwarps * 4) {
+    const int64_t pair = base + (lane >> 3);
+    const bool valid = pair < total;
+    const int64_t pp = valid ? pair : total - 1;
+    const int h = (int)(pp % n_kv);
+    const int64_t t = pp / n_kv;
+    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(kp + pp * (d / 2) + sub * 8));
+    const uint32_t w[2] = {raw.x, raw.y};
+    float kx[16];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const uint32_t byte = (w[e / 8] >> (8 * ((e / 2) & 3))) & 0xffu;
+      const int c = sub * 16 + e;
+      kx[e] = (float)((int)(byte >> 4) - 8) * __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + h * d + c)), 16.0f);
+      kx[e + 1] = (float)((int)(byte & 15) - 8) * __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + h * d + c + 1)), 16.0f);
+    }
+    const float *cr = cs + t * rope_stride;
+    const float *sr = sn + t * rope_stride;
+    const int coff = halves_equal ? ((sub * 16) & 63) : sub * 16;
+    float dot = 0.0f, nk = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, kx[e], 4);
+      const float rh = sub < 4 ? -partner : partner;
+      const float kr = __fadd_rn(__fmul_rn(kx[e], __ldg(cr + coff + e)), __fmul_rn(rh, __ldg(sr + coff + e)));
+      dot = fmaf(qa[h * d + sub * 16 + e], kr, dot);
+      nk = fmaf(kr, kr, nk);
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      nk += __shfl_xor_sync(0xffffffffu, nk, o);
+    }
+    if (valid && sub == 0) {
+      float s = dot / (qn_s[h] * (sqrtf(nk) + 1e-8f));
+      if (s != s) s = -INFINITY;
+      scores[(int64_t)h * score_stride + t] = s;
+    }
+  }
+}
+
+// --------------------------------------------------- cosine chunk scores ----
+// One warp per (chunk, head); lane owns dims 4l..4l+3 (rotate_half partner in lane ^ 16).
+__global__ void __launch_bounds__(256) chunk_scores_kernel(
+    const float *__restrict__ q, int n_q, const uint8_t *__restrict__ kp, const float *__restrict__ sc,
+    const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, int halves_equal, int n_kv,
+    int64_t n_chunks, int chunk, float *__restrict__ scores, int64_t score_stride) {
+  constexpr int d = 128;
+  __shared__ float qa[8 * d];
+  stage_qavg(q, n_q, n_kv, d, qa);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t wi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < n_chunks * n_kv; wi += warps) {
+    const int h = (int)(wi % n_kv);
+    const int64_t ci = wi / n_kv;
+    float step[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) step[r] = __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + h * d + lane * 4 + r)), 16.0f);
+    const int coff = halves_equal ? ((lane * 4) & 63) : lane * 4;
+    for (int j = 0; j < chunk; ++j) {
+      const int64_t t = ci * chunk + j;
+      const uint16_t two = __ldg(reinterpret_cast<const uint16_t *>(kp + (t * n_kv + h) * (d / 2) + lane * 2));
+      float kx[4];
+      kx[0] = (float)((int)((two >> 4) & 15) - 8) * step[0];
+      kx[1] = (float)((int)(two & 15) - 8) * step[1];
+      kx[2] = (float)((int)((two >> 12) & 15) - 8) * step[2];
+      kx[3] = (float)((int)((two >> 8) & 15) - 8) * step[3];
+      const float4 c4 = __ldg(reinterpret_cast<const float4 *>(cs + t * rope_stride + coff));
+      const float4 s4 = __ldg(reinterpret_cast<const float4 *>(sn + t * rope_stride + coff));
+      const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float partner = __shfl_xor_sync(0xffffffffu, kx[r], 16);
+        const float rh = lane < 16 ? -partner : partner;
+        acc[r] += __fadd_rn(__fmul_rn(kx[r], cv[r]), __fmul_rn(rh, sv[r]));
+      }
+    }
+    float dot = 0.f, nk = 0.f, nq = 0.f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float m = acc[r] / (float)chunk;
+      const float qv = qa[h * d + lane * 4 + r];
+      dot = fmaf(qv, m, dot);
+      nk = fmaf(m, m, nk);
+      nq = fmaf(qv, qv, nq);
+    }
+    dot = warp_sum(dot);
+    nk = warp_sum(nk);
+    nq = warp_sum(nq);
+    if (lane == 0) {
+      float s = dot / ((sqrtf(nq) + 1e-8f) * (sqrtf(nk) + 1e-8f));
+      if (s != s) s = -INFINITY;
+      scores[(int64_t)h * score_stride + ci] = s;
+    }
+  }
+}
+
+// ----------------------------------------------------------------- top-k ----
+constexpr int kTopkThreads = 1024;
+__global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float *__restrict__ scores, int64_t n,
+                                                                 int64_t row_stride, int k, int64_t ex0,
+                                                                 int64_t ex1, int64_t *__restrict__ idx,
+                                                                 float *__restrict__ vals, int64_t ors,
+                                                                 int64_t oes) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn);
+  unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn + align_up(sizeof(TopkSmem), 16));
+  const float *row = scores + (int64_t)blockIdx.x * row_stride;
+  block_topk<kTopkThreads>([&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldg(row + i); },
+                           n, k, cand, tsm);
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const int64_t o = (int64_t)blockIdx.x * ors + (int64_t)j * oes;
+    idx[o] = key_index(cand[j]);
+    if (vals) vals[o] = key_score(cand[j]);
+  }
+}
+
+// ---------------------------------------------------------------- gather ----
+// One warp per (i, h): ret_k row (RoPE'd head h) and the all-heads x row.
+__global__ void __launch_bounds__(256) gather_kernel(const uint8_t *__restrict__ kp, const float *__restrict__ sc,
+                                                     const int64_t *__restrict__ top, int k, int n_kv,
+                                                     const float *__restrict__ cs, const float *__restrict__ sn,
+                                                     int64_t rope_stride, const float *__restrict__ kmean,
+                                                     float *__restrict__ ret_k, float *__restrict__ x) {
+  constexpr int d = 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t wi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < (int64_t)k * n_kv; wi += warps) {
+    const int h = (int)(wi % n_kv);
+    const int64_t i = wi / n_kv;
+    const int64_t t = top[i * n_kv + h];
+    const int D = n_kv * d;
+    // x[h, i, :] = deq K[t, all heads] - K_mean
+    float *xr = x + ((int64_t)h * k + i) * D;
+    for (int e = lane * 4; e < D; e += 128) {
+      const int hh = e / d, c = e - hh * d;
+      const uint16_t two = *reinterpret_cast<const uint16_t *>(kp + (t * n_kv + hh) * (d / 2) + c / 2);
+      const int codes[4] = {(int)((two >> 4) & 15) - 8, (int)(two & 15) - 8, (int)((two >> 12) & 15) - 8,
+                            (int)((two >> 8) & 15) - 8};
+      float4 o;
+      float *op = &o.x;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float step = __fdiv_rn(__fmul_rn(2.0f, sc[hh * d + c + r]), 16.0f);
+        op[r] = __fsub_rn(__fmul_rn((float)codes[r], step), kmean[e + r]);
+      }
+      *reinterpret_cast<float4 *>(xr + e) = o;
+    }
+    // ret_k[i, h, :] = RoPE(deq K[t, h]) at position t
+    const uint16_t two = *reinterpret_cast<const uint16_t *>(kp + (t * n_kv + h) * (d / 2) + lane * 2);
+    const int codes[4] = {(int)((two >> 4) & 15) - 8, (int)(two & 15) - 8, (int)((two >> 12) & 15) - 8,
+                          (int)((two >> 8) & 15) - 8};
+    float kx[4], out4[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      kx[r] = __fmul_rn((float)codes[r], __fdiv_rn(__fmul_rn(2.0f, sc[h * d + lane * 4 + r]), 16.0f));
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float partner = __shfl_xor_sync(0xffffffffu, kx[r], 16);
+      const float rh = lane < 16 ? -partner : partner;
+      out4[r] = __fadd_rn(__fmul_rn(kx[r], cs[t * rope_stride + lane * 4 + r]),
+                          __fmul_rn(rh, sn[t * rope_stride + lane * 4 + r]));
+    }
+    *reinterpret_cast<float4 *>(ret_k + (i * n_kv + h) * d + lane * 4) = make_float4(out4[0], out4[1], out4[2], out4[3]);
+  }
+}
+
+__global__ void vres_add_kernel(const float *__restrict__ vb, const uint8_t *__restrict__ vr,
+                                const float *__restrict__ vrs, const int64_t *__restrict__ top, int k, int n_kv,
+                                uint16_t *__restrict__ out) {
+  constexpr int d = 128;
+  const int64_t total = (int64_t)k * n_kv * d;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % d);
+    const int64_t ih = e / d;
+    const int h = (int)(ih % n_kv);
+    const int64_t i = ih / n_kv;
+    const int64_t t = top[i * n_kv + h];
+    const uint8_t byte = vr[(t * n_kv + h) * (d / 4) + c / 4];
+    const int code = (int)((byte >> (6 - 2 * (c & 3))) & 3) - 2;
+    const float step = __fdiv_rn(__fmul_rn(2.0f, vrs[h]), 4.0f);
+    const float v = __fadd_rn(vb[((int64_t)h * k + i) * d + c], __fmul_rn((float)code, step));
+    out[e] = __half_as_ushort(__float2half_rn(v));
+  }
+}
+
+// ---------------------------------------------------------------- window ----
+template <int DT>
+__global__ void window_write_kernel(const void *__restrict__ k, const void *__restrict__ v, int64_t first,
+                                   int64_t count, int64_t row_elems, uint16_t *__restrict__ rk,
+                                   uint16_t *__restrict__ rv, int64_t cap, int64_t pos) {
+  const int64_t total = count * row_elems;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / row_elems, c = e - i * row_elems;
+    const int64_t src = (first + i) * row_elems + c;
+    const int64_t slot = (pos + first + i) % cap;
+    rk[slot * row_elems + c] = __half_as_ushort(__float2half_rn(load_elem<DT>(k, src)));
+    rv[slot * row_elems + c] = __half_as_ushort(__float2half_rn(load_elem<DT>(v, src)));
+  }
+}
+
+}  // namespace kvr
+
+using namespace kvr;
+
+extern "C" int kvr_absmax_scales(const void *x, int dtype, int64_t n, int64_t cols, float clamp_min, float *out,
+                                 kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(x && out && n > 0 && cols > 0 && valid_dtype(dtype), "kvr_absmax_scales: bad arguments");
+  cudaStream_t st = as_cuda(stream);
+  if (cudaMemsetAsync(out, 0, cols * 4, st) != cudaSuccess) return check_launch("kvr_absmax_scales memset");
+  const int64_t rows_per = 256;
+  dim3 grid((unsigned)((cols + 255) / 256), (unsigned)((n + rows_per - 1) / rows_per));
+  unsigned *bits = reinterpret_cast<unsigned *>(out);
+  if (dtype == KVR_F32) absmax_kernel<KVR_F32><<<grid, 256, 0, st>>>(x, n, cols, rows_per, bits);
+  else if (dtype == KVR_F16) absmax_kernel<KVR_F16><<<grid, 256, 0, st>>>(x, n, cols, rows_per, bits);
+  else absmax_kernel<KVR_BF16><<<grid, 256, 0, st>>>(x, n, cols, rows_per, bits);
+  clamp_min_kernel<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(out, cols, clamp_min);
+  return check_launch("kvr_absmax_scales");
+}
+
+extern "C" int kvr_int4w_encode_k(const void *k, int dtype, int64_t n, int n_kv, int d, int64_t tok_stride,
+                                  const float *k_scales, uint8_t *k_packed, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(k && k_scales && k_packed && valid_dtype(dtype), "kvr_int4w_encode_k: bad arguments");
+  KVR_REQUIRE(n >= 0 && n_kv > 0 && d > 0 && d % 16 == 0, "kvr_int4w_encode_k: d must be a multiple of 16");
+  if (n == 0) return KVR_OK;
+  const int64_t total = n * n_kv * (d / 8);
+  cudaStream_t st = as_cuda(stream);
+  if (dtype == KVR_F32) encode_k_kernel<KVR_F32><<<blocks_for(total, 256), 256, 0, st>>>(k, n, n_kv, d, tok_stride, k_scales, k_packed);
+  else if (dtype == KVR_F16) encode_k_kernel<KVR_F16><<<blocks_for(total, 256), 256, 0, st>>>(k, n, n_kv, d, tok_stride, k_scales, k_packed);
+  else encode_k_kernel<KVR_BF16><<<blocks_for(total, 256), 256, 0, st>>>(k, n, n_kv, d, tok_stride, k_scales, k_packed);
+  return check_launch("kvr_int4w_encode_k");
+}
+
+extern "C" int kvr_int4w_encode_vres(const void *v, int dtype, const float *v_pred, int64_t n, int n_kv, int d,
+                                     const float *vr_scales, uint8_t *vr_packed, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(v && v_pred && vr_scales && vr_packed && valid_dtype(dtype), "kvr_int4w_encode_vres: bad arguments");
+  KVR_REQUIRE(n >= 0 && n_kv > 0 && d > 0 && d % 16 == 0, "kvr_int4w_encode_vres: d must be a multiple of 16");
+  if (n == 0) return KVR_OK;
+  const int64_t total = n * n_kv * (d / 16);
+  cudaStream_t st = as_cuda(stream);
+  if (dtype == KVR_F32) encode_vres_kernel<KVR_F32><<<blocks_for(total, 256), 256, 0, st>>>(v, v_pred, n, n_kv, d, vr_scales, vr_packed);
+  else if (dtype == KVR_F16) encode_vres_kernel<KVR_F16><<<blocks_for(total, 256), 256, 0, st>>>(v, v_pred, n, n_kv, d, vr_scales, vr_packed);
+  else encode_vres_kernel<KVR_BF16><<<blocks_for(total, 256), 256, 0, st>>>(v, v_pred, n, n_kv, d, vr_scales, vr_packed);
+  return check_launch("kvr_int4w_encode_vres");
+}
+
+extern "C" int kvr_compute_scores(const float *q_avg, const uint8_t *k_pack, const float *k_scales, const float *cos_tbl,
+                                  const float *sin_tbl, int n_kv, int d, int64_t n_stored, float *scores,
+                                  kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(q_avg && k_pack && k_scales && cos_tbl && sin_tbl && scores, "kvr_compute_scores: null pointer");
+  KVR_REQUIRE(n_kv > 0 && d > 0 && d % 2 == 0 && n_stored >= 0, "kvr_compute_scores: bad shape");
+  if (n_stored == 0) return KVR_OK;
+  const int64_t total = n_stored * n_kv;
+  scores_interleaved_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_cuda(stream)>>>(
+      q_avg, k_pack, k_scales, cos_tbl, sin_tbl, n_kv, d, n_stored, scores);
+  return check_launch("kvr_compute_scores");
+}
+
+extern "C" int kvr_int4w_token_scores(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                                      const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                      int rope_halves_equal, int n_kv, int d, int64_t n_stored, float *scores,
+                                      int64_t score_stride, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == 128, "kvr_int4w_token_scores: head_dim must be 128");
+  KVR_REQUIRE(n_kv > 0 && n_kv <= 8 && n_q % n_kv == 0, "kvr_int4w_token_scores: need n_kv <= 8, n_q %% n_kv == 0");
+  KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && scores, "kvr_int4w_token_scores: null pointer");
+  KVR_REQUIRE(score_stride >= n_stored && rope_stride >= (rope_halves_equal ? 64 : 128), "kvr_int4w_token_scores: bad strides");
+  if (n_stored <= 0) return KVR_OK;
+  const int64_t pairs = n_stored * n_kv;
+  token_scores_kernel<<<blocks_for(pairs, 32), 256, 0, as_cuda(stream)>>>(
+      q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride, rope_halves_equal, n_kv, n_stored, scores,
+      score_stride);
+  return check_launch("kvr_int4w_token_scores");
+}
+
+extern "C" int kvr_int4w_chunk_scores(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                                      const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                      int rope_halves_equal, int n_kv, int d, int64_t n_stored, int chunk,
+                                      float *scores, int64_t score_stride, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == 128, "kvr_int4w_chunk_scores: head_dim must be 128");
+  KVR_REQUIRE(n_kv > 0 && n_kv <= 8 && n_q % n_kv == 0 && chunk > 0, "kvr_int4w_chunk_scores: bad shape");
+  KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && scores, "kvr_int4w_chunk_scores: null pointer");
+  const int64_t n_chunks = n_stored / chunk;
+  KVR_REQUIRE(score_stride >= n_chunks, "kvr_int4w_chunk_scores: bad score stride");
+  if (n_chunks <= 0) return KVR_OK;
+  chunk_scores_kernel<<<blocks_for(n_chunks * n_kv, 8), 256, 0, as_cuda(stream)>>>(
+      q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride, rope_halves_equal, n_kv, n_chunks, chunk, scores,
+      score_stride);
+  return check_launch("kvr_int4w_chunk_scores");
+}
+
+extern "C" int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t row_stride, int k, int64_t ex_start,
+                             int64_t ex_end, int64_t *idx, float *vals, int64_t out_row_stride,
+                             int64_t out_elem_stride, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(scores && idx && rows >= 0, "kvr_topk_rows: bad arguments");
+  KVR_REQUIRE(k >= 0 && k <= n && k <= 4096, "kvr_topk_rows: need 0 <= k <= min(n, 4096) (k=%d n=%lld)", k, (long long)n);
+  KVR_REQUIRE(n < 0xffffffffll, "kvr_topk_rows: rows longer than 2^32-1");
+  if (rows == 0 || k == 0) return KVR_OK;
+  int P = 1;
+  while (P < k) P <<= 1;
+  const size_t smem = align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  topk_rows_kernel<<<rows, kTopkThreads, smem, as_cuda(stream)>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
+                                                                   out_row_stride, out_elem_stride);
+  return check_launch("kvr_topk_rows");
+}
+
+extern "C" int kvr_int4w_gather(const uint8_t *k_packed, const float *k_scales, const int64_t *top, int k, int n_kv,
+                                int d, const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                const float *k_mean, float *ret_k, float *x, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == 128, "kvr_int4w_gather: head_dim must be 128");
+  KVR_REQUIRE(k_packed && k_scales && top && cos_tbl && sin_tbl && k_mean && ret_k && x, "kvr_int4w_gather: null pointer");
+  KVR_REQUIRE(k >= 0 && n_kv > 0, "kvr_int4w_gather: bad shape");
+  if (k == 0) return KVR_OK;
+  gather_kernel<<<blocks_for((int64_t)k * n_kv, 8), 256, 0, as_cuda(stream)>>>(
+      k_packed, k_scales, top, k, n_kv, cos_tbl, sin_tbl, rope_stride, k_mean, ret_k, x);
+  return check_launch("kvr_int4w_gather");
+}
+
+extern "C" int kvr_int4w_vres_add(const float *v_base, const uint8_t *vr_packed, const float *vr_scales,
+                                  const int64_t *top, int k, int n_kv, int d, uint16_t *ret_v, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == 128, "kvr_int4w_vres_add: head_dim must be 128");
+  KVR_REQUIRE(v_base && vr_packed && vr_scales && top && ret_v && k >= 0 && n_kv > 0, "kvr_int4w_vres_add: bad arguments");
+  if (k == 0) return KVR_OK;
+  vres_add_kernel<<<blocks_for((int64_t)k * n_kv * d, 256), 256, 0, as_cuda(stream)>>>(v_base, vr_packed, vr_scales,
+                                                                                        top, k, n_kv, ret_v);
+  return check_launch("kvr_int4w_vres_add");
+}
+
+extern "C" int kvr_window_write(const void *k, const void *v, int dtype, int64_t n, int n_kv, int d, uint16_t *ring_k,
+                                uint16_t *ring_v, int64_t cap, int64_t pos, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(k && v && ring_k && ring_v && valid_dtype(dtype), "kvr_window_write: bad arguments");
+  KVR_REQUIRE(n >= 0 && cap > 0 && pos >= 0 && n_kv > 0 && d > 0, "kvr_window_write: bad shape");
+  if (n == 0) return KVR_OK;
+  const int64_t count = n < cap ? n : cap;
+  const int64_t first = n - count;
+  const int64_t row = (int64_t)n_kv * d;
+  cudaStream_t st = as_cuda(stream);
+  const int blocks = blocks_for(count * row, 256);
+  if (dtype == KVR_F32) window_write_kernel<KVR_F32><<<blocks, 256, 0, st>>>(k, v, first, count, row, ring_k, ring_v, cap, pos);
+  else if (dtype == KVR_F16) window_write_kernel<KVR_F16><<<blocks, 256, 0, st>>>(k, v, first, count, row, ring_k, ring_v, cap, pos);
+  else window_write_kernel<KVR_BF16><<<blocks, 256, 0, st>>>(k, v, first, count, row, ring_k, ring_v, cap, pos);
+  return check_launch("kvr_window_write");
+}

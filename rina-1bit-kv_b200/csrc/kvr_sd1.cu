@@ -1,0 +1,520 @@
+// sd1 1-bit codec: encoder, tile scoring + selection, tile decode (sm_100a).
+//
+// The codec has no counterpart in the reference (which stores int4 K and int2
+// V residuals, modules/kvr_retrieval.py:2-4); its specification is the CPU
+// statement in oracle/sd1_ref.py, which these kernels match bit for bit for
+// the packed bits, the fp16 scales and the tile scores.  Selection follows the
+// reference's design: the GQA-group mean of the post-RoPE query scores fixed
+// tiles (modules/kvr_retrieval.py:270, 291-315) and a per-KV-head top-k keeps
+// the best ones (modules/kvr_retrieval.py:370-392).
+#include "kvr_common.cuh"
+#include "kvr_topk.cuh"
+#include "kvr_transform.cuh"
+
+namespace kvr {
+
+// ------------------------------------------------------------ transform ----
+__global__ void __launch_bounds__(256) transform_kernel(const float *x, float *y, int64_t rows, int kind,
+                                                        int inverse) {
+  __shared__ float lee_s[kD];
+  __shared__ __align__(16) float buf_s[8][2 * kD];
+  load_lee(lee_s);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += (int64_t)gridDim.x * 8) {
+    float v[4];
+    float4 t = reinterpret_cast<const float4 *>(x + r * kD)[lane];
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    transform128(v, lane, kind, inverse != 0, buf_s[warp], lee_s);
+    reinterpret_cast<float4 *>(y + r * kD)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// -------------------------------------------------------------- encoder ----
+// One CTA of 256 threads per (tile, kv head, batch).  Phase 1: each warp
+// loads token vectors (K, then V), applies RoPE to K when tables are given,
+// transforms them and parks them in shared memory X[kv][j][c].  Phase 2:
+// threads 0-127 run the sigma-delta scan of one K channel each, threads
+// 128-255 of one V channel; the bits of a token come out of a warp ballot
+// (warp w owns channels 32w..32w+31 = word w).
+template <int DT, int TILE>
+__global__ void __launch_bounds__(256) sd1_encode_kernel(
+    const void *__restrict__ k, const void *__restrict__ v, int n_kv, int64_t batch_stride,
+    int64_t tok_stride, const float *__restrict__ cos_tbl, const float *__restrict__ sin_tbl,
+    int64_t rope_stride, int64_t pos0, int kind, uint32_t *__restrict__ kbits, uint16_t *__restrict__ kscale,
+    uint32_t *__restrict__ vbits, uint16_t *__restrict__ vscale, int64_t nt_cap, int64_t tile0) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float *X = reinterpret_cast<float *>(smem_raw);                       // [2][TILE][128]
+  uint32_t *bits_s = reinterpret_cast<uint32_t *>(X + 2 * TILE * kD);    // [2][TILE][4]
+  float *buf_s = reinterpret_cast<float *>(bits_s + 2 * TILE * 4);       // [8][256]
+  float *lee_s = buf_s + 8 * 2 * kD;                                     // [128]
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int64_t tile_in = blockIdx.x;
+  load_lee(lee_s);
+  __syncthreads();
+
+  const int64_t base_in = (int64_t)b * batch_stride + (int64_t)h * kD;
+  const bool rope = cos_tbl != nullptr;
+  constexpr int NV = 2 * TILE;   // vectors per CTA
+  constexpr int PER_WARP = NV / 8;
+  constexpr int BATCH = 8;       // vectors loaded ahead per warp
+  static_assert(PER_WARP % BATCH == 0, "tile too small");
+#pragma unroll 1
+  for (int v0 = 0; v0 < PER_WARP; v0 += BATCH) {
+    float xv[BATCH][4];
+    float cv[BATCH][4], sv[BATCH][4];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int vid = warp * PER_WARP + v0 + u;  // K: vid < TILE, V: vid >= TILE
+      const bool is_k = vid < TILE;
+      const int j = is_k ? vid : vid - TILE;
+      const int64_t tok = tile_in * TILE + j;
+      load4<DT>(is_k ? k : v, base_in + tok * tok_stride + lane * 4, xv[u]);
+      if (rope && is_k) {
+        const float *cr = cos_tbl + (pos0 + tok) * rope_stride + lane * 4;
+        const float *sr = sin_tbl + (pos0 + tok) * rope_stride + lane * 4;
+        float4 c4 = __ldg(reinterpret_cast<const float4 *>(cr));
+        float4 s4 = __ldg(reinterpret_cast<const float4 *>(sr));
+        cv[u][0] = c4.x; cv[u][1] = c4.y; cv[u][2] = c4.z; cv[u][3] = c4.w;
+        sv[u][0] = s4.x; sv[u][1] = s4.y; sv[u][2] = s4.z; sv[u][3] = s4.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int vid = warp * PER_WARP + v0 + u;
+      const bool is_k = vid < TILE;
+      float x[4] = {xv[u][0], xv[u][1], xv[u][2], xv[u][3]};
+      if (rope && is_k) {
+        // rotate_half: partner element i +/- 64 lives in lane ^ 16
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float p = __shfl_xor_sync(0xffffffffu, x[r], 16);
+          const float rh = lane < 16 ? -p : p;
+          x[r] = __fadd_rn(__fmul_rn(xv[u][r], cv[u][r]), __fmul_rn(rh, sv[u][r]));
+        }
+      }
+      transform128(x, lane, kind, false, buf_s + warp * 2 * kD, lee_s);
+      reinterpret_cast<float4 *>(X + vid * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    }
+  }
+  __syncthreads();
+
+  // phase 2: sigma-delta per channel
+  const int kv = threadIdx.x >> 7;  // 0 = K, 1 = V
+  const int c = threadIdx.x & 127;
+  const float *Xc = X + kv * TILE * kD + c;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int j = 0; j < TILE; ++j) acc = __fadd_rn(acc, fabsf(Xc[j * kD]));
+  const float mean = __fmul_rn(acc, 1.0f / TILE);
+  const __half s16 = __float2half_rn(fminf(mean, 65504.0f));
+  const float s = __half2float(s16);
+  const int64_t out_tile = ((int64_t)b * n_kv + h) * nt_cap + tile0 + tile_in;
+  (kv == 0 ? kscale : vscale)[out_tile * kD + c] = __half_as_ushort(s16);
+  float e = 0.0f;
+  uint32_t *bs = bits_s + kv * TILE * 4;
+  const int word = (threadIdx.x >> 5) & 3;
+#pragma unroll 8
+  for (int j = 0; j < TILE; ++j) {
+    const float u = __fadd_rn(Xc[j * kD], e);
+    const bool bit = u >= 0.0f;
+    e = __fsub_rn(u, bit ? s : -s);
+    const uint32_t w = __ballot_sync(0xffffffffu, bit);
+    if (lane == 0) bs[j * 4 + word] = w;
+  }
+  __syncthreads();
+  // store bits: 2 * TILE uint4
+  for (int i = threadIdx.x; i < 2 * TILE; i += blockDim.x) {
+    const int kvi = i / TILE, j = i - kvi * TILE;
+    const uint4 w = reinterpret_cast<const uint4 *>(bits_s)[i];
+    uint32_t *dst = (kvi == 0 ? kbits : vbits) + (out_tile * TILE + j) * 4;
+    *reinterpret_cast<uint4 *>(dst) = w;
+  }
+}
+
+// ---------------------------------------------------------- tile scores ----
+// One CTA (256 threads, 8 warps) covers 16 consecutive tiles of one (b, h);
+// each warp scores 2 tiles.  Warp 0 first forms q' = T(mean of the group's
+// query heads).  Per tile: w_c = q'_c * s_c, M = max|w|, wq = rint(w*127/M),
+// bit planes of wq via ballots, S_j = 2*sum_c wq_c*bit_jc - sum wq from
+// popcounts, score = float(max_j S_j) * (M/127).  With `select` set, the
+// last CTA of each (b, h) to finish runs the block top-k over that row.
+constexpr int kScoreTilesPerCta = 16;
+
+struct SelectArgs {
+  int k_sel;
+  int64_t ex_t0, ex_t1, tile_base;
+  int32_t *sel;         // (B, n_kv, k_sel)
+  float *sel_scores;    // (B, n_kv, k_sel) or null
+  unsigned *counters;   // (B, n_kv), zero on entry, reset on exit
+};
+
+template <int DTQ, int TILE>
+__global__ void __launch_bounds__(256) sd1_score_kernel(
+    const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
+    const uint16_t *__restrict__ kscale, int64_t nt_cap, int64_t n_tiles, int kind,
+    float *__restrict__ scores /* (B, n_kv, n_tiles) */, float *__restrict__ qprime /* (B, n_q, d) or null */,
+    SelectArgs sa, int do_select) {
+  __shared__ float lee_s[kD];
+  __shared__ __align__(16) float buf_s[8][2 * kD];
+  __shared__ __align__(16) float qp_s[kD];
+  __shared__ int last_s;
+  extern __shared__ __align__(16) unsigned char dyn_smem[];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int g = n_q / n_kv;
+  const int64_t row = (int64_t)b * n_kv + h;
+  load_lee(lee_s);
+
+  // prefetch this warp's tile data while q' is formed
+  constexpr int TPL = TILE / 32;  // tokens per lane
+  const int64_t t_first = (int64_t)blockIdx.x * kScoreTilesPerCta + warp * 2;
+  uint4 kb[2][TPL];
+  uint16_t ks[2][4];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int64_t t = t_first + u;
+    if (t < n_tiles) {
+      const int64_t tix = row * nt_cap + t;
+      const uint4 *src = reinterpret_cast<const uint4 *>(kbits + tix * TILE * 4);
+#pragma unroll
+      for (int r = 0; r < TPL; ++r) kb[u][r] = __ldg(src + lane + 32 * r);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) ks[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float acc[4];
+    const int64_t qb = ((int64_t)b * n_q + (int64_t)h * g) * kD + lane * 4;
+    load4<DTQ>(q, qb, acc);
+    for (int i = 1; i < g; ++i) {
+      float t[4];
+      load4<DTQ>(q, qb + (int64_t)i * kD, t);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], t[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = __fdiv_rn(acc[r], (float)g);
+    transform128(acc, lane, kind, false, buf_s[0], lee_s);
+    reinterpret_cast<float4 *>(qp_s)[lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  } else if (blockIdx.x == 0 && qprime != nullptr) {
+    // per-head transformed queries for the attention kernel
+    for (int i = warp - 1; i < g; i += 7) {
+      float x[4];
+      const int64_t qh = (int64_t)b * n_q + (int64_t)h * g + i;
+      load4<DTQ>(q, qh * kD + lane * 4, x);
+      transform128(x, lane, kind, false, buf_s[warp], lee_s);
+      reinterpret_cast<float4 *>(qprime + qh * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    }
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int64_t t = t_first + u;
+    if (t >= n_tiles) continue;  // warp-uniform
+    int wq[4];
+    float w[4], mx = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      w[m] = __fmul_rn(qp_s[lane + 32 * m], __half2float(__ushort_as_half(ks[u][m])));
+      mx = fmaxf(mx, fabsf(w[m]));
+    }
+    mx = warp_max(mx);
+    const float inv = mx > 0.0f ? __fdiv_rn(127.0f, mx) : 0.0f;
+    int wsum = 0;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      wq[m] = __float2int_rn(__fmul_rn(w[m], inv));
+      wsum += wq[m];
+    }
+    wsum = warp_sum_int(wsum);
+    uint32_t plane[8][4];
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) plane[p][m] = __ballot_sync(0xffffffffu, (wq[m] >> p) & 1);
+    int best = INT_MIN;
+#pragma unroll
+    for (int r = 0; r < TPL; ++r) {
+      const uint32_t bw[4] = {kb[u][r].x, kb[u][r].y, kb[u][r].z, kb[u][r].w};
+      int P = 0;
+#pragma unroll
+      for (int p = 0; p < 7; ++p) {
+        int cnt = 0;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) cnt += __popc(plane[p][m] & bw[m]);
+        P += cnt << p;
+      }
+      int c7 = 0;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) c7 += __popc(plane[7][m] & bw[m]);
+      P -= c7 << 7;
+      best = max(best, 2 * P - wsum);
+    }
+    best = warp_max_int(best);
+    const float delta = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) scores[row * n_tiles + t] = __fmul_rn((float)best, delta);
+  }
+  if (!do_select) return;
+
+  // ---- fused selection by the last CTA of this (b, h)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&sa.counters[row], 1u);
+    last_s = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn_smem);
+  unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn_smem + align_up(sizeof(TopkSmem), 16));
+  const float *srow = scores + row * n_tiles;
+  const int64_t ex0 = sa.ex_t0, ex1 = sa.ex_t1;
+  const int kk = (int)(n_tiles < sa.k_sel ? n_tiles : sa.k_sel);
+  if (kk > 0) {
+    block_topk<256>(
+        [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i); }, n_tiles, kk,
+        cand, tsm);
+  }
+  for (int j = threadIdx.x; j < sa.k_sel; j += blockDim.x) {
+    const bool ok = j < kk;
+    sa.sel[row * sa.k_sel + j] = ok ? (int32_t)(key_index(cand[j]) + sa.tile_base) : -1;
+    if (sa.sel_scores) sa.sel_scores[row * sa.k_sel + j] = ok ? key_score(cand[j]) : -INFINITY;
+  }
+  if (threadIdx.x == 0) sa.counters[row] = 0u;
+}
+
+// ---------------------------------------------------------- tile decode ----
+// One warp per (b, h, selected slot, token): k_hat = T^T(s * (2 bit - 1)).
+__global__ void __launch_bounds__(256) sd1_decode_tiles_kernel(
+    const uint32_t *__restrict__ kbits, const uint16_t *__restrict__ kscale, const uint32_t *__restrict__ vbits,
+    const uint16_t *__restrict__ vscale, int64_t nt_cap, int n_kv, int tile, int kind,
+    const int64_t *__restrict__ sel, int k, float *__restrict__ out_k, uint16_t *__restrict__ out_v,
+    int64_t total_rows) {
+  __shared__ float lee_s[kD];
+  __shared__ __align__(16) float buf_s[8][2 * kD];
+  load_lee(lee_s);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < total_rows; r += (int64_t)gridDim.x * 8) {
+    // r enumerates (b, h, slot, j)
+    const int j = (int)(r % tile);
+    const int64_t bhs = r / tile;
+    const int slot = (int)(bhs % k);
+    const int64_t bh = bhs / k;
+    const int h = (int)(bh % n_kv);
+    const int64_t b = bh / n_kv;
+    const int64_t t = sel[bh * k + slot];
+    const int64_t orow = ((b * k + slot) * tile + j) * n_kv + h;  // (B, k*t, n_kv, d)
+    if (t < 0) {
+      reinterpret_cast<float4 *>(out_k + orow * kD)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<uint2 *>(out_v + orow * kD)[lane] = make_uint2(0u, 0u);
+      continue;
+    }
+    const int64_t tix = bh * nt_cap + t;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint32_t *bits = (kv == 0 ? kbits : vbits) + (tix * tile + j) * 4;
+      const uint16_t *sc = (kv == 0 ? kscale : vscale) + tix * kD;
+      const uint32_t w = __ldg(bits + (lane >> 3));
+      float x[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = lane * 4 + q;
+        const float s = __half2float(__ushort_as_half(__ldg(sc + c)));
+        x[q] = ((w >> (c & 31)) & 1u) ? s : -s;
+      }
+      transform128(x, lane, kind, true, buf_s[warp], lee_s);
+      if (kv == 0) {
+        reinterpret_cast<float4 *>(out_k + orow * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+      } else {
+        __half2 a = __floats2half2_rn(x[0], x[1]), c2 = __floats2half2_rn(x[2], x[3]);
+        reinterpret_cast<uint2 *>(out_v + orow * kD)[lane] =
+            make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&c2));
+      }
+    }
+  }
+}
+
+static int grid_for(int64_t items, int per_block) {
+  int64_t g = (items + per_block - 1) / per_block;
+  if (g > 148 * 64) g = 148 * 64;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <int DT>
+static int launch_encode(int tile, dim3 grid, size_t smem, cudaStream_t st, const void *k, const void *v,
+                         int n_kv, int64_t bs, int64_t ts, const float *c, const float *s, int64_t rs, int64_t pos0,
+                         int kind, uint32_t *kb, uint16_t *ks, uint32_t *vb, uint16_t *vs, int64_t cap,
+                         int64_t t0) {
+  switch (tile) {
+#define KVR_ENC(T)                                                                                       \
+  case T:                                                                                                \
+    cudaFuncSetAttribute(sd1_encode_kernel<DT, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    sd1_encode_kernel<DT, T><<<grid, 256, smem, st>>>(k, v, n_kv, bs, ts, c, s, rs, pos0, kind, kb, ks, vb, \
+                                                       vs, cap, t0);                                     \
+    break;
+    KVR_ENC(32)
+    KVR_ENC(64)
+    KVR_ENC(128)
+#undef KVR_ENC
+    default:
+      return set_error(KVR_ENOTSUP, "sd1: tile must be 32, 64 or 128 (got %d)", tile);
+  }
+  return check_launch("kvr_sd1_encode");
+}
+
+size_t select_dyn_smem(int k_sel) {
+  int P = 1;
+  while (P < k_sel) P <<= 1;
+  return align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
+}
+
+template <int DTQ>
+static int launch_score(int tile, dim3 grid, cudaStream_t st, const void *q, int n_q, int n_kv,
+                        const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind, float *scores,
+                        float *qprime, SelectArgs sa, int do_select) {
+  const size_t smem = do_select ? select_dyn_smem(sa.k_sel) : 0;
+  switch (tile) {
+#define KVR_SC(T)                                                                                        \
+  case T:                                                                                                \
+    if (smem > 48 * 1024)                                                                                \
+      cudaFuncSetAttribute(sd1_score_kernel<DTQ, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    sd1_score_kernel<DTQ, T><<<grid, 256, smem, st>>>(q, n_q, n_kv, kb, ks, cap, nt, kind, scores, qprime, sa, \
+                                                       do_select);                                       \
+    break;
+    KVR_SC(32)
+    KVR_SC(64)
+    KVR_SC(128)
+#undef KVR_SC
+    default:
+      return set_error(KVR_ENOTSUP, "sd1: tile must be 32, 64 or 128 (got %d)", tile);
+  }
+  return check_launch("sd1 tile scores");
+}
+
+int sd1_scores_impl(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                    const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, float *scores,
+                    float *qprime, SelectArgs sa, int do_select, cudaStream_t st) {
+  dim3 grid((unsigned)((n_tiles + kScoreTilesPerCta - 1) / kScoreTilesPerCta), n_kv, batch);
+  if (n_tiles <= 0) grid.x = 1;
+  switch (q_dtype) {
+    case KVR_F32: return launch_score<KVR_F32>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+    case KVR_F16: return launch_score<KVR_F16>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+    default: return launch_score<KVR_BF16>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+  }
+}
+
+}  // namespace kvr
+
+using namespace kvr;
+
+static int check_common_sd1(int batch, int n_q, int n_kv, int tile, int kind) {
+  KVR_REQUIRE(batch > 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0, "sd1: bad batch/head counts (B=%d n_q=%d n_kv=%d)", batch, n_q, n_kv);
+  KVR_REQUIRE(tile == 32 || tile == 64 || tile == 128, "sd1: tile must be 32, 64 or 128 (got %d)", tile);
+  KVR_REQUIRE(kind == KVR_HADAMARD || kind == KVR_DCT, "sd1: unknown transform kind %d", kind);
+  return KVR_OK;
+}
+
+extern "C" int kvr_transform(const float *x, float *y, int64_t rows, int kind, int inverse, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(x && y && rows >= 0, "kvr_transform: null pointer or negative rows");
+  KVR_REQUIRE(kind == KVR_HADAMARD || kind == KVR_DCT, "kvr_transform: unknown kind %d", kind);
+  if (rows == 0) return KVR_OK;
+  transform_kernel<<<grid_for(rows, 8), 256, 0, as_cuda(stream)>>>(x, y, rows, kind, inverse);
+  return check_launch("kvr_transform");
+}
+
+extern "C" int kvr_sd1_encode(const void *k, const void *v, int dtype, int batch, int n_kv, int64_t n_tiles,
+                              int tile, int64_t batch_stride, int64_t tok_stride, const float *cos_tbl,
+                              const float *sin_tbl, int64_t rope_stride, int64_t pos0, int kind, uint32_t *kbits,
+                              uint16_t *kscale, uint32_t *vbits, uint16_t *vscale, int64_t nt_cap, int64_t tile0,
+                              kvr_stream_t stream) {
+  clear_error();
+  int rc = check_common_sd1(batch, n_kv, n_kv, tile, kind);
+  if (rc) return rc;
+  KVR_REQUIRE(valid_dtype(dtype), "kvr_sd1_encode: bad dtype %d", dtype);
+  KVR_REQUIRE(k && v && kbits && kscale && vbits && vscale, "kvr_sd1_encode: null pointer");
+  KVR_REQUIRE(n_tiles >= 0 && tile0 >= 0 && tile0 + n_tiles <= nt_cap, "kvr_sd1_encode: tiles [%lld, %lld) exceed nt_cap %lld",
+              (long long)tile0, (long long)(tile0 + n_tiles), (long long)nt_cap);
+  KVR_REQUIRE(tok_stride % 4 == 0 && batch_stride % 4 == 0, "kvr_sd1_encode: strides must be multiples of 4 elements");
+  KVR_REQUIRE((cos_tbl == nullptr) == (sin_tbl == nullptr), "kvr_sd1_encode: give both rope tables or neither");
+  KVR_REQUIRE(cos_tbl == nullptr || (rope_stride % 4 == 0 && pos0 >= 0), "kvr_sd1_encode: bad rope table stride/pos0");
+  KVR_REQUIRE(n_tiles <= 0x7fffffff, "kvr_sd1_encode: too many tiles per launch");
+  if (n_tiles == 0) return KVR_OK;
+  const size_t smem = (size_t)2 * tile * kD * 4 + (size_t)2 * tile * 16 + 8 * 2 * kD * 4 + kD * 4;
+  dim3 grid((unsigned)n_tiles, n_kv, batch);
+  cudaStream_t st = as_cuda(stream);
+  switch (dtype) {
+    case KVR_F32: return launch_encode<KVR_F32>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
+    case KVR_F16: return launch_encode<KVR_F16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
+    default: return launch_encode<KVR_BF16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
+  }
+}
+
+extern "C" int kvr_sd1_tile_scores(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                                   const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
+                                   float *scores, kvr_stream_t stream) {
+  clear_error();
+  int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
+  if (rc) return rc;
+  KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_tile_scores: bad dtype %d", q_dtype);
+  KVR_REQUIRE(q && kbits && kscale && scores, "kvr_sd1_tile_scores: null pointer");
+  KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_tile_scores: n_tiles > nt_cap");
+  if (n_tiles == 0) return KVR_OK;
+  SelectArgs sa{};
+  return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores,
+                         nullptr, sa, 0, as_cuda(stream));
+}
+
+extern "C" size_t kvr_sd1_select_workspace_bytes(int batch, int n_kv, int64_t n_tiles) {
+  const size_t rows = (size_t)batch * n_kv;
+  return align_up(rows * 4, 256) + align_up(rows * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
+}
+
+extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                              const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
+                              int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
+                              float *qprime, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
+  clear_error();
+  int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
+  if (rc) return rc;
+  KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
+  KVR_REQUIRE(q && sel && qprime && workspace, "kvr_sd1_select: null pointer");
+  KVR_REQUIRE(k_sel >= 0 && k_sel <= 4096, "kvr_sd1_select: k_sel must be in [0, 4096]");
+  KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_select: n_tiles > nt_cap");
+  KVR_REQUIRE(n_tiles == 0 || (kbits && kscale), "kvr_sd1_select: null store pointers");
+  const size_t need = kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles);
+  KVR_REQUIRE(workspace_bytes >= need, "kvr_sd1_select: workspace %zu < %zu bytes", workspace_bytes, need);
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_select: workspace must be 256-byte aligned");
+  cudaStream_t st = as_cuda(stream);
+  const size_t rows = (size_t)batch * n_kv;
+  unsigned *counters = reinterpret_cast<unsigned *>(workspace);
+  float *scores = reinterpret_cast<float *>(reinterpret_cast<char *>(workspace) + align_up(rows * 4, 256));
+  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters};
+  // With no full tile there is nothing to score; the kernel still forms q'
+  // and writes an all-empty selection.
+  return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
+                         sa, 1, st);
+}
+
+extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
+                                    const uint16_t *vscale, int64_t nt_cap, int batch, int n_kv, int tile, int kind,
+                                    const int64_t *sel, int k, float *out_k, uint16_t *out_v, kvr_stream_t stream) {
+  clear_error();
+  int rc = check_common_sd1(batch, n_kv, n_kv, tile, kind);
+  if (rc) return rc;
+  KVR_REQUIRE(kbits && kscale && vbits && vscale && sel && out_k && out_v, "kvr_sd1_decode_tiles: null pointer");
+  KVR_REQUIRE(k >= 0, "kvr_sd1_decode_tiles: negative k");
+  const int64_t rows = (int64_t)batch * n_kv * k * tile;
+  if (rows == 0) return KVR_OK;
+  sd1_decode_tiles_kernel<<<grid_for(rows, 8), 256, 0, as_cuda(stream)>>>(kbits, kscale, vbits, vscale, nt_cap, n_kv,
+                                                                           tile, kind, sel, k, out_k, out_v, rows);
+  return check_launch("kvr_sd1_decode_tiles");
+}

@@ -1,0 +1,166 @@
+// Warp-level orthonormal transforms along head_dim (d = 128) for the sd1 codec.
+//
+// Register layout: lane L holds elements 4L .. 4L+3 of the vector in x[0..3].
+// Every arithmetic step uses explicit round-to-nearest intrinsics so the
+// results are bit-identical to the CPU specification (operation order fixed,
+// no FMA contraction):
+//   * Walsh-Hadamard: butterfly stages of stride 1, 2, 4, ..., 64 with
+//     (a, b) -> (a + b, a - b), then x * fp32(1/sqrt(128));
+//   * DCT-II: Lee's recursive factorisation (split levels M = 128..2:
+//     a_j = x_j + x_{M-1-j}, b_j = (x_j - x_{M-1-j}) * f_M[j]; merge levels
+//     M = 2..128: y_{2k} = A_k, y_{2k+1} = B_k + B_{k+1}), then the
+//     orthonormal scaling sqrt(1/128) for k = 0 and sqrt(2/128) otherwise;
+//   * DCT-III (inverse): the transposed flow graph of the above.
+// The DCT variants stage through a 256-float per-warp shared buffer; the
+// Hadamard runs entirely in registers with xor shuffles.
+#pragma once
+
+#include "kvr_common.cuh"
+#include "kvr_lee_table.h"
+
+namespace kvr {
+
+constexpr int kD = 128;
+constexpr uint32_t kInvSqrt128Bits = 0x3db504f3u;  // fp32(1/sqrt(128)) == fp32(sqrt(1/128))
+
+__device__ __forceinline__ void wht128(float (&x)[4], int lane) {
+  float a0 = x[0], a1 = x[1], a2 = x[2], a3 = x[3];
+  // stride 1
+  x[0] = __fadd_rn(a0, a1); x[1] = __fsub_rn(a0, a1);
+  x[2] = __fadd_rn(a2, a3); x[3] = __fsub_rn(a2, a3);
+  // stride 2
+  a0 = x[0]; a1 = x[1]; a2 = x[2]; a3 = x[3];
+  x[0] = __fadd_rn(a0, a2); x[2] = __fsub_rn(a0, a2);
+  x[1] = __fadd_rn(a1, a3); x[3] = __fsub_rn(a1, a3);
+  // strides 4..64 live across lanes (lane mask 1..16)
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float p = __shfl_xor_sync(0xffffffffu, x[r], m);
+      x[r] = upper ? __fsub_rn(p, x[r]) : __fadd_rn(x[r], p);
+    }
+  }
+  const float c = __uint_as_float(kInvSqrt128Bits);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) x[r] = __fmul_rn(x[r], c);
+}
+
+// Loads the Lee factors into shared memory (call by all threads of a block,
+// followed by a __syncthreads before first use).
+__device__ __forceinline__ void load_lee(float *lee_s) {
+  for (int i = threadIdx.x; i < kD - 1; i += blockDim.x) lee_s[i] = __uint_as_float(kLeeBits[i]);
+}
+
+// buf: 256 floats owned by this warp.  lee: the 127 factors (shared memory).
+__device__ __forceinline__ void dct128_fwd(float (&x)[4], int lane, float *buf, const float *lee) {
+  float *in = buf, *out = buf + kD;
+  reinterpret_cast<float4 *>(in)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  __syncwarp();
+#pragma unroll
+  for (int M = kD; M >= 2; M >>= 1) {
+    const int half = M >> 1;
+    const float *f = lee + half - 1;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int p = lane + 32 * q;
+      const int blk = p / half, j = p - blk * half, o = blk * M;
+      const float xa = in[o + j], xb = in[o + M - 1 - j];
+      out[o + j] = __fadd_rn(xa, xb);
+      out[o + half + j] = __fmul_rn(__fsub_rn(xa, xb), f[j]);
+    }
+    __syncwarp();
+    float *t = in; in = out; out = t;
+  }
+#pragma unroll
+  for (int M = 2; M <= kD; M <<= 1) {
+    const int half = M >> 1;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = lane + 32 * q;
+      const int blk = i / M, r = i - blk * M, o = blk * M;
+      float v;
+      if ((r & 1) == 0) {
+        v = in[o + (r >> 1)];
+      } else {
+        const int k = r >> 1;
+        v = in[o + half + k];
+        if (k < half - 1) v = __fadd_rn(v, in[o + half + k + 1]);
+      }
+      out[i] = v;
+    }
+    __syncwarp();
+    float *t = in; in = out; out = t;
+  }
+  float4 r4 = reinterpret_cast<const float4 *>(in)[lane];
+  __syncwarp();
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  x[0] = __fmul_rn(r4.x, lane == 0 ? c0 : c1);
+  x[1] = __fmul_rn(r4.y, c1);
+  x[2] = __fmul_rn(r4.z, c1);
+  x[3] = __fmul_rn(r4.w, c1);
+}
+
+__device__ __forceinline__ void dct128_inv(float (&x)[4], int lane, float *buf, const float *lee) {
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  float *in = buf, *out = buf + kD;
+  reinterpret_cast<float4 *>(in)[lane] = make_float4(__fmul_rn(x[0], lane == 0 ? c0 : c1),
+                                                      __fmul_rn(x[1], c1), __fmul_rn(x[2], c1),
+                                                      __fmul_rn(x[3], c1));
+  __syncwarp();
+  // transposed merge levels, M = 128 .. 2
+#pragma unroll
+  for (int M = kD; M >= 2; M >>= 1) {
+    const int half = M >> 1;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = lane + 32 * q;
+      const int blk = i / M, r = i - blk * M, o = blk * M;
+      float v;
+      if (r < half) {
+        v = in[o + 2 * r];
+      } else {
+        const int k = r - half;
+        v = in[o + 2 * k + 1];
+        if (k > 0) v = __fadd_rn(v, in[o + 2 * k - 1]);
+      }
+      out[i] = v;
+    }
+    __syncwarp();
+    float *t = in; in = out; out = t;
+  }
+  // transposed split levels, M = 2 .. 128
+#pragma unroll
+  for (int M = 2; M <= kD; M <<= 1) {
+    const int half = M >> 1;
+    const float *f = lee + half - 1;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int p = lane + 32 * q;
+      const int blk = p / half, j = p - blk * half, o = blk * M;
+      const float a = in[o + j], fb = __fmul_rn(in[o + half + j], f[j]);
+      out[o + j] = __fadd_rn(a, fb);
+      out[o + M - 1 - j] = __fsub_rn(a, fb);
+    }
+    __syncwarp();
+    float *t = in; in = out; out = t;
+  }
+  float4 r4 = reinterpret_cast<const float4 *>(in)[lane];
+  __syncwarp();
+  x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
+}
+
+// kind: KVR_HADAMARD or KVR_DCT; the Hadamard is its own inverse.
+__device__ __forceinline__ void transform128(float (&x)[4], int lane, int kind, bool inverse, float *buf,
+                                             const float *lee) {
+  if (kind == KVR_HADAMARD) {
+    wht128(x, lane);
+  } else if (inverse) {
+    dct128_inv(x, lane, buf, lee);
+  } else {
+    dct128_fwd(x, lane, buf, lee);
+  }
+}
+
+}  // namespace kvr

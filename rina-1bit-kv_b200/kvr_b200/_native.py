@@ -1,0 +1,132 @@
+"""ctypes binding of the C ABI in include/kvr_b200.h (libkvr_b200.so, in-tree).
+
+There is no fallback: if the library is missing, importing an operator raises.
+Tensors are passed as raw device pointers; every call runs on the current
+torch CUDA stream and raises ``KvrError`` on a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libkvr_b200.so")
+
+KVR_F32, KVR_F16, KVR_BF16 = 0, 1, 2
+KVR_HADAMARD, KVR_DCT = 0, 1
+STATUS = {0: "KVR_OK", 1: "KVR_EINVAL", 2: "KVR_ECUDA", 3: "KVR_ENOTSUP", 4: "KVR_ETIMEOUT"}
+
+_DT = {torch.float32: KVR_F32, torch.float16: KVR_F16, torch.bfloat16: KVR_BF16}
+TRANSFORMS = {"hadamard": KVR_HADAMARD, "dct": KVR_DCT}
+
+
+class KvrError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+P, I, I64, F, SZ = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "kvr_last_error": (C.c_char_p, []),
+    "kvr_abi_version": (I, []),
+    "kvr_absmax_scales": (I, [P, I, I64, I64, F, P, P]),
+    "kvr_int4w_encode_k": (I, [P, I, I64, I, I, I64, P, P, P]),
+    "kvr_int4w_encode_vres": (I, [P, I, P, I64, I, I, P, P, P]),
+    "kvr_compute_scores": (I, [P, P, P, P, P, I, I, I64, P, P]),
+    "kvr_int4w_token_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, P, I64, P]),
+    "kvr_int4w_chunk_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, I, P, I64, P]),
+    "kvr_topk_rows": (I, [P, I, I64, I64, I, I64, I64, P, P, I64, I64, P]),
+    "kvr_int4w_gather": (I, [P, P, P, I, I, I, P, P, I64, P, P, P, P]),
+    "kvr_int4w_vres_add": (I, [P, P, P, P, I, I, I, P, P]),
+    "kvr_window_write": (I, [P, P, I, I64, I, I, P, P, I64, I64, P]),
+    "kvr_decode_attn_workspace_bytes": (SZ, [I, I, I, I64]),
+    "kvr_decode_attn": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, F, P, I, P, SZ, P]),
+    "kvr_transform": (I, [P, P, I64, I, I, P]),
+    "kvr_sd1_encode": (I, [P, P, I, I, I, I64, I, I64, I64, P, P, I64, I64, I, P, P, P, P, I64, I64, P]),
+    "kvr_sd1_tile_scores": (I, [P, I, I, I, I, P, P, I64, I64, I, I, P, P]),
+    "kvr_sd1_decode_tiles": (I, [P, P, P, P, I64, I, I, I, I, P, I, P, P, P]),
+    "kvr_sd1_select_workspace_bytes": (SZ, [I, I, I64]),
+    "kvr_sd1_select": (I, [P, I, I, I, I, P, P, I64, I64, I, I, I, I64, I64, I64, P, P, P, P, SZ, P]),
+    "kvr_sd1_attend_workspace_bytes": (SZ, [I, I, I, I, I, I64, I64]),
+    "kvr_sd1_attend": (I, [P, I, P, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I, I, P, I, F, P, I, P,
+                           P, SZ, P]),
+    "kvr_sd1_workspace_bytes": (SZ, [I, I, I, I64, I, I, I64, I64]),
+    "kvr_sd1_decode_step": (I, [P, I, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I64, I, I, I, I64, I64,
+                                F, P, I, P, P, SZ, P]),
+    "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),
+    "kvr_workspace_status": (I, [P, P]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load libkvr_b200.so once; raise if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"kvr_b200 native library not built: {LIB_PATH} is missing "
+                               "(run __graft_entry__.build() or python -m kvr_b200._build)")
+        h = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(lib(), name)(*args)
+    if name.endswith("_bytes") or name in ("kvr_last_error", "kvr_abi_version"):
+        return rc
+    if rc != 0:
+        raise KvrError(rc, lib().kvr_last_error().decode())
+    return rc
+
+
+def ptr(t) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("kvr_b200 operators need CUDA tensors (this build has no CPU path)")
+    return t.data_ptr()
+
+
+def dtype_code(t) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError as e:
+        raise TypeError(f"unsupported dtype {t.dtype}") from e
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class Workspace:
+    """A zero-initialised device scratch buffer that grows on demand.  The
+    kernels leave it zeroed after every successful call, so it is reused
+    across calls without clearing."""
+
+    def __init__(self, device=None):
+        self.buf = None
+        self.device = device
+
+    def get(self, nbytes: int, device) -> torch.Tensor:
+        nbytes = max(int(nbytes), 256)
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
+            self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+        return self.buf
+
+
+_WS: dict = {}
+
+
+def workspace(tag: str, nbytes: int, device) -> torch.Tensor:
+    ws = _WS.setdefault((tag, str(device)), Workspace())
+    return ws.get(nbytes, device)

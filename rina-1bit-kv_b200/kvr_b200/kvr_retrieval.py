@@ -1,0 +1,483 @@
+"""RetrievalIndex — compressed store of evicted tokens, drop-in for
+modules/kvr_retrieval.py.
+
+``codec='int4w'`` (default) keeps the reference's format and semantics: int4
+K_pre codes with a per-(head, channel) absmax scale, V = W-predict(K) + int2
+per-head residual, both bit-packed (kvr_retrieval.py:2-4, 69-91, 95-207).
+Encode, scoring, top-k, gather and residual dequantisation run as sm_100a
+kernels; the two dense one-offs — ``torch.linalg.pinv`` in ``calibrate`` and
+the V-predict GEMM — stay library calls (cuSOLVER / cuBLAS), as in the
+reference.
+
+``codec='sd1'`` stores post-RoPE K and V as 1-bit sigma-delta codes in the
+Hadamard/DCT domain with per-tile fp16 scales (no reference counterpart; spec
+in oracle/sd1_ref.py).  Tokens that do not yet fill a tile wait, exact and
+post-RoPE in fp16, in a tail buffer.
+
+Selection order is deterministic: score descending, then index ascending
+(torch.topk's tie order is unspecified, kvr_retrieval.py:392).
+"""
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+
+
+def _rotate_half(x):
+    d2 = x.shape[-1] // 2
+    return torch.cat([-x[..., d2:], x[..., :d2]], dim=-1)
+
+
+def _apply_rotary(x, cos, sin):
+    """kvr_retrieval.py:32-33."""
+    return x * cos[:x.shape[0]] + _rotate_half(x) * sin[:x.shape[0]]
+
+
+def _reverse_rotary(x, cos, sin):
+    """kvr_retrieval.py:36-37."""
+    return x * cos[:x.shape[0]] - _rotate_half(x) * sin[:x.shape[0]]
+
+
+class RetrievalIndex:
+    def __init__(self, n_kv, d_head, top_k=128, device="cuda", chunk_size=8, codec="int4w", tile=64,
+                 transform="hadamard"):
+        if codec not in ("int4w", "sd1"):
+            raise ValueError(f"unknown codec {codec!r}")
+        self.n_kv = n_kv
+        self.d_head = d_head
+        self.kv_dim = n_kv * d_head
+        self.top_k = top_k
+        self.chunk_size = chunk_size
+        self.top_per_basin = 16
+        self.device = device
+        self.codec = codec
+        self.k_scales = None
+        self.k_packed = None
+        self.vr_scales = None
+        self.vr_packed = None
+        self.n_stored = 0
+        self.W = None
+        self.K_mean = None
+        self.V_mean = None
+        self.cos = None
+        self.sin = None
+        self._halves_equal = False
+        self.n_attractors = 128
+        self.attractors = None
+        self.labels = None
+        # sd1 state
+        self.tile = tile
+        self.transform = transform
+        self.store = None
+        self.tail_k = None
+        self.tail_v = None
+        self.n_tail = 0
+
+    # ------------------------------------------------------------ tables --
+    def set_rotary_tables(self, cos, sin):
+        """kvr_retrieval.py:63-65.  Also records whether the halves of each row
+        are duplicated (true for HF tables), which lets kernels read half rows."""
+        self.cos = cos
+        self.sin = sin
+        d2 = cos.shape[-1] // 2
+        self._halves_equal = bool(torch.equal(cos[..., :d2], cos[..., d2:]) and torch.equal(sin[..., :d2], sin[..., d2:]))
+
+    def _tables(self, n):
+        if self.cos is None:
+            z = torch.zeros(max(n, 1), self.d_head, device=self.device)
+            return z + 1.0, z, False
+        return self.cos, self.sin, self._halves_equal
+
+    # ----------------------------------------------------- pack / unpack --
+    def _pack_int4(self, x):
+        u = (x.to(torch.uint8) + 8)
+        return (u[..., 0::2] << 4) | u[..., 1::2]
+
+    def _unpack_int4(self, p):
+        hi = ((p >> 4).to(torch.int8) - 8)
+        lo = ((p & 0x0F).to(torch.int8) - 8)
+        return torch.stack([hi, lo], dim=-1).reshape(*p.shape[:-1], p.shape[-1] * 2)
+
+    def _pack_int2(self, x):
+        u = (x.to(torch.uint8) + 2)
+        return (u[..., 0::4] << 6) | (u[..., 1::4] << 4) | (u[..., 2::4] << 2) | u[..., 3::4]
+
+    def _unpack_int2(self, p):
+        v = [((p >> s) & 0x03).to(torch.int8) - 2 for s in (6, 4, 2, 0)]
+        return torch.stack(v, dim=-1).reshape(*p.shape[:-1], p.shape[-1] * 4)
+
+    # -------------------------------------------------------------- core --
+    @torch.no_grad()
+    def calibrate(self, k_pre_sample, v_sample=None):
+        """kvr_retrieval.py:95-122 (int4w).  For sd1 this only resets the store."""
+        n = k_pre_sample.shape[0]
+        self.n_stored = 0
+        self.attractors = self.labels = None
+        if self.codec == "sd1":
+            self.k_scales = torch.ones(self.n_kv, self.d_head, device=self.device)  # marks "calibrated"
+            self._sd1_reset()
+            return
+        k = k_pre_sample.to(self.device)
+        self.k_scales = K.absmax_scales(k.float().reshape(n, self.n_kv, self.d_head))
+        self.k_packed = torch.zeros(0, self.n_kv, self.d_head // 2, device=self.device, dtype=torch.uint8)
+        self.vr_packed = torch.zeros(0, self.n_kv, self.d_head // 4, device=self.device, dtype=torch.uint8)
+        self.k_codes = None
+        self.vr_codes = None
+        if v_sample is not None and n > 10:
+            k2 = k.reshape(n, self.kv_dim).float()
+            v2 = v_sample.to(self.device).reshape(n, self.kv_dim).float()
+            half = n // 2
+            k_tr, v_tr = k2[:half], v2[:half]
+            self.K_mean = k_tr.mean(0, keepdim=True)
+            self.V_mean = v_tr.mean(0, keepdim=True)
+            kc = k_tr - self.K_mean
+            vc = v_tr - self.V_mean
+            self.W = (kc.T @ vc).T @ torch.linalg.pinv(kc.T @ kc)
+            v_res = v2 - ((k2 - self.K_mean) @ self.W.T + self.V_mean)
+            self.vr_scales = v_res.view(-1, self.n_kv, self.d_head).abs().amax(dim=(0, 2)).unsqueeze(1).clamp(min=1e-8)
+        else:
+            self.W = torch.eye(self.kv_dim, device=self.device)
+            self.K_mean = torch.zeros(1, self.kv_dim, device=self.device)
+            self.V_mean = torch.zeros(1, self.kv_dim, device=self.device)
+            self.vr_scales = torch.ones(self.n_kv, 1, device=self.device)
+
+    def _deq_k(self, kvh):
+        """kvr_retrieval.py:124-129."""
+        step = 2 * self.k_scales / 16
+        packed = self.k_packed[:self.n_stored, kvh, :]
+        return self._unpack_int4(packed).float() * step[kvh].float()
+
+    def _predict_v(self, k_pre_flat):
+        """kvr_retrieval.py:131-134 (a library GEMM)."""
+        if self.W is None:
+            return torch.zeros_like(k_pre_flat)
+        return (k_pre_flat - self.K_mean) @ self.W.T + self.V_mean
+
+    def _rotary(self, k_pre_2d, indices):
+        if self.cos is None:
+            return k_pre_2d
+        c = self.cos[indices].squeeze(1).to(k_pre_2d.dtype)
+        s = self.sin[indices].squeeze(1).to(k_pre_2d.dtype)
+        return _apply_rotary(k_pre_2d, c, s)
+
+    def _reconstruct_v(self, k_pre_top, top_idx):
+        kv_flat = k_pre_top.reshape(-1, self.kv_dim)
+        v_base = self._predict_v(kv_flat).reshape(-1, self.n_kv, self.d_head)
+        vr_step = 2 * self.vr_scales / 4
+        vr_dq = self._unpack_int2(self.vr_packed[top_idx]).float() * vr_step.unsqueeze(0)
+        return (v_base + vr_dq).float()
+
+    @torch.no_grad()
+    def _ensure_capacity(self, needed):
+        """kvr_retrieval.py:150-160: grow x2."""
+        if needed <= self.k_packed.shape[0]:
+            return
+        new_cap = max(needed, self.k_packed.shape[0] * 2)
+        k_ext = torch.zeros(new_cap - self.k_packed.shape[0], self.n_kv, self.d_head // 2, device=self.device,
+                            dtype=torch.uint8)
+        self.k_packed = torch.cat([self.k_packed, k_ext], dim=0)
+        vr_ext = torch.zeros(new_cap - self.vr_packed.shape[0], self.n_kv, self.d_head // 4, device=self.device,
+                             dtype=torch.uint8)
+        self.vr_packed = torch.cat([self.vr_packed, vr_ext], dim=0)
+
+    @torch.no_grad()
+    def append(self, k_pre_rope, v=None):
+        """kvr_retrieval.py:162-185."""
+        if self.k_scales is None:
+            raise RuntimeError("Call calibrate() first")
+        if self.codec == "sd1":
+            return self._sd1_append(k_pre_rope.reshape(1, self.n_kv, self.d_head),
+                                    None if v is None else v.reshape(1, self.n_kv, self.d_head))
+        self._ensure_capacity(self.n_stored + 1)
+        k1 = k_pre_rope.to(self.device).reshape(1, self.n_kv, self.d_head)
+        K.int4w_encode_k(k1, self.k_scales, out=self.k_packed[self.n_stored:self.n_stored + 1])
+        if v is not None and self.W is not None:
+            vp = self._predict_v(k1.float().reshape(1, -1)).reshape(1, self.n_kv, self.d_head)
+            K.int4w_encode_vres(v.to(self.device).reshape(1, self.n_kv, self.d_head), vp, self.vr_scales,
+                                out=self.vr_packed[self.n_stored:self.n_stored + 1])
+        else:
+            self.vr_packed[self.n_stored] = 0
+        self.n_stored += 1
+
+    @torch.no_grad()
+    def batch_append(self, k_pre_all, v_all):
+        """kvr_retrieval.py:187-207: REPLACES the store, pads max(1024, n//2) zero rows."""
+        if self.codec == "sd1":
+            self._sd1_reset()
+            return self._sd1_append(k_pre_all, v_all)
+        n = k_pre_all.shape[0]
+        extra = max(1024, n // 2)
+        k = k_pre_all.to(self.device)
+        self.k_packed = torch.zeros(n + extra, self.n_kv, self.d_head // 2, device=self.device, dtype=torch.uint8)
+        K.int4w_encode_k(k, self.k_scales, out=self.k_packed[:n])
+        self.vr_packed = torch.zeros(n + extra, self.n_kv, self.d_head // 4, device=self.device, dtype=torch.uint8)
+        if self.W is not None and n > 0:
+            v_pred = self._predict_v(k.reshape(n, -1).float()).reshape(n, self.n_kv, self.d_head)
+            K.int4w_encode_vres(v_all.to(self.device), v_pred, self.vr_scales, out=self.vr_packed[:n])
+        self.n_stored = n
+
+    # ----------------------------------------------------------- scoring --
+    @torch.no_grad()
+    def compute_all_scores(self, q_post_rope):
+        """kvr_retrieval.py:265-289 -> (n_stored, n_kv) (a transposed view of
+        the kernel's head-major buffer)."""
+        self._require_int4w("compute_all_scores")
+        cos, sin, he = self._tables(self.n_stored)
+        return K.int4w_token_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, self.n_stored, he).t()
+
+    @torch.no_grad()
+    def compute_chunk_scores(self, q_post_rope):
+        """kvr_retrieval.py:291-315 -> (n_chunks, n_kv)."""
+        self._require_int4w("compute_chunk_scores")
+        cs = self.chunk_size
+        if cs <= 0 or self.n_stored // cs < 1:
+            return self.compute_all_scores(q_post_rope)
+        cos, sin, he = self._tables(self.n_stored)
+        return K.int4w_chunk_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, self.n_stored, cs, he).t()
+
+    @torch.no_grad()
+    def build_attractors(self):
+        """kvr_retrieval.py:234-246: host-side MiniBatchKMeans on head-0 K
+        (sklearn; parity unpinned).  Kept for API compatibility."""
+        if self.codec != "int4w":
+            return
+        from sklearn.cluster import MiniBatchKMeans
+
+        nr = self.n_stored
+        if nr < self.n_attractors * 2:
+            return
+        kp = self._deq_k(0).float().cpu().numpy()
+        kmeans = MiniBatchKMeans(n_clusters=self.n_attractors, random_state=42, batch_size=min(1024, nr), n_init=1)
+        self.labels = torch.from_numpy(kmeans.fit_predict(kp)).to(self.device)
+        self.attractors = torch.from_numpy(kmeans.cluster_centers_.astype(np.float32)).to(self.device)
+
+    @torch.no_grad()
+    def compute_attractor_scores(self, q_post_rope):
+        """kvr_retrieval.py:248-263 (head-0 proxy)."""
+        if self.attractors is None:
+            return self.compute_all_scores(q_post_rope)
+        d, n_kv = self.d_head, self.n_kv
+        g = q_post_rope.shape[0] // n_kv
+        q_avg = q_post_rope.view(n_kv, g, d).mean(dim=1)
+        scores = torch.empty(self.attractors.shape[0], n_kv, device=self.device)
+        qn = q_avg[0] / (q_avg[0].norm() + 1e-8)
+        an = self.attractors / (self.attractors.norm(dim=-1, keepdim=True) + 1e-8)
+        scores[:, 0] = qn @ an.T
+        return scores
+
+    # --------------------------------------------------------- retrieval --
+    def _empty(self):
+        z = torch.zeros(0, self.n_kv, self.d_head, device=self.device, dtype=torch.float16)
+        return z, z
+
+    @torch.no_grad()
+    def select_indices(self, q_post_rope, exclude_start=0, exclude_end=0):
+        """Token indices (top_k, n_kv) the int4w retrieve_topk gathers, or None
+        when it would return nothing."""
+        nr = self.n_stored
+        if nr == 0 or exclude_start >= nr or (exclude_start <= 0 and exclude_end >= nr):
+            return None
+        top_k = min(self.top_k, nr)
+        if self.attractors is not None and self.labels is not None:
+            return self._attractor_indices(q_post_rope, exclude_start, exclude_end)
+        cs = self.chunk_size
+        if cs > 0 and nr >= cs * 2:
+            # intended chunk branch (kvr_retrieval.py:370-388; the reference body is unreachable)
+            sc = self.compute_chunk_scores(q_post_rope).t().contiguous()  # (n_kv, n_chunks)
+            n_chunks = sc.shape[1]
+            ec0 = exclude_start // cs
+            ec1 = min((exclude_end + cs - 1) // cs, n_chunks)
+            if ec0 >= ec1:
+                ec0 = ec1 = 0
+            top_chunks = min(max(1, top_k // cs), n_chunks)
+            cidx, _ = K.topk_rows(sc, top_chunks, ec0, ec1, transpose_out=True)  # (top_chunks, n_kv)
+            tok = cidx.unsqueeze(1) * cs + torch.arange(cs, device=self.device).view(1, cs, 1)
+            return tok.reshape(top_chunks * cs, self.n_kv)
+        cos, sin, he = self._tables(nr)
+        sc = K.int4w_token_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, nr, he)
+        idx, _ = K.topk_rows(sc, top_k, exclude_start, exclude_end, transpose_out=True)
+        return idx
+
+    def _attractor_indices(self, q_post_rope, exclude_start, exclude_end):
+        """kvr_retrieval.py:332-367 (host-assisted, parity unpinned)."""
+        scores = self.compute_attractor_scores(q_post_rope)
+        top_a = min(48, scores.shape[0])
+        top_aidx = torch.topk(scores[:, 0], top_a, dim=0)[1]
+        d, n_kv = self.d_head, self.n_kv
+        g = q_post_rope.shape[0] // n_kv
+        q_avg = q_post_rope.view(n_kv, g, d).mean(dim=1)
+        all_tidx = []
+        k0 = self._deq_k(0)
+        for aidx in top_aidx:
+            tidx = (self.labels == aidx).nonzero(as_tuple=True)[0]
+            if tidx.shape[0] <= self.top_per_basin:
+                all_tidx.append(tidx)
+            else:
+                kp_rot = self._rotary(k0[tidx], tidx)
+                kn = kp_rot / (kp_rot.norm(dim=-1, keepdim=True) + 1e-8)
+                qn = q_avg[0] / (q_avg[0].norm() + 1e-8)
+                all_tidx.append(tidx[(qn @ kn.T).argsort(descending=True)[:self.top_per_basin]])
+        all_tidx = torch.unique(torch.cat(all_tidx)) if all_tidx else torch.zeros(0, device=self.device, dtype=torch.long)
+        if exclude_end > exclude_start:
+            all_tidx = all_tidx[(all_tidx < exclude_start) | (all_tidx >= exclude_end)]
+        if all_tidx.shape[0] == 0:
+            return None
+        return all_tidx.unsqueeze(1).expand(-1, self.n_kv).contiguous()
+
+    @torch.no_grad()
+    def retrieve_topk(self, q_post_rope, n_q=None, exclude_start=0, exclude_end=0):
+        """kvr_retrieval.py:317-412 -> (ret_k fp32 post-RoPE, ret_v fp16), each
+        (rows, n_kv, d).  For sd1: the decoded selected tiles followed by the
+        exact pending tail."""
+        if self.codec == "sd1":
+            return self._sd1_retrieve(q_post_rope, exclude_start, exclude_end)
+        top = self.select_indices(q_post_rope, exclude_start, exclude_end)
+        if top is None:
+            return self._empty()
+        cos, sin, _ = self._tables(self.n_stored)
+        ret_k, x = K.int4w_gather(self.k_packed, self.k_scales, top, cos, sin, self.K_mean)
+        # V-predict GEMM restricted to each head's output columns: (n_kv, k, D) @ (n_kv, D, d)
+        W_h = self.W.view(self.n_kv, self.d_head, self.kv_dim)
+        v_base = torch.baddbmm(self.V_mean.view(self.n_kv, 1, self.d_head), x, W_h.transpose(1, 2))
+        ret_v = K.int4w_vres_add(v_base, self.vr_packed, self.vr_scales, top)
+        return ret_k, ret_v
+
+    @torch.no_grad()
+    def retrieve(self, q_post_rope, n_q=None):
+        """Legacy per-Q-head path (kvr_retrieval.py:209-232): dot/sqrt(d) scores of
+        each Q head, its own top-k, softmax over those only."""
+        self._require_int4w("retrieve")
+        n_q = n_q or q_post_rope.shape[0]
+        g = n_q // self.n_kv
+        d = self.d_head
+        out = torch.zeros(n_q, d, device=q_post_rope.device, dtype=torch.float32)
+        nr = self.n_stored
+        if nr == 0:
+            return out
+        top_k = min(self.top_k, nr)
+        all_idx = torch.arange(nr, device=self.device)
+        for hi in range(n_q):
+            kvh = hi // g
+            qh = q_post_rope[hi].float()
+            k_post = self._rotary(self._deq_k(kvh), all_idx)
+            sim = (k_post @ qh) / math.sqrt(d)
+            sc = sim.unsqueeze(0).contiguous()
+            tidx = K.topk_rows(sc, top_k)[0][0]
+            k_top_post = k_post[tidx]
+            k_top_pre = self._unpack_int4(self.k_packed[tidx]).float() * (2 * self.k_scales / 16).unsqueeze(0)
+            v_top = self._reconstruct_v(k_top_pre, tidx)[:, kvh, :]
+            s = (k_top_post @ qh) / math.sqrt(d)
+            out[hi] = F.softmax(s, dim=-1) @ v_top
+        return out
+
+    def _require_int4w(self, what):
+        if self.codec != "int4w":
+            raise NotImplementedError(f"{what} is defined for codec='int4w' only")
+
+    # --------------------------------------------------------------- sd1 --
+    def _sd1_reset(self):
+        self.store = K.Sd1Store(1, self.n_kv, 64, self.tile, self.transform, self.device)
+        self.tail_k = torch.zeros(1, self.tile, self.n_kv, self.d_head, dtype=torch.float16, device=self.device)
+        self.tail_v = torch.zeros_like(self.tail_k)
+        self.n_tail = 0
+        self.n_stored = 0
+
+    def _rope_post(self, k_pre, pos0):
+        if self.cos is None:
+            return k_pre.float()
+        n = k_pre.shape[0]
+        c = self.cos[pos0:pos0 + n].to(self.device).float().unsqueeze(1)
+        s = self.sin[pos0:pos0 + n].to(self.device).float().unsqueeze(1)
+        return k_pre.float() * c + _rotate_half(k_pre.float()) * s
+
+    def _sd1_append(self, k_pre, v):
+        """Encode whole tiles straight from K_pre (RoPE at positions n_stored+i
+        inside the encoder); keep the remainder exact in the tail."""
+        if self.store is None:
+            self._sd1_reset()
+        k_pre = k_pre.to(self.device)
+        v = torch.zeros_like(k_pre) if v is None else v.to(self.device)
+        n = k_pre.shape[0]
+        t = self.tile
+        i = 0
+        # fill a partial tail first
+        if self.n_tail:
+            take = min(t - self.n_tail, n)
+            self._tail_put(k_pre[:take], v[:take], self.n_stored)
+            i = take
+        n_full = (n - i) // t
+        if n_full:
+            need = self.store.n_tiles + n_full
+            if need > self.store.nt_cap:
+                self.store.grow(max(need, 2 * self.store.nt_cap))
+            cos = self.cos.to(self.device) if self.cos is not None else None
+            sin = self.sin.to(self.device) if self.sin is not None else None
+            K.sd1_encode(self.store, k_pre[i:i + n_full * t], v[i:i + n_full * t], cos=cos, sin=sin,
+                         pos0=self.n_stored)
+            self.n_stored += n_full * t
+            i += n_full * t
+        if i < n:
+            self._tail_put(k_pre[i:], v[i:], self.n_stored)
+
+    def _tail_put(self, k_pre, v, pos0):
+        m = k_pre.shape[0]
+        self.tail_k[0, self.n_tail:self.n_tail + m] = self._rope_post(k_pre, pos0 + self.n_tail).half()
+        self.tail_v[0, self.n_tail:self.n_tail + m] = v.half()
+        self.n_tail += m
+        if self.n_tail == self.tile:
+            if self.store.n_tiles + 1 > self.store.nt_cap:
+                self.store.grow(2 * self.store.nt_cap)
+            K.sd1_encode(self.store, self.tail_k, self.tail_v)
+            self.n_stored += self.tile
+            self.n_tail = 0
+
+    @property
+    def n_tokens(self):
+        """Tokens held: encoded + pending tail (sd1); n_stored (int4w)."""
+        return self.n_stored + (self.n_tail if self.codec == "sd1" else 0)
+
+    def _sd1_select(self, q_post_rope, exclude_start=0, exclude_end=0):
+        t = self.tile
+        k_sel = max(1, self.top_k // t)
+        ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, self.store.n_tiles)
+        if ex0 >= ex1:
+            ex0 = ex1 = 0
+        return K.sd1_select(self.store, q_post_rope.unsqueeze(0), k_sel, ex0, ex1)
+
+    def _sd1_retrieve(self, q_post_rope, exclude_start, exclude_end):
+        if self.store is None or self.n_tokens == 0:
+            return self._empty()
+        parts_k, parts_v = [], []
+        if self.store.n_tiles:
+            sel, _, _ = self._sd1_select(q_post_rope, exclude_start, exclude_end)
+            rk, rv = K.sd1_decode_tiles(self.store, sel.long())
+            keep = (sel[0] >= 0).repeat_interleave(self.tile, dim=1).all(0)  # drop empty slots
+            parts_k.append(rk[0][keep])
+            parts_v.append(rv[0][keep])
+        if self.n_tail:
+            parts_k.append(self.tail_k[0, :self.n_tail].float())
+            parts_v.append(self.tail_v[0, :self.n_tail])
+        return torch.cat(parts_k, 0).contiguous(), torch.cat(parts_v, 0).contiguous()
+
+    @torch.no_grad()
+    def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None):
+        """sd1 fast path: one fused decode step over the window buffer, the
+        pending tail and the selected tiles.  q (n_q, d); returns (n_q, d)."""
+        if self.codec != "sd1":
+            raise NotImplementedError("attend() is the sd1 fused path")
+        if self.store is None:
+            self._sd1_reset()
+        t = self.tile
+        k_sel = max(1, self.top_k // t) if self.store.n_tiles else 0
+        ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, self.store.n_tiles)
+        if ex0 >= ex1:
+            ex0 = ex1 = 0
+        wk = window.k.unsqueeze(0) if window is not None else None
+        wv = window.v.unsqueeze(0) if window is not None else None
+        nw = window.n if window is not None else 0
+        out = K.sd1_decode_step(self.store, q_post_rope.unsqueeze(0), k_sel, wk, wv, nw,
+                                self.tail_k, self.tail_v, self.n_tail, ex0, ex1)
+        return out[0] if out_dtype is None else out[0].to(out_dtype)

@@ -1,0 +1,247 @@
+"""GPU parity of the sd1 1-bit codec against its CPU specification
+(oracle/sd1_ref.py): bits, scales, transforms and tile scores bit-exact;
+selection indices bit-exact; attention within the stated tolerance."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import sd1_ref as S
+from oracle import int4w_ref as R
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+F32 = np.float32
+
+
+def K():
+    from kvr_b200 import kernels
+    return kernels
+
+
+def t(x, dtype=None):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV, dtype=dtype)
+
+
+def cfg0(seed, n, n_kv=8, n_q=32, d=128, B=None):
+    rng = np.random.default_rng(seed)
+    scale = np.exp(rng.standard_normal((n_kv, d))).astype(F32)
+    for h in range(n_kv):
+        scale[h, rng.permutation(d)[:4]] *= 20
+    shape = (n, n_kv, d) if B is None else (B, n, n_kv, d)
+    k = (rng.standard_normal(shape) * scale).astype(F32)
+    v = rng.standard_normal(shape).astype(F32)
+    q = rng.standard_normal((n_q, d) if B is None else (B, n_q, d)).astype(F32)
+    return k, v, q
+
+
+def bits_eq(a, b):
+    return np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", ["hadamard", "dct"])
+def test_transform_bit_exact(kind):
+    x = np.random.default_rng(0).standard_normal((777, 128)).astype(F32) * 3
+    got = K().transform(t(x), kind).cpu().numpy()
+    assert bits_eq(got, S.transform(x, kind))
+    inv = K().transform(t(x), kind, inverse=True).cpu().numpy()
+    assert bits_eq(inv, S.transform(x, kind, inverse=True))
+
+
+@pytest.mark.parametrize("tile", [32, 64, 128])
+@pytest.mark.parametrize("kind", ["hadamard", "dct"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_encode_bit_exact(tile, kind, dtype):
+    n = tile * 5
+    k, v, q = cfg0(tile + (kind == "dct"), n, n_kv=4)
+    kt, vt = t(k).to(dtype), t(v).to(dtype)
+    kf, vf = kt.float().cpu().numpy(), vt.float().cpu().numpy()
+    st = K().Sd1Store(1, 4, 8, tile, kind, DEV)
+    K().sd1_encode(st, kt, vt)
+    assert st.n_tiles == 5
+    for h in range(4):
+        want = S.encode(kf[:, h], vf[:, h], tile, kind)
+        assert np.array_equal(st.kbits[0, h, :5].cpu().numpy().view(np.uint32), want["kbits"])
+        assert np.array_equal(st.vbits[0, h, :5].cpu().numpy().view(np.uint32), want["vbits"])
+        assert bits_eq(st.kscale[0, h, :5].cpu().numpy().view(np.uint16), want["kscale"].view(np.uint16))
+        assert bits_eq(st.vscale[0, h, :5].cpu().numpy().view(np.uint16), want["vscale"].view(np.uint16))
+
+
+@pytest.mark.parametrize("kind", ["hadamard", "dct"])
+def test_encode_with_rope_and_offsets_bit_exact(kind):
+    tile, n_kv = 64, 2
+    k, v, q = cfg0(7, 3 * tile, n_kv=n_kv)
+    cos, sin = R.rope_tables(4096, 128)
+    st = K().Sd1Store(1, n_kv, 10, tile, kind, DEV)
+    st.n_tiles = 4  # write at tiles 4..6, positions 1000..
+    K().sd1_encode(st, t(k), t(v), cos=t(cos), sin=t(sin), pos0=1000)
+    assert st.n_tiles == 7
+    for h in range(n_kv):
+        want = S.encode(k[:, h], v[:, h], tile, kind, cos=cos, sin=sin, pos0=1000)
+        assert np.array_equal(st.kbits[0, h, 4:7].cpu().numpy().view(np.uint32), want["kbits"])
+        assert np.array_equal(st.vbits[0, h, 4:7].cpu().numpy().view(np.uint32), want["vbits"])
+
+
+def _store(seed, n_tiles, tile=64, kind="hadamard", n_kv=8, n_q=32, B=1):
+    k, v, q = cfg0(seed, n_tiles * tile, n_kv=n_kv, n_q=n_q, B=B)
+    st = K().Sd1Store(B, n_kv, n_tiles + 3, tile, kind, DEV)
+    K().sd1_encode(st, t(k), t(v))
+    return st, k, v, q
+
+
+@pytest.mark.parametrize("kind,tile,g", [("hadamard", 64, 4), ("dct", 64, 4), ("dct", 32, 8), ("hadamard", 128, 1)])
+def test_tile_scores_and_selection_bit_exact(kind, tile, g):
+    n_kv, nt, B = 4, 40, 2
+    st, k, v, q = _store(11, nt, tile, kind, n_kv=n_kv, n_q=n_kv * g, B=B)
+    qb = t(q).to(torch.bfloat16)
+    qf = qb.float().cpu().numpy()
+    got = K().sd1_tile_scores(st, qb).cpu().numpy()
+    sel, sc, qp = K().sd1_select(st, qb, 7, 3, 9)
+    sel = sel.cpu().numpy()
+    for b in range(B):
+        qa = S.q_group_mean_f32(qf[b], n_kv)
+        qprime = S.transform(qa, kind)
+        for h in range(n_kv):
+            kb = st.kbits[b, h, :nt].cpu().numpy().view(np.uint32)
+            ks = st.kscale[b, h, :nt].cpu().numpy()
+            want = S.tile_scores(qprime[h], kb, ks)
+            assert bits_eq(got[b, h], want)
+            assert np.array_equal(sel[b, h], S.select_tiles(want, 7, 3, 9))
+        # per-head transformed queries for the attention kernel
+        np.testing.assert_allclose(qp[b].cpu().numpy(), S.transform(qf[b], kind), rtol=0, atol=0)
+
+
+def test_select_more_than_available_and_empty():
+    st, k, v, q = _store(3, 5)
+    sel, sc, _ = K().sd1_select(st, t(q), 8)
+    s = sel.cpu().numpy()
+    assert (s[..., 5:] == -1).all() and (np.sort(s[..., :5], -1) == np.arange(5)).all()
+    st.n_tiles = 0
+    sel, _, qp = K().sd1_select(st, t(q), 4)
+    assert (sel.cpu().numpy() == -1).all()
+
+
+def _oracle_attend(q, st, b, h, sel_row, win_k, win_v, nw, tail_k, tail_v, ntl, kind, g):
+    rows_k = [win_k[b, :nw, h].astype(np.float64), tail_k[b, :ntl, h].astype(np.float64)]
+    rows_v = [win_v[b, :nw, h].astype(np.float64), tail_v[b, :ntl, h].astype(np.float64)]
+    good = [s for s in sel_row if s >= 0]
+    if good:
+        dk = S.decode_tiles(st.kbits[b, h].cpu().numpy().view(np.uint32)[good], st.kscale[b, h].cpu().numpy()[good], kind)
+        dv = S.decode_tiles(st.vbits[b, h].cpu().numpy().view(np.uint32)[good], st.vscale[b, h].cpu().numpy()[good], kind)
+        rows_k.append(dk.reshape(-1, 128))
+        rows_v.append(dv.reshape(-1, 128))
+    return S.decode_attention(q[b, h * g:(h + 1) * g], np.concatenate(rows_k), np.concatenate(rows_v),
+                              np.empty((0, 128)), np.empty((0, 128)))
+
+
+@pytest.mark.parametrize("kind,tile,nw,ntl,g,B", [
+    ("hadamard", 64, 512, 17, 4, 1), ("dct", 64, 256, 0, 4, 2), ("dct", 32, 100, 31, 8, 1),
+    ("hadamard", 128, 0, 5, 4, 1), ("dct", 64, 1024, 63, 8, 1)])
+def test_attend_vs_oracle(kind, tile, nw, ntl, g, B):
+    n_kv, nt, k_sel = 4, 24, 6
+    st, k, v, q = _store(21, nt, tile, kind, n_kv=n_kv, n_q=n_kv * g, B=B)
+    rng = np.random.default_rng(1)
+    cap = max(nw, 1) + 3
+    win_k = rng.standard_normal((B, cap, n_kv, 128)).astype(np.float16)
+    win_v = rng.standard_normal((B, cap, n_kv, 128)).astype(np.float16)
+    tail_k = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    tail_v = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    qt = t(q)
+    sel, _, qp = K().sd1_select(st, qt, k_sel)
+    out = K().sd1_attend(st, qt, qp, sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                         out_dtype=torch.float32).cpu().numpy()
+    step = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl).cpu().numpy()
+    assert np.array_equal(out, step)
+    s = sel.cpu().numpy()
+    for b in range(B):
+        for h in range(n_kv):
+            want = _oracle_attend(q, st, b, h, s[b, h], win_k, win_v, nw, tail_k, tail_v, ntl, kind, g)
+            got = out[b, h * g:(h + 1) * g]
+            err = np.abs(got - want).max() / np.abs(want).max()
+            assert err < 1e-5, (b, h, err)
+
+
+def test_partial_rows_merge_like_whole():
+    """Sequence split: two halves of the selection -> partials -> kvr_lse_merge."""
+    st, k, v, q = _store(5, 30, n_kv=8, n_q=32)
+    qt = t(q)
+    sel, _, qp = K().sd1_select(st, qt, 8)
+    whole = K().sd1_attend(st, qt, qp, sel, out_dtype=torch.float32)
+    a, b = sel.clone(), sel.clone()
+    a[..., 4:] = -1
+    b[..., :4] = -1
+    pa = K().sd1_attend(st, qt, qp, a, partial=True)
+    pb = K().sd1_attend(st, qt, qp, b, partial=True)
+    merged = K().lse_merge(torch.stack([pa[0], pb[0]]))
+    np.testing.assert_allclose(merged.cpu().numpy(), whole[0].cpu().numpy(), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("kind", ["hadamard", "dct"])
+def test_decode_tiles_vs_oracle(kind):
+    st, k, v, q = _store(9, 12, kind=kind, n_kv=2, n_q=8)
+    sel = torch.tensor([[[3, 0, 11], [5, -1, 2]]], device=DEV)
+    dk, dv = K().sd1_decode_tiles(st, sel)
+    dk, dv = dk.cpu().numpy(), dv.float().cpu().numpy()
+    for h in range(2):
+        for j, s in enumerate(sel[0, h].tolist()):
+            rows = slice(j * 64, (j + 1) * 64)
+            if s < 0:
+                assert (dk[0, rows, h] == 0).all()
+                continue
+            wk = S.decode_tiles(st.kbits[0, h, [s]].cpu().numpy().view(np.uint32), st.kscale[0, h, [s]].cpu().numpy(), kind)[0]
+            np.testing.assert_allclose(dk[0, rows, h], wk, rtol=1e-5, atol=1e-5 * np.abs(wk).max())
+
+
+def test_full_size_config1_layer_sampled_parity():
+    """Config-1 shape (T = 32768 - 512 stored tokens, 8 heads, tile 64, DCT):
+    encode on the GPU, check 16 random tiles bit-exactly against the oracle and
+    the selection of every head against the oracle's scores."""
+    n_kv, tile, T = 8, 64, 32256
+    k, v, q = cfg0(1234, T, n_kv=n_kv)
+    kb16, vb16 = t(k).to(torch.bfloat16), t(v).to(torch.bfloat16)
+    st = K().Sd1Store(1, n_kv, T // tile, tile, "dct", DEV)
+    K().sd1_encode(st, kb16, vb16)
+    kf = kb16.float().cpu().numpy()
+    vf = vb16.float().cpu().numpy()
+    rng = np.random.default_rng(0)
+    for ti in rng.choice(T // tile, 16, replace=False):
+        h = int(rng.integers(n_kv))
+        rows = slice(ti * tile, (ti + 1) * tile)
+        want = S.encode(kf[rows, h], vf[rows, h], tile, "dct")
+        assert np.array_equal(st.kbits[0, h, ti].cpu().numpy().view(np.uint32), want["kbits"][0])
+        assert np.array_equal(st.vscale[0, h, ti].cpu().numpy().view(np.uint16), want["vscale"][0].view(np.uint16))
+    qb = t(q).to(torch.bfloat16)
+    sel, _, _ = K().sd1_select(st, qb, 16)
+    qa = S.q_group_mean_f32(qb.float().cpu().numpy(), n_kv)
+    qp = S.transform(qa, "dct")
+    for h in range(n_kv):
+        want = S.tile_scores(qp[h], st.kbits[0, h].cpu().numpy().view(np.uint32), st.kscale[0, h].cpu().numpy())
+        assert np.array_equal(sel[0, h].cpu().numpy(), S.select_tiles(want, 16))
+
+
+def test_retrieval_index_sd1_api():
+    from kvr_b200 import RetrievalIndex, WindowBuffer
+    n_kv, tile = 2, 64
+    k, v, q = cfg0(4, 1000, n_kv=n_kv, n_q=8)
+    cos, sin = R.rope_tables(2048, 128)
+    ri = RetrievalIndex(n_kv, 128, top_k=256, device=DEV, codec="sd1", tile=tile, transform="dct")
+    ri.set_rotary_tables(t(cos), t(sin))
+    ri.calibrate(t(k[:900]), t(v[:900]))
+    ri.batch_append(t(k[:900]), t(v[:900]))
+    assert (ri.n_stored, ri.n_tail) == (896, 4)
+    for i in range(900, 1000):
+        ri.append(t(k[i]), t(v[i]))
+    assert ri.n_tokens == 1000 and ri.n_stored == 960 and ri.n_tail == 40
+    # encoded tiles equal the oracle's encoding of the RoPE'd stream
+    for h in range(n_kv):
+        want = S.encode(k[:960, h], v[:960, h], tile, "dct", cos=cos, sin=sin, pos0=0)
+        got = ri.store.kbits[0, h, :15].cpu().numpy().view(np.uint32)
+        # tiles that passed through the fp16 tail were rounded to fp16 first
+        assert np.array_equal(got[:14], want["kbits"][:14])
+    rk, rv = ri.retrieve_topk(t(q), n_q=8)
+    assert rk.shape == (4 * tile + 40, n_kv, 128) and rv.dtype == torch.float16
+    wb = WindowBuffer(n_kv, 128, 128, DEV)
+    wb.batch_append(t(k[:128]), t(v[:128]))
+    out = ri.attend(t(q), wb)
+    want = K().decode_attn(t(q), [(wb.k, wb.v), (rk, rv)], out_dtype=torch.float32)
+    # the API returns V in fp16 (reference format), the fused path keeps it exact
+    np.testing.assert_allclose(out.cpu().numpy(), want.cpu().numpy(), rtol=3e-3, atol=3e-3)
