@@ -496,16 +496,17 @@ static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) 
   AttnWs w{};
   char *p = reinterpret_cast<char *>(base);
   const size_t rows = (size_t)batch * n_kv;
-  size_t off = 0;
-  w.err = reinterpret_cast<unsigned *>(p + off);
-  off += 256;
-  w.counters = reinterpret_cast<unsigned *>(p + off);
-  off += align_up(rows * 4, 256);
-  w.part = reinterpret_cast<float *>(p + off);
-  off += align_up(rows * (size_t)units * g * (kD + 2) * 4, 256);
-  w.bytes = off;
+  w.err = reinterpret_cast<unsigned *>(p);
+  w.counters = reinterpret_cast<unsigned *>(p + kWsAttnCounters);
+  w.part = reinterpret_cast<float *>(p + kWsHeader);
+  w.bytes = kWsHeader + align_up(rows * (size_t)units * g * (kD + 2) * 4, 256);
   return w;
 }
+
+int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                       const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
+                       int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
+                       float *qprime, unsigned *counters, float *scores, cudaStream_t st);
 
 int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what) {
   if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
@@ -570,6 +571,7 @@ extern "C" int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, in
     cudaMemsetAsync(out, 0, (size_t)n_q * d * dtype_size(out_dtype), as_cuda(stream));
     return check_launch("kvr_decode_attn (empty)");
   }
+  KVR_REQUIRE(n_kv <= kWsMaxRows, "kvr_decode_attn: n_kv > %d", kWsMaxRows);
   AttnWs w = attn_ws_layout(workspace, 1, n_kv, a.units, a.g);
   KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_decode_attn: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
   a.err = w.err; a.counters = w.counters; a.part = w.part;
@@ -631,16 +633,18 @@ extern "C" int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, i
     cudaMemsetAsync(out, 0, (size_t)batch * n_q * kD * dtype_size(out_dtype), st);
     return check_launch("kvr_sd1_attend (empty)");
   }
+  KVR_REQUIRE((int64_t)batch * n_kv <= kWsMaxRows, "kvr_sd1_attend: batch*n_kv > %d", kWsMaxRows);
   AttnWs w = attn_ws_layout(workspace, batch, n_kv, a.units, a.g);
   KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_sd1_attend: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
   a.err = w.err; a.counters = w.counters; a.part = w.part;
   return launch_attn(a, batch, as_cuda(stream), "kvr_sd1_attend");
 }
 
+// decode_step layout: [header | attention partials | tile scores | sel | qprime]
 extern "C" size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,
                                           int64_t n_win, int64_t n_tail) {
   const size_t a = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
-  const size_t s = align_up(kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles), 256);
+  const size_t s = align_up((size_t)batch * n_kv * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
   const size_t sel = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);
   const size_t qp = align_up((size_t)batch * n_q * kD * 4, 256);
   return a + s + sel + qp;
@@ -661,18 +665,18 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_decode_step: workspace must be 256-byte aligned");
   char *p = reinterpret_cast<char *>(workspace);
   const size_t a_bytes = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
-  const size_t s_bytes = align_up(kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles), 256);
+  const size_t s_bytes = align_up((size_t)batch * n_kv * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
   const size_t sel_bytes = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);
-  void *ws_attn = p;
-  void *ws_sel = p + a_bytes;
+  float *scores = reinterpret_cast<float *>(p + a_bytes);
   int32_t *sel = sel_out ? sel_out : reinterpret_cast<int32_t *>(p + a_bytes + s_bytes);
   float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
-  int rc = kvr_sd1_select(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
-                          ex_t1, 0, sel, nullptr, qprime, ws_sel, s_bytes, stream);
+  int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
+                              ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
+                              as_cuda(stream));
   if (rc) return rc;
   return kvr_sd1_attend(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
                         kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
-                        ws_attn, a_bytes, stream);
+                        workspace, a_bytes, stream);
 }
 
 extern "C" int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,

@@ -113,6 +113,17 @@ __device__ __forceinline__ float key_float(uint32_t k) {
   return __uint_as_float(u);
 }
 
+// Every workspace starts with the same fixed header, so that no change of
+// shapes between calls can move a counter onto stale data:
+//   [0, 256)                         error word
+//   [kWsSelCounters, +4*kWsMaxRows)  per-(b, h) counters of the selection kernel
+//   [kWsAttnCounters, +4*kWsMaxRows) per-(b, h) counters of the attention kernel
+// The counters are zero on entry and reset to zero by the kernel that used them.
+constexpr int kWsMaxRows = 4096;  // batch * n_kv
+constexpr size_t kWsSelCounters = 256;
+constexpr size_t kWsAttnCounters = kWsSelCounters + 4 * kWsMaxRows;
+constexpr size_t kWsHeader = kWsAttnCounters + 4 * kWsMaxRows;
+
 // Bound on device-side spin iterations (each iteration also sleeps ~64 ns).
 constexpr uint32_t kSpinLimit = 1u << 22;
 

@@ -473,9 +473,31 @@ extern "C" int kvr_sd1_tile_scores(const void *q, int q_dtype, int batch, int n_
                          nullptr, sa, 0, as_cuda(stream));
 }
 
+namespace kvr {
+// Selection with explicit scratch: counters (B*n_kv) and scores (B*n_kv*n_tiles).
+int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
+                       const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
+                       int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
+                       float *qprime, unsigned *counters, float *scores, cudaStream_t st) {
+  int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
+  if (rc) return rc;
+  KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
+  KVR_REQUIRE(q && sel && qprime, "kvr_sd1_select: null pointer");
+  KVR_REQUIRE(k_sel >= 0 && k_sel <= 4096, "kvr_sd1_select: k_sel must be in [0, 4096]");
+  KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_select: n_tiles > nt_cap");
+  KVR_REQUIRE(n_tiles == 0 || (kbits && kscale), "kvr_sd1_select: null store pointers");
+  KVR_REQUIRE((int64_t)batch * n_kv <= kWsMaxRows, "kvr_sd1_select: batch*n_kv > %d", kWsMaxRows);
+  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters};
+  // With no full tile there is nothing to score; the kernel still forms q'
+  // and writes an all-empty selection.
+  return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
+                         sa, 1, st);
+}
+}  // namespace kvr
+
 extern "C" size_t kvr_sd1_select_workspace_bytes(int batch, int n_kv, int64_t n_tiles) {
   const size_t rows = (size_t)batch * n_kv;
-  return align_up(rows * 4, 256) + align_up(rows * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
+  return kWsHeader + align_up(rows * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
 }
 
 extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
@@ -483,25 +505,15 @@ extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, in
                               int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                               float *qprime, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
   clear_error();
-  int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
-  if (rc) return rc;
-  KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
-  KVR_REQUIRE(q && sel && qprime && workspace, "kvr_sd1_select: null pointer");
-  KVR_REQUIRE(k_sel >= 0 && k_sel <= 4096, "kvr_sd1_select: k_sel must be in [0, 4096]");
-  KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_select: n_tiles > nt_cap");
-  KVR_REQUIRE(n_tiles == 0 || (kbits && kscale), "kvr_sd1_select: null store pointers");
+  KVR_REQUIRE(workspace, "kvr_sd1_select: null workspace");
+  KVR_REQUIRE(batch > 0 && n_kv > 0, "kvr_sd1_select: bad batch/head counts");
   const size_t need = kvr_sd1_select_workspace_bytes(batch, n_kv, n_tiles);
   KVR_REQUIRE(workspace_bytes >= need, "kvr_sd1_select: workspace %zu < %zu bytes", workspace_bytes, need);
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_select: workspace must be 256-byte aligned");
-  cudaStream_t st = as_cuda(stream);
-  const size_t rows = (size_t)batch * n_kv;
-  unsigned *counters = reinterpret_cast<unsigned *>(workspace);
-  float *scores = reinterpret_cast<float *>(reinterpret_cast<char *>(workspace) + align_up(rows * 4, 256));
-  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters};
-  // With no full tile there is nothing to score; the kernel still forms q'
-  // and writes an all-empty selection.
-  return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
-                         sa, 1, st);
+  char *p = reinterpret_cast<char *>(workspace);
+  return sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
+                            ex_t1, tile_base, sel, sel_scores, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters),
+                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream));
 }
 
 extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,

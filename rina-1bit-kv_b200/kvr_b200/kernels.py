@@ -142,8 +142,8 @@ def window_write(k, v, ring_k, ring_v, pos: int):
         v = v.to(k.dtype)
     n = k.shape[0]
     n_kv, d = ring_k.shape[1], ring_k.shape[2]
-    call("kvr_window_write", ptr(k), dtype_code(k), n, n_kv, d, ptr(ring_k), ptr(ring_v), ring_k.shape[0], pos,
-         stream())
+    call("kvr_window_write", ptr(k), ptr(v), dtype_code(k), n, n_kv, d, ptr(ring_k), ptr(ring_v), ring_k.shape[0],
+         pos, stream())
 
 
 # -------------------------------------------------------------- attention --
