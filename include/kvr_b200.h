@@ -240,6 +240,25 @@ KVR_API int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, 
 KVR_API int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,
                   kvr_stream_t stream);
 
+/* Allocation-free variant of kvr_decode_attn (no counterpart in the
+ * reference).  For callers that cannot allocate device memory — a plugin
+ * inside a host that owns the GPU heap, or a path where cudaMalloc would
+ * stall or is forbidden — it takes no workspace: its scratch is a fixed
+ * 2 MiB device array inside the library (kvr_decode_attn_noalloc_max_scratch_bytes),
+ * held on every GPU that loads the library until the process exits.  A call
+ * whose scratch need (kvr_decode_attn_workspace_bytes) exceeds it returns
+ * KVR_EINVAL.  It calls no cudaMalloc/cudaFree.  The first call on each device
+ * looks up the array's device address with that device current; make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other host threads) race and
+ * must be serialised by the caller.  Arguments as kvr_decode_attn. */
+KVR_API size_t kvr_decode_attn_noalloc_max_scratch_bytes(void);
+KVR_API int kvr_decode_attn_noalloc(const void *q, int q_dtype, int n_q, int n_kv, int d,
+                                    const void *k0, const void *v0, int kdt0, int vdt0, int64_t n0,
+                                    int64_t tok_stride0, const void *k1, const void *v1, int kdt1, int vdt1,
+                                    int64_t n1, int64_t tok_stride1, float scale, void *out, int out_dtype,
+                                    kvr_stream_t stream);
+
 /* Synchronises `stream`, then reads and clears the error word every workspace
  * starts with: KVR_ETIMEOUT if a bounded device-side wait of an earlier call
  * using this workspace gave up, else KVR_OK. */

@@ -17,6 +17,8 @@
 #include "kvr_common.cuh"
 #include "kvr_transform.cuh"
 
+#include <mutex>
+
 namespace kvr {
 
 constexpr int kChunk = 64;
@@ -701,4 +703,91 @@ extern "C" int kvr_workspace_status(const void *workspace, kvr_stream_t stream) 
     return set_error(KVR_ETIMEOUT, "a bounded device-side wait gave up (flag %u)", flag);
   }
   return KVR_OK;
+}
+
+// ------------------------------------------------- allocation-free variant ----
+// Some callers cannot allocate device memory at all: plugins that run inside a
+// host whose allocator owns the whole GPU heap, or code on a path where a
+// cudaMalloc would stall the device or break a latency budget.  For them,
+// kvr_decode_attn_noalloc keeps its scratch (error word, per-head counters and
+// log-sum-exp partials) in this fixed array, which every GPU that loads the
+// library holds until the process exits.
+namespace kvr {
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static void *g_scratch_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_scratch_mu;
+
+// Device address of g_attn_scratch on the current device (looked up once per
+// device; the name itself is only a host-side stand-in).
+static int scratch_address(void **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("kvr_decode_attn_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return set_error(KVR_ENOTSUP, "kvr_decode_attn_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess)
+      return set_error(KVR_ECUDA, "kvr_decode_attn_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return KVR_OK;
+}
+}  // namespace kvr
+
+extern "C" size_t kvr_decode_attn_noalloc_max_scratch_bytes(void) { return kvr::kNoAllocScratchBytes; }
+
+extern "C" int kvr_decode_attn_noalloc(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0,
+                                       const void *v0, int kdt0, int vdt0, int64_t n0, int64_t tok_stride0,
+                                       const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1,
+                                       int64_t tok_stride1, float scale, void *out, int out_dtype,
+                                       kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == kD, "kvr_decode_attn_noalloc: head_dim must be 128 (got %d)", d);
+  KVR_REQUIRE(n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
+              "kvr_decode_attn_noalloc: need n_q %% n_kv == 0 and n_q/n_kv <= 8 (n_q=%d n_kv=%d)", n_q, n_kv);
+  KVR_REQUIRE(n_kv <= kWsMaxRows, "kvr_decode_attn_noalloc: n_kv > %d", kWsMaxRows);
+  KVR_REQUIRE(valid_dtype(q_dtype) && valid_dtype(out_dtype), "kvr_decode_attn_noalloc: bad q/out dtype");
+  KVR_REQUIRE(q && out, "kvr_decode_attn_noalloc: null pointer");
+  KVR_REQUIRE(n0 >= 0 && n1 >= 0, "kvr_decode_attn_noalloc: negative token count");
+  KVR_REQUIRE(n0 == 0 || (k0 && v0 && valid_dtype(kdt0) && valid_dtype(vdt0) && tok_stride0 % 4 == 0),
+              "kvr_decode_attn_noalloc: bad segment 0");
+  KVR_REQUIRE(n1 == 0 || (k1 && v1 && valid_dtype(kdt1) && valid_dtype(vdt1) && tok_stride1 % 4 == 0),
+              "kvr_decode_attn_noalloc: bad segment 1");
+  AttnArgs a{};
+  a.q = q; a.q_dt = q_dtype; a.n_q = n_q; a.n_kv = n_kv; a.g = n_q / n_kv;
+  a.inv_scale = (float)(1.0 / (scale > 0.f ? (double)scale : sqrt((double)d)));
+  a.k[0] = k0; a.v[0] = v0; a.kdt[0] = kdt0; a.vdt[0] = vdt0; a.n[0] = n0; a.tok_stride[0] = tok_stride0;
+  a.k[1] = k1; a.v[1] = v1; a.kdt[1] = kdt1; a.vdt[1] = vdt1; a.n[1] = n1; a.tok_stride[1] = tok_stride1;
+  a.nchunk[0] = (int)((n0 + kChunk - 1) / kChunk);
+  a.nchunk[1] = (int)((n1 + kChunk - 1) / kChunk);
+  a.units = a.nchunk[0] + a.nchunk[1];
+  a.tile = 64; a.kind = KVR_HADAMARD;
+  a.out = out; a.out_dt = out_dtype;
+  cudaStream_t st = as_cuda(stream);
+  if (a.units == 0) {
+    cudaMemsetAsync(out, 0, (size_t)n_q * d * dtype_size(out_dtype), st);
+    return check_launch("kvr_decode_attn_noalloc (empty)");
+  }
+  const size_t need = attn_ws_layout(nullptr, 1, n_kv, a.units, a.g).bytes;
+  if (need > kNoAllocScratchBytes)
+    return set_error(KVR_EINVAL,
+                     "kvr_decode_attn_noalloc: this call needs %zu bytes of scratch, the built-in maximum is %zu "
+                     "(fewer tokens or heads per call, or use kvr_decode_attn with a caller workspace)",
+                     need, kNoAllocScratchBytes);
+  void *base = nullptr;
+  int rc = scratch_address(&base);
+  if (rc) return rc;
+  // The array keeps whatever the previous call left: zero the error word and
+  // this call's counters, which must start at zero.
+  if (cudaMemsetAsync(base, 0, 4, st) != cudaSuccess ||
+      cudaMemsetAsync(static_cast<char *>(base) + kWsAttnCounters, 0, (size_t)n_kv * 4, st) != cudaSuccess)
+    return check_launch("kvr_decode_attn_noalloc: clearing scratch");
+  AttnWs w = attn_ws_layout(base, 1, n_kv, a.units, a.g);
+  a.err = w.err; a.counters = w.counters; a.part = w.part;
+  return launch_attn(a, 1, st, "kvr_decode_attn_noalloc");
 }

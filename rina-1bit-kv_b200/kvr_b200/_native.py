@@ -59,6 +59,8 @@ SIGNATURES = {
                                 F, P, I, P, P, SZ, P]),
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),
     "kvr_workspace_status": (I, [P, P]),
+    "kvr_decode_attn_noalloc_max_scratch_bytes": (SZ, []),
+    "kvr_decode_attn_noalloc": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, F, P, I, P]),
 }
 
 _lib = None
