@@ -24,6 +24,9 @@ namespace kvr {
 constexpr int kChunk = 64;
 constexpr int kMaxG = 8;
 constexpr int kKsStride = kD + 4;  // padded fp32 row of the staged K chunk
+// workspace partial row: [m, l, pad, pad, o_0 .. o_127] (16-byte aligned o)
+constexpr int kPartStride = kD + 4;
+constexpr int kPartO = 4;
 
 struct AttnArgs {
   const void *q;
@@ -57,6 +60,30 @@ __device__ __forceinline__ void load4_rt(const void *p, int64_t i, int dt, float
   else if (dt == KVR_F16) load4<KVR_F16>(p, i, x);
   else load4<KVR_BF16>(p, i, x);
 }
+
+// Raw 4-element load (16 bytes for fp32, 8 bytes for 16-bit types) and its
+// widening to fp32; split so that many loads can be in flight at once.
+__device__ __forceinline__ uint4 raw4(const void *p, int64_t i, int dt) {
+  if (dt == KVR_F32) return __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(p) + i));
+  const uint2 u = __ldg(reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(p) + i));
+  return make_uint4(u.x, u.y, 0u, 0u);
+}
+__device__ __forceinline__ float4 cvt4(uint4 r, int dt) {
+  if (dt == KVR_F32) return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                                        __uint_as_float(r.w));
+  if (dt == KVR_F16) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&r.x));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&r.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  }
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.x));
+  const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.y));
+  return make_float4(a.x, a.y, c.x, c.y);
+}
+
+// Programmatic dependent launch: wait for the preceding grid (a no-op when
+// the kernel was not launched as a dependent), and let dependents start.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---- mbarrier + bulk copy (PTX)
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -114,7 +141,8 @@ struct AttnSmem {
   static constexpr int kML = kP + 128 * kMaxG * 4;                   // fp32 [8][2]
   static constexpr int kBar = kML + kMaxG * 2 * 4;                   // u64
   static constexpr int kFlag = kBar + 16;
-  static constexpr int kTotal = kFlag + 16;
+  static constexpr int kLee = kFlag + 16;                             // fp32 [128] DCT factors
+  static constexpr int kTotal = kLee + kD * 4;
 };
 
 // Softmax over the scores S[hq][0..nt) of every query head; writes P[j][hq],
@@ -141,12 +169,12 @@ __device__ __forceinline__ void softmax_rows(const AttnArgs &a, int nt, const fl
 }
 
 __device__ __forceinline__ float *part_row(const AttnArgs &a, int64_t row, int u, int hq) {
-  return a.part + (((row * a.units + u) * a.g) + hq) * (int64_t)(kD + 2);
+  return a.part + (((row * a.units + u) * a.g) + hq) * (int64_t)kPartStride;
 }
 
 __device__ void write_empty_partial(const AttnArgs &a, int64_t row, int u) {
-  for (int i = threadIdx.x; i < a.g * (kD + 2); i += blockDim.x) {
-    const int hq = i / (kD + 2), c = i - hq * (kD + 2);
+  for (int i = threadIdx.x; i < a.g * kPartStride; i += blockDim.x) {
+    const int hq = i / kPartStride, c = i - hq * kPartStride;
     part_row(a, row, u, hq)[c] = c == 0 ? -INFINITY : 0.0f;
   }
 }
@@ -164,46 +192,57 @@ __device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int 
   const int64_t t0 = (int64_t)chunk * kChunk;
   const int nt = (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk);
 
-  // stage q (scaled) and the K/V chunk as fp32
-  for (int i = tid; i < a.g * 32; i += blockDim.x) {
-    const int hq = i >> 5, qd = i & 31;
-    float x[4];
-    load4_rt(a.q, (b * a.n_q + (int64_t)h * a.g + hq) * kD + qd * 4, a.q_dt, x);
-    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] =
-        make_float4(x[0] * a.inv_scale, x[1] * a.inv_scale, x[2] * a.inv_scale, x[3] * a.inv_scale);
-  }
+  // Stage q (scaled) and the K/V chunk as fp32: every global load of the
+  // chunk is issued before the first shared-memory store, so the chunk
+  // arrives in one DRAM round trip.
   const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD;
-  for (int i = tid; i < kChunk * 32; i += blockDim.x) {
-    const int j = i >> 5, qd = i & 31;
-    float xk[4] = {0.f, 0.f, 0.f, 0.f}, xv[4] = {0.f, 0.f, 0.f, 0.f};
+  const int kdt = a.kdt[seg], vdt = a.vdt[seg];
+  uint4 rk[8], rv[8], rq = make_uint4(0u, 0u, 0u, 0u);
+  const bool has_q = tid < a.g * 32;
+  if (has_q) rq = raw4(a.q, (b * a.n_q + (int64_t)h * a.g + (tid >> 5)) * kD + (tid & 31) * 4, a.q_dt);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = tid + i * 256, j = idx >> 5, qd = idx & 31;
+    rk[i] = rv[i] = make_uint4(0u, 0u, 0u, 0u);
     if (j < nt) {
       const int64_t off = base + (t0 + j) * a.tok_stride[seg] + qd * 4;
-      load4_rt(a.k[seg], off, a.kdt[seg], xk);
-      load4_rt(a.v[seg], off, a.vdt[seg], xv);
+      rk[i] = raw4(a.k[seg], off, kdt);
+      rv[i] = raw4(a.v[seg], off, vdt);
     }
-    *reinterpret_cast<float4 *>(Ks + j * kKsStride + qd * 4) = make_float4(xk[0], xk[1], xk[2], xk[3]);
-    *reinterpret_cast<float4 *>(Vs + j * kD + qd * 4) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+  }
+  if (has_q) {
+    const float4 x = cvt4(rq, a.q_dt);
+    reinterpret_cast<float4 *>(Qs + (tid >> 5) * kD)[tid & 31] =
+        make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int idx = tid + i * 256, j = idx >> 5, qd = idx & 31;
+    *reinterpret_cast<float4 *>(Ks + j * kKsStride + qd * 4) = cvt4(rk[i], kdt);
+    *reinterpret_cast<float4 *>(Vs + j * kD + qd * 4) = cvt4(rv[i], vdt);
   }
   __syncthreads();
+  KVR_TRACE_POINT(1, 1);
   // scores: (hq, 32-token block) pairs, lane = token
   for (int p = warp; p < a.g * 2; p += 8) {
     const int hq = p >> 1, j = (p & 1) * 32 + lane;
     const float4 *kr = reinterpret_cast<const float4 *>(Ks + j * kKsStride);
     const float4 *qr = reinterpret_cast<const float4 *>(Qs + hq * kD);
-    float acc = 0.0f;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll 8
     for (int c = 0; c < 32; ++c) {
       const float4 kk = kr[c], qq = qr[c];
-      acc = fmaf(qq.x, kk.x, acc);
-      acc = fmaf(qq.y, kk.y, acc);
-      acc = fmaf(qq.z, kk.z, acc);
-      acc = fmaf(qq.w, kk.w, acc);
+      a0 = fmaf(qq.x, kk.x, a0);
+      a1 = fmaf(qq.y, kk.y, a1);
+      a2 = fmaf(qq.z, kk.z, a2);
+      a3 = fmaf(qq.w, kk.w, a3);
     }
-    S[hq * kD + j] = j < nt ? acc : -INFINITY;
+    S[hq * kD + j] = j < nt ? (a0 + a1) + (a2 + a3) : -INFINITY;
   }
   __syncthreads();
   softmax_rows(a, nt, S, P, ML);
   __syncthreads();
+  KVR_TRACE_POINT(1, 2);
   // P.V: thread = (channel, token half)
   const int c = tid & 127, half = tid >> 7;
   float o[kMaxG];
@@ -226,7 +265,7 @@ __device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int 
   if (half == 0) {
     for (int hq = 0; hq < a.g; ++hq) {
       float *pr = part_row(a, row, u, hq);
-      pr[2 + c] = o[hq] + S[hq * kD + c];
+      pr[kPartO + c] = o[hq] + S[hq * kD + c];
       if (c == 0) {
         pr[0] = ML[hq * 2];
         pr[1] = ML[hq * 2 + 1];
@@ -251,6 +290,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   int *flag = reinterpret_cast<int *>(sm + AttnSmem::kFlag);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = b * a.n_kv + h;
+  griddep_wait();  // sel and qprime come from the selection kernel
   const int32_t t = a.sel[row * a.k_sel + slot];
   if (t < 0) {
     write_empty_partial(a, row, u);
@@ -276,6 +316,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
         make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
   }
   __syncthreads();  // barrier initialised, Qs staged
+  KVR_TRACE_POINT(1, 1);
   if (!mbar_wait_bounded(bar, 0)) {
     atomicOr(a.err, 1u);
     flag[0] = 0;  // benign race: every thread that fails writes 0
@@ -309,14 +350,15 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
     const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[j];
     const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
     const float *L = LUT + hq * 32 * 16;
-    float acc = 0.0f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int grp = 0; grp < 32; ++grp) acc += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
-    S[hq * kD + j] = acc;
+    for (int grp = 0; grp < 32; ++grp) acc[grp & 3] += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
+    S[hq * kD + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
   __syncthreads();
   softmax_rows(a, TILE, S, P, ML);
   __syncthreads();
+  KVR_TRACE_POINT(1, 2);
   const int c = tid & 127, half = tid >> 7;
   float o[kMaxG];
 #pragma unroll
@@ -341,7 +383,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
     for (int hq = 0; hq < a.g; ++hq) {
       float *pr = part_row(a, row, u, hq);
       const float l = ML[hq * 2 + 1];
-      pr[2 + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - l);
+      pr[kPartO + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - l);
       if (c == 0) {
         pr[0] = ML[hq * 2];
         pr[1] = l;
@@ -361,15 +403,28 @@ __device__ void merge_group(const AttnArgs &a, unsigned char *sm, int64_t b, int
   float *Ex = W + U * kMaxG;
   float *Tr = Ex + kMaxG * kD;
   float *buf = Tr + kMaxG * kD;
-  float *lee = buf + 8 * 2 * kD;
+  const float *lee = reinterpret_cast<const float *>(sm + AttnSmem::kLee);  // loaded at kernel start
   float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);  // [g] (M, L)
-  load_lee(lee);
   for (int hq = warp; hq < a.g; hq += 8) {
-    float mx = -INFINITY;
-    for (int u = lane; u < U; u += 32) mx = fmaxf(mx, __ldcg(part_row(a, row, u, hq)));
+    // (m, l) of up to 64 units per lane pass, read once as float2
+    float2 ml[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int u = lane + 32 * r;
+      ml[r] = u < U ? __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, u, hq))) : make_float2(-INFINITY, 0.f);
+    }
+    float mx = warp_max(fmaxf(ml[0].x, ml[1].x));
+    for (int u = lane + 64; u < U; u += 32) mx = fmaxf(mx, __ldcg(part_row(a, row, u, hq)));
     mx = warp_max(mx);
     float l = 0.0f;
-    for (int u = lane; u < U; u += 32) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int u = lane + 32 * r;
+      const float w = (ml[r].x == -INFINITY) ? 0.0f : expf(ml[r].x - mx);
+      if (u < U) W[u * kMaxG + hq] = w;
+      l += w * ml[r].y;
+    }
+    for (int u = lane + 64; u < U; u += 32) {
       const float *pr = part_row(a, row, u, hq);
       const float mu = __ldcg(pr);
       const float w = (mu == -INFINITY) ? 0.0f : expf(mu - mx);
@@ -383,20 +438,52 @@ __device__ void merge_group(const AttnArgs &a, unsigned char *sm, int64_t b, int
     }
   }
   __syncthreads();
-  for (int i = tid; i < a.g * kD; i += blockDim.x) {
-    const int hq = i >> 7, c = i & 127;
-    float ex = 0.0f, tr = 0.0f;
-    for (int u = 0; u < U; ++u) {
-      const float w = W[u * kMaxG + hq];
-      if (w == 0.0f) continue;
-      const float o = __ldcg(part_row(a, row, u, hq) + 2 + c);
-      if (u < n_exact) ex = fmaf(w, o, ex);
-      else tr = fmaf(w, o, tr);
+  // thread -> (head, 4-channel group, slice of the units); partial rows are
+  // read as float4 in unrolled batches so the loads overlap
+  {
+    const int pairs = a.g * 32;
+    const int nparts = blockDim.x / pairs;  // 2 for g = 4, 1 for g = 8
+    const int p = tid % pairs, part = tid / pairs;
+    const int hq = p >> 5, c4 = p & 31;
+    float4 ex = make_float4(0.f, 0.f, 0.f, 0.f), tr = ex;
+    if (part < nparts) {
+      constexpr int UB = 8;
+      for (int u0 = part; u0 < U; u0 += UB * nparts) {
+        float4 o[UB];
+#pragma unroll
+        for (int k = 0; k < UB; ++k) {
+          const int u = u0 + k * nparts;
+          o[k] = u < U ? __ldcg(reinterpret_cast<const float4 *>(part_row(a, row, u, hq) + kPartO) + c4)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < UB; ++k) {
+          const int u = u0 + k * nparts;
+          if (u >= U) break;
+          const float w = W[u * kMaxG + hq];
+          float4 &acc = u < n_exact ? ex : tr;
+          acc.x = fmaf(w, o[k].x, acc.x); acc.y = fmaf(w, o[k].y, acc.y);
+          acc.z = fmaf(w, o[k].z, acc.z); acc.w = fmaf(w, o[k].w, acc.w);
+        }
+      }
     }
-    Ex[hq * kD + c] = ex;
-    Tr[hq * kD + c] = tr;
+    // combine the unit slices through shared memory (Ex/Tr rows, part 0 first)
+    for (int q = 0; q < nparts; ++q) {
+      if (part == q) {
+        float4 *e = reinterpret_cast<float4 *>(Ex + hq * kD) + c4;
+        float4 *t = reinterpret_cast<float4 *>(Tr + hq * kD) + c4;
+        if (q == 0) {
+          *e = ex;
+          *t = tr;
+        } else {
+          float4 e0 = *e, t0 = *t;
+          *e = make_float4(e0.x + ex.x, e0.y + ex.y, e0.z + ex.z, e0.w + ex.w);
+          *t = make_float4(t0.x + tr.x, t0.y + tr.y, t0.z + tr.z, t0.w + tr.w);
+        }
+      }
+      __syncthreads();
+    }
   }
-  __syncthreads();
   const bool any_tiles = U > n_exact;
   for (int hq = warp; hq < a.g; hq += 8) {
     float x[4];
@@ -435,6 +522,8 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   const int u = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int64_t row = b * a.n_kv + h;
+  KVR_TRACE_POINT(1, 0);
+  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));  // visible after the unit's barriers
   if (u < a.nchunk[0]) {
     exact_unit(a, sm, b, h, 0, u, u);
   } else if (u < a.nchunk[0] + a.nchunk[1]) {
@@ -443,6 +532,7 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
     tile_unit<TILE>(a, sm, b, h, u - a.nchunk[0] - a.nchunk[1], u);
   }
   __syncthreads();
+  KVR_TRACE_POINT(1, 3);
   int *last = reinterpret_cast<int *>(sm + AttnSmem::kFlag) + 1;
   if (threadIdx.x == 0) {
     __threadfence();
@@ -452,7 +542,9 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!*last) return;
   __threadfence();
+  KVR_TRACE_POINT(1, 4);
   merge_group(a, sm, b, h);
+  KVR_TRACE_POINT(1, 5);
   if (threadIdx.x == 0) a.counters[row] = 0u;
 }
 
@@ -501,7 +593,7 @@ static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) 
   w.err = reinterpret_cast<unsigned *>(p);
   w.counters = reinterpret_cast<unsigned *>(p + kWsAttnCounters);
   w.part = reinterpret_cast<float *>(p + kWsHeader);
-  w.bytes = kWsHeader + align_up(rows * (size_t)units * g * (kD + 2) * 4, 256);
+  w.bytes = kWsHeader + align_up(rows * (size_t)units * g * kPartStride * 4, 256);
   return w;
 }
 
@@ -510,17 +602,39 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                        float *qprime, unsigned *counters, float *scores, cudaStream_t st);
 
-int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what) {
+int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool pdl = false) {
   if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
   size_t smem = AttnSmem::kTotal;
   const size_t ms = merge_smem_bytes(a.units);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
   dim3 grid(a.units, a.n_kv, batch);
+  // per-device attribute cache (the attribute is per function and device)
+  static thread_local int cached_dev = -1;
+  static thread_local bool smem_set[3] = {false, false, false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    smem_set[0] = smem_set[1] = smem_set[2] = false;
+    cached_dev = dev;
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   switch (a.tile) {
 #define KVR_AT(T)                                                                                  \
   case T:                                                                                          \
-    cudaFuncSetAttribute(attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
-    attn_kernel<T><<<grid, 256, smem, st>>>(a);                                                    \
+    if (!smem_set[T / 64]) {                                                                       \
+      cudaFuncSetAttribute(attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+      smem_set[T / 64] = true;                                                                     \
+    }                                                                                              \
+    cfg.gridDim = grid;                                                                            \
+    cfg.blockDim = dim3(256);                                                                      \
+    cfg.dynamicSmemBytes = smem;                                                                   \
+    cfg.stream = st;                                                                               \
+    cfg.attrs = attr;                                                                              \
+    cfg.numAttrs = pdl ? 1 : 0;                                                                    \
+    if (cudaLaunchKernelEx(&cfg, attn_kernel<T>, a) != cudaSuccess) return check_launch(what);     \
     break;
     KVR_AT(32)
     KVR_AT(64)
@@ -591,14 +705,13 @@ extern "C" size_t kvr_sd1_attend_workspace_bytes(int batch, int n_q, int n_kv, i
   return attn_ws_layout(nullptr, batch, n_kv, sd1_units(n_win, n_tail, k_sel), n_q / n_kv).bytes;
 }
 
-extern "C" int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int batch, int n_q, int n_kv,
-                              const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
-                              const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
-                              const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
-                              int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out,
-                              int out_dtype, float *partial_out, void *workspace, size_t workspace_bytes,
-                              kvr_stream_t stream) {
-  clear_error();
+static int sd1_attend_impl(const void *q, int q_dtype, const float *qprime, int batch, int n_q, int n_kv,
+                           const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                           const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
+                           const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
+                           int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out,
+                           int out_dtype, float *partial_out, void *workspace, size_t workspace_bytes,
+                           kvr_stream_t stream, bool pdl) {
   KVR_REQUIRE(batch > 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
               "kvr_sd1_attend: need n_q %% n_kv == 0 and n_q/n_kv <= 8");
   KVR_REQUIRE(tile == 32 || tile == 64 || tile == 128, "kvr_sd1_attend: tile must be 32, 64 or 128");
@@ -639,7 +752,20 @@ extern "C" int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, i
   AttnWs w = attn_ws_layout(workspace, batch, n_kv, a.units, a.g);
   KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_sd1_attend: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
   a.err = w.err; a.counters = w.counters; a.part = w.part;
-  return launch_attn(a, batch, as_cuda(stream), "kvr_sd1_attend");
+  return launch_attn(a, batch, as_cuda(stream), "kvr_sd1_attend", pdl);
+}
+
+extern "C" int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int batch, int n_q, int n_kv,
+                              const uint16_t *win_k, const uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                              const uint16_t *tail_k, const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits,
+                              const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
+                              int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out,
+                              int out_dtype, float *partial_out, void *workspace, size_t workspace_bytes,
+                              kvr_stream_t stream) {
+  clear_error();
+  return sd1_attend_impl(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
+                         kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype,
+                         partial_out, workspace, workspace_bytes, stream, false);
 }
 
 // decode_step layout: [header | attention partials | tile scores | sel | qprime]
@@ -676,10 +802,18 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
                               as_cuda(stream));
   if (rc) return rc;
-  return kvr_sd1_attend(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
-                        kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
-                        workspace, a_bytes, stream);
+  // the attention kernel is a programmatic dependent of the selection
+  // kernel: its window/tail units overlap the tile scan, its tile units wait
+  return sd1_attend_impl(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
+                         kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
+                         workspace, a_bytes, stream, true);
 }
+
+#ifdef KVR_TRACE
+extern "C" KVR_API int kvr_debug_trace_attn(unsigned long long *host, int n) {
+  return cudaMemcpyFromSymbol(host, kvr::g_kvr_trace, sizeof(unsigned long long) * n) == cudaSuccess ? 0 : 2;
+}
+#endif
 
 extern "C" int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,
                              kvr_stream_t stream) {

@@ -124,6 +124,22 @@ constexpr size_t kWsSelCounters = 256;
 constexpr size_t kWsAttnCounters = kWsSelCounters + 4 * kWsMaxRows;
 constexpr size_t kWsHeader = kWsAttnCounters + 4 * kWsMaxRows;
 
+// Optional phase timestamps for latency studies (compiled only with -DKVR_TRACE).
+#ifdef KVR_TRACE
+static __device__ unsigned long long g_kvr_trace[1 << 16];  // one copy per translation unit
+__device__ __forceinline__ void kvr_trace(int kernel, int point) {
+  if (threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const unsigned blk = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (blk < 2048) g_kvr_trace[(kernel * 2048 + blk) * 8 + point] = t;
+  }
+}
+#define KVR_TRACE_POINT(k, p) ::kvr::kvr_trace(k, p)
+#else
+#define KVR_TRACE_POINT(k, p) ((void)0)
+#endif
+
 // Bound on device-side spin iterations (each iteration also sleeps ~64 ns).
 constexpr uint32_t kSpinLimit = 1u << 22;
 

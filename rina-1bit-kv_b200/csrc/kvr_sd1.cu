@@ -142,6 +142,13 @@ __global__ void __launch_bounds__(256) sd1_encode_kernel(
 // popcounts, score = float(max_j S_j) * (M/127).  With `select` set, the
 // last CTA of each (b, h) to finish runs the block top-k over that row.
 constexpr int kScoreTilesPerCta = 16;
+constexpr int64_t kSelectSmemScores = 8192;  // rows up to this many tiles are selected from shared memory
+
+__host__ __device__ inline size_t select_cand_bytes(int k_sel) {
+  int P = 1;
+  while (P < k_sel) P <<= 1;
+  return align_up((size_t)P * 8, 16);
+}
 
 struct SelectArgs {
   int k_sel;
@@ -163,6 +170,10 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   __shared__ int last_s;
   extern __shared__ __align__(16) unsigned char dyn_smem[];
 
+  // a dependent attention kernel may start now: it only reads what this
+  // kernel writes after its own griddepcontrol.wait
+  asm volatile("griddepcontrol.launch_dependents;");
+  KVR_TRACE_POINT(0, 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int h = blockIdx.y, b = blockIdx.z;
   const int g = n_q / n_kv;
@@ -186,17 +197,22 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
       for (int m = 0; m < 4; ++m) ks[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
     }
   }
+  // warp 0: all g query heads of the group are loaded before the (ordered) sum
+  float qv[8][4];
+  if (warp == 0) {
+    const int64_t qb = ((int64_t)b * n_q + (int64_t)h * g) * kD + lane * 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < g) load4<DTQ>(q, qb + (int64_t)i * kD, qv[i]);
+  }
   __syncthreads();
   if (warp == 0) {
-    float acc[4];
-    const int64_t qb = ((int64_t)b * n_q + (int64_t)h * g) * kD + lane * 4;
-    load4<DTQ>(q, qb, acc);
-    for (int i = 1; i < g; ++i) {
-      float t[4];
-      load4<DTQ>(q, qb + (int64_t)i * kD, t);
+    float acc[4] = {qv[0][0], qv[0][1], qv[0][2], qv[0][3]};
 #pragma unroll
-      for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], t[r]);
-    }
+    for (int i = 1; i < 8; ++i)
+      if (i < g)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], qv[i][r]);
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc[r] = __fdiv_rn(acc[r], (float)g);
     transform128(acc, lane, kind, false, buf_s[0], lee_s);
@@ -212,6 +228,7 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
     }
   }
   __syncthreads();
+  KVR_TRACE_POINT(0, 1);
 
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
@@ -264,6 +281,7 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
 
   // ---- fused selection by the last CTA of this (b, h)
   __syncthreads();
+  KVR_TRACE_POINT(0, 2);
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(&sa.counters[row], 1u);
@@ -272,21 +290,37 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   __syncthreads();
   if (!last_s) return;
   __threadfence();
+  KVR_TRACE_POINT(0, 3);
   TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn_smem);
   unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn_smem + align_up(sizeof(TopkSmem), 16));
   const float *srow = scores + row * n_tiles;
   const int64_t ex0 = sa.ex_t0, ex1 = sa.ex_t1;
   const int kk = (int)(n_tiles < sa.k_sel ? n_tiles : sa.k_sel);
   if (kk > 0) {
-    block_topk<256>(
-        [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i); }, n_tiles, kk,
-        cand, tsm);
+    if (n_tiles <= kSelectSmemScores) {
+      // one pass over L2 into shared memory; the radix passes then stay on chip
+      float *row_s = reinterpret_cast<float *>(dyn_smem + align_up(sizeof(TopkSmem), 16) + select_cand_bytes(sa.k_sel));
+      for (int64_t i = threadIdx.x; i < n_tiles; i += blockDim.x)
+        row_s[i] = (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i);
+      __syncthreads();
+      if (kk <= 32) {
+        unsigned long long *lists = tsm.lists;
+        block_topk_warp32<256>(row_s, n_tiles, kk, lists, cand);
+      } else {
+        block_topk<256>([&](int64_t i) -> float { return row_s[i]; }, n_tiles, kk, cand, tsm);
+      }
+    } else {
+      block_topk<256>(
+          [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i); }, n_tiles, kk,
+          cand, tsm);
+    }
   }
   for (int j = threadIdx.x; j < sa.k_sel; j += blockDim.x) {
     const bool ok = j < kk;
     sa.sel[row * sa.k_sel + j] = ok ? (int32_t)(key_index(cand[j]) + sa.tile_base) : -1;
     if (sa.sel_scores) sa.sel_scores[row * sa.k_sel + j] = ok ? key_score(cand[j]) : -INFINITY;
   }
+  KVR_TRACE_POINT(0, 4);
   if (threadIdx.x == 0) sa.counters[row] = 0u;
 }
 
@@ -370,17 +404,16 @@ static int launch_encode(int tile, dim3 grid, size_t smem, cudaStream_t st, cons
   return check_launch("kvr_sd1_encode");
 }
 
-size_t select_dyn_smem(int k_sel) {
-  int P = 1;
-  while (P < k_sel) P <<= 1;
-  return align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
+size_t select_dyn_smem(int k_sel, int64_t n_tiles) {
+  return align_up(sizeof(TopkSmem), 16) + select_cand_bytes(k_sel) +
+         (n_tiles <= kSelectSmemScores ? (size_t)(n_tiles > 0 ? n_tiles : 1) * 4 : 0);
 }
 
 template <int DTQ>
 static int launch_score(int tile, dim3 grid, cudaStream_t st, const void *q, int n_q, int n_kv,
                         const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind, float *scores,
                         float *qprime, SelectArgs sa, int do_select) {
-  const size_t smem = do_select ? select_dyn_smem(sa.k_sel) : 0;
+  const size_t smem = do_select ? select_dyn_smem(sa.k_sel, nt) : 0;
   switch (tile) {
 #define KVR_SC(T)                                                                                        \
   case T:                                                                                                \
@@ -530,3 +563,9 @@ extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscal
                                                                            tile, kind, sel, k, out_k, out_v, rows);
   return check_launch("kvr_sd1_decode_tiles");
 }
+
+#ifdef KVR_TRACE
+extern "C" KVR_API int kvr_debug_trace_sd1(unsigned long long *host, int n) {
+  return cudaMemcpyFromSymbol(host, kvr::g_kvr_trace, sizeof(unsigned long long) * n) == cudaSuccess ? 0 : 2;
+}
+#endif

@@ -16,6 +16,7 @@ struct TopkSmem {
   unsigned long long prefix, mask;
   int remaining, bin_count, n_out;
   int hist[256];
+  unsigned long long lists[256];  // per-warp top-32 lists (8 warps)
 };
 
 __device__ __forceinline__ unsigned long long make_key(float s, int64_t i) {
@@ -115,6 +116,64 @@ __device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long lon
       __syncthreads();
     }
   }
+}
+
+// Top-k (k <= 32) of a row held in shared memory by warp-level bitonic
+// networks: each warp keeps a descending top-32 list in registers (one key
+// per lane) and folds in its slice 32 keys at a time (sort the new keys,
+// max against the reversed list, bitonic merge); warp 0 then folds the
+// other warps' lists.  One block barrier; no shared-memory atomics.
+// row_s: n scores; lists: 32 * (NT/32) keys of scratch; cand: >= k keys.
+__device__ __forceinline__ unsigned long long warp_bitonic_merge_desc(unsigned long long key, int lane) {
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, stride);
+    const bool lower = (lane & stride) == 0;
+    key = lower ? (key > other ? key : other) : (key < other ? key : other);
+  }
+  return key;
+}
+__device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long key, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, stride);
+      const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0 || size == 32);
+      key = keep_max ? (key > other ? key : other) : (key < other ? key : other);
+    }
+  }
+  return key;
+}
+// list and incoming both descending; returns the descending top 32 of the union
+__device__ __forceinline__ unsigned long long warp_fold_top32(unsigned long long list, unsigned long long sorted_new,
+                                                             int lane) {
+  const unsigned long long rev = __shfl_sync(0xffffffffu, sorted_new, 31 - lane);
+  return warp_bitonic_merge_desc(list > rev ? list : rev, lane);
+}
+
+template <int NT>
+__device__ void block_topk_warp32(const float *row_s, int64_t n, int k, unsigned long long *lists,
+                                  unsigned long long *cand) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t per = ((n + NW - 1) / NW + 31) / 32 * 32;  // slice per warp, multiple of 32
+  unsigned long long list = 0ull;
+  for (int64_t c0 = warp * per; c0 < (warp + 1) * per && c0 < n; c0 += 32) {
+    const int64_t i = c0 + lane;
+    const unsigned long long key = i < n ? make_key(row_s[i], i) : 0ull;
+    list = warp_fold_top32(list, warp_sort_desc(key, lane), lane);
+  }
+  lists[warp * 32 + lane] = list;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < NW; ++w) {
+      const unsigned long long other = lists[w * 32 + (31 - lane)];  // reversed: ascending
+      list = warp_bitonic_merge_desc(list > other ? list : other, lane);
+    }
+    if (lane < k) cand[lane] = list;
+  }
+  __syncthreads();
 }
 
 }  // namespace kvr

@@ -53,47 +53,91 @@ __device__ __forceinline__ void load_lee(float *lee_s) {
   for (int i = threadIdx.x; i < kD - 1; i += blockDim.x) lee_s[i] = __uint_as_float(kLeeBits[i]);
 }
 
+// Lee levels as compile-time steps (block size M is a template constant, so
+// every index below is shift/mask arithmetic).
+template <int M>
+__device__ __forceinline__ void lee_split(const float *in, float *out, const float *lee, int lane) {
+  constexpr int half = M / 2;
+  const float *f = lee + half - 1;
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int p = lane + 32 * q;
+    const int o = (p / half) * M, j = p % half;
+    const float xa = in[o + j], xb = in[o + M - 1 - j];
+    out[o + j] = __fadd_rn(xa, xb);
+    out[o + half + j] = __fmul_rn(__fsub_rn(xa, xb), f[j]);
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_merge(const float *in, float *out, int lane) {
+  constexpr int half = M / 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int i = lane + 32 * q;
+    const int o = (i / M) * M, r = i % M;
+    float v;
+    if ((r & 1) == 0) {
+      v = in[o + (r >> 1)];
+    } else {
+      const int k = r >> 1;
+      v = in[o + half + k];
+      if (k < half - 1) v = __fadd_rn(v, in[o + half + k + 1]);
+    }
+    out[i] = v;
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_merge_t(const float *in, float *out, int lane) {
+  constexpr int half = M / 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int i = lane + 32 * q;
+    const int o = (i / M) * M, r = i % M;
+    float v;
+    if (r < half) {
+      v = in[o + 2 * r];
+    } else {
+      const int k = r - half;
+      v = in[o + 2 * k + 1];
+      if (k > 0) v = __fadd_rn(v, in[o + 2 * k - 1]);
+    }
+    out[i] = v;
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_split_t(const float *in, float *out, const float *lee, int lane) {
+  constexpr int half = M / 2;
+  const float *f = lee + half - 1;
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int p = lane + 32 * q;
+    const int o = (p / half) * M, j = p % half;
+    const float a = in[o + j], fb = __fmul_rn(in[o + half + j], f[j]);
+    out[o + j] = __fadd_rn(a, fb);
+    out[o + M - 1 - j] = __fsub_rn(a, fb);
+  }
+}
+
 // buf: 256 floats owned by this warp.  lee: the 127 factors (shared memory).
 __device__ __forceinline__ void dct128_fwd(float (&x)[4], int lane, float *buf, const float *lee) {
-  float *in = buf, *out = buf + kD;
-  reinterpret_cast<float4 *>(in)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  float *A = buf, *B = buf + kD;
+  reinterpret_cast<float4 *>(A)[lane] = make_float4(x[0], x[1], x[2], x[3]);
   __syncwarp();
-#pragma unroll
-  for (int M = kD; M >= 2; M >>= 1) {
-    const int half = M >> 1;
-    const float *f = lee + half - 1;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int p = lane + 32 * q;
-      const int blk = p / half, j = p - blk * half, o = blk * M;
-      const float xa = in[o + j], xb = in[o + M - 1 - j];
-      out[o + j] = __fadd_rn(xa, xb);
-      out[o + half + j] = __fmul_rn(__fsub_rn(xa, xb), f[j]);
-    }
-    __syncwarp();
-    float *t = in; in = out; out = t;
-  }
-#pragma unroll
-  for (int M = 2; M <= kD; M <<= 1) {
-    const int half = M >> 1;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = lane + 32 * q;
-      const int blk = i / M, r = i - blk * M, o = blk * M;
-      float v;
-      if ((r & 1) == 0) {
-        v = in[o + (r >> 1)];
-      } else {
-        const int k = r >> 1;
-        v = in[o + half + k];
-        if (k < half - 1) v = __fadd_rn(v, in[o + half + k + 1]);
-      }
-      out[i] = v;
-    }
-    __syncwarp();
-    float *t = in; in = out; out = t;
-  }
-  float4 r4 = reinterpret_cast<const float4 *>(in)[lane];
+  lee_split<128>(A, B, lee, lane); __syncwarp();
+  lee_split<64>(B, A, lee, lane); __syncwarp();
+  lee_split<32>(A, B, lee, lane); __syncwarp();
+  lee_split<16>(B, A, lee, lane); __syncwarp();
+  lee_split<8>(A, B, lee, lane); __syncwarp();
+  lee_split<4>(B, A, lee, lane); __syncwarp();
+  lee_split<2>(A, B, lee, lane); __syncwarp();
+  lee_merge<2>(B, A, lane); __syncwarp();
+  lee_merge<4>(A, B, lane); __syncwarp();
+  lee_merge<8>(B, A, lane); __syncwarp();
+  lee_merge<16>(A, B, lane); __syncwarp();
+  lee_merge<32>(B, A, lane); __syncwarp();
+  lee_merge<64>(A, B, lane); __syncwarp();
+  lee_merge<128>(B, A, lane); __syncwarp();
+  const float4 r4 = reinterpret_cast<const float4 *>(A)[lane];
   __syncwarp();
   const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
   x[0] = __fmul_rn(r4.x, lane == 0 ? c0 : c1);
@@ -104,49 +148,25 @@ __device__ __forceinline__ void dct128_fwd(float (&x)[4], int lane, float *buf, 
 
 __device__ __forceinline__ void dct128_inv(float (&x)[4], int lane, float *buf, const float *lee) {
   const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
-  float *in = buf, *out = buf + kD;
-  reinterpret_cast<float4 *>(in)[lane] = make_float4(__fmul_rn(x[0], lane == 0 ? c0 : c1),
-                                                      __fmul_rn(x[1], c1), __fmul_rn(x[2], c1),
-                                                      __fmul_rn(x[3], c1));
+  float *A = buf, *B = buf + kD;
+  reinterpret_cast<float4 *>(A)[lane] = make_float4(__fmul_rn(x[0], lane == 0 ? c0 : c1), __fmul_rn(x[1], c1),
+                                                     __fmul_rn(x[2], c1), __fmul_rn(x[3], c1));
   __syncwarp();
-  // transposed merge levels, M = 128 .. 2
-#pragma unroll
-  for (int M = kD; M >= 2; M >>= 1) {
-    const int half = M >> 1;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = lane + 32 * q;
-      const int blk = i / M, r = i - blk * M, o = blk * M;
-      float v;
-      if (r < half) {
-        v = in[o + 2 * r];
-      } else {
-        const int k = r - half;
-        v = in[o + 2 * k + 1];
-        if (k > 0) v = __fadd_rn(v, in[o + 2 * k - 1]);
-      }
-      out[i] = v;
-    }
-    __syncwarp();
-    float *t = in; in = out; out = t;
-  }
-  // transposed split levels, M = 2 .. 128
-#pragma unroll
-  for (int M = 2; M <= kD; M <<= 1) {
-    const int half = M >> 1;
-    const float *f = lee + half - 1;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int p = lane + 32 * q;
-      const int blk = p / half, j = p - blk * half, o = blk * M;
-      const float a = in[o + j], fb = __fmul_rn(in[o + half + j], f[j]);
-      out[o + j] = __fadd_rn(a, fb);
-      out[o + M - 1 - j] = __fsub_rn(a, fb);
-    }
-    __syncwarp();
-    float *t = in; in = out; out = t;
-  }
-  float4 r4 = reinterpret_cast<const float4 *>(in)[lane];
+  lee_merge_t<128>(A, B, lane); __syncwarp();
+  lee_merge_t<64>(B, A, lane); __syncwarp();
+  lee_merge_t<32>(A, B, lane); __syncwarp();
+  lee_merge_t<16>(B, A, lane); __syncwarp();
+  lee_merge_t<8>(A, B, lane); __syncwarp();
+  lee_merge_t<4>(B, A, lane); __syncwarp();
+  lee_merge_t<2>(A, B, lane); __syncwarp();
+  lee_split_t<2>(B, A, lee, lane); __syncwarp();
+  lee_split_t<4>(A, B, lee, lane); __syncwarp();
+  lee_split_t<8>(B, A, lee, lane); __syncwarp();
+  lee_split_t<16>(A, B, lee, lane); __syncwarp();
+  lee_split_t<32>(B, A, lee, lane); __syncwarp();
+  lee_split_t<64>(A, B, lee, lane); __syncwarp();
+  lee_split_t<128>(B, A, lee, lane); __syncwarp();
+  const float4 r4 = reinterpret_cast<const float4 *>(A)[lane];
   __syncwarp();
   x[0] = r4.x; x[1] = r4.y; x[2] = r4.z; x[3] = r4.w;
 }
