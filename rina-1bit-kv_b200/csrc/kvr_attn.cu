@@ -17,6 +17,8 @@
 #include "kvr_common.cuh"
 #include "kvr_transform.cuh"
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace kvr {
@@ -59,67 +61,6 @@ __device__ __forceinline__ void load4_rt(const void *p, int64_t i, int dt, float
   if (dt == KVR_F32) load4<KVR_F32>(p, i, x);
   else if (dt == KVR_F16) load4<KVR_F16>(p, i, x);
   else load4<KVR_BF16>(p, i, x);
-}
-
-// Raw 4-element load (16 bytes for fp32, 8 bytes for 16-bit types) and its
-// widening to fp32; split so that many loads can be in flight at once.
-__device__ __forceinline__ uint4 raw4(const void *p, int64_t i, int dt) {
-  if (dt == KVR_F32) return __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(p) + i));
-  const uint2 u = __ldg(reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(p) + i));
-  return make_uint4(u.x, u.y, 0u, 0u);
-}
-__device__ __forceinline__ float4 cvt4(uint4 r, int dt) {
-  if (dt == KVR_F32) return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
-                                        __uint_as_float(r.w));
-  if (dt == KVR_F16) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&r.x));
-    const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&r.y));
-    return make_float4(a.x, a.y, c.x, c.y);
-  }
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.x));
-  const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.y));
-  return make_float4(a.x, a.y, c.x, c.y);
-}
-
-// Programmatic dependent launch: wait for the preceding grid (a no-op when
-// the kernel was not launched as a dependent), and let dependents start.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// ---- mbarrier + bulk copy (PTX)
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned phase) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return done != 0;
-}
-// Bounded wait; returns false if it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    if (mbar_try_wait(bar, phase)) return true;
-    __nanosleep(64);
-  }
-  return false;
 }
 
 // ---- shared memory plan (bytes)
@@ -597,6 +538,13 @@ static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) 
   return w;
 }
 
+int sd1_fused_launch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint16_t *win_k,
+                     const uint16_t *win_v, int64_t win_cap, int64_t n_win, const uint16_t *tail_k,
+                     const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits, const uint16_t *kscale,
+                     const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
+                     int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
+                     int32_t *sel_out, unsigned *err, cudaStream_t st);
+
 int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
@@ -792,6 +740,20 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
               workspace_bytes, need);
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_decode_step: workspace must be 256-byte aligned");
   char *p = reinterpret_cast<char *>(workspace);
+  // Optional clustered single-kernel path (KVR_SD1_PATH=fused).  Measured on
+  // B200 at the config-1 shape it is slower than the select + attend pair
+  // (about 32 vs 26 us per layer), so the pair is the default.
+  const char *path = getenv("KVR_SD1_PATH");
+  if ((path && strcmp(path, "fused") == 0) && valid_dtype(q_dtype) && valid_dtype(out_dtype) && out && kbits &&
+      kscale && vbits && vscale && n_tiles <= nt_cap && n_win <= win_cap && n_tail <= tile && n_q / n_kv * n_kv == n_q &&
+      (kind == KVR_HADAMARD || kind == KVR_DCT) && (tile == 32 || tile == 64 || tile == 128)) {
+    const int rc = sd1_fused_launch(q, q_dtype, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v,
+                                    n_tail, kbits, kscale, vbits, vscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
+                                    ex_t1, scale, out, out_dtype, sel_out, reinterpret_cast<unsigned *>(p),
+                                    as_cuda(stream));
+    if (rc != KVR_ENOTSUP) return rc;
+    clear_error();
+  }
   const size_t a_bytes = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
   const size_t s_bytes = align_up((size_t)batch * n_kv * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
   const size_t sel_bytes = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);

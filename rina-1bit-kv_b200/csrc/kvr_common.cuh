@@ -143,4 +143,67 @@ __device__ __forceinline__ void kvr_trace(int kernel, int point) {
 // Bound on device-side spin iterations (each iteration also sleeps ~64 ns).
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+// Raw 4-element load (16 bytes for fp32, 8 bytes for 16-bit types) and its
+// widening to fp32; split so that many loads can be in flight at once.
+__device__ __forceinline__ uint4 raw4(const void *p, int64_t i, int dt) {
+  if (dt == KVR_F32) return __ldg(reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(p) + i));
+  const uint2 u = __ldg(reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(p) + i));
+  return make_uint4(u.x, u.y, 0u, 0u);
+}
+__device__ __forceinline__ float4 cvt4(uint4 r, int dt) {
+  if (dt == KVR_F32) return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                                        __uint_as_float(r.w));
+  if (dt == KVR_F16) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&r.x));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&r.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  }
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.x));
+  const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r.y));
+  return make_float4(a.x, a.y, c.x, c.y);
+}
+
+// Programmatic dependent launch: wait for the preceding grid (a no-op when
+// the kernel was not launched as a dependent), and let dependents start.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- mbarrier + bulk copy (PTX)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait; returns false if it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    if (mbar_try_wait(bar, phase)) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+
+
 }  // namespace kvr

@@ -8,6 +8,7 @@
 // tiles (modules/kvr_retrieval.py:270, 291-315) and a per-KV-head top-k keeps
 // the best ones (modules/kvr_retrieval.py:370-392).
 #include "kvr_common.cuh"
+#include "kvr_sd1_score.cuh"
 #include "kvr_topk.cuh"
 #include "kvr_transform.cuh"
 
@@ -234,48 +235,8 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   for (int u = 0; u < 2; ++u) {
     const int64_t t = t_first + u;
     if (t >= n_tiles) continue;  // warp-uniform
-    int wq[4];
-    float w[4], mx = 0.0f;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      w[m] = __fmul_rn(qp_s[lane + 32 * m], __half2float(__ushort_as_half(ks[u][m])));
-      mx = fmaxf(mx, fabsf(w[m]));
-    }
-    mx = warp_max(mx);
-    const float inv = mx > 0.0f ? __fdiv_rn(127.0f, mx) : 0.0f;
-    int wsum = 0;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      wq[m] = __float2int_rn(__fmul_rn(w[m], inv));
-      wsum += wq[m];
-    }
-    wsum = warp_sum_int(wsum);
-    uint32_t plane[8][4];
-#pragma unroll
-    for (int p = 0; p < 8; ++p)
-#pragma unroll
-      for (int m = 0; m < 4; ++m) plane[p][m] = __ballot_sync(0xffffffffu, (wq[m] >> p) & 1);
-    int best = INT_MIN;
-#pragma unroll
-    for (int r = 0; r < TPL; ++r) {
-      const uint32_t bw[4] = {kb[u][r].x, kb[u][r].y, kb[u][r].z, kb[u][r].w};
-      int P = 0;
-#pragma unroll
-      for (int p = 0; p < 7; ++p) {
-        int cnt = 0;
-#pragma unroll
-        for (int m = 0; m < 4; ++m) cnt += __popc(plane[p][m] & bw[m]);
-        P += cnt << p;
-      }
-      int c7 = 0;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) c7 += __popc(plane[7][m] & bw[m]);
-      P -= c7 << 7;
-      best = max(best, 2 * P - wsum);
-    }
-    best = warp_max_int(best);
-    const float delta = __fdiv_rn(mx, 127.0f);
-    if (lane == 0) scores[row * n_tiles + t] = __fmul_rn((float)best, delta);
+    const float score = sd1_score_tile<TILE>(qp_s, kb[u], ks[u], lane);
+    if (lane == 0) scores[row * n_tiles + t] = score;
   }
   if (!do_select) return;
 

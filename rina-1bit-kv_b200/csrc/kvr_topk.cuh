@@ -16,7 +16,7 @@ struct TopkSmem {
   unsigned long long prefix, mask;
   int remaining, bin_count, n_out;
   int hist[256];
-  unsigned long long lists[256];  // per-warp top-32 lists (8 warps)
+  unsigned long long lists[512];  // per-warp top-32 lists (up to 16 warps)
 };
 
 __device__ __forceinline__ unsigned long long make_key(float s, int64_t i) {
@@ -166,13 +166,16 @@ __device__ void block_topk_warp32(const float *row_s, int64_t n, int k, unsigned
   }
   lists[warp * 32 + lane] = list;
   __syncthreads();
-  if (warp == 0) {
-    for (int w = 1; w < NW; ++w) {
-      const unsigned long long other = lists[w * 32 + (31 - lane)];  // reversed: ascending
+  // tree: in round s, warp w (w % 2s == 0) folds in the list of warp w + s
+  for (int s = 1; s < NW; s <<= 1) {
+    if ((warp % (2 * s)) == 0 && warp + s < NW) {
+      const unsigned long long other = lists[(warp + s) * 32 + (31 - lane)];  // reversed: ascending
       list = warp_bitonic_merge_desc(list > other ? list : other, lane);
+      lists[warp * 32 + lane] = list;
     }
-    if (lane < k) cand[lane] = list;
+    __syncthreads();
   }
+  if (warp == 0 && lane < k) cand[lane] = list;
   __syncthreads();
 }
 

@@ -1,6 +1,8 @@
 """GPU parity of the sd1 1-bit codec against its CPU specification
 (oracle/sd1_ref.py): bits, scales, transforms and tile scores bit-exact;
 selection indices bit-exact; attention within the stated tolerance."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -149,15 +151,27 @@ def test_attend_vs_oracle(kind, tile, nw, ntl, g, B):
     sel, _, qp = K().sd1_select(st, qt, k_sel)
     out = K().sd1_attend(st, qt, qp, sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
                          out_dtype=torch.float32).cpu().numpy()
-    step = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl).cpu().numpy()
-    assert np.array_equal(out, step)
+    # decode_step selects the same tiles as select (both variants)
+    sel_f = torch.empty_like(sel)
+    step = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                               sel_out=sel_f).cpu().numpy()
+    assert torch.equal(sel_f, sel)
+    assert np.array_equal(step, out)  # default: the select + attend kernels
+    os.environ["KVR_SD1_PATH"] = "fused"  # clustered single-kernel variant
+    try:
+        sel_c = torch.empty_like(sel)
+        fused = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                                    sel_out=sel_c).cpu().numpy()
+    finally:
+        del os.environ["KVR_SD1_PATH"]
+    assert torch.equal(sel_c, sel)
     s = sel.cpu().numpy()
     for b in range(B):
         for h in range(n_kv):
             want = _oracle_attend(q, st, b, h, s[b, h], win_k, win_v, nw, tail_k, tail_v, ntl, kind, g)
-            got = out[b, h * g:(h + 1) * g]
-            err = np.abs(got - want).max() / np.abs(want).max()
-            assert err < 1e-5, (b, h, err)
+            for got in (out[b, h * g:(h + 1) * g], fused[b, h * g:(h + 1) * g]):
+                err = np.abs(got - want).max() / np.abs(want).max()
+                assert err < 1e-5, (b, h, err)
 
 
 def test_partial_rows_merge_like_whole():
