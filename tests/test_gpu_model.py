@@ -1,0 +1,90 @@
+"""Model integration (KVRHook / KVRGenerator drop-ins) on a tiny random-init
+fp16 Llama with head_dim 128, on the GPU."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import int4w_ref as R
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def tiny_llama(layers=2, n_q=4, n_kv=2, vocab=500, max_pos=4096, seed=0):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(vocab_size=vocab, hidden_size=n_q * 128, intermediate_size=1024, num_hidden_layers=layers,
+                      num_attention_heads=n_q, num_key_value_heads=n_kv, head_dim=128,
+                      max_position_embeddings=max_pos, rope_theta=500000.0)
+    return LlamaForCausalLM(cfg).half().to(DEV).eval()
+
+
+@pytest.mark.parametrize("codec", ["int4w", "sd1"])
+def test_generator_matches_hf_when_window_holds_everything(codec):
+    from kvr_b200 import KVRGenerator
+    m = tiny_llama()
+    prompt = torch.randint(0, 500, (1, 100), device=DEV)
+    x = torch.tensor([[7]], device=DEV)
+    gen = KVRGenerator(m, window_size=256, top_k=64, codec=codec, attractors=False)
+    gen.prefill(prompt)
+    gen._is_first = False  # x is a new token at position 100: store it, then attend
+    ours = gen.logits_step(x)
+    with torch.no_grad():
+        want = m(torch.cat([prompt, x], 1)).logits[0, -1].float()
+    assert torch.allclose(ours, want, rtol=2e-2, atol=2e-2), (ours - want).abs().max()
+
+
+def test_hook_retrieval_wiring_matches_oracle():
+    from kvr_b200 import KVRGenerator
+    m = tiny_llama()
+    prompt = torch.randint(0, 500, (1, 400), device=DEV)
+    gen = KVRGenerator(m, window_size=128, top_k=96, codec="int4w", attractors=False)
+    gen.prefill(prompt)
+    kvr = gen.kvr
+    assert kvr._retrieval_built and kvr.retrievals[0].n_stored == 272
+    win, ret = kvr.windows[0], kvr.retrievals[0]
+    q = torch.randn(4, 128, device=DEV)
+    ours = kvr.attend(0, q).cpu().numpy()
+    st = {"k_packed": ret.k_packed.cpu().numpy(), "vr_packed": ret.vr_packed.cpu().numpy(),
+          "k_scales": ret.k_scales.cpu().numpy(), "vr_scales": ret.vr_scales.cpu().numpy(),
+          "W": ret.W.cpu().numpy(), "K_mean": ret.K_mean.cpu().numpy(), "V_mean": ret.V_mean.cpu().numpy(),
+          "n_stored": ret.n_stored}
+    cos, sin = kvr.cos_tbl.cpu().numpy(), kvr.sin_tbl.cpu().numpy()
+    ex = (max(0, 400 - win.n), min(ret.n_stored, 400))
+    ex = (0, 0) if ex[0] >= ex[1] else ex
+    rk, rv, _ = R.retrieve_token_branch(q.cpu().numpy(), st, cos, sin, 96, *ex)
+    kc = np.concatenate([win.k[:win.n].float().cpu().numpy(), rk])
+    vc = np.concatenate([win.v[:win.n].float().cpu().numpy(), rv.astype(np.float32)])
+    want = R.softmax_attention(q.cpu().numpy(), kc, vc)
+    assert np.abs(ours - want).max() <= 2e-3 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("codec", ["int4w", "sd1"])
+def test_generator_runs_with_eviction(codec):
+    from kvr_b200 import KVRGenerator
+    m = tiny_llama()
+    prompt = torch.randint(0, 500, (1, 300), device=DEV)
+    gen = KVRGenerator(m, window_size=128, top_k=128, codec=codec, attractors=False)
+    gen.prefill(prompt)
+    n0 = gen.kvr.retrievals[0].n_tokens
+    gen.step(prompt[0, -1])
+    ids = gen.generate(5, temperature=0.7, top_k=20)
+    assert ids.shape == (5,) and gen.kvr._context_len == 306
+    # every step past the first evicts one window token into the index
+    assert gen.kvr.retrievals[0].n_tokens == n0 + 5
+    assert torch.isfinite(gen.logits_step(ids[-1])).all()
+
+
+def test_hook_path_runs():
+    from kvr_b200 import KVRHook
+    m = tiny_llama()
+    prompt = torch.randint(0, 500, (1, 200), device=DEV)
+    hook = KVRHook(m, window_size=128, top_k=64, codec="sd1", attractors=False, num_denoise_steps=0)
+    hook.prefill(prompt)
+    hook.register()
+    hook._step = 1
+    hook._context_len = 201
+    with torch.no_grad():
+        out = m(torch.cat([prompt, prompt[:, :1]], 1)).logits
+    hook.remove()
+    assert torch.isfinite(out).all()

@@ -93,3 +93,11 @@ def test_kernel_constants_match_spec():
     tsrc = open(os.path.join(ROOT, "rina-1bit-kv_b200", "csrc", "kvr_transform.cuh")).read()
     inv = int(re.search(r"kInvSqrt128Bits = 0x([0-9a-f]{8})u", tsrc).group(1), 16)
     assert inv == np.array([F32(1.0 / np.sqrt(128))]).view(np.uint32)[0]
+
+
+def test_exclusion_range_rule():
+    # kvr_hook.py:262-267 / kvr_generator.py:439-444
+    from kvr_b200.kvr_hook import exclusion_range
+    assert exclusion_range(1000, 512, 488) == (0, 0)   # window holds the newest, index the rest
+    assert exclusion_range(600, 512, 300) == (88, 300)
+    assert exclusion_range(100, 512, 0) == (0, 0)
