@@ -262,10 +262,17 @@ def run_gpu(args, rank, world, local_rank):
         e2e_ms = float(tt.item())
 
     peak, peak_kind = measured_peak_hbm()
+    traffic = None
+    try:  # DRAM bytes per launch from the committed ncu capture of this workload
+        tj = json.load(open(os.path.join(ROOT, "profiles", "traffic_config1.json")))["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        tj = {}
     layer_bytes = sel_b + att_b
     dom = "select" if ms_sel >= ms_att else "attend"
     dom_bytes, dom_ms = (sel_b, ms_sel) if dom == "select" else (att_b, ms_att)
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    if world == 1:
+        traffic = tj.get("sd1_score_kernel" if dom == "select" else "attn_kernel")
     res = {
         "metric": METRIC,
         "value": round(B * 1e3 / ms_per_step, 3),
@@ -291,7 +298,7 @@ def run_gpu(args, rank, world, local_rank):
                    "tokens_per_layer": B * T_STORED},
         "roofline": {"bound": "hbm", "kernel": f"sd1_{dom}", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": None,
+                     "traffic": traffic, "traffic_source": "profiles/traffic_config1.json (ncu)",
                      "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5),
                      "select_ms": round(ms_sel, 5), "attend_ms": round(ms_att, 5),
                      "select_bytes": sel_b, "attend_bytes": att_b},
