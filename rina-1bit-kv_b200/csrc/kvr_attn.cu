@@ -26,9 +26,11 @@ namespace kvr {
 constexpr int kChunk = 64;
 constexpr int kMaxG = 8;
 constexpr int kKsStride = kD + 4;  // padded fp32 row of the staged K chunk
-// workspace partial row: [m, l, pad, pad, o_0 .. o_127] (16-byte aligned o)
-constexpr int kPartStride = kD + 4;
-constexpr int kPartO = 4;
+// workspace partial row of one CTA slot and query head:
+// [m, l, pad, pad, o_exact[128], o_transformed[128]] (16-byte aligned rows)
+constexpr int kPartStride = 4 + 2 * kD;
+constexpr int kPartEx = 4;
+constexpr int kPartTr = 4 + kD;
 
 struct AttnArgs {
   const void *q;
@@ -53,7 +55,9 @@ struct AttnArgs {
   float *part;         // (B, n_kv, units, g, d+2)
   unsigned *counters;  // (B, n_kv)
   unsigned *err;
-  int units;
+  int units;  // work units per (b, h)
+  int upc;    // units per CTA
+  int slots;  // CTAs per (b, h) = ceil(units / upc)
 };
 
 // ---- runtime-dtype loads
@@ -83,7 +87,12 @@ struct AttnSmem {
   static constexpr int kBar = kML + kMaxG * 2 * 4;                   // u64
   static constexpr int kFlag = kBar + 16;
   static constexpr int kLee = kFlag + 16;                             // fp32 [128] DCT factors
-  static constexpr int kTotal = kLee + kD * 4;
+  static constexpr int kAccM = kLee + kD * 4;                         // fp32 [8] running max
+  static constexpr int kAccL = kAccM + kMaxG * 4;                     // fp32 [8] running sum
+  static constexpr int kAccSC = kAccL + kMaxG * 4;                    // fp32 [8][2] fold factors
+  static constexpr int kAccEx = kAccSC + kMaxG * 2 * 4;               // fp32 [8][128] exact part
+  static constexpr int kAccTr = kAccEx + kMaxG * kD * 4;              // fp32 [8][128] transformed part
+  static constexpr int kTotal = kAccTr + kMaxG * kD * 4;
 };
 
 // Softmax over the scores S[hq][0..nt) of every query head; writes P[j][hq],
@@ -109,15 +118,40 @@ __device__ __forceinline__ void softmax_rows(const AttnArgs &a, int nt, const fl
   }
 }
 
-__device__ __forceinline__ float *part_row(const AttnArgs &a, int64_t row, int u, int hq) {
-  return a.part + (((row * a.units + u) * a.g) + hq) * (int64_t)kPartStride;
+__device__ __forceinline__ float *part_row(const AttnArgs &a, int64_t row, int slot, int hq) {
+  return a.part + (((row * a.slots + slot) * a.g) + hq) * (int64_t)kPartStride;
 }
 
-__device__ void write_empty_partial(const AttnArgs &a, int64_t row, int u) {
-  for (int i = threadIdx.x; i < a.g * kPartStride; i += blockDim.x) {
-    const int hq = i / kPartStride, c = i - hq * kPartStride;
-    part_row(a, row, u, hq)[c] = c == 0 ? -INFINITY : 0.0f;
+// Folds the unit just computed (unit m, l in ML; unit output rows in S[hq][128])
+// into the CTA's running accumulators (online softmax).
+__device__ void fold_unit(const AttnArgs &a, unsigned char *sm, bool into_tr) {
+  float *M = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
+  float *L = reinterpret_cast<float *>(sm + AttnSmem::kAccL);
+  float *SC = reinterpret_cast<float *>(sm + AttnSmem::kAccSC);
+  float *Ex = reinterpret_cast<float *>(sm + AttnSmem::kAccEx);
+  float *Tr = reinterpret_cast<float *>(sm + AttnSmem::kAccTr);
+  const float *UML = reinterpret_cast<const float *>(sm + AttnSmem::kML);
+  const float *S = reinterpret_cast<const float *>(sm + AttnSmem::kS);
+  const int tid = threadIdx.x;
+  if (tid < a.g) {
+    const float mo = M[tid], mu = UML[2 * tid], lu = UML[2 * tid + 1];
+    const float mn = fmaxf(mo, mu);
+    const float al = (mo == -INFINITY) ? 0.0f : expf(mo - mn);
+    const float be = (mu == -INFINITY) ? 0.0f : expf(mu - mn);
+    SC[2 * tid] = al;
+    SC[2 * tid + 1] = be;
+    M[tid] = mn;
+    L[tid] = L[tid] * al + lu * be;
   }
+  __syncthreads();
+  for (int i = tid; i < a.g * kD; i += blockDim.x) {
+    const int hq = i >> 7;
+    const float al = SC[2 * hq], be = SC[2 * hq + 1];
+    const float u = S[i] * be;
+    Ex[i] = Ex[i] * al + (into_tr ? 0.0f : u);
+    Tr[i] = Tr[i] * al + (into_tr ? u : 0.0f);
+  }
+  __syncthreads();
 }
 
 // ----------------------------------------------------------- exact unit ----
@@ -203,16 +237,10 @@ __device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int 
   if (half == 1)
     for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
   __syncthreads();
-  if (half == 0) {
-    for (int hq = 0; hq < a.g; ++hq) {
-      float *pr = part_row(a, row, u, hq);
-      pr[kPartO + c] = o[hq] + S[hq * kD + c];
-      if (c == 0) {
-        pr[0] = ML[hq * 2];
-        pr[1] = ML[hq * 2 + 1];
-      }
-    }
-  }
+  if (half == 0)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] += o[hq];
+  __syncthreads();
+  fold_unit(a, sm, false);
 }
 
 // ------------------------------------------------------------- sd1 unit ----
@@ -233,10 +261,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   const int64_t row = b * a.n_kv + h;
   griddep_wait();  // sel and qprime come from the selection kernel
   const int32_t t = a.sel[row * a.k_sel + slot];
-  if (t < 0) {
-    write_empty_partial(a, row, u);
-    return;
-  }
+  if (t < 0) return;  // empty slot: nothing to fold
   const int64_t tix = row * a.nt_cap + t;
   constexpr unsigned kBits = TILE * 16, kScale = kD * 2;
   if (tid == 0) {
@@ -264,10 +289,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
     mbar_wait_bounded(bar, 0);  // let copies in flight land before smem is reused
   }
   __syncthreads();
-  if (!flag[0]) {
-    write_empty_partial(a, row, u);
-    return;
-  }
+  if (!flag[0]) return;  // dropped after a bounded wait gave up (reported via the error word)
   // signed nibble LUT: L[hq][grp][x] = sum_r (bit r of x ? +a : -a)_{4 grp + r}, a_c = q'_c s_c
   for (int i = tid; i < a.g * 32; i += blockDim.x) {
     const int hq = i >> 5, grp = i & 31;
@@ -321,116 +343,26 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   __syncthreads();
   if (half == 0) {
     const float vs = __half2float(__ushort_as_half(VS[c]));
-    for (int hq = 0; hq < a.g; ++hq) {
-      float *pr = part_row(a, row, u, hq);
-      const float l = ML[hq * 2 + 1];
-      pr[kPartO + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - l);
-      if (c == 0) {
-        pr[0] = ML[hq * 2];
-        pr[1] = l;
-      }
-    }
-  }
-}
-
-// ---------------------------------------------------------------- merge ----
-__device__ void merge_group(const AttnArgs &a, unsigned char *sm, int64_t b, int h) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t row = b * a.n_kv + h;
-  const int U = a.units;
-  const int n_exact = a.nchunk[0] + a.nchunk[1];
-  // merge layout (all below kML): W [U][8] | Ex [8][128] | Tr [8][128] | buf [8][256] | lee [127]
-  float *W = reinterpret_cast<float *>(sm);
-  float *Ex = W + U * kMaxG;
-  float *Tr = Ex + kMaxG * kD;
-  float *buf = Tr + kMaxG * kD;
-  const float *lee = reinterpret_cast<const float *>(sm + AttnSmem::kLee);  // loaded at kernel start
-  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);  // [g] (M, L)
-  for (int hq = warp; hq < a.g; hq += 8) {
-    // (m, l) of up to 64 units per lane pass, read once as float2
-    float2 ml[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int u = lane + 32 * r;
-      ml[r] = u < U ? __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, u, hq))) : make_float2(-INFINITY, 0.f);
-    }
-    float mx = warp_max(fmaxf(ml[0].x, ml[1].x));
-    for (int u = lane + 64; u < U; u += 32) mx = fmaxf(mx, __ldcg(part_row(a, row, u, hq)));
-    mx = warp_max(mx);
-    float l = 0.0f;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int u = lane + 32 * r;
-      const float w = (ml[r].x == -INFINITY) ? 0.0f : expf(ml[r].x - mx);
-      if (u < U) W[u * kMaxG + hq] = w;
-      l += w * ml[r].y;
-    }
-    for (int u = lane + 64; u < U; u += 32) {
-      const float *pr = part_row(a, row, u, hq);
-      const float mu = __ldcg(pr);
-      const float w = (mu == -INFINITY) ? 0.0f : expf(mu - mx);
-      W[u * kMaxG + hq] = w;
-      l += w * __ldcg(pr + 1);
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      ML[hq * 2] = mx;
-      ML[hq * 2 + 1] = l;
-    }
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - ML[hq * 2 + 1]);
   }
   __syncthreads();
-  // thread -> (head, 4-channel group, slice of the units); partial rows are
-  // read as float4 in unrolled batches so the loads overlap
-  {
-    const int pairs = a.g * 32;
-    const int nparts = blockDim.x / pairs;  // 2 for g = 4, 1 for g = 8
-    const int p = tid % pairs, part = tid / pairs;
-    const int hq = p >> 5, c4 = p & 31;
-    float4 ex = make_float4(0.f, 0.f, 0.f, 0.f), tr = ex;
-    if (part < nparts) {
-      constexpr int UB = 8;
-      for (int u0 = part; u0 < U; u0 += UB * nparts) {
-        float4 o[UB];
-#pragma unroll
-        for (int k = 0; k < UB; ++k) {
-          const int u = u0 + k * nparts;
-          o[k] = u < U ? __ldcg(reinterpret_cast<const float4 *>(part_row(a, row, u, hq) + kPartO) + c4)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < UB; ++k) {
-          const int u = u0 + k * nparts;
-          if (u >= U) break;
-          const float w = W[u * kMaxG + hq];
-          float4 &acc = u < n_exact ? ex : tr;
-          acc.x = fmaf(w, o[k].x, acc.x); acc.y = fmaf(w, o[k].y, acc.y);
-          acc.z = fmaf(w, o[k].z, acc.z); acc.w = fmaf(w, o[k].w, acc.w);
-        }
-      }
-    }
-    // combine the unit slices through shared memory (Ex/Tr rows, part 0 first)
-    for (int q = 0; q < nparts; ++q) {
-      if (part == q) {
-        float4 *e = reinterpret_cast<float4 *>(Ex + hq * kD) + c4;
-        float4 *t = reinterpret_cast<float4 *>(Tr + hq * kD) + c4;
-        if (q == 0) {
-          *e = ex;
-          *t = tr;
-        } else {
-          float4 e0 = *e, t0 = *t;
-          *e = make_float4(e0.x + ex.x, e0.y + ex.y, e0.z + ex.z, e0.w + ex.w);
-          *t = make_float4(t0.x + tr.x, t0.y + tr.y, t0.z + tr.z, t0.w + tr.w);
-        }
-      }
-      __syncthreads();
-    }
-  }
-  const bool any_tiles = U > n_exact;
+  fold_unit(a, sm, true);
+}
+
+// ------------------------------------------------------------- finalize ----
+// Ex/Tr: [g][128] exact and transformed sums, ML: [g] (M, L).  Maps Tr back
+// with one inverse transform per query head and writes out (or the partial
+// rows [m, l, o] for a sequence-split merge).
+__device__ void finalize_group(const AttnArgs &a, unsigned char *sm, int64_t b, int h, const float *Ex,
+                               const float *Tr, const float *ML, float *buf, bool any_tiles) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float *lee = reinterpret_cast<const float *>(sm + AttnSmem::kLee);
   for (int hq = warp; hq < a.g; hq += 8) {
     float x[4];
     const float4 t4 = reinterpret_cast<const float4 *>(Tr + hq * kD)[lane];
     x[0] = t4.x; x[1] = t4.y; x[2] = t4.z; x[3] = t4.w;
     if (any_tiles) transform128(x, lane, a.kind, true, buf + warp * 2 * kD, lee);
+    KVR_TRACE_POINT(1, 7);
     const float4 e4 = reinterpret_cast<const float4 *>(Ex + hq * kD)[lane];
     const float y[4] = {e4.x + (any_tiles ? x[0] : 0.f), e4.y + (any_tiles ? x[1] : 0.f),
                         e4.z + (any_tiles ? x[2] : 0.f), e4.w + (any_tiles ? x[3] : 0.f)};
@@ -457,36 +389,160 @@ __device__ void merge_group(const AttnArgs &a, unsigned char *sm, int64_t b, int
   }
 }
 
+// ---------------------------------------------------------------- merge ----
+// Run by the last CTA of a (b, h) when several CTAs share its units: one L2
+// round trip for the slot rows (o loads in registers while other threads
+// stage the slots' (m, l) in shared memory).
+__device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int h, bool any_tiles) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = b * a.n_kv + h;
+  const int NS = a.slots;
+  // layout (the unit staging region is free now): WL [NS][8] float2 | Ex | Tr | buf
+  float2 *WL = reinterpret_cast<float2 *>(sm);
+  float *Ex = reinterpret_cast<float *>(sm) + 2 * NS * kMaxG;
+  float *Tr = Ex + kMaxG * kD;
+  float *buf = Tr + kMaxG * kD;
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+  constexpr int UB = 8;
+  const int pairs = a.g * 32;
+  const int nparts = blockDim.x / pairs;  // 2 for g = 4, 1 for g = 8
+  const int p = tid % pairs, part = tid / pairs;
+  const int hq = p >> 5, c4 = p & 31;
+  float4 ex = make_float4(0.f, 0.f, 0.f, 0.f), tr = ex;
+  for (int s0 = 0; s0 < NS; s0 += UB * nparts) {
+    float4 oe[UB], ot[UB];
+#pragma unroll
+    for (int k = 0; k < UB; ++k) {
+      const int s = s0 + part + nparts * k;
+      const bool ok = part < nparts && s < NS;
+      const float *pr = ok ? part_row(a, row, s, hq) : nullptr;
+      oe[k] = ok ? __ldcg(reinterpret_cast<const float4 *>(pr + kPartEx) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ot[k] = ok ? __ldcg(reinterpret_cast<const float4 *>(pr + kPartTr) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (s0 == 0) {
+      for (int i = tid; i < NS * a.g; i += blockDim.x) {
+        const int s = i / a.g, h2 = i - s * a.g;
+        WL[s * kMaxG + h2] = __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, s, h2)));
+      }
+      __syncthreads();
+      for (int h2 = warp; h2 < a.g; h2 += 8) {
+        float mx = -INFINITY;
+        for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, WL[s * kMaxG + h2].x);
+        mx = warp_max(mx);
+        float l = 0.0f;
+        for (int s = lane; s < NS; s += 32) {
+          const float2 v = WL[s * kMaxG + h2];
+          const float w = (v.x == -INFINITY) ? 0.0f : expf(v.x - mx);
+          WL[s * kMaxG + h2].x = w;  // (m, l) -> (weight, l)
+          l += w * v.y;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+          ML[h2 * 2] = mx;
+          ML[h2 * 2 + 1] = l;
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < UB; ++k) {
+      const int s = s0 + part + nparts * k;
+      if (part >= nparts || s >= NS) break;
+      const float w = WL[s * kMaxG + hq].x;
+      ex.x = fmaf(w, oe[k].x, ex.x); ex.y = fmaf(w, oe[k].y, ex.y);
+      ex.z = fmaf(w, oe[k].z, ex.z); ex.w = fmaf(w, oe[k].w, ex.w);
+      tr.x = fmaf(w, ot[k].x, tr.x); tr.y = fmaf(w, ot[k].y, tr.y);
+      tr.z = fmaf(w, ot[k].z, tr.z); tr.w = fmaf(w, ot[k].w, tr.w);
+    }
+  }
+  for (int q = 0; q < nparts; ++q) {
+    if (part == q) {
+      float4 *e = reinterpret_cast<float4 *>(Ex + hq * kD) + c4;
+      float4 *t = reinterpret_cast<float4 *>(Tr + hq * kD) + c4;
+      if (q == 0) {
+        *e = ex;
+        *t = tr;
+      } else {
+        const float4 e0 = *e, t0 = *t;
+        *e = make_float4(e0.x + ex.x, e0.y + ex.y, e0.z + ex.z, e0.w + ex.w);
+        *t = make_float4(t0.x + tr.x, t0.y + tr.y, t0.z + tr.z, t0.w + tr.w);
+      }
+    }
+    __syncthreads();
+  }
+  KVR_TRACE_POINT(1, 6);
+  finalize_group(a, sm, b, h, Ex, Tr, ML, buf, any_tiles);
+}
+
 template <int TILE>
 __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   extern __shared__ __align__(128) unsigned char sm[];
-  const int u = blockIdx.x, h = blockIdx.y;
+  const int slot = blockIdx.x, h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int64_t row = b * a.n_kv + h;
+  const int tid = threadIdx.x;
   KVR_TRACE_POINT(1, 0);
-  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));  // visible after the unit's barriers
-  if (u < a.nchunk[0]) {
-    exact_unit(a, sm, b, h, 0, u, u);
-  } else if (u < a.nchunk[0] + a.nchunk[1]) {
-    exact_unit(a, sm, b, h, 1, u - a.nchunk[0], u);
-  } else {
-    tile_unit<TILE>(a, sm, b, h, u - a.nchunk[0] - a.nchunk[1], u);
+  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
+  float *AM = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
+  float *AL = reinterpret_cast<float *>(sm + AttnSmem::kAccL);
+  float *AEx = reinterpret_cast<float *>(sm + AttnSmem::kAccEx);
+  float *ATr = reinterpret_cast<float *>(sm + AttnSmem::kAccTr);
+  for (int i = tid; i < a.g * kD; i += blockDim.x) {
+    AEx[i] = 0.0f;
+    ATr[i] = 0.0f;
+  }
+  if (tid < a.g) {
+    AM[tid] = -INFINITY;
+    AL[tid] = 0.0f;
   }
   __syncthreads();
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  const int u_end = min(a.units, (slot + 1) * a.upc);
+  for (int u = slot * a.upc; u < u_end; ++u) {
+    if (u < a.nchunk[0]) {
+      exact_unit(a, sm, b, h, 0, u, u);
+    } else if (u < n_exact) {
+      exact_unit(a, sm, b, h, 1, u - a.nchunk[0], u);
+    } else {
+      tile_unit<TILE>(a, sm, b, h, u - n_exact, u);
+    }
+    __syncthreads();
+  }
   KVR_TRACE_POINT(1, 3);
+  const bool any_tiles = a.units > n_exact;
+  if (a.slots == 1) {
+    // this CTA owns every unit of its row: no partials, no merge
+    float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+    if (tid < a.g) {
+      ML[2 * tid] = AM[tid];
+      ML[2 * tid + 1] = AL[tid];
+    }
+    __syncthreads();
+    finalize_group(a, sm, b, h, AEx, ATr, ML, reinterpret_cast<float *>(sm), any_tiles);
+    return;
+  }
+  // write this CTA's partial rows, then the last CTA of the row merges
+  for (int i = tid; i < a.g * (kD / 4); i += blockDim.x) {
+    const int hq = i / (kD / 4), c4 = i - hq * (kD / 4);
+    float *pr = part_row(a, row, slot, hq);
+    reinterpret_cast<float4 *>(pr + kPartEx)[c4] = reinterpret_cast<const float4 *>(AEx + hq * kD)[c4];
+    reinterpret_cast<float4 *>(pr + kPartTr)[c4] = reinterpret_cast<const float4 *>(ATr + hq * kD)[c4];
+    if (c4 == 0) *reinterpret_cast<float2 *>(pr) = make_float2(AM[hq], AL[hq]);
+  }
+  __syncthreads();
   int *last = reinterpret_cast<int *>(sm + AttnSmem::kFlag) + 1;
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(&a.counters[row], 1u);
-    *last = (prev == (unsigned)a.units - 1);
+    *last = (prev == (unsigned)a.slots - 1);
   }
   __syncthreads();
   if (!*last) return;
   __threadfence();
   KVR_TRACE_POINT(1, 4);
-  merge_group(a, sm, b, h);
+  merge_slots(a, sm, b, h, any_tiles);
   KVR_TRACE_POINT(1, 5);
-  if (threadIdx.x == 0) a.counters[row] = 0u;
+  if (tid == 0) a.counters[row] = 0u;
 }
 
 // Merge kernel for sequence-split partials: one warp per query row.
@@ -523,8 +579,8 @@ struct AttnWs {
   size_t bytes;
 };
 
-static size_t merge_smem_bytes(int units) {
-  return (size_t)units * kMaxG * 4 + 2 * kMaxG * kD * 4 + 8 * 2 * kD * 4 + kD * 4;
+static size_t merge_smem_bytes(int slots) {
+  return (size_t)slots * kMaxG * 8 + 2 * kMaxG * kD * 4 + 8 * 2 * kD * 4;
 }
 
 static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) {
@@ -548,14 +604,24 @@ int sd1_fused_launch(const void *q, int q_dtype, int batch, int n_q, int n_kv, c
 int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
-                       float *qprime, unsigned *counters, float *scores, cudaStream_t st);
+                       float *qprime, unsigned *counters, float *scores, cudaStream_t st,
+                       const uint32_t *vbits, const uint16_t *vscale);
 
 int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool pdl = false) {
   if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
   size_t smem = AttnSmem::kTotal;
-  const size_t ms = merge_smem_bytes(a.units);
+  // Units per CTA: one unit per CTA while the rows leave the GPU idle (batch 1,
+  // latency-bound), more as rows grow, so about two CTAs per SM are launched
+  // and each folds its units on chip (batched decode, bandwidth-bound).
+  const int64_t rows = (int64_t)batch * a.n_kv;
+  const int64_t target = 2 * 148;
+  int upc = (int)((a.units * rows + target - 1) / target);
+  upc = upc < 1 ? 1 : (upc > a.units ? a.units : upc);
+  a.upc = upc;
+  a.slots = (a.units + upc - 1) / upc;
+  const size_t ms = merge_smem_bytes(a.slots);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
-  dim3 grid(a.units, a.n_kv, batch);
+  dim3 grid(a.slots, a.n_kv, batch);
   // per-device attribute cache (the attribute is per function and device)
   static thread_local int cached_dev = -1;
   static thread_local bool smem_set[3] = {false, false, false};
@@ -762,7 +828,7 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
   int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
-                              as_cuda(stream));
+                              as_cuda(stream), vbits, vscale);
   if (rc) return rc;
   // the attention kernel is a programmatic dependent of the selection
   // kernel: its window/tail units overlap the tile scan, its tile units wait

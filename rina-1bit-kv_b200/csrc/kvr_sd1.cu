@@ -157,6 +157,8 @@ struct SelectArgs {
   int32_t *sel;         // (B, n_kv, k_sel)
   float *sel_scores;    // (B, n_kv, k_sel) or null
   unsigned *counters;   // (B, n_kv), zero on entry, reset on exit
+  const uint32_t *vbits;   // optional: V data of the scanned tiles is
+  const uint16_t *vscale;  // prefetched into L2 for the attention kernel
 };
 
 template <int DTQ, int TILE>
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
     const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
     const uint16_t *__restrict__ kscale, int64_t nt_cap, int64_t n_tiles, int kind,
     float *__restrict__ scores /* (B, n_kv, n_tiles) */, float *__restrict__ qprime /* (B, n_q, d) or null */,
-    SelectArgs sa, int do_select) {
+    SelectArgs sa, int do_select, int64_t tpc) {
   __shared__ float lee_s[kD];
   __shared__ __align__(16) float buf_s[8][2 * kD];
   __shared__ __align__(16) float qp_s[kD];
@@ -181,23 +183,37 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   const int64_t row = (int64_t)b * n_kv + h;
   load_lee(lee_s);
 
-  // prefetch this warp's tile data while q' is formed
+  // Each CTA owns tiles [blockIdx.x * tpc, +tpc) of its row; warp w scores
+  // the pairs w, w + 8, ... of that range.  The first pair is loaded while q'
+  // is formed, and every later pair is loaded before the current one is
+  // scored (software pipeline in registers).
   constexpr int TPL = TILE / 32;  // tokens per lane
-  const int64_t t_first = (int64_t)blockIdx.x * kScoreTilesPerCta + warp * 2;
+  const int64_t cta_t0 = (int64_t)blockIdx.x * tpc;
+  const int64_t cta_t1 = min(n_tiles, cta_t0 + tpc);
   uint4 kb[2][TPL];
   uint16_t ks[2][4];
+  auto load_pair = [&](int64_t t_first, uint4 (&kbd)[2][TPL], uint16_t (&ksd)[2][4]) {
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int64_t t = t_first + u;
-    if (t < n_tiles) {
+    for (int u = 0; u < 2; ++u) {
+      const int64_t t = min(t_first + u, cta_t1 - 1);  // a lone last tile is scored twice, stored once
       const int64_t tix = row * nt_cap + t;
       const uint4 *src = reinterpret_cast<const uint4 *>(kbits + tix * TILE * 4);
 #pragma unroll
-      for (int r = 0; r < TPL; ++r) kb[u][r] = __ldg(src + lane + 32 * r);
+      for (int r = 0; r < TPL; ++r) kbd[u][r] = __ldg(src + lane + 32 * r);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) ks[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
+      for (int m = 0; m < 4; ++m) ksd[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
+      if (sa.vbits != nullptr && lane == 0 && t == t_first + u) {
+        // the selected tiles' V is read right after this kernel: stage every
+        // scanned tile's V bits + scales in L2 while this (latency-bound) scan runs
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.vbits + tix * TILE * 4),
+                     "r"((unsigned)(TILE * 16)) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.vscale + tix * kD),
+                     "r"((unsigned)(kD * 2)) : "memory");
+      }
     }
-  }
+  };
+  int64_t t_cur = cta_t0 + 2 * warp;
+  if (t_cur < cta_t1) load_pair(t_cur, kb, ks);
   // warp 0: all g query heads of the group are loaded before the (ordered) sum
   float qv[8][4];
   if (warp == 0) {
@@ -231,12 +247,27 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   __syncthreads();
   KVR_TRACE_POINT(0, 1);
 
+  while (t_cur < cta_t1) {  // warp-uniform
+    const int64_t t_next = t_cur + 16;
+    uint4 kbn[2][TPL];
+    uint16_t ksn[2][4];
+    if (t_next < cta_t1) load_pair(t_next, kbn, ksn);
+    float sc[2];
+    sd1_score_tile2<TILE>(qp_s, kb, ks, lane, sc);
+    if (lane == 0) {
+      scores[row * n_tiles + t_cur] = sc[0];
+      if (t_cur + 1 < cta_t1) scores[row * n_tiles + t_cur + 1] = sc[1];
+    }
+    t_cur = t_next;
+    if (t_cur < cta_t1) {
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int64_t t = t_first + u;
-    if (t >= n_tiles) continue;  // warp-uniform
-    const float score = sd1_score_tile<TILE>(qp_s, kb[u], ks[u], lane);
-    if (lane == 0) scores[row * n_tiles + t] = score;
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int r = 0; r < TPL; ++r) kb[u][r] = kbn[u][r];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) ks[u][m] = ksn[u][m];
+      }
+    }
   }
   if (!do_select) return;
 
@@ -371,7 +402,7 @@ size_t select_dyn_smem(int k_sel, int64_t n_tiles) {
 }
 
 template <int DTQ>
-static int launch_score(int tile, dim3 grid, cudaStream_t st, const void *q, int n_q, int n_kv,
+static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const void *q, int n_q, int n_kv,
                         const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind, float *scores,
                         float *qprime, SelectArgs sa, int do_select) {
   const size_t smem = do_select ? select_dyn_smem(sa.k_sel, nt) : 0;
@@ -381,7 +412,7 @@ static int launch_score(int tile, dim3 grid, cudaStream_t st, const void *q, int
     if (smem > 48 * 1024)                                                                                \
       cudaFuncSetAttribute(sd1_score_kernel<DTQ, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     sd1_score_kernel<DTQ, T><<<grid, 256, smem, st>>>(q, n_q, n_kv, kb, ks, cap, nt, kind, scores, qprime, sa, \
-                                                       do_select);                                       \
+                                                       do_select, tpc);                                  \
     break;
     KVR_SC(32)
     KVR_SC(64)
@@ -396,12 +427,21 @@ static int launch_score(int tile, dim3 grid, cudaStream_t st, const void *q, int
 int sd1_scores_impl(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                     const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, float *scores,
                     float *qprime, SelectArgs sa, int do_select, cudaStream_t st) {
-  dim3 grid((unsigned)((n_tiles + kScoreTilesPerCta - 1) / kScoreTilesPerCta), n_kv, batch);
-  if (n_tiles <= 0) grid.x = 1;
+  // Tiles per CTA: about one resident wave (2 CTAs per SM) in total, at least
+  // 16 (two per warp); each CTA forms q' once for all of its tiles.
+  const int64_t rows = (int64_t)batch * n_kv;
+  int64_t cph = 296 / (rows > 0 ? rows : 1);
+  const int64_t max_cph = (n_tiles + kScoreTilesPerCta - 1) / kScoreTilesPerCta;
+  cph = cph < 1 ? 1 : (cph > max_cph ? max_cph : cph);
+  if (cph < 1) cph = 1;
+  int64_t tpc = (n_tiles + cph - 1) / cph;
+  tpc = (tpc + kScoreTilesPerCta - 1) / kScoreTilesPerCta * kScoreTilesPerCta;
+  if (tpc < kScoreTilesPerCta) tpc = kScoreTilesPerCta;
+  dim3 grid((unsigned)(n_tiles > 0 ? (n_tiles + tpc - 1) / tpc : 1), n_kv, batch);
   switch (q_dtype) {
-    case KVR_F32: return launch_score<KVR_F32>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
-    case KVR_F16: return launch_score<KVR_F16>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
-    default: return launch_score<KVR_BF16>(tile, grid, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+    case KVR_F32: return launch_score<KVR_F32>(tile, grid, tpc, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+    case KVR_F16: return launch_score<KVR_F16>(tile, grid, tpc, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+    default: return launch_score<KVR_BF16>(tile, grid, tpc, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
   }
 }
 
@@ -472,7 +512,8 @@ namespace kvr {
 int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
-                       float *qprime, unsigned *counters, float *scores, cudaStream_t st) {
+                       float *qprime, unsigned *counters, float *scores, cudaStream_t st,
+                       const uint32_t *vbits, const uint16_t *vscale) {
   int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
   if (rc) return rc;
   KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
@@ -481,7 +522,7 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
   KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_select: n_tiles > nt_cap");
   KVR_REQUIRE(n_tiles == 0 || (kbits && kscale), "kvr_sd1_select: null store pointers");
   KVR_REQUIRE((int64_t)batch * n_kv <= kWsMaxRows, "kvr_sd1_select: batch*n_kv > %d", kWsMaxRows);
-  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters};
+  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters, vbits, vscale};
   // With no full tile there is nothing to score; the kernel still forms q'
   // and writes an all-empty selection.
   return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
@@ -507,7 +548,7 @@ extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, in
   char *p = reinterpret_cast<char *>(workspace);
   return sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                             ex_t1, tile_base, sel, sel_scores, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters),
-                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream));
+                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream), nullptr, nullptr);
 }
 
 extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
