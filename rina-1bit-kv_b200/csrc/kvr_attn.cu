@@ -58,6 +58,7 @@ struct AttnArgs {
   int units;  // work units per (b, h)
   int upc;    // units per CTA
   int slots;  // CTAs per (b, h) = ceil(units / upc)
+  int pipelined;  // several units per CTA over fp16 exact data: cp.async double buffering
 };
 
 // ---- runtime-dtype loads
@@ -79,7 +80,10 @@ struct AttnSmem {
   static constexpr int kVS = kKS + kD * 2;                           // fp16 [128]
   static constexpr int kLUT = kVS + kD * 2;                          // fp32 [g][32][16]
   static constexpr int kTileEnd = kLUT + kMaxG * 32 * 16 * 4;
-  static constexpr int kUnion = kExactEnd > kTileEnd ? kExactEnd : kTileEnd;
+  static constexpr int kRawRow = kD * 2 + 16;                         // padded fp16 row (272 B)
+  static constexpr int kRawBuf = 2 * kChunk * kRawRow;                // K + V rows of one chunk (pipelined)
+  static constexpr int kUnion0 = kExactEnd > kTileEnd ? kExactEnd : kTileEnd;
+  static constexpr int kUnion = kUnion0 > 2 * kRawBuf ? kUnion0 : 2 * kRawBuf;
   static constexpr int kQ = kUnion;                                  // fp32 [8][128]
   static constexpr int kS = kQ + kMaxG * kD * 4;                     // fp32 [8][128] scores / reduce
   static constexpr int kP = kS + kMaxG * kD * 4;                     // fp32 [128][8] probabilities
@@ -93,7 +97,15 @@ struct AttnSmem {
   static constexpr int kAccEx = kAccSC + kMaxG * 2 * 4;               // fp32 [8][128] exact part
   static constexpr int kAccTr = kAccEx + kMaxG * kD * 4;              // fp32 [8][128] transformed part
   static constexpr int kTotal = kAccTr + kMaxG * kD * 4;
+  // pipelined mode (several units per CTA, fp16 exact data): two raw staging
+  // buffers alias the unit region above; LUT and q' get their own space
+  static constexpr int kRaw0 = 0;
+  static constexpr int kRaw1 = kRawBuf;
+  static constexpr int kPipeQp = kTotal;                              // fp32 [8][128] q' * inv_scale
+  static constexpr int kPipeLUT2 = kPipeQp + kMaxG * kD * 4;          // fp32 [8][32][16]
+  static constexpr int kPipeTotal = kPipeLUT2 + kMaxG * 32 * 16 * 4;
 };
+static_assert(2 * AttnSmem::kRawBuf <= AttnSmem::kQ, "raw buffers must stay inside the unit region");
 
 // Softmax over the scores S[hq][0..nt) of every query head; writes P[j][hq],
 // ML[hq] = (m, l).  Rows with no valid token get m = -inf, l = 0.
@@ -349,6 +361,225 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   fold_unit(a, sm, true);
 }
 
+// ------------------------------------------------------------ pipelined ----
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Issues the copies of unit u into raw buffer `buf` (no wait).
+template <int TILE>
+__device__ void pipe_issue(const AttnArgs &a, unsigned char *buf, int64_t b, int h, int u) {
+  const int tid = threadIdx.x;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  if (u < n_exact) {
+    const int seg = u < a.nchunk[0] ? 0 : 1;
+    const int chunk = seg == 0 ? u : u - a.nchunk[0];
+    const int64_t t0 = (int64_t)chunk * kChunk;
+    const int nt = (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk);
+    const uint16_t *kp = reinterpret_cast<const uint16_t *>(a.k[seg]);
+    const uint16_t *vp = reinterpret_cast<const uint16_t *>(a.v[seg]);
+    const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD;
+    for (int i = tid; i < 2 * nt * 16; i += blockDim.x) {
+      const int kv = i / (nt * 16), r = i - kv * nt * 16, j = r >> 4, c = r & 15;
+      const uint16_t *src = (kv == 0 ? kp : vp) + base + (t0 + j) * a.tok_stride[seg] + c * 8;
+      cp_async16(buf + kv * kChunk * AttnSmem::kRawRow + j * AttnSmem::kRawRow + c * 16, src);
+    }
+  } else {
+    griddep_wait();  // the selection comes from the preceding kernel
+    const int64_t row = b * a.n_kv + h;
+    const int32_t t = a.sel[row * a.k_sel + (u - n_exact)];
+    if (t < 0) return;
+    const int64_t tix = row * a.nt_cap + t;
+    constexpr int kBitChunks = TILE;  // TILE * 16 bytes
+    const unsigned char *kb = reinterpret_cast<const unsigned char *>(a.kbits + tix * TILE * 4);
+    const unsigned char *vb = reinterpret_cast<const unsigned char *>(a.vbits + tix * TILE * 4);
+    const unsigned char *ks = reinterpret_cast<const unsigned char *>(a.kscale + tix * kD);
+    const unsigned char *vs = reinterpret_cast<const unsigned char *>(a.vscale + tix * kD);
+    for (int i = tid; i < 2 * kBitChunks + 32; i += blockDim.x) {
+      if (i < kBitChunks) cp_async16(buf + i * 16, kb + i * 16);
+      else if (i < 2 * kBitChunks) cp_async16(buf + 2048 + (i - kBitChunks) * 16, vb + (i - kBitChunks) * 16);
+      else if (i < 2 * kBitChunks + 16) cp_async16(buf + 4096 + (i - 2 * kBitChunks) * 16, ks + (i - 2 * kBitChunks) * 16);
+      else cp_async16(buf + 4352 + (i - 2 * kBitChunks - 16) * 16, vs + (i - 2 * kBitChunks - 16) * 16);
+    }
+  }
+}
+
+// Exact unit from the raw fp16 buffer (rows of kRawRow bytes).
+__device__ void pipe_exact(const AttnArgs &a, unsigned char *sm, const unsigned char *buf, int nt) {
+  const float *Qs = reinterpret_cast<const float *>(sm + AttnSmem::kQ);
+  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
+  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int p = warp; p < a.g * 2; p += 8) {
+    const int hq = p >> 1, j = (p & 1) * 32 + lane;
+    const uint2 *kr = reinterpret_cast<const uint2 *>(buf + j * AttnSmem::kRawRow);
+    const float4 *qr = reinterpret_cast<const float4 *>(Qs + hq * kD);
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < 32; ++c) {
+      const float4 kk = cvt4(make_uint4(kr[c].x, kr[c].y, 0u, 0u), KVR_F16);
+      const float4 qq = qr[c];
+      a0 = fmaf(qq.x, kk.x, a0);
+      a1 = fmaf(qq.y, kk.y, a1);
+      a2 = fmaf(qq.z, kk.z, a2);
+      a3 = fmaf(qq.w, kk.w, a3);
+    }
+    S[hq * kD + j] = j < nt ? (a0 + a1) + (a2 + a3) : -INFINITY;
+  }
+  __syncthreads();
+  softmax_rows(a, nt, S, P, ML);
+  __syncthreads();
+  const int c = tid & 127, half = tid >> 7;
+  float o[kMaxG];
+#pragma unroll
+  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
+  const __half *V = reinterpret_cast<const __half *>(buf + kChunk * AttnSmem::kRawRow);
+  const int j1 = min(nt, half * 32 + 32);
+  for (int j = half * 32; j < j1; ++j) {
+    const float vv = __half2float(V[j * (AttnSmem::kRawRow / 2) + c]);
+    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
+    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
+    o[0] = fmaf(p0.x, vv, o[0]); o[1] = fmaf(p0.y, vv, o[1]);
+    o[2] = fmaf(p0.z, vv, o[2]); o[3] = fmaf(p0.w, vv, o[3]);
+    if (a.g > 4) {
+      o[4] = fmaf(p1.x, vv, o[4]); o[5] = fmaf(p1.y, vv, o[5]);
+      o[6] = fmaf(p1.z, vv, o[6]); o[7] = fmaf(p1.w, vv, o[7]);
+    }
+  }
+  if (half == 1)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
+  __syncthreads();
+  if (half == 0)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] += o[hq];
+  __syncthreads();
+  fold_unit(a, sm, false);
+}
+
+// sd1 tile unit from the raw buffer: [KB 2 KB | VB 2 KB | KS 256 B | VS 256 B].
+template <int TILE>
+__device__ void pipe_tile(const AttnArgs &a, unsigned char *sm, const unsigned char *buf) {
+  const uint32_t *KB = reinterpret_cast<const uint32_t *>(buf);
+  const uint32_t *VB = reinterpret_cast<const uint32_t *>(buf + 2048);
+  const uint16_t *KS = reinterpret_cast<const uint16_t *>(buf + 4096);
+  const uint16_t *VS = reinterpret_cast<const uint16_t *>(buf + 4352);
+  float *LUT = reinterpret_cast<float *>(sm + AttnSmem::kPipeLUT2);
+  const float *Qp = reinterpret_cast<const float *>(sm + AttnSmem::kPipeQp);
+  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
+  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
+  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < a.g * 32; i += blockDim.x) {
+    const int hq = i >> 5, grp = i & 31;
+    float av[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) av[r] = Qp[hq * kD + 4 * grp + r] * __half2float(__ushort_as_half(KS[4 * grp + r]));
+    float *L = LUT + (hq * 32 + grp) * 16;
+#pragma unroll
+    for (int x = 0; x < 16; ++x) {
+      float s = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) s += ((x >> r) & 1) ? av[r] : -av[r];
+      L[x] = s;
+    }
+  }
+  __syncthreads();
+  constexpr int NB = TILE / 32;
+  for (int p = warp; p < a.g * NB; p += 8) {
+    const int hq = p / NB, j = (p - hq * NB) * 32 + lane;
+    const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[j];
+    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+    const float *L = LUT + hq * 32 * 16;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int grp = 0; grp < 32; ++grp) acc[grp & 3] += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
+    S[hq * kD + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  }
+  __syncthreads();
+  softmax_rows(a, TILE, S, P, ML);
+  __syncthreads();
+  const int c = tid & 127, half = tid >> 7;
+  float o[kMaxG];
+#pragma unroll
+  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
+  const int word = c >> 5, bit = c & 31;
+  for (int j = half * (TILE / 2); j < (half + 1) * (TILE / 2); ++j) {
+    const float bf = (float)((VB[j * 4 + word] >> bit) & 1u);
+    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
+    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
+    o[0] = fmaf(p0.x, bf, o[0]); o[1] = fmaf(p0.y, bf, o[1]);
+    o[2] = fmaf(p0.z, bf, o[2]); o[3] = fmaf(p0.w, bf, o[3]);
+    if (a.g > 4) {
+      o[4] = fmaf(p1.x, bf, o[4]); o[5] = fmaf(p1.y, bf, o[5]);
+      o[6] = fmaf(p1.z, bf, o[6]); o[7] = fmaf(p1.w, bf, o[7]);
+    }
+  }
+  if (half == 1)
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
+  __syncthreads();
+  if (half == 0) {
+    const float vs = __half2float(__ushort_as_half(VS[c]));
+    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - ML[hq * 2 + 1]);
+  }
+  __syncthreads();
+  fold_unit(a, sm, true);
+}
+
+// All units [u_begin, u_end) of this CTA with the next unit's copies in
+// flight while the current one is computed.
+template <int TILE>
+__device__ void pipe_units(const AttnArgs &a, unsigned char *sm, int64_t b, int h, int u_begin, int u_end) {
+  const int tid = threadIdx.x;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  // per-row query data, loaded once
+  float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);
+  for (int i = tid; i < a.g * 32; i += blockDim.x) {
+    const int hq = i >> 5, qd = i & 31;
+    const float4 x = cvt4(raw4(a.q, (b * a.n_q + (int64_t)h * a.g + hq) * kD + qd * 4, a.q_dt), a.q_dt);
+    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] =
+        make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
+  }
+  bool have_qp = false;
+  pipe_issue<TILE>(a, sm + AttnSmem::kRaw0, b, h, u_begin);
+  cp_async_commit();
+  for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
+    unsigned char *cur = sm + ((i & 1) ? AttnSmem::kRaw1 : AttnSmem::kRaw0);
+    unsigned char *nxt = sm + ((i & 1) ? AttnSmem::kRaw0 : AttnSmem::kRaw1);
+    if (u + 1 < u_end) {
+      pipe_issue<TILE>(a, nxt, b, h, u + 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    if (u >= n_exact && !have_qp) {
+      griddep_wait();
+      float *Qp = reinterpret_cast<float *>(sm + AttnSmem::kPipeQp);
+      for (int k = tid; k < a.g * 32; k += blockDim.x) {
+        const int hq = k >> 5, qd = k & 31;
+        const float4 x = __ldg(reinterpret_cast<const float4 *>(a.qprime + (b * a.n_q + (int64_t)h * a.g + hq) * kD) + qd);
+        reinterpret_cast<float4 *>(Qp + hq * kD)[qd] =
+            make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
+      }
+      have_qp = true;
+    }
+    __syncthreads();
+    if (u < n_exact) {
+      const int seg = u < a.nchunk[0] ? 0 : 1;
+      const int chunk = seg == 0 ? u : u - a.nchunk[0];
+      const int64_t t0 = (int64_t)chunk * kChunk;
+      pipe_exact(a, sm, cur, (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk));
+    } else {
+      const int64_t row = b * a.n_kv + h;
+      if (a.sel[row * a.k_sel + (u - n_exact)] >= 0) pipe_tile<TILE>(a, sm, cur);
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------- finalize ----
 // Ex/Tr: [g][128] exact and transformed sums, ML: [g] (M, L).  Maps Tr back
 // with one inverse transform per query head and writes out (or the partial
@@ -498,6 +729,9 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   __syncthreads();
   const int n_exact = a.nchunk[0] + a.nchunk[1];
   const int u_end = min(a.units, (slot + 1) * a.upc);
+  if (a.pipelined) {
+    if (slot * a.upc < u_end) pipe_units<TILE>(a, sm, b, h, slot * a.upc, u_end);
+  } else
   for (int u = slot * a.upc; u < u_end; ++u) {
     if (u < a.nchunk[0]) {
       exact_unit(a, sm, b, h, 0, u, u);
@@ -619,6 +853,16 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
   upc = upc < 1 ? 1 : (upc > a.units ? a.units : upc);
   a.upc = upc;
   a.slots = (a.units + upc - 1) / upc;
+  // the pipelined path streams fp16 rows with 16-byte async copies
+  bool f16 = upc > 1;
+  for (int s = 0; s < 2; ++s) {
+    if (a.n[s] == 0) continue;
+    f16 = f16 && a.kdt[s] == KVR_F16 && a.vdt[s] == KVR_F16 && (a.tok_stride[s] % 8) == 0 &&
+          (a.batch_stride[s] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.k[s]) % 16) == 0 &&
+          (reinterpret_cast<uintptr_t>(a.v[s]) % 16) == 0;
+  }
+  a.pipelined = f16 ? 1 : 0;
+  if (a.pipelined) smem = AttnSmem::kPipeTotal;
   const size_t ms = merge_smem_bytes(a.slots);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
   dim3 grid(a.slots, a.n_kv, batch);
