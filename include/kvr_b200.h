@@ -234,6 +234,17 @@ KVR_API int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, 
                         int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
                         int32_t *sel_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
+/* Prefill-sized tile scoring on the tensor cores (tcgen05, kind::f16):
+ * q (nq, n_q, d) post-RoPE queries of a prefill block (batch 1); for every
+ * query and KV head, the score of each stored tile is the max over its tokens
+ * of q'.k_hat with q' = fp16(T(group mean of q)) and k_hat = s (2 bit - 1)
+ * (fp32 accumulation).  scores (nq, n_kv, n_tiles) fp32.  tile must be 64.
+ * No reference counterpart (north_star: tensor cores for prefill Q.K^T). */
+KVR_API size_t kvr_sd1_prefill_workspace_bytes(int64_t nq, int n_kv);
+KVR_API int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, int n_q, int n_kv, const uint32_t *kbits,
+                                   const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
+                                   float *scores, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
 /* Partial-attention merge for a sequence split across P sources:
  * partials (P, n_q, d + 2) fp32 rows = [m, l, o_0 .. o_{d-1}] with o
  * unnormalised (sum_j e^{s_j - m} v_j); out (n_q, d) = sum_p e^{m_p-M} o_p / sum_p e^{m_p-M} l_p. */

@@ -307,3 +307,26 @@ def decode_attention(q, win_k, win_v, tiles_k, tiles_v, scale=None):
     s = s - s.max(-1, keepdims=True)
     w = np.exp(s)
     return (w / w.sum(-1, keepdims=True)) @ v
+
+
+# ----------------------------------------------------------------------------
+# prefill-sized tile scoring (tensor cores)
+# ----------------------------------------------------------------------------
+
+
+def prefill_qprime_f16(q: np.ndarray, n_kv: int, kind: str) -> np.ndarray:
+    """q (Nq, n_q, d) post-RoPE queries of a prefill block -> (Nq, n_kv, d) fp16:
+    the GQA-group mean (q_group_mean_f32 order) transformed by T, rounded to fp16."""
+    out = np.stack([transform(q_group_mean_f32(qi, n_kv), kind) for qi in q.astype(F32)])
+    return out.astype(F16)
+
+
+def prefill_tile_scores(qp16: np.ndarray, kbits: np.ndarray, kscale: np.ndarray) -> np.ndarray:
+    """qp16 (Nq, d) fp16 transformed queries of one KV head; kbits (nt, t, d/32),
+    kscale (nt, d).  Score of tile i for query r = max over the tile's tokens j of
+    the exact dot q'_r . k_hat_j, k_hat_j = s (2 bit_j - 1) (transformed domain,
+    exact products; the kernels accumulate in fp32).  float64 (Nq, nt)."""
+    b = unpack_bits(kbits).astype(np.float64) * 2.0 - 1.0          # (nt, t, d)
+    khat = b * kscale.astype(np.float64)[:, None, :]
+    s = np.einsum("rd,ntd->rnt", qp16.astype(np.float64), khat)
+    return s.max(-1)

@@ -346,6 +346,20 @@ def sd1_decode_tiles(store: Sd1Store, sel):
     return ok, ov
 
 
+def sd1_prefill_scores(store: Sd1Store, q):
+    """Tensor-core tile scores for a block of prefill queries (batch-1 store):
+    q (nq, n_q, d) -> (nq, n_kv, n_tiles) fp32."""
+    if store.batch != 1:
+        raise ValueError("prefill scoring takes a batch-1 store")
+    q = _c(q)
+    nq, n_q, _ = q.shape
+    out = torch.empty(nq, store.n_kv, store.n_tiles, dtype=torch.float32, device=q.device)
+    ws = N.workspace("sd1_prefill", call("kvr_sd1_prefill_workspace_bytes", nq, store.n_kv), q.device)
+    call("kvr_sd1_prefill_scores", ptr(q), dtype_code(q), nq, n_q, store.n_kv, ptr(store.kbits), ptr(store.kscale),
+         store.nt_cap, store.n_tiles, store.tile, N.TRANSFORMS[store.kind], ptr(out), ptr(ws), ws.numel(), stream())
+    return out
+
+
 def workspace_status(ws: torch.Tensor):
     call("kvr_workspace_status", ptr(ws), stream())
 
