@@ -4,31 +4,45 @@
 // decode over an existing sd1 store) every query must score every stored
 // tile: S = Q' Khat^T with Q' the transformed GQA-group-mean queries and
 // Khat the decoded keys s_c (2 bit - 1) in the transformed domain.  That is a
-// dense contraction (M = 128 queries, N = 256 tokens, K = 128 channels per
-// CTA), so it runs as tcgen05.mma (kind::f16: fp16 operands, fp32 accumulate
-// in tensor memory).  Khat is exact in fp16 (the scales are fp16 and the
-// signs are exact); Q' is rounded to fp16 once.  The epilogue reads the
-// accumulator back with tcgen05.ld and reduces each query's row to the max
-// over each 64-token tile.  Spec: oracle/sd1_ref.py prefill_tile_scores.
+// dense contraction, so it runs as tcgen05.mma (kind::f16: fp16 operands,
+// fp32 accumulate in tensor memory).  Khat is exact in fp16 (the scales are
+// fp16 and the signs are exact); Q' is rounded to fp16 once.  Spec:
+// oracle/sd1_ref.py prefill_tile_scores.
+//
+// Work split: a CTA owns 256 stored tokens (4 tiles of 64) of one KV head.
+// It decodes them once into shared memory (B, 64 KB) and keeps them there
+// while it walks over 128-query blocks of Q' (A, 32 KB each).  The prep
+// kernel writes Q' already in the MMA's shared-memory layout, so each A block
+// is ONE contiguous bulk copy (cp.async.bulk, local memory, no multicast)
+// into a 4-deep ring.  Per block one thread issues 8 MMAs (M 128, N 256,
+// K 16 each) into one of two 256-column TMEM accumulators; while the tensor
+// core works on block i+1, the 8 warps read block i's accumulator back with
+// tcgen05.ld and reduce every query row to the max over each 64-token tile.
 //
 // Operands sit in shared memory in the K-major, no-swizzle canonical layout:
 // 8-row x 16-byte core matrices; SBO = 128 B between 8-row groups, LBO =
 // (rows/8) * 128 B between 8-element K chunks; one MMA consumes K = 16 (two
-// chunks), so K = 128 takes 8 MMAs issued by one thread.  This file is used by
-// single-GPU calls only and its copies read local memory (no multicast).
+// chunks).  Every wait is bounded; a timeout sets the error word, lets the
+// copies and MMAs in flight drain and frees the tensor memory.
 #include "kvr_common.cuh"
 #include "kvr_transform.cuh"
 
 namespace kvr {
 
-constexpr int kPfM = 128;       // queries per CTA (MMA M)
-constexpr int kPfN = 256;       // tokens per CTA (MMA N) = 4 tiles of 64
+constexpr int kPfM = 128;        // queries per block (MMA M)
+constexpr int kPfN = 256;        // tokens per CTA (MMA N) = 4 tiles of 64
 constexpr int kPfTile = 64;
-constexpr int kPfThreads = 128;  // 4 warps: one per TMEM lane quarter
+constexpr int kPfThreads = 320;  // 8 reader warps + MMA warp + copy warp
 constexpr uint32_t kPfLboA = (kPfM / 8) * 128;  // 2048 B
 constexpr uint32_t kPfLboB = (kPfN / 8) * 128;  // 4096 B
-constexpr int kPfSmemA = kPfM * kD * 2;         // 32 KB
+constexpr int kPfSmemA = kPfM * kD * 2;         // 32 KB per A block
 constexpr int kPfSmemB = kPfN * kD * 2;         // 64 KB
+constexpr int kPfStages = 4;                    // A ring depth
+constexpr int kPfOffA = kPfSmemB;
+constexpr int kPfOffLut = kPfOffA + kPfStages * kPfSmemA;
+constexpr int kPfOffBar = kPfOffLut + 16 * 8;
+constexpr int kPfSmem = kPfOffBar + 8 * (2 * kPfStages + 4) + 16;
+constexpr uint32_t kPfTmemCols = 2 * kPfN;      // double-buffered accumulator
 
 // sm100 shared-memory matrix descriptor, K-major, no swizzle
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -46,41 +60,52 @@ constexpr uint32_t kPfIdesc = (1u << 4)                      // D format: F32
                               | ((uint32_t)(kPfN >> 3) << 17)  // N / 8
                               | ((uint32_t)(kPfM >> 4) << 24); // M / 16
 
-// q (Nq, n_q, d) -> qp16 (Nq, n_kv, d) fp16: group mean, transform, round.
+// Byte offset of (query m, 8-channel chunk kc) inside one A block.
+__device__ __forceinline__ uint32_t pf_a_off(int m, int kc) {
+  return (uint32_t)kc * kPfLboA + (uint32_t)(m >> 3) * 128 + (uint32_t)(m & 7) * 16;
+}
+
+// q (Nq, n_q, d) -> Q' fp16 in A-block layout: block (h, qb) is 32 KB at
+// ((h * nqb + qb) * 32 KB); query rows past nq are zero.
 template <int DTQ>
 __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void *__restrict__ q, int64_t nq, int n_q,
-                                                            int n_kv, int kind, __half *__restrict__ qp16) {
+                                                            int n_kv, int kind, int64_t nqb,
+                                                            unsigned char *__restrict__ qa) {
   __shared__ float lee_s[kD];
   __shared__ __align__(16) float buf_s[8][2 * kD];
   load_lee(lee_s);
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = n_q / n_kv;
-  const int64_t rows = nq * n_kv;
+  const int64_t rows = nqb * kPfM * n_kv;
   for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += (int64_t)gridDim.x * 8) {
     const int64_t i = r / n_kv;
     const int h = (int)(r - i * n_kv);
-    const int64_t qb = (i * n_q + (int64_t)h * g) * kD + lane * 4;
-    float acc[4];
-    load4<DTQ>(q, qb, acc);
-    for (int k = 1; k < g; ++k) {
-      float t[4];
-      load4<DTQ>(q, qb + (int64_t)k * kD, t);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (i < nq) {  // warp-uniform
+      const int64_t qb = (i * n_q + (int64_t)h * g) * kD + lane * 4;
+      load4<DTQ>(q, qb, acc);
+      for (int k = 1; k < g; ++k) {
+        float t[4];
+        load4<DTQ>(q, qb + (int64_t)k * kD, t);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], t[e]);
+        for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], t[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = __fdiv_rn(acc[e], (float)g);
+      transform128(acc, lane, kind, false, buf_s[warp], lee_s);
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] = __fdiv_rn(acc[e], (float)g);
-    transform128(acc, lane, kind, false, buf_s[warp], lee_s);
-    __half2 *dst = reinterpret_cast<__half2 *>(qp16 + r * kD + lane * 4);
+    const int64_t blk = (int64_t)h * nqb + i / kPfM;
+    const int m = (int)(i % kPfM);
+    __half2 *dst = reinterpret_cast<__half2 *>(qa + blk * kPfSmemA + pf_a_off(m, lane >> 1) + (lane & 1) * 8);
     dst[0] = __floats2half2_rn(acc[0], acc[1]);
     dst[1] = __floats2half2_rn(acc[2], acc[3]);
   }
 }
 
 struct PrefillArgs {
-  const __half *qp16;  // (Nq, n_kv, d)
-  int64_t nq;
+  const unsigned char *qa;  // A blocks, (n_kv, nqb) x 32 KB
+  int64_t nq, nqb;
   int n_kv;
   const uint32_t *kbits;
   const uint16_t *kscale;
@@ -89,132 +114,241 @@ struct PrefillArgs {
   unsigned *err;
 };
 
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, unsigned phase) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it)
+    if (mbar_try_wait(bar, phase)) return true;
+  return false;
+}
+// Same, but also gives up once another role has aborted.
+__device__ __forceinline__ bool pf_wait_or_abort(uint64_t *bar, unsigned phase, volatile int *abort_s) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((it & 255u) == 255u && *abort_s) return false;
+  }
+  return false;
+}
+// B decoded: named barrier 1 over the 8 reader warps and the MMA warp
+__device__ __forceinline__ void pf_b_ready_sync() { asm volatile("bar.sync 1, 288;" ::: "memory"); }
+
+__device__ __forceinline__ void pf_mma_block(uint32_t tmem_d, uint32_t a_base, uint32_t b_base) {
+#pragma unroll
+  for (int s = 0; s < kD / 16; ++s) {
+    const uint64_t da = umma_desc(a_base + s * 2 * kPfLboA, kPfLboA, 128);
+    const uint64_t db = umma_desc(b_base + s * 2 * kPfLboB, kPfLboB, 128);
+    const uint32_t acc = s > 0 ? 1u : 0u;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(kPfIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+  }
+}
+
+__device__ __forceinline__ void pf_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void pf_tmem_ld32(uint32_t taddr, uint32_t *r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// max of 64 fp32 bit patterns (tree, exact)
+__device__ __forceinline__ float pf_max64(const uint32_t *r) {
+  float m[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m[e] = __uint_as_float(r[e]);
+#pragma unroll
+  for (int e = 8; e < 64; ++e) m[e & 7] = fmaxf(m[e & 7], __uint_as_float(r[e]));
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
+// Roles: warps 0-7 decode B, then read accumulators back (warp w: TMEM lanes
+// 32(w%4).., columns 128(w/4)..); warp 8 lane 0 issues the MMAs; warp 9 lane 0
+// streams the A blocks.  Barriers: afull[s] (copy landed), aempty[s] (MMAs
+// reading stage s done, via tcgen05.commit), done[b] (accumulator b ready),
+// tfree[b] (the 8 reader warps are through with accumulator b).
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillArgs a) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char *As = sm;                 // [16 kc][16 mg][8 r][16 B]
-  unsigned char *Bs = sm + kPfSmemA;      // [16 kc][32 ng][8 r][16 B]
-  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + kPfSmemA + kPfSmemB);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kPfSmemA + kPfSmemB + 16);
-  int *ok_s = reinterpret_cast<int *>(sm + kPfSmemA + kPfSmemB + 32);
+  unsigned char *Bs = sm;                         // [16 kc][32 ng][8 r][16 B]
+  unsigned char *As = sm + kPfOffA;               // kPfStages x [16 kc][16 mg][8 r][16 B]
+  uint2 *lut = reinterpret_cast<uint2 *>(sm + kPfOffLut);  // nibble -> fp16 sign-flip masks
+  uint64_t *afull = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
+  uint64_t *aempty = afull + kPfStages;
+  uint64_t *done = aempty + kPfStages;
+  uint64_t *tfree = done + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+  volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h = blockIdx.z;
-  const int64_t q0 = (int64_t)blockIdx.y * kPfM;
   const int64_t t0 = (int64_t)blockIdx.x * (kPfN / kPfTile);  // first tile of this CTA
   const int64_t row = h;                                      // batch 1: store row = head
+  const int64_t qb0 = blockIdx.y, qstep = gridDim.y;
+  const int64_t nblk = qb0 < a.nqb ? (a.nqb - qb0 + qstep - 1) / qstep : 0;
+  const unsigned char *qa_h = a.qa + (int64_t)h * a.nqb * kPfSmemA;
 
-  // ---- TMEM accumulator: 256 fp32 columns x 128 lanes
-  if (warp == 0) {
+  if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kPfN));
+                 "r"(kPfTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  if (tid == 0) {
-    ok_s[0] = 1;
-    mbar_init(bar, 1);
+  if (tid < 16) {  // channel pair e of a nibble: bits 2e, 2e+1 -> halves 0/1 of word e
+    const uint32_t nb = ~(uint32_t)tid;
+    lut[tid] = make_uint2(((nb & 1u) << 15) | ((nb & 2u) << 30), ((nb & 4u) << 13) | ((nb & 8u) << 28));
   }
-
-  // ---- A: 128 queries x 128 channels fp16 (rows past nq are zero)
-  for (int i = tid; i < kPfM * (kD / 8); i += kPfThreads) {
-    const int m = i >> 4, kc = i & 15;  // 16-byte chunk (8 channels) of query m
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (q0 + m < a.nq) v = __ldg(reinterpret_cast<const uint4 *>(a.qp16 + ((q0 + m) * a.n_kv + h) * kD + kc * 8));
-    *reinterpret_cast<uint4 *>(As + kc * kPfLboA + (m >> 3) * 128 + (m & 7) * 16) = v;
-  }
-  // ---- B: 256 tokens x 128 channels, k_hat = +-s (fp16, exact)
-  for (int i = tid; i < kPfN * (kD / 8); i += kPfThreads) {
-    const int n = i >> 4, kc = i & 15;
-    const int64_t tile = t0 + n / kPfTile;
-    const int j = n % kPfTile;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (tile < a.n_tiles) {
-      const int64_t tix = row * a.nt_cap + tile;
-      const uint32_t w = __ldg(a.kbits + (tix * kPfTile + j) * 4 + (kc >> 2));
-      const uint4 s = __ldg(reinterpret_cast<const uint4 *>(a.kscale + tix * kD + kc * 8));
-      const uint32_t sw[4] = {s.x, s.y, s.z, s.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c0 = kc * 8 + 2 * e;  // channels c0, c0 + 1
-        uint32_t lo = sw[e] & 0xffffu, hi = sw[e] >> 16;
-        if (!((w >> (c0 & 31)) & 1u)) lo ^= 0x8000u;        // sign bit 0 -> -s
-        if (!((w >> ((c0 + 1) & 31)) & 1u)) hi ^= 0x8000u;
-        o[e] = lo | (hi << 16);
-      }
-      v = make_uint4(o[0], o[1], o[2], o[3]);
+  if (tid == 9 * 32) {
+    *abort_s = 0;
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
     }
-    *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) = v;
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&done[b], 1);
+      mbar_init(&tfree[b], 8);
+    }
   }
-  // generic-proxy smem writes -> visible to the tensor core (async proxy)
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  // ---- 8 MMAs over K = 128, issued by one thread
-  if (tid == 0) {
-    const uint32_t a_base = smem_u32(As), b_base = smem_u32(Bs);
+  if (warp == 9) {
+    // ---- producer: A blocks through the ring
+    int64_t last[kPfStages];
 #pragma unroll
-    for (int s = 0; s < kD / 16; ++s) {
-      const uint64_t da = umma_desc(a_base + s * 2 * kPfLboA, kPfLboA, 128);
-      const uint64_t db = umma_desc(b_base + s * 2 * kPfLboB, kPfLboB, 128);
-      const uint32_t acc = s > 0 ? 1u : 0u;
-      asm volatile(
-          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
-          "l"(da), "l"(db), "r"(kPfIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-          : "memory");
+    for (int s = 0; s < kPfStages; ++s) last[s] = -1;
+    if (lane == 0) {
+      for (int64_t j = 0; j < nblk; ++j) {
+        if (*abort_s) break;
+        const int s = (int)(j % kPfStages);
+        if (j >= kPfStages && !pf_wait_or_abort(&aempty[s], (unsigned)((j / kPfStages - 1) & 1), abort_s)) {
+          atomicOr(a.err, 1u);
+          *abort_s = 1;
+          break;
+        }
+        mbar_expect_tx(&afull[s], kPfSmemA);
+        bulk_g2s(As + s * kPfSmemA, qa_h + (qb0 + j * qstep) * kPfSmemA, kPfSmemA, &afull[s]);
+        last[s] = j;
+      }
     }
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-  }
-  if (!mbar_wait_bounded(bar, 0)) {
-    atomicOr(a.err, 1u);
-    ok_s[0] = 0;
-    mbar_wait_bounded(bar, 0);  // let MMAs in flight finish before TMEM is freed
-  }
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  __syncthreads();
+    __syncwarp();
+    __syncthreads();  // end of work
+    if (lane == 0 && *abort_s)  // copies in flight must land before the CTA exits
+      for (int s = 0; s < kPfStages; ++s)
+        if (last[s] >= 0) pf_wait(&afull[s], (unsigned)((last[s] / kPfStages) & 1));
+  } else if (warp == 8) {
+    // ---- MMA issuer
+    int64_t issued = 0;
+    pf_b_ready_sync();  // B decoded and visible to the async proxy
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (lane == 0) {
+      const uint32_t a_base = smem_u32(As), b_base = smem_u32(Bs);
+      for (int64_t i = 0; i < nblk; ++i) {
+        if (*abort_s) break;
+        const int s = (int)(i % kPfStages), b = (int)(i & 1);
+        bool ok = pf_wait_or_abort(&afull[s], (unsigned)((i / kPfStages) & 1), abort_s);
+        if (ok && i >= 2) ok = pf_wait_or_abort(&tfree[b], (unsigned)((i / 2 - 1) & 1), abort_s);
+        if (!ok) {
+          atomicOr(a.err, 1u);
+          *abort_s = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        pf_mma_block(tmem + (uint32_t)(b * kPfN), a_base + s * kPfSmemA, b_base);
+        pf_commit(&done[b]);
+        pf_commit(&aempty[s]);
+        issued = i + 1;
+      }
+      if (*abort_s && issued > 0)  // MMAs in flight must finish before TMEM is freed
+        pf_wait(&done[(issued - 1) & 1], (unsigned)(((issued - 1) / 2) & 1));
+    }
+    __syncwarp();
+    __syncthreads();
+  } else {
+    // ---- B: 256 tokens x 128 channels, k_hat = +-s (fp16, exact); thread = token
+    {
+      const int n = tid;
+      const int64_t tile = t0 + n / kPfTile;
+      const int j = n % kPfTile;
+      if (tile < a.n_tiles) {
+        const int64_t tix = row * a.nt_cap + tile;
+        const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(a.kbits + (tix * kPfTile + j) * 4));
+        const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+        const uint4 *sc = reinterpret_cast<const uint4 *>(a.kscale + tix * kD);
+#pragma unroll
+        for (int kc = 0; kc < 16; ++kc) {
+          const uint32_t byte = (ww[kc >> 2] >> ((kc & 3) * 8)) & 0xffu;
+          const uint2 lo = lut[byte & 15u], hi = lut[byte >> 4];
+          const uint4 sv = __ldg(sc + kc);
+          *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) =
+              make_uint4(sv.x ^ lo.x, sv.y ^ lo.y, sv.z ^ hi.x, sv.w ^ hi.y);
+        }
+      } else {
+#pragma unroll
+        for (int kc = 0; kc < 16; ++kc)
+          *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    // generic-proxy smem writes -> visible to the tensor core (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    pf_b_ready_sync();
 
-  // ---- epilogue: warp w reads TMEM lanes 32w..32w+31 (its queries)
-  const int64_t qi = q0 + warp * 32 + lane;
-  if (ok_s[0]) {
-    float best[kPfN / kPfTile];
-#pragma unroll
-    for (int t = 0; t < kPfN / kPfTile; ++t) best[t] = -INFINITY;
-#pragma unroll
-    for (int c0 = 0; c0 < kPfN; c0 += 16) {
-      uint32_t r[16];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-          "%15}, [%16];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-          : "r"(taddr));
+    // ---- readers
+    const int quarter = warp & 3, half = warp >> 2;
+    const int nt_here = (int)(a.n_tiles - t0 < 4 ? a.n_tiles - t0 : 4);
+    for (int64_t i = 0; i < nblk; ++i) {
+      if (__shfl_sync(~0u, *abort_s, 0)) break;
+      const int b = (int)(i & 1);
+      if (!__all_sync(~0u, pf_wait_or_abort(&done[b], (unsigned)((i >> 1) & 1), abort_s))) {
+        if (lane == 0) atomicOr(a.err, 1u);
+        *abort_s = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t r[128];
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kPfN + half * 128);
+      pf_tmem_ld32(taddr, r);
+      pf_tmem_ld32(taddr + 32, r + 32);
+      pf_tmem_ld32(taddr + 64, r + 64);
+      pf_tmem_ld32(taddr + 96, r + 96);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-      for (int e = 0; e < 16; ++e) best[c0 / kPfTile] = fmaxf(best[c0 / kPfTile], __uint_as_float(r[e]));
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&tfree[b])) : "memory");
+      const float best0 = pf_max64(r), best1 = pf_max64(r + 64);
+      const int64_t qi = (qb0 + i * qstep) * kPfM + quarter * 32 + lane;
+      if (qi < a.nq) {
+        float *o = a.out + (qi * a.n_kv + h) * a.n_tiles + t0 + half * 2;
+        if (half * 2 < nt_here) o[0] = best0;
+        if (half * 2 + 1 < nt_here) o[1] = best1;
+      }
     }
-    if (qi < a.nq) {
-#pragma unroll
-      for (int t = 0; t < kPfN / kPfTile; ++t)
-        if (t0 + t < a.n_tiles) a.out[(qi * a.n_kv + h) * a.n_tiles + t0 + t] = best[t];
-    }
+    __syncthreads();
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfN));
+
+  // every role is past its last TMEM access (or drained after an abort)
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 8)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols));
 }
 
 }  // namespace kvr
 
 using namespace kvr;
 
+static int64_t pf_qblocks(int64_t nq) { return (nq + kPfM - 1) / kPfM; }
+
 extern "C" size_t kvr_sd1_prefill_workspace_bytes(int64_t nq, int n_kv) {
-  return kWsHeader + align_up((size_t)nq * n_kv * kD * 2, 256);
+  return kWsHeader + (size_t)pf_qblocks(nq) * n_kv * kPfSmemA;
 }
 
 extern "C" int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, int n_q, int n_kv,
@@ -225,34 +359,42 @@ extern "C" int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, in
   KVR_REQUIRE(q && kbits && kscale && scores && workspace, "kvr_sd1_prefill_scores: null pointer");
   KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_prefill_scores: bad dtype");
   KVR_REQUIRE(nq >= 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0, "kvr_sd1_prefill_scores: bad head counts");
+  KVR_REQUIRE(n_kv <= 65535, "kvr_sd1_prefill_scores: too many KV heads");
   KVR_REQUIRE(tile == kPfTile, "kvr_sd1_prefill_scores: tile must be 64");
   KVR_REQUIRE(kind == KVR_HADAMARD || kind == KVR_DCT, "kvr_sd1_prefill_scores: unknown transform");
   KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_prefill_scores: n_tiles > nt_cap");
   const size_t need = kvr_sd1_prefill_workspace_bytes(nq, n_kv);
   KVR_REQUIRE(workspace_bytes >= need, "kvr_sd1_prefill_scores: workspace %zu < %zu bytes", workspace_bytes, need);
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_prefill_scores: workspace alignment");
-  KVR_REQUIRE((reinterpret_cast<uintptr_t>(kscale) & 15) == 0, "kvr_sd1_prefill_scores: kscale must be 16-byte aligned");
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(kscale) & 15) == 0 && (reinterpret_cast<uintptr_t>(kbits) & 15) == 0,
+              "kvr_sd1_prefill_scores: kbits/kscale must be 16-byte aligned");
   if (nq == 0 || n_tiles == 0) return KVR_OK;
   cudaStream_t st = as_cuda(stream);
   char *p = reinterpret_cast<char *>(workspace);
-  __half *qp16 = reinterpret_cast<__half *>(p + kWsHeader);
-  const int64_t rows = nq * n_kv;
-  const int qb = (int)((rows + 7) / 8 < 148 * 16 ? (rows + 7) / 8 : 148 * 16);
-  if (q_dtype == KVR_F32) prefill_qprep_kernel<KVR_F32><<<qb, 256, 0, st>>>(q, nq, n_q, n_kv, kind, qp16);
-  else if (q_dtype == KVR_F16) prefill_qprep_kernel<KVR_F16><<<qb, 256, 0, st>>>(q, nq, n_q, n_kv, kind, qp16);
-  else prefill_qprep_kernel<KVR_BF16><<<qb, 256, 0, st>>>(q, nq, n_q, n_kv, kind, qp16);
+  unsigned char *qa = reinterpret_cast<unsigned char *>(p + kWsHeader);
+  const int64_t nqb = pf_qblocks(nq);
+  const int64_t rows = nqb * kPfM * n_kv;
+  const int qgrid = (int)((rows + 7) / 8 < 148 * 16 ? (rows + 7) / 8 : 148 * 16);
+  if (q_dtype == KVR_F32) prefill_qprep_kernel<KVR_F32><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
+  else if (q_dtype == KVR_F16) prefill_qprep_kernel<KVR_F16><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
+  else prefill_qprep_kernel<KVR_BF16><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
   int rc = check_launch("kvr_sd1_prefill_scores (q prep)");
   if (rc) return rc;
-  PrefillArgs a{qp16, nq, n_kv, kbits, kscale, nt_cap, n_tiles, scores, reinterpret_cast<unsigned *>(p)};
-  const size_t smem = kPfSmemA + kPfSmemB + 64;
+  PrefillArgs a{qa, nq, nqb, n_kv, kbits, kscale, nt_cap, n_tiles, scores, reinterpret_cast<unsigned *>(p)};
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (set_dev != dev) {
-    cudaFuncSetAttribute(prefill_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(prefill_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
     set_dev = dev;
   }
-  dim3 grid((unsigned)((n_tiles + 3) / 4), (unsigned)((nq + kPfM - 1) / kPfM), n_kv);
-  prefill_scores_kernel<<<grid, kPfThreads, smem, st>>>(a);
+  // one CTA per (256 tokens, head); split the query blocks over grid.y only
+  // when that alone leaves SMs idle (each split re-decodes its B)
+  const int64_t base = ((n_tiles + 3) / 4) * n_kv;
+  int64_t gy = (2 * 148 + base - 1) / base;
+  gy = gy < 1 ? 1 : (gy > nqb ? nqb : gy);
+  gy = gy > 65535 ? 65535 : gy;
+  dim3 grid((unsigned)((n_tiles + 3) / 4), (unsigned)gy, (unsigned)n_kv);
+  prefill_scores_kernel<<<grid, kPfThreads, kPfSmem, st>>>(a);
   return check_launch("kvr_sd1_prefill_scores");
 }

@@ -11,7 +11,8 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-@pytest.mark.parametrize("kind,nq,nt", [("dct", 200, 10), ("hadamard", 128, 4), ("dct", 37, 7), ("hadamard", 300, 13)])
+@pytest.mark.parametrize("kind,nq,nt", [("dct", 200, 10), ("hadamard", 128, 4), ("dct", 37, 7), ("hadamard", 300, 13),
+                                             ("dct", 1000, 301), ("hadamard", 700, 512)])
 def test_prefill_scores_vs_spec(kind, nq, nt):
     from kvr_b200 import kernels as K
     rng = np.random.default_rng(nq + nt)
