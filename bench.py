@@ -261,6 +261,37 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
 
+    # ---- tcgen05 prefill tile scoring (secondary line): a 4096-query chunk
+    # of prefill positions scored against layer 0's store (batch-1 stores only)
+    prefill = None
+    if B == 1:
+        nq_pf = 4096
+        q_pf = torch.randn(nq_pf, hq, D, device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(3):
+            K.sd1_prefill_scores(stores[0], q_pf)
+        torch.cuda.synchronize()
+        reps = 20
+        e0.record()
+        for _ in range(reps):
+            K.sd1_prefill_scores(stores[0], q_pf)
+        e1.record()
+        torch.cuda.synchronize()
+        pf_ms = e0.elapsed_time(e1) / reps
+        pf_flops = 2.0 * nq_pf * hkv * stores[0].n_tiles * TILE * D
+        pf_peak = None
+        try:
+            pf_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+            pf_src = "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+        except (OSError, KeyError, ValueError):
+            pf_peak, pf_src = 1590.0, "fallback"
+        pf_tf = pf_flops / (pf_ms / 1e3) / 1e12
+        prefill = {"kernel": "prefill_scores_kernel (tcgen05.mma kind::f16) + q prep", "queries": nq_pf,
+                   "tokens": stores[0].n_tiles * TILE, "kv_heads": hkv, "ms_per_launch": round(pf_ms, 5),
+                   "flops_per_launch": pf_flops, "achieved": round(pf_tf, 1), "unit": "TFLOP/s",
+                   "peak": pf_peak, "frac": round(pf_tf / pf_peak, 4), "peak_source": pf_src,
+                   "bound": "tensor"}
+        del q_pf
+
     peak, peak_kind = measured_peak_hbm()
     traffic = None
     try:  # DRAM bytes per launch from the committed ncu capture of this workload
@@ -305,6 +336,7 @@ def run_gpu(args, rank, world, local_rank):
         "e2e": {"value": round(B * 1e3 / e2e_ms, 3), "unit": "sequence decode-steps/s (32 layers per step)",
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                 "d2h_bytes_per_step": o_host.numel() * o_host.element_size(), "path": "kvr_b200.kernels eager API"},
+        "prefill_scores": prefill,
         "gpu_launches": args.steps * LAYERS * 2,
         "clocks": clocks,
     }

@@ -32,105 +32,111 @@ __global__ void __launch_bounds__(256) transform_kernel(const float *x, float *y
 }
 
 // -------------------------------------------------------------- encoder ----
-// One CTA of 256 threads per (tile, kv head, batch).  Phase 1: each warp
-// loads token vectors (K, then V), applies RoPE to K when tables are given,
-// transforms them and parks them in shared memory X[kv][j][c].  Phase 2:
-// threads 0-127 run the sigma-delta scan of one K channel each, threads
-// 128-255 of one V channel; the bits of a token come out of a warp ballot
-// (warp w owns channels 32w..32w+31 = word w).
+// One CTA of 2*TILE threads per (tile, kv head, batch).  Phase 1: each
+// thread owns one token vector (threads < TILE: K, the rest: V), holds all
+// 128 elements in registers, applies RoPE to K when tables are given, runs
+// the transform with compile-time indices (no shuffles, no shared memory),
+// and writes the result channel-major into X[kv][c][j].  Phase 2: one thread
+// per (kv, channel) chain reads its channel's TILE values as float4 runs,
+// forms the fp16 scale and runs the sigma-delta scan; a token's bits come out
+// of a warp ballot (a warp covers channels 32w'..32w'+31 = one word).
 template <int DT, int TILE>
-__global__ void __launch_bounds__(256) sd1_encode_kernel(
+__global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
     const void *__restrict__ k, const void *__restrict__ v, int n_kv, int64_t batch_stride,
     int64_t tok_stride, const float *__restrict__ cos_tbl, const float *__restrict__ sin_tbl,
     int64_t rope_stride, int64_t pos0, int kind, uint32_t *__restrict__ kbits, uint16_t *__restrict__ kscale,
     uint32_t *__restrict__ vbits, uint16_t *__restrict__ vscale, int64_t nt_cap, int64_t tile0) {
+  constexpr int NT = 2 * TILE;    // one thread per token vector (K: tid < TILE, V: tid >= TILE)
+  constexpr int LD = TILE + 4;    // channel-major row stride: conflict-free both ways
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float *X = reinterpret_cast<float *>(smem_raw);                       // [2][TILE][128]
-  uint32_t *bits_s = reinterpret_cast<uint32_t *>(X + 2 * TILE * kD);    // [2][TILE][4]
-  float *buf_s = reinterpret_cast<float *>(bits_s + 2 * TILE * 4);       // [8][256]
-  float *lee_s = buf_s + 8 * 2 * kD;                                     // [128]
+  float *X = reinterpret_cast<float *>(smem_raw);  // [2][128][LD]: X[kv][c][j]
+  __shared__ __align__(16) uint32_t bits_s[2 * TILE * 4];
 
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   const int64_t tile_in = blockIdx.x;
-  load_lee(lee_s);
-  __syncthreads();
+  const int kv = tid / TILE, j = tid % TILE;  // warp-uniform kv (TILE is a multiple of 32)
+  const int64_t tok = tile_in * TILE + j;
 
-  const int64_t base_in = (int64_t)b * batch_stride + (int64_t)h * kD;
-  const bool rope = cos_tbl != nullptr;
-  constexpr int NV = 2 * TILE;   // vectors per CTA
-  constexpr int PER_WARP = NV / 8;
-  constexpr int BATCH = 8;       // vectors loaded ahead per warp
-  static_assert(PER_WARP % BATCH == 0, "tile too small");
-#pragma unroll 1
-  for (int v0 = 0; v0 < PER_WARP; v0 += BATCH) {
-    float xv[BATCH][4];
-    float cv[BATCH][4], sv[BATCH][4];
+  // ---- phase 1: load this thread's vector, RoPE (K), transform, transpose to smem
+  {
+    float x[kD];
+    const int64_t base = (int64_t)b * batch_stride + (int64_t)h * kD + tok * tok_stride;
+    const void *src = kv == 0 ? k : v;
 #pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int vid = warp * PER_WARP + v0 + u;  // K: vid < TILE, V: vid >= TILE
-      const bool is_k = vid < TILE;
-      const int j = is_k ? vid : vid - TILE;
-      const int64_t tok = tile_in * TILE + j;
-      load4<DT>(is_k ? k : v, base_in + tok * tok_stride + lane * 4, xv[u]);
-      if (rope && is_k) {
-        const float *cr = cos_tbl + (pos0 + tok) * rope_stride + lane * 4;
-        const float *sr = sin_tbl + (pos0 + tok) * rope_stride + lane * 4;
-        float4 c4 = __ldg(reinterpret_cast<const float4 *>(cr));
-        float4 s4 = __ldg(reinterpret_cast<const float4 *>(sr));
-        cv[u][0] = c4.x; cv[u][1] = c4.y; cv[u][2] = c4.z; cv[u][3] = c4.w;
-        sv[u][0] = s4.x; sv[u][1] = s4.y; sv[u][2] = s4.z; sv[u][3] = s4.w;
-      }
+    for (int q = 0; q < kD / 4; ++q) {
+      float t[4];
+      load4<DT>(src, base + q * 4, t);
+      x[4 * q] = t[0]; x[4 * q + 1] = t[1]; x[4 * q + 2] = t[2]; x[4 * q + 3] = t[3];
     }
+    if (cos_tbl != nullptr && kv == 0) {
+      // (x * cos) + (rotate_half(x) * sin), rotate_half(x)_i = -x_{i+64} (i < 64), x_{i-64}
+      const float4 *cr = reinterpret_cast<const float4 *>(cos_tbl + (pos0 + tok) * rope_stride);
+      const float4 *sr = reinterpret_cast<const float4 *>(sin_tbl + (pos0 + tok) * rope_stride);
+      float y[kD];
 #pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int vid = warp * PER_WARP + v0 + u;
-      const bool is_k = vid < TILE;
-      float x[4] = {xv[u][0], xv[u][1], xv[u][2], xv[u][3]};
-      if (rope && is_k) {
-        // rotate_half: partner element i +/- 64 lives in lane ^ 16
+      for (int q = 0; q < kD / 4; ++q) {
+        const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const float p = __shfl_xor_sync(0xffffffffu, x[r], 16);
-          const float rh = lane < 16 ? -p : p;
-          x[r] = __fadd_rn(__fmul_rn(xv[u][r], cv[u][r]), __fmul_rn(rh, sv[u][r]));
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * q + e;
+          const float rh = i < kD / 2 ? -x[i + kD / 2] : x[i - kD / 2];
+          y[i] = __fadd_rn(__fmul_rn(x[i], cc[e]), __fmul_rn(rh, ss[e]));
         }
       }
-      transform128(x, lane, kind, false, buf_s + warp * 2 * kD, lee_s);
-      reinterpret_cast<float4 *>(X + vid * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+#pragma unroll
+      for (int i = 0; i < kD; ++i) x[i] = y[i];
     }
+    if (kind == KVR_HADAMARD) wht128_reg(x);
+    else dct128_fwd_reg(x);
+    float *xo = X + (kv * kD) * LD + j;
+#pragma unroll
+    for (int c = 0; c < kD; ++c) xo[c * LD] = x[c];
   }
   __syncthreads();
 
-  // phase 2: sigma-delta per channel
-  const int kv = threadIdx.x >> 7;  // 0 = K, 1 = V
-  const int c = threadIdx.x & 127;
-  const float *Xc = X + kv * TILE * kD + c;
-  float acc = 0.0f;
-#pragma unroll 8
-  for (int j = 0; j < TILE; ++j) acc = __fadd_rn(acc, fabsf(Xc[j * kD]));
-  const float mean = __fmul_rn(acc, 1.0f / TILE);
-  const __half s16 = __float2half_rn(fminf(mean, 65504.0f));
-  const float s = __half2float(s16);
+  // ---- phase 2: per channel chain (kv, c): scale = fp16(mean |x|), sigma-delta bits
   const int64_t out_tile = ((int64_t)b * n_kv + h) * nt_cap + tile0 + tile_in;
-  (kv == 0 ? kscale : vscale)[out_tile * kD + c] = __half_as_ushort(s16);
-  float e = 0.0f;
-  uint32_t *bs = bits_s + kv * TILE * 4;
-  const int word = (threadIdx.x >> 5) & 3;
-#pragma unroll 8
-  for (int j = 0; j < TILE; ++j) {
-    const float u = __fadd_rn(Xc[j * kD], e);
-    const bool bit = u >= 0.0f;
-    e = __fsub_rn(u, bit ? s : -s);
-    const uint32_t w = __ballot_sync(0xffffffffu, bit);
-    if (lane == 0) bs[j * 4 + word] = w;
+#pragma unroll
+  for (int chain = tid; chain < 2 * kD; chain += NT) {
+    const int kvc = chain / kD, c = chain % kD;  // a warp covers 32 consecutive channels of one kv
+    const float4 *Xc = reinterpret_cast<const float4 *>(X + (kvc * kD + c) * LD);
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < TILE / 4; ++q) {
+      const float4 t = Xc[q];
+      acc = __fadd_rn(acc, fabsf(t.x));
+      acc = __fadd_rn(acc, fabsf(t.y));
+      acc = __fadd_rn(acc, fabsf(t.z));
+      acc = __fadd_rn(acc, fabsf(t.w));
+    }
+    const float mean = __fmul_rn(acc, 1.0f / TILE);
+    const __half s16 = __float2half_rn(fminf(mean, 65504.0f));
+    const float s = __half2float(s16), ns = -s;
+    (kvc == 0 ? kscale : vscale)[out_tile * kD + c] = __half_as_ushort(s16);
+    uint32_t *bs = bits_s + kvc * TILE * 4 + (c >> 5);
+    float e = 0.0f;
+#pragma unroll
+    for (int q = 0; q < TILE / 4; ++q) {
+      const float4 t = Xc[q];
+      const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float u = __fadd_rn(tv[r], e);
+        const bool bit = u >= 0.0f;
+        e = __fsub_rn(u, bit ? s : ns);
+        const uint32_t w = __ballot_sync(0xffffffffu, bit);
+        if (lane == 0) bs[(4 * q + r) * 4] = w;
+      }
+    }
   }
   __syncthreads();
-  // store bits: 2 * TILE uint4
-  for (int i = threadIdx.x; i < 2 * TILE; i += blockDim.x) {
-    const int kvi = i / TILE, j = i - kvi * TILE;
+  // ---- store bits: 2 * TILE uint4 (token-major)
+  for (int i = tid; i < 2 * TILE; i += NT) {
+    const int kvi = i / TILE, jj = i - kvi * TILE;
     const uint4 w = reinterpret_cast<const uint4 *>(bits_s)[i];
-    uint32_t *dst = (kvi == 0 ? kbits : vbits) + (out_tile * TILE + j) * 4;
+    uint32_t *dst = (kvi == 0 ? kbits : vbits) + (out_tile * TILE + jj) * 4;
     *reinterpret_cast<uint4 *>(dst) = w;
   }
 }
@@ -383,7 +389,7 @@ static int launch_encode(int tile, dim3 grid, size_t smem, cudaStream_t st, cons
 #define KVR_ENC(T)                                                                                       \
   case T:                                                                                                \
     cudaFuncSetAttribute(sd1_encode_kernel<DT, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    sd1_encode_kernel<DT, T><<<grid, 256, smem, st>>>(k, v, n_kv, bs, ts, c, s, rs, pos0, kind, kb, ks, vb, \
+    sd1_encode_kernel<DT, T><<<grid, 2 * T, smem, st>>>(k, v, n_kv, bs, ts, c, s, rs, pos0, kind, kb, ks, vb, \
                                                        vs, cap, t0);                                     \
     break;
     KVR_ENC(32)
@@ -482,7 +488,7 @@ extern "C" int kvr_sd1_encode(const void *k, const void *v, int dtype, int batch
   KVR_REQUIRE(cos_tbl == nullptr || (rope_stride % 4 == 0 && pos0 >= 0), "kvr_sd1_encode: bad rope table stride/pos0");
   KVR_REQUIRE(n_tiles <= 0x7fffffff, "kvr_sd1_encode: too many tiles per launch");
   if (n_tiles == 0) return KVR_OK;
-  const size_t smem = (size_t)2 * tile * kD * 4 + (size_t)2 * tile * 16 + 8 * 2 * kD * 4 + kD * 4;
+  const size_t smem = (size_t)2 * kD * (tile + 4) * 4;
   dim3 grid((unsigned)n_tiles, n_kv, batch);
   cudaStream_t st = as_cuda(stream);
   switch (dtype) {

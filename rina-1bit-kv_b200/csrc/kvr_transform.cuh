@@ -183,4 +183,76 @@ __device__ __forceinline__ void transform128(float (&x)[4], int lane, int kind, 
   }
 }
 
+// ---- one thread per vector: all 128 elements in registers (x[0..127]).
+// Same operations in the same order as the warp versions above (so the same
+// bits), with every index a compile-time constant: no shuffles, no shared
+// memory, factors read as constant-bank operands.  Used by the encoder,
+// where each thread transforms one token vector.
+__device__ __forceinline__ float lee_factor(int i) { return __uint_as_float(kLeeBits[i]); }
+
+__device__ __forceinline__ void wht128_reg(float (&x)[kD]) {
+#pragma unroll
+  for (int m = 1; m < kD; m <<= 1) {
+#pragma unroll
+    for (int i = 0; i < kD; ++i) {
+      if ((i & m) == 0) {
+        const float a = x[i], b = x[i + m];
+        x[i] = __fadd_rn(a, b);
+        x[i + m] = __fsub_rn(a, b);
+      }
+    }
+  }
+  const float c = __uint_as_float(kInvSqrt128Bits);
+#pragma unroll
+  for (int i = 0; i < kD; ++i) x[i] = __fmul_rn(x[i], c);
+}
+
+template <int M>
+__device__ __forceinline__ void lee_split_reg(const float (&in)[kD], float (&out)[kD]) {
+  constexpr int half = M / 2;
+#pragma unroll
+  for (int o = 0; o < kD; o += M) {
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float xa = in[o + j], xb = in[o + M - 1 - j];
+      out[o + j] = __fadd_rn(xa, xb);
+      out[o + half + j] = __fmul_rn(__fsub_rn(xa, xb), lee_factor(half - 1 + j));
+    }
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_merge_reg(const float (&in)[kD], float (&out)[kD]) {
+  constexpr int half = M / 2;
+#pragma unroll
+  for (int o = 0; o < kD; o += M) {
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      out[o + 2 * k] = in[o + k];
+      out[o + 2 * k + 1] = k < half - 1 ? __fadd_rn(in[o + half + k], in[o + half + k + 1]) : in[o + half + k];
+    }
+  }
+}
+
+__device__ __forceinline__ void dct128_fwd_reg(float (&x)[kD]) {
+  float y[kD];
+  lee_split_reg<128>(x, y);
+  lee_split_reg<64>(y, x);
+  lee_split_reg<32>(x, y);
+  lee_split_reg<16>(y, x);
+  lee_split_reg<8>(x, y);
+  lee_split_reg<4>(y, x);
+  lee_split_reg<2>(x, y);
+  lee_merge_reg<2>(y, x);
+  lee_merge_reg<4>(x, y);
+  lee_merge_reg<8>(y, x);
+  lee_merge_reg<16>(x, y);
+  lee_merge_reg<32>(y, x);
+  lee_merge_reg<64>(x, y);
+  lee_merge_reg<128>(y, x);
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  x[0] = __fmul_rn(x[0], c0);
+#pragma unroll
+  for (int i = 1; i < kD; ++i) x[i] = __fmul_rn(x[i], c1);
+}
+
 }  // namespace kvr

@@ -51,7 +51,7 @@ def test_transform_bit_exact(kind):
 
 @pytest.mark.parametrize("tile", [32, 64, 128])
 @pytest.mark.parametrize("kind", ["hadamard", "dct"])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 def test_encode_bit_exact(tile, kind, dtype):
     n = tile * 5
     k, v, q = cfg0(tile + (kind == "dct"), n, n_kv=4)
