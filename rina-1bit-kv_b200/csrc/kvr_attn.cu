@@ -362,12 +362,6 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
 }
 
 // ------------------------------------------------------------ pipelined ----
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Issues the copies of unit u into raw buffer `buf` (no wait).
 template <int TILE>

@@ -195,6 +195,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned phase) {
       : "memory");
   return done != 0;
 }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 // Bounded wait; returns false if it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase) {
   for (uint32_t it = 0; it < kSpinLimit; ++it) {

@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
     const void *__restrict__ k, const void *__restrict__ v, int n_kv, int64_t batch_stride,
     int64_t tok_stride, const float *__restrict__ cos_tbl, const float *__restrict__ sin_tbl,
     int64_t rope_stride, int64_t pos0, int kind, uint32_t *__restrict__ kbits, uint16_t *__restrict__ kscale,
-    uint32_t *__restrict__ vbits, uint16_t *__restrict__ vscale, int64_t nt_cap, int64_t tile0) {
+    uint32_t *__restrict__ vbits, uint16_t *__restrict__ vscale, int64_t nt_cap, int64_t tile0, int vec16) {
   constexpr int NT = 2 * TILE;    // one thread per token vector (K: tid < TILE, V: tid >= TILE)
   constexpr int LD = TILE + 4;    // channel-major row stride: conflict-free both ways
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -58,25 +58,92 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
   const int kv = tid / TILE, j = tid % TILE;  // warp-uniform kv (TILE is a multiple of 32)
   const int64_t tok = tile_in * TILE + j;
 
-  // ---- phase 1: load this thread's vector, RoPE (K), transform, transpose to smem
+  // ---- phase 1a: stage the tile's 2*TILE rows (and the RoPE rows) into
+  // shared memory with coalesced asynchronous copies; the staging area
+  // aliases X and is released by the barrier before X is written
+  constexpr int ES = DT == KVR_F32 ? 4 : 2;
+  constexpr int RB = kD * ES;          // row bytes
+  constexpr int RS = RB + 16;          // padded row stride: conflict-free row reads
+  constexpr int CS = kD * 4 + 16;      // RoPE row stride
+  unsigned char *raw = smem_raw;                      // [2*TILE][RS]
+  unsigned char *cs_s = smem_raw + 2 * TILE * RS;     // [2][TILE][CS] cos, sin
+  const bool rope = cos_tbl != nullptr;
+  {
+    const int64_t base = (int64_t)b * batch_stride + (int64_t)h * kD + tile_in * TILE * tok_stride;
+    const unsigned char *kp = reinterpret_cast<const unsigned char *>(k) + base * ES;
+    const unsigned char *vp = reinterpret_cast<const unsigned char *>(v) + base * ES;
+    const int64_t tsb = tok_stride * ES;
+    if (vec16) {
+      constexpr int CPR = RB / 16;
+      for (int i = tid; i < 2 * TILE * CPR; i += NT) {
+        const int r = i / CPR, c = i % CPR;
+        const unsigned char *src = (r < TILE ? kp + r * tsb : vp + (r - TILE) * tsb) + c * 16;
+        cp_async16(raw + r * RS + c * 16, src);
+      }
+      if (rope) {
+        constexpr int CPC = kD * 4 / 16;
+        for (int i = tid; i < 2 * TILE * CPC; i += NT) {
+          const int r = i / CPC, c = i % CPC;
+          const int jj = r % TILE;
+          const float *tbl = r < TILE ? cos_tbl : sin_tbl;
+          cp_async16(cs_s + r * CS + c * 16, tbl + (pos0 + tile_in * TILE + jj) * rope_stride + c * 4);
+        }
+      }
+    } else {
+      constexpr int CPR = RB / 8;
+      for (int i = tid; i < 2 * TILE * CPR; i += NT) {
+        const int r = i / CPR, c = i % CPR;
+        const unsigned char *src = (r < TILE ? kp + r * tsb : vp + (r - TILE) * tsb) + c * 8;
+        cp_async8(raw + r * RS + c * 8, src);
+      }
+      if (rope) {
+        constexpr int CPC = kD * 4 / 8;
+        for (int i = tid; i < 2 * TILE * CPC; i += NT) {
+          const int r = i / CPC, c = i % CPC;
+          const int jj = r % TILE;
+          const float *tbl = r < TILE ? cos_tbl : sin_tbl;
+          cp_async8(cs_s + r * CS + c * 8, tbl + (pos0 + tile_in * TILE + jj) * rope_stride + c * 2);
+        }
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+  }
+  __syncthreads();
+
+  // ---- phase 1b: this thread's vector from shared memory, RoPE (K), transform
   {
     float x[kD];
-    const int64_t base = (int64_t)b * batch_stride + (int64_t)h * kD + tok * tok_stride;
-    const void *src = kv == 0 ? k : v;
+    const uint4 *row = reinterpret_cast<const uint4 *>(raw + tid * RS);
 #pragma unroll
-    for (int q = 0; q < kD / 4; ++q) {
-      float t[4];
-      load4<DT>(src, base + q * 4, t);
-      x[4 * q] = t[0]; x[4 * q + 1] = t[1]; x[4 * q + 2] = t[2]; x[4 * q + 3] = t[3];
+    for (int q = 0; q < RB / 16; ++q) {
+      const uint4 u = row[q];
+      if constexpr (DT == KVR_F32) {
+        x[4 * q] = __uint_as_float(u.x); x[4 * q + 1] = __uint_as_float(u.y);
+        x[4 * q + 2] = __uint_as_float(u.z); x[4 * q + 3] = __uint_as_float(u.w);
+      } else {
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint16_t lo = w[e] & 0xffffu, hi = w[e] >> 16;
+          if constexpr (DT == KVR_F16) {
+            x[8 * q + 2 * e] = __half2float(__ushort_as_half(lo));
+            x[8 * q + 2 * e + 1] = __half2float(__ushort_as_half(hi));
+          } else {
+            x[8 * q + 2 * e] = __bfloat162float(__ushort_as_bfloat16(lo));
+            x[8 * q + 2 * e + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+          }
+        }
+      }
     }
-    if (cos_tbl != nullptr && kv == 0) {
+    if (rope && kv == 0) {
       // (x * cos) + (rotate_half(x) * sin), rotate_half(x)_i = -x_{i+64} (i < 64), x_{i-64}
-      const float4 *cr = reinterpret_cast<const float4 *>(cos_tbl + (pos0 + tok) * rope_stride);
-      const float4 *sr = reinterpret_cast<const float4 *>(sin_tbl + (pos0 + tok) * rope_stride);
+      const float4 *cr = reinterpret_cast<const float4 *>(cs_s + j * CS);
+      const float4 *sr = reinterpret_cast<const float4 *>(cs_s + (TILE + j) * CS);
       float y[kD];
 #pragma unroll
       for (int q = 0; q < kD / 4; ++q) {
-        const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
+        const float4 c4 = cr[q], s4 = sr[q];
         const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -88,6 +155,7 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
 #pragma unroll
       for (int i = 0; i < kD; ++i) x[i] = y[i];
     }
+    __syncthreads();  // staging area is read: X may overwrite it
     if (kind == KVR_HADAMARD) wht128_reg(x);
     else dct128_fwd_reg(x);
     float *xo = X + (kv * kD) * LD + j;
@@ -117,6 +185,7 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
     (kvc == 0 ? kscale : vscale)[out_tile * kD + c] = __half_as_ushort(s16);
     uint32_t *bs = bits_s + kvc * TILE * 4 + (c >> 5);
     float e = 0.0f;
+    uint32_t mine = 0;  // lane L keeps the word of token 32m + L
 #pragma unroll
     for (int q = 0; q < TILE / 4; ++q) {
       const float4 t = Xc[q];
@@ -127,7 +196,8 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
         const bool bit = u >= 0.0f;
         e = __fsub_rn(u, bit ? s : ns);
         const uint32_t w = __ballot_sync(0xffffffffu, bit);
-        if (lane == 0) bs[(4 * q + r) * 4] = w;
+        mine = lane == ((4 * q + r) & 31) ? w : mine;
+        if (((4 * q + r) & 31) == 31) bs[((4 * q + r) - 31 + lane) * 4] = mine;
       }
     }
   }
@@ -384,13 +454,13 @@ template <int DT>
 static int launch_encode(int tile, dim3 grid, size_t smem, cudaStream_t st, const void *k, const void *v,
                          int n_kv, int64_t bs, int64_t ts, const float *c, const float *s, int64_t rs, int64_t pos0,
                          int kind, uint32_t *kb, uint16_t *ks, uint32_t *vb, uint16_t *vs, int64_t cap,
-                         int64_t t0) {
+                         int64_t t0, int vec16) {
   switch (tile) {
 #define KVR_ENC(T)                                                                                       \
   case T:                                                                                                \
     cudaFuncSetAttribute(sd1_encode_kernel<DT, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     sd1_encode_kernel<DT, T><<<grid, 2 * T, smem, st>>>(k, v, n_kv, bs, ts, c, s, rs, pos0, kind, kb, ks, vb, \
-                                                       vs, cap, t0);                                     \
+                                                         vs, cap, t0, vec16);                            \
     break;
     KVR_ENC(32)
     KVR_ENC(64)
@@ -488,13 +558,23 @@ extern "C" int kvr_sd1_encode(const void *k, const void *v, int dtype, int batch
   KVR_REQUIRE(cos_tbl == nullptr || (rope_stride % 4 == 0 && pos0 >= 0), "kvr_sd1_encode: bad rope table stride/pos0");
   KVR_REQUIRE(n_tiles <= 0x7fffffff, "kvr_sd1_encode: too many tiles per launch");
   if (n_tiles == 0) return KVR_OK;
-  const size_t smem = (size_t)2 * kD * (tile + 4) * 4;
+  const int es = dtype == KVR_F32 ? 4 : 2;
+  auto al = [](const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+  KVR_REQUIRE(al(k, 8) && al(v, 8) && (cos_tbl == nullptr || (al(cos_tbl, 8) && al(sin_tbl, 8))),
+              "kvr_sd1_encode: k, v and rope tables must be 8-byte aligned");
+  // 16-byte staging copies when every row start is 16-byte aligned, else 8-byte ones
+  const int vec16 = al(k, 16) && al(v, 16) && (tok_stride * es) % 16 == 0 && (batch_stride * es) % 16 == 0 &&
+                    (cos_tbl == nullptr || (al(cos_tbl, 16) && al(sin_tbl, 16) && (rope_stride * 4) % 16 == 0));
+  // X[2][128][tile + 4] fp32, aliased by the staging rows (+ RoPE rows)
+  const size_t x_bytes = (size_t)2 * kD * (tile + 4) * 4;
+  const size_t stage = (size_t)2 * tile * (kD * es + 16) + (cos_tbl ? (size_t)2 * tile * (kD * 4 + 16) : 0);
+  const size_t smem = x_bytes > stage ? x_bytes : stage;
   dim3 grid((unsigned)n_tiles, n_kv, batch);
   cudaStream_t st = as_cuda(stream);
   switch (dtype) {
-    case KVR_F32: return launch_encode<KVR_F32>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
-    case KVR_F16: return launch_encode<KVR_F16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
-    default: return launch_encode<KVR_BF16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0);
+    case KVR_F32: return launch_encode<KVR_F32>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0, vec16);
+    case KVR_F16: return launch_encode<KVR_F16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0, vec16);
+    default: return launch_encode<KVR_BF16>(tile, grid, smem, st, k, v, n_kv, batch_stride, tok_stride, cos_tbl, sin_tbl, rope_stride, pos0, kind, kbits, kscale, vbits, vscale, nt_cap, tile0, vec16);
   }
 }
 

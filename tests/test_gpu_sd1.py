@@ -83,6 +83,31 @@ def test_encode_with_rope_and_offsets_bit_exact(kind):
         assert np.array_equal(st.vbits[0, h, 4:7].cpu().numpy().view(np.uint32), want["vbits"])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_encode_8_byte_aligned_rows_with_rope_bit_exact(dtype):
+    """Token rows that start on 8- but not 16-byte boundaries take the 8-byte
+    staging copies; the result is the same as for aligned rows."""
+    tile, n_kv, n = 64, 2, 2 * 64
+    k, v, q = cfg0(11, n, n_kv=n_kv)
+    cos, sin = R.rope_tables(1024, 128)
+
+    def skew(x):  # (n, n_kv, d) with token stride n_kv*d + 4, storage offset 4 elements
+        buf = torch.zeros(n * (n_kv * 128 + 4) + 8, dtype=dtype, device=DEV)
+        y = buf.as_strided((n, n_kv, 128), (n_kv * 128 + 4, 128, 1), 4)
+        y.copy_(t(x).to(dtype))
+        return y
+
+    ks, vs = skew(k), skew(v)
+    st = K().Sd1Store(1, n_kv, 4, tile, "dct", DEV)
+    K().sd1_encode(st, ks, vs, cos=t(cos), sin=t(sin), pos0=300)
+    kf, vf = ks.float().cpu().numpy(), vs.float().cpu().numpy()
+    for h in range(n_kv):
+        want = S.encode(kf[:, h], vf[:, h], tile, "dct", cos=cos, sin=sin, pos0=300)
+        assert np.array_equal(st.kbits[0, h, :2].cpu().numpy().view(np.uint32), want["kbits"])
+        assert np.array_equal(st.vbits[0, h, :2].cpu().numpy().view(np.uint32), want["vbits"])
+        assert bits_eq(st.kscale[0, h, :2].cpu().numpy().view(np.uint16), want["kscale"].view(np.uint16))
+
+
 def _store(seed, n_tiles, tile=64, kind="hadamard", n_kv=8, n_q=32, B=1):
     k, v, q = cfg0(seed, n_tiles * tile, n_kv=n_kv, n_q=n_q, B=B)
     st = K().Sd1Store(B, n_kv, n_tiles + 3, tile, kind, DEV)
