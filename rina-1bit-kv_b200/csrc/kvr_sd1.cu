@@ -22,6 +22,29 @@ __global__ void __launch_bounds__(256) transform_kernel(const float *x, float *y
   load_lee(lee_s);
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (kind == KVR_DCT) {
+    // quad form: each warp transforms 8 rows at a time
+    __shared__ __align__(16) float qscr[8][8 * kD];
+    for (int64_t r0 = ((int64_t)blockIdx.x * 8 + warp) * 8; r0 < rows; r0 += (int64_t)gridDim.x * 64) {
+      const int64_t r = r0 + (lane >> 2);
+      const int t = lane & 3;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 a = r < rows ? reinterpret_cast<const float4 *>(x + r * kD + 32 * t)[i]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+      }
+      if (inverse) dct128_inv_quad(v, lane, qscr[warp]);
+      else dct128_fwd_quad(v, lane, qscr[warp]);
+      if (r < rows)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4 *>(y + r * kD + 32 * t)[i] =
+              make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    return;
+  }
   for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += (int64_t)gridDim.x * 8) {
     float v[4];
     float4 t = reinterpret_cast<const float4 *>(x + r * kD)[lane];

@@ -255,4 +255,261 @@ __device__ __forceinline__ void dct128_fwd_reg(float (&x)[kD]) {
   for (int i = 1; i < kD; ++i) x[i] = __fmul_rn(x[i], c1);
 }
 
+// ---- quad form: 4 lanes per vector, 32 elements per lane in registers.
+// Lane t (= lane & 3) of a quad enters and leaves holding elements
+// 32t .. 32t+31 in order; the 8 quads of a warp transform 8 vectors at once
+// (all 32 lanes must call).  Only the two outermost Lee levels on each side
+// cross lanes: for the forward split levels the lanes hold their blocks in
+// orientations chosen so that the partner element sits in the SAME register
+// of the xor partner (one shuffle per element, no index arithmetic); the
+// 128-point merge goes through `scr` (128 floats per quad, private to the
+// quad).  Every value is produced by the same operation on the same operands
+// as in the specification, so the results are bit-identical to dct128_fwd /
+// dct128_inv.  Latency: ~1 k instructions per lane, no block barriers.
+template <int N, int M>
+__device__ __forceinline__ void lee_split_n(float (&v)[N]) {
+  constexpr int half = M / 2;
+  float y[N];
+#pragma unroll
+  for (int o = 0; o < N; o += M) {
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float xa = v[o + j], xb = v[o + M - 1 - j];
+      y[o + j] = __fadd_rn(xa, xb);
+      y[o + half + j] = __fmul_rn(__fsub_rn(xa, xb), lee_factor(half - 1 + j));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = y[i];
+}
+template <int N, int M>
+__device__ __forceinline__ void lee_merge_n(float (&v)[N]) {
+  constexpr int half = M / 2;
+  float y[N];
+#pragma unroll
+  for (int o = 0; o < N; o += M) {
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      y[o + 2 * k] = v[o + k];
+      y[o + 2 * k + 1] = k < half - 1 ? __fadd_rn(v[o + half + k], v[o + half + k + 1]) : v[o + half + k];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = y[i];
+}
+// transposed levels (inverse)
+template <int N, int M>
+__device__ __forceinline__ void lee_merge_t_n(float (&v)[N]) {
+  constexpr int half = M / 2;
+  float y[N];
+#pragma unroll
+  for (int o = 0; o < N; o += M) {
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      y[o + k] = v[o + 2 * k];
+      y[o + half + k] = k > 0 ? __fadd_rn(v[o + 2 * k + 1], v[o + 2 * k - 1]) : v[o + 1];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = y[i];
+}
+template <int N, int M>
+__device__ __forceinline__ void lee_split_t_n(float (&v)[N]) {
+  constexpr int half = M / 2;
+  float y[N];
+#pragma unroll
+  for (int o = 0; o < N; o += M) {
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float a = v[o + j], fb = __fmul_rn(v[o + half + j], lee_factor(half - 1 + j));
+      y[o + j] = __fadd_rn(a, fb);
+      y[o + M - 1 - j] = __fsub_rn(a, fb);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = y[i];
+}
+
+__device__ __forceinline__ void quad_reverse_if(float (&v)[32], bool rev) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float a = v[i], b = v[31 - i];
+    v[i] = rev ? b : a;
+    v[31 - i] = rev ? a : b;
+  }
+}
+
+__device__ __forceinline__ void dct128_fwd_quad(float (&v)[32], int lane, float *scr) {
+  const int t = lane & 3;
+  // split 128 (partner: t ^ 3).  Lanes 1 and 3 hold their block reversed, so
+  // register i of a lane and register i of its partner form a pair (j, 127-j).
+  quad_reverse_if(v, (t & 1) != 0);
+  {
+    const bool ra = t < 2;  // lanes 0, 1 keep a_j = x_j + x_{127-j}; lanes 2, 3 form b_j
+    const float sg = ra ? 1.0f : -1.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float r = __shfl_xor_sync(0xffffffffu, v[i], 3);
+      // b-role: lane 3 holds x_{127-i} (pairs with x_i: factor index i),
+      // lane 2 holds x_{64+i} (pairs with x_{63-i}: factor index 63-i)
+      const float f = t == 3 ? lee_factor(63 + i) : lee_factor(126 - i);
+      const float sum = __fadd_rn(r, v[i] * sg);  // a: x_j + x_{127-j}; b: x_j - x_{127-j}
+      v[i] = __fmul_rn(sum, ra ? 1.0f : f);
+    }
+  }
+  // now lane 0: [0,32), lane 1: [32,64) reversed, lane 3: [64,96), lane 2: [96,128) reversed
+  // split 64 (partner: t ^ 1); lanes 0 and 3 hold the first halves
+  {
+    const bool fa = t == 0 || t == 3;
+    const float sg = fa ? 1.0f : -1.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float r = __shfl_xor_sync(0xffffffffu, v[i], 1);
+      const float sum = __fadd_rn(r, v[i] * sg);
+      v[i] = __fmul_rn(sum, fa ? 1.0f : lee_factor(31 + i));
+    }
+  }
+  // lane 0: [0,32), lane 1: [32,64), lane 3: [64,96), lane 2: [96,128), all in order
+  lee_split_n<32, 32>(v);
+  lee_split_n<32, 16>(v);
+  lee_split_n<32, 8>(v);
+  lee_split_n<32, 4>(v);
+  lee_split_n<32, 2>(v);
+  lee_merge_n<32, 2>(v);
+  lee_merge_n<32, 4>(v);
+  lee_merge_n<32, 8>(v);
+  lee_merge_n<32, 16>(v);
+  lee_merge_n<32, 32>(v);
+  // merge 64 (partner t ^ 1): first-half lanes (A) emit block positions 0..31,
+  // second-half lanes (B) emit 32..63
+  {
+    const bool first = t == 0 || t == 3;
+    float rcv[17];
+#pragma unroll
+    for (int k = 0; k < 17; ++k) {
+      const float send = first ? v[16 + k < 32 ? 16 + k : 31] : v[k];
+      rcv[k] = __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+    float o[32];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      o[2 * k] = first ? v[k] : rcv[k];
+      const float bf = __fadd_rn(rcv[k], rcv[k + 1]);
+      const float bs = k < 15 ? __fadd_rn(v[16 + k], v[17 + k]) : v[31];
+      o[2 * k + 1] = first ? bf : bs;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = o[i];
+  }
+  // merge 128 and the orthonormal scaling through the quad's scratch
+  const int quad_base = (lane >> 2) * kD;
+  float *q = scr + quad_base;
+  const int bpos = t == 2 ? 96 : (t == 3 ? 64 : 32 * t);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    reinterpret_cast<float4 *>(q + bpos)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  __syncwarp();
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  float A[16], B[17];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 a4 = reinterpret_cast<const float4 *>(q + 16 * t)[i];
+    const float4 b4 = reinterpret_cast<const float4 *>(q + 64 + 16 * t)[i];
+    A[4 * i] = a4.x; A[4 * i + 1] = a4.y; A[4 * i + 2] = a4.z; A[4 * i + 3] = a4.w;
+    B[4 * i] = b4.x; B[4 * i + 1] = b4.y; B[4 * i + 2] = b4.z; B[4 * i + 3] = b4.w;
+  }
+  B[16] = t < 3 ? q[64 + 16 * t + 16] : 0.0f;
+  __syncwarp();
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    v[2 * m] = __fmul_rn(A[m], (t == 0 && m == 0) ? c0 : c1);
+    const float bo = (t == 3 && m == 15) ? B[15] : __fadd_rn(B[m], B[m + 1]);
+    v[2 * m + 1] = __fmul_rn(bo, c1);
+  }
+}
+
+__device__ __forceinline__ void dct128_inv_quad(float (&v)[32], int lane, float *scr) {
+  const int t = lane & 3;
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  const int quad_base = (lane >> 2) * kD;
+  float *q = scr + quad_base;
+  // scaling, then the transposed merges 128 and 64 read from the scratch:
+  // y -> new (new_k = y_2k, B_j = new_{64+j} = y_{2j+1} + y_{2j-1}) -> the
+  // 64-blocks; lane t takes block positions 32t .. 32t+31 of the result
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    reinterpret_cast<float4 *>(q + 32 * t)[i] =
+        make_float4(__fmul_rn(v[4 * i], (t == 0 && i == 0) ? c0 : c1), __fmul_rn(v[4 * i + 1], c1),
+                    __fmul_rn(v[4 * i + 2], c1), __fmul_rn(v[4 * i + 3], c1));
+  __syncwarp();
+  if (t == 0) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = q[4 * k];
+  } else if (t == 1) {
+    v[0] = q[2];
+#pragma unroll
+    for (int k = 1; k < 32; ++k) v[k] = __fadd_rn(q[4 * k + 2], q[4 * k - 2]);
+  } else {
+    // B_j = y_{2j+1} + y_{2j-1} (B_0 = y_1)
+    float Bv[65];
+    Bv[0] = q[1];
+#pragma unroll
+    for (int j = 1; j < 64; ++j) Bv[j] = __fadd_rn(q[2 * j + 1], q[2 * j - 1]);
+    if (t == 2) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = Bv[2 * k];
+    } else {
+      v[0] = Bv[1];
+#pragma unroll
+      for (int k = 1; k < 32; ++k) v[k] = __fadd_rn(Bv[2 * k + 1], Bv[2 * k - 1]);
+    }
+  }
+  __syncwarp();
+  lee_merge_t_n<32, 32>(v);
+  lee_merge_t_n<32, 16>(v);
+  lee_merge_t_n<32, 8>(v);
+  lee_merge_t_n<32, 4>(v);
+  lee_merge_t_n<32, 2>(v);
+  lee_split_t_n<32, 2>(v);
+  lee_split_t_n<32, 4>(v);
+  lee_split_t_n<32, 8>(v);
+  lee_split_t_n<32, 16>(v);
+  lee_split_t_n<32, 32>(v);
+  // transposed split 64 (partner t ^ 1): lanes 0, 2 hold a, lanes 1, 3 hold b
+  {
+    const bool first = (t & 1) == 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float r = __shfl_xor_sync(0xffffffffu, v[i], 1);
+      const float a = first ? v[i] : r, b = first ? r : v[i];
+      const float fb = __fmul_rn(b, lee_factor(31 + i));
+      v[i] = first ? __fadd_rn(a, fb) : __fsub_rn(a, fb);  // second lanes: position 63-i
+    }
+  }
+  // lane 0: [0,32), lane 1: [32,64) reversed, lane 2: [64,96), lane 3: [96,128) reversed
+  // transposed split 128 (partner t ^ 2): lanes 0, 1 hold a, lanes 2, 3 hold b
+  {
+    const bool ha = t < 2;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float r = __shfl_xor_sync(0xffffffffu, v[i], 2);
+      const float a = ha ? v[i] : r, b = ha ? r : v[i];
+      const float fb = __fmul_rn(b, (t & 1) ? lee_factor(126 - i) : lee_factor(63 + i));
+      v[i] = ha ? __fadd_rn(a, fb) : __fsub_rn(a, fb);
+    }
+  }
+  // lane 0: [0,32), lane 1: [32,64) reversed, lane 2: [96,128) reversed, lane 3: [64,96)
+  const bool rev = t == 1 || t == 2;
+  const int bpos = t == 2 ? 96 : (t == 3 ? 64 : 32 * t);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) q[bpos + (rev ? 31 - i : i)] = v[i];
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 x4 = reinterpret_cast<const float4 *>(q + 32 * t)[i];
+    v[4 * i] = x4.x; v[4 * i + 1] = x4.y; v[4 * i + 2] = x4.z; v[4 * i + 3] = x4.w;
+  }
+  __syncwarp();
+}
+
 }  // namespace kvr
