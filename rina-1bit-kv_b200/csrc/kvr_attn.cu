@@ -15,6 +15,7 @@
 // with GQA kvh = hq / g (modules/kvr_window.py:43-69, kvr_hook.py:274-282,
 // kvr_triton.py:42-79, kvr_generator.py:448-450).
 #include "kvr_common.cuh"
+#include "kvr_topk.cuh"
 #include "kvr_transform.cuh"
 
 #include <cstdlib>
@@ -49,6 +50,11 @@ struct AttnArgs {
   int64_t nt_cap;
   int tile, kind, k_sel;
   const int32_t *sel;  // (B, n_kv, k_sel)
+  // selection inside the tile units (batch-1 decode): scores of the row
+  // (B, n_kv, rank_n), exclusion range, and where the chosen indices go
+  const float *rank_scores;
+  int64_t rank_n, rank_ex0, rank_ex1;
+  int32_t *sel_out;
   void *out;
   int out_dt;
   float *partial_out;  // (B, n_q, d+2) or null
@@ -255,6 +261,35 @@ __device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int 
   fold_unit(a, sm, false);
 }
 
+// ------------------------------------------------------- in-unit select ----
+// Tile unit `slot` attends the tile of rank `slot` (score desc, index asc).
+// Every tile unit of a row finds its own order statistic of the row's scores
+// with a block radix select, so the selection needs no cross-CTA hand-off
+// (no counter, no second pass over L2); the result equals the selection
+// kernel's sel[row][slot] exactly (the keys are unique).  Uses the unit
+// staging region before the unit's copies are issued.
+constexpr int64_t kRankMaxTiles = 4096;
+__device__ int32_t rank_select(const AttnArgs &a, unsigned char *sm, int64_t row, int slot) {
+  const int64_t n = a.rank_n;
+  const int kk = (int)(n < a.k_sel ? n : a.k_sel);
+  int32_t t = -1;
+  if (slot < kk) {
+    float *sc = reinterpret_cast<float *>(sm);
+    TopkSmem &ts = *reinterpret_cast<TopkSmem *>(sm + kRankMaxTiles * 4);
+    const float *src = a.rank_scores + row * n;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+      sc[i] = (i >= a.rank_ex0 && i < a.rank_ex1) ? -INFINITY : __ldcg(src + i);
+    __syncthreads();
+    const unsigned long long key = block_kth_largest<256>([&](int64_t i) -> float { return sc[i]; }, n, slot + 1, ts);
+    t = (int32_t)key_index(key);
+    __syncthreads();  // the region is reused for the unit's copies
+  }
+  if (threadIdx.x == 0 && a.sel_out != nullptr) a.sel_out[row * a.k_sel + slot] = t;
+  return t;
+}
+
+static_assert(kRankMaxTiles * 4 + sizeof(TopkSmem) <= AttnSmem::kQ, "in-unit selection must fit the unit region");
+
 // ------------------------------------------------------------- sd1 unit ----
 template <int TILE>
 __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h, int slot, int u) {
@@ -271,8 +306,8 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   int *flag = reinterpret_cast<int *>(sm + AttnSmem::kFlag);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = b * a.n_kv + h;
-  griddep_wait();  // sel and qprime come from the selection kernel
-  const int32_t t = a.sel[row * a.k_sel + slot];
+  griddep_wait();  // sel (or the scores) and qprime come from the selection kernel
+  const int32_t t = a.rank_scores != nullptr ? rank_select(a, sm, row, slot) : a.sel[row * a.k_sel + slot];
   if (t < 0) return;  // empty slot: nothing to fold
   const int64_t tix = row * a.nt_cap + t;
   constexpr unsigned kBits = TILE * 16, kScale = kD * 2;
@@ -833,18 +868,22 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                        float *qprime, unsigned *counters, float *scores, cudaStream_t st,
-                       const uint32_t *vbits, const uint16_t *vscale);
+                       const uint32_t *vbits, const uint16_t *vscale, int do_select);
+
+// Units per CTA: one unit per CTA while the rows leave the GPU idle (batch 1,
+// latency-bound), more as rows grow, so about two CTAs per SM are launched
+// and each folds its units on chip (batched decode, bandwidth-bound).
+static int attn_upc(int64_t units, int64_t rows) {
+  const int64_t target = 2 * 148;
+  int64_t upc = (units * rows + target - 1) / target;
+  return (int)(upc < 1 ? 1 : (upc > units ? units : upc));
+}
 
 int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool pdl = false) {
   if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
   size_t smem = AttnSmem::kTotal;
-  // Units per CTA: one unit per CTA while the rows leave the GPU idle (batch 1,
-  // latency-bound), more as rows grow, so about two CTAs per SM are launched
-  // and each folds its units on chip (batched decode, bandwidth-bound).
-  const int64_t rows = (int64_t)batch * a.n_kv;
-  const int64_t target = 2 * 148;
-  int upc = (int)((a.units * rows + target - 1) / target);
-  upc = upc < 1 ? 1 : (upc > a.units ? a.units : upc);
+  const int upc = attn_upc(a.units, (int64_t)batch * a.n_kv);
+  KVR_REQUIRE(a.rank_scores == nullptr || upc == 1, "%s: in-unit selection needs one unit per CTA", what);
   a.upc = upc;
   a.slots = (a.units + upc - 1) / upc;
   // the pipelined path streams fp16 rows with 16-byte async copies
@@ -963,7 +1002,9 @@ static int sd1_attend_impl(const void *q, int q_dtype, const float *qprime, int 
                            const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap,
                            int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out,
                            int out_dtype, float *partial_out, void *workspace, size_t workspace_bytes,
-                           kvr_stream_t stream, bool pdl) {
+                           kvr_stream_t stream, bool pdl, const float *rank_scores = nullptr,
+                           int64_t rank_n = 0, int64_t rank_ex0 = 0, int64_t rank_ex1 = 0,
+                           int32_t *sel_out = nullptr) {
   KVR_REQUIRE(batch > 0 && n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
               "kvr_sd1_attend: need n_q %% n_kv == 0 and n_q/n_kv <= 8");
   KVR_REQUIRE(tile == 32 || tile == 64 || tile == 128, "kvr_sd1_attend: tile must be 32, 64 or 128");
@@ -988,6 +1029,8 @@ static int sd1_attend_impl(const void *q, int q_dtype, const float *qprime, int 
   a.nchunk[1] = (int)((n_tail + kChunk - 1) / kChunk);
   a.kbits = kbits; a.kscale = kscale; a.vbits = vbits; a.vscale = vscale; a.nt_cap = nt_cap;
   a.tile = tile; a.kind = kind; a.sel = sel; a.k_sel = k_sel;
+  a.rank_scores = rank_scores; a.rank_n = rank_n; a.rank_ex0 = rank_ex0; a.rank_ex1 = rank_ex1;
+  a.sel_out = sel_out;
   a.out = out; a.out_dt = out_dtype; a.partial_out = partial_out;
   a.units = sd1_units(n_win, n_tail, k_sel);
   if (a.units == 0) {
@@ -1064,15 +1107,20 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   float *scores = reinterpret_cast<float *>(p + a_bytes);
   int32_t *sel = sel_out ? sel_out : reinterpret_cast<int32_t *>(p + a_bytes + s_bytes);
   float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
+  // One unit per attention CTA (batch-1, latency-bound): the selection
+  // kernel only scores, and every tile unit picks its own tile by rank.
+  const bool rank = k_sel > 0 && n_tiles > 0 && n_tiles <= kRankMaxTiles &&
+                    attn_upc(sd1_units(n_win, n_tail, k_sel), (int64_t)batch * n_kv) == 1;
   int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
-                              as_cuda(stream), vbits, vscale);
+                              as_cuda(stream), vbits, vscale, rank ? 0 : 1);
   if (rc) return rc;
   // the attention kernel is a programmatic dependent of the selection
   // kernel: its window/tail units overlap the tile scan, its tile units wait
   return sd1_attend_impl(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
                          kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
-                         workspace, a_bytes, stream, true);
+                         workspace, a_bytes, stream, true, rank ? scores : nullptr, n_tiles, ex_t0, ex_t1,
+                         rank ? sel : nullptr);
 }
 
 #ifdef KVR_TRACE

@@ -622,7 +622,7 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                        float *qprime, unsigned *counters, float *scores, cudaStream_t st,
-                       const uint32_t *vbits, const uint16_t *vscale) {
+                       const uint32_t *vbits, const uint16_t *vscale, int do_select) {
   int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
   if (rc) return rc;
   KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
@@ -635,7 +635,7 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
   // With no full tile there is nothing to score; the kernel still forms q'
   // and writes an all-empty selection.
   return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
-                         sa, 1, st);
+                         sa, do_select, st);
 }
 }  // namespace kvr
 
@@ -657,7 +657,7 @@ extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, in
   char *p = reinterpret_cast<char *>(workspace);
   return sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                             ex_t1, tile_base, sel, sel_scores, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters),
-                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream), nullptr, nullptr);
+                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream), nullptr, nullptr, 1);
 }
 
 extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,

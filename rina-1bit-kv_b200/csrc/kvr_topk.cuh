@@ -13,7 +13,7 @@
 namespace kvr {
 
 struct TopkSmem {
-  unsigned long long prefix, mask;
+  unsigned long long prefix, mask, result;
   int remaining, bin_count, n_out;
   int hist[256];
   unsigned long long lists[512];  // per-warp top-32 lists (up to 16 warps)
@@ -26,6 +26,78 @@ __device__ __forceinline__ int64_t key_index(unsigned long long key) {
   return (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
 }
 __device__ __forceinline__ float key_score(unsigned long long key) { return key_float((uint32_t)(key >> 32)); }
+
+// The m-th largest key (1 <= m <= n) of the n entries: the same MSB-first
+// digit walk as block_topk, stopping as soon as the chosen bin holds a single
+// key (or after all 64 bits).  Must be called by all NT threads; every
+// thread gets the result.
+template <int NT, typename ScoreFn>
+__device__ unsigned long long block_kth_largest(ScoreFn score_of, int64_t n, int m, TopkSmem &sm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    sm.prefix = 0ull;
+    sm.mask = 0ull;
+    sm.remaining = m;
+    sm.bin_count = -1;
+  }
+  for (int b = tid; b < 256; b += NT) sm.hist[b] = 0;
+  __syncthreads();
+  int pass = 0;
+  for (; pass < 8; ++pass) {
+    const int shift = 56 - 8 * pass;
+    const unsigned long long prefix = sm.prefix, mask = sm.mask;
+    for (int64_t i = tid; i < n; i += NT) {
+      const unsigned long long key = make_key(score_of(i), i);
+      if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending)
+      int c[8], s = 0;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        c[r] = sm.hist[255 - 8 * lane - r];
+        s += c[r];
+      }
+      int incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int excl = incl - s;
+      const int rem = sm.remaining;
+      __syncwarp();
+      if (excl < rem && rem <= incl) {
+        int cum = excl;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          if (cum + c[r] >= rem) {
+            const unsigned long long digit = (unsigned long long)(255 - 8 * lane - r);
+            sm.prefix = prefix | (digit << shift);
+            sm.mask = mask | (0xffull << shift);
+            sm.remaining = rem - cum;
+            sm.bin_count = c[r];
+            break;
+          }
+          cum += c[r];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) sm.hist[8 * lane + r] = 0;  // ready for the next pass
+    }
+    __syncthreads();
+    if (sm.bin_count == 1) break;
+  }
+  if (pass == 8) return sm.prefix;  // all 64 bits fixed
+  const unsigned long long prefix = sm.prefix, mask = sm.mask;
+  for (int64_t i = tid; i < n; i += NT) {
+    const unsigned long long key = make_key(score_of(i), i);
+    if ((key & mask) == prefix) sm.result = key;  // exactly one entry matches
+  }
+  __syncthreads();
+  return sm.result;
+}
 
 // score_of(i) -> float for 0 <= i < n (exclusions already mapped to -inf).
 // cand: shared array of at least next_pow2(k) keys.  On return (after a

@@ -147,6 +147,30 @@ def test_select_more_than_available_and_empty():
     assert (sel.cpu().numpy() == -1).all()
 
 
+@pytest.mark.parametrize("nt,k_sel,ex", [(24, 9, (5, 11)), (7, 12, (0, 0)), (300, 16, (250, 300)), (40, 16, (0, 40))])
+def test_decode_step_in_unit_selection_matches_select(nt, k_sel, ex):
+    """The decode step picks tiles inside the attention units (one order
+    statistic per unit); with duplicated tiles (exact score ties, broken by
+    index), an exclusion range and fewer tiles than k_sel it must select
+    exactly what the selection kernel selects, and attend the same."""
+    tile, n_kv, g, B = 64, 4, 4, 2
+    rng = np.random.default_rng(nt)
+    base = rng.standard_normal((B, 4 * tile, n_kv, 128)).astype(F32)
+    reps = (nt + 3) // 4
+    k = np.concatenate([base] * reps, 1)[:, :nt * tile]  # tile i == tile i % 4
+    v = rng.standard_normal(k.shape).astype(F32)
+    st = K().Sd1Store(B, n_kv, nt + 2, tile, "dct", DEV)
+    K().sd1_encode(st, t(k), t(v))
+    q = t(rng.standard_normal((B, n_kv * g, 128)).astype(F32))
+    win = t(rng.standard_normal((B, 70, n_kv, 128)).astype(np.float16))
+    sel, _, qp = K().sd1_select(st, q, k_sel, ex_t0=ex[0], ex_t1=ex[1])
+    sel_f = torch.full_like(sel, -7)
+    step = K().sd1_decode_step(st, q, k_sel, win, win, 70, ex_t0=ex[0], ex_t1=ex[1], sel_out=sel_f)
+    assert torch.equal(sel_f, sel)
+    want = K().sd1_attend(st, q, qp, sel, win, win, 70)
+    assert torch.equal(step, want)
+
+
 def _oracle_attend(q, st, b, h, sel_row, win_k, win_v, nw, tail_k, tail_v, ntl, kind, g):
     rows_k = [win_k[b, :nw, h].astype(np.float64), tail_k[b, :ntl, h].astype(np.float64)]
     rows_v = [win_v[b, :nw, h].astype(np.float64), tail_v[b, :ntl, h].astype(np.float64)]
