@@ -11,7 +11,10 @@ import os
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libkvr_b200.so")
+# KVR_B200_LIB: load another build of the same library (A/B measurements of
+# kernel variants); default: the in-tree build.
+LIB_PATH = os.environ.get("KVR_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib",
+                                                           "libkvr_b200.so")
 
 KVR_F32, KVR_F16, KVR_BF16 = 0, 1, 2
 KVR_HADAMARD, KVR_DCT = 0, 1
