@@ -66,18 +66,57 @@ __device__ __forceinline__ uint32_t pf_a_off(int m, int kc) {
 }
 
 // q (Nq, n_q, d) -> Q' fp16 in A-block layout: block (h, qb) is 32 KB at
-// ((h * nqb + qb) * 32 KB); query rows past nq are zero.
+// ((h * nqb + qb) * 32 KB); query rows past nq are zero.  A quad of lanes per
+// row (lane t: elements 32t .. 32t+31): group mean in head order, then the
+// transform in registers (quad DCT / 32-lane Hadamard), fp16 out.
 template <int DTQ>
 __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void *__restrict__ q, int64_t nq, int n_q,
                                                             int n_kv, int kind, int64_t nqb,
                                                             unsigned char *__restrict__ qa) {
-  __shared__ float lee_s[kD];
-  __shared__ __align__(16) float buf_s[8][2 * kD];
-  load_lee(lee_s);
-  __syncthreads();
+  __shared__ __align__(16) float qscr[8][8 * kD];  // quad scratch per warp
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = n_q / n_kv;
   const int64_t rows = nqb * kPfM * n_kv;
+  if (kind == KVR_DCT) {
+    const int t = lane & 3;
+    for (int64_t r0 = ((int64_t)blockIdx.x * 8 + warp) * 8; r0 < rows; r0 += (int64_t)gridDim.x * 64) {
+      const int64_t r = r0 + (lane >> 2);
+      const int64_t i = r / n_kv;
+      const int h = (int)(r - i * n_kv);
+      float v[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = 0.0f;
+      if (r < rows && i < nq) {
+        const int64_t qb = (i * n_q + (int64_t)h * g) * kD + 32 * t;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) load4<DTQ>(q, qb + 4 * c, *reinterpret_cast<float(*)[4]>(v + 4 * c));
+        for (int k = 1; k < g; ++k) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float x4[4];
+            load4<DTQ>(q, qb + (int64_t)k * kD + 4 * c, x4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[4 * c + e] = __fadd_rn(v[4 * c + e], x4[e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __fdiv_rn(v[e], (float)g);
+      }
+      dct128_fwd_quad(v, lane, qscr[warp]);  // all lanes (rows past the end carry zeros)
+      if (r < rows) {
+        const int64_t blk = (int64_t)h * nqb + i / kPfM;
+        const int m = (int)(i % kPfM);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 8-channel chunks 4t .. 4t+3
+          __half2 hv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(v[8 * c + 2 * e], v[8 * c + 2 * e + 1]);
+          *reinterpret_cast<uint4 *>(qa + blk * kPfSmemA + pf_a_off(m, 4 * t + c)) = *reinterpret_cast<uint4 *>(hv);
+        }
+      }
+    }
+    return;
+  }
   for (int64_t r = (int64_t)blockIdx.x * 8 + warp; r < rows; r += (int64_t)gridDim.x * 8) {
     const int64_t i = r / n_kv;
     const int h = (int)(r - i * n_kv);
@@ -93,7 +132,7 @@ __global__ void __launch_bounds__(256) prefill_qprep_kernel(const void *__restri
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[e] = __fdiv_rn(acc[e], (float)g);
-      transform128(acc, lane, kind, false, buf_s[warp], lee_s);
+      wht128(acc, lane);
     }
     const int64_t blk = (int64_t)h * nqb + i / kPfM;
     const int m = (int)(i % kPfM);
@@ -374,7 +413,8 @@ extern "C" int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, in
   unsigned char *qa = reinterpret_cast<unsigned char *>(p + kWsHeader);
   const int64_t nqb = pf_qblocks(nq);
   const int64_t rows = nqb * kPfM * n_kv;
-  const int qgrid = (int)((rows + 7) / 8 < 148 * 16 ? (rows + 7) / 8 : 148 * 16);
+  const int64_t per_cta = kind == KVR_DCT ? 64 : 8;  // rows per CTA per pass
+  const int qgrid = (int)((rows + per_cta - 1) / per_cta < 148 * 8 ? (rows + per_cta - 1) / per_cta : 148 * 8);
   if (q_dtype == KVR_F32) prefill_qprep_kernel<KVR_F32><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
   else if (q_dtype == KVR_F16) prefill_qprep_kernel<KVR_F16><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
   else prefill_qprep_kernel<KVR_BF16><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
