@@ -742,6 +742,9 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   const int64_t row = b * a.n_kv + h;
   const int tid = threadIdx.x;
   KVR_TRACE_POINT(1, 0);
+  // the next layer's selection kernel may start its store loads now; it
+  // waits for this kernel to finish before it reads q or writes anything
+  asm volatile("griddepcontrol.launch_dependents;");
   if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
   float *AM = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
   float *AL = reinterpret_cast<float *>(sm + AttnSmem::kAccL);

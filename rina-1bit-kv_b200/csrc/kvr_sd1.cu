@@ -272,9 +272,6 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   __shared__ int last_s;
   extern __shared__ __align__(16) unsigned char dyn_smem[];
 
-  // a dependent attention kernel may start now: it only reads what this
-  // kernel writes after its own griddepcontrol.wait
-  asm volatile("griddepcontrol.launch_dependents;");
   KVR_TRACE_POINT(0, 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -313,6 +310,12 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   };
   int64_t t_cur = cta_t0 + 2 * warp;
   if (t_cur < cta_t1) load_pair(t_cur, kb, ks);
+  // launched as a programmatic dependent of the previous kernel: everything
+  // above reads only the store; q is read, and anything written, after the
+  // previous kernel has finished.  Only then may the attention kernel that
+  // follows start (it shares the workspace with the previous one).
+  griddep_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
   // warp 0: all g query heads of the group are loaded before the (ordered) sum
   float qv[8][4];
   if (warp == 0) {
@@ -510,8 +513,20 @@ static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const
   case T:                                                                                                \
     if (smem > 48 * 1024)                                                                                \
       cudaFuncSetAttribute(sd1_score_kernel<DTQ, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    sd1_score_kernel<DTQ, T><<<grid, 256, smem, st>>>(q, n_q, n_kv, kb, ks, cap, nt, kind, scores, qprime, sa, \
-                                                       do_select, tpc);                                  \
+    {                                                                                                    \
+      cudaLaunchConfig_t cfg{};                                                                          \
+      cfg.gridDim = grid;                                                                                \
+      cfg.blockDim = dim3(256);                                                                          \
+      cfg.dynamicSmemBytes = smem;                                                                       \
+      cfg.stream = st;                                                                                   \
+      cudaLaunchAttribute at[1];                                                                         \
+      at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                     \
+      at[0].val.programmaticStreamSerializationAllowed = 1;                                              \
+      cfg.attrs = at;                                                                                    \
+      cfg.numAttrs = 1;                                                                                  \
+      cudaLaunchKernelEx(&cfg, sd1_score_kernel<DTQ, T>, q, n_q, n_kv, kb, ks, cap, nt, kind, scores,     \
+                         qprime, sa, do_select, tpc);                                                    \
+    }                                                                                                    \
     break;
     KVR_SC(32)
     KVR_SC(64)
