@@ -1111,12 +1111,15 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   int32_t *sel = sel_out ? sel_out : reinterpret_cast<int32_t *>(p + a_bytes + s_bytes);
   float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
   // One unit per attention CTA (batch-1, latency-bound): the selection
-  // kernel only scores, and every tile unit picks its own tile by rank.
+  // kernel only scores, every tile unit picks its own tile by rank, and the
+  // scan prefetches the V data of every scanned tile into L2 (at larger
+  // batches that prefetch would double the DRAM traffic for tiles that are
+  // mostly never selected).
   const bool rank = k_sel > 0 && n_tiles > 0 && n_tiles <= kRankMaxTiles &&
                     attn_upc(sd1_units(n_win, n_tail, k_sel), (int64_t)batch * n_kv) == 1;
   int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
-                              as_cuda(stream), vbits, vscale, rank ? 0 : 1);
+                              as_cuda(stream), rank ? vbits : nullptr, rank ? vscale : nullptr, rank ? 0 : 1);
   if (rc) return rc;
   // the attention kernel is a programmatic dependent of the selection
   // kernel: its window/tail units overlap the tile scan, its tile units wait
