@@ -384,6 +384,15 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    # stdout carries exactly one JSON line: anything else written to file
+    # descriptor 1 (library banners, warnings) is sent to stderr, and the
+    # result goes to a private copy of the original stdout
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(obj):
+        os.write(json_fd, (json.dumps(obj) + "\n").encode())
 
     if args.impl == "reference":
         if rank != 0:
@@ -397,11 +406,10 @@ def main():
                            "layers": LAYERS, "context": CTX, "window": WIN, "top_k_tokens": KSEL * TILE},
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
+        emit(line)
         return
 
     if world > 1:
-        # stdout carries exactly one JSON line: keep NCCL's version banner off it
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
         import torch
@@ -412,7 +420,7 @@ def main():
     if rank == 0:
         if world == 1:
             res["cpu_baseline"] = cpu_reference(args.cpu_sample)
-        print(json.dumps(res))
+        emit(res)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
