@@ -337,62 +337,87 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   }
   __syncthreads();
   if (!flag[0]) return;  // dropped after a bounded wait gave up (reported via the error word)
-  // signed nibble LUT: L[hq][grp][x] = sum_r (bit r of x ? +a : -a)_{4 grp + r}, a_c = q'_c s_c
-  for (int i = tid; i < a.g * 32; i += blockDim.x) {
-    const int hq = i >> 5, grp = i & 31;
-    float av[4];
+  if (warp < a.g) {
+    // one warp per query head: nibble LUT, scores, softmax and the bit-serial
+    // P.V of this head without block barriers
+    const int hq = warp;
+    {
+      const int grp = lane;
+      float av[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      av[r] = Qs[hq * kD + 4 * grp + r] * __half2float(__ushort_as_half(KS[4 * grp + r]));
-    float *L = LUT + (hq * 32 + grp) * 16;
+      for (int r = 0; r < 4; ++r)
+        av[r] = Qs[hq * kD + 4 * grp + r] * __half2float(__ushort_as_half(KS[4 * grp + r]));
+      float *Lw = LUT + (hq * 32 + grp) * 16;
 #pragma unroll
-    for (int x = 0; x < 16; ++x) {
-      float s = 0.0f;
+      for (int x = 0; x < 16; ++x) {
+        float s = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) s += ((x >> r) & 1) ? av[r] : -av[r];
-      L[x] = s;
+        for (int r = 0; r < 4; ++r) s += ((x >> r) & 1) ? av[r] : -av[r];
+        Lw[x] = s;
+      }
+    }
+    __syncwarp();
+    constexpr int TPLw = TILE / 32;
+    const float *Lh = LUT + hq * 32 * 16;
+    float sj[TPLw];
+#pragma unroll
+    for (int r = 0; r < TPLw; ++r) {
+      const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[lane + 32 * r];
+      const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int grp = 0; grp < 32; ++grp) acc[grp & 3] += Lh[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
+      sj[r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    }
+    float mx = sj[0];
+#pragma unroll
+    for (int r = 1; r < TPLw; ++r) mx = fmaxf(mx, sj[r]);
+    mx = warp_max(mx);
+    float l = 0.0f;
+#pragma unroll
+    for (int r = 0; r < TPLw; ++r) {
+      const float p = expf(sj[r] - mx);
+      P[(lane + 32 * r) * kMaxG + hq] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    __syncwarp();
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int j = 0; j < TILE; ++j) {
+      const float pj = P[j * kMaxG + hq];
+      const uint4 v4 = reinterpret_cast<const uint4 *>(VB)[j];
+      const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int mask = (int)(vw[m] << (31 - lane)) >> 31;  // all ones if channel lane + 32 m is set
+        o[m] += __int_as_float(__float_as_int(pj) & mask);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int c = lane + 32 * m;
+      S[hq * kD + c] = __half2float(__ushort_as_half(VS[c])) * (2.0f * o[m] - l);
+    }
+    if (lane == 0) {
+      ML[hq * 2] = mx;
+      ML[hq * 2 + 1] = l;
     }
   }
   __syncthreads();
-  constexpr int NB = TILE / 32;
-  for (int p = warp; p < a.g * NB; p += 8) {
-    const int hq = p / NB, j = (p - hq * NB) * 32 + lane;
-    const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[j];
-    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-    const float *L = LUT + hq * 32 * 16;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int grp = 0; grp < 32; ++grp) acc[grp & 3] += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
-    S[hq * kD + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-  }
-  __syncthreads();
-  softmax_rows(a, TILE, S, P, ML);
-  __syncthreads();
-  KVR_TRACE_POINT(1, 2);
-  const int c = tid & 127, half = tid >> 7;
-  float o[kMaxG];
-#pragma unroll
-  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
-  const int word = c >> 5, bit = c & 31;
-  for (int j = half * (TILE / 2); j < (half + 1) * (TILE / 2); ++j) {
-    const float bf = (float)((VB[j * 4 + word] >> bit) & 1u);
-    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
-    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
-    o[0] = fmaf(p0.x, bf, o[0]); o[1] = fmaf(p0.y, bf, o[1]);
-    o[2] = fmaf(p0.z, bf, o[2]); o[3] = fmaf(p0.w, bf, o[3]);
-    if (a.g > 4) {
-      o[4] = fmaf(p1.x, bf, o[4]); o[5] = fmaf(p1.y, bf, o[5]);
-      o[6] = fmaf(p1.z, bf, o[6]); o[7] = fmaf(p1.w, bf, o[7]);
+  if (a.upc == 1 && a.slots > 1) {
+    // one unit per CTA: its (m, l, o) is the CTA's partial row
+    for (int i = tid; i < a.g * (kD / 4); i += blockDim.x) {
+      const int hq = i / (kD / 4), c4 = i - hq * (kD / 4);
+      float *pr = part_row(a, row, blockIdx.x, hq);
+      reinterpret_cast<float4 *>(pr + kPartEx)[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4 *>(pr + kPartTr)[c4] = reinterpret_cast<const float4 *>(S + hq * kD)[c4];
+      if (c4 == 0) *reinterpret_cast<float2 *>(pr) = make_float2(ML[2 * hq], ML[2 * hq + 1]);
     }
+    if (tid == 0) flag[2] = 1;
+    __syncthreads();
+    return;
   }
-  if (half == 1)
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
-  __syncthreads();
-  if (half == 0) {
-    const float vs = __half2float(__ushort_as_half(VS[c]));
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - ML[hq * 2 + 1]);
-  }
-  __syncthreads();
   fold_unit(a, sm, true);
 }
 
@@ -758,6 +783,7 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
     AM[tid] = -INFINITY;
     AL[tid] = 0.0f;
   }
+  if (tid == 0) reinterpret_cast<int *>(sm + AttnSmem::kFlag)[2] = 0;  // partial row written by the unit
   __syncthreads();
   const int n_exact = a.nchunk[0] + a.nchunk[1];
   const int u_end = min(a.units, (slot + 1) * a.upc);
@@ -788,6 +814,8 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
     return;
   }
   // write this CTA's partial rows, then the last CTA of the row merges
+  const bool written = reinterpret_cast<const int *>(sm + AttnSmem::kFlag)[2] != 0;
+  if (!written)
   for (int i = tid; i < a.g * (kD / 4); i += blockDim.x) {
     const int hq = i / (kD / 4), c4 = i - hq * (kD / 4);
     float *pr = part_row(a, row, slot, hq);
