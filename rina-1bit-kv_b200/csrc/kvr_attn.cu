@@ -642,6 +642,37 @@ __device__ void finalize_group(const AttnArgs &a, unsigned char *sm, int64_t b, 
                                const float *Tr, const float *ML, float *buf, bool any_tiles) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float *lee = reinterpret_cast<const float *>(sm + AttnSmem::kLee);
+  if (any_tiles && a.kind == KVR_DCT) {
+    // strided layout (lane l: elements l + 32 s), the shuffle inverse DCT
+    for (int hq = warp; hq < a.g; hq += 8) {
+      float x[4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) x[s] = Tr[hq * kD + lane + 32 * s];
+      dct128_inv_shfl(x, lane, lee);
+      const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
+      const float M = ML[hq * 2], L = ML[hq * 2 + 1];
+      if (a.partial_out) {
+        float *pr = a.partial_out + qh * (kD + 2);
+        if (lane == 0) {
+          pr[0] = M;
+          pr[1] = L;
+        }
+#pragma unroll
+        for (int s = 0; s < 4; ++s) pr[2 + lane + 32 * s] = Ex[hq * kD + lane + 32 * s] + x[s];
+      } else {
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const int64_t idx = qh * kD + lane + 32 * s;
+          const float y = (Ex[hq * kD + lane + 32 * s] + x[s]) * inv;
+          if (a.out_dt == KVR_F32) store_elem<KVR_F32>(a.out, idx, y);
+          else if (a.out_dt == KVR_F16) store_elem<KVR_F16>(a.out, idx, y);
+          else store_elem<KVR_BF16>(a.out, idx, y);
+        }
+      }
+    }
+    return;
+  }
   for (int hq = warp; hq < a.g; hq += 8) {
     float x[4];
     const float4 t4 = reinterpret_cast<const float4 *>(Tr + hq * kD)[lane];

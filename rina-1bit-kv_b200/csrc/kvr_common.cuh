@@ -143,6 +143,14 @@ __device__ __forceinline__ void kvr_trace(int kernel, int point) {
 // Bound on device-side spin iterations (each iteration also sleeps ~64 ns).
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+// One element as fp32.
+template <int DT>
+__device__ __forceinline__ float load1(const void *p, int64_t i) {
+  if constexpr (DT == KVR_F32) return __ldg(reinterpret_cast<const float *>(p) + i);
+  else if constexpr (DT == KVR_F16) return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(p) + i)));
+  else return __bfloat162float(__ushort_as_bfloat16(__ldg(reinterpret_cast<const unsigned short *>(p) + i)));
+}
+
 // Raw 4-element load (16 bytes for fp32, 8 bytes for 16-bit types) and its
 // widening to fp32; split so that many loads can be in flight at once.
 __device__ __forceinline__ uint4 raw4(const void *p, int64_t i, int dt) {

@@ -316,6 +316,37 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   // follows start (it shares the workspace with the previous one).
   griddep_wait();
   asm volatile("griddepcontrol.launch_dependents;");
+  if (kind == KVR_DCT) {
+    // strided layout (lane l: elements l + 32 s), the shuffle DCT: warp 0
+    // forms q' of the group mean, the other warps of CTA 0 the per-head T q_h
+    const int64_t qb = ((int64_t)b * n_q + (int64_t)h * g) * kD;
+    float xv[4];
+    if (warp == 0) {
+#pragma unroll
+      for (int s = 0; s < 4; ++s) xv[s] = load1<DTQ>(q, qb + lane + 32 * s);
+      for (int i = 1; i < g; ++i)
+#pragma unroll
+        for (int s = 0; s < 4; ++s) xv[s] = __fadd_rn(xv[s], load1<DTQ>(q, qb + (int64_t)i * kD + lane + 32 * s));
+#pragma unroll
+      for (int s = 0; s < 4; ++s) xv[s] = __fdiv_rn(xv[s], (float)g);
+    }
+    __syncthreads();  // Lee factors in shared memory
+    if (warp == 0) {
+      dct128_fwd_shfl(xv, lane, lee_s);
+#pragma unroll
+      for (int s = 0; s < 4; ++s) qp_s[lane + 32 * s] = xv[s];
+    } else if (blockIdx.x == 0 && qprime != nullptr) {
+      for (int i = warp - 1; i < g; i += 7) {
+        const int64_t qh = qb + (int64_t)i * kD;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) xv[s] = load1<DTQ>(q, qh + lane + 32 * s);
+        dct128_fwd_shfl(xv, lane, lee_s);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) qprime[qh + lane + 32 * s] = xv[s];
+      }
+    }
+    __syncthreads();
+  } else {
   // warp 0: all g query heads of the group are loaded before the (ordered) sum
   float qv[8][4];
   if (warp == 0) {
@@ -347,6 +378,7 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
     }
   }
   __syncthreads();
+  }
   KVR_TRACE_POINT(0, 1);
 
   while (t_cur < cta_t1) {  // warp-uniform

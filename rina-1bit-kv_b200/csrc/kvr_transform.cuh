@@ -512,4 +512,212 @@ __device__ __forceinline__ void dct128_inv_quad(float (&v)[32], int lane, float 
   __syncwarp();
 }
 
+// ---- strided warp form: lane l holds elements l, 32+l, 64+l, 96+l in
+// x[0..3] (the layout the tile scoring reads q' in).  Every Lee level moves
+// data register to register with shuffles: the 128- and 64-point levels pair
+// slot s with slot s' at lane 31-l (one xor-31 shuffle), the levels of 32
+// points and less stay inside a slot (at most three shuffles with computed
+// source lanes).  No shared-memory round trips, no warp barriers; the same
+// operations on the same operands as the specification (bit-identical to
+// dct128_fwd / dct128_inv).  lee: the 127 Lee factors (any memory).
+__device__ __forceinline__ float shf_(float v, int src) { return __shfl_sync(0xffffffffu, v, src); }
+__device__ __forceinline__ float shx_(float v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+
+template <int M>
+__device__ __forceinline__ void lee_split_shfl(float (&x)[4], int lane, const float *lee) {
+  constexpr int half = M / 2;
+  const int q = lane & (M - 1);
+  const bool first = q < half;
+  const float f = lee[half - 1 + (q & (half - 1))];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const float v = x[s];
+    const float r1 = shx_(v, M - 1), r2 = shx_(v, half), r3 = shx_(v, half - 1);
+    const float A = first ? v : r2, B = first ? r1 : r3;
+    x[s] = first ? __fadd_rn(A, B) : __fmul_rn(__fsub_rn(A, B), f);
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_merge_shfl(float (&x)[4], int lane) {
+  constexpr int half = M / 2;
+  const int q = lane & (M - 1), base = lane & ~(M - 1), k = q >> 1;
+  const bool even = (q & 1) == 0, last = q == M - 1;
+  const int s1 = base + k, s2 = base + half + k, s3 = min(base + half + k + 1, base + M - 1);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const float v = x[s];
+    const float r1 = shf_(v, s1), r2 = shf_(v, s2), r3 = shf_(v, s3);
+    x[s] = even ? r1 : (last ? r2 : __fadd_rn(r2, r3));
+  }
+}
+
+__device__ __forceinline__ void dct128_fwd_shfl(float (&x)[4], int lane, const float *lee) {
+  {  // split 128: slot pairs (0,3), (1,2) at mirrored lanes
+    const float b3 = shx_(x[3], 31), b2 = shx_(x[2], 31);
+    const float f0 = lee[63 + lane], f1 = lee[95 + lane];
+    const float n0 = __fadd_rn(x[0], b3), n1 = __fadd_rn(x[1], b2);
+    const float n2 = __fmul_rn(__fsub_rn(x[0], b3), f0), n3 = __fmul_rn(__fsub_rn(x[1], b2), f1);
+    x[0] = n0; x[1] = n1; x[2] = n2; x[3] = n3;
+  }
+  {  // split 64: slot pairs (0,1), (2,3)
+    const float f = lee[31 + lane];
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
+      const float a = x[s], b = shx_(x[s + 1], 31);
+      x[s] = __fadd_rn(a, b);
+      x[s + 1] = __fmul_rn(__fsub_rn(a, b), f);
+    }
+  }
+  lee_split_shfl<32>(x, lane, lee);
+  lee_split_shfl<16>(x, lane, lee);
+  lee_split_shfl<8>(x, lane, lee);
+  lee_split_shfl<4>(x, lane, lee);
+  lee_split_shfl<2>(x, lane, lee);
+  lee_merge_shfl<2>(x, lane);
+  lee_merge_shfl<4>(x, lane);
+  lee_merge_shfl<8>(x, lane);
+  lee_merge_shfl<16>(x, lane);
+  lee_merge_shfl<32>(x, lane);
+  const int k = lane >> 1;
+  const bool even = (lane & 1) == 0;
+  {  // merge 64 on slots (0,1) and (2,3)
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
+      const float A = x[s], B = x[s + 1];
+      const float a1 = shf_(A, k), a2 = shf_(B, k), a3 = shf_(B, k + 1);
+      const float b1 = shf_(A, 16 + k), b2 = shf_(B, 16 + k), b3 = shf_(B, min(17 + k, 31));
+      x[s] = even ? a1 : __fadd_rn(a2, a3);
+      x[s + 1] = even ? b1 : (lane == 31 ? b2 : __fadd_rn(b2, b3));
+    }
+  }
+  {  // merge 128
+    float y[4];
+    const float p96 = shf_(x[3], 0);
+#pragma unroll
+    for (int sp = 0; sp < 4; ++sp) {
+      const float A = x[sp >> 1], B = x[2 + (sp >> 1)];
+      const int o = 16 * (sp & 1);
+      const float r1 = shf_(A, o + k), r2 = shf_(B, o + k);
+      float r3 = shf_(B, min(o + k + 1, 31));
+      float odd;
+      if (sp == 1) {
+        r3 = lane == 31 ? p96 : r3;
+        odd = __fadd_rn(r2, r3);
+      } else if (sp == 3) {
+        odd = lane == 31 ? r2 : __fadd_rn(r2, r3);
+      } else {
+        odd = __fadd_rn(r2, r3);
+      }
+      y[sp] = even ? r1 : odd;
+    }
+    const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+    x[0] = __fmul_rn(y[0], lane == 0 ? c0 : c1);
+    x[1] = __fmul_rn(y[1], c1);
+    x[2] = __fmul_rn(y[2], c1);
+    x[3] = __fmul_rn(y[3], c1);
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void lee_merge_t_shfl(float (&x)[4], int lane) {
+  constexpr int half = M / 2;
+  const int q = lane & (M - 1), base = lane & ~(M - 1), kk = q & (half - 1);
+  const bool lo = q < half, k0 = kk == 0;
+  const int s1 = base + 2 * kk, s2 = base + 2 * kk + 1, s3 = base + max(2 * kk - 1, 0);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const float v = x[s];
+    const float r1 = shf_(v, s1), r2 = shf_(v, s2), r3 = shf_(v, s3);
+    x[s] = lo ? r1 : (k0 ? r2 : __fadd_rn(r2, r3));
+  }
+}
+template <int M>
+__device__ __forceinline__ void lee_split_t_shfl(float (&x)[4], int lane, const float *lee) {
+  constexpr int half = M / 2;
+  const int q = lane & (M - 1);
+  const bool lo = q < half;
+  const int j = lo ? q : M - 1 - q;
+  const float f = lee[half - 1 + j];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const float v = x[s];
+    const float ra = shx_(v, M - 1), rbl = shx_(v, half), rbh = shx_(v, half - 1);
+    const float a = lo ? v : ra;
+    const float fb = __fmul_rn(lo ? rbl : rbh, f);
+    x[s] = lo ? __fadd_rn(a, fb) : __fsub_rn(a, fb);
+  }
+}
+
+__device__ __forceinline__ void dct128_inv_shfl(float (&x)[4], int lane, const float *lee) {
+  const float c0 = __uint_as_float(kDctC0Bits), c1 = __uint_as_float(kDctC1Bits);
+  x[0] = __fmul_rn(x[0], lane == 0 ? c0 : c1);
+  x[1] = __fmul_rn(x[1], c1);
+  x[2] = __fmul_rn(x[2], c1);
+  x[3] = __fmul_rn(x[3], c1);
+  const int e = (2 * lane) & 31, o1 = (2 * lane + 1) & 31, o2 = (2 * lane - 1) & 31;
+  const bool low16 = lane < 16, le16 = lane <= 16;
+  {  // transposed merge 128
+    float y[4];
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp) {
+      const float ra = shf_(x[2 * sp], e), rb = shf_(x[2 * sp + 1], e);
+      y[sp] = low16 ? ra : rb;
+    }
+#pragma unroll
+    for (int sp = 2; sp < 4; ++sp) {
+      const int slo = 2 * (sp - 2), shi = slo + 1;
+      const float r1a = shf_(x[slo], o1), r1b = shf_(x[shi], o1);
+      const float p1 = low16 ? r1a : r1b;
+      const float r2a = shf_(x[slo], o2), r2b = shf_(x[shi], o2);
+      const float r2c = shf_(x[slo > 0 ? slo - 1 : 0], 31);
+      const float p2 = lane == 0 ? r2c : (le16 ? r2a : r2b);
+      float v = __fadd_rn(p1, p2);
+      if (sp == 2) v = lane == 0 ? p1 : v;
+      y[sp] = v;
+    }
+    x[0] = y[0]; x[1] = y[1]; x[2] = y[2]; x[3] = y[3];
+  }
+  {  // transposed merge 64 on slots (0,1) and (2,3)
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
+      const float A = x[s], B = x[s + 1];
+      const float ra = shf_(A, e), rb = shf_(B, e);
+      const float r1a = shf_(A, o1), r1b = shf_(B, o1);
+      const float r2a = shf_(A, o2), r2b = shf_(B, o2);
+      const float p1 = low16 ? r1a : r1b, p2 = le16 ? r2a : r2b;
+      x[s] = low16 ? ra : rb;
+      x[s + 1] = lane == 0 ? p1 : __fadd_rn(p1, p2);
+    }
+  }
+  lee_merge_t_shfl<32>(x, lane);
+  lee_merge_t_shfl<16>(x, lane);
+  lee_merge_t_shfl<8>(x, lane);
+  lee_merge_t_shfl<4>(x, lane);
+  lee_merge_t_shfl<2>(x, lane);
+  lee_split_t_shfl<2>(x, lane, lee);
+  lee_split_t_shfl<4>(x, lane, lee);
+  lee_split_t_shfl<8>(x, lane, lee);
+  lee_split_t_shfl<16>(x, lane, lee);
+  lee_split_t_shfl<32>(x, lane, lee);
+  {  // transposed split 64
+    const float f = lee[31 + lane];
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
+      const float a = x[s], fb = __fmul_rn(x[s + 1], f);
+      const float d = __fsub_rn(a, fb);
+      x[s] = __fadd_rn(a, fb);
+      x[s + 1] = shx_(d, 31);
+    }
+  }
+  {  // transposed split 128
+    const float fb0 = __fmul_rn(x[2], lee[63 + lane]), fb1 = __fmul_rn(x[3], lee[95 + lane]);
+    const float s0 = __fadd_rn(x[0], fb0), s1 = __fadd_rn(x[1], fb1);
+    const float d0 = __fsub_rn(x[0], fb0), d1 = __fsub_rn(x[1], fb1);
+    x[0] = s0;
+    x[1] = s1;
+    x[2] = shx_(d1, 31);
+    x[3] = shx_(d0, 31);
+  }
+}
+
 }  // namespace kvr
