@@ -725,7 +725,63 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
   const int p = tid % pairs, part = tid / pairs;
   const int hq = p >> 5, c4 = p & 31;
   float4 ex = make_float4(0.f, 0.f, 0.f, 0.f), tr = ex;
-  for (int s0 = 0; s0 < NS; s0 += UB * nparts) {
+  // (m, l) of every slot -> per-head weights exp(m - M) and the merged (M, L)
+  auto slot_weights = [&]() {
+    for (int i = tid; i < NS * a.g; i += blockDim.x) {
+      const int s = i / a.g, h2 = i - s * a.g;
+      WL[s * kMaxG + h2] = __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, s, h2)));
+    }
+    __syncthreads();
+    for (int h2 = warp; h2 < a.g; h2 += 8) {
+      float mx = -INFINITY;
+      for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, WL[s * kMaxG + h2].x);
+      mx = warp_max(mx);
+      float l = 0.0f;
+      for (int s = lane; s < NS; s += 32) {
+        const float2 v = WL[s * kMaxG + h2];
+        const float w = (v.x == -INFINITY) ? 0.0f : expf(v.x - mx);
+        WL[s * kMaxG + h2].x = w;  // (m, l) -> (weight, l)
+        l += w * v.y;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        ML[h2 * 2] = mx;
+        ML[h2 * 2 + 1] = l;
+      }
+    }
+    __syncthreads();
+  };
+  // One unit per CTA: a slot carries an exact-domain part (window / tail
+  // unit) or a transformed part (tile unit), never both.  The halves that
+  // matter are copied into shared memory with asynchronous copies issued
+  // together with the (m, l) loads: one round trip, no registers held.
+  constexpr int kStage = 18432;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  const bool staged = a.upc == 1 && 2 * NS * kMaxG * 4 + 4 * kMaxG * kD * 4 <= kStage &&
+                      kStage + NS * a.g * 512 <= AttnSmem::kQ;
+  if (staged) {
+    float4 *stg = reinterpret_cast<float4 *>(sm + kStage);
+    for (int idx = tid; idx < NS * a.g * 32; idx += blockDim.x) {
+      const int s = idx / (a.g * 32), r = idx - s * a.g * 32;
+      const float *src = part_row(a, row, s, r >> 5) + (s < n_exact ? kPartEx : kPartTr) + 4 * (r & 31);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(stg + idx)), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    slot_weights();
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    if (part < nparts)
+      for (int s = part; s < NS; s += nparts) {
+        const float4 v = stg[(s * a.g + hq) * 32 + c4];
+        const float w = WL[s * kMaxG + hq].x;
+        if (s < n_exact) {
+          ex.x = fmaf(w, v.x, ex.x); ex.y = fmaf(w, v.y, ex.y); ex.z = fmaf(w, v.z, ex.z); ex.w = fmaf(w, v.w, ex.w);
+        } else {
+          tr.x = fmaf(w, v.x, tr.x); tr.y = fmaf(w, v.y, tr.y); tr.z = fmaf(w, v.z, tr.z); tr.w = fmaf(w, v.w, tr.w);
+        }
+      }
+  }
+  for (int s0 = 0; s0 < (staged ? 0 : NS); s0 += UB * nparts) {
     float4 oe[UB], ot[UB];
 #pragma unroll
     for (int k = 0; k < UB; ++k) {
@@ -735,31 +791,7 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
       oe[k] = ok ? __ldcg(reinterpret_cast<const float4 *>(pr + kPartEx) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
       ot[k] = ok ? __ldcg(reinterpret_cast<const float4 *>(pr + kPartTr) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (s0 == 0) {
-      for (int i = tid; i < NS * a.g; i += blockDim.x) {
-        const int s = i / a.g, h2 = i - s * a.g;
-        WL[s * kMaxG + h2] = __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, s, h2)));
-      }
-      __syncthreads();
-      for (int h2 = warp; h2 < a.g; h2 += 8) {
-        float mx = -INFINITY;
-        for (int s = lane; s < NS; s += 32) mx = fmaxf(mx, WL[s * kMaxG + h2].x);
-        mx = warp_max(mx);
-        float l = 0.0f;
-        for (int s = lane; s < NS; s += 32) {
-          const float2 v = WL[s * kMaxG + h2];
-          const float w = (v.x == -INFINITY) ? 0.0f : expf(v.x - mx);
-          WL[s * kMaxG + h2].x = w;  // (m, l) -> (weight, l)
-          l += w * v.y;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-          ML[h2 * 2] = mx;
-          ML[h2 * 2 + 1] = l;
-        }
-      }
-      __syncthreads();
-    }
+    if (s0 == 0) slot_weights();
 #pragma unroll
     for (int k = 0; k < UB; ++k) {
       const int s = s0 + part + nparts * k;
