@@ -382,6 +382,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
     }
     l = warp_sum(l);
     __syncwarp();
+    KVR_TRACE_POINT(1, 2);
     float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
     for (int j = 0; j < TILE; ++j) {
@@ -403,6 +404,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
       ML[hq * 2] = mx;
       ML[hq * 2 + 1] = l;
     }
+    KVR_TRACE_POINT(1, 7);
   }
   __syncthreads();
   if (a.upc == 1 && a.slots > 1) {
