@@ -37,11 +37,11 @@ constexpr uint32_t kPfLboA = (kPfM / 8) * 128;  // 2048 B
 constexpr uint32_t kPfLboB = (kPfN / 8) * 128;  // 4096 B
 constexpr int kPfSmemA = kPfM * kD * 2;         // 32 KB per A block
 constexpr int kPfSmemB = kPfN * kD * 2;         // 64 KB
-constexpr int kPfStages = 4;                    // A ring depth
-constexpr int kPfOffA = kPfSmemB;
+constexpr int kPfStages = 3;                    // A ring depth
+constexpr int kPfOffA = 2 * kPfSmemB;           // two B buffers, then the A ring
 constexpr int kPfOffLut = kPfOffA + kPfStages * kPfSmemA;
 constexpr int kPfOffBar = kPfOffLut + 16 * 8;
-constexpr int kPfSmem = kPfOffBar + 8 * (2 * kPfStages + 4) + 16;
+constexpr int kPfSmem = kPfOffBar + 8 * (2 * kPfStages + 6) + 16;
 constexpr uint32_t kPfTmemCols = 2 * kPfN;      // double-buffered accumulator
 
 // sm100 shared-memory matrix descriptor, K-major, no swizzle
@@ -146,6 +146,7 @@ struct PrefillArgs {
   const unsigned char *qa;  // A blocks, (n_kv, nqb) x 32 KB
   int64_t nq, nqb;
   int n_kv;
+  int64_t ntg, qsplit, items;  // token groups of 256, query splits, work items
   const uint32_t *kbits;
   const uint16_t *kscale;
   int64_t nt_cap, n_tiles;
@@ -166,8 +167,6 @@ __device__ __forceinline__ bool pf_wait_or_abort(uint64_t *bar, unsigned phase, 
   }
   return false;
 }
-// B decoded: named barrier 1 over the 8 reader warps and the MMA warp
-__device__ __forceinline__ void pf_b_ready_sync() { asm volatile("bar.sync 1, 288;" ::: "memory"); }
 
 __device__ __forceinline__ void pf_mma_block(uint32_t tmem_d, uint32_t a_base, uint32_t b_base) {
 #pragma unroll
@@ -209,30 +208,78 @@ __device__ __forceinline__ float pf_max64(const uint32_t *r) {
   return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
-// Roles: warps 0-7 decode B, then read accumulators back (warp w: TMEM lanes
-// 32(w%4).., columns 128(w/4)..); warp 8 lane 0 issues the MMAs; warp 9 lane 0
-// streams the A blocks.  Barriers: afull[s] (copy landed), aempty[s] (MMAs
-// reading stage s done, via tcgen05.commit), done[b] (accumulator b ready),
-// tfree[b] (the 8 reader warps are through with accumulator b).
+// Work item w = (head h, token group tg, query split y): the 256 stored
+// tokens [256 tg, 256 tg + 256) of head h against query blocks y, y + qsplit,
+// ...  A persistent grid (one CTA per SM) walks items w = blockIdx.x,
+// blockIdx.x + gridDim.x, ...
+struct PfItem {
+  int h;
+  int64_t t0, qb0, nblk;  // first tile, first query block, query blocks
+};
+__device__ __forceinline__ PfItem pf_item(const PrefillArgs &a, int64_t w) {
+  PfItem it;
+  const int64_t y = w % a.qsplit, r = w / a.qsplit;
+  const int64_t tg = r % a.ntg;
+  it.h = (int)(r / a.ntg);
+  it.t0 = tg * (kPfN / kPfTile);
+  it.qb0 = y;
+  it.nblk = y < a.nqb ? (a.nqb - y + a.qsplit - 1) / a.qsplit : 0;
+  return it;
+}
+
+// Decodes the 256 tokens of an item into B (fp16 +-s in the MMA layout); one
+// token per reader thread (256 threads).
+__device__ __forceinline__ void pf_decode_b(const PrefillArgs &a, const PfItem &it, unsigned char *Bs,
+                                            const uint2 *lut, int tid) {
+  const int n = tid;
+  const int64_t tile = it.t0 + n / kPfTile;
+  const int j = n % kPfTile;
+  if (tile < a.n_tiles) {
+    const int64_t tix = (int64_t)it.h * a.nt_cap + tile;  // batch 1: store row = head
+    const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(a.kbits + (tix * kPfTile + j) * 4));
+    const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+    const uint4 *sc = reinterpret_cast<const uint4 *>(a.kscale + tix * kD);
+#pragma unroll
+    for (int kc = 0; kc < 16; ++kc) {
+      const uint32_t byte = (ww[kc >> 2] >> ((kc & 3) * 8)) & 0xffu;
+      const uint2 lo = lut[byte & 15u], hi = lut[byte >> 4];
+      const uint4 sv = __ldg(sc + kc);
+      *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) =
+          make_uint4(sv.x ^ lo.x, sv.y ^ lo.y, sv.z ^ hi.x, sv.w ^ hi.y);
+    }
+  } else {
+#pragma unroll
+    for (int kc = 0; kc < 16; ++kc)
+      *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  // generic-proxy writes -> visible to the tensor core (async proxy)
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Roles: warps 0-7 decode B operands and read accumulators back (warp w: TMEM
+// lanes 32(w%4).., columns 128(w/4)..); warp 8 lane 0 issues the MMAs; warp 9
+// lane 0 streams the A blocks.  A stages and accumulators are used round-
+// robin by a block counter that runs on across the CTA's items.  Barriers:
+// afull[s] (copy landed), aempty[s] (MMAs reading stage s done, via
+// tcgen05.commit), done[b] (accumulator b ready), tfree[b] (the 8 reader warps
+// are through with accumulator b), bfull[k] (B buffer k decoded; count 8).
+// A B buffer is rewritten only after the readers have seen every MMA of the
+// item that used it complete.
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillArgs a) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char *Bs = sm;                         // [16 kc][32 ng][8 r][16 B]
-  unsigned char *As = sm + kPfOffA;               // kPfStages x [16 kc][16 mg][8 r][16 B]
+  unsigned char *As = sm + kPfOffA;
   uint2 *lut = reinterpret_cast<uint2 *>(sm + kPfOffLut);  // nibble -> fp16 sign-flip masks
   uint64_t *afull = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
   uint64_t *aempty = afull + kPfStages;
   uint64_t *done = aempty + kPfStages;
   uint64_t *tfree = done + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+  uint64_t *bfull = tfree + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bfull + 2);
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int h = blockIdx.z;
-  const int64_t t0 = (int64_t)blockIdx.x * (kPfN / kPfTile);  // first tile of this CTA
-  const int64_t row = h;                                      // batch 1: store row = head
-  const int64_t qb0 = blockIdx.y, qstep = gridDim.y;
-  const int64_t nblk = qb0 < a.nqb ? (a.nqb - qb0 + qstep - 1) / qstep : 0;
-  const unsigned char *qa_h = a.qa + (int64_t)h * a.nqb * kPfSmemA;
+  const int64_t n_items = a.items;
+  const int64_t w0 = blockIdx.x, wstep = gridDim.x;
 
   if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -252,6 +299,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillAr
     for (int b = 0; b < 2; ++b) {
       mbar_init(&done[b], 1);
       mbar_init(&tfree[b], 8);
+      mbar_init(&bfull[b], 8);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -260,22 +308,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillAr
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 9) {
-    // ---- producer: A blocks through the ring
+    // ---- producer: the A blocks of every item through the ring
     int64_t last[kPfStages];
 #pragma unroll
     for (int s = 0; s < kPfStages; ++s) last[s] = -1;
     if (lane == 0) {
-      for (int64_t j = 0; j < nblk; ++j) {
-        if (*abort_s) break;
-        const int s = (int)(j % kPfStages);
-        if (j >= kPfStages && !pf_wait_or_abort(&aempty[s], (unsigned)((j / kPfStages - 1) & 1), abort_s)) {
-          atomicOr(a.err, 1u);
-          *abort_s = 1;
-          break;
+      int64_t j = 0;
+      for (int64_t w = w0; w < n_items && !*abort_s; w += wstep) {
+        const PfItem it = pf_item(a, w);
+        const unsigned char *qa_h = a.qa + (int64_t)it.h * a.nqb * kPfSmemA;
+        for (int64_t i = 0; i < it.nblk; ++i, ++j) {
+          if (*abort_s) break;
+          const int s = (int)(j % kPfStages);
+          if (j >= kPfStages && !pf_wait_or_abort(&aempty[s], (unsigned)((j / kPfStages - 1) & 1), abort_s)) {
+            atomicOr(a.err, 1u);
+            *abort_s = 1;
+            break;
+          }
+          mbar_expect_tx(&afull[s], kPfSmemA);
+          bulk_g2s(As + s * kPfSmemA, qa_h + (it.qb0 + i * a.qsplit) * kPfSmemA, kPfSmemA, &afull[s]);
+          last[s] = j;
         }
-        mbar_expect_tx(&afull[s], kPfSmemA);
-        bulk_g2s(As + s * kPfSmemA, qa_h + (qb0 + j * qstep) * kPfSmemA, kPfSmemA, &afull[s]);
-        last[s] = j;
       }
     }
     __syncwarp();
@@ -286,25 +339,34 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillAr
   } else if (warp == 8) {
     // ---- MMA issuer
     int64_t issued = 0;
-    pf_b_ready_sync();  // B decoded and visible to the async proxy
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (lane == 0) {
-      const uint32_t a_base = smem_u32(As), b_base = smem_u32(Bs);
-      for (int64_t i = 0; i < nblk; ++i) {
-        if (*abort_s) break;
-        const int s = (int)(i % kPfStages), b = (int)(i & 1);
-        bool ok = pf_wait_or_abort(&afull[s], (unsigned)((i / kPfStages) & 1), abort_s);
-        if (ok && i >= 2) ok = pf_wait_or_abort(&tfree[b], (unsigned)((i / 2 - 1) & 1), abort_s);
-        if (!ok) {
+      const uint32_t a_base = smem_u32(As), b_base0 = smem_u32(sm);
+      int64_t i = 0;  // block counter across items
+      int64_t k = 0;  // item counter of this CTA
+      for (int64_t w = w0; w < n_items && !*abort_s; w += wstep, ++k) {
+        const PfItem it = pf_item(a, w);
+        const int bb = (int)(k & 1);
+        if (!pf_wait_or_abort(&bfull[bb], (unsigned)((k >> 1) & 1), abort_s)) {
           atomicOr(a.err, 1u);
           *abort_s = 1;
           break;
         }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        pf_mma_block(tmem + (uint32_t)(b * kPfN), a_base + s * kPfSmemA, b_base);
-        pf_commit(&done[b]);
-        pf_commit(&aempty[s]);
-        issued = i + 1;
+        const uint32_t b_base = b_base0 + bb * kPfSmemB;
+        for (int64_t q = 0; q < it.nblk; ++q, ++i) {
+          const int s = (int)(i % kPfStages), b = (int)(i & 1);
+          bool ok = pf_wait_or_abort(&afull[s], (unsigned)((i / kPfStages) & 1), abort_s);
+          if (ok && i >= 2) ok = pf_wait_or_abort(&tfree[b], (unsigned)((i / 2 - 1) & 1), abort_s);
+          if (!ok) {
+            atomicOr(a.err, 1u);
+            *abort_s = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          pf_mma_block(tmem + (uint32_t)(b * kPfN), a_base + s * kPfSmemA, b_base);
+          pf_commit(&done[b]);
+          pf_commit(&aempty[s]);
+          issued = i + 1;
+        }
       }
       if (*abort_s && issued > 0)  // MMAs in flight must finish before TMEM is freed
         pf_wait(&done[(issued - 1) & 1], (unsigned)(((issued - 1) / 2) & 1));
@@ -312,63 +374,54 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_scores_kernel(PrefillAr
     __syncwarp();
     __syncthreads();
   } else {
-    // ---- B: 256 tokens x 128 channels, k_hat = +-s (fp16, exact); thread = token
-    {
-      const int n = tid;
-      const int64_t tile = t0 + n / kPfTile;
-      const int j = n % kPfTile;
-      if (tile < a.n_tiles) {
-        const int64_t tix = row * a.nt_cap + tile;
-        const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(a.kbits + (tix * kPfTile + j) * 4));
-        const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
-        const uint4 *sc = reinterpret_cast<const uint4 *>(a.kscale + tix * kD);
-#pragma unroll
-        for (int kc = 0; kc < 16; ++kc) {
-          const uint32_t byte = (ww[kc >> 2] >> ((kc & 3) * 8)) & 0xffu;
-          const uint2 lo = lut[byte & 15u], hi = lut[byte >> 4];
-          const uint4 sv = __ldg(sc + kc);
-          *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) =
-              make_uint4(sv.x ^ lo.x, sv.y ^ lo.y, sv.z ^ hi.x, sv.w ^ hi.y);
-        }
-      } else {
-#pragma unroll
-        for (int kc = 0; kc < 16; ++kc)
-          *reinterpret_cast<uint4 *>(Bs + kc * kPfLboB + (n >> 3) * 128 + (n & 7) * 16) =
-              make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    // generic-proxy smem writes -> visible to the tensor core (async proxy)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    pf_b_ready_sync();
-
-    // ---- readers
+    // ---- readers: decode B of item k+1 ahead, then read back item k
     const int quarter = warp & 3, half = warp >> 2;
-    const int nt_here = (int)(a.n_tiles - t0 < 4 ? a.n_tiles - t0 : 4);
-    for (int64_t i = 0; i < nblk; ++i) {
-      if (__shfl_sync(~0u, *abort_s, 0)) break;
-      const int b = (int)(i & 1);
-      if (!__all_sync(~0u, pf_wait_or_abort(&done[b], (unsigned)((i >> 1) & 1), abort_s))) {
-        if (lane == 0) atomicOr(a.err, 1u);
-        *abort_s = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      uint32_t r[128];
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kPfN + half * 128);
-      pf_tmem_ld32(taddr, r);
-      pf_tmem_ld32(taddr + 32, r + 32);
-      pf_tmem_ld32(taddr + 64, r + 64);
-      pf_tmem_ld32(taddr + 96, r + 96);
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    int64_t i = 0, k = 0;
+    bool stop = false;
+    if (w0 < n_items) {
+      pf_decode_b(a, pf_item(a, w0), sm, lut, tid);
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&tfree[b])) : "memory");
-      const float best0 = pf_max64(r), best1 = pf_max64(r + 64);
-      const int64_t qi = (qb0 + i * qstep) * kPfM + quarter * 32 + lane;
-      if (qi < a.nq) {
-        float *o = a.out + (qi * a.n_kv + h) * a.n_tiles + t0 + half * 2;
-        if (half * 2 < nt_here) o[0] = best0;
-        if (half * 2 + 1 < nt_here) o[1] = best1;
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bfull[0])) : "memory");
+    }
+    for (int64_t w = w0; w < n_items && !stop; w += wstep, ++k) {
+      const PfItem it = pf_item(a, w);
+      if (w + wstep < n_items) {  // next item's B into the other buffer: its last reader was item k-1
+        pf_decode_b(a, pf_item(a, w + wstep), sm + ((k + 1) & 1) * kPfSmemB, lut, tid);
+        __syncwarp();
+        if (lane == 0)
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bfull[(k + 1) & 1])) : "memory");
+      }
+      const int nt_here = (int)(a.n_tiles - it.t0 < 4 ? a.n_tiles - it.t0 : 4);
+      for (int64_t q = 0; q < it.nblk; ++q, ++i) {
+        if (__shfl_sync(~0u, *abort_s, 0)) {
+          stop = true;
+          break;
+        }
+        const int b = (int)(i & 1);
+        if (!__all_sync(~0u, pf_wait_or_abort(&done[b], (unsigned)((i >> 1) & 1), abort_s))) {
+          if (lane == 0) atomicOr(a.err, 1u);
+          *abort_s = 1;
+          stop = true;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint32_t r[128];
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * kPfN + half * 128);
+        pf_tmem_ld32(taddr, r);
+        pf_tmem_ld32(taddr + 32, r + 32);
+        pf_tmem_ld32(taddr + 64, r + 64);
+        pf_tmem_ld32(taddr + 96, r + 96);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&tfree[b])) : "memory");
+        const float best0 = pf_max64(r), best1 = pf_max64(r + 64);
+        const int64_t qi = (it.qb0 + q * a.qsplit) * kPfM + quarter * 32 + lane;
+        if (qi < a.nq) {
+          float *o = a.out + (qi * a.n_kv + it.h) * a.n_tiles + it.t0 + half * 2;
+          if (half * 2 < nt_here) o[0] = best0;
+          if (half * 2 + 1 < nt_here) o[1] = best1;
+        }
       }
     }
     __syncthreads();
@@ -420,7 +473,14 @@ extern "C" int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, in
   else prefill_qprep_kernel<KVR_BF16><<<qgrid, 256, 0, st>>>(q, nq, n_q, n_kv, kind, nqb, qa);
   int rc = check_launch("kvr_sd1_prefill_scores (q prep)");
   if (rc) return rc;
-  PrefillArgs a{qa, nq, nqb, n_kv, kbits, kscale, nt_cap, n_tiles, scores, reinterpret_cast<unsigned *>(p)};
+  // work items: (head, 256-token group, query split); query blocks are split
+  // only when the items alone would leave SMs idle (each split re-decodes B)
+  const int64_t ntg = (n_tiles + 3) / 4;
+  int64_t qsplit = (148 + ntg * n_kv - 1) / (ntg * n_kv);
+  qsplit = qsplit < 1 ? 1 : (qsplit > nqb ? nqb : qsplit);
+  const int64_t items = ntg * n_kv * qsplit;
+  PrefillArgs a{qa, nq, nqb, n_kv, ntg, qsplit, items, kbits, kscale, nt_cap, n_tiles, scores,
+                reinterpret_cast<unsigned *>(p)};
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -428,13 +488,9 @@ extern "C" int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, in
     cudaFuncSetAttribute(prefill_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
     set_dev = dev;
   }
-  // one CTA per (256 tokens, head); split the query blocks over grid.y only
-  // when that alone leaves SMs idle (each split re-decodes its B)
-  const int64_t base = ((n_tiles + 3) / 4) * n_kv;
-  int64_t gy = (2 * 148 + base - 1) / base;
-  gy = gy < 1 ? 1 : (gy > nqb ? nqb : gy);
-  gy = gy > 65535 ? 65535 : gy;
-  dim3 grid((unsigned)((n_tiles + 3) / 4), (unsigned)gy, (unsigned)n_kv);
-  prefill_scores_kernel<<<grid, kPfThreads, kPfSmem, st>>>(a);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = items < sms ? items : sms;  // persistent: one CTA per SM
+  prefill_scores_kernel<<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(a);
   return check_launch("kvr_sd1_prefill_scores");
 }
