@@ -651,6 +651,7 @@ __device__ void finalize_group(const AttnArgs &a, unsigned char *sm, int64_t b, 
 #pragma unroll
       for (int s = 0; s < 4; ++s) x[s] = Tr[hq * kD + lane + 32 * s];
       dct128_inv_shfl(x, lane, lee);
+      KVR_TRACE_POINT(3, 3);
       const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
       const float M = ML[hq * 2], L = ML[hq * 2 + 1];
       if (a.partial_out) {
@@ -770,8 +771,10 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     slot_weights();
+    KVR_TRACE_POINT(3, 0);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+    KVR_TRACE_POINT(3, 1);
     if (part < nparts)
       for (int s = part; s < NS; s += nparts) {
         const float4 v = stg[(s * a.g + hq) * 32 + c4];
