@@ -729,11 +729,15 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
   const int hq = p >> 5, c4 = p & 31;
   float4 ex = make_float4(0.f, 0.f, 0.f, 0.f), tr = ex;
   // (m, l) of every slot -> per-head weights exp(m - M) and the merged (M, L)
-  auto slot_weights = [&]() {
+  auto slot_ml_loads = [&]() {
     for (int i = tid; i < NS * a.g; i += blockDim.x) {
       const int s = i / a.g, h2 = i - s * a.g;
       WL[s * kMaxG + h2] = __ldcg(reinterpret_cast<const float2 *>(part_row(a, row, s, h2)));
     }
+  };
+  bool ml_loaded = false;
+  auto slot_weights = [&]() {
+    if (!ml_loaded) slot_ml_loads();
     __syncthreads();
     for (int h2 = warp; h2 < a.g; h2 += 8) {
       float mx = -INFINITY;
@@ -763,6 +767,9 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
   const bool staged = a.upc == 1 && 2 * NS * kMaxG * 4 + 4 * kMaxG * kD * 4 <= kStage &&
                       kStage + NS * a.g * 512 <= AttnSmem::kQ;
   if (staged) {
+    // the (m, l) pairs first: the weights are formed while the bulk halves travel
+    slot_ml_loads();
+    ml_loaded = true;
     float4 *stg = reinterpret_cast<float4 *>(sm + kStage);
     for (int idx = tid; idx < NS * a.g * 32; idx += blockDim.x) {
       const int s = idx / (a.g * 32), r = idx - s * a.g * 32;
