@@ -280,7 +280,9 @@ __device__ int32_t rank_select(const AttnArgs &a, unsigned char *sm, int64_t row
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
       sc[i] = (i >= a.rank_ex0 && i < a.rank_ex1) ? -INFINITY : __ldcg(src + i);
     __syncthreads();
+    KVR_TRACE_POINT(3, 4);
     const unsigned long long key = block_kth_largest<256>([&](int64_t i) -> float { return sc[i]; }, n, slot + 1, ts);
+    KVR_TRACE_POINT(3, 5);
     t = (int32_t)key_index(key);
     __syncthreads();  // the region is reused for the unit's copies
   }
@@ -307,6 +309,7 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = b * a.n_kv + h;
   griddep_wait();  // sel (or the scores) and qprime come from the selection kernel
+  KVR_TRACE_POINT(3, 6);
   const int32_t t = a.rank_scores != nullptr ? rank_select(a, sm, row, slot) : a.sel[row * a.k_sel + slot];
   if (t < 0) return;  // empty slot: nothing to fold
   const int64_t tix = row * a.nt_cap + t;
