@@ -74,6 +74,9 @@ class KVRHook:
         self.transform = kwargs.get("transform", "hadamard")
         self.use_attractors = kwargs.get("attractors", True)
         self.reference_eviction_rope = kwargs.get("reference_eviction_rope", False)
+        # sd1: encode each layer's evicted prefix inside its projection hook
+        # during the prefill forward (no fp32 K/V capture of the prompt)
+        self.fused_prefill = kwargs.get("fused_prefill", True)
         self._context_len = 0
         self._prefill_done = False
         self._hooks = []
@@ -131,6 +134,8 @@ class KVRHook:
         """kvr_hook.py:85-134: one HF forward with capture hooks on k/v
         projections; the window keeps the last `window` tokens, the index the
         evicted prefix (calibrated on the whole prompt)."""
+        if self.codec == "sd1" and self.fused_prefill:
+            return self._prefill_sd1_fused(input_ids)
         n_prompt = input_ids.shape[1]
         cap_k, cap_v, hooks = {}, {}, []
         for li in range(self.n_layers):
@@ -161,6 +166,45 @@ class KVRHook:
                 ret.batch_append(cap_k[li][:n_ret], cap_v[li][:n_ret])
                 if self.use_attractors:
                     ret.build_attractors()
+            self._retrieval_built = True
+
+    def _prefill_sd1_fused(self, input_ids):
+        """prefill for codec='sd1' with the stores built inside the forward:
+        each layer's k/v projection hook writes the last `window` tokens
+        (post-RoPE) into the window ring and encodes the evicted prefix into
+        the 1-bit store straight from the projection output (RoPE applied in
+        the encoder).  Same stores as the capture path of `prefill` (the sd1
+        index needs no whole-prompt calibration), without holding fp32 copies
+        of every layer's K/V for the whole prompt."""
+        n = input_ids.shape[1]
+        hooks = []
+        for li in range(self.n_layers):
+            attn = self.model.model.layers[li].self_attn
+
+            def hook_fn(mod, args, kwargs, output, li=li):
+                hidden = kwargs["hidden_states"] if "hidden_states" in kwargs else args[0]
+                k = mod.k_proj(hidden).view(-1, self.n_kv, self.d_head)
+                v = mod.v_proj(hidden).view(-1, self.n_kv, self.d_head)
+                win = self.windows[li]
+                m = min(n, win.cap)
+                win.pos = n - m  # the ring holds the last m tokens in the slots a full write leaves them in
+                win.batch_append(self._rotate(k[n - m:].float(), n - m), v[n - m:].float())
+                ret = self.retrievals[li]
+                ret.set_rotary_tables(self.cos_tbl, self.sin_tbl)
+                if n > self.window_size:
+                    n_ret = n - self.window_size
+                    ret.calibrate(k)
+                    ret.batch_append(k[:n_ret], v[:n_ret])
+
+            hooks.append(attn.register_forward_hook(hook_fn, with_kwargs=True))
+        try:
+            self.model(input_ids, logits_to_keep=1)
+        finally:
+            for h in hooks:
+                h.remove()
+        self._context_len = n
+        self._prefill_done = True
+        if n > self.window_size:
             self._retrieval_built = True
 
     def _update_stores(self, li, k_pre, v_val, k_post):

@@ -424,8 +424,8 @@ class RetrievalIndex:
 
     def _tail_put(self, k_pre, v, pos0):
         m = k_pre.shape[0]
-        self.tail_k[0, self.n_tail:self.n_tail + m] = self._rope_post(k_pre, pos0 + self.n_tail).half()
-        self.tail_v[0, self.n_tail:self.n_tail + m] = v.half()
+        self.tail_k[0, self.n_tail:self.n_tail + m] = self._rope_post(k_pre.float(), pos0 + self.n_tail).half()
+        self.tail_v[0, self.n_tail:self.n_tail + m] = v.float().half()
         self.n_tail += m
         if self.n_tail == self.tile:
             if self.store.n_tiles + 1 > self.store.nt_cap:

@@ -88,3 +88,34 @@ def test_hook_path_runs():
         out = m(torch.cat([prompt, prompt[:, :1]], 1)).logits
     hook.remove()
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("n_prompt", [300, 90])
+def test_sd1_fused_prefill_builds_the_same_stores(n_prompt):
+    """The sd1 prefill that encodes inside the projection hooks (no fp32
+    capture of the prompt) leaves exactly the window rings and 1-bit stores
+    of the capture-then-encode path (ragged tail included)."""
+    from kvr_b200 import KVRHook
+    m = tiny_llama(layers=2)
+    prompt = torch.randint(0, 500, (1, n_prompt), device=DEV)
+    hooks = []
+    for fused in (False, True):
+        h = KVRHook(m, window_size=128, top_k=64, codec="sd1", transform="dct", attractors=False,
+                    fused_prefill=fused, num_denoise_steps=0)
+        h.prefill(prompt)
+        hooks.append(h)
+    a, b = hooks
+    assert a._retrieval_built == b._retrieval_built and a._context_len == b._context_len == n_prompt
+    for li in range(2):
+        wa, wb = a.windows[li], b.windows[li]
+        assert (wa.pos, wa.n) == (wb.pos, wb.n)
+        assert torch.equal(wa.k, wb.k) and torch.equal(wa.v, wb.v)
+        ra, rb = a.retrievals[li], b.retrievals[li]
+        assert (ra.n_stored, ra.n_tail) == (rb.n_stored, rb.n_tail)
+        if ra.n_stored:
+            nt = ra.store.n_tiles
+            assert nt == rb.store.n_tiles and nt > 0
+            for name in ("kbits", "kscale", "vbits", "vscale"):
+                assert torch.equal(getattr(ra.store, name)[:, :, :nt], getattr(rb.store, name)[:, :, :nt]), name
+            assert torch.equal(ra.tail_k[:, :ra.n_tail], rb.tail_k[:, :rb.n_tail])
+            assert torch.equal(ra.tail_v[:, :ra.n_tail], rb.tail_v[:, :rb.n_tail])
