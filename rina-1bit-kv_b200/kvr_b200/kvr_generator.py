@@ -50,6 +50,18 @@ class KVRGenerator:
         self._step_count = 0
         self._is_first = True
 
+    def save_cache(self, path):
+        """Saves the compressed KV state (KVRHook.save_cache) and this
+        generator's step counters, so that decoding can resume later."""
+        self.kvr.save_cache(path, extra={"is_first": self._is_first, "step_count": self._step_count,
+                                         "generated_ids": [int(i) for i in self._generated_ids]})
+
+    def load_cache(self, path):
+        extra = self.kvr.load_cache(path) or {}
+        self._is_first = bool(extra.get("is_first", False))
+        self._step_count = int(extra.get("step_count", 0))
+        self._generated_ids = list(extra.get("generated_ids", []))
+
     @torch.no_grad()
     def logits_step(self, token_id):
         """One incremental forward pass; returns the (vocab,) fp32 logits."""

@@ -207,6 +207,45 @@ class KVRHook:
         if n > self.window_size:
             self._retrieval_built = True
 
+    # ------------------------------------------------------- save / load --
+    def save_cache(self, path, extra=None):
+        """Writes every layer's window and packed index plus the decode
+        counters to `path` (kvr_b200.cache_io container); `extra` (a JSON
+        value) is stored alongside and returned by load_cache."""
+        from .cache_io import write_cache
+
+        meta = {"n_layers": self.n_layers, "n_kv": self.n_kv, "d_head": self.d_head,
+                "window_size": self.window_size, "codec": self.codec, "tile": self.tile,
+                "transform": self.transform, "context_len": self._context_len, "step": self._step,
+                "retrieval_built": self._retrieval_built, "prefill_done": self._prefill_done, "layers": [],
+                "extra": extra}
+        tensors = {}
+        for li in range(self.n_layers):
+            wm, wt = self.windows[li].state_dict(f"L{li}.win.")
+            rm, rt = self.retrievals[li].state_dict(f"L{li}.ret.")
+            meta["layers"].append({"window": wm, "index": rm})
+            tensors.update(wt)
+            tensors.update(rt)
+        write_cache(path, meta, tensors)
+
+    def load_cache(self, path):
+        """Restores a cache written by save_cache for the same model shape,
+        window size and codec; decoding continues where it stopped."""
+        from .cache_io import read_cache
+
+        meta, tensors = read_cache(path)
+        for key, mine in (("n_layers", self.n_layers), ("n_kv", self.n_kv), ("d_head", self.d_head),
+                          ("window_size", self.window_size), ("codec", self.codec)):
+            if meta[key] != mine:
+                raise ValueError(f"cache {key}={meta[key]!r} does not match this hook ({mine!r})")
+        for li in range(self.n_layers):
+            self.windows[li].load_state_dict(meta["layers"][li]["window"], tensors, f"L{li}.win.")
+            self.retrievals[li].load_state_dict(meta["layers"][li]["index"], tensors, f"L{li}.ret.")
+            self.retrievals[li].set_rotary_tables(self.cos_tbl, self.sin_tbl)
+        self._context_len, self._step = int(meta["context_len"]), int(meta["step"])
+        self._retrieval_built, self._prefill_done = bool(meta["retrieval_built"]), bool(meta["prefill_done"])
+        return meta.get("extra")
+
     def _update_stores(self, li, k_pre, v_val, k_post):
         """kvr_hook.py:136-148: on a full window, move the slot about to be
         overwritten into the index, then append the new token."""

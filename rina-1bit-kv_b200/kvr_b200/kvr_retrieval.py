@@ -377,6 +377,69 @@ class RetrievalIndex:
         if self.codec != "int4w":
             raise NotImplementedError(f"{what} is defined for codec='int4w' only")
 
+    # ------------------------------------------------------- save / load --
+    _INT4W_TENSORS = ("k_scales", "vr_scales", "W", "K_mean", "V_mean", "attractors", "labels")
+
+    def state_dict(self, prefix=""):
+        """(meta, tensors) for kvr_b200.cache_io: the packed store and its
+        counters.  RoPE tables are not part of it (set_rotary_tables again
+        after loading; KVRHook does)."""
+        meta = {"codec": self.codec, "n_kv": self.n_kv, "d_head": self.d_head, "top_k": self.top_k,
+                "chunk_size": self.chunk_size, "tile": self.tile, "transform": self.transform,
+                "n_stored": self.n_stored, "n_tail": self.n_tail, "calibrated": self.k_scales is not None}
+        t = {}
+        if self.codec == "int4w":
+            for name in self._INT4W_TENSORS:
+                v = getattr(self, name)
+                if v is not None:
+                    t[prefix + name] = v
+            if self.k_packed is not None:
+                t[prefix + "k_packed"] = self.k_packed[:self.n_stored]
+            if self.vr_packed is not None:
+                t[prefix + "vr_packed"] = self.vr_packed[:self.n_stored]
+        elif self.store is not None:
+            nt = self.store.n_tiles
+            meta["n_tiles"] = nt
+            for name in ("kbits", "kscale", "vbits", "vscale"):
+                t[prefix + name] = getattr(self.store, name)[:, :, :nt]
+            t[prefix + "tail_k"] = self.tail_k[:, :self.n_tail]
+            t[prefix + "tail_v"] = self.tail_v[:, :self.n_tail]
+        return meta, t
+
+    def load_state_dict(self, meta, tensors, prefix=""):
+        for key in ("codec", "n_kv", "d_head", "tile", "transform"):
+            if meta[key] != getattr(self, key):
+                raise ValueError(f"cache {key}={meta[key]!r} does not match this index ({getattr(self, key)!r})")
+        self.top_k, self.chunk_size = meta["top_k"], meta["chunk_size"]
+        dev = self.device
+        if self.codec == "sd1":
+            self._sd1_reset()  # fresh buffers (clears the counters), filled below
+            self.attractors = self.labels = None
+            self.k_scales = (torch.ones(self.n_kv, self.d_head, device=dev)  # marks "calibrated"
+                             if meta.get("calibrated", self.n_stored > 0) else None)
+        self.n_stored, self.n_tail = int(meta["n_stored"]), int(meta["n_tail"])
+        if self.codec == "int4w":
+            for name in self._INT4W_TENSORS:
+                setattr(self, name, tensors[prefix + name].to(dev) if prefix + name in tensors else None)
+            n = self.n_stored
+            for name in ("k_packed", "vr_packed"):
+                if prefix + name in tensors:
+                    src = tensors[prefix + name].to(dev)
+                    buf = torch.zeros(n + max(1024, n // 2), *src.shape[1:], dtype=src.dtype, device=dev)
+                    buf[:n] = src
+                    setattr(self, name, buf)
+                else:
+                    setattr(self, name, None)
+            return
+        if "n_tiles" in meta:
+            nt = int(meta["n_tiles"])
+            self.store.grow(max(64, 2 * nt))
+            for name in ("kbits", "kscale", "vbits", "vscale"):
+                getattr(self.store, name)[:, :, :nt] = tensors[prefix + name].to(dev)
+            self.store.n_tiles = nt
+            self.tail_k[:, :self.n_tail] = tensors[prefix + "tail_k"].to(dev)
+            self.tail_v[:, :self.n_tail] = tensors[prefix + "tail_v"].to(dev)
+
     # --------------------------------------------------------------- sd1 --
     def _sd1_reset(self):
         self.store = K.Sd1Store(1, self.n_kv, 64, self.tile, self.transform, self.device)

@@ -28,6 +28,20 @@ class WindowBuffer:
         self.pos += 1
         self.n = min(self.n + 1, self.cap)
 
+    # ------------------------------------------------------- save / load --
+    def state_dict(self, prefix=""):
+        """(meta, tensors) for kvr_b200.cache_io: the fp16 rings and counters."""
+        return ({"cap": self.cap, "pos": self.pos, "n": self.n, "n_kv": self.n_kv, "d_head": self.d_head},
+                {prefix + "k": self.k, prefix + "v": self.v})
+
+    def load_state_dict(self, meta, tensors, prefix=""):
+        if (meta["cap"], meta["n_kv"], meta["d_head"]) != (self.cap, self.n_kv, self.d_head):
+            raise ValueError(f"window shape {(meta['cap'], meta['n_kv'], meta['d_head'])} does not match "
+                             f"{(self.cap, self.n_kv, self.d_head)}")
+        self.k.copy_(tensors[prefix + "k"])
+        self.v.copy_(tensors[prefix + "v"])
+        self.pos, self.n = int(meta["pos"]), int(meta["n"])
+
     @torch.no_grad()
     def batch_append(self, k_all, v_all):
         """kvr_window.py:27-41: token i lands in slot (pos + i) % cap."""

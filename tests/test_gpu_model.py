@@ -119,3 +119,23 @@ def test_sd1_fused_prefill_builds_the_same_stores(n_prompt):
                 assert torch.equal(getattr(ra.store, name)[:, :, :nt], getattr(rb.store, name)[:, :, :nt]), name
             assert torch.equal(ra.tail_k[:, :ra.n_tail], rb.tail_k[:, :rb.n_tail])
             assert torch.equal(ra.tail_v[:, :ra.n_tail], rb.tail_v[:, :rb.n_tail])
+
+
+@pytest.mark.parametrize("codec", ["int4w", "sd1"])
+def test_save_and_resume_decoding(codec, tmp_path):
+    """save_cache / load_cache: a fresh generator that loads the compressed
+    state continues with exactly the logits of the one that saved it."""
+    from kvr_b200 import KVRGenerator
+    m = tiny_llama()
+    prompt = torch.randint(0, 500, (1, 300), device=DEV)
+    gen = KVRGenerator(m, window_size=128, top_k=128, codec=codec, transform="dct", attractors=False)
+    gen.prefill(prompt)
+    gen.step(prompt[0, -1])
+    gen.step(torch.tensor(5, device=DEV))
+    path = tmp_path / f"{codec}.kvrc"
+    gen.save_cache(path)
+    gen2 = KVRGenerator(m, window_size=128, top_k=128, codec=codec, transform="dct", attractors=False)
+    gen2.load_cache(path)
+    x = torch.tensor(11, device=DEV)
+    assert torch.equal(gen.logits_step(x), gen2.logits_step(x))
+    assert gen.kvr._context_len == gen2.kvr._context_len
