@@ -245,6 +245,16 @@ KVR_API int kvr_sd1_prefill_scores(const void *q, int q_dtype, int64_t nq, int n
                                    const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
                                    float *scores, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
+/* k-means on the device for the int4w attractor branch (replaces the host
+ * MiniBatchKMeans of modules/kvr_retrieval.py:234-246; the reference's basins
+ * are then used by retrieve_topk, :332-367).  x (n, d) fp32, d = 128,
+ * 1 <= k <= 256, n >= k.  Deterministic Lloyd iterations: centroid j starts at
+ * point floor(j n / k); `iters` updates; labels (n) int32 from a final
+ * assignment (lowest index on ties); centroids (k, d) fp32. */
+KVR_API size_t kvr_kmeans_workspace_bytes(int64_t n, int k);
+KVR_API int kvr_kmeans(const float *x, int64_t n, int d, int k, int iters, float *centroids, int32_t *labels,
+                       void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
 /* Partial-attention merge for a sequence split across P sources:
  * partials (P, n_q, d + 2) fp32 rows = [m, l, o_0 .. o_{d-1}] with o
  * unnormalised (sum_j e^{s_j - m} v_j); out (n_q, d) = sum_p e^{m_p-M} o_p / sum_p e^{m_p-M} l_p. */

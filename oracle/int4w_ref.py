@@ -370,3 +370,30 @@ def window_ring_write(ring_k, ring_v, pos, k_new, v_new):
         ring_k[slot] = k_new[i].astype(np.float16)
         ring_v[slot] = v_new[i].astype(np.float16)
     return pos + k_new.shape[0]
+
+
+def kmeans_lloyd(x, k, iters):
+    """Specification of the device k-means that replaces the reference's host
+    MiniBatchKMeans (modules/kvr_retrieval.py:234-246; not a restatement of
+    it: sklearn's mini-batch algorithm is version-dependent).  x (n, d)
+    float32.  centroid j starts at x[j*n//k]; each iteration assigns every
+    point to argmin_j ||c_j||^2 - 2 x.c_j (lowest j on ties) and moves each
+    non-empty cluster's centroid to the mean of its points; a final assignment
+    gives the labels.  Returns (labels int64, centroids float32), float64
+    arithmetic (the device accumulates in fp32: compare labels on separated
+    data, centroids with a tolerance)."""
+    x = np.asarray(x, np.float64)
+    n = x.shape[0]
+    c = x[(np.arange(k) * n) // k].copy()
+
+    def assign(c):
+        d = (c * c).sum(1)[None, :] - 2.0 * x @ c.T
+        return d.argmin(1)
+
+    for _ in range(iters):
+        lab = assign(c)
+        for j in range(k):
+            m = lab == j
+            if m.any():
+                c[j] = x[m].mean(0)
+    return assign(c).astype(np.int64), c.astype(np.float32)

@@ -63,6 +63,8 @@ SIGNATURES = {
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),
     "kvr_sd1_prefill_workspace_bytes": (SZ, [I64, I]),
     "kvr_sd1_prefill_scores": (I, [P, I, I64, I, I, P, P, I64, I64, I, I, P, P, SZ, P]),
+    "kvr_kmeans_workspace_bytes": (SZ, [I64, I]),
+    "kvr_kmeans": (I, [P, I64, I, I, I, P, P, P, SZ, P]),
     "kvr_workspace_status": (I, [P, P]),
     "kvr_decode_attn_noalloc_max_scratch_bytes": (SZ, []),
     "kvr_decode_attn_noalloc": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, F, P, I, P]),

@@ -360,6 +360,18 @@ def sd1_prefill_scores(store: Sd1Store, q):
     return out
 
 
+def kmeans(x, k=128, iters=10):
+    """Deterministic Lloyd k-means on the device: x (n, 128) -> (labels (n,)
+    int64, centroids (k, 128) fp32)."""
+    x = _c(x.float())
+    n = x.shape[0]
+    c = torch.empty(k, D, dtype=torch.float32, device=x.device)
+    lab = torch.empty(n, dtype=torch.int32, device=x.device)
+    ws = N.workspace("kmeans", call("kvr_kmeans_workspace_bytes", n, k), x.device)
+    call("kvr_kmeans", ptr(x), n, D, k, iters, ptr(c), ptr(lab), ptr(ws), ws.numel(), stream())
+    return lab.long(), c
+
+
 def workspace_status(ws: torch.Tensor):
     call("kvr_workspace_status", ptr(ws), stream())
 

@@ -239,20 +239,19 @@ class RetrievalIndex:
         return K.int4w_chunk_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, self.n_stored, cs, he).t()
 
     @torch.no_grad()
-    def build_attractors(self):
-        """kvr_retrieval.py:234-246: host-side MiniBatchKMeans on head-0 K
-        (sklearn; parity unpinned).  Kept for API compatibility."""
+    def build_attractors(self, iters=10):
+        """kvr_retrieval.py:234-246: 128 basins of head-0 K_pre.  The reference
+        clusters on the host with sklearn's MiniBatchKMeans (seed 42); here the
+        clustering is a deterministic Lloyd k-means on the device
+        (kernels.kmeans, kvr_cluster.cu) — same role and output shapes, not
+        the same basins (sklearn's mini-batch result is version-dependent, so
+        the branch was never pinned)."""
         if self.codec != "int4w":
             return
-        from sklearn.cluster import MiniBatchKMeans
-
         nr = self.n_stored
         if nr < self.n_attractors * 2:
             return
-        kp = self._deq_k(0).float().cpu().numpy()
-        kmeans = MiniBatchKMeans(n_clusters=self.n_attractors, random_state=42, batch_size=min(1024, nr), n_init=1)
-        self.labels = torch.from_numpy(kmeans.fit_predict(kp)).to(self.device)
-        self.attractors = torch.from_numpy(kmeans.cluster_centers_.astype(np.float32)).to(self.device)
+        self.labels, self.attractors = K.kmeans(self._deq_k(0).float(), self.n_attractors, iters)
 
     @torch.no_grad()
     def compute_attractor_scores(self, q_post_rope):
