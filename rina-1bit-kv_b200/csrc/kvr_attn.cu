@@ -64,7 +64,7 @@ struct AttnArgs {
   int units;  // work units per (b, h)
   int upc;    // units per CTA
   int slots;  // CTAs per (b, h) = ceil(units / upc)
-  int pipelined;  // several units per CTA over fp16 exact data: cp.async double buffering
+  int pipelined;  // batched rows over fp16 exact data: attn_rows_kernel
 };
 
 // ---- runtime-dtype loads
@@ -86,8 +86,10 @@ struct AttnSmem {
   static constexpr int kVS = kKS + kD * 2;                           // fp16 [128]
   static constexpr int kLUT = kVS + kD * 2;                          // fp32 [g][32][16]
   static constexpr int kTileEnd = kLUT + kMaxG * 32 * 16 * 4;
-  static constexpr int kRawRow = kD * 2 + 16;                         // padded fp16 row (272 B)
-  static constexpr int kRawBuf = 2 * kChunk * kRawRow;                // K + V rows of one chunk (pipelined)
+  // the unit region also hosts the batched-decode staging (RowSmem); its size
+  // is kept at two 64-row K + V chunks of padded fp16 rows
+  static constexpr int kRawRow = kD * 2 + 16;
+  static constexpr int kRawBuf = 2 * kChunk * kRawRow;
   static constexpr int kUnion0 = kExactEnd > kTileEnd ? kExactEnd : kTileEnd;
   static constexpr int kUnion = kUnion0 > 2 * kRawBuf ? kUnion0 : 2 * kRawBuf;
   static constexpr int kQ = kUnion;                                  // fp32 [8][128]
@@ -103,15 +105,7 @@ struct AttnSmem {
   static constexpr int kAccEx = kAccSC + kMaxG * 2 * 4;               // fp32 [8][128] exact part
   static constexpr int kAccTr = kAccEx + kMaxG * kD * 4;              // fp32 [8][128] transformed part
   static constexpr int kTotal = kAccTr + kMaxG * kD * 4;
-  // pipelined mode (several units per CTA, fp16 exact data): two raw staging
-  // buffers alias the unit region above; LUT and q' get their own space
-  static constexpr int kRaw0 = 0;
-  static constexpr int kRaw1 = kRawBuf;
-  static constexpr int kPipeQp = kTotal;                              // fp32 [8][128] q' * inv_scale
-  static constexpr int kPipeLUT2 = kPipeQp + kMaxG * kD * 4;          // fp32 [8][32][16]
-  static constexpr int kPipeTotal = kPipeLUT2 + kMaxG * 32 * 16 * 4;
 };
-static_assert(2 * AttnSmem::kRawBuf <= AttnSmem::kQ, "raw buffers must stay inside the unit region");
 
 // Softmax over the scores S[hq][0..nt) of every query head; writes P[j][hq],
 // ML[hq] = (m, l).  Rows with no valid token get m = -inf, l = 0.
@@ -426,219 +420,6 @@ __device__ void tile_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int h
   fold_unit(a, sm, true);
 }
 
-// ------------------------------------------------------------ pipelined ----
-
-// Issues the copies of unit u into raw buffer `buf` (no wait).
-template <int TILE>
-__device__ void pipe_issue(const AttnArgs &a, unsigned char *buf, int64_t b, int h, int u) {
-  const int tid = threadIdx.x;
-  const int n_exact = a.nchunk[0] + a.nchunk[1];
-  if (u < n_exact) {
-    const int seg = u < a.nchunk[0] ? 0 : 1;
-    const int chunk = seg == 0 ? u : u - a.nchunk[0];
-    const int64_t t0 = (int64_t)chunk * kChunk;
-    const int nt = (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk);
-    const uint16_t *kp = reinterpret_cast<const uint16_t *>(a.k[seg]);
-    const uint16_t *vp = reinterpret_cast<const uint16_t *>(a.v[seg]);
-    const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD;
-    for (int i = tid; i < 2 * nt * 16; i += blockDim.x) {
-      const int kv = i / (nt * 16), r = i - kv * nt * 16, j = r >> 4, c = r & 15;
-      const uint16_t *src = (kv == 0 ? kp : vp) + base + (t0 + j) * a.tok_stride[seg] + c * 8;
-      cp_async16(buf + kv * kChunk * AttnSmem::kRawRow + j * AttnSmem::kRawRow + c * 16, src);
-    }
-  } else {
-    griddep_wait();  // the selection comes from the preceding kernel
-    const int64_t row = b * a.n_kv + h;
-    const int32_t t = a.sel[row * a.k_sel + (u - n_exact)];
-    if (t < 0) return;
-    const int64_t tix = row * a.nt_cap + t;
-    constexpr int kBitChunks = TILE;  // TILE * 16 bytes
-    const unsigned char *kb = reinterpret_cast<const unsigned char *>(a.kbits + tix * TILE * 4);
-    const unsigned char *vb = reinterpret_cast<const unsigned char *>(a.vbits + tix * TILE * 4);
-    const unsigned char *ks = reinterpret_cast<const unsigned char *>(a.kscale + tix * kD);
-    const unsigned char *vs = reinterpret_cast<const unsigned char *>(a.vscale + tix * kD);
-    for (int i = tid; i < 2 * kBitChunks + 32; i += blockDim.x) {
-      if (i < kBitChunks) cp_async16(buf + i * 16, kb + i * 16);
-      else if (i < 2 * kBitChunks) cp_async16(buf + 2048 + (i - kBitChunks) * 16, vb + (i - kBitChunks) * 16);
-      else if (i < 2 * kBitChunks + 16) cp_async16(buf + 4096 + (i - 2 * kBitChunks) * 16, ks + (i - 2 * kBitChunks) * 16);
-      else cp_async16(buf + 4352 + (i - 2 * kBitChunks - 16) * 16, vs + (i - 2 * kBitChunks - 16) * 16);
-    }
-  }
-}
-
-// Exact unit from the raw fp16 buffer (rows of kRawRow bytes).
-__device__ void pipe_exact(const AttnArgs &a, unsigned char *sm, const unsigned char *buf, int nt) {
-  const float *Qs = reinterpret_cast<const float *>(sm + AttnSmem::kQ);
-  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
-  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
-  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int p = warp; p < a.g * 2; p += 8) {
-    const int hq = p >> 1, j = (p & 1) * 32 + lane;
-    const uint2 *kr = reinterpret_cast<const uint2 *>(buf + j * AttnSmem::kRawRow);
-    const float4 *qr = reinterpret_cast<const float4 *>(Qs + hq * kD);
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < 32; ++c) {
-      const float4 kk = cvt4(make_uint4(kr[c].x, kr[c].y, 0u, 0u), KVR_F16);
-      const float4 qq = qr[c];
-      a0 = fmaf(qq.x, kk.x, a0);
-      a1 = fmaf(qq.y, kk.y, a1);
-      a2 = fmaf(qq.z, kk.z, a2);
-      a3 = fmaf(qq.w, kk.w, a3);
-    }
-    S[hq * kD + j] = j < nt ? (a0 + a1) + (a2 + a3) : -INFINITY;
-  }
-  __syncthreads();
-  softmax_rows(a, nt, S, P, ML);
-  __syncthreads();
-  const int c = tid & 127, half = tid >> 7;
-  float o[kMaxG];
-#pragma unroll
-  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
-  const __half *V = reinterpret_cast<const __half *>(buf + kChunk * AttnSmem::kRawRow);
-  const int j1 = min(nt, half * 32 + 32);
-  for (int j = half * 32; j < j1; ++j) {
-    const float vv = __half2float(V[j * (AttnSmem::kRawRow / 2) + c]);
-    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
-    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
-    o[0] = fmaf(p0.x, vv, o[0]); o[1] = fmaf(p0.y, vv, o[1]);
-    o[2] = fmaf(p0.z, vv, o[2]); o[3] = fmaf(p0.w, vv, o[3]);
-    if (a.g > 4) {
-      o[4] = fmaf(p1.x, vv, o[4]); o[5] = fmaf(p1.y, vv, o[5]);
-      o[6] = fmaf(p1.z, vv, o[6]); o[7] = fmaf(p1.w, vv, o[7]);
-    }
-  }
-  if (half == 1)
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
-  __syncthreads();
-  if (half == 0)
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] += o[hq];
-  __syncthreads();
-  fold_unit(a, sm, false);
-}
-
-// sd1 tile unit from the raw buffer: [KB 2 KB | VB 2 KB | KS 256 B | VS 256 B].
-template <int TILE>
-__device__ void pipe_tile(const AttnArgs &a, unsigned char *sm, const unsigned char *buf) {
-  const uint32_t *KB = reinterpret_cast<const uint32_t *>(buf);
-  const uint32_t *VB = reinterpret_cast<const uint32_t *>(buf + 2048);
-  const uint16_t *KS = reinterpret_cast<const uint16_t *>(buf + 4096);
-  const uint16_t *VS = reinterpret_cast<const uint16_t *>(buf + 4352);
-  float *LUT = reinterpret_cast<float *>(sm + AttnSmem::kPipeLUT2);
-  const float *Qp = reinterpret_cast<const float *>(sm + AttnSmem::kPipeQp);
-  float *S = reinterpret_cast<float *>(sm + AttnSmem::kS);
-  float *P = reinterpret_cast<float *>(sm + AttnSmem::kP);
-  float *ML = reinterpret_cast<float *>(sm + AttnSmem::kML);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < a.g * 32; i += blockDim.x) {
-    const int hq = i >> 5, grp = i & 31;
-    float av[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) av[r] = Qp[hq * kD + 4 * grp + r] * __half2float(__ushort_as_half(KS[4 * grp + r]));
-    float *L = LUT + (hq * 32 + grp) * 16;
-#pragma unroll
-    for (int x = 0; x < 16; ++x) {
-      float s = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) s += ((x >> r) & 1) ? av[r] : -av[r];
-      L[x] = s;
-    }
-  }
-  __syncthreads();
-  constexpr int NB = TILE / 32;
-  for (int p = warp; p < a.g * NB; p += 8) {
-    const int hq = p / NB, j = (p - hq * NB) * 32 + lane;
-    const uint4 w4 = reinterpret_cast<const uint4 *>(KB)[j];
-    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-    const float *L = LUT + hq * 32 * 16;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int grp = 0; grp < 32; ++grp) acc[grp & 3] += L[grp * 16 + ((w[grp >> 3] >> (4 * (grp & 7))) & 15u)];
-    S[hq * kD + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-  }
-  __syncthreads();
-  softmax_rows(a, TILE, S, P, ML);
-  __syncthreads();
-  const int c = tid & 127, half = tid >> 7;
-  float o[kMaxG];
-#pragma unroll
-  for (int i = 0; i < kMaxG; ++i) o[i] = 0.0f;
-  const int word = c >> 5, bit = c & 31;
-  for (int j = half * (TILE / 2); j < (half + 1) * (TILE / 2); ++j) {
-    const float bf = (float)((VB[j * 4 + word] >> bit) & 1u);
-    const float4 p0 = *reinterpret_cast<const float4 *>(P + j * kMaxG);
-    const float4 p1 = *reinterpret_cast<const float4 *>(P + j * kMaxG + 4);
-    o[0] = fmaf(p0.x, bf, o[0]); o[1] = fmaf(p0.y, bf, o[1]);
-    o[2] = fmaf(p0.z, bf, o[2]); o[3] = fmaf(p0.w, bf, o[3]);
-    if (a.g > 4) {
-      o[4] = fmaf(p1.x, bf, o[4]); o[5] = fmaf(p1.y, bf, o[5]);
-      o[6] = fmaf(p1.z, bf, o[6]); o[7] = fmaf(p1.w, bf, o[7]);
-    }
-  }
-  if (half == 1)
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = o[hq];
-  __syncthreads();
-  if (half == 0) {
-    const float vs = __half2float(__ushort_as_half(VS[c]));
-    for (int hq = 0; hq < a.g; ++hq) S[hq * kD + c] = vs * (2.0f * (o[hq] + S[hq * kD + c]) - ML[hq * 2 + 1]);
-  }
-  __syncthreads();
-  fold_unit(a, sm, true);
-}
-
-// All units [u_begin, u_end) of this CTA with the next unit's copies in
-// flight while the current one is computed.
-template <int TILE>
-__device__ void pipe_units(const AttnArgs &a, unsigned char *sm, int64_t b, int h, int u_begin, int u_end) {
-  const int tid = threadIdx.x;
-  const int n_exact = a.nchunk[0] + a.nchunk[1];
-  // per-row query data, loaded once
-  float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);
-  for (int i = tid; i < a.g * 32; i += blockDim.x) {
-    const int hq = i >> 5, qd = i & 31;
-    const float4 x = cvt4(raw4(a.q, (b * a.n_q + (int64_t)h * a.g + hq) * kD + qd * 4, a.q_dt), a.q_dt);
-    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] =
-        make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
-  }
-  bool have_qp = false;
-  pipe_issue<TILE>(a, sm + AttnSmem::kRaw0, b, h, u_begin);
-  cp_async_commit();
-  for (int u = u_begin, i = 0; u < u_end; ++u, ++i) {
-    unsigned char *cur = sm + ((i & 1) ? AttnSmem::kRaw1 : AttnSmem::kRaw0);
-    unsigned char *nxt = sm + ((i & 1) ? AttnSmem::kRaw0 : AttnSmem::kRaw1);
-    if (u + 1 < u_end) {
-      pipe_issue<TILE>(a, nxt, b, h, u + 1);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    if (u >= n_exact && !have_qp) {
-      griddep_wait();
-      float *Qp = reinterpret_cast<float *>(sm + AttnSmem::kPipeQp);
-      for (int k = tid; k < a.g * 32; k += blockDim.x) {
-        const int hq = k >> 5, qd = k & 31;
-        const float4 x = __ldg(reinterpret_cast<const float4 *>(a.qprime + (b * a.n_q + (int64_t)h * a.g + hq) * kD) + qd);
-        reinterpret_cast<float4 *>(Qp + hq * kD)[qd] =
-            make_float4(x.x * a.inv_scale, x.y * a.inv_scale, x.z * a.inv_scale, x.w * a.inv_scale);
-      }
-      have_qp = true;
-    }
-    __syncthreads();
-    if (u < n_exact) {
-      const int seg = u < a.nchunk[0] ? 0 : 1;
-      const int chunk = seg == 0 ? u : u - a.nchunk[0];
-      const int64_t t0 = (int64_t)chunk * kChunk;
-      pipe_exact(a, sm, cur, (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk));
-    } else {
-      const int64_t row = b * a.n_kv + h;
-      if (a.sel[row * a.k_sel + (u - n_exact)] >= 0) pipe_tile<TILE>(a, sm, cur);
-    }
-    __syncthreads();
-  }
-}
-
 // ------------------------------------------------------------- finalize ----
 // Ex/Tr: [g][128] exact and transformed sums, ML: [g] (M, L).  Maps Tr back
 // with one inverse transform per query head and writes out (or the partial
@@ -837,48 +618,18 @@ __device__ void merge_slots(const AttnArgs &a, unsigned char *sm, int64_t b, int
   finalize_group(a, sm, b, h, Ex, Tr, ML, buf, any_tiles);
 }
 
-template <int TILE>
-__global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
-  extern __shared__ __align__(128) unsigned char sm[];
-  const int slot = blockIdx.x, h = blockIdx.y;
-  const int64_t b = blockIdx.z;
-  const int64_t row = b * a.n_kv + h;
+// End of a CTA's units: the CTA accumulators (kAccM/L/Ex/Tr) hold its
+// result.  A CTA that owns the whole row finalizes it; otherwise it writes its
+// partial rows and the last CTA of the row merges them.
+__device__ void attn_finish(const AttnArgs &a, unsigned char *sm, int64_t b, int h) {
   const int tid = threadIdx.x;
-  KVR_TRACE_POINT(1, 0);
-  // the next layer's selection kernel may start its store loads now; it
-  // waits for this kernel to finish before it reads q or writes anything
-  asm volatile("griddepcontrol.launch_dependents;");
-  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
+  const int64_t row = b * a.n_kv + h;
+  const int slot = blockIdx.x;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
   float *AM = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
   float *AL = reinterpret_cast<float *>(sm + AttnSmem::kAccL);
   float *AEx = reinterpret_cast<float *>(sm + AttnSmem::kAccEx);
   float *ATr = reinterpret_cast<float *>(sm + AttnSmem::kAccTr);
-  for (int i = tid; i < a.g * kD; i += blockDim.x) {
-    AEx[i] = 0.0f;
-    ATr[i] = 0.0f;
-  }
-  if (tid < a.g) {
-    AM[tid] = -INFINITY;
-    AL[tid] = 0.0f;
-  }
-  if (tid == 0) reinterpret_cast<int *>(sm + AttnSmem::kFlag)[2] = 0;  // partial row written by the unit
-  __syncthreads();
-  const int n_exact = a.nchunk[0] + a.nchunk[1];
-  const int u_end = min(a.units, (slot + 1) * a.upc);
-  if (a.pipelined) {
-    if (slot * a.upc < u_end) pipe_units<TILE>(a, sm, b, h, slot * a.upc, u_end);
-  } else
-  for (int u = slot * a.upc; u < u_end; ++u) {
-    if (u < a.nchunk[0]) {
-      exact_unit(a, sm, b, h, 0, u, u);
-    } else if (u < n_exact) {
-      exact_unit(a, sm, b, h, 1, u - a.nchunk[0], u);
-    } else {
-      tile_unit<TILE>(a, sm, b, h, u - n_exact, u);
-    }
-    __syncthreads();
-  }
-  KVR_TRACE_POINT(1, 3);
   const bool any_tiles = a.units > n_exact;
   if (a.slots == 1) {
     // this CTA owns every unit of its row: no partials, no merge
@@ -915,6 +666,517 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
   merge_slots(a, sm, b, h, any_tiles);
   KVR_TRACE_POINT(1, 5);
   if (tid == 0) a.counters[row] = 0u;
+}
+
+template <int TILE>
+__global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int slot = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t row = b * a.n_kv + h;
+  const int tid = threadIdx.x;
+  KVR_TRACE_POINT(1, 0);
+  // the next layer's selection kernel may start its store loads now; it
+  // waits for this kernel to finish before it reads q or writes anything
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
+  float *AM = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
+  float *AL = reinterpret_cast<float *>(sm + AttnSmem::kAccL);
+  float *AEx = reinterpret_cast<float *>(sm + AttnSmem::kAccEx);
+  float *ATr = reinterpret_cast<float *>(sm + AttnSmem::kAccTr);
+  for (int i = tid; i < a.g * kD; i += blockDim.x) {
+    AEx[i] = 0.0f;
+    ATr[i] = 0.0f;
+  }
+  if (tid < a.g) {
+    AM[tid] = -INFINITY;
+    AL[tid] = 0.0f;
+  }
+  if (tid == 0) reinterpret_cast<int *>(sm + AttnSmem::kFlag)[2] = 0;  // partial row written by the unit
+  __syncthreads();
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  const int u_end = min(a.units, (slot + 1) * a.upc);
+  for (int u = slot * a.upc; u < u_end; ++u) {
+    if (u < a.nchunk[0]) {
+      exact_unit(a, sm, b, h, 0, u, u);
+    } else if (u < n_exact) {
+      exact_unit(a, sm, b, h, 1, u - a.nchunk[0], u);
+    } else {
+      tile_unit<TILE>(a, sm, b, h, u - n_exact, u);
+    }
+    __syncthreads();
+  }
+  KVR_TRACE_POINT(1, 3);
+  attn_finish(a, sm, b, h);
+}
+
+// ------------------------------------------------------ batched decode ----
+// Many (b, h) rows (batched decode, bandwidth-bound).  The units of a CTA are
+// cut into 32-token pieces (half a 64-token exact chunk, or a 32-token slice
+// of a selected tile) that its 8 warps take round-robin, so no barrier is
+// crossed until the CTA's last piece is done.  Every warp keeps its own online
+// softmax state and computes both products of a piece on the tensor cores
+// (mma.sync m16n8k16, fp16 operands, fp32 accumulation):
+//   S^T = K q^T   M = 32 tokens, N = 8 query heads, K = 128 channels
+//   O^T = V^T P^T M = 128 channels, N = 8 query heads, K = 16 tokens a step
+// K, V (fp16 rows) and the sd1 values +-scale are exact in fp16; q and P are
+// split into fp16 hi + lo parts (two MMAs), which keeps about 22 bits.  q is
+// first scaled by a power of two per row so that both parts stay in fp16
+// range.  Lane l = 4 g + t reads its A fragments straight from memory: exact
+// rows as 16-byte loads (channels paired as (c, c+1)); sd1 rows as bit words,
+// with channels paired as (c, c+16) so that one shift and mask of a word gives
+// the two sign bits of a half2 register.  Its accumulator holds channels
+// 16 g .. 16 g + 15 of heads 2t, 2t+1 (exact pieces in the natural domain, sd1
+// pieces in the transformed domain).  A warp's exact pieces come before its
+// sd1 pieces: at the switch the exact sum is parked in shared memory with the
+// running max it is relative to.  At the end the warp states are folded into
+// the CTA accumulators in warp order.
+constexpr int kPiece = 32;
+constexpr int kPStride = 40;  // halves per head row of the P staging (conflict-free B loads)
+struct RowSmem {
+  static constexpr int kFm = 0;                              // fp32 [8 warps][8] running max at the end
+  static constexpr int kFl = kFm + 8 * kMaxG * 4;            // fp32 [8][8] running sum
+  static constexpr int kFs = kFl + 8 * kMaxG * 4;            // fp32 [8][8] max of the parked sum
+  static constexpr int kFex = kFs + 8 * kMaxG * 4;           // fp32 [8 warps][8][128] parked exact sums
+  static constexpr int kQBx = kFex + 8 * kMaxG * kD * 4;     // uint4 [8 k-steps][32 lanes] q B fragments
+  static constexpr int kQBt = kQBx + 8 * 32 * 16;            // uint4 [8][32] q' B fragments
+  static constexpr int kP = kQBt + 8 * 32 * 16;              // per warp: fp16 [hi, lo][8 heads][40]
+  static constexpr int kPWarp = 2 * kMaxG * kPStride * 2;
+  static constexpr int kSc = kP + 8 * kPWarp;                // per warp: fp16 [-ks, -vs][128]
+  static constexpr int kEnd = kSc + 8 * 2 * kD * 2;
+  static constexpr int kFtr = kQBx;                          // fp32 [8][8][128], after every warp is done
+  static constexpr int kFEnd = kFtr + 8 * kMaxG * kD * 4;
+  static constexpr int kRed = kFEnd;                         // fp32 [8] max |q| per warp (start only)
+};
+static_assert(RowSmem::kEnd <= AttnSmem::kQ && RowSmem::kFEnd + 64 <= AttnSmem::kQ,
+              "batched decode staging must stay inside the unit region");
+
+__device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// x -> fp16 hi + lo (x = hi + lo to about 22 bits for |x| in fp16 range)
+__device__ __forceinline__ void split_f16(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  hi = h2u(h);
+  lo = h2u(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+
+// sign bits of the half2 pair (bit c -> bit 15, bit c + 16 -> bit 31) applied to -scale
+__device__ __forceinline__ uint32_t sgn_pair(uint32_t neg_scale2, uint32_t w_shifted) {
+  return neg_scale2 ^ (w_shifted & 0x80008000u);
+}
+
+struct RowState {
+  float m[2], l[2];  // running max / sum of query heads 2t, 2t+1
+  float o[8][4];     // m-tile j: (channel 16g + 2j, heads 2t, 2t+1), (16g + 2j + 1, heads 2t, 2t+1)
+};
+
+// Online softmax of a piece's scores s[mt][r] (token 16 mt + g (+8 for r >= 2),
+// head 2t + (r & 1)), then P (hi, lo) into the warp's staging.
+__device__ __forceinline__ void row_softmax(RowState &st, float (&s)[2][4], __half *Ph, int nt, int g_heads) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int tok = 16 * mt + g + (r >= 2 ? 8 : 0), hq = 2 * t + (r & 1);
+      if (tok >= nt || hq >= g_heads) s[mt][r] = -INFINITY;
+    }
+  float al[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    float pm = fmaxf(fmaxf(s[0][e], s[0][e + 2]), fmaxf(s[1][e], s[1][e + 2]));
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+    const float mn = fmaxf(st.m[e], pm);
+    al[e] = st.m[e] == -INFINITY ? 0.0f : expf(st.m[e] - mn);
+    float ps = 0.0f;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = e + 2 * rr;
+        const float p = s[mt][r] == -INFINITY ? 0.0f : expf(s[mt][r] - mn);
+        s[mt][r] = p;
+        ps += p;
+      }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    st.l[e] = fmaf(st.l[e], al[e], ps);
+    st.m[e] = mn;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    st.o[j][0] *= al[0];
+    st.o[j][1] *= al[1];
+    st.o[j][2] *= al[0];
+    st.o[j][3] *= al[1];
+  }
+  // P[head][token] as fp16 hi / lo
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int tok = 16 * mt + g + (r >= 2 ? 8 : 0), hq = 2 * t + (r & 1);
+      const __half hi = __float2half_rn(s[mt][r]);
+      Ph[hq * kPStride + tok] = hi;
+      Ph[(kMaxG + hq) * kPStride + tok] = __float2half_rn(s[mt][r] - __half2float(hi));
+    }
+  __syncwarp();
+}
+
+// O^T += V^T P^T for one 16-token step: A fragments of m-tile j from the
+// packed pairs (token 2t, 2t+1) and (2t+8, 2t+9) of channel 16g + 2j (+1).
+template <typename AF>
+__device__ __forceinline__ void row_pv_step(RowState &st, const __half *Ph, int k0, AF a_frag) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t *P32 = reinterpret_cast<const uint32_t *>(Ph);
+  const uint32_t bh0 = P32[(g * kPStride + k0 + 2 * t) >> 1];
+  const uint32_t bh1 = P32[(g * kPStride + k0 + 2 * t + 8) >> 1];
+  const uint32_t bl0 = P32[((kMaxG + g) * kPStride + k0 + 2 * t) >> 1];
+  const uint32_t bl1 = P32[((kMaxG + g) * kPStride + k0 + 2 * t + 8) >> 1];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint32_t a0, a1, a2, a3;
+    a_frag(j, a0, a1, a2, a3);
+    hmma16816(st.o[j], a0, a1, a2, a3, bh0, bh1);
+    hmma16816(st.o[j], a0, a1, a2, a3, bl0, bl1);
+  }
+}
+
+// Exact piece: nt fp16 rows at kp / vp (token stride ts, elements).
+__device__ __forceinline__ void row_piece_exact(RowState &st, const uint4 *QB, __half *Ph, int nt, const __half *kp,
+                                                const __half *vp, int64_t ts, float sscale, int g_heads) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // scores: rows g, g + 8 of both m-tiles, channels 32p + 8t .. +8
+  float s[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    uint4 ka[4], kb[4];
+    const int r0 = 16 * mt + g, r1 = r0 + 8;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      ka[p] = r0 < nt ? __ldg(reinterpret_cast<const uint4 *>(kp + r0 * ts + 32 * p + 8 * t)) : make_uint4(0u, 0u, 0u, 0u);
+      kb[p] = r1 < nt ? __ldg(reinterpret_cast<const uint4 *>(kp + r1 * ts + 32 * p + 8 * t)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint4 q0 = QB[(2 * p) * 32 + lane], q1 = QB[(2 * p + 1) * 32 + lane];
+      hmma16816(c, ka[p].x, kb[p].x, ka[p].y, kb[p].y, q0.x, q0.y);
+      hmma16816(c, ka[p].x, kb[p].x, ka[p].y, kb[p].y, q0.z, q0.w);
+      hmma16816(c, ka[p].z, kb[p].z, ka[p].w, kb[p].w, q1.x, q1.y);
+      hmma16816(c, ka[p].z, kb[p].z, ka[p].w, kb[p].w, q1.z, q1.w);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) s[mt][r] = c[r] * sscale;
+  }
+  // V rows of the 4 tokens 2t, 2t+1, 2t+8, 2t+9 of each step, channels 16g .. +16
+  uint4 vr[2][4][2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tok = 16 * k + 2 * t + (i & 1) + (i >> 1) * 8;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        vr[k][i][hh] = tok < nt ? __ldg(reinterpret_cast<const uint4 *>(vp + tok * ts + 16 * g + 8 * hh))
+                                : make_uint4(0u, 0u, 0u, 0u);
+    }
+  row_softmax(st, s, Ph, nt, g_heads);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    auto word = [&](int i, int j) -> uint32_t {  // channels 16g + 2j, 2j + 1 of token i
+      const uint4 &u = vr[k][i][j >> 2];
+      const int e = j & 3;
+      return e == 0 ? u.x : (e == 1 ? u.y : (e == 2 ? u.z : u.w));
+    };
+    row_pv_step(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+      a0 = __byte_perm(word(0, j), word(1, j), 0x5410);
+      a1 = __byte_perm(word(0, j), word(1, j), 0x7632);
+      a2 = __byte_perm(word(2, j), word(3, j), 0x5410);
+      a3 = __byte_perm(word(2, j), word(3, j), 0x7632);
+    });
+  }
+  __syncwarp();
+}
+
+// sd1 piece: 32 token rows of 4 bit words at kw / vw; SC = the warp's staged
+// negated scales (-ks [128], -vs [128], fp16).
+__device__ __forceinline__ void row_piece_sd1(RowState &st, const uint4 *QB, __half *Ph, const uint32_t *kw,
+                                              const uint32_t *vw, const __half *SC, float sscale, int g_heads) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // -ks pairs (32p + 8s + t, +16) and (32p + 8s + 4 + t, +16) of k-step 2p + s
+  uint32_t ksp[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int c0 = 32 * (kk >> 1) + 8 * (kk & 1) + t;
+    ksp[kk][0] = h2u(__halves2half2(SC[c0], SC[c0 + 16]));
+    ksp[kk][1] = h2u(__halves2half2(SC[c0 + 4], SC[c0 + 20]));
+  }
+  float s[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    uint32_t wa[4], wb[4];
+    const int r0 = 16 * mt + g, r1 = r0 + 8;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      wa[p] = __ldg(kw + r0 * 4 + p);
+      wb[p] = __ldg(kw + r1 * 4 + p);
+    }
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int p = kk >> 1, c0 = 8 * (kk & 1) + t;
+      const uint32_t a0 = sgn_pair(ksp[kk][0], wa[p] << (15 - c0));
+      const uint32_t a1 = sgn_pair(ksp[kk][0], wb[p] << (15 - c0));
+      const uint32_t a2 = sgn_pair(ksp[kk][1], wa[p] << (11 - c0));
+      const uint32_t a3 = sgn_pair(ksp[kk][1], wb[p] << (11 - c0));
+      const uint4 q = QB[kk * 32 + lane];
+      hmma16816(c, a0, a1, a2, a3, q.x, q.y);
+      hmma16816(c, a0, a1, a2, a3, q.z, q.w);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) s[mt][r] = c[r] * sscale;
+  }
+  // V words (word g / 2) of tokens 2t, 2t+1, 2t+8, 2t+9 of each step
+  uint32_t vwd[2][4];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) vwd[k][i] = __ldg(vw + (16 * k + 2 * t + (i & 1) + (i >> 1) * 8) * 4 + (g >> 1));
+  // -vs of channels 16g + 2j (even) and + 1 (odd), both halves
+  uint32_t vse[8], vso[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const __half e = SC[kD + 16 * g + 2 * j], o = SC[kD + 16 * g + 2 * j + 1];
+    vse[j] = h2u(__halves2half2(e, e));
+    vso[j] = h2u(__halves2half2(o, o));
+  }
+  row_softmax(st, s, Ph, kPiece, g_heads);
+  const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;  // this lane's 16 channels are half g & 1 of the word
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t x01 = __byte_perm(vwd[k][0], vwd[k][1], sel);
+    const uint32_t x23 = __byte_perm(vwd[k][2], vwd[k][3], sel);
+    row_pv_step(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+      a0 = sgn_pair(vse[j], x01 << (15 - 2 * j));
+      a1 = sgn_pair(vso[j], x01 << (14 - 2 * j));
+      a2 = sgn_pair(vse[j], x23 << (15 - 2 * j));
+      a3 = sgn_pair(vso[j], x23 << (14 - 2 * j));
+    });
+  }
+  __syncwarp();
+}
+
+// q B fragments of one k-step for lane l = 4g + t (head g): natural channel
+// pairs for exact K (pairs ch, ch + 1 at 32p + 8t + 4s) or (c, c + 16) pairs at
+// 32p + 8s + t (+4) for sd1 K.  q is multiplied by the power of two qsc.
+__device__ __forceinline__ uint4 q_bfrag(const float *Qrow, int kk, int lane, bool sd1, float qsc) {
+  const int t = lane & 3, p = kk >> 1, s = kk & 1;
+  float x[4];
+  if (!sd1) {
+    const int c = 32 * p + 8 * t + 4 * s;
+    x[0] = Qrow[c]; x[1] = Qrow[c + 1]; x[2] = Qrow[c + 2]; x[3] = Qrow[c + 3];
+  } else {
+    const int c = 32 * p + 8 * s + t;
+    x[0] = Qrow[c]; x[1] = Qrow[c + 16]; x[2] = Qrow[c + 4]; x[3] = Qrow[c + 20];
+  }
+  uint4 r;
+  split_f16(x[0] * qsc, x[1] * qsc, r.x, r.z);
+  split_f16(x[2] * qsc, x[3] * qsc, r.y, r.w);
+  return r;
+}
+
+// power of two bringing max |q| near 2^12 (fp16 range for hi, normal range for lo)
+__device__ __forceinline__ float pow2_scale(float amax) {
+  if (!(amax > 0.0f) || !isfinite(amax)) return 1.0f;
+  int e;
+  frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+  return ldexpf(1.0f, 12 - e);
+}
+
+template <int TILE>
+__global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  const int slot = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t row = b * a.n_kv + h;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int n_exact = a.nchunk[0] + a.nchunk[1];
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
+  if (tid == 0) reinterpret_cast<int *>(sm + AttnSmem::kFlag)[2] = 0;
+  // q and q' of the group (q' and the selection come from the preceding
+  // kernel) staged as fp32 rows, rows of heads >= g zero
+  griddep_wait();
+  float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);   // fp32 [8][128]
+  float *Qps = reinterpret_cast<float *>(sm + AttnSmem::kS);  // fp32 [8][128]
+  float *red = reinterpret_cast<float *>(sm + RowSmem::kRed);
+  const bool any_tiles = a.units > n_exact;
+  float amx = 0.0f, amt = 0.0f;
+  for (int i = tid; i < kMaxG * 32; i += blockDim.x) {
+    const int hq = i >> 5, qd = i & 31;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
+    if (hq < a.g) {
+      const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
+      x = cvt4(raw4(a.q, qh * kD + qd * 4, a.q_dt), a.q_dt);
+      if (any_tiles) y = __ldcg(reinterpret_cast<const float4 *>(a.qprime + qh * kD) + qd);
+    }
+    amx = fmaxf(amx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+    amt = fmaxf(amt, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] = x;
+    reinterpret_cast<float4 *>(Qps + hq * kD)[qd] = y;
+  }
+  amx = warp_max(amx);
+  amt = warp_max(amt);
+  if (lane == 0) {
+    red[warp] = amx;
+    red[8 + warp] = amt;
+  }
+  __syncthreads();
+  float qsx = 0.0f, qst = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    qsx = fmaxf(qsx, red[w]);
+    qst = fmaxf(qst, red[8 + w]);
+  }
+  qsx = pow2_scale(qsx);
+  qst = pow2_scale(qst);
+  uint4 *QBx = reinterpret_cast<uint4 *>(sm + RowSmem::kQBx);
+  uint4 *QBt = reinterpret_cast<uint4 *>(sm + RowSmem::kQBt);
+  {
+    const int kk = tid >> 5;  // 8 k-steps x 32 lanes = 256 threads
+    QBx[kk * 32 + lane] = q_bfrag(Qs + g * kD, kk, lane, false, qsx);
+    if (any_tiles) QBt[kk * 32 + lane] = q_bfrag(Qps + g * kD, kk, lane, true, qst);
+  }
+  __syncthreads();
+  const float sx = a.inv_scale / qsx, stl = a.inv_scale / qst;
+
+  RowState st;
+  st.m[0] = st.m[1] = -INFINITY;
+  st.l[0] = st.l[1] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st.o[j][i] = 0.0f;
+  __half *Ph = reinterpret_cast<__half *>(sm + RowSmem::kP + warp * RowSmem::kPWarp);
+  __half *SC = reinterpret_cast<__half *>(sm + RowSmem::kSc) + warp * 2 * kD;
+  float *Fex = reinterpret_cast<float *>(sm + RowSmem::kFex) + warp * kMaxG * kD;
+  float m_park[2] = {-INFINITY, -INFINITY};
+  bool parked = false;
+  // the accumulator's (channel, head) entries as [head][channel] rows
+  auto store_acc = [&](float *dst) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = 16 * g + 2 * j;
+      dst[(2 * t) * kD + c] = st.o[j][0];
+      dst[(2 * t + 1) * kD + c] = st.o[j][1];
+      dst[(2 * t) * kD + c + 1] = st.o[j][2];
+      dst[(2 * t + 1) * kD + c + 1] = st.o[j][3];
+    }
+  };
+  auto park = [&]() {
+    store_acc(Fex);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) st.o[j][i] = 0.0f;
+    m_park[0] = st.m[0];
+    m_park[1] = st.m[1];
+    parked = true;
+  };
+
+  const int u0 = slot * a.upc, u1 = min(a.units, u0 + a.upc);
+  const int ex_units = max(0, min(u1, n_exact) - u0);
+  constexpr int PPT = TILE / kPiece;  // pieces per tile
+  const int n_pieces = 2 * ex_units + PPT * max(0, u1 - u0 - ex_units);
+  for (int pc = warp; pc < n_pieces; pc += 8) {
+    if (pc < 2 * ex_units) {
+      const int u = u0 + pc / 2;
+      const int seg = u < a.nchunk[0] ? 0 : 1;
+      const int chunk = seg == 0 ? u : u - a.nchunk[0];
+      const int64_t t0 = (int64_t)chunk * kChunk + (pc & 1) * kPiece;
+      const int64_t left = a.n[seg] - t0;
+      if (left <= 0) continue;
+      const int nt = (int)(left < kPiece ? left : kPiece);
+      const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD + t0 * a.tok_stride[seg];
+      row_piece_exact(st, QBx, Ph, nt, reinterpret_cast<const __half *>(a.k[seg]) + base,
+                      reinterpret_cast<const __half *>(a.v[seg]) + base, a.tok_stride[seg], sx, a.g);
+    } else {
+      if (!parked) park();
+      const int r = pc - 2 * ex_units;
+      const int u = u0 + ex_units + r / PPT, sub = r % PPT;
+      const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+      if (tsel < 0) continue;
+      const int64_t tix = row * a.nt_cap + tsel;
+      // negated scales of the tile into the warp's staging
+      const uint2 ksr = __ldg(reinterpret_cast<const uint2 *>(a.kscale + tix * kD) + lane);
+      const uint2 vsr = __ldg(reinterpret_cast<const uint2 *>(a.vscale + tix * kD) + lane);
+      reinterpret_cast<uint2 *>(SC)[lane] = make_uint2(ksr.x ^ 0x80008000u, ksr.y ^ 0x80008000u);
+      reinterpret_cast<uint2 *>(SC + kD)[lane] = make_uint2(vsr.x ^ 0x80008000u, vsr.y ^ 0x80008000u);
+      __syncwarp();
+      const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
+      row_piece_sd1(st, QBt, Ph, a.kbits + w0, a.vbits + w0, SC, stl, a.g);
+    }
+  }
+  if (!parked) park();  // only exact pieces (or none): the sd1 sum is zero
+
+  // fold the 8 warp states into the CTA accumulators (warp order)
+  __syncthreads();  // the B fragments and P staging are dead from here on
+  float *Ftr = reinterpret_cast<float *>(sm + RowSmem::kFtr);
+  float *Fm = reinterpret_cast<float *>(sm + RowSmem::kFm);
+  float *Fl = reinterpret_cast<float *>(sm + RowSmem::kFl);
+  float *Fs = reinterpret_cast<float *>(sm + RowSmem::kFs);
+  if (g == 0) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      Fm[warp * kMaxG + 2 * t + e] = st.m[e];
+      Fl[warp * kMaxG + 2 * t + e] = st.l[e];
+      Fs[warp * kMaxG + 2 * t + e] = m_park[e];
+    }
+  }
+  store_acc(Ftr + warp * kMaxG * kD);
+  __syncthreads();
+  float *AM = reinterpret_cast<float *>(sm + AttnSmem::kAccM);
+  float *AL = reinterpret_cast<float *>(sm + AttnSmem::kAccL);
+  float *AEx = reinterpret_cast<float *>(sm + AttnSmem::kAccEx);
+  float *ATr = reinterpret_cast<float *>(sm + AttnSmem::kAccTr);
+  const float *FexAll = reinterpret_cast<const float *>(sm + RowSmem::kFex);
+  for (int i = tid; i < a.g * kD; i += blockDim.x) {
+    const int hq = i >> 7, c = i & (kD - 1);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, Fm[w * kMaxG + hq]);
+    float ex = 0.0f, tr = 0.0f, L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float mw = Fm[w * kMaxG + hq], ms = Fs[w * kMaxG + hq];
+      if (mw == -INFINITY) continue;
+      const float sc = expf(mw - M);
+      tr = fmaf(Ftr[(w * kMaxG + hq) * kD + c], sc, tr);
+      L = fmaf(Fl[w * kMaxG + hq], sc, L);
+      if (ms != -INFINITY) ex = fmaf(FexAll[(w * kMaxG + hq) * kD + c], expf(ms - M), ex);
+    }
+    AEx[i] = ex;
+    ATr[i] = tr;
+    if (c == 0) {
+      AM[hq] = M;
+      AL[hq] = L;
+    }
+  }
+  __syncthreads();
+  KVR_TRACE_POINT(1, 3);
+  attn_finish(a, sm, b, h);
 }
 
 // Merge kernel for sequence-split partials: one warp per query row.
@@ -993,9 +1255,9 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
   size_t smem = AttnSmem::kTotal;
   const int upc = attn_upc(a.units, (int64_t)batch * a.n_kv);
   KVR_REQUIRE(a.rank_scores == nullptr || upc == 1, "%s: in-unit selection needs one unit per CTA", what);
-  a.upc = upc;
   a.slots = (a.units + upc - 1) / upc;
-  // the pipelined path streams fp16 rows with 16-byte async copies
+  a.upc = (a.units + a.slots - 1) / a.slots;  // even split over the slots
+  // the batched path reads fp16 rows as 8-byte quads
   bool f16 = upc > 1;
   for (int s = 0; s < 2; ++s) {
     if (a.n[s] == 0) continue;
@@ -1004,17 +1266,18 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
           (reinterpret_cast<uintptr_t>(a.v[s]) % 16) == 0;
   }
   a.pipelined = f16 ? 1 : 0;
-  if (a.pipelined) smem = AttnSmem::kPipeTotal;
   const size_t ms = merge_smem_bytes(a.slots);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
   dim3 grid(a.slots, a.n_kv, batch);
   // per-device attribute cache (the attribute is per function and device)
   static thread_local int cached_dev = -1;
   static thread_local bool smem_set[3] = {false, false, false};
+  static thread_local bool rows_set[3] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != cached_dev) {
     smem_set[0] = smem_set[1] = smem_set[2] = false;
+    for (auto &r : rows_set) r = false;
     cached_dev = dev;
   }
   cudaLaunchConfig_t cfg{};
@@ -1034,7 +1297,16 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
     cfg.stream = st;                                                                               \
     cfg.attrs = attr;                                                                              \
     cfg.numAttrs = pdl ? 1 : 0;                                                                    \
-    if (cudaLaunchKernelEx(&cfg, attn_kernel<T>, a) != cudaSuccess) return check_launch(what);     \
+    if (a.pipelined) {                                                                             \
+      if (!rows_set[T / 64]) {                                                                     \
+        cudaFuncSetAttribute(attn_rows_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                             (int)smem);                                                           \
+        rows_set[T / 64] = true;                                                                   \
+      }                                                                                            \
+      if (cudaLaunchKernelEx(&cfg, attn_rows_kernel<T>, a) != cudaSuccess) return check_launch(what); \
+    } else if (cudaLaunchKernelEx(&cfg, attn_kernel<T>, a) != cudaSuccess) {                       \
+      return check_launch(what);                                                                   \
+    }                                                                                              \
     break;
     KVR_AT(32)
     KVR_AT(64)

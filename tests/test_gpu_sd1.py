@@ -223,6 +223,73 @@ def test_attend_vs_oracle(kind, tile, nw, ntl, g, B):
                 assert err < 1e-5, (b, h, err)
 
 
+def _batched_path_taken(B, n_kv, nw, ntl, k_sel):
+    """The attention host picks the batched-rows kernel when the rows x units
+    of the step exceed two CTAs per SM (296 on B200)."""
+    units = -(-nw // 64) + -(-ntl // 64) + k_sel
+    return B * n_kv * units > 296
+
+
+@pytest.mark.parametrize("kind,tile,nw,ntl,g,B,n_kv,nt,k_sel,q_dtype", [
+    ("dct", 64, 256, 17, 4, 16, 8, 24, 16, torch.bfloat16),
+    ("hadamard", 32, 100, 0, 8, 12, 4, 30, 12, torch.float32),
+    ("dct", 128, 200, 63, 4, 8, 8, 12, 8, torch.float16),
+    ("hadamard", 64, 0, 5, 2, 32, 4, 10, 16, torch.float32),  # no window, 6 of 16 slots empty
+    ("dct", 64, 512, 0, 8, 6, 8, 20, 16, torch.float32),
+    ("dct", 64, 300, 1, 1, 24, 8, 20, 4, torch.float32),       # g = 1 (MHA)
+])
+def test_attend_batched_rows_vs_oracle(kind, tile, nw, ntl, g, B, n_kv, nt, k_sel, q_dtype):
+    """Batched decode (many (b, h) rows): every lane-owned channel quad, the
+    reduce-scatter of the scores, the per-warp online softmax, the parked
+    exact sums and the cross-warp fold against the float64 oracle."""
+    assert _batched_path_taken(B, n_kv, nw, ntl, k_sel)
+    st, k, v, q = _store(31, nt, tile, kind, n_kv=n_kv, n_q=n_kv * g, B=B)
+    rng = np.random.default_rng(3)
+    cap = max(nw, 1) + 5
+    win_k = rng.standard_normal((B, cap, n_kv, 128)).astype(np.float16)
+    win_v = rng.standard_normal((B, cap, n_kv, 128)).astype(np.float16)
+    tail_k = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    tail_v = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    qt = t(q).to(q_dtype)
+    qn = qt.float().cpu().numpy()
+    sel, _, qp = K().sd1_select(st, qt, k_sel)
+    out = K().sd1_attend(st, qt, qp, sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                         out_dtype=torch.float32).cpu().numpy()
+    sel_f = torch.empty_like(sel)
+    step = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                               sel_out=sel_f, out=torch.empty(B, n_kv * g, 128, device=DEV)).cpu().numpy()
+    assert torch.equal(sel_f, sel)
+    assert np.array_equal(step, out)
+    s = sel.cpu().numpy()
+    assert (s < 0).any() == (nt < k_sel)
+    worst = 0.0
+    for b in range(B):
+        for h in range(n_kv):
+            want = _oracle_attend(qn, st, b, h, s[b, h], win_k, win_v, nw, tail_k, tail_v, ntl, kind, g)
+            got = out[b, h * g:(h + 1) * g]
+            worst = max(worst, np.abs(got - want).max() / np.abs(want).max())
+    assert worst < 1e-5, worst
+
+
+def test_attend_batched_rows_partial_merge_like_whole():
+    """Sequence split on the batched path: two halves of the selection as
+    partial rows, merged by kvr_lse_merge, equal the whole attention."""
+    B, n_kv, g = 16, 8, 4
+    st, k, v, q = _store(7, 30, n_kv=n_kv, n_q=n_kv * g, B=B)
+    assert _batched_path_taken(B, n_kv, 0, 0, 16)
+    qt = t(q)
+    sel, _, qp = K().sd1_select(st, qt, 16)
+    whole = K().sd1_attend(st, qt, qp, sel, out_dtype=torch.float32)
+    a, b = sel.clone(), sel.clone()
+    a[..., 8:] = -1
+    b[..., :8] = -1
+    pa = K().sd1_attend(st, qt, qp, a, partial=True)
+    pb = K().sd1_attend(st, qt, qp, b, partial=True)
+    for bi in range(B):
+        merged = K().lse_merge(torch.stack([pa[bi], pb[bi]]))
+        np.testing.assert_allclose(merged.cpu().numpy(), whole[bi].cpu().numpy(), rtol=1e-5, atol=1e-6)
+
+
 def test_partial_rows_merge_like_whole():
     """Sequence split: two halves of the selection -> partials -> kvr_lse_merge."""
     st, k, v, q = _store(5, 30, n_kv=8, n_q=32)
