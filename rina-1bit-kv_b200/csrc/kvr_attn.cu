@@ -762,6 +762,11 @@ __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
+// bulk prefetch of `bytes` (multiple of 16) at a 16-byte aligned address into L2
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // x -> fp16 hi + lo (x = hi + lo to about 22 bits for |x| in fp16 range)
 __device__ __forceinline__ void split_f16(float x0, float x1, uint32_t &hi, uint32_t &lo) {
   const __half2 h = __floats2half2_rn(x0, x1);
@@ -1100,6 +1105,32 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   const int ex_units = max(0, min(u1, n_exact) - u0);
   constexpr int PPT = TILE / kPiece;  // pieces per tile
   const int n_pieces = 2 * ex_units + PPT * max(0, u1 - u0 - ex_units);
+  // Every piece of this warp is requested into L2 first (no registers held):
+  // the loads of the pieces then wait for L2 instead of a DRAM round trip each.
+  for (int pc = warp; pc < n_pieces; pc += 8) {
+    if (pc < 2 * ex_units) {
+      const int u = u0 + pc / 2;
+      const int seg = u < a.nchunk[0] ? 0 : 1;
+      const int64_t t0 = (int64_t)(seg == 0 ? u : u - a.nchunk[0]) * kChunk + (pc & 1) * kPiece;
+      if (t0 + lane < a.n[seg]) {
+        const int64_t off = b * a.batch_stride[seg] + (int64_t)h * kD + (t0 + lane) * a.tok_stride[seg];
+        prefetch_l2(reinterpret_cast<const __half *>(a.k[seg]) + off, kD * 2);
+        prefetch_l2(reinterpret_cast<const __half *>(a.v[seg]) + off, kD * 2);
+      }
+    } else if (lane < 4) {
+      const int r = pc - 2 * ex_units;
+      const int u = u0 + ex_units + r / PPT, sub = r % PPT;
+      const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+      if (tsel >= 0) {
+        const int64_t tix = row * a.nt_cap + tsel;
+        const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
+        if (lane == 0) prefetch_l2(a.kbits + w0, kPiece * 16);
+        if (lane == 1) prefetch_l2(a.vbits + w0, kPiece * 16);
+        if (lane == 2) prefetch_l2(a.kscale + tix * kD, kD * 2);
+        if (lane == 3) prefetch_l2(a.vscale + tix * kD, kD * 2);
+      }
+    }
+  }
   for (int pc = warp; pc < n_pieces; pc += 8) {
     if (pc < 2 * ex_units) {
       const int u = u0 + pc / 2;
@@ -1239,7 +1270,7 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                        float *qprime, unsigned *counters, float *scores, cudaStream_t st,
-                       const uint32_t *vbits, const uint16_t *vscale, int do_select);
+                       const uint32_t *vbits, const uint16_t *vscale, int do_select, const RowPrefetch *rows);
 
 // Units per CTA: one unit per CTA while the rows leave the GPU idle (batch 1,
 // latency-bound), more as rows grow, so about two CTAs per SM are launched
@@ -1256,7 +1287,15 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
   const int upc = attn_upc(a.units, (int64_t)batch * a.n_kv);
   KVR_REQUIRE(a.rank_scores == nullptr || upc == 1, "%s: in-unit selection needs one unit per CTA", what);
   a.slots = (a.units + upc - 1) / upc;
+  if (upc > 1) {
+    // batched rows: one CTA per row once the rows fill every SM (one wave,
+    // each warp with the same number of pieces), else about two CTAs per SM
+    const int64_t rows = (int64_t)batch * a.n_kv;
+    const int64_t want = rows >= 148 ? 1 : (296 + rows / 2) / rows;
+    a.slots = (int)(want < a.units ? want : a.units);
+  }
   a.upc = (a.units + a.slots - 1) / a.slots;  // even split over the slots
+  a.slots = (a.units + a.upc - 1) / a.upc;
   // the batched path reads fp16 rows as 8-byte quads
   bool f16 = upc > 1;
   for (int s = 0; s < 2; ++s) {
@@ -1495,9 +1534,20 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   // mostly never selected).
   const bool rank = k_sel > 0 && n_tiles > 0 && n_tiles <= kRankMaxTiles &&
                     attn_upc(sd1_units(n_win, n_tail, k_sel), (int64_t)batch * n_kv) == 1;
+  // Batched steps: the selection kernel is ALU-bound with DRAM mostly idle, so
+  // it streams the window / tail rows into L2 for the attention kernel.
+  RowPrefetch rows{};
+  const int64_t tokw = (int64_t)n_kv * kD;
+  rows.k[0] = n_win > 0 ? win_k : nullptr; rows.v[0] = win_v; rows.n[0] = n_win; rows.batch_stride[0] = win_cap * tokw;
+  rows.k[1] = n_tail > 0 ? tail_k : nullptr; rows.v[1] = tail_v; rows.n[1] = n_tail;
+  rows.batch_stride[1] = (int64_t)tile * tokw;
+  rows.tok_stride = tokw;
+  const bool rows_ok = (reinterpret_cast<uintptr_t>(win_k) | reinterpret_cast<uintptr_t>(win_v) |
+                        reinterpret_cast<uintptr_t>(tail_k) | reinterpret_cast<uintptr_t>(tail_v)) % 16 == 0;
   int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
-                              as_cuda(stream), rank ? vbits : nullptr, rank ? vscale : nullptr, rank ? 0 : 1);
+                              as_cuda(stream), rank ? vbits : nullptr, rank ? vscale : nullptr, rank ? 0 : 1,
+                              !rank && rows_ok ? &rows : nullptr);
   if (rc) return rc;
   // the attention kernel is a programmatic dependent of the selection
   // kernel: its window/tail units overlap the tile scan, its tile units wait

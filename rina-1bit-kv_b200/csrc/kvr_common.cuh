@@ -173,6 +173,14 @@ __device__ __forceinline__ float4 cvt4(uint4 r, int dt) {
 
 // Programmatic dependent launch: wait for the preceding grid (a no-op when
 // the kernel was not launched as a dependent), and let dependents start.
+// Exact K/V segments (fp16 rows of kD channels: the window ring and the
+// pending tail) of every (b, h) row, for a kernel that stages them in L2
+// ahead of the attention kernel that reads them.
+struct RowPrefetch {
+  const uint16_t *k[2], *v[2];
+  int64_t n[2], batch_stride[2], tok_stride;
+};
+
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---- mbarrier + bulk copy (PTX)

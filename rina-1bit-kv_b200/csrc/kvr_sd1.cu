@@ -258,6 +258,7 @@ struct SelectArgs {
   unsigned *counters;   // (B, n_kv), zero on entry, reset on exit
   const uint32_t *vbits;   // optional: V data of the scanned tiles is
   const uint16_t *vscale;  // prefetched into L2 for the attention kernel
+  RowPrefetch rows;        // optional (k[s] null = none): exact rows prefetched into L2
 };
 
 template <int DTQ, int TILE>
@@ -308,6 +309,19 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
       }
     }
   };
+  // batched decode: this row's exact K/V rows (read by the attention kernel
+  // that follows) stream into L2 while the ALU-bound scan runs
+#pragma unroll 1
+  for (int s = 0; s < 2; ++s) {
+    if (sa.rows.k[s] == nullptr) continue;
+    const int64_t base = b * sa.rows.batch_stride[s] + (int64_t)h * kD;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < sa.rows.n[s];
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t off = base + i * sa.rows.tok_stride;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.rows.k[s] + off), "r"(kD * 2) : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.rows.v[s] + off), "r"(kD * 2) : "memory");
+    }
+  }
   int64_t t_cur = cta_t0 + 2 * warp;
   if (t_cur < cta_t1) load_pair(t_cur, kb, ks);
   // launched as a programmatic dependent of the previous kernel: everything
@@ -669,7 +683,7 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
                        float *qprime, unsigned *counters, float *scores, cudaStream_t st,
-                       const uint32_t *vbits, const uint16_t *vscale, int do_select) {
+                       const uint32_t *vbits, const uint16_t *vscale, int do_select, const RowPrefetch *rows) {
   int rc = check_common_sd1(batch, n_q, n_kv, tile, kind);
   if (rc) return rc;
   KVR_REQUIRE(valid_dtype(q_dtype), "kvr_sd1_select: bad dtype %d", q_dtype);
@@ -678,7 +692,8 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
   KVR_REQUIRE(n_tiles >= 0 && n_tiles <= nt_cap, "kvr_sd1_select: n_tiles > nt_cap");
   KVR_REQUIRE(n_tiles == 0 || (kbits && kscale), "kvr_sd1_select: null store pointers");
   KVR_REQUIRE((int64_t)batch * n_kv <= kWsMaxRows, "kvr_sd1_select: batch*n_kv > %d", kWsMaxRows);
-  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters, vbits, vscale};
+  SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters, vbits, vscale, RowPrefetch{}};
+  if (rows) sa.rows = *rows;
   // With no full tile there is nothing to score; the kernel still forms q'
   // and writes an all-empty selection.
   return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,
@@ -704,7 +719,7 @@ extern "C" int kvr_sd1_select(const void *q, int q_dtype, int batch, int n_q, in
   char *p = reinterpret_cast<char *>(workspace);
   return sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                             ex_t1, tile_base, sel, sel_scores, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters),
-                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream), nullptr, nullptr, 1);
+                            reinterpret_cast<float *>(p + kWsHeader), as_cuda(stream), nullptr, nullptr, 1, nullptr);
 }
 
 extern "C" int kvr_sd1_decode_tiles(const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
