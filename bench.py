@@ -96,6 +96,100 @@ def measured_peak_hbm():
 
 # ----------------------------------------------------------------- GPU arm --
 
+# batched decode stress, batch 32 x 16384 context, window
+# 256, top 16 tiles of 64 (Llama-3-8B attention shapes, 32 q / 8 KV heads).
+B2, CTX2, WIN2, L2_LAYERS = 32, 16384, 256, 4
+NT2 = (CTX2 - WIN2) // TILE  # 252
+
+
+def run_batched(dev, g, peak):
+    """Secondary measurement on configs[2] at one GPU: the decode step of a
+    layer over a batch of 32 sequences, timed as a CUDA graph over 4 layers
+    (4 x 127 MB of stores + windows, larger than L2), then the select and
+    attend kernels alone.  Bytes are the algorithmic bytes of the step: the
+    select reads every stored tile's K bits + K scales, the attention the
+    selected tiles' K/V bits and scales, the fp16 window rows, q and out."""
+    import torch
+
+    from kvr_b200 import kernels as K
+    from kvr_b200 import _native as N
+
+    stores, wins = [], []
+    for li in range(L2_LAYERS):
+        scale = torch.exp(torch.randn(HKV, D, device=dev, generator=g))
+        idx = torch.randint(0, D, (HKV, 4), device=dev, generator=g)
+        scale.scatter_(1, idx, scale.gather(1, idx) * 20)
+        k = (torch.randn(B2, NT2 * TILE, HKV, D, device=dev, generator=g) * scale).to(torch.bfloat16)
+        v = torch.randn(B2, NT2 * TILE, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+        st = K.Sd1Store(B2, HKV, NT2, TILE, KIND, dev)
+        K.sd1_encode(st, k, v)
+        stores.append(st)
+        del k, v
+        wins.append((torch.randn(B2, WIN2, HKV, D, device=dev, generator=g).half(),
+                     torch.randn(B2, WIN2, HKV, D, device=dev, generator=g).half()))
+    q = torch.randn(L2_LAYERS, B2, HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws = torch.zeros(N.call("kvr_sd1_workspace_bytes", B2, HQ, HKV, NT2, TILE, KSEL, WIN2, 0) + 256,
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def timed(fn, reps=30):
+        with torch.cuda.stream(stream):
+            fn()
+            fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                gr.replay()
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / L2_LAYERS
+
+    def step():
+        for li in range(L2_LAYERS):
+            wk, wv = wins[li]
+            K.sd1_decode_step(stores[li], q[li], KSEL, wk, wv, WIN2, out=out[li], ws=ws)
+
+    ms_step = timed(step)
+    sels = [K.sd1_select(stores[li], q[li], KSEL) for li in range(L2_LAYERS)]
+
+    def sel_only():
+        for li in range(L2_LAYERS):
+            K.sd1_select(stores[li], q[li], KSEL)
+
+    def att_only():
+        for li in range(L2_LAYERS):
+            s_, _, qp = sels[li]
+            wk, wv = wins[li]
+            K.sd1_attend(stores[li], q[li], qp, s_, wk, wv, WIN2, out_dtype=torch.bfloat16)
+
+    ms_sel, ms_att = timed(sel_only), timed(att_only)
+    kb, sc = TILE * D // 8, D * 2
+    sel_b = B2 * HKV * NT2 * (kb + sc)
+    att_b = B2 * HKV * (KSEL * 2 * (kb + sc) + WIN2 * D * 2 * 2) + 2 * B2 * HQ * D * 2
+    gbs = (sel_b + att_b) / (ms_step / 1e3) / 1e9
+    res = {"workload": "configs[2] batched decode stress: batch 32 x 16384 context, window 256, "
+                       "top 16 tiles of 64, dct, Llama-3-8B attention shapes",
+           "layers_in_graph": L2_LAYERS, "us_per_layer": round(ms_step * 1e3, 2),
+           "sequence_layer_steps_per_s": round(B2 / (ms_step / 1e3), 1),
+           "bytes_per_layer": sel_b + att_b, "hbm_gbs": round(gbs, 1), "peak": peak,
+           "frac": round(gbs / peak, 4), "select_us": round(ms_sel * 1e3, 2), "attend_us": round(ms_att * 1e3, 2),
+           "select_bytes": sel_b, "attend_bytes": att_b,
+           "select_gbs": round(sel_b / (ms_sel / 1e3) / 1e9, 1), "attend_gbs": round(att_b / (ms_att / 1e3) / 1e9, 1),
+           "kernels": "sd1_score_kernel (popcount tile scores + top-k, streams the window into L2) -> "
+                      "attn_rows_kernel (mma.sync pieces)"}
+    del stores, wins, sels
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
 
@@ -294,6 +388,9 @@ def run_gpu(args, rank, world, local_rank):
         del q_pf
 
     peak, peak_kind = measured_peak_hbm()
+    batched = None
+    if world == 1 and not args.no_batched:
+        batched = run_batched(dev, g, peak)
     traffic = None
     try:  # DRAM bytes per launch from the committed ncu capture of this workload
         tj = json.load(open(os.path.join(ROOT, "profiles", "traffic_config1.json")))["dram_bytes_per_launch"]
@@ -338,6 +435,7 @@ def run_gpu(args, rank, world, local_rank):
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
                 "d2h_bytes_per_step": o_host.numel() * o_host.element_size(), "path": "kvr_b200.kernels eager API"},
         "prefill_scores": prefill,
+        "batched": batched,
         "gpu_launches": args.steps * LAYERS * 2,
         "clocks": clocks,
     }
@@ -379,6 +477,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the configs[2] batched measurement")
     ap.add_argument("--cpu-sample", type=int, default=8, help="layers timed for the CPU baseline")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
