@@ -7,6 +7,9 @@
 // reference's design: the GQA-group mean of the post-RoPE query scores fixed
 // tiles (modules/kvr_retrieval.py:270, 291-315) and a per-KV-head top-k keeps
 // the best ones (modules/kvr_retrieval.py:370-392).
+#include <utility>
+#include <vector>
+
 #include "kvr_common.cuh"
 #include "kvr_sd1_score.cuh"
 #include "kvr_topk.cuh"
@@ -549,6 +552,22 @@ size_t select_dyn_smem(int k_sel, int64_t n_tiles) {
          (n_tiles <= kSelectSmemScores ? (size_t)(n_tiles > 0 ? n_tiles : 1) * 4 : 0);
 }
 
+// Raises a kernel's dynamic shared-memory limit (once per device and size)
+// when its static + dynamic shared memory may pass the default 48 KB.
+template <typename F>
+static void ensure_dyn_smem(F *fn, size_t dyn_bytes) {
+  constexpr int kMaxDev = 64;
+  if (dyn_bytes + 16 * 1024 <= 48 * 1024) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDev) dev = 0;
+  static thread_local std::vector<std::pair<const void *, size_t>> done[kMaxDev];
+  for (auto &e : done[dev])
+    if (e.first == reinterpret_cast<const void *>(fn) && e.second >= dyn_bytes) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_bytes);
+  done[dev].emplace_back(reinterpret_cast<const void *>(fn), dyn_bytes);
+}
+
 template <int DTQ>
 static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const void *q, int n_q, int n_kv,
                         const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind, float *scores,
@@ -557,8 +576,7 @@ static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const
   switch (tile) {
 #define KVR_SC(T)                                                                                        \
   case T:                                                                                                \
-    if (smem > 48 * 1024)                                                                                \
-      cudaFuncSetAttribute(sd1_score_kernel<DTQ, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    ensure_dyn_smem(sd1_score_kernel<DTQ, T>, smem);                                                    \
     {                                                                                                    \
       cudaLaunchConfig_t cfg{};                                                                          \
       cfg.gridDim = grid;                                                                                \

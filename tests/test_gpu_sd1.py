@@ -137,6 +137,22 @@ def test_tile_scores_and_selection_bit_exact(kind, tile, g):
         np.testing.assert_allclose(qp[b].cpu().numpy(), S.transform(qf[b], kind), rtol=0, atol=0)
 
 
+def test_select_large_row_static_plus_dynamic_shared_memory():
+    """8192 tiles in a row with k_sel 256: the selection stages the row's
+    scores in shared memory and needs more than 48 KB together with the
+    kernel's static shared memory; the launcher raises the limit."""
+    nt, tile, k_sel = 8192, 32, 256
+    rng = np.random.default_rng(9)
+    k = rng.standard_normal((1, nt * tile, 1, 128)).astype(F32)
+    v = rng.standard_normal(k.shape).astype(F32)
+    st = K().Sd1Store(1, 1, nt, tile, "hadamard", DEV)
+    K().sd1_encode(st, t(k), t(v))
+    q = t(rng.standard_normal((1, 4, 128)).astype(F32))
+    scores = K().sd1_tile_scores(st, q).cpu().numpy()
+    sel, _, _ = K().sd1_select(st, q, k_sel, 100, 200)
+    assert np.array_equal(sel.cpu().numpy()[0, 0], S.select_tiles(scores[0, 0], k_sel, 100, 200))
+
+
 def test_select_more_than_available_and_empty():
     st, k, v, q = _store(3, 5)
     sel, sc, _ = K().sd1_select(st, t(q), 8)
