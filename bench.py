@@ -478,6 +478,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the configs[2] batched measurement")
+    ap.add_argument("--batched-only", action="store_true",
+                    help="run only the configs[2] batched measurement (one GPU; for profiling)")
     ap.add_argument("--cpu-sample", type=int, default=8, help="layers timed for the CPU baseline")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -506,6 +508,13 @@ def main():
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
         emit(line)
+        return
+
+    if args.batched_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        g = torch.Generator(device=dev).manual_seed(1234)
+        emit({"batched": run_batched(dev, g, measured_peak_hbm()[0])})
         return
 
     if world > 1:
