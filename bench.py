@@ -183,7 +183,8 @@ def run_batched(dev, g, peak):
            "frac": round(gbs / peak, 4), "select_us": round(ms_sel * 1e3, 2), "attend_us": round(ms_att * 1e3, 2),
            "select_bytes": sel_b, "attend_bytes": att_b,
            "select_gbs": round(sel_b / (ms_sel / 1e3) / 1e9, 1), "attend_gbs": round(att_b / (ms_att / 1e3) / 1e9, 1),
-           "kernels": "sd1_score_kernel (popcount tile scores + top-k, streams the window into L2) -> "
+           "kernels": "sd1_score_flat_kernel (popcount tile scores over equal (row, tile) ranges + top-k, "
+                      "streams the window into L2) -> "
                       "attn_rows_kernel (mma.sync pieces)"}
     del stores, wins, sels
     torch.cuda.empty_cache()

@@ -7,6 +7,8 @@
 // reference's design: the GQA-group mean of the post-RoPE query scores fixed
 // tiles (modules/kvr_retrieval.py:270, 291-315) and a per-KV-head top-k keeps
 // the best ones (modules/kvr_retrieval.py:370-392).
+#include <cstdlib>
+#include <cstring>
 #include <utility>
 #include <vector>
 
@@ -264,6 +266,44 @@ struct SelectArgs {
   RowPrefetch rows;        // optional (k[s] null = none): exact rows prefetched into L2
 };
 
+
+// Selection of one (b, h) row by the whole block (NT threads): the k_sel
+// largest scores outside [ex_t0, ex_t1) as unique keys (score desc, index
+// asc), written as indices + tile_base; -1 past the row's tile count.
+template <int NT>
+__device__ void select_row(const float *scores, int64_t row, int64_t n_tiles, const SelectArgs &sa,
+                           unsigned char *dyn_smem) {
+  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn_smem);
+  unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn_smem + align_up(sizeof(TopkSmem), 16));
+  const float *srow = scores + row * n_tiles;
+  const int64_t ex0 = sa.ex_t0, ex1 = sa.ex_t1;
+  const int kk = (int)(n_tiles < sa.k_sel ? n_tiles : sa.k_sel);
+  if (kk > 0) {
+    if (n_tiles <= kSelectSmemScores) {
+      // one pass over L2 into shared memory; the radix passes then stay on chip
+      float *row_s = reinterpret_cast<float *>(dyn_smem + align_up(sizeof(TopkSmem), 16) + select_cand_bytes(sa.k_sel));
+      for (int64_t i = threadIdx.x; i < n_tiles; i += NT)
+        row_s[i] = (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i);
+      __syncthreads();
+      if (kk <= 32) {
+        unsigned long long *lists = tsm.lists;
+        block_topk_warp32<NT>(row_s, n_tiles, kk, lists, cand);
+      } else {
+        block_topk<NT>([&](int64_t i) -> float { return row_s[i]; }, n_tiles, kk, cand, tsm);
+      }
+    } else {
+      block_topk<NT>(
+          [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i); }, n_tiles, kk,
+          cand, tsm);
+    }
+  }
+  for (int j = threadIdx.x; j < sa.k_sel; j += NT) {
+    const bool ok = j < kk;
+    sa.sel[row * sa.k_sel + j] = ok ? (int32_t)(key_index(cand[j]) + sa.tile_base) : -1;
+    if (sa.sel_scores) sa.sel_scores[row * sa.k_sel + j] = ok ? key_score(cand[j]) : -INFINITY;
+  }
+}
+
 template <int DTQ, int TILE>
 __global__ void __launch_bounds__(256) sd1_score_kernel(
     const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
@@ -434,37 +474,207 @@ __global__ void __launch_bounds__(256) sd1_score_kernel(
   if (!last_s) return;
   __threadfence();
   KVR_TRACE_POINT(0, 3);
-  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn_smem);
-  unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn_smem + align_up(sizeof(TopkSmem), 16));
-  const float *srow = scores + row * n_tiles;
-  const int64_t ex0 = sa.ex_t0, ex1 = sa.ex_t1;
-  const int kk = (int)(n_tiles < sa.k_sel ? n_tiles : sa.k_sel);
-  if (kk > 0) {
-    if (n_tiles <= kSelectSmemScores) {
-      // one pass over L2 into shared memory; the radix passes then stay on chip
-      float *row_s = reinterpret_cast<float *>(dyn_smem + align_up(sizeof(TopkSmem), 16) + select_cand_bytes(sa.k_sel));
-      for (int64_t i = threadIdx.x; i < n_tiles; i += blockDim.x)
-        row_s[i] = (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i);
-      __syncthreads();
-      if (kk <= 32) {
-        unsigned long long *lists = tsm.lists;
-        block_topk_warp32<256>(row_s, n_tiles, kk, lists, cand);
-      } else {
-        block_topk<256>([&](int64_t i) -> float { return row_s[i]; }, n_tiles, kk, cand, tsm);
-      }
-    } else {
-      block_topk<256>(
-          [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(srow + i); }, n_tiles, kk,
-          cand, tsm);
-    }
-  }
-  for (int j = threadIdx.x; j < sa.k_sel; j += blockDim.x) {
-    const bool ok = j < kk;
-    sa.sel[row * sa.k_sel + j] = ok ? (int32_t)(key_index(cand[j]) + sa.tile_base) : -1;
-    if (sa.sel_scores) sa.sel_scores[row * sa.k_sel + j] = ok ? key_score(cand[j]) : -INFINITY;
-  }
+  select_row<256>(scores, row, n_tiles, sa, dyn_smem);
   KVR_TRACE_POINT(0, 4);
   if (threadIdx.x == 0) sa.counters[row] = 0u;
+}
+
+
+// ------------------------------------------------------ flat tile scan ----
+// Batched steps: the CTAs take equal ranges of the flattened (row, tile)
+// space, so every SM gets the same number of tiles whatever the row count
+// (one CTA per row leaves SMs with one row next to SMs with two).  A range
+// covers at most two rows; its warps score tile pairs inside a row segment
+// with the arithmetic of sd1_score_kernel (sd1_score_tile2, one pair loaded
+// ahead), and the CTA whose tiles complete a row (per-row tile counter)
+// selects that row.  q' of each row is formed with sd1_score_kernel's
+// operations.
+
+// One warp: q' = T(mean of the group's query heads) of KV head h into out[128].
+template <int DTQ>
+__device__ void warp_group_qprime(const void *__restrict__ q, int n_q, int g, int64_t b, int h, int kind,
+                                  const float *lee, float *buf, float *out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t qb = (b * n_q + (int64_t)h * g) * kD;
+  if (kind == KVR_DCT) {
+    float xv[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) xv[s] = load1<DTQ>(q, qb + lane + 32 * s);
+    for (int i = 1; i < g; ++i)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) xv[s] = __fadd_rn(xv[s], load1<DTQ>(q, qb + (int64_t)i * kD + lane + 32 * s));
+#pragma unroll
+    for (int s = 0; s < 4; ++s) xv[s] = __fdiv_rn(xv[s], (float)g);
+    dct128_fwd_shfl(xv, lane, lee);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) out[lane + 32 * s] = xv[s];
+    return;
+  }
+  float acc[4], x[4];
+  load4<DTQ>(q, qb + lane * 4, acc);
+  for (int i = 1; i < g; ++i) {
+    load4<DTQ>(q, qb + (int64_t)i * kD + lane * 4, x);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], x[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) acc[r] = __fdiv_rn(acc[r], (float)g);
+  transform128(acc, lane, kind, false, buf, lee);
+  reinterpret_cast<float4 *>(out)[lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// One warp: T q of query head qh (global index) into qprime.
+template <int DTQ>
+__device__ void warp_head_qprime(const void *__restrict__ q, int64_t qh, int kind, const float *lee, float *buf,
+                                 float *__restrict__ qprime) {
+  const int lane = threadIdx.x & 31;
+  if (kind == KVR_DCT) {
+    float xv[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) xv[s] = load1<DTQ>(q, qh * kD + lane + 32 * s);
+    dct128_fwd_shfl(xv, lane, lee);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) qprime[qh * kD + lane + 32 * s] = xv[s];
+    return;
+  }
+  float x[4];
+  load4<DTQ>(q, qh * kD + lane * 4, x);
+  transform128(x, lane, kind, false, buf, lee);
+  reinterpret_cast<float4 *>(qprime + qh * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+}
+
+template <int DTQ, int TILE>
+__global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
+    const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
+    const uint16_t *__restrict__ kscale, int64_t nt_cap, int64_t n_tiles, int kind, int64_t rows,
+    float *__restrict__ scores, float *__restrict__ qprime, SelectArgs sa, int64_t tpc) {
+  __shared__ float lee_s[kD];
+  __shared__ __align__(16) float buf_s[8][2 * kD];
+  __shared__ __align__(16) float qp_s[2][kD];
+  __shared__ int last_rows[2];
+  __shared__ int n_last;
+  extern __shared__ __align__(16) unsigned char dyn_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = n_q / n_kv;
+  const int64_t f0 = (int64_t)blockIdx.x * tpc;
+  const int64_t f1 = min(rows * n_tiles, f0 + tpc);
+  const int64_t r0 = f0 / n_tiles;                 // tpc <= n_tiles: rows r0 and at most r0 + 1
+  const int nrows = (int)((f1 - 1) / n_tiles - r0) + 1;
+  // segment 0: tiles [st0, st0 + n0) of row r0; segment 1: tiles [0, n1) of row r0 + 1
+  const int st0 = (int)(f0 - r0 * n_tiles);
+  const int n0 = (int)(min(f1, (r0 + 1) * n_tiles) - f0);
+  const int n1 = nrows == 2 ? (int)(f1 - (r0 + 1) * n_tiles) : 0;
+  const int pairs0 = (int)((n0 + 1) / 2), n_pairs = pairs0 + (int)((n1 + 1) / 2);
+  load_lee(lee_s);
+  // the CTA holding tile 0 of a row streams that row's exact K/V rows into L2
+  // for the attention kernel that follows (a hint: no ordering needed)
+  for (int sl = 0; sl < nrows; ++sl) {
+    if (sl == 0 && st0 != 0) continue;
+    const int64_t r = r0 + sl, b = r / n_kv;
+    const int h = (int)(r - b * n_kv);
+#pragma unroll 1
+    for (int s = 0; s < 2; ++s) {
+      if (sa.rows.k[s] == nullptr) continue;
+      const int64_t base = b * sa.rows.batch_stride[s] + (int64_t)h * kD;
+      for (int64_t i = threadIdx.x; i < sa.rows.n[s]; i += blockDim.x) {
+        const int64_t off = base + i * sa.rows.tok_stride;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.rows.k[s] + off), "r"(kD * 2) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sa.rows.v[s] + off), "r"(kD * 2) : "memory");
+      }
+    }
+  }
+  constexpr int TPL = TILE / 32;  // tokens per lane
+  // pair p -> (row slot, first tile, last tile of its segment)
+  auto pair_at = [&](int p, int &sl, int &t_first, int &t_end) {
+    sl = p < pairs0 ? 0 : 1;
+    t_first = sl == 0 ? st0 + 2 * p : 2 * (p - pairs0);
+    t_end = sl == 0 ? st0 + n0 : n1;
+  };
+  uint4 kb[2][TPL];
+  uint16_t ks[2][4];
+  auto load_pair = [&](int sl, int t_first, int t_end, uint4 (&kbd)[2][TPL], uint16_t (&ksd)[2][4]) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int t = min(t_first + u, t_end - 1);  // a lone last tile is scored twice, stored once
+      const int64_t tix = (r0 + sl) * nt_cap + t;
+      const uint4 *src = reinterpret_cast<const uint4 *>(kbits + tix * TILE * 4);
+#pragma unroll
+      for (int r = 0; r < TPL; ++r) kbd[u][r] = __ldg(src + lane + 32 * r);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) ksd[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
+    }
+  };
+  int p = warp, sl = 0, t_first = 0, t_end = 0;
+  if (p < n_pairs) {
+    pair_at(p, sl, t_first, t_end);
+    load_pair(sl, t_first, t_end, kb, ks);
+  }
+  // q is read, and anything written, after the previous kernel has finished
+  griddep_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
+  __syncthreads();  // Lee factors
+  if (warp < nrows) {
+    const int64_t r = r0 + warp, b = r / n_kv;
+    warp_group_qprime<DTQ>(q, n_q, g, b, (int)(r - b * n_kv), kind, lee_s, buf_s[warp], qp_s[warp]);
+  } else if (warp >= 2 && qprime != nullptr) {
+    // per-head T q for the attention kernel (warps 2..7), from the CTA holding
+    // the row's tile 0
+    for (int it = warp - 2; it < 2 * g; it += 6) {
+      const int s2 = it / g, i = it - s2 * g;
+      if (s2 >= nrows || (s2 == 0 && st0 != 0)) continue;
+      const int64_t r = r0 + s2, b = r / n_kv;
+      warp_head_qprime<DTQ>(q, (b * n_q + (r - b * n_kv) * g + i), kind, lee_s, buf_s[warp], qprime);
+    }
+  }
+  __syncthreads();
+  while (p < n_pairs) {  // warp-uniform
+    const int pn = p + 8;
+    uint4 kbn[2][TPL];
+    uint16_t ksn[2][4];
+    if (pn < n_pairs) {
+      int sln, tfn, ten;
+      pair_at(pn, sln, tfn, ten);
+      load_pair(sln, tfn, ten, kbn, ksn);
+    }
+    float sc[2];
+    sd1_score_tile2<TILE>(qp_s[sl], kb, ks, lane, sc);
+    if (lane == 0) {
+      const int64_t r = r0 + sl;
+      scores[r * n_tiles + t_first] = sc[0];
+      if (t_first + 1 < t_end) scores[r * n_tiles + t_first + 1] = sc[1];
+    }
+    p = pn;
+    if (p < n_pairs) {
+      pair_at(p, sl, t_first, t_end);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int r = 0; r < TPL; ++r) kb[u][r] = kbn[u][r];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) ks[u][m] = ksn[u][m];
+      }
+    }
+  }
+  // the CTA whose tiles complete a row selects it
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    int nl = 0;
+    for (int s2 = 0; s2 < nrows; ++s2) {
+      const unsigned cnt = (unsigned)(s2 == 0 ? n0 : n1);
+      const unsigned prev = atomicAdd(&sa.counters[r0 + s2], cnt);
+      if (prev + cnt == (unsigned)n_tiles) last_rows[nl++] = s2;
+    }
+    n_last = nl;
+  }
+  __syncthreads();
+  for (int i = 0; i < n_last; ++i) {
+    __threadfence();
+    const int64_t r = r0 + last_rows[i];
+    select_row<256>(scores, r, n_tiles, sa, dyn_smem);
+    if (threadIdx.x == 0) sa.counters[r] = 0u;
+    __syncthreads();
+  }
 }
 
 // ---------------------------------------------------------- tile decode ----
@@ -602,12 +812,63 @@ static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const
   return check_launch("sd1 tile scores");
 }
 
+
+template <int DTQ>
+static int launch_score_flat(int tile, int64_t rows, int64_t tpc, cudaStream_t st, const void *q, int n_q,
+                             int n_kv, const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind,
+                             float *scores, float *qprime, SelectArgs sa) {
+  const size_t smem = select_dyn_smem(sa.k_sel, nt);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)((rows * nt + tpc - 1) / tpc));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  switch (tile) {
+#define KVR_SF(T)                                                                                       \
+  case T:                                                                                               \
+    ensure_dyn_smem(sd1_score_flat_kernel<DTQ, T>, smem);                                               \
+    cudaLaunchKernelEx(&cfg, sd1_score_flat_kernel<DTQ, T>, q, n_q, n_kv, kb, ks, cap, nt, kind, rows,  \
+                       scores, qprime, sa, tpc);                                                        \
+    break;
+    KVR_SF(32)
+    KVR_SF(64)
+    KVR_SF(128)
+#undef KVR_SF
+    default:
+      return set_error(KVR_ENOTSUP, "sd1: tile must be 32, 64 or 128 (got %d)", tile);
+  }
+  return check_launch("sd1 tile scores (flat)");
+}
+
 int sd1_scores_impl(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                     const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, float *scores,
                     float *qprime, SelectArgs sa, int do_select, cudaStream_t st) {
+  const int64_t rows = (int64_t)batch * n_kv;
+  // Batched steps with selection: equal flat ranges of the (row, tile) space,
+  // two CTAs per SM, once that gives every CTA at least 16 tiles and at most
+  // one row's worth (KVR_SD1_SCAN=flat / warps forces a path where valid).
+  {
+    const char *scan = getenv("KVR_SD1_SCAN");
+    const bool force_flat = scan && strcmp(scan, "flat") == 0, force_warps = scan && strcmp(scan, "warps") == 0;
+    const int64_t total = rows * n_tiles;
+    const int64_t ftpc = (total + 295) / 296;
+    if (do_select && sa.vbits == nullptr && n_tiles >= 16 && !force_warps &&
+        (force_flat ? (total > 0 && ftpc <= n_tiles) : (ftpc >= 16 && ftpc <= n_tiles && rows > 1))) {
+      const int64_t t = force_flat && ftpc < 16 ? (n_tiles < 16 ? n_tiles : 16) : ftpc;
+      switch (q_dtype) {
+        case KVR_F32: return launch_score_flat<KVR_F32>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
+        case KVR_F16: return launch_score_flat<KVR_F16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
+        default: return launch_score_flat<KVR_BF16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
+      }
+    }
+  }
   // Tiles per CTA: about one resident wave (2 CTAs per SM) in total, at least
   // 16 (two per warp); each CTA forms q' once for all of its tiles.
-  const int64_t rows = (int64_t)batch * n_kv;
   int64_t cph = 296 / (rows > 0 ? rows : 1);
   const int64_t max_cph = (n_tiles + kScoreTilesPerCta - 1) / kScoreTilesPerCta;
   cph = cph < 1 ? 1 : (cph > max_cph ? max_cph : cph);

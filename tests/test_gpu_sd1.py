@@ -153,6 +153,61 @@ def test_select_large_row_static_plus_dynamic_shared_memory():
     assert np.array_equal(sel.cpu().numpy()[0, 0], S.select_tiles(scores[0, 0], k_sel, 100, 200))
 
 
+@pytest.mark.parametrize("kind,tile,g,B,n_kv,nt,k_sel,ex,dtype", [
+    ("hadamard", 64, 4, 3, 4, 40, 7, (3, 9), torch.bfloat16),
+    ("dct", 64, 4, 2, 8, 100, 16, (0, 0), torch.float32),
+    ("dct", 32, 8, 2, 4, 57, 12, (50, 57), torch.float16),
+    ("hadamard", 128, 1, 2, 4, 21, 40, (0, 0), torch.float32),  # k_sel > n_tiles
+    ("dct", 64, 2, 5, 8, 17, 5, (2, 4), torch.bfloat16),        # ranges start mid-row, odd segments
+])
+def test_flat_scan_bit_exact(monkeypatch, kind, tile, g, B, n_kv, nt, k_sel, ex, dtype):
+    """The flat scan (equal (row, tile) ranges, up to two rows per CTA, the CTA
+    completing a row selects it) gives the oracle's selection and the same
+    q' and selection as the per-row scan."""
+    st, k, v, q = _store(17, nt, tile, kind, n_kv=n_kv, n_q=n_kv * g, B=B)
+    qt = t(q).to(dtype)
+    qf = qt.float().cpu().numpy()
+    res = {}
+    for scan in ("flat", "warps"):
+        monkeypatch.setenv("KVR_SD1_SCAN", scan)
+        res[scan] = [x.cpu().numpy() for x in K().sd1_select(st, qt, k_sel, *ex)]
+    monkeypatch.delenv("KVR_SD1_SCAN")
+    for a, b_ in zip(res["flat"], res["warps"]):
+        assert bits_eq(a, b_) if a.dtype != np.int32 else np.array_equal(a, b_)
+    sel, sc, qp = res["flat"]
+    for b in range(B):
+        qprime = S.transform(S.q_group_mean_f32(qf[b], n_kv), kind)
+        for h in range(n_kv):
+            want = S.tile_scores(qprime[h], st.kbits[b, h, :nt].cpu().numpy().view(np.uint32),
+                                 st.kscale[b, h, :nt].cpu().numpy())
+            exp_sel = S.select_tiles(want, k_sel, *ex)
+            assert np.array_equal(sel[b, h, :len(exp_sel)], exp_sel) and (sel[b, h, len(exp_sel):] == -1).all()
+            assert bits_eq(sc[b, h, :len(exp_sel)], want[exp_sel])
+        np.testing.assert_allclose(qp[b], S.transform(qf[b], kind), rtol=0, atol=0)
+
+
+def test_flat_scan_in_batched_decode_step():
+    """At a batched shape the decode step takes the flat scan by itself; its
+    selection equals the per-row scan's and the output equals the attention
+    over that selection."""
+    B, n_kv, g, nt, k_sel = 40, 8, 4, 240, 16  # 76800 row-tiles: 260 tiles per CTA, ranges cross rows
+    st, k, v, q = _store(23, nt, 64, "dct", n_kv=n_kv, n_q=n_kv * g, B=B)
+    qt = t(q).to(torch.bfloat16)
+    rng = np.random.default_rng(5)
+    win = t(rng.standard_normal((B, 96, n_kv, 128)).astype(np.float16))
+    sel_w, _, qp = K().sd1_select(st, qt, k_sel)
+    sel_f = torch.empty_like(sel_w)
+    step = K().sd1_decode_step(st, qt, k_sel, win, win, 96, sel_out=sel_f)
+    os.environ["KVR_SD1_SCAN"] = "warps"
+    try:
+        sel_ref, _, qp_ref = K().sd1_select(st, qt, k_sel)
+    finally:
+        del os.environ["KVR_SD1_SCAN"]
+    assert torch.equal(sel_w, sel_ref) and torch.equal(sel_f, sel_ref) and torch.equal(qp, qp_ref)
+    want = K().sd1_attend(st, qt, qp_ref, sel_ref, win, win, 96)
+    assert torch.equal(step, want)
+
+
 def test_select_more_than_available_and_empty():
     st, k, v, q = _store(3, 5)
     sel, sc, _ = K().sd1_select(st, t(q), 8)
