@@ -786,7 +786,8 @@ struct RowState {
 };
 
 // Online softmax of a piece's scores s[mt][r] (token 16 mt + g (+8 for r >= 2),
-// head 2t + (r & 1)), then P (hi, lo) into the warp's staging.
+// head 2t + (r & 1); log2 units: the scores carry a factor log2(e)), then P
+// (hi, lo) into the warp's staging.
 __device__ __forceinline__ void row_softmax(RowState &st, float (&s)[2][4], __half *Ph, int nt, int g_heads) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -803,14 +804,14 @@ __device__ __forceinline__ void row_softmax(RowState &st, float (&s)[2][4], __ha
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
     const float mn = fmaxf(st.m[e], pm);
-    al[e] = st.m[e] == -INFINITY ? 0.0f : expf(st.m[e] - mn);
+    al[e] = st.m[e] == -INFINITY ? 0.0f : exp2f(st.m[e] - mn);
     float ps = 0.0f;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int r = e + 2 * rr;
-        const float p = s[mt][r] == -INFINITY ? 0.0f : expf(s[mt][r] - mn);
+        const float p = s[mt][r] == -INFINITY ? 0.0f : exp2f(s[mt][r] - mn);
         s[mt][r] = p;
         ps += p;
       }
@@ -841,7 +842,7 @@ __device__ __forceinline__ void row_softmax(RowState &st, float (&s)[2][4], __ha
 
 // O^T += V^T P^T for one 16-token step: A fragments of m-tile j from the
 // packed pairs (token 2t, 2t+1) and (2t+8, 2t+9) of channel 16g + 2j (+1).
-template <typename AF>
+template <bool PLO, typename AF>
 __device__ __forceinline__ void row_pv_step(RowState &st, const __half *Ph, int k0, AF a_frag) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const uint32_t *P32 = reinterpret_cast<const uint32_t *>(Ph);
@@ -854,37 +855,47 @@ __device__ __forceinline__ void row_pv_step(RowState &st, const __half *Ph, int 
     uint32_t a0, a1, a2, a3;
     a_frag(j, a0, a1, a2, a3);
     hmma16816(st.o[j], a0, a1, a2, a3, bh0, bh1);
-    hmma16816(st.o[j], a0, a1, a2, a3, bl0, bl1);
+    if (PLO) hmma16816(st.o[j], a0, a1, a2, a3, bl0, bl1);
   }
 }
 
 // Exact piece: nt fp16 rows at kp / vp (token stride ts, elements).
+template <bool PLO>
 __device__ __forceinline__ void row_piece_exact(RowState &st, const uint4 *QB, __half *Ph, int nt, const __half *kp,
                                                 const __half *vp, int64_t ts, float sscale, int g_heads) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  // scores: rows g, g + 8 of both m-tiles, channels 32p + 8t .. +8
+  // scores: rows g, g + 8 of both m-tiles, channels 32p + 8t .. +8; both
+  // m-tiles' rows in one round trip, four independent MMA chains (m-tile x
+  // hi / lo part of q)
+  uint4 kr[2][2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      const int r = 16 * mt + g + 8 * rh;
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+        kr[mt][rh][p] = r < nt ? __ldg(reinterpret_cast<const uint4 *>(kp + r * ts + 32 * p + 8 * t))
+                               : make_uint4(0u, 0u, 0u, 0u);
+    }
+  float ch[2][4] = {}, cl[2][4] = {};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint4 q0 = QB[(2 * p) * 32 + lane], q1 = QB[(2 * p + 1) * 32 + lane];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const uint4 &ka = kr[mt][0][p], &kb = kr[mt][1][p];
+      hmma16816(ch[mt], ka.x, kb.x, ka.y, kb.y, q0.x, q0.y);
+      hmma16816(cl[mt], ka.x, kb.x, ka.y, kb.y, q0.z, q0.w);
+      hmma16816(ch[mt], ka.z, kb.z, ka.w, kb.w, q1.x, q1.y);
+      hmma16816(cl[mt], ka.z, kb.z, ka.w, kb.w, q1.z, q1.w);
+    }
+  }
   float s[2][4];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    uint4 ka[4], kb[4];
-    const int r0 = 16 * mt + g, r1 = r0 + 8;
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      ka[p] = r0 < nt ? __ldg(reinterpret_cast<const uint4 *>(kp + r0 * ts + 32 * p + 8 * t)) : make_uint4(0u, 0u, 0u, 0u);
-      kb[p] = r1 < nt ? __ldg(reinterpret_cast<const uint4 *>(kp + r1 * ts + 32 * p + 8 * t)) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint4 q0 = QB[(2 * p) * 32 + lane], q1 = QB[(2 * p + 1) * 32 + lane];
-      hmma16816(c, ka[p].x, kb[p].x, ka[p].y, kb[p].y, q0.x, q0.y);
-      hmma16816(c, ka[p].x, kb[p].x, ka[p].y, kb[p].y, q0.z, q0.w);
-      hmma16816(c, ka[p].z, kb[p].z, ka[p].w, kb[p].w, q1.x, q1.y);
-      hmma16816(c, ka[p].z, kb[p].z, ka[p].w, kb[p].w, q1.z, q1.w);
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) s[mt][r] = c[r] * sscale;
-  }
+    for (int r = 0; r < 4; ++r) s[mt][r] = (ch[mt][r] + cl[mt][r]) * sscale;
   // V rows of the 4 tokens 2t, 2t+1, 2t+8, 2t+9 of each step, channels 16g .. +16
   uint4 vr[2][4][2];
 #pragma unroll
@@ -905,7 +916,7 @@ __device__ __forceinline__ void row_piece_exact(RowState &st, const uint4 *QB, _
       const int e = j & 3;
       return e == 0 ? u.x : (e == 1 ? u.y : (e == 2 ? u.z : u.w));
     };
-    row_pv_step(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    row_pv_step<PLO>(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
       a0 = __byte_perm(word(0, j), word(1, j), 0x5410);
       a1 = __byte_perm(word(0, j), word(1, j), 0x7632);
       a2 = __byte_perm(word(2, j), word(3, j), 0x5410);
@@ -915,11 +926,33 @@ __device__ __forceinline__ void row_piece_exact(RowState &st, const uint4 *QB, _
   __syncwarp();
 }
 
-// sd1 piece: 32 token rows of 4 bit words at kw / vw; SC = the warp's staged
-// negated scales (-ks [128], -vs [128], fp16).
+// sd1 piece: 32 token rows of 4 bit words at kw / vw, the tile's fp16 scales
+// at ksg / vsg; SC = the warp's staging for the negated scales.
+template <bool PLO>
 __device__ __forceinline__ void row_piece_sd1(RowState &st, const uint4 *QB, __half *Ph, const uint32_t *kw,
-                                              const uint32_t *vw, const __half *SC, float sscale, int g_heads) {
+                                              const uint32_t *vw, const uint16_t *ksg, const uint16_t *vsg,
+                                              __half *SC, float sscale, int g_heads) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  // one round trip: the scales, the K words of rows g, g+8 of both m-tiles
+  // and the V words (word g / 2) of tokens 2t, 2t+1, 2t+8, 2t+9 of each step
+  const uint2 ksr = __ldg(reinterpret_cast<const uint2 *>(ksg) + lane);
+  const uint2 vsr = __ldg(reinterpret_cast<const uint2 *>(vsg) + lane);
+  uint32_t kwd[2][2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh)
+#pragma unroll
+      for (int p = 0; p < 4; ++p) kwd[mt][rh][p] = __ldg(kw + (16 * mt + g + 8 * rh) * 4 + p);
+  uint32_t vwd[2][4];
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) vwd[k][i] = __ldg(vw + (16 * k + 2 * t + (i & 1) + (i >> 1) * 8) * 4 + (g >> 1));
+  // negated scales into the warp's staging, then gathered in fragment order
+  reinterpret_cast<uint2 *>(SC)[lane] = make_uint2(ksr.x ^ 0x80008000u, ksr.y ^ 0x80008000u);
+  reinterpret_cast<uint2 *>(SC + kD)[lane] = make_uint2(vsr.x ^ 0x80008000u, vsr.y ^ 0x80008000u);
+  __syncwarp();
   // -ks pairs (32p + 8s + t, +16) and (32p + 8s + 4 + t, +16) of k-step 2p + s
   uint32_t ksp[8][2];
 #pragma unroll
@@ -928,37 +961,26 @@ __device__ __forceinline__ void row_piece_sd1(RowState &st, const uint4 *QB, __h
     ksp[kk][0] = h2u(__halves2half2(SC[c0], SC[c0 + 16]));
     ksp[kk][1] = h2u(__halves2half2(SC[c0 + 4], SC[c0 + 20]));
   }
+  float ch[2][4] = {}, cl[2][4] = {};
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int p = kk >> 1, c0 = 8 * (kk & 1) + t;
+    const uint4 q = QB[kk * 32 + lane];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const uint32_t a0 = sgn_pair(ksp[kk][0], kwd[mt][0][p] << (15 - c0));
+      const uint32_t a1 = sgn_pair(ksp[kk][0], kwd[mt][1][p] << (15 - c0));
+      const uint32_t a2 = sgn_pair(ksp[kk][1], kwd[mt][0][p] << (11 - c0));
+      const uint32_t a3 = sgn_pair(ksp[kk][1], kwd[mt][1][p] << (11 - c0));
+      hmma16816(ch[mt], a0, a1, a2, a3, q.x, q.y);
+      hmma16816(cl[mt], a0, a1, a2, a3, q.z, q.w);
+    }
+  }
   float s[2][4];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    uint32_t wa[4], wb[4];
-    const int r0 = 16 * mt + g, r1 = r0 + 8;
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      wa[p] = __ldg(kw + r0 * 4 + p);
-      wb[p] = __ldg(kw + r1 * 4 + p);
-    }
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int p = kk >> 1, c0 = 8 * (kk & 1) + t;
-      const uint32_t a0 = sgn_pair(ksp[kk][0], wa[p] << (15 - c0));
-      const uint32_t a1 = sgn_pair(ksp[kk][0], wb[p] << (15 - c0));
-      const uint32_t a2 = sgn_pair(ksp[kk][1], wa[p] << (11 - c0));
-      const uint32_t a3 = sgn_pair(ksp[kk][1], wb[p] << (11 - c0));
-      const uint4 q = QB[kk * 32 + lane];
-      hmma16816(c, a0, a1, a2, a3, q.x, q.y);
-      hmma16816(c, a0, a1, a2, a3, q.z, q.w);
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) s[mt][r] = c[r] * sscale;
-  }
-  // V words (word g / 2) of tokens 2t, 2t+1, 2t+8, 2t+9 of each step
-  uint32_t vwd[2][4];
-#pragma unroll
-  for (int k = 0; k < 2; ++k)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) vwd[k][i] = __ldg(vw + (16 * k + 2 * t + (i & 1) + (i >> 1) * 8) * 4 + (g >> 1));
+    for (int r = 0; r < 4; ++r) s[mt][r] = (ch[mt][r] + cl[mt][r]) * sscale;
   // -vs of channels 16g + 2j (even) and + 1 (odd), both halves
   uint32_t vse[8], vso[8];
 #pragma unroll
@@ -973,7 +995,7 @@ __device__ __forceinline__ void row_piece_sd1(RowState &st, const uint4 *QB, __h
   for (int k = 0; k < 2; ++k) {
     const uint32_t x01 = __byte_perm(vwd[k][0], vwd[k][1], sel);
     const uint32_t x23 = __byte_perm(vwd[k][2], vwd[k][3], sel);
-    row_pv_step(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    row_pv_step<PLO>(st, Ph, 16 * k, [&](int j, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
       a0 = sgn_pair(vse[j], x01 << (15 - 2 * j));
       a1 = sgn_pair(vso[j], x01 << (14 - 2 * j));
       a2 = sgn_pair(vse[j], x23 << (15 - 2 * j));
@@ -1010,7 +1032,10 @@ __device__ __forceinline__ float pow2_scale(float amax) {
   return ldexpf(1.0f, 12 - e);
 }
 
-template <int TILE>
+// PLO: the P.V products also take the fp16 low part of P (fp32 and fp16
+// outputs, partial rows); a bf16 output rounds at 2^-9, far above the 2^-12
+// of the high part alone.
+template <int TILE, bool PLO>
 __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   extern __shared__ __align__(128) unsigned char sm[];
   const int slot = blockIdx.x, h = blockIdx.y;
@@ -1065,7 +1090,8 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
     if (any_tiles) QBt[kk * 32 + lane] = q_bfrag(Qps + g * kD, kk, lane, true, qst);
   }
   __syncthreads();
-  const float sx = a.inv_scale / qsx, stl = a.inv_scale / qst;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float sx = a.inv_scale * kLog2e / qsx, stl = a.inv_scale * kLog2e / qst;
 
   RowState st;
   st.m[0] = st.m[1] = -INFINITY;
@@ -1141,7 +1167,7 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
       if (left <= 0) continue;
       const int nt = (int)(left < kPiece ? left : kPiece);
       const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD + t0 * a.tok_stride[seg];
-      row_piece_exact(st, QBx, Ph, nt, reinterpret_cast<const __half *>(a.k[seg]) + base,
+      row_piece_exact<PLO>(st, QBx, Ph, nt, reinterpret_cast<const __half *>(a.k[seg]) + base,
                       reinterpret_cast<const __half *>(a.v[seg]) + base, a.tok_stride[seg], sx, a.g);
     } else {
       if (!parked) park();
@@ -1150,14 +1176,9 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
       const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
       if (tsel < 0) continue;
       const int64_t tix = row * a.nt_cap + tsel;
-      // negated scales of the tile into the warp's staging
-      const uint2 ksr = __ldg(reinterpret_cast<const uint2 *>(a.kscale + tix * kD) + lane);
-      const uint2 vsr = __ldg(reinterpret_cast<const uint2 *>(a.vscale + tix * kD) + lane);
-      reinterpret_cast<uint2 *>(SC)[lane] = make_uint2(ksr.x ^ 0x80008000u, ksr.y ^ 0x80008000u);
-      reinterpret_cast<uint2 *>(SC + kD)[lane] = make_uint2(vsr.x ^ 0x80008000u, vsr.y ^ 0x80008000u);
-      __syncwarp();
       const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
-      row_piece_sd1(st, QBt, Ph, a.kbits + w0, a.vbits + w0, SC, stl, a.g);
+      row_piece_sd1<PLO>(st, QBt, Ph, a.kbits + w0, a.vbits + w0, a.kscale + tix * kD, a.vscale + tix * kD, SC,
+                         stl, a.g);
     }
   }
   if (!parked) park();  // only exact pieces (or none): the sd1 sum is zero
@@ -1169,11 +1190,13 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   float *Fl = reinterpret_cast<float *>(sm + RowSmem::kFl);
   float *Fs = reinterpret_cast<float *>(sm + RowSmem::kFs);
   if (g == 0) {
+    // maxima back to natural units (the CTA fold and the merge use expf)
+    constexpr float kLn2 = 0.6931471805599453f;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      Fm[warp * kMaxG + 2 * t + e] = st.m[e];
+      Fm[warp * kMaxG + 2 * t + e] = st.m[e] * kLn2;
       Fl[warp * kMaxG + 2 * t + e] = st.l[e];
-      Fs[warp * kMaxG + 2 * t + e] = m_park[e];
+      Fs[warp * kMaxG + 2 * t + e] = m_park[e] * kLn2;
     }
   }
   store_acc(Ftr + warp * kMaxG * kD);
@@ -1311,12 +1334,12 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
   // per-device attribute cache (the attribute is per function and device)
   static thread_local int cached_dev = -1;
   static thread_local bool smem_set[3] = {false, false, false};
-  static thread_local bool rows_set[3] = {};
+  static thread_local bool rows_set[3][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != cached_dev) {
     smem_set[0] = smem_set[1] = smem_set[2] = false;
-    for (auto &r : rows_set) r = false;
+    for (auto &r : rows_set) r[0] = r[1] = false;
     cached_dev = dev;
   }
   cudaLaunchConfig_t cfg{};
@@ -1337,12 +1360,13 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
     cfg.attrs = attr;                                                                              \
     cfg.numAttrs = pdl ? 1 : 0;                                                                    \
     if (a.pipelined) {                                                                             \
-      if (!rows_set[T / 64]) {                                                                     \
-        cudaFuncSetAttribute(attn_rows_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
-                             (int)smem);                                                           \
-        rows_set[T / 64] = true;                                                                   \
+      const bool plo = a.out_dt != KVR_BF16 || a.partial_out != nullptr;                           \
+      auto *fn = plo ? attn_rows_kernel<T, true> : attn_rows_kernel<T, false>;                     \
+      if (!rows_set[T / 64][plo]) {                                                                \
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);          \
+        rows_set[T / 64][plo] = true;                                                              \
       }                                                                                            \
-      if (cudaLaunchKernelEx(&cfg, attn_rows_kernel<T>, a) != cudaSuccess) return check_launch(what); \
+      if (cudaLaunchKernelEx(&cfg, fn, a) != cudaSuccess) return check_launch(what);               \
     } else if (cudaLaunchKernelEx(&cfg, attn_kernel<T>, a) != cudaSuccess) {                       \
       return check_launch(what);                                                                   \
     }                                                                                              \

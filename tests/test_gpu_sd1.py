@@ -342,6 +342,39 @@ def test_attend_batched_rows_vs_oracle(kind, tile, nw, ntl, g, B, n_kv, nt, k_se
     assert worst < 1e-5, worst
 
 
+@pytest.mark.parametrize("kind,tile,g,out_dtype", [("dct", 64, 4, torch.bfloat16), ("hadamard", 32, 8, torch.float16)])
+def test_attend_batched_rows_16bit_output_vs_oracle(kind, tile, g, out_dtype):
+    """16-bit outputs on the batched path (for bf16 the P.V products take only
+    the fp16 high part of P: the output's own rounding is far coarser):
+    relative error (norm of the group's rows) within 2e-3 of the float64
+    oracle, and elementwise the fp32-output result rounded to the output type,
+    up to half an ulp of that type plus 5e-4 of the row maximum."""
+    B, n_kv, nt, k_sel, nw, ntl = 16, 8, 24, 16, 256, 9
+    assert _batched_path_taken(B, n_kv, nw, ntl, k_sel)
+    st, k, v, q = _store(41, nt, tile, kind, n_kv=n_kv, n_q=n_kv * g, B=B)
+    rng = np.random.default_rng(8)
+    win_k = rng.standard_normal((B, nw + 4, n_kv, 128)).astype(np.float16)
+    win_v = rng.standard_normal((B, nw + 4, n_kv, 128)).astype(np.float16)
+    tail_k = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    tail_v = rng.standard_normal((B, tile, n_kv, 128)).astype(np.float16)
+    qt = t(q).to(torch.bfloat16)
+    qn = qt.float().cpu().numpy()
+    sel, _, qp = K().sd1_select(st, qt, k_sel)
+    args = (st, qt, qp, sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl)
+    out = K().sd1_attend(*args, out_dtype=out_dtype).float().cpu().numpy()
+    full = K().sd1_attend(*args, out_dtype=torch.float32).cpu().numpy()
+    half_ulp = np.abs(full) * (2.0 ** -8 if out_dtype == torch.bfloat16 else 2.0 ** -11)
+    assert (np.abs(out - full) <= half_ulp + 5e-4 * np.abs(full).max(-1, keepdims=True)).all()
+    s = sel.cpu().numpy()
+    worst = 0.0
+    for b in range(B):
+        for h in range(n_kv):
+            want = _oracle_attend(qn, st, b, h, s[b, h], win_k, win_v, nw, tail_k, tail_v, ntl, kind, g)
+            got = out[b, h * g:(h + 1) * g]
+            worst = max(worst, np.linalg.norm(got - want) / np.linalg.norm(want))
+    assert worst < 2e-3, worst
+
+
 def test_attend_batched_rows_partial_merge_like_whole():
     """Sequence split on the batched path: two halves of the selection as
     partial rows, merged by kvr_lse_merge, equal the whole attention."""
