@@ -192,16 +192,25 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
   }
   __syncthreads();
 
-  // ---- phase 2: per channel chain (kv, c): scale = fp16(mean |x|), sigma-delta bits
+  // ---- phase 2: per channel chain (kv, c): scale = fp16(mean |x|), sigma-delta bits.
+  // A thread's CPT chains (tid + i * NT) are independent: they advance together,
+  // so their dependent sigma-delta steps overlap.
   const int64_t out_tile = ((int64_t)b * n_kv + h) * nt_cap + tile0 + tile_in;
+  constexpr int CPT = 2 * kD / NT;  // chains per thread: 4, 2, 1 for tiles of 32, 64, 128
+  const float4 *Xc[CPT];
+  uint32_t *bs[CPT];
+  float s_[CPT], ns_[CPT], e_[CPT];
+  uint32_t mine[CPT];  // lane L keeps the word of token 32m + L
 #pragma unroll
-  for (int chain = tid; chain < 2 * kD; chain += NT) {
+  for (int i = 0; i < CPT; ++i) {
+    const int chain = tid + i * NT;
     const int kvc = chain / kD, c = chain % kD;  // a warp covers 32 consecutive channels of one kv
-    const float4 *Xc = reinterpret_cast<const float4 *>(X + (kvc * kD + c) * LD);
+    Xc[i] = reinterpret_cast<const float4 *>(X + (kvc * kD + c) * LD);
+    bs[i] = bits_s + kvc * TILE * 4 + (c >> 5);
     float acc = 0.0f;
 #pragma unroll
     for (int q = 0; q < TILE / 4; ++q) {
-      const float4 t = Xc[q];
+      const float4 t = Xc[i][q];
       acc = __fadd_rn(acc, fabsf(t.x));
       acc = __fadd_rn(acc, fabsf(t.y));
       acc = __fadd_rn(acc, fabsf(t.z));
@@ -209,23 +218,31 @@ __global__ void __launch_bounds__(2 * TILE) sd1_encode_kernel(
     }
     const float mean = __fmul_rn(acc, 1.0f / TILE);
     const __half s16 = __float2half_rn(fminf(mean, 65504.0f));
-    const float s = __half2float(s16), ns = -s;
+    s_[i] = __half2float(s16);
+    ns_[i] = -s_[i];
+    e_[i] = 0.0f;
+    mine[i] = 0u;
     (kvc == 0 ? kscale : vscale)[out_tile * kD + c] = __half_as_ushort(s16);
-    uint32_t *bs = bits_s + kvc * TILE * 4 + (c >> 5);
-    float e = 0.0f;
-    uint32_t mine = 0;  // lane L keeps the word of token 32m + L
+  }
 #pragma unroll
-    for (int q = 0; q < TILE / 4; ++q) {
-      const float4 t = Xc[q];
-      const float tv[4] = {t.x, t.y, t.z, t.w};
+  for (int q = 0; q < TILE / 4; ++q) {
+    float tv[CPT][4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float u = __fadd_rn(tv[r], e);
+    for (int i = 0; i < CPT; ++i) {
+      const float4 t = Xc[i][q];
+      tv[i][0] = t.x; tv[i][1] = t.y; tv[i][2] = t.z; tv[i][3] = t.w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = 4 * q + r;
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) {
+        const float u = __fadd_rn(tv[i][r], e_[i]);
         const bool bit = u >= 0.0f;
-        e = __fsub_rn(u, bit ? s : ns);
+        e_[i] = __fsub_rn(u, bit ? s_[i] : ns_[i]);
         const uint32_t w = __ballot_sync(0xffffffffu, bit);
-        mine = lane == ((4 * q + r) & 31) ? w : mine;
-        if (((4 * q + r) & 31) == 31) bs[((4 * q + r) - 31 + lane) * 4] = mine;
+        mine[i] = lane == (j & 31) ? w : mine[i];
+        if ((j & 31) == 31) bs[i][(j - 31 + lane) * 4] = mine[i];
       }
     }
   }
