@@ -272,7 +272,10 @@ KVR_API int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *ou
  * looks up the array's device address with that device current; make that
  * first call before any stream capture.  All calls share the one array:
  * calls that overlap on the GPU (other streams, other host threads) race and
- * must be serialised by the caller.  Arguments as kvr_decode_attn. */
+ * must be serialised by the caller.  The array's address is kept per device
+ * ordinal for the life of the process: after cudaDeviceReset, or from a
+ * different CUDA context on the same device, that address is stale and this
+ * entry point must not be called again.  Arguments as kvr_decode_attn. */
 KVR_API size_t kvr_decode_attn_noalloc_max_scratch_bytes(void);
 KVR_API int kvr_decode_attn_noalloc(const void *q, int q_dtype, int n_q, int n_kv, int d,
                                     const void *k0, const void *v0, int kdt0, int vdt0, int64_t n0,

@@ -1282,13 +1282,6 @@ static AttnWs attn_ws_layout(void *base, int batch, int n_kv, int units, int g) 
   return w;
 }
 
-int sd1_fused_launch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint16_t *win_k,
-                     const uint16_t *win_v, int64_t win_cap, int64_t n_win, const uint16_t *tail_k,
-                     const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits, const uint16_t *kscale,
-                     const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
-                     int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
-                     int32_t *sel_out, unsigned *err, cudaStream_t st);
-
 int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint32_t *kbits,
                        const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
                        int64_t ex_t0, int64_t ex_t1, int64_t tile_base, int32_t *sel, float *sel_scores,
@@ -1531,20 +1524,6 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
               workspace_bytes, need);
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_sd1_decode_step: workspace must be 256-byte aligned");
   char *p = reinterpret_cast<char *>(workspace);
-  // Optional clustered single-kernel path (KVR_SD1_PATH=fused).  Measured on
-  // B200 at the config-1 shape it is slower than the select + attend pair
-  // (about 32 vs 26 us per layer), so the pair is the default.
-  const char *path = getenv("KVR_SD1_PATH");
-  if ((path && strcmp(path, "fused") == 0) && valid_dtype(q_dtype) && valid_dtype(out_dtype) && out && kbits &&
-      kscale && vbits && vscale && n_tiles <= nt_cap && n_win <= win_cap && n_tail <= tile && n_q / n_kv * n_kv == n_q &&
-      (kind == KVR_HADAMARD || kind == KVR_DCT) && (tile == 32 || tile == 64 || tile == 128)) {
-    const int rc = sd1_fused_launch(q, q_dtype, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v,
-                                    n_tail, kbits, kscale, vbits, vscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
-                                    ex_t1, scale, out, out_dtype, sel_out, reinterpret_cast<unsigned *>(p),
-                                    as_cuda(stream));
-    if (rc != KVR_ENOTSUP) return rc;
-    clear_error();
-  }
   const size_t a_bytes = align_up(kvr_sd1_attend_workspace_bytes(batch, n_q, n_kv, tile, k_sel, n_win, n_tail), 256);
   const size_t s_bytes = align_up((size_t)batch * n_kv * (size_t)(n_tiles > 0 ? n_tiles : 1) * 4, 256);
   const size_t sel_bytes = align_up((size_t)batch * n_kv * (k_sel > 0 ? k_sel : 1) * 4, 256);

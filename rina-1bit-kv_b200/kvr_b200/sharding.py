@@ -97,25 +97,41 @@ class SeqSplitDecoder:
         self.n_win = n_win
 
     def local_candidates(self, q, k_sel):
-        sel, sc, qp = K.sd1_select(self.store, q, k_sel, tile_base=self.tile_base)
-        return sel, sc, qp
+        """Local top `k_sel` of this rank's tiles: (sel (B, H, k_sel) int32
+        global tile indices, scores fp32, q').  A rank that owns fewer than
+        k_sel tiles (or none) pads its list with index -1 / score -inf, so
+        every rank passes tensors of the same shape to the all-gather."""
+        return K.sd1_select(self.store, q, k_sel, tile_base=self.tile_base)
+
+    def local_partial(self, q, qp, local_sel):
+        """Log-sum-exp partial rows (B, n_q, d+2) over the selected tiles this
+        rank owns (local indices, -1 = not here) plus, on the window rank, the
+        window."""
+        wk = wv = None
+        if self.window is not None and self.n_win:
+            wk, wv = self.window
+        return K.sd1_attend(self.store, q, qp, local_sel, wk, wv, self.n_win if wk is not None else 0, partial=True)
+
+    def n_local_tiles(self):
+        return self.store.n_tiles
 
     def step(self, q, k_sel, out_dtype=None):
         """q (B, n_q, d) on this rank's GPU (same on every rank) -> (B, n_q, d)."""
         q = q if q.dim() == 3 else q.unsqueeze(0)
         B, n_q, d = q.shape
-        k_loc = max(1, min(k_sel, self.store.n_tiles)) if self.store.n_tiles else 1
-        sel, sc, qp = self.local_candidates(q, k_loc)
-        all_sc = torch.stack(self.comm.all_gather(sc))
-        all_idx = torch.stack(self.comm.all_gather(sel.long()))
+        sel, sc, qp = self.local_candidates(q, k_sel)
+        all_sc = torch.stack(self.comm.all_gather(sc.contiguous()))
+        all_idx = torch.stack(self.comm.all_gather(sel.long().contiguous()))
         gsel = global_selection(all_sc, all_idx, k_sel)
+        n_loc = self.n_local_tiles()
         local = gsel - self.tile_base
-        mine = (gsel >= 0) & (local >= 0) & (local < self.store.n_tiles)
+        mine = (gsel >= 0) & (local >= 0) & (local < n_loc)
         local = torch.where(mine, local, torch.full_like(local, -1)).to(torch.int32).contiguous()
-        wk = wv = None
-        if self.window is not None and self.n_win:
-            wk, wv = self.window
-        part = K.sd1_attend(self.store, q, qp, local, wk, wv, self.n_win if wk is not None else 0, partial=True)
-        parts = torch.stack(self.comm.all_gather(part))       # (N, B, n_q, d+2)
-        merged = K.lse_merge(parts.reshape(parts.shape[0], B * n_q, d + 2), out_dtype or q.dtype)
+        part = self.local_partial(q, qp, local)
+        parts = torch.stack(self.comm.all_gather(part.contiguous()))       # (N, B, n_q, d+2)
+        merged = self.merge(parts.reshape(parts.shape[0], B * n_q, d + 2), out_dtype or q.dtype)
         return merged.view(B, n_q, d), gsel
+
+    def merge(self, parts, out_dtype):
+        """(N, rows, d+2) gathered partial rows -> (rows, d) (kvr_lse_merge)."""
+        return K.lse_merge(parts, out_dtype)

@@ -137,3 +137,100 @@ def test_tile_ranges_and_head_shard():
     assert head_shard(8, 32, 1, 4) == (slice(2, 4), slice(8, 16))
     with pytest.raises(ValueError):
         head_shard(8, 32, 0, 3)
+
+
+# ---- SeqSplitDecoder.step itself, with the per-rank GPU work done by the oracle
+
+
+class _OracleSplit:
+    """Stands in for the GPU parts of SeqSplitDecoder (local selection,
+    partial attention, merge) with the sd1 oracle, so that the class's own
+    exchange logic runs on gloo ranks."""
+
+    @staticmethod
+    def make(rank, world, nt, k_sel, comm):
+        from kvr_b200.sharding import SeqSplitDecoder, tile_ranges
+
+        rng = np.random.default_rng(11)
+        k = rng.standard_normal((nt * TILE, 128)).astype(np.float32)
+        v = rng.standard_normal((nt * TILE, 128)).astype(np.float32)
+        enc = S.encode(k, v, TILE, "hadamard")
+        base, n = tile_ranges(nt, world)[rank]
+
+        class Dec(SeqSplitDecoder):
+            def local_candidates(self, q, kk):
+                qp = S.transform(S.q_group_mean_f32(q[0].numpy(), 1), "hadamard")[0]
+                scores = S.tile_scores(qp, enc["kbits"][base:base + n], enc["kscale"][base:base + n]) if n else []
+                loc = S.select_tiles(np.asarray(scores, np.float32), min(kk, n)) if n else np.zeros(0, np.int64)
+                sc = torch.full((1, 1, kk), float("-inf"))
+                ix = torch.full((1, 1, kk), -1, dtype=torch.int32)
+                sc[0, 0, :len(loc)] = torch.from_numpy(np.asarray(scores, np.float32)[loc])
+                ix[0, 0, :len(loc)] = torch.from_numpy((base + loc).astype(np.int32))
+                return ix, sc, None
+
+            def n_local_tiles(self):
+                return n
+
+            def local_partial(self, q, qp, local_sel):
+                owned = [base + int(t) for t in local_sel[0, 0] if t >= 0]
+                dk = S.decode_tiles(enc["kbits"][owned], enc["kscale"][owned], "hadamard").reshape(-1, 128)
+                dv = S.decode_tiles(enc["vbits"][owned], enc["vscale"][owned], "hadamard").reshape(-1, 128)
+                return torch.from_numpy(_partial(q[0].numpy(), dk, dv)).unsqueeze(0)
+
+            def merge(self, parts, out_dtype):
+                return torch.from_numpy(_merge(parts.numpy()))
+
+        return Dec(None, base, comm), enc
+
+
+def _split_worker(rank, world, port, nt, k_sel, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    from kvr_b200.sharding import TorchDistComm
+
+    try:
+        dec, _ = _OracleSplit.make(rank, world, nt, k_sel, TorchDistComm())
+        q = torch.from_numpy(np.random.default_rng(3).standard_normal((1, G, 128)).astype(np.float32))
+        out, gsel = dec.step(q, k_sel)
+        results[rank] = (gsel[0, 0].numpy(), out[0].numpy())
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        results[rank] = ("error", repr(e))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nt,world", [(9, 2), (5, 3), (2, 3)])
+def test_seq_split_decoder_with_fewer_tiles_than_k(nt, world):
+    """Ranks owning fewer than k_sel tiles (uneven, or none at all) still pass
+    equal shapes to the all-gathers, and the result equals the one-process
+    selection and attention."""
+    k_sel = 6
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        res = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_split_worker, args=(r, world, port, nt, k_sel, res)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            if p.is_alive():
+                p.kill()
+                pytest.fail("gloo rank hung")
+        res = dict(res)
+    rng = np.random.default_rng(11)
+    k = rng.standard_normal((nt * TILE, 128)).astype(np.float32)
+    v = rng.standard_normal((nt * TILE, 128)).astype(np.float32)
+    enc = S.encode(k, v, TILE, "hadamard")
+    q = np.random.default_rng(3).standard_normal((G, 128)).astype(np.float32)
+    qp = S.transform(S.q_group_mean_f32(q, 1), "hadamard")[0]
+    want_sel = S.select_tiles(S.tile_scores(qp, enc["kbits"], enc["kscale"]), min(k_sel, nt))
+    dk = S.decode_tiles(enc["kbits"][want_sel], enc["kscale"][want_sel], "hadamard").reshape(-1, 128)
+    dv = S.decode_tiles(enc["vbits"][want_sel], enc["vscale"][want_sel], "hadamard").reshape(-1, 128)
+    want = _merge(_partial(q, dk, dv)[None])
+    for r in range(world):
+        assert not isinstance(res[r][0], str), res[r]
+        got_sel = res[r][0]
+        assert np.array_equal(got_sel[:len(want_sel)], want_sel)
+        assert np.all(got_sel[len(want_sel):] == -1)
+        np.testing.assert_allclose(res[r][1], want, rtol=1e-9, atol=1e-9)
