@@ -1,22 +1,32 @@
-"""Benchmark of the compressed-KV decode hot path (sd1 1-bit codec) on B200.
+"""Benchmark of the compressed-KV decode hot path on B200.
 
-Workload: Llama-3-8B attention shapes — 32 layers,
+Headline: Llama-3-8B attention shapes — 32 layers,
 32 query / 8 KV heads, head_dim 128 — batch 1 at 32768-token context: the last
 512 tokens sit in the fp16 window, the other 32256 are encoded (DCT, tiles of
-64) into the 1-bit store; each decode step selects the top 16 tiles per KV
+64) into the 1-bit sd1 store; each decode step selects the top 16 tiles per KV
 head and attends window + selected tiles, layer after layer.  Synthetic data
 of the config-0 distribution stands in for a random-init model's K/V and
-queries (there is no checkpoint or dataset here).
+queries (there is no checkpoint or dataset here).  A "step" = one decode step
+of all 32 layers; the 32 layers' stores and windows (~395 MB) exceed L2
+(126 MB), so every step reads its inputs from HBM.  With --gpus N (torchrun)
+the headline is weak-scaled (each rank serves its own sequence's heads).
 
-A "step" = one decode step of all 32 layers (2 kernels per layer).  The 32
-layers' stores and windows (~395 MB) exceed L2 (126 MB), so every step reads
-its inputs from HBM.  With --gpus N (torchrun) the KV heads are sharded: each
-rank holds Hkv/N heads of a batch of N sequences (weak scaling, no
-collective); value counts sequence-steps of the whole job.
+Secondary objects of the same JSON line:
+  c2_heads_sharded  configs[2] strong scaling: a fixed job of 32 sequences x
+                    16384 context, the 8 KV heads split over the N ranks;
+  c4_seq_split      configs[4]: 70B attention shapes, 131072 context split by
+                    tile range over the N ranks, NCCL candidate all-gather +
+                    partial (m, l, o) all-gather, per-phase timing;
+  int4w_c1          the reference's own codec (int4 K + W-predicted V + int2
+                    residual) at the configs[1] shapes the reference arm times,
+                    through RetrievalIndex.retrieve_topk + decode attention;
+  encode_sweep      configs[3]: Hadamard / DCT x tile 32/64/128 x batch x seq;
+  prefill_scores    tcgen05 tile scoring of a 4096-query prefill chunk;
+  cpu_baseline      the reference algorithm's CPU path on the host cores.
 
---impl reference times the reference algorithm's CPU path (the int4w
+--impl reference times the reference algorithm's CPU decode path (the int4w
 retrieve_topk token branch + window/retrieved softmax, restated in
-oracle/int4w_ref_cpu.py) on the host cores at the same shapes.
+oracle/int4w_ref_cpu.py) on the host cores, whole 32-layer steps.
 """
 import argparse
 import json
@@ -35,16 +45,26 @@ CTX, WIN, TILE, KSEL, KIND = 32768, 512, 64, 16, "dct"
 T_STORED = CTX - WIN                      # 32256
 NT = T_STORED // TILE                     # 504
 METRIC = "decode-attn steps/s + achieved HBM GB/s at 32k ctx; KV encode tokens/s"
+UNIT = "sequence decode-steps/s (32 layers per step)"
 
 
-def step_bytes_per_layer(hkv, batch):
-    """Algorithmic bytes of one layer-step (sd1): scan all K bits + K scales,
+def sd1_bytes(batch, hkv, hq, nt, ksel, win, tile=TILE):
+    """Algorithmic bytes of one sd1 layer-step: scan all K bits + K scales,
     re-read the selected K tiles, selected V bits + scales, window K and V in
-    fp16, q in and out in bf16."""
-    kb, sc = TILE * D // 8, 2 * D
-    select = batch * hkv * NT * (kb + sc)
-    attend = batch * hkv * (KSEL * 2 * (kb + sc) + WIN * D * 2 * 2) + 2 * batch * hkv * (HQ // HKV) * D * 2
+    fp16, q in and out in bf16.  Returns (select, attend)."""
+    kb, sc = tile * D // 8, 2 * D
+    select = batch * hkv * nt * (kb + sc)
+    attend = batch * hkv * (ksel * 2 * (kb + sc) + win * D * 2 * 2) + 2 * batch * hq * D * 2
     return select, attend
+
+
+def int4w_bytes(n_stored, top_k, win, hkv=HKV, hq=HQ):
+    """Algorithmic bytes of one int4w layer-step: every stored token's packed
+    K (d/2 B per head), the selected tokens' packed K of all heads (the V
+    prediction mixes heads) and int2 residuals, W (fp32, read once), the
+    window K/V in fp16, q/out fp32."""
+    return (hkv * n_stored * D // 2 + hkv * top_k * (hkv * D // 2 + D // 4) + 4 * (hkv * D) ** 2
+            + hkv * D * 4 + hkv * win * D * 2 * 2 + 2 * hq * D * 4)
 
 
 def clocks_sampler():
@@ -86,141 +106,88 @@ def clocks_summary(proc, dev_index):
     return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def measured_peak_hbm():
+def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        return float(json.load(open(p))["hbm_gbs"]), "measured"
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured (MEASURED_PEAKS.json)"
     except (OSError, KeyError, ValueError):
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
-# ----------------------------------------------------------------- GPU arm --
+def cfg0_kv(torch, dev, g, batch, n, hkv, dtype):
+    """Config-0 distribution: K ~ N(0,1) x per-channel log-normal scale with 4
+    outlier channels x20 per head, V ~ N(0,1)."""
+    scale = torch.exp(torch.randn(hkv, D, device=dev, generator=g))
+    idx = torch.randint(0, D, (hkv, 4), device=dev, generator=g)
+    scale.scatter_(1, idx, scale.gather(1, idx) * 20)
+    k = (torch.randn(batch, n, hkv, D, device=dev, generator=g) * scale).to(dtype)
+    v = torch.randn(batch, n, hkv, D, device=dev, generator=g).to(dtype)
+    return k, v
 
-# batched decode stress, batch 32 x 16384 context, window
-# 256, top 16 tiles of 64 (Llama-3-8B attention shapes, 32 q / 8 KV heads).
-B2, CTX2, WIN2, L2_LAYERS = 32, 16384, 256, 4
-NT2 = (CTX2 - WIN2) // TILE  # 252
+
+class Dist:
+    def __init__(self, world, rank, dev):
+        self.world, self.rank, self.dev = world, rank, dev
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([float(x)], device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
 
-def run_batched(dev, g, peak):
-    """Secondary measurement on configs[2] at one GPU: the decode step of a
-    layer over a batch of 32 sequences, timed as a CUDA graph over 4 layers
-    (4 x 127 MB of stores + windows, larger than L2), then the select and
-    attend kernels alone.  Bytes are the algorithmic bytes of the step: the
-    select reads every stored tile's K bits + K scales, the attention the
-    selected tiles' K/V bits and scales, the fp16 window rows, q and out."""
+def graph_time(torch, fn, stream, reps, warm=3):
+    """Capture fn() in a CUDA graph and return ms per replay (CUDA events on
+    the replay stream, after `warm` untimed replays)."""
+    with torch.cuda.stream(stream):
+        fn()
+        fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream, capture_error_mode="thread_local"):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            gr.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+# ---------------------------------------------------------- headline (c1) --
+
+def run_headline(args, dist_, peak_hbm):
     import torch
 
     from kvr_b200 import kernels as K
     from kvr_b200 import _native as N
+    from kvr_b200.kvr_retrieval import RetrievalIndex
+    from kvr_b200.kvr_window import WindowBuffer
 
-    stores, wins = [], []
-    for li in range(L2_LAYERS):
-        scale = torch.exp(torch.randn(HKV, D, device=dev, generator=g))
-        idx = torch.randint(0, D, (HKV, 4), device=dev, generator=g)
-        scale.scatter_(1, idx, scale.gather(1, idx) * 20)
-        k = (torch.randn(B2, NT2 * TILE, HKV, D, device=dev, generator=g) * scale).to(torch.bfloat16)
-        v = torch.randn(B2, NT2 * TILE, HKV, D, device=dev, generator=g).to(torch.bfloat16)
-        st = K.Sd1Store(B2, HKV, NT2, TILE, KIND, dev)
-        K.sd1_encode(st, k, v)
-        stores.append(st)
-        del k, v
-        wins.append((torch.randn(B2, WIN2, HKV, D, device=dev, generator=g).half(),
-                     torch.randn(B2, WIN2, HKV, D, device=dev, generator=g).half()))
-    q = torch.randn(L2_LAYERS, B2, HQ, D, device=dev, generator=g).to(torch.bfloat16)
-    out = torch.empty_like(q)
-    ws = torch.zeros(N.call("kvr_sd1_workspace_bytes", B2, HQ, HKV, NT2, TILE, KSEL, WIN2, 0) + 256,
-                     dtype=torch.uint8, device=dev)
-    stream = torch.cuda.Stream(device=dev)
-
-    def timed(fn, reps=30):
-        with torch.cuda.stream(stream):
-            fn()
-            fn()
-        torch.cuda.synchronize()
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            fn()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                gr.replay()
-            e0.record(stream)
-            for _ in range(reps):
-                gr.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps / L2_LAYERS
-
-    def step():
-        for li in range(L2_LAYERS):
-            wk, wv = wins[li]
-            K.sd1_decode_step(stores[li], q[li], KSEL, wk, wv, WIN2, out=out[li], ws=ws)
-
-    ms_step = timed(step)
-    sels = [K.sd1_select(stores[li], q[li], KSEL) for li in range(L2_LAYERS)]
-
-    def sel_only():
-        for li in range(L2_LAYERS):
-            K.sd1_select(stores[li], q[li], KSEL)
-
-    def att_only():
-        for li in range(L2_LAYERS):
-            s_, _, qp = sels[li]
-            wk, wv = wins[li]
-            K.sd1_attend(stores[li], q[li], qp, s_, wk, wv, WIN2, out_dtype=torch.bfloat16)
-
-    ms_sel, ms_att = timed(sel_only), timed(att_only)
-    kb, sc = TILE * D // 8, D * 2
-    sel_b = B2 * HKV * NT2 * (kb + sc)
-    att_b = B2 * HKV * (KSEL * 2 * (kb + sc) + WIN2 * D * 2 * 2) + 2 * B2 * HQ * D * 2
-    gbs = (sel_b + att_b) / (ms_step / 1e3) / 1e9
-    res = {"workload": "configs[2] batched decode stress: batch 32 x 16384 context, window 256, "
-                       "top 16 tiles of 64, dct, Llama-3-8B attention shapes",
-           "layers_in_graph": L2_LAYERS, "us_per_layer": round(ms_step * 1e3, 2),
-           "sequence_layer_steps_per_s": round(B2 / (ms_step / 1e3), 1),
-           "bytes_per_layer": sel_b + att_b, "hbm_gbs": round(gbs, 1), "peak": peak,
-           "frac": round(gbs / peak, 4), "select_us": round(ms_sel * 1e3, 2), "attend_us": round(ms_att * 1e3, 2),
-           "select_bytes": sel_b, "attend_bytes": att_b,
-           "select_gbs": round(sel_b / (ms_sel / 1e3) / 1e9, 1), "attend_gbs": round(att_b / (ms_att / 1e3) / 1e9, 1),
-           "kernels": "sd1_score_flat_kernel (popcount tile scores over equal (row, tile) ranges + top-k, "
-                      "streams the window into L2) -> "
-                      "attn_rows_kernel (mma.sync pieces)"}
-    del stores, wins, sels
-    torch.cuda.empty_cache()
-    return res
-
-
-def run_gpu(args, rank, world, local_rank):
-    import torch
-
-    from kvr_b200 import kernels as K
-    from kvr_b200 import _native as N
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    hkv = HKV // world            # heads owned by this rank
-    hq = HQ // world
-    B = world                     # sequences in the job (weak scaling)
+    dev, world, rank = dist_.dev, dist_.world, dist_.rank
+    hkv, hq, B = HKV, HQ, 1          # each rank: one sequence, all heads (weak scaling)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
 
-    def cfg0_kv(n):
-        scale = torch.exp(torch.randn(hkv, D, device=dev, generator=g))
-        idx = torch.randint(0, D, (hkv, 4), device=dev, generator=g)
-        scale.scatter_(1, idx, scale.gather(1, idx) * 20)
-        k = (torch.randn(B, n, hkv, D, device=dev, generator=g) * scale).to(torch.bfloat16)
-        v = torch.randn(B, n, hkv, D, device=dev, generator=g).to(torch.bfloat16)
-        return k, v
-
     # ---- prefill encode of every layer (also the encode measurement)
-    stores, wins = [], []
-    enc_ms = []
+    stores, wins, enc_ms = [], [], []
     st_ev, en_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for li in range(LAYERS):
-        k, v = cfg0_kv(CTX)
+        k, v = cfg0_kv(torch, dev, g, B, CTX, hkv, torch.bfloat16)
         st = K.Sd1Store(B, hkv, NT, TILE, KIND, dev)
-        reps = 3 if li == 0 else 1
-        for r in range(reps):
+        for r in range(3 if li == 0 else 1):
             st.n_tiles = 0
             torch.cuda._sleep(100000)  # the GPU is busy while the host enqueues: events bracket the kernel
             st_ev.record()
@@ -233,10 +200,9 @@ def run_gpu(args, rank, world, local_rank):
         wins.append((k[:, T_STORED:].to(torch.float16).contiguous(), v[:, T_STORED:].to(torch.float16).contiguous()))
         del k, v
     enc_s = statistics.median(enc_ms) / 1e3
-    enc_tok_layer = B * T_STORED / enc_s
     enc_bytes = B * T_STORED * hkv * (2 * D * 2 + 2 * D // 8) + B * hkv * NT * 2 * 2 * D
 
-    # ---- decode step: all layers, q per layer
+    # ---- decode step: all layers, q per layer, CUDA graph
     qs = torch.randn(LAYERS, B, hq, D, device=dev, generator=g).to(torch.bfloat16)
     outs = torch.empty_like(qs)
     need = N.call("kvr_sd1_workspace_bytes", B, hq, hkv, NT, TILE, KSEL, WIN, 0)
@@ -248,150 +214,105 @@ def run_gpu(args, rank, world, local_rank):
             K.sd1_decode_step(stores[li], q_all[li], KSEL, wk, wv, WIN, out=o_all[li], ws=ws)
 
     stream = torch.cuda.Stream(device=dev)
-    torch.cuda.synchronize()
-    graph, mode = None, "eager"
     with torch.cuda.stream(stream):
         for _ in range(2):
             step(qs, outs)
     torch.cuda.synchronize()
-    if not args.no_graph:
-        try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-                step(qs, outs)
-            mode = "cuda_graph"
-        except Exception as e:  # noqa: BLE001 - report and fall back to eager launches
-            print(f"[bench] graph capture failed, eager launches: {e}", file=sys.stderr)
-            graph = None
-            torch.cuda.synchronize()
-
-    def run_once():
-        if graph is not None:
-            graph.replay()
-        else:
-            step(qs, outs)
-
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+        step(qs, outs)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            run_once()
+            graph.replay()
     torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+    dist_.barrier()
     clk = clocks_sampler() if rank == 0 else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
-            run_once()
+            graph.replay()
         e1.record(stream)
     torch.cuda.synchronize()
-    t_ms = e0.elapsed_time(e1)
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([t_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_ms = float(tt.item())
-        dist.barrier()
-    clocks = clocks_summary(clk, local_rank) if rank == 0 else None
+    t_ms = dist_.max(e0.elapsed_time(e1))
+    dist_.barrier()
+    clocks = clocks_summary(clk, torch.cuda.current_device()) if rank == 0 else None
     ms_per_step = t_ms / args.steps
 
-    # ---- per-kernel durations (eager, events on the launching stream)
-    sel_b, att_b = step_bytes_per_layer(hkv, B)
-    qp = torch.empty(B, hq, D, dtype=torch.float32, device=dev)
-    sel = torch.empty(B, hkv, KSEL, dtype=torch.int32, device=dev)
-    sws = torch.zeros(N.call("kvr_sd1_select_workspace_bytes", B, hkv, NT) + 256, dtype=torch.uint8, device=dev)
-    aws = torch.zeros(N.call("kvr_sd1_attend_workspace_bytes", B, hq, hkv, TILE, KSEL, WIN, 0) + 256,
-                      dtype=torch.uint8, device=dev)
-    # each timed launch sits behind a GPU sleep, so the host-side enqueue cost
-    # of the eager call is hidden and the events bracket only the kernel
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    t_sel, t_att = [], []
-    P = N.ptr
-    with torch.cuda.stream(stream):
-        sp = stream.cuda_stream
-        for rep in range(3):
-            for li in range(LAYERS):
-                st = stores[li]
-                wk, wv = wins[li]
-                torch.cuda._sleep(200000)
-                ev[0].record(stream)
-                N.call("kvr_sd1_select", P(qs[li]), N.dtype_code(qs[li]), B, hq, hkv, P(st.kbits), P(st.kscale),
-                       st.nt_cap, st.n_tiles, TILE, N.TRANSFORMS[KIND], KSEL, 0, 0, 0, P(sel), None, P(qp), P(sws),
-                       sws.numel(), sp)
-                ev[1].record(stream)
-                torch.cuda._sleep(200000)
-                ev[2].record(stream)
-                N.call("kvr_sd1_attend", P(qs[li]), N.dtype_code(qs[li]), P(qp), B, hq, hkv, P(wk), P(wv), WIN, WIN,
-                       None, None, 0, P(st.kbits), P(st.kscale), P(st.vbits), P(st.vscale), st.nt_cap, TILE,
-                       N.TRANSFORMS[KIND], P(sel), KSEL, 0.0, P(outs[li]), N.dtype_code(outs[li]), None, P(aws),
-                       aws.numel(), sp)
-                ev[3].record(stream)
-                ev[3].synchronize()
-                if rep:
-                    t_sel.append(ev[0].elapsed_time(ev[1]))
-                    t_att.append(ev[2].elapsed_time(ev[3]))
-    ms_sel, ms_att = statistics.mean(t_sel), statistics.mean(t_att)
+    # ---- each kernel alone: a graph of its 32 launches (one per layer)
+    sel_b, att_b = sd1_bytes(B, hkv, hq, NT, KSEL, WIN)
+    sels = [K.sd1_select(stores[li], qs[li], KSEL) for li in range(LAYERS)]
 
-    # ---- end to end through the public API with pinned host buffers
+    def sel_only():
+        for li in range(LAYERS):
+            K.sd1_select(stores[li], qs[li], KSEL)
+
+    def att_only():
+        for li in range(LAYERS):
+            s_, _, qp = sels[li]
+            wk, wv = wins[li]
+            K.sd1_attend(stores[li], qs[li], qp, s_, wk, wv, WIN, out_dtype=torch.bfloat16)
+
+    ms_sel = graph_time(torch, sel_only, stream, 50) / LAYERS
+    ms_att = graph_time(torch, att_only, stream, 50) / LAYERS
+    del sels
+
+    # ---- end to end through the reference-facing API: RetrievalIndex.attend
+    # per layer, q copied from pinned host memory per layer, output read back
+    # per layer, every step
+    rets, wbufs = [], []
+    for li in range(LAYERS):
+        r = RetrievalIndex(hkv, D, top_k=KSEL * TILE, device=dev, codec="sd1", tile=TILE, transform=KIND)
+        r.calibrate(torch.zeros(1, hkv, D, device=dev))
+        r.store = stores[li]
+        r.n_stored = NT * TILE
+        wb = WindowBuffer(hkv, D, WIN, dev)
+        wb.k.copy_(wins[li][0][0])
+        wb.v.copy_(wins[li][1][0])
+        wb.pos = wb.n = WIN
+        rets.append(r)
+        wbufs.append(wb)
     q_host = qs.cpu().pin_memory()
     o_host = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
-    q_dev = torch.empty_like(qs)
-    e2e_steps = max(3, min(args.steps, 100))
+    e2e_steps = max(3, min(args.steps, 50))
     with torch.cuda.stream(stream):
         for i in range(e2e_steps + 2):
             if i == 2:
                 e0.record(stream)
-            q_dev.copy_(q_host, non_blocking=True)
             for li in range(LAYERS):
-                wk, wv = wins[li]
-                K.sd1_decode_step(stores[li], q_dev[li], KSEL, wk, wv, WIN, out=outs[li], ws=ws)
-            o_host.copy_(outs, non_blocking=True)
+                q_dev = q_host[li, 0].to(dev, non_blocking=True)
+                o = rets[li].attend(q_dev, wbufs[li], out_dtype=torch.bfloat16)
+                o_host[li, 0].copy_(o, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    e2e_ms = dist_.max(e0.elapsed_time(e1) / e2e_steps)
 
-    # ---- tcgen05 prefill tile scoring (secondary line): a 4096-query chunk
-    # of prefill positions scored against layer 0's store (batch-1 stores only)
+    # ---- tcgen05 prefill tile scoring (secondary): a 4096-query chunk of
+    # prefill positions scored against layer 0's store
     prefill = None
-    if B == 1:
-        nq_pf = 4096
-        q_pf = torch.randn(nq_pf, hq, D, device=dev, generator=g).to(torch.bfloat16)
-        for _ in range(3):
-            K.sd1_prefill_scores(stores[0], q_pf)
-        torch.cuda.synchronize()
-        reps = 20
-        e0.record()
-        for _ in range(reps):
-            K.sd1_prefill_scores(stores[0], q_pf)
-        e1.record()
-        torch.cuda.synchronize()
-        pf_ms = e0.elapsed_time(e1) / reps
-        pf_flops = 2.0 * nq_pf * hkv * stores[0].n_tiles * TILE * D
-        pf_peak = None
-        try:
-            pf_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
-            pf_src = "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
-        except (OSError, KeyError, ValueError):
-            pf_peak, pf_src = 1590.0, "fallback"
-        pf_tf = pf_flops / (pf_ms / 1e3) / 1e12
-        prefill = {"kernel": "prefill_scores_kernel (tcgen05.mma kind::f16) + q prep", "queries": nq_pf,
-                   "tokens": stores[0].n_tiles * TILE, "kv_heads": hkv, "ms_per_launch": round(pf_ms, 5),
-                   "flops_per_launch": pf_flops, "achieved": round(pf_tf, 1), "unit": "TFLOP/s",
-                   "peak": pf_peak, "frac": round(pf_tf / pf_peak, 4), "peak_source": pf_src,
-                   "bound": "tensor"}
-        del q_pf
+    _, pf_peak, pf_src = measured_peaks()
+    nq_pf = 4096
+    q_pf = torch.randn(nq_pf, hq, D, device=dev, generator=g).to(torch.bfloat16)
+    for _ in range(3):
+        K.sd1_prefill_scores(stores[0], q_pf)
+    torch.cuda.synchronize()
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        K.sd1_prefill_scores(stores[0], q_pf)
+    e1.record()
+    torch.cuda.synchronize()
+    pf_ms = e0.elapsed_time(e1) / reps
+    pf_flops = 2.0 * nq_pf * hkv * stores[0].n_tiles * TILE * D
+    pf_tf = pf_flops / (pf_ms / 1e3) / 1e12
+    prefill = {"kernel": "prefill_scores_kernel (tcgen05.mma kind::f16) + q prep", "queries": nq_pf,
+               "tokens": stores[0].n_tiles * TILE, "kv_heads": hkv, "ms_per_launch": round(pf_ms, 5),
+               "flops_per_launch": pf_flops, "achieved": round(pf_tf, 1), "unit": "TFLOP/s",
+               "peak": pf_peak, "frac": round(pf_tf / pf_peak, 4), "peak_source": pf_src + " bf16 burst",
+               "bound": "tensor"}
+    del q_pf, rets, wbufs
 
-    peak, peak_kind = measured_peak_hbm()
-    batched = None
-    if world == 1 and not args.no_batched:
-        batched = run_batched(dev, g, peak)
     traffic = None
     try:  # DRAM bytes per launch from the committed ncu capture of this workload
         tj = json.load(open(os.path.join(ROOT, "profiles", "traffic_config1.json")))["dram_bytes_per_launch"]
@@ -401,12 +322,12 @@ def run_gpu(args, rank, world, local_rank):
     dom = "select" if ms_sel >= ms_att else "attend"
     dom_bytes, dom_ms = (sel_b, ms_sel) if dom == "select" else (att_b, ms_att)
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    if world == 1:
-        traffic = tj.get("sd1_score_kernel" if dom == "select" else "attn_kernel")
+    traffic = tj.get("sd1_score_kernel" if dom == "select" else "attn_kernel")
+    step_gbs = LAYERS * layer_bytes / (ms_per_step / 1e3) / 1e9
     res = {
         "metric": METRIC,
-        "value": round(B * 1e3 / ms_per_step, 3),
-        "unit": "sequence decode-steps/s (32 layers per step)",
+        "value": round(world * 1e3 / ms_per_step, 3),
+        "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -416,45 +337,417 @@ def run_gpu(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16 q / fp16 window / 1-bit sd1 codes, fp32 accumulate",
         "data": "synthetic: config-0 K/V distribution (log-normal channel scales, 4 outlier channels x20), N(0,1) q",
-        "config": {"workload": "configs[1] Llama-3-8B attention shapes, decode over sd1 store",
+        "config": {"workload": "configs[1] Llama-3-8B attention shapes, 32-layer decode step over the sd1 store",
                    "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
                    "window": WIN, "tile": TILE, "top_k_tiles": KSEL, "transform": KIND,
-                   "batch_per_rank": B, "kv_heads_per_rank": hkv, "parallelism": f"kv-head shard x{world}",
-                   "l2": "inputs larger than L2 (~395 MB of stores+windows per step)", "launch": mode},
-        "hbm_gbs": round(LAYERS * layer_bytes * world / (ms_per_step / 1e3) / 1e9, 1),
-        "encode": {"layer_tokens_per_s": round(enc_tok_layer * world, 1),
-                   "prefill_tokens_per_s": round(enc_tok_layer * world / LAYERS, 1),
+                   "batch_per_rank": B, "parallelism": f"one sequence per rank x{world} (weak)",
+                   "l2": "inputs larger than L2 (~395 MB of stores+windows per step)", "launch": "cuda_graph"},
+        "hbm_gbs": round(step_gbs * world, 1),
+        "roofline_step": {"bound": "hbm", "what": "whole decode step (32 x (select + attend)), per GPU",
+                          "achieved": round(step_gbs, 1), "peak": peak_hbm, "unit": "GB/s",
+                          "frac": round(step_gbs / peak_hbm, 4), "bytes_per_step": LAYERS * layer_bytes},
+        "encode": {"layer_tokens_per_s": round(B * T_STORED / enc_s * world, 1),
+                   "prefill_tokens_per_s": round(B * T_STORED / enc_s * world / LAYERS, 1),
                    "hbm_gbs": round(enc_bytes / enc_s / 1e9, 1), "ms_per_layer": round(enc_s * 1e3, 4),
                    "tokens_per_layer": B * T_STORED},
-        "roofline": {"bound": "hbm", "kernel": f"sd1_{dom}", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": traffic, "traffic_source": "profiles/traffic_config1.json (ncu)",
+        "roofline": {"bound": "hbm", "kernel": f"sd1_{dom}", "achieved": round(achieved, 1), "peak": peak_hbm,
+                     "unit": "GB/s", "frac": round(achieved / peak_hbm, 4), "traffic": traffic,
+                     "traffic_source": "profiles/traffic_config1.json (ncu)",
                      "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5),
+                     "timing": "CUDA events around a graph of the kernel's 32 launches (one per layer)",
                      "select_ms": round(ms_sel, 5), "attend_ms": round(ms_att, 5),
                      "select_bytes": sel_b, "attend_bytes": att_b},
-        "e2e": {"value": round(B * 1e3 / e2e_ms, 3), "unit": "sequence decode-steps/s (32 layers per step)",
+        "e2e": {"value": round(world * 1e3 / e2e_ms, 3), "unit": UNIT,
                 "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
-                "d2h_bytes_per_step": o_host.numel() * o_host.element_size(), "path": "kvr_b200.kernels eager API"},
+                "d2h_bytes_per_step": o_host.numel() * o_host.element_size(),
+                "path": "RetrievalIndex.attend(q, window) per layer (kvr_b200, codec='sd1'), q H2D and out D2H "
+                        "per layer from pinned host memory, eager launches"},
         "prefill_scores": prefill,
-        "batched": batched,
         "gpu_launches": args.steps * LAYERS * 2,
         "clocks": clocks,
     }
+    del stores, wins
+    torch.cuda.empty_cache()
     return res
+
+
+# ----------------------------------------------- c2: heads sharded, strong --
+B2, CTX2, WIN2 = 32, 16384, 256
+NT2 = (CTX2 - WIN2) // TILE  # 252
+
+
+def run_c2(args, dist_, peak_hbm):
+    """configs[2] strong scaling: the job is 32 sequences x 16384 context with
+    8 KV heads; rank r owns KV heads [r*8/N, (r+1)*8/N) of every sequence
+    (and their query groups).  sd1 heads are independent, so there is no
+    collective.  Timed as a CUDA graph over L layers, L = 4N, so each rank's
+    stores + windows exceed L2 at every N."""
+    import torch
+
+    from kvr_b200 import kernels as K
+    from kvr_b200 import _native as N
+
+    dev, world, rank = dist_.dev, dist_.world, dist_.rank
+    hkv, hq = HKV // world, HQ // world
+    L = 4 * world
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    stores, wins = [], []
+    for li in range(L):
+        k, v = cfg0_kv(torch, dev, g, B2, NT2 * TILE, hkv, torch.bfloat16)
+        st = K.Sd1Store(B2, hkv, NT2, TILE, KIND, dev)
+        K.sd1_encode(st, k, v)
+        stores.append(st)
+        del k, v
+        wins.append((torch.randn(B2, WIN2, hkv, D, device=dev, generator=g).half(),
+                     torch.randn(B2, WIN2, hkv, D, device=dev, generator=g).half()))
+    q = torch.randn(L, B2, hq, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws = torch.zeros(N.call("kvr_sd1_workspace_bytes", B2, hq, hkv, NT2, TILE, KSEL, WIN2, 0) + 256,
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for li in range(L):
+            wk, wv = wins[li]
+            K.sd1_decode_step(stores[li], q[li], KSEL, wk, wv, WIN2, out=out[li], ws=ws)
+
+    reps = 30
+    dist_.barrier()
+    ms_layer = graph_time(torch, step, stream, reps) / L
+    ms_layer_max = dist_.max(ms_layer)
+    sels = [K.sd1_select(stores[li], q[li], KSEL) for li in range(L)]
+
+    def sel_only():
+        for li in range(L):
+            K.sd1_select(stores[li], q[li], KSEL)
+
+    def att_only():
+        for li in range(L):
+            s_, _, qp = sels[li]
+            wk, wv = wins[li]
+            K.sd1_attend(stores[li], q[li], qp, s_, wk, wv, WIN2, out_dtype=torch.bfloat16)
+
+    ms_sel = graph_time(torch, sel_only, stream, reps) / L
+    ms_att = graph_time(torch, att_only, stream, reps) / L
+    sel_b, att_b = sd1_bytes(B2, hkv, hq, NT2, KSEL, WIN2)
+    rank_gbs = (sel_b + att_b) / (ms_layer / 1e3) / 1e9
+    res = {"workload": "configs[2]: 32 sequences x 16384 context, window 256, top 16 tiles of 64, dct, "
+                       "Llama-3-8B attention shapes; KV heads sharded over the ranks (strong scaling)",
+           "n_gpus": world, "kv_heads_per_rank": hkv, "layers_in_graph": L,
+           "us_per_layer": round(ms_layer_max * 1e3, 2),
+           "value": round(B2 / (ms_layer_max / 1e3), 1), "unit": "sequence-layer-steps/s (whole job)",
+           "bytes_per_layer_per_rank": sel_b + att_b, "rank_hbm_gbs": round(rank_gbs, 1), "peak": peak_hbm,
+           "frac": round(rank_gbs / peak_hbm, 4), "select_us": round(ms_sel * 1e3, 2),
+           "attend_us": round(ms_att * 1e3, 2),
+           "select_gbs": round(sel_b / (ms_sel / 1e3) / 1e9, 1), "attend_gbs": round(att_b / (ms_att / 1e3) / 1e9, 1),
+           "collectives": "none (sd1 heads are independent)",
+           "kernels": "sd1_score_flat_kernel -> attn_rows_kernel (rows >= 2/SM) or sd1_score_kernel -> attn_kernel"}
+    del stores, wins, sels
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------- c4: sequence split (70B) --
+L4, HQ4, HKV4, CTX4, WIN4, K4 = 80, 64, 8, 131072, 1024, 32
+NT4 = (CTX4 - WIN4) // TILE  # 2032
+
+
+def run_c4(args, dist_, peak_hbm):
+    """70B attention shapes (80 layers, 64 q / 8 KV heads), one
+    sequence at 131072 context, window 1024, top 32 tiles of 64.  Rank r owns
+    the tiles tile_ranges(2032, N)[r] of every head; the last rank also owns
+    the window.  Per layer: local selection, NCCL all-gather of the
+    candidates, kvr_merge_candidates, partial attention over owned tiles,
+    NCCL all-gather of the (m, l, o) rows, kvr_lse_merge.  At N=1 the
+    one-GPU fused decode step runs instead."""
+    import torch
+
+    from kvr_b200 import kernels as K
+    from kvr_b200 import _native as N
+    from kvr_b200.sharding import SeqSplitDecoder, TorchDistComm, tile_ranges
+
+    dev, world, rank = dist_.dev, dist_.world, dist_.rank
+    base, n_own = tile_ranges(NT4, world)[rank]
+    last = rank == world - 1
+    g = torch.Generator(device=dev).manual_seed(777 + rank)
+    stores, wins = [], []
+    for li in range(L4):
+        k, v = cfg0_kv(torch, dev, g, 1, n_own * TILE, HKV4, torch.bfloat16)
+        st = K.Sd1Store(1, HKV4, n_own, TILE, KIND, dev)
+        K.sd1_encode(st, k, v)
+        stores.append(st)
+        del k, v
+        if last:
+            wins.append((torch.randn(1, WIN4, HKV4, D, device=dev, generator=g).half(),
+                         torch.randn(1, WIN4, HKV4, D, device=dev, generator=g).half()))
+    gq = torch.Generator(device=dev).manual_seed(99)   # same queries on every rank
+    q = torch.randn(L4, 1, HQ4, D, device=dev, generator=gq).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    stream = torch.cuda.Stream(device=dev)
+    sel_b, att_b = sd1_bytes(1, HKV4, HQ4, NT4, K4, WIN4)
+    res = {"workload": "configs[4]: Llama-3-70B attention shapes, 80 layers, 64 q / 8 KV heads, batch 1, "
+                       "131072 context, window 1024, top 32 tiles of 64, dct; tiles split by range over the ranks",
+           "n_gpus": world, "tiles_per_rank": n_own, "layers": L4,
+           "bytes_per_step_job": L4 * (sel_b + att_b)}
+    if world == 1:
+        ws = torch.zeros(N.call("kvr_sd1_workspace_bytes", 1, HQ4, HKV4, NT4, TILE, K4, WIN4, 0) + 256,
+                         dtype=torch.uint8, device=dev)
+
+        def step():
+            for li in range(L4):
+                wk, wv = wins[li]
+                K.sd1_decode_step(stores[li], q[li], K4, wk, wv, WIN4, out=out[li], ws=ws)
+
+        ms = graph_time(torch, step, stream, 20)
+        res.update({"mode": "one GPU, fused decode step (no split)", "ms_per_step": round(ms, 4),
+                    "value": round(1e3 / ms, 2), "unit": "decode-steps/s (80 layers)",
+                    "hbm_gbs": round(L4 * (sel_b + att_b) / (ms / 1e3) / 1e9, 1)})
+        del stores, wins
+        torch.cuda.empty_cache()
+        return res
+
+    comm = TorchDistComm()
+    decs = [SeqSplitDecoder(stores[li], base, comm, window=wins[li] if last else None, n_win=WIN4 if last else 0)
+            for li in range(L4)]
+
+    def step(marks=None):
+        for li in range(L4):
+            o, _ = decs[li].step(q[li], K4, out_dtype=torch.bfloat16, marks=marks)
+            out[li].copy_(o)
+
+    # eager, per-phase CUDA events
+    phases = ["local_select", "candidate_allgather", "local_attend", "partial_allgather", "merge"]
+    acc = {p: 0.0 for p in phases}
+    n_meas = 3
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    torch.cuda.synchronize()
+    dist_.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.c4_steps):
+            step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = dist_.max(e0.elapsed_time(e1) / args.c4_steps)
+    for _ in range(n_meas):
+        evs = []
+
+        def mark(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream())
+            evs.append((name, ev))
+
+        with torch.cuda.stream(stream):
+            st0 = torch.cuda.Event(enable_timing=True)
+            st0.record(stream)
+            step(marks=mark)
+        torch.cuda.synchronize()
+        prev = st0
+        for name, ev in evs:
+            acc[name] += prev.elapsed_time(ev) / n_meas
+            prev = ev
+    breakdown = {p: round(dist_.max(acc[p]), 4) for p in phases}
+    # graph-captured (NCCL collectives inside the graph)
+    graph_ms, graph_err = None, None
+    try:
+        dist_.barrier()
+        gms = graph_time(torch, step, stream, args.c4_steps)
+        graph_ms = dist_.max(gms)
+    except Exception as e:  # noqa: BLE001 - reported in the line, eager number stands
+        graph_err = repr(e)[:200]
+        torch.cuda.synchronize()
+    best = min(x for x in (eager_ms, graph_ms) if x is not None)
+    coll = breakdown["candidate_allgather"] + breakdown["partial_allgather"]
+    res.update({"mode": "sequence split, NCCL all-gathers", "ms_per_step": round(best, 4),
+                "value": round(1e3 / best, 2), "unit": "decode-steps/s (80 layers)",
+                "eager_ms_per_step": round(eager_ms, 4),
+                "graph_ms_per_step": None if graph_ms is None else round(graph_ms, 4),
+                "graph_error": graph_err,
+                "phase_ms_per_step_eager": breakdown,
+                "collective_share_eager": round(coll / max(sum(breakdown.values()), 1e-9), 4),
+                "bytes_crossing_nvlink_per_layer": {"candidates": world * HKV4 * K4 * 8,
+                                                    "partials": world * HQ4 * (D + 2) * 4},
+                "job_hbm_gbs": round(L4 * (sel_b + att_b) / (best / 1e3) / 1e9, 1)})
+    del decs, stores, wins
+    torch.cuda.empty_cache()
+    return res
+
+
+# -------------------------------------------------- int4w at configs[1] --
+
+def run_int4w(args, dist_, peak_hbm):
+    """The reference's own codec at the shapes the reference arm times: 32
+    layers, 32256 stored tokens + 512 window, top_k 1024 tokens per KV head
+    (token branch, chunk_size=0, attractors off), through
+    RetrievalIndex.retrieve_topk and the decode attention over cat(window,
+    retrieved) — the path of modules/kvr_hook.py:250-282."""
+    import torch
+
+    from kvr_b200 import kernels as K
+    from kvr_b200.kvr_retrieval import RetrievalIndex
+
+    dev = dist_.dev
+    g = torch.Generator(device=dev).manual_seed(55)
+    theta = 500000.0
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, device=dev).float() / D))
+    fr = torch.arange(CTX, device=dev).float()[:, None] * inv[None]
+    emb = torch.cat([fr, fr], -1)
+    cos, sin = emb.cos(), emb.sin()
+    top_k = KSEL * TILE
+    rets, wins = [], []
+    enc_ms = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for li in range(LAYERS):
+        k, v = cfg0_kv(torch, dev, g, 1, CTX, HKV, torch.float32)
+        k, v = k[0], v[0]
+        r = RetrievalIndex(HKV, D, top_k=top_k, device=dev, chunk_size=0, codec="int4w")
+        r.set_rotary_tables(cos, sin)
+        r.calibrate(k[:T_STORED], v[:T_STORED])
+        torch.cuda.synchronize()
+        e0.record()
+        r.batch_append(k[:T_STORED], v[:T_STORED])
+        e1.record()
+        torch.cuda.synchronize()
+        enc_ms.append(e0.elapsed_time(e1))
+        rets.append(r)
+        kp = (k[T_STORED:] * cos[T_STORED:, None] + torch.cat([-k[T_STORED:, :, 64:], k[T_STORED:, :, :64]], -1)
+              * sin[T_STORED:, None])
+        wins.append((kp.half(), v[T_STORED:].half()))
+        del k, v
+    qs = torch.randn(LAYERS, HQ, D, device=dev, generator=g)
+    outs = torch.empty_like(qs)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for li in range(LAYERS):
+            wk, wv = wins[li]
+            rk, rv = rets[li].retrieve_topk(qs[li], n_q=HQ)
+            outs[li].copy_(K.decode_attn(qs[li], [(wk, wv), (rk, rv)], out_dtype=torch.float32, n_kv=HKV))
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize()
+    mode = "eager"
+    try:
+        ms = graph_time(torch, step, stream, 20)
+        mode = "cuda_graph"
+    except Exception:  # noqa: BLE001 - a host sync inside the path: time eager
+        torch.cuda.synchronize()
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(10):
+                step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+    b = int4w_bytes(T_STORED, top_k, WIN)
+    gbs = LAYERS * b / (ms / 1e3) / 1e9
+    res = {"workload": "configs[1] shapes, int4w codec (the reference's format), token branch top_k=1024, "
+                       "window 512, 32 layers, fp32 q",
+           "value": round(1e3 / ms, 3), "unit": UNIT, "ms_per_step": round(ms, 4), "launch": mode,
+           "bytes_per_layer": b, "hbm_gbs": round(gbs, 1), "frac": round(gbs / peak_hbm, 4),
+           "encode_ms_per_layer": round(statistics.median(enc_ms), 4),
+           "encode_tokens_per_s": round(T_STORED / (statistics.median(enc_ms) / 1e3), 1),
+           "path": "RetrievalIndex.retrieve_topk + kvr_decode_attn (kvr_b200, codec='int4w')"}
+    del rets, wins
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------- encode sweep --
+
+def run_encode_sweep(args, dist_, peak_hbm):
+    """sd1 encode of bf16 K/V [B, seq, 8, 128] for Hadamard and
+    DCT x tile 32/64/128 x batch x seq.  Bytes per token: read K and V bf16,
+    write sign bits and the per-tile fp16 scales."""
+    import torch
+
+    from kvr_b200 import kernels as K
+
+    dev = dist_.dev
+    g = torch.Generator(device=dev).manual_seed(3)
+    batches = [1, 4, 16] if args.encode_sweep == "full" else [1, 16]
+    seqs = [4096, 32768, 65536] if args.encode_sweep == "full" else [32768]
+    points = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for B in batches:
+        for n in seqs:
+            k, v = cfg0_kv(torch, dev, g, B, n, HKV, torch.bfloat16)
+            for kind in ("hadamard", "dct"):
+                for tile in (32, 64, 128):
+                    st = K.Sd1Store(B, HKV, n // tile, tile, kind, dev)
+                    for _ in range(2):
+                        st.n_tiles = 0
+                        K.sd1_encode(st, k, v)
+                    reps = 5
+                    torch.cuda.synchronize()
+                    e0.record()
+                    for _ in range(reps):
+                        st.n_tiles = 0
+                        K.sd1_encode(st, k, v)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ms = e0.elapsed_time(e1) / reps
+                    tok = B * n
+                    byts = tok * HKV * (2 * D * 2 + 2 * D // 8) + B * HKV * (n // tile) * 2 * 2 * D
+                    gbs = byts / (ms / 1e3) / 1e9
+                    points.append({"transform": kind, "tile": tile, "batch": B, "seq": n, "ms": round(ms, 4),
+                                   "tokens_per_s": round(tok / (ms / 1e3), 1), "hbm_gbs": round(gbs, 1),
+                                   "frac": round(gbs / peak_hbm, 4)})
+                    del st
+            del k, v
+            torch.cuda.empty_cache()
+    return {"workload": "configs[3] sd1 encoder sweep, bf16 K/V, 8 KV heads, head_dim 128",
+            "l2": "inputs >= 4096 x 8 x 128 x 2 x 2 B = 16.8 MB per batch row; the 32k/64k points exceed L2",
+            "points": points}
 
 
 # --------------------------------------------------------------- CPU arm --
 
-def cpu_reference(sample_layers, threads=None):
-    """The reference algorithm's CPU decode path on the host cores, timed per
-    layer on a bounded sample and scaled to a 32-layer step."""
+def cpu_decode_case(torch, C):
+    return C.make_case(seed=0, n_stored=T_STORED, window=WIN, n_kv=HKV, n_q=HQ, d=D)
+
+
+def cpu_reference_steps(steps, budget_s=90.0, threads=None):
+    """Whole 32-layer decode steps of the reference algorithm on the host
+    cores (the 32 layers share one layer's packed data: the CPU path is
+    compute-bound, not cache-bound).  Runs min(steps, what fits the time
+    budget) steps and reports the number it ran."""
     import torch
 
     from oracle import int4w_ref_cpu as C
 
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
-    case = C.make_case(seed=0, n_stored=T_STORED, window=WIN, n_kv=HKV, n_q=HQ, d=D)
+    case = cpu_decode_case(torch, C)
+    top_k = KSEL * TILE
+    C.decode_layer(case, top_k)  # warm-up
+    ts, t_start = [], time.perf_counter()
+    for i in range(max(1, steps)):
+        t0 = time.perf_counter()
+        for li in range(LAYERS):
+            C.decode_layer(case, top_k, q_index=i * LAYERS + li)
+        ts.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s and len(ts) >= 1:
+            break
+    return ts, threads
+
+
+def cpu_baseline(sample_layers, threads=None):
+    """The reference algorithm's CPU decode path on the host cores, timed per
+    layer on a bounded sample and scaled to a 32-layer step; plus the CPU
+    encode (calibrate + batch_append) of one configs[1] layer."""
+    import torch
+
+    from oracle import int4w_ref_cpu as C
+
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    case = cpu_decode_case(torch, C)
     top_k = KSEL * TILE
     C.decode_layer(case, top_k)  # warm-up
     ts = []
@@ -463,12 +756,14 @@ def cpu_reference(sample_layers, threads=None):
         C.decode_layer(case, top_k, q_index=i)
         ts.append(time.perf_counter() - t0)
     layer_s = statistics.median(ts)
-    step_s = layer_s * LAYERS
-    return {"value": round(1.0 / step_s, 5), "unit": "sequence decode-steps/s (32 layers per step)",
-            "cores": threads, "kind": "port",
+    enc = C.encode_layer_timed(seed=1, n=T_STORED, n_kv=HKV, d=D, reps=3)
+    return {"value": round(1.0 / (layer_s * LAYERS), 5), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{sample_layers} single-layer decode steps (int4w retrieve_topk token branch, top_k={top_k}, "
                       f"{T_STORED} stored + {WIN} window tokens, 8 KV / 32 Q heads), median x {LAYERS} layers",
-            "layer_ms": round(layer_s * 1e3, 3)}
+            "layer_ms": round(layer_s * 1e3, 3),
+            "encode": {"what": "calibrate + batch_append of one configs[1] layer (32256 tokens, fp32), median of 3",
+                       "tokens_per_s": round(T_STORED / enc["median_s"], 1),
+                       "calibrate_s": round(enc["calibrate_s"], 4), "batch_append_s": round(enc["append_s"], 4)}}
 
 
 def main():
@@ -477,10 +772,9 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--no-batched", action="store_true", help="skip the configs[2] batched measurement")
-    ap.add_argument("--batched-only", action="store_true",
-                    help="run only the configs[2] batched measurement (one GPU; for profiling)")
+    ap.add_argument("--only", default="", help="comma list of sections to run: headline,c2,c4,int4w,sweep")
+    ap.add_argument("--encode-sweep", default="short", choices=["short", "full", "off"])
+    ap.add_argument("--c4-steps", type=int, default=10)
     ap.add_argument("--cpu-sample", type=int, default=8, help="layers timed for the CPU baseline")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -499,39 +793,60 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_reference(max(args.steps, 3))
-        line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / cb["value"], 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
+        ts, threads = cpu_reference_steps(args.steps)
+        step_s = statistics.median(ts)
+        value = 1.0 / step_s
+        cb = {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": "port",
+              "sample": f"{len(ts)} whole 32-layer decode steps (int4w retrieve_topk token branch, top_k="
+                        f"{KSEL * TILE}, {T_STORED} stored + {WIN} window tokens, 8 KV / 32 Q heads), median"}
+        line = {"metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": args.gpus,
+                "steps": len(ts), "steps_requested": args.steps, "warmup": 1,
+                "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
                 "data": "synthetic: config-0 K/V distribution", "impl": "reference",
                 "config": {"workload": "configs[1] Llama-3-8B attention shapes, int4w reference decode path",
                            "layers": LAYERS, "context": CTX, "window": WIN, "top_k_tokens": KSEL * TILE},
-                "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                "cpu_baseline": cb, "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
         emit(line)
         return
 
-    if args.batched_only:
-        import torch
-        dev = torch.device("cuda", 0)
-        g = torch.Generator(device=dev).manual_seed(1234)
-        emit({"batched": run_batched(dev, g, measured_peak_hbm()[0])})
-        return
-
+    import torch
     if world > 1:
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
-        import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    res = run_gpu(args, rank, world, local_rank)
+    torch.cuda.set_device(local_rank)
+    dist_ = Dist(world, rank, torch.device("cuda", local_rank))
+    peak_hbm, _, _ = measured_peaks()
+    only = set(x for x in args.only.split(",") if x) or {"headline", "c2", "c4", "int4w", "sweep"}
+
+    def section(name, fn):
+        if name not in only:
+            return None
+        try:
+            return fn(args, dist_, peak_hbm)
+        except Exception as e:  # noqa: BLE001 - a failed secondary section is reported, not hidden
+            import traceback
+            traceback.print_exc()
+            return {"error": repr(e)[:400]}
+
+    res = section("headline", run_headline) or {"metric": METRIC, "n_gpus": world}
+    res["c2_heads_sharded"] = section("c2", run_c2)
+    res["c4_seq_split"] = section("c4", run_c4)
+    if world == 1:
+        res["int4w_c1"] = section("int4w", run_int4w)
+        if args.encode_sweep != "off":
+            res["encode_sweep"] = section("sweep", run_encode_sweep)
     if rank == 0:
         if world == 1:
-            res["cpu_baseline"] = cpu_reference(args.cpu_sample)
+            res["cpu_baseline"] = cpu_baseline(args.cpu_sample)
         emit(res)
     if world > 1:
         import torch.distributed as dist
+        dist.barrier()
         dist.destroy_process_group()
 
 

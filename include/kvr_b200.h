@@ -261,6 +261,19 @@ KVR_API int kvr_kmeans(const float *x, int64_t n, int d, int k, int iters, float
 KVR_API int kvr_lse_merge(const float *partials, int P, int n_q, int d, void *out, int out_dtype,
                   kvr_stream_t stream);
 
+/* Global top-k of a sequence split (no reference counterpart: the reference
+ * has no multi-GPU code; the selection rule is its top-k,
+ * modules/kvr_retrieval.py:389-392, with the tie rule score descending then
+ * index ascending).  scores/idx (n_ranks, rows, k_local): every rank's local
+ * candidates (global tile indices, -1 = none) as gathered by an all-gather.
+ * Writes global_sel (rows, k_sel) (optional) and local_sel (rows, k_sel): the
+ * selected tiles in [tile_base, tile_base + n_local) as local indices, -1
+ * elsewhere and past the number of candidates.  At most 4096 candidates per
+ * row. */
+KVR_API int kvr_merge_candidates(const float *scores, const int32_t *idx, int n_ranks, int rows, int k_local,
+                                 int k_sel, int64_t tile_base, int64_t n_local, int32_t *global_sel,
+                                 int32_t *local_sel, kvr_stream_t stream);
+
 /* Allocation-free variant of kvr_decode_attn (no counterpart in the
  * reference).  For callers that cannot allocate device memory — a plugin
  * inside a host that owns the GPU heap, or a path where cudaMalloc would

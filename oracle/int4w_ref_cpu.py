@@ -119,3 +119,48 @@ def decode_layer(c, top_k, q_index=0):
     sc = torch.einsum("hgd, thd -> h g t", qg, k_cat)
     w = torch.softmax(sc / math.sqrt(d), dim=-1)
     return torch.einsum("h g t, t h d -> h g d", w, v_cat).reshape(n_q, d)
+
+
+@torch.no_grad()
+def encode_layer_timed(seed, n, n_kv=8, d=128, reps=3):
+    """The reference's prefill encode of one layer on the host cores:
+    RetrievalIndex.calibrate (absmax scales, W fit with pinv on the first
+    half, residual scales; modules/kvr_retrieval.py:95-122) followed by
+    batch_append (quantise + pack K, V-predict GEMM, int2 residual;
+    :187-207), timed separately; returns medians over `reps` runs."""
+    import time
+
+    g = torch.Generator().manual_seed(seed)
+    scale = torch.exp(torch.randn(n_kv, d, generator=g))
+    k = torch.randn(n, n_kv, d, generator=g) * scale
+    v = torch.randn(n, n_kv, d, generator=g)
+    D_ = n_kv * d
+    cal, app = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        k_scales = k.abs().max(0).values.clamp(min=1e-8)              # :99
+        k2, v2 = k.reshape(n, D_), v.reshape(n, D_)
+        half = n // 2
+        K_mean, V_mean = k2[:half].mean(0, keepdim=True), v2[:half].mean(0, keepdim=True)
+        kc, vc = k2[:half] - K_mean, v2[:half] - V_mean
+        W = (kc.T @ vc).T @ torch.linalg.pinv(kc.T @ kc)               # :105-112
+        vres = v2 - ((k2 - K_mean) @ W.T + V_mean)
+        vr_scales = vres.view(-1, n_kv, d).abs().amax(dim=(0, 2)).unsqueeze(1).clamp(min=1e-8)  # :116
+        t1 = time.perf_counter()
+        step = 2 * k_scales / 16                                       # :190-193
+        kq = torch.round(k / step).clamp(-8, 7).to(torch.int8)
+        u = kq.to(torch.uint8) + 8
+        k_packed = torch.zeros(n + max(1024, n // 2), n_kv, d // 2, dtype=torch.uint8)
+        k_packed[:n] = (u[..., 0::2] << 4) | u[..., 1::2]
+        v_pred = ((k2 - K_mean) @ W.T + V_mean).view(n, n_kv, d)       # :196-198
+        vrq = torch.round((v - v_pred) / (2 * vr_scales / 4)).clamp(-2, 1).to(torch.int8)
+        u2 = vrq.to(torch.uint8) + 2
+        vr_packed = torch.zeros(n + max(1024, n // 2), n_kv, d // 4, dtype=torch.uint8)
+        vr_packed[:n] = (u2[..., 0::4] << 6) | (u2[..., 1::4] << 4) | (u2[..., 2::4] << 2) | u2[..., 3::4]
+        t2 = time.perf_counter()
+        cal.append(t1 - t0)
+        app.append(t2 - t1)
+    cal.sort()
+    app.sort()
+    tot = sorted(c + a for c, a in zip(cal, app))
+    return {"calibrate_s": cal[len(cal) // 2], "append_s": app[len(app) // 2], "median_s": tot[len(tot) // 2]}

@@ -61,6 +61,7 @@ SIGNATURES = {
     "kvr_sd1_decode_step": (I, [P, I, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I64, I, I, I, I64, I64,
                                 F, P, I, P, P, SZ, P]),
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),
+    "kvr_merge_candidates": (I, [P, P, I, I, I, I, I64, I64, P, P, P]),
     "kvr_sd1_prefill_workspace_bytes": (SZ, [I64, I]),
     "kvr_sd1_prefill_scores": (I, [P, I, I64, I, I, P, P, I64, I64, I, I, P, P, SZ, P]),
     "kvr_kmeans_workspace_bytes": (SZ, [I64, I]),

@@ -192,6 +192,18 @@ def lse_merge(partials: torch.Tensor, out_dtype=torch.float32):
     return out
 
 
+def merge_candidates(scores, idx, k_sel, tile_base=0, n_local=0, global_out=True):
+    """scores fp32 / idx int32 (N, B, H, k_local) gathered candidates ->
+    (global_sel (B, H, k_sel) int32 or None, local_sel (B, H, k_sel) int32)."""
+    N_, B, H, kl = scores.shape
+    sc, ix = _c(scores.float()), _c(idx.to(torch.int32))
+    lsel = torch.empty(B, H, k_sel, dtype=torch.int32, device=sc.device)
+    gsel = torch.empty_like(lsel) if global_out else None
+    call("kvr_merge_candidates", ptr(sc), ptr(ix), N_, B * H, kl, k_sel, tile_base, n_local, ptr(gsel), ptr(lsel),
+         stream())
+    return gsel, lsel
+
+
 # -------------------------------------------------------------------- sd1 --
 
 

@@ -15,6 +15,8 @@ the window and the pending tail.  One decode step is
   3. each rank attends the selected tiles it owns (+ the window on the last
      rank) and emits log-sum-exp partial rows (m, l, o);
   4. all-gather of the partial rows and a local merge (kvr_lse_merge).
+The global top k of step 2 is one kernel (kvr_merge_candidates) that also
+writes the rank's own slice of the selection as local tile indices.
 Both exchanges use a communicator with ``all_gather(tensor) -> list``;
 ``TorchDistComm`` wraps torch.distributed (NCCL over NVLink on the GPU box,
 gloo in the CPU tests); remote data lands in local memory before any kernel
@@ -83,6 +85,16 @@ class TorchDistComm:
         self.dist.all_gather(out, t.contiguous(), group=self.group)
         return out
 
+    def all_gather_stacked(self, t: torch.Tensor):
+        """(N, *t.shape): rank r's tensor at [r] (one all_gather_into_tensor
+        on NCCL; a list all-gather elsewhere)."""
+        t = t.contiguous()
+        if t.is_cuda:
+            out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+            self.dist.all_gather_into_tensor(out, t, group=self.group)
+            return out
+        return torch.stack(self.all_gather(t))
+
 
 class SeqSplitDecoder:
     """Per-rank state of a sequence-split layer: the local sd1 store (global
@@ -115,21 +127,34 @@ class SeqSplitDecoder:
     def n_local_tiles(self):
         return self.store.n_tiles
 
-    def step(self, q, k_sel, out_dtype=None):
-        """q (B, n_q, d) on this rank's GPU (same on every rank) -> (B, n_q, d)."""
+    def select_global(self, all_sc, all_idx, k_sel):
+        """Gathered candidates (N, B, H, k) -> this rank's local selection
+        (B, H, k_sel) int32 (-1 = tile not owned here) and the global
+        selection (B, H, k_sel) (kvr_merge_candidates)."""
+        gsel, lsel = K.merge_candidates(all_sc, all_idx, k_sel, self.tile_base, self.n_local_tiles())
+        return lsel, gsel
+
+    def step(self, q, k_sel, out_dtype=None, marks=None):
+        """q (B, n_q, d) on this rank's GPU (same on every rank) -> (out
+        (B, n_q, d), global selection (B, H, k_sel)).  `marks`, if given, is
+        called between the phases with the phase name just finished (the
+        bench records CUDA events there)."""
         q = q if q.dim() == 3 else q.unsqueeze(0)
         B, n_q, d = q.shape
+        mark = marks or (lambda name: None)
         sel, sc, qp = self.local_candidates(q, k_sel)
-        all_sc = torch.stack(self.comm.all_gather(sc.contiguous()))
-        all_idx = torch.stack(self.comm.all_gather(sel.long().contiguous()))
-        gsel = global_selection(all_sc, all_idx, k_sel)
-        n_loc = self.n_local_tiles()
-        local = gsel - self.tile_base
-        mine = (gsel >= 0) & (local >= 0) & (local < n_loc)
-        local = torch.where(mine, local, torch.full_like(local, -1)).to(torch.int32).contiguous()
+        mark("local_select")
+        gather = getattr(self.comm, "all_gather_stacked", None) or (lambda t: torch.stack(self.comm.all_gather(t)))
+        all_sc = gather(sc)
+        all_idx = gather(sel.to(torch.int32))
+        mark("candidate_allgather")
+        local, gsel = self.select_global(all_sc, all_idx, k_sel)
         part = self.local_partial(q, qp, local)
-        parts = torch.stack(self.comm.all_gather(part.contiguous()))       # (N, B, n_q, d+2)
+        mark("local_attend")
+        parts = gather(part)       # (N, B, n_q, d+2)
+        mark("partial_allgather")
         merged = self.merge(parts.reshape(parts.shape[0], B * n_q, d + 2), out_dtype or q.dtype)
+        mark("merge")
         return merged.view(B, n_q, d), gsel
 
     def merge(self, parts, out_dtype):

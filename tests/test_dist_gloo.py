@@ -180,6 +180,13 @@ class _OracleSplit:
             def merge(self, parts, out_dtype):
                 return torch.from_numpy(_merge(parts.numpy()))
 
+            def select_global(self, all_sc, all_idx, kk):
+                from kvr_b200.sharding import global_selection
+                g = global_selection(all_sc, all_idx.long(), kk)
+                loc = g - base
+                mine = (g >= 0) & (loc >= 0) & (loc < n)
+                return torch.where(mine, loc, torch.full_like(loc, -1)), g
+
         return Dec(None, base, comm), enc
 
 

@@ -93,6 +93,43 @@ def test_seq_split_two_ranks_one_gpu():
         assert torch.equal(gsel.to(torch.int32), want_sel)
         err = (out - want).abs().max() / want.abs().max()
         assert err < 1e-5, err
+    # and both against the CPU specification (selection exact, attention 1e-5)
+    from oracle import sd1_ref as S
+    kc, vc, qc, wc = k[0].cpu().numpy(), v[0].cpu().numpy(), q[0].cpu().numpy(), win[0].float().cpu().numpy()
+    qp = S.transform(S.q_group_mean_f32(qc, NKV), "dct")
+    g = NQ // NKV
+    for h in range(NKV):
+        enc = S.encode(kc[:, h], vc[:, h], TILE, "dct")
+        sel_h = S.select_tiles(S.tile_scores(qp[h], enc["kbits"], enc["kscale"]), K_SEL)
+        assert np.array_equal(res[0][1][0, h].cpu().numpy(), sel_h)
+        dk = S.decode_tiles(enc["kbits"][sel_h], enc["kscale"][sel_h], "dct").reshape(-1, 128)
+        dv = S.decode_tiles(enc["vbits"][sel_h], enc["vscale"][sel_h], "dct").reshape(-1, 128)
+        ref_h = S.decode_attention(qc[h * g:(h + 1) * g], wc[:, h], wc[:, h], dk, dv)
+        got_h = res[0][0][0, h * g:(h + 1) * g].cpu().numpy()
+        assert np.abs(got_h - ref_h).max() <= 1e-5 * np.abs(ref_h).max()
+
+
+def test_merge_candidates_matches_global_selection():
+    """kvr_merge_candidates against the torch restatement of the rule (score
+    desc, index asc; -1 / -inf / NaN are not candidates), with ties, empty
+    slots and uneven ownership."""
+    from kvr_b200 import kernels as K
+    from kvr_b200.sharding import global_selection
+    g = torch.Generator().manual_seed(0)
+    for N_, B, H, kl, k_sel in [(2, 1, 8, 16, 16), (4, 2, 8, 32, 32), (8, 1, 8, 32, 32), (3, 3, 2, 5, 9)]:
+        sc = torch.randint(-4, 5, (N_, B, H, kl), generator=g).float() / 4  # many ties
+        ix = torch.randperm(N_ * kl * 4, generator=g)[:N_ * kl].view(N_, 1, 1, kl).expand(N_, B, H, kl).clone()
+        drop = torch.rand(N_, B, H, kl, generator=g) < 0.2
+        ix[drop] = -1
+        sc[torch.rand(N_, B, H, kl, generator=g) < 0.05] = float("nan")
+        sc[torch.rand(N_, B, H, kl, generator=g) < 0.05] = float("-inf")
+        want = global_selection(sc, ix, k_sel).to(torch.int32)
+        base, n_loc = 7, 40
+        gsel, lsel = K.merge_candidates(sc.cuda(), ix.to(torch.int32).cuda(), k_sel, base, n_loc)
+        assert torch.equal(gsel.cpu(), want)
+        loc = want - base
+        want_l = torch.where((want >= 0) & (loc >= 0) & (loc < n_loc), loc, torch.full_like(loc, -1))
+        assert torch.equal(lsel.cpu(), want_l)
 
 
 def _nccl_worker(rank, world, port, q_path):
