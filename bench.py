@@ -586,8 +586,8 @@ def run_int4w(args, dist_, peak_hbm):
     retrieved) — the path of modules/kvr_hook.py:250-282."""
     import torch
 
-    from kvr_b200 import kernels as K
     from kvr_b200.kvr_retrieval import RetrievalIndex
+    from kvr_b200.kvr_window import WindowBuffer
 
     dev = dist_.dev
     g = torch.Generator(device=dev).manual_seed(55)
@@ -615,7 +615,9 @@ def run_int4w(args, dist_, peak_hbm):
         rets.append(r)
         kp = (k[T_STORED:] * cos[T_STORED:, None] + torch.cat([-k[T_STORED:, :, 64:], k[T_STORED:, :, :64]], -1)
               * sin[T_STORED:, None])
-        wins.append((kp.half(), v[T_STORED:].half()))
+        wb = WindowBuffer(HKV, D, WIN, dev)
+        wb.batch_append(kp, v[T_STORED:])
+        wins.append(wb)
         del k, v
     qs = torch.randn(LAYERS, HQ, D, device=dev, generator=g)
     outs = torch.empty_like(qs)
@@ -623,9 +625,7 @@ def run_int4w(args, dist_, peak_hbm):
 
     def step():
         for li in range(LAYERS):
-            wk, wv = wins[li]
-            rk, rv = rets[li].retrieve_topk(qs[li], n_q=HQ)
-            outs[li].copy_(K.decode_attn(qs[li], [(wk, wv), (rk, rv)], out_dtype=torch.float32, n_kv=HKV))
+            outs[li].copy_(rets[li].attend(qs[li], wins[li]))
 
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -652,7 +652,8 @@ def run_int4w(args, dist_, peak_hbm):
            "bytes_per_layer": b, "hbm_gbs": round(gbs, 1), "frac": round(gbs / peak_hbm, 4),
            "encode_ms_per_layer": round(statistics.median(enc_ms), 4),
            "encode_tokens_per_s": round(T_STORED / (statistics.median(enc_ms) / 1e3), 1),
-           "path": "RetrievalIndex.retrieve_topk + kvr_decode_attn (kvr_b200, codec='int4w')"}
+           "path": "RetrievalIndex.attend(q, window) per layer (kvr_b200, codec='int4w'): token scores -> top-k -> "
+                   "gather -> tensor-core V-predict -> window + retrieved attention, no host sync"}
     del rets, wins
     torch.cuda.empty_cache()
     return res

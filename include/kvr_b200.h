@@ -18,7 +18,9 @@
  *   modules/kvr_retrieval.py:265-289 (all scores)      -> kvr_int4w_token_scores
  *   modules/kvr_retrieval.py:291-315 (chunk scores)    -> kvr_int4w_chunk_scores
  *   modules/kvr_retrieval.py:370-392 (top-k)           -> kvr_topk_rows
- *   modules/kvr_retrieval.py:394-412 (gather, V recon) -> kvr_int4w_gather, kvr_int4w_vres_add
+ *   modules/kvr_retrieval.py:394-412 (gather, V recon) -> kvr_int4w_gather, kvr_int4w_vpredict(_prepare),
+ *                                                         kvr_int4w_vres_add
+ *   modules/kvr_retrieval.py:248-263, 332-367 (attractor branch) -> kvr_int4w_attractor_select
  *   modules/kvr_window.py:19-41      (ring append)     -> kvr_window_write
  *   modules/kvr_window.py:43-69, kvr_hook.py:274-282,
  *   modules/kvr_triton.py:42-104     (attention)       -> kvr_decode_attn
@@ -86,7 +88,9 @@ KVR_API int kvr_int4w_encode_vres(const void *v, int dtype, const float *v_pred,
 
 /* Drop-in for the reference's native score kernel (kvr_cuda.cu:9-49, 53-77):
  * interleaved-pair RoPE from (n_stored, d/2) cos/sin tables, dot with the
- * pre-averaged q, divided by sqrt(d).  scores (n_stored, n_kv) fp32. */
+ * pre-averaged q, divided by sqrt(d).  scores (n_stored, n_kv) fp32,
+ * bit-identical to the reference kernel (same per-element rounding order).
+ * d in {64, 128, 256}; every pointer 16-byte aligned. */
 KVR_API int kvr_compute_scores(const float *q_avg /* (n_kv, d) */, const uint8_t *k_pack, const float *k_scales,
                        const float *cos_tbl, const float *sin_tbl, int n_kv, int d, int64_t n_stored,
                        float *scores, kvr_stream_t stream);
@@ -126,10 +130,48 @@ KVR_API int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t row_
  * top (k, n_kv) int64 token indices.  Writes
  *   ret_k (k, n_kv, d) fp32 : RoPE(deq K[top[i,h], h]) at position top[i,h];
  *   x     (n_kv, k, n_kv*d) fp32 : deq K_pre of ALL heads of token top[i,h]
- *                                  minus K_mean (the V-predict GEMM input). */
+ *                                  minus K_mean (input of a library V-predict
+ *                                  GEMM; NULL skips it, k_mean may then be NULL).
+ * count (optional, device int32): only rows i < *count are written. */
 KVR_API int kvr_int4w_gather(const uint8_t *k_packed, const float *k_scales, const int64_t *top, int k, int n_kv,
                      int d, const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
-                     const float *k_mean /* (n_kv*d) */, float *ret_k, float *x, kvr_stream_t stream);
+                     const float *k_mean /* (n_kv*d) */, float *ret_k, float *x, const int32_t *count,
+                     kvr_stream_t stream);
+
+/* V reconstruction of the selected tokens on the tensor cores
+ * (kvr_retrieval.py:131-134, 394-402): ret_v[i, h, :] = fp16(W[h] . (deq K[t] -
+ * K_mean) + V_mean[h] + int2 residual[t, h] * (2*vr_scales[h]/4)),
+ * t = top[i, h], contracting over all n_kv*d channels of token t straight from
+ * its packed int4 codes.  w3/unscale/bias come from kvr_int4w_vpredict_prepare
+ * (once per calibration): W' = W * diag(step) split into fp16 hi + lo parts
+ * with a power-of-two scale per output row (fp32-level accuracy).
+ * count (optional, device int32): only rows i < *count are written.  d = 128. */
+KVR_API size_t kvr_int4w_vpredict_weights_bytes(int n_kv, int d);
+KVR_API int kvr_int4w_vpredict_prepare(const float *W /* (n_kv*d, n_kv*d) */, const float *k_mean,
+                                       const float *v_mean, const float *k_scales, int n_kv, int d, void *w3,
+                                       float *unscale /* (n_kv*d) */, float *bias /* (n_kv*d) */,
+                                       kvr_stream_t stream);
+KVR_API int kvr_int4w_vpredict(const uint8_t *k_packed, const int64_t *top, const int32_t *count, int k, int n_kv,
+                               int d, const void *w3, const float *unscale, const float *bias,
+                               const uint8_t *vr_packed, const float *vr_scales, uint16_t *ret_v /* fp16 */,
+                               kvr_stream_t stream);
+
+/* Attractor branch of retrieve_topk (kvr_retrieval.py:248-263, 332-367)
+ * with no host sync: head-0 group-mean query vs the centroids (n_attractors,
+ * d), the top_a basins, the top 16 tokens of each basin by head-0 cosine of
+ * the re-rotated dequantised K (basins given as a CSR list: basin b's tokens
+ * are basin_tokens[basin_start[b] .. basin_start[b+1]), ascending), the
+ * ascending union minus [ex_start, ex_end).  Writes top (top_a*16, n_kv)
+ * int64 (the same token in every column; rows past the count repeat a valid
+ * token) and count (device int32).  Ties: score desc, then index asc.
+ * Full-row (max_pos, d) rope tables; d = 128. */
+KVR_API size_t kvr_int4w_attractor_workspace_bytes(int64_t n_labelled, int top_a);
+KVR_API int kvr_int4w_attractor_select(const float *q, int n_q, int n_kv, const uint8_t *k_packed,
+                                       const float *k_scales, const float *cos_tbl, const float *sin_tbl,
+                                       int64_t rope_stride, const float *centroids, int n_attractors,
+                                       const int32_t *basin_start, const int32_t *basin_tokens, int64_t n_labelled,
+                                       int top_a, int64_t ex_start, int64_t ex_end, int64_t *top, int32_t *count,
+                                       void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
 /* ret_v[i, h, :] = fp16(v_base[h, i, :] + unpack2(vr_packed[top[i,h], h]) * (2*vr[h]/4))
  * with v_base (n_kv, k, d) fp32 (= x @ W_h^T + V_mean_h) (kvr_retrieval.py:399-402). */
@@ -157,6 +199,14 @@ KVR_API int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, int d
                     const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1, int64_t tok_stride1,
                     float scale, void *out, int out_dtype, void *workspace, size_t workspace_bytes,
                     kvr_stream_t stream);
+/* kvr_decode_attn whose segment 1 holds *n1_count rows (a device-side
+ * count, at most n1): for a retrieved set whose size is only known on the
+ * device (the attractor branch), with no host round trip. */
+KVR_API int kvr_decode_attn_counted(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0,
+                                    const void *v0, int kdt0, int vdt0, int64_t n0, int64_t tok_stride0,
+                                    const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1,
+                                    int64_t tok_stride1, const int32_t *n1_count, float scale, void *out,
+                                    int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
 /* ------------------------------------------------------------------ sd1 ----
  * 1-bit codec (no reference counterpart).  head_dim d = 128, tile t in
@@ -300,6 +350,13 @@ KVR_API int kvr_decode_attn_noalloc(const void *q, int q_dtype, int n_q, int n_k
  * starts with: KVR_ETIMEOUT if a bounded device-side wait of an earlier call
  * using this workspace gave up, else KVR_OK. */
 KVR_API int kvr_workspace_status(const void *workspace, kvr_stream_t stream);
+
+/* Test of the failure path above (no reference counterpart): one kernel
+ * whose mbarrier can never complete runs the kernels' bounded wait with
+ * spin_limit (<= 65536) polls, gives up, sets the workspace's error word and
+ * returns — no copy in flight, no fault; kvr_workspace_status then reports
+ * KVR_ETIMEOUT and the context stays usable. */
+KVR_API int kvr_selftest_bounded_wait(void *workspace, uint32_t spin_limit, kvr_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -337,6 +337,36 @@ def gather_selected(st, top, cos, sin):
     return ret_k, ret_v.astype(np.float16)
 
 
+def attractor_select(q_post, st, cos, sin, labels, centroids, top_a=48, per_basin=16, ex_start=0, ex_end=0):
+    """kvr_retrieval.py:248-263 + 332-367 — the attractor branch given the
+    basins (labels, centroids): cosine of the head-0 group-mean query with each
+    centroid, the top_a basins, in each basin with more than per_basin tokens
+    the per_basin best by head-0 cosine of RoPE(deq K) at the token's own
+    position, the sorted union, minus [ex_start, ex_end) when that range is
+    non-empty.  Ties by index ascending (torch leaves them unspecified).
+    Returns (tokens ascending, basin scores, {basin: token scores})."""
+    n_kv = st["k_packed"].shape[1]
+    qa = q_group_mean(q_post, n_kv)[0]
+    bs = _cosine(qa, centroids.astype(F32))
+    bs = np.where(np.isnan(bs), -np.inf, bs)
+    basins = topk_rule(bs[:, None], min(top_a, len(bs)))[:, 0]
+    k0 = deq_k(st["k_packed"], st["k_scales"], len(labels))[:, 0]
+    chosen, tok_scores = [], {}
+    for b in basins:
+        tidx = np.nonzero(labels == b)[0]
+        if len(tidx) <= per_basin:
+            chosen.append(tidx)
+            continue
+        kr = apply_rotary(k0[tidx], cos[tidx], sin[tidx]).astype(F32)
+        sc = _cosine(qa, kr)
+        tok_scores[int(b)] = (tidx, sc)
+        chosen.append(tidx[topk_rule(sc[:, None], per_basin)[:, 0]])
+    toks = np.unique(np.concatenate(chosen)) if chosen else np.zeros(0, np.int64)
+    if ex_end > ex_start:
+        toks = toks[(toks < ex_start) | (toks >= ex_end)]
+    return toks, bs, tok_scores
+
+
 # --------------------------------------------------------------------------
 # attention (kvr_window.py:43-69, kvr_hook.py:274-282, kvr_triton.py:42-79)
 # --------------------------------------------------------------------------

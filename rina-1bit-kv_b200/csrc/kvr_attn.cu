@@ -65,6 +65,7 @@ struct AttnArgs {
   int upc;    // units per CTA
   int slots;  // CTAs per (b, h) = ceil(units / upc)
   int pipelined;  // batched rows over fp16 exact data: attn_rows_kernel
+  const int32_t *n1_dev;  // optional device-side bound on segment 1's rows (exact units only)
 };
 
 // ---- runtime-dtype loads
@@ -177,7 +178,12 @@ __device__ void exact_unit(const AttnArgs &a, unsigned char *sm, int64_t b, int 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = b * a.n_kv + h;
   const int64_t t0 = (int64_t)chunk * kChunk;
-  const int nt = (int)(a.n[seg] - t0 < kChunk ? a.n[seg] - t0 : kChunk);
+  int64_t nseg = a.n[seg];
+  if (seg == 1 && a.n1_dev) {
+    const int64_t nd = __ldg(a.n1_dev);
+    nseg = nd < nseg ? nd : nseg;
+  }
+  const int nt = (int)(nseg - t0 < kChunk ? nseg - t0 : kChunk);
 
   // Stage q (scaled) and the K/V chunk as fp32: every global load of the
   // chunk is issued before the first shared-memory store, so the chunk
@@ -1320,7 +1326,7 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
           (a.batch_stride[s] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.k[s]) % 16) == 0 &&
           (reinterpret_cast<uintptr_t>(a.v[s]) % 16) == 0;
   }
-  a.pipelined = f16 ? 1 : 0;
+  a.pipelined = (f16 && a.n1_dev == nullptr) ? 1 : 0;
   const size_t ms = merge_smem_bytes(a.slots);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
   dim3 grid(a.slots, a.n_kv, batch);
@@ -1385,22 +1391,22 @@ extern "C" size_t kvr_decode_attn_workspace_bytes(int n_q, int n_kv, int d, int6
   return attn_ws_layout(nullptr, 1, n_kv, units, n_q / n_kv).bytes;
 }
 
-extern "C" int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0, const void *v0,
-                               int kdt0, int vdt0, int64_t n0, int64_t tok_stride0, const void *k1, const void *v1,
-                               int kdt1, int vdt1, int64_t n1, int64_t tok_stride1, float scale, void *out,
-                               int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
-  clear_error();
-  KVR_REQUIRE(d == kD, "kvr_decode_attn: head_dim must be 128 (got %d)", d);
+static int decode_attn_impl(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0, const void *v0,
+                            int kdt0, int vdt0, int64_t n0, int64_t tok_stride0, const void *k1, const void *v1,
+                            int kdt1, int vdt1, int64_t n1, int64_t tok_stride1, float scale, void *out,
+                            int out_dtype, void *workspace, size_t workspace_bytes, const int32_t *n1_dev,
+                            kvr_stream_t stream, const char *what) {
+  KVR_REQUIRE(d == kD, "%s: head_dim must be 128 (got %d)", what, d);
   KVR_REQUIRE(n_kv > 0 && n_q > 0 && n_q % n_kv == 0 && n_q / n_kv <= kMaxG,
-              "kvr_decode_attn: need n_q %% n_kv == 0 and n_q/n_kv <= 8 (n_q=%d n_kv=%d)", n_q, n_kv);
-  KVR_REQUIRE(valid_dtype(q_dtype) && valid_dtype(out_dtype), "kvr_decode_attn: bad q/out dtype");
-  KVR_REQUIRE(q && out && workspace, "kvr_decode_attn: null pointer");
-  KVR_REQUIRE(n0 >= 0 && n1 >= 0, "kvr_decode_attn: negative token count");
+              "%s: need n_q %% n_kv == 0 and n_q/n_kv <= 8 (n_q=%d n_kv=%d)", what, n_q, n_kv);
+  KVR_REQUIRE(valid_dtype(q_dtype) && valid_dtype(out_dtype), "%s: bad q/out dtype", what);
+  KVR_REQUIRE(q && out && workspace, "%s: null pointer", what);
+  KVR_REQUIRE(n0 >= 0 && n1 >= 0, "%s: negative token count", what);
   KVR_REQUIRE(n0 == 0 || (k0 && v0 && valid_dtype(kdt0) && valid_dtype(vdt0) && tok_stride0 % 4 == 0),
-              "kvr_decode_attn: bad segment 0");
+              "%s: bad segment 0", what);
   KVR_REQUIRE(n1 == 0 || (k1 && v1 && valid_dtype(kdt1) && valid_dtype(vdt1) && tok_stride1 % 4 == 0),
-              "kvr_decode_attn: bad segment 1");
-  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_decode_attn: workspace must be 256-byte aligned");
+              "%s: bad segment 1", what);
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "%s: workspace must be 256-byte aligned", what);
   AttnArgs a{};
   a.q = q; a.q_dt = q_dtype; a.n_q = n_q; a.n_kv = n_kv; a.g = n_q / n_kv;
   a.inv_scale = (float)(1.0 / (scale > 0.f ? (double)scale : sqrt((double)d)));
@@ -1411,15 +1417,38 @@ extern "C" int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, in
   a.units = a.nchunk[0] + a.nchunk[1];
   a.tile = 64; a.kind = KVR_HADAMARD;
   a.out = out; a.out_dt = out_dtype;
+  a.n1_dev = n1 > 0 ? n1_dev : nullptr;
   if (a.units == 0) {
     cudaMemsetAsync(out, 0, (size_t)n_q * d * dtype_size(out_dtype), as_cuda(stream));
-    return check_launch("kvr_decode_attn (empty)");
+    return check_launch(what);
   }
-  KVR_REQUIRE(n_kv <= kWsMaxRows, "kvr_decode_attn: n_kv > %d", kWsMaxRows);
+  KVR_REQUIRE(n_kv <= kWsMaxRows, "%s: n_kv > %d", what, kWsMaxRows);
   AttnWs w = attn_ws_layout(workspace, 1, n_kv, a.units, a.g);
-  KVR_REQUIRE(workspace_bytes >= w.bytes, "kvr_decode_attn: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  KVR_REQUIRE(workspace_bytes >= w.bytes, "%s: workspace %zu < %zu bytes", what, workspace_bytes, w.bytes);
   a.err = w.err; a.counters = w.counters; a.part = w.part;
-  return launch_attn(a, 1, as_cuda(stream), "kvr_decode_attn");
+  return launch_attn(a, 1, as_cuda(stream), what);
+}
+
+extern "C" int kvr_decode_attn(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0, const void *v0,
+                               int kdt0, int vdt0, int64_t n0, int64_t tok_stride0, const void *k1, const void *v1,
+                               int kdt1, int vdt1, int64_t n1, int64_t tok_stride1, float scale, void *out,
+                               int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
+  clear_error();
+  return decode_attn_impl(q, q_dtype, n_q, n_kv, d, k0, v0, kdt0, vdt0, n0, tok_stride0, k1, v1, kdt1, vdt1, n1,
+                          tok_stride1, scale, out, out_dtype, workspace, workspace_bytes, nullptr, stream,
+                          "kvr_decode_attn");
+}
+
+extern "C" int kvr_decode_attn_counted(const void *q, int q_dtype, int n_q, int n_kv, int d, const void *k0,
+                                       const void *v0, int kdt0, int vdt0, int64_t n0, int64_t tok_stride0,
+                                       const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1,
+                                       int64_t tok_stride1, const int32_t *n1_count, float scale, void *out,
+                                       int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(n1_count || n1 == 0, "kvr_decode_attn_counted: null row count");
+  return decode_attn_impl(q, q_dtype, n_q, n_kv, d, k0, v0, kdt0, vdt0, n0, tok_stride0, k1, v1, kdt1, vdt1, n1,
+                          tok_stride1, scale, out, out_dtype, workspace, workspace_bytes, n1_count, stream,
+                          "kvr_decode_attn_counted");
 }
 
 static int sd1_units(int64_t n_win, int64_t n_tail, int k_sel) {

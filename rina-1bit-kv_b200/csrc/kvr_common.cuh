@@ -221,8 +221,8 @@ __device__ __forceinline__ void cp_async8(void *dst, const void *src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 // Bounded wait; returns false if it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned phase, uint32_t limit = kSpinLimit) {
+  for (uint32_t it = 0; it < limit; ++it) {
     if (mbar_try_wait(bar, phase)) return true;
     __nanosleep(64);
   }

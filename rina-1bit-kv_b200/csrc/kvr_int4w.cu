@@ -95,31 +95,88 @@ __global__ void encode_vres_kernel(const void *__restrict__ v, const float *__re
 }
 
 // ---------------------------------------- drop-in interleaved scores ----
-// Same arithmetic as the reference kernel (kvr_cuda.cu:25-48): one thread
-// per (token, head), (hi*s)/8, fmaf rotation with (n, d/2) tables, /sqrt(d).
-__global__ void scores_interleaved_kernel(const float *__restrict__ q, const uint8_t *__restrict__ kp,
-                                          const float *__restrict__ sc, const float *__restrict__ cs,
-                                          const float *__restrict__ sn, int n_kv, int d, int64_t n_stored,
-                                          float *__restrict__ scores) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_stored * n_kv) return;
-  const int h = (int)(i % n_kv);
-  const int64_t t = i / n_kv;
-  const int half = d / 2;
-  const uint8_t *p = kp + (t * n_kv + h) * half;
-  const float *s = sc + h * d;
-  const float *c_t = cs + t * half;
-  const float *s_t = sn + t * half;
-  float score = 0.0f;
-  for (int j = 0; j < half; ++j) {
-    const uint8_t b = p[j];
-    const float hi = (float)((b >> 4) - 8), lo = (float)((b & 0x0F) - 8);
-    const float ke = hi * s[2 * j] / 8.0f, ko = lo * s[2 * j + 1] / 8.0f;
-    const float cv = c_t[j], sv = s_t[j];
-    const float k0 = fmaf(ke, cv, -ko * sv), k1 = fmaf(ke, sv, ko * cv);
-    score = fmaf(q[h * d + 2 * j], k0, fmaf(q[h * d + 2 * j + 1], k1, score));
+// Drop-in for the reference's native score op (modules/kvr_cuda.cu:9-77):
+// score[t, h] = sum_i q[h,2i]*k0r + q[h,2i+1]*k1r, / sqrt(d), where the int4
+// pair (hi, lo) of byte i is dequantised as code*s/8 and rotated by the
+// interleaved-pair tables cos/sin (n, d/2).
+//
+// Layout of the work: a warp owns 32 consecutive (token, head) pairs, which
+// are 32 consecutive packed rows of d/2 bytes in memory.  The warp first
+// copies those rows into its shared-memory slot with coalesced 16-byte loads
+// (each load instruction covers 512 contiguous bytes), rows padded by 16 B so
+// that the per-lane 16-byte reads that follow hit distinct banks; then each
+// lane walks its own row 16 bytes at a time with float4 loads of q, the
+// scales and the cos/sin rows (lanes of the same token share those rows, so
+// the loads broadcast from L1).  The element order and every rounding step
+// follow the reference expression — (code*s)/8, fmaf(ke, c, -(ko*s)),
+// fmaf(ke, s, ko*c), score = fmaf(q_even, k0, fmaf(q_odd, k1, score)) in
+// increasing i, then an IEEE division by sqrt(d) — so the scores are
+// bit-identical to the reference kernel's.
+template <int D>
+__global__ void __launch_bounds__(256) compute_scores_kernel(const float *__restrict__ q,
+                                                             const uint8_t *__restrict__ kp,
+                                                             const float *__restrict__ sc,
+                                                             const float *__restrict__ cs,
+                                                             const float *__restrict__ sn, int n_kv,
+                                                             int64_t n_stored, float *__restrict__ scores) {
+  constexpr int kRow = D / 2;            // packed bytes per (token, head)
+  constexpr int kChunks = kRow / 16;     // 16-byte pieces per row
+  constexpr int kPitch = kRow + 16;      // padded smem row
+  __shared__ __align__(16) uint8_t stage[8][32 * kPitch];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *my = stage[warp];
+  const int64_t total = n_stored * n_kv;
+  const float inv_div = __fsqrt_rn((float)D);
+  for (int64_t base = ((int64_t)blockIdx.x * 8 + warp) * 32; base < total; base += (int64_t)gridDim.x * 8 * 32) {
+    const int rows = (int)(total - base < 32 ? total - base : 32);
+    const uint4 *src = reinterpret_cast<const uint4 *>(kp + base * kRow);
+    for (int c = lane; c < rows * kChunks; c += 32) {
+      const int r = c / kChunks, o = c - r * kChunks;
+      *reinterpret_cast<uint4 *>(my + r * kPitch + o * 16) = __ldg(src + c);
+    }
+    __syncwarp();
+    if (lane < rows) {
+      const int64_t pair = base + lane;
+      const int64_t t = pair / n_kv;
+      const int h = (int)(pair - t * n_kv);
+      const float4 *qh = reinterpret_cast<const float4 *>(q + (int64_t)h * D);
+      const float4 *sh = reinterpret_cast<const float4 *>(sc + (int64_t)h * D);
+      const float4 *ct = reinterpret_cast<const float4 *>(cs + t * kRow);
+      const float4 *st = reinterpret_cast<const float4 *>(sn + t * kRow);
+      float score = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        const uint4 w4 = *reinterpret_cast<const uint4 *>(my + lane * kPitch + c * 16);
+        const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int wq = 0; wq < 4; ++wq) {
+          // bytes i = 16c + 4wq .. +3: elements 2i, 2i+1 -> q/scale float4 pairs, cos/sin one float4
+          const int i0 = 16 * c + 4 * wq;
+          const float4 cv4 = __ldg(ct + i0 / 4), sv4 = __ldg(st + i0 / 4);
+          const float cvs[4] = {cv4.x, cv4.y, cv4.z, cv4.w}, svs[4] = {sv4.x, sv4.y, sv4.z, sv4.w};
+#pragma unroll
+          for (int b = 0; b < 4; b += 2) {
+            const float4 qv = __ldg(qh + (i0 + b) / 2), sv = __ldg(sh + (i0 + b) / 2);
+            const float qe[2] = {qv.x, qv.z}, qo[2] = {qv.y, qv.w};
+            const float se[2] = {sv.x, sv.z}, so[2] = {sv.y, sv.w};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const uint32_t byte = (words[wq] >> (8 * (b + u))) & 0xffu;
+              const float hi = (float)((int)(byte >> 4) - 8), lo = (float)((int)(byte & 15u) - 8);
+              const float ke = __fdiv_rn(__fmul_rn(hi, se[u]), 8.0f);
+              const float ko = __fdiv_rn(__fmul_rn(lo, so[u]), 8.0f);
+              const float cv = cvs[b + u], svv = svs[b + u];
+              const float k0 = fmaf(ke, cv, -__fmul_rn(ko, svv));
+              const float k1 = fmaf(ke, svv, __fmul_rn(ko, cv));
+              score = fmaf(qe[u], k0, fmaf(qo[u], k1, score));
+            }
+          }
+        }
+      }
+      scores[pair] = __fdiv_rn(score, inv_div);
+    }
+    __syncwarp();
   }
-  scores[t * n_kv + h] = score / sqrtf((float)d);
 }
 
 // ------------------------------------------------- group-mean queries ----
@@ -280,18 +337,20 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t *__restrict__
                                                      const int64_t *__restrict__ top, int k, int n_kv,
                                                      const float *__restrict__ cs, const float *__restrict__ sn,
                                                      int64_t rope_stride, const float *__restrict__ kmean,
-                                                     float *__restrict__ ret_k, float *__restrict__ x) {
+                                                     float *__restrict__ ret_k, float *__restrict__ x,
+                                                     const int32_t *__restrict__ count) {
   constexpr int d = 128;
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t wi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < (int64_t)k * n_kv; wi += warps) {
+  const int64_t kv = count ? min((int64_t)k, (int64_t)__ldg(count)) : (int64_t)k;
+  for (int64_t wi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < kv * n_kv; wi += warps) {
     const int h = (int)(wi % n_kv);
     const int64_t i = wi / n_kv;
     const int64_t t = top[i * n_kv + h];
     const int D = n_kv * d;
-    // x[h, i, :] = deq K[t, all heads] - K_mean
-    float *xr = x + ((int64_t)h * k + i) * D;
-    for (int e = lane * 4; e < D; e += 128) {
+    // x[h, i, :] = deq K[t, all heads] - K_mean (only for the library V-predict path)
+    float *xr = x ? x + ((int64_t)h * k + i) * D : nullptr;
+    for (int e = lane * 4; xr && e < D; e += 128) {
       const int hh = e / d, c = e - hh * d;
       const uint16_t two = *reinterpret_cast<const uint16_t *>(kp + (t * n_kv + hh) * (d / 2) + c / 2);
       const int codes[4] = {(int)((two >> 4) & 15) - 8, (int)(two & 15) - 8, (int)((two >> 12) & 15) - 8,
@@ -411,11 +470,19 @@ extern "C" int kvr_compute_scores(const float *q_avg, const uint8_t *k_pack, con
                                   kvr_stream_t stream) {
   clear_error();
   KVR_REQUIRE(q_avg && k_pack && k_scales && cos_tbl && sin_tbl && scores, "kvr_compute_scores: null pointer");
-  KVR_REQUIRE(n_kv > 0 && d > 0 && d % 2 == 0 && n_stored >= 0, "kvr_compute_scores: bad shape");
+  KVR_REQUIRE(n_kv > 0 && n_stored >= 0, "kvr_compute_scores: bad shape");
+  KVR_REQUIRE(d == 64 || d == 128 || d == 256, "kvr_compute_scores: head_dim must be 64, 128 or 256 (got %d)", d);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  KVR_REQUIRE(al16(q_avg) && al16(k_pack) && al16(k_scales) && al16(cos_tbl) && al16(sin_tbl),
+              "kvr_compute_scores: all inputs must be 16-byte aligned");
   if (n_stored == 0) return KVR_OK;
-  const int64_t total = n_stored * n_kv;
-  scores_interleaved_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_cuda(stream)>>>(
-      q_avg, k_pack, k_scales, cos_tbl, sin_tbl, n_kv, d, n_stored, scores);
+  const int64_t warps = (n_stored * n_kv + 31) / 32;
+  int64_t bl = (warps + 7) / 8;
+  int blocks = (int)(bl < 148 * 8 ? bl : 148 * 8);
+  cudaStream_t st = as_cuda(stream);
+  if (d == 64) compute_scores_kernel<64><<<blocks, 256, 0, st>>>(q_avg, k_pack, k_scales, cos_tbl, sin_tbl, n_kv, n_stored, scores);
+  else if (d == 128) compute_scores_kernel<128><<<blocks, 256, 0, st>>>(q_avg, k_pack, k_scales, cos_tbl, sin_tbl, n_kv, n_stored, scores);
+  else compute_scores_kernel<256><<<blocks, 256, 0, st>>>(q_avg, k_pack, k_scales, cos_tbl, sin_tbl, n_kv, n_stored, scores);
   return check_launch("kvr_compute_scores");
 }
 
@@ -472,14 +539,16 @@ extern "C" int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t r
 
 extern "C" int kvr_int4w_gather(const uint8_t *k_packed, const float *k_scales, const int64_t *top, int k, int n_kv,
                                 int d, const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
-                                const float *k_mean, float *ret_k, float *x, kvr_stream_t stream) {
+                                const float *k_mean, float *ret_k, float *x, const int32_t *count,
+                                kvr_stream_t stream) {
   clear_error();
   KVR_REQUIRE(d == 128, "kvr_int4w_gather: head_dim must be 128");
-  KVR_REQUIRE(k_packed && k_scales && top && cos_tbl && sin_tbl && k_mean && ret_k && x, "kvr_int4w_gather: null pointer");
+  KVR_REQUIRE(k_packed && k_scales && top && cos_tbl && sin_tbl && ret_k && (x == nullptr || k_mean),
+              "kvr_int4w_gather: null pointer");
   KVR_REQUIRE(k >= 0 && n_kv > 0, "kvr_int4w_gather: bad shape");
   if (k == 0) return KVR_OK;
   gather_kernel<<<blocks_for((int64_t)k * n_kv, 8), 256, 0, as_cuda(stream)>>>(
-      k_packed, k_scales, top, k, n_kv, cos_tbl, sin_tbl, rope_stride, k_mean, ret_k, x);
+      k_packed, k_scales, top, k, n_kv, cos_tbl, sin_tbl, rope_stride, k_mean, ret_k, x, count);
   return check_launch("kvr_int4w_gather");
 }
 

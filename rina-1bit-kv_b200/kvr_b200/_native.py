@@ -43,7 +43,14 @@ SIGNATURES = {
     "kvr_int4w_token_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, P, I64, P]),
     "kvr_int4w_chunk_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, I, P, I64, P]),
     "kvr_topk_rows": (I, [P, I, I64, I64, I, I64, I64, P, P, I64, I64, P]),
-    "kvr_int4w_gather": (I, [P, P, P, I, I, I, P, P, I64, P, P, P, P]),
+    "kvr_int4w_gather": (I, [P, P, P, I, I, I, P, P, I64, P, P, P, P, P]),
+    "kvr_int4w_vpredict_weights_bytes": (SZ, [I, I]),
+    "kvr_int4w_vpredict_prepare": (I, [P, P, P, P, I, I, P, P, P, P]),
+    "kvr_int4w_vpredict": (I, [P, P, P, I, I, I, P, P, P, P, P, P, P]),
+    "kvr_int4w_attractor_workspace_bytes": (SZ, [I64, I]),
+    "kvr_int4w_attractor_select": (I, [P, I, I, P, P, P, P, I64, P, I, P, P, I64, I, I64, I64, P, P, P, SZ, P]),
+    "kvr_decode_attn_counted": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, P, F, P, I, P, SZ,
+                                    P]),
     "kvr_int4w_vres_add": (I, [P, P, P, P, I, I, I, P, P]),
     "kvr_window_write": (I, [P, P, I, I64, I, I, P, P, I64, I64, P]),
     "kvr_decode_attn_workspace_bytes": (SZ, [I, I, I, I64]),
@@ -67,6 +74,7 @@ SIGNATURES = {
     "kvr_kmeans_workspace_bytes": (SZ, [I64, I]),
     "kvr_kmeans": (I, [P, I64, I, I, I, P, P, P, SZ, P]),
     "kvr_workspace_status": (I, [P, P]),
+    "kvr_selftest_bounded_wait": (I, [P, C.c_uint32, P]),
     "kvr_decode_attn_noalloc_max_scratch_bytes": (SZ, []),
     "kvr_decode_attn_noalloc": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, F, P, I, P]),
 }

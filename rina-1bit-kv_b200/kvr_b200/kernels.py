@@ -112,15 +112,63 @@ def topk_rows(scores: torch.Tensor, k: int, ex_start: int = 0, ex_end: int = 0, 
     return idx, vals
 
 
-def int4w_gather(k_packed, k_scales, top, cos, sin, k_mean):
-    """-> (ret_k (k, n_kv, d) fp32 post-RoPE, x (n_kv, k, n_kv*d) fp32 = deq K_pre - K_mean)."""
+def int4w_gather(k_packed, k_scales, top, cos, sin, k_mean=None, want_x=True, count=None, ret_k=None):
+    """-> (ret_k (k, n_kv, d) fp32 post-RoPE, x (n_kv, k, n_kv*d) fp32 = deq
+    K_pre - K_mean, or None when want_x is False).  count: optional device
+    int32 row count (rows past it are left untouched)."""
     k, n_kv = top.shape
     cos, sin, rs = _rope_args(cos.float(), sin.float())
-    ret_k = torch.empty(k, n_kv, D, dtype=torch.float32, device=top.device)
-    x = torch.empty(n_kv, k, n_kv * D, dtype=torch.float32, device=top.device)
+    if ret_k is None:
+        ret_k = torch.empty(k, n_kv, D, dtype=torch.float32, device=top.device)
+    x = torch.empty(n_kv, k, n_kv * D, dtype=torch.float32, device=top.device) if want_x else None
+    km = _c(k_mean.float().reshape(-1)) if want_x else None
     call("kvr_int4w_gather", ptr(_c(k_packed)), ptr(_c(k_scales.float())), ptr(_c(top)), k, n_kv, D, ptr(cos),
-         ptr(sin), rs, ptr(_c(k_mean.float().reshape(-1))), ptr(ret_k), ptr(x), stream())
+         ptr(sin), rs, ptr(km), ptr(ret_k), ptr(x), ptr(count), stream())
     return ret_k, x
+
+
+def int4w_vpredict_prepare(W, k_mean, v_mean, k_scales, n_kv):
+    """Once per calibration: (w3 fp16 (n_kv, 2, d, n_kv*d), unscale fp32
+    (n_kv*d), bias fp32 (n_kv*d)) for int4w_vpredict."""
+    dev = W.device
+    KD = n_kv * D
+    w3 = torch.empty(n_kv, 2, D, KD, dtype=torch.float16, device=dev)
+    unscale = torch.empty(KD, dtype=torch.float32, device=dev)
+    bias = torch.empty(KD, dtype=torch.float32, device=dev)
+    call("kvr_int4w_vpredict_prepare", ptr(_c(W.float())), ptr(_c(k_mean.float().reshape(-1))),
+         ptr(_c(v_mean.float().reshape(-1))), ptr(_c(k_scales.float().reshape(-1))), n_kv, D, ptr(w3),
+         ptr(unscale), ptr(bias), stream())
+    return w3, unscale, bias
+
+
+def int4w_vpredict(k_packed, top, prep, vr_packed, vr_scales, count=None, out=None):
+    """ret_v (k, n_kv, d) fp16 = W-predicted V + int2 residual of the tokens
+    top (k, n_kv) int64 (kvr_retrieval.py:394-402), on the tensor cores."""
+    k, n_kv = top.shape
+    w3, unscale, bias = prep
+    if out is None:
+        out = torch.empty(k, n_kv, D, dtype=torch.float16, device=top.device)
+    call("kvr_int4w_vpredict", ptr(_c(k_packed)), ptr(_c(top)), ptr(count), k, n_kv, D, ptr(w3), ptr(unscale),
+         ptr(bias), ptr(_c(vr_packed)), ptr(_c(vr_scales.float().reshape(-1))), ptr(out), stream())
+    return out
+
+
+def int4w_attractor_select(q, n_kv, k_packed, k_scales, cos, sin, centroids, basin_start, basin_tokens, top_a=48,
+                           ex_start=0, ex_end=0):
+    """Attractor branch selection (kvr_retrieval.py:332-367) on the device:
+    -> (top (top_a*16, n_kv) int64, count (1,) int32 device tensor)."""
+    q = _c(q.float())
+    n_q = q.shape[0]
+    cos, sin, rs = _rope_args(cos.float(), sin.float())
+    rows = top_a * 16
+    top = torch.empty(rows, n_kv, dtype=torch.int64, device=q.device)
+    count = torch.empty(1, dtype=torch.int32, device=q.device)
+    nl = basin_tokens.numel()
+    ws = N.workspace("attractor", call("kvr_int4w_attractor_workspace_bytes", nl, top_a), q.device)
+    call("kvr_int4w_attractor_select", ptr(q), n_q, n_kv, ptr(_c(k_packed)), ptr(_c(k_scales.float())), ptr(cos),
+         ptr(sin), rs, ptr(_c(centroids.float())), centroids.shape[0], ptr(_c(basin_start)), ptr(_c(basin_tokens)),
+         nl, top_a, ex_start, ex_end, ptr(top), ptr(count), ptr(ws), ws.numel(), stream())
+    return top, count
 
 
 def int4w_vres_add(v_base, vr_packed, vr_scales, top):
@@ -149,37 +197,50 @@ def window_write(k, v, ring_k, ring_v, pos: int):
 # -------------------------------------------------------------- attention --
 
 
-def decode_attn(q, segments, scale=None, out_dtype=None, n_kv=None):
+def _seg_rows(k, v, d):
+    if k.stride(-1) != 1 or k.stride(-2) != d:
+        k = k.contiguous()
+    if v.stride(-1) != 1 or v.stride(-2) != d or v.stride(0) != k.stride(0):
+        v = v.contiguous()
+        if v.stride(0) != k.stride(0):
+            k = k.contiguous()
+    return k, v
+
+
+def decode_attn(q, segments, scale=None, out_dtype=None, n_kv=None, n1_count=None, out=None):
     """Exact attention of q (n_q, d) over up to two K/V segments
-    [(k0, v0), (k1, v1)], each (n_i, n_kv, d) with contiguous rows."""
+    [(k0, v0), (k1, v1)], each (n_i, n_kv, d) with contiguous rows.
+    n1_count: optional device int32 holding how many rows of the second
+    segment are valid (kvr_decode_attn_counted)."""
     q = _c(q)
     n_q, d = q.shape
-    segs = []
-    for k, v in segments:
-        if k.shape[0] == 0:
-            continue
-        if k.stride(-1) != 1 or k.stride(-2) != d:
-            k = k.contiguous()
-        if v.stride(-1) != 1 or v.stride(-2) != d or v.stride(0) != k.stride(0):
-            v = v.contiguous()
-            if v.stride(0) != k.stride(0):
-                k = k.contiguous()
-        segs.append((k, v))
     if n_kv is None:
         n_kv = segments[0][0].shape[1]
+    segs = [_seg_rows(k, v, d) if k.shape[0] else None for k, v in segments]
+    if n1_count is None:
+        segs = [sg for sg in segs if sg is not None]
+    while len(segs) < 2:
+        segs.append(None)
+    if segs[1] is None:
+        n1_count = None
     out_dtype = out_dtype or q.dtype
-    out = torch.empty(n_q, d, dtype=out_dtype, device=q.device)
-    n_tot = sum(s[0].shape[0] for s in segs)
+    if out is None:
+        out = torch.empty(n_q, d, dtype=out_dtype, device=q.device)
+    n_tot = sum(sg[0].shape[0] for sg in segs if sg is not None)
     ws = N.workspace("attn", call("kvr_decode_attn_workspace_bytes", n_q, n_kv, d, n_tot), q.device)
     args = []
-    for i in range(2):
-        if i < len(segs):
-            k, v = segs[i]
-            args += [ptr(k), ptr(v), dtype_code(k), dtype_code(v), k.shape[0], k.stride(0)]
+    for sg in segs:
+        if sg is not None:
+            k, v = sg
+            args.append([ptr(k), ptr(v), dtype_code(k), dtype_code(v), k.shape[0], k.stride(0)])
         else:
-            args += [None, None, 0, 0, 0, 0]
-    call("kvr_decode_attn", ptr(q), dtype_code(q), n_q, n_kv, d, *args, float(scale or 0.0), ptr(out),
-         dtype_code(out), ptr(ws), ws.numel(), stream())
+            args.append([None, None, 0, 0, 0, 0])
+    if n1_count is not None:
+        call("kvr_decode_attn_counted", ptr(q), dtype_code(q), n_q, n_kv, d, *args[0], *args[1], ptr(n1_count),
+             float(scale or 0.0), ptr(out), dtype_code(out), ptr(ws), ws.numel(), stream())
+    else:
+        call("kvr_decode_attn", ptr(q), dtype_code(q), n_q, n_kv, d, *args[0], *args[1], float(scale or 0.0),
+             ptr(out), dtype_code(out), ptr(ws), ws.numel(), stream())
     return out
 
 

@@ -5,9 +5,10 @@ constructor keywords, ``prefill/register/remove/reset``, the ``_step`` and
 ``retrievals``.
 
 Differences, all deliberate:
-* attention runs on the B200 kernels: ``kvr_decode_attn`` over the window and
-  the retrieved rows (int4w), or the fused sd1 step ``RetrievalIndex.attend``
-  (``codec='sd1'``), instead of the reference's einsum
+* attention runs on the B200 kernels through ``RetrievalIndex.attend``
+  (selection, gather, tensor-core V-predict and the window + retrieved
+  attention for int4w; the fused 1-bit step for ``codec='sd1'``), with no
+  host synchronisation, instead of the reference's einsum
   (modules/kvr_hook.py:274-282);
 * RoPE tables come from ``model.model.rotary_emb`` when the attention module
   has none (transformers >= 5 removed ``self_attn.rotary_emb``, which
@@ -15,8 +16,10 @@ Differences, all deliberate:
 * eviction un-rotates the evicted key at its own position ``pos - cap``; the
   reference un-rotates at ``pos`` (modules/kvr_hook.py:142-144) —
   ``reference_eviction_rope=True`` reproduces that for parity studies;
-* ``attractors=False`` skips the host-side k-means the reference runs after
-  prefill (modules/kvr_hook.py:133), so retrieval takes the kernel path.
+* the k-means the reference runs on the host after prefill
+  (modules/kvr_hook.py:133, sklearn) is a device Lloyd k-means here, and the
+  attractor branch it enables runs on kernels; ``attractors=False`` skips it
+  (token branch).
 The quality experiments of the reference (calibration s/b, MLP adapters,
 denoise steps, warm-up capture; modules/kvr_hook.py:157-214, 286-307) are kept
 as plain torch code — they are not part of the compressed-KV hot path.
@@ -266,15 +269,10 @@ class KVRHook:
         win = self.windows[li]
         ret = self.retrievals[li]
         active = self._ret_weight > 0 and self._retrieval_built and ret.n_tokens > 0
-        ex = exclusion_range(self._context_len, win.n, ret.n_stored)
-        if active and ret.codec == "sd1":
-            return ret.attend(q_post, win, ex[0], ex[1], out_dtype=out_dtype)
-        segs = [(win.k[:win.n], win.v[:win.n])]
         if active:
-            rk, rv = ret.retrieve_topk(q_post.float(), n_q=self.n_q, exclude_start=ex[0], exclude_end=ex[1])
-            if rk.shape[0]:
-                segs.append((rk, rv))
-        return K.decode_attn(q_post, segs, out_dtype=out_dtype, n_kv=self.n_kv)
+            ex = exclusion_range(self._context_len, win.n, ret.n_stored)
+            return ret.attend(q_post, win, ex[0], ex[1], out_dtype=out_dtype)
+        return K.decode_attn(q_post, [(win.k[:win.n], win.v[:win.n])], out_dtype=out_dtype, n_kv=self.n_kv)
 
     def register(self):
         for li in range(self.n_layers):

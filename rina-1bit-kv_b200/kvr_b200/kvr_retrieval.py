@@ -4,10 +4,12 @@ modules/kvr_retrieval.py.
 ``codec='int4w'`` (default) keeps the reference's format and semantics: int4
 K_pre codes with a per-(head, channel) absmax scale, V = W-predict(K) + int2
 per-head residual, both bit-packed (kvr_retrieval.py:2-4, 69-91, 95-207).
-Encode, scoring, top-k, gather and residual dequantisation run as sm_100a
-kernels; the two dense one-offs — ``torch.linalg.pinv`` in ``calibrate`` and
-the V-predict GEMM — stay library calls (cuSOLVER / cuBLAS), as in the
-reference.
+Encode, scoring, top-k (token, chunk and attractor branches), gather, the
+V-predict contraction (tensor cores, straight from the packed codes) and the
+residual dequantisation run as sm_100a kernels; the one dense one-off —
+``torch.linalg.pinv`` in ``calibrate`` — stays a library call, as in the
+reference.  ``attend`` runs a whole layer's retrieval + attention with no host
+synchronisation.
 
 ``codec='sd1'`` stores post-RoPE K and V as 1-bit sigma-delta codes in the
 Hadamard/DCT domain with per-tile fp16 scales (no reference counterpart; spec
@@ -68,6 +70,8 @@ class RetrievalIndex:
         self.n_attractors = 128
         self.attractors = None
         self.labels = None
+        self._vp = None          # (key, prepared V-predict weights)
+        self._csr = None         # (key, basin_start, basin_tokens)
         # sd1 state
         self.tile = tile
         self.transform = transform
@@ -255,33 +259,65 @@ class RetrievalIndex:
 
     @torch.no_grad()
     def compute_attractor_scores(self, q_post_rope):
-        """kvr_retrieval.py:248-263 (head-0 proxy)."""
+        """kvr_retrieval.py:248-263: cosine of the head-0 group-mean query
+        against every basin centroid, in column 0 of an (n_attractors, n_kv)
+        tensor (the reference scores head 0 only and leaves the other columns
+        unset; here they are zero)."""
         if self.attractors is None:
             return self.compute_all_scores(q_post_rope)
-        d, n_kv = self.d_head, self.n_kv
-        g = q_post_rope.shape[0] // n_kv
-        q_avg = q_post_rope.view(n_kv, g, d).mean(dim=1)
-        scores = torch.empty(self.attractors.shape[0], n_kv, device=self.device)
-        qn = q_avg[0] / (q_avg[0].norm() + 1e-8)
-        an = self.attractors / (self.attractors.norm(dim=-1, keepdim=True) + 1e-8)
-        scores[:, 0] = qn @ an.T
-        return scores
+        g = q_post_rope.shape[0] // self.n_kv
+        qa = q_post_rope[:g].float().mean(0)
+        cen = self.attractors.float()
+        out = torch.zeros(cen.shape[0], self.n_kv, device=cen.device)
+        out[:, 0] = (cen @ qa) / ((cen.norm(dim=1) + 1e-8) * (qa.norm() + 1e-8))
+        return out
 
     # --------------------------------------------------------- retrieval --
     def _empty(self):
         z = torch.zeros(0, self.n_kv, self.d_head, device=self.device, dtype=torch.float16)
         return z, z
 
+    def _basins_csr(self):
+        """Basin membership as a CSR list (tokens sorted within each basin),
+        rebuilt when the labels change."""
+        lab = self.labels
+        key = (lab.data_ptr(), lab._version, lab.numel(), self.attractors.shape[0])
+        if self._csr is None or self._csr[0] != key:
+            lab = lab.to(self.device).long()
+            order = torch.argsort(lab, stable=True).to(torch.int32)
+            counts = torch.bincount(lab, minlength=self.attractors.shape[0])
+            start = torch.zeros(self.attractors.shape[0] + 1, dtype=torch.int32, device=self.device)
+            start[1:] = torch.cumsum(counts, 0).to(torch.int32)
+            self._csr = (key, start, order.contiguous())
+        return self._csr[1], self._csr[2]
+
+    def _vpredict_weights(self):
+        """W' = W * diag(step) split for the tensor-core V-predict, prepared
+        once per calibration (re-prepared if W, the means or the scales are
+        replaced or modified in place)."""
+        parts = (self.W, self.K_mean, self.V_mean, self.k_scales)
+        key = tuple((t.data_ptr(), t._version) for t in parts)
+        if self._vp is None or self._vp[0] != key:
+            self._vp = (key, K.int4w_vpredict_prepare(self.W, self.K_mean, self.V_mean, self.k_scales, self.n_kv))
+        return self._vp[1]
+
     @torch.no_grad()
-    def select_indices(self, q_post_rope, exclude_start=0, exclude_end=0):
-        """Token indices (top_k, n_kv) the int4w retrieve_topk gathers, or None
-        when it would return nothing."""
+    def select_device(self, q_post_rope, exclude_start=0, exclude_end=0):
+        """The token indices retrieve_topk gathers, on the device: (top
+        (rows, n_kv) int64, count) where count is None (all rows valid) or a
+        device int32 (attractor branch, whose size is data-dependent); None
+        when the reference would return nothing.  No host synchronisation."""
         nr = self.n_stored
         if nr == 0 or exclude_start >= nr or (exclude_start <= 0 and exclude_end >= nr):
             return None
         top_k = min(self.top_k, nr)
         if self.attractors is not None and self.labels is not None:
-            return self._attractor_indices(q_post_rope, exclude_start, exclude_end)
+            # kvr_retrieval.py:332-367: top 48 basins x top 16 tokens, same list for every head
+            start, toks = self._basins_csr()
+            cos, sin, _ = self._tables(nr)
+            top_a = min(48, self.attractors.shape[0])
+            return K.int4w_attractor_select(q_post_rope, self.n_kv, self.k_packed, self.k_scales, cos, sin,
+                                            self.attractors, start, toks, top_a, exclude_start, exclude_end)
         cs = self.chunk_size
         if cs > 0 and nr >= cs * 2:
             # intended chunk branch (kvr_retrieval.py:370-388; the reference body is unreachable)
@@ -294,37 +330,34 @@ class RetrievalIndex:
             top_chunks = min(max(1, top_k // cs), n_chunks)
             cidx, _ = K.topk_rows(sc, top_chunks, ec0, ec1, transpose_out=True)  # (top_chunks, n_kv)
             tok = cidx.unsqueeze(1) * cs + torch.arange(cs, device=self.device).view(1, cs, 1)
-            return tok.reshape(top_chunks * cs, self.n_kv)
+            return tok.reshape(top_chunks * cs, self.n_kv), None
         cos, sin, he = self._tables(nr)
         sc = K.int4w_token_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, nr, he)
         idx, _ = K.topk_rows(sc, top_k, exclude_start, exclude_end, transpose_out=True)
-        return idx
+        return idx, None
 
-    def _attractor_indices(self, q_post_rope, exclude_start, exclude_end):
-        """kvr_retrieval.py:332-367 (host-assisted, parity unpinned)."""
-        scores = self.compute_attractor_scores(q_post_rope)
-        top_a = min(48, scores.shape[0])
-        top_aidx = torch.topk(scores[:, 0], top_a, dim=0)[1]
-        d, n_kv = self.d_head, self.n_kv
-        g = q_post_rope.shape[0] // n_kv
-        q_avg = q_post_rope.view(n_kv, g, d).mean(dim=1)
-        all_tidx = []
-        k0 = self._deq_k(0)
-        for aidx in top_aidx:
-            tidx = (self.labels == aidx).nonzero(as_tuple=True)[0]
-            if tidx.shape[0] <= self.top_per_basin:
-                all_tidx.append(tidx)
-            else:
-                kp_rot = self._rotary(k0[tidx], tidx)
-                kn = kp_rot / (kp_rot.norm(dim=-1, keepdim=True) + 1e-8)
-                qn = q_avg[0] / (q_avg[0].norm() + 1e-8)
-                all_tidx.append(tidx[(qn @ kn.T).argsort(descending=True)[:self.top_per_basin]])
-        all_tidx = torch.unique(torch.cat(all_tidx)) if all_tidx else torch.zeros(0, device=self.device, dtype=torch.long)
-        if exclude_end > exclude_start:
-            all_tidx = all_tidx[(all_tidx < exclude_start) | (all_tidx >= exclude_end)]
-        if all_tidx.shape[0] == 0:
+    @torch.no_grad()
+    def select_indices(self, q_post_rope, exclude_start=0, exclude_end=0):
+        """Token indices (rows, n_kv) the int4w retrieve_topk gathers, or None
+        when it would return nothing (reads the attractor branch's row count
+        back to the host)."""
+        sel = self.select_device(q_post_rope, exclude_start, exclude_end)
+        if sel is None:
             return None
-        return all_tidx.unsqueeze(1).expand(-1, self.n_kv).contiguous()
+        top, count = sel
+        if count is not None:
+            n = int(count.item())
+            if n == 0:
+                return None
+            top = top[:n]
+        return top
+
+    def _gather_kv(self, top, count=None):
+        cos, sin, _ = self._tables(self.n_stored)
+        ret_k, _ = K.int4w_gather(self.k_packed, self.k_scales, top, cos, sin, want_x=False, count=count)
+        ret_v = K.int4w_vpredict(self.k_packed, top, self._vpredict_weights(), self.vr_packed, self.vr_scales,
+                                 count=count)
+        return ret_k, ret_v
 
     @torch.no_grad()
     def retrieve_topk(self, q_post_rope, n_q=None, exclude_start=0, exclude_end=0):
@@ -336,18 +369,16 @@ class RetrievalIndex:
         top = self.select_indices(q_post_rope, exclude_start, exclude_end)
         if top is None:
             return self._empty()
-        cos, sin, _ = self._tables(self.n_stored)
-        ret_k, x = K.int4w_gather(self.k_packed, self.k_scales, top, cos, sin, self.K_mean)
-        # V-predict GEMM restricted to each head's output columns: (n_kv, k, D) @ (n_kv, D, d)
-        W_h = self.W.view(self.n_kv, self.d_head, self.kv_dim)
-        v_base = torch.baddbmm(self.V_mean.view(self.n_kv, 1, self.d_head), x, W_h.transpose(1, 2))
-        ret_v = K.int4w_vres_add(v_base, self.vr_packed, self.vr_scales, top)
-        return ret_k, ret_v
+        return self._gather_kv(top)
 
     @torch.no_grad()
     def retrieve(self, q_post_rope, n_q=None):
-        """Legacy per-Q-head path (kvr_retrieval.py:209-232): dot/sqrt(d) scores of
-        each Q head, its own top-k, softmax over those only."""
+        """Legacy per-Q-head path (kvr_retrieval.py:209-232): every query head
+        scores all stored tokens of its KV head by dot / sqrt(d) (post-RoPE),
+        keeps its own top_k and attends only those.  Kernel pieces: the
+        dequantised, re-rotated keys of all tokens (kvr_int4w_gather over
+        every index), per-head score rows, kvr_topk_rows, the V-predict
+        kernel, and one decode attention per query head."""
         self._require_int4w("retrieve")
         n_q = n_q or q_post_rope.shape[0]
         g = n_q // self.n_kv
@@ -357,19 +388,19 @@ class RetrievalIndex:
         if nr == 0:
             return out
         top_k = min(self.top_k, nr)
-        all_idx = torch.arange(nr, device=self.device)
+        every = torch.arange(nr, device=self.device).view(nr, 1).expand(nr, self.n_kv).contiguous()
+        cos, sin, _ = self._tables(nr)
+        k_post, _ = K.int4w_gather(self.k_packed, self.k_scales, every, cos, sin, want_x=False)  # (nr, n_kv, d)
+        q = q_post_rope[:n_q].float().view(self.n_kv, g, d)
+        # (n_kv, g, nr) dot products, one row per query head
+        sc = torch.einsum("hgd,thd->hgt", q, k_post).reshape(n_q, nr).div_(math.sqrt(d)).contiguous()
+        idx, _ = K.topk_rows(sc, top_k)                                    # (n_q, top_k)
         for hi in range(n_q):
             kvh = hi // g
-            qh = q_post_rope[hi].float()
-            k_post = self._rotary(self._deq_k(kvh), all_idx)
-            sim = (k_post @ qh) / math.sqrt(d)
-            sc = sim.unsqueeze(0).contiguous()
-            tidx = K.topk_rows(sc, top_k)[0][0]
-            k_top_post = k_post[tidx]
-            k_top_pre = self._unpack_int4(self.k_packed[tidx]).float() * (2 * self.k_scales / 16).unsqueeze(0)
-            v_top = self._reconstruct_v(k_top_pre, tidx)[:, kvh, :]
-            s = (k_top_post @ qh) / math.sqrt(d)
-            out[hi] = F.softmax(s, dim=-1) @ v_top
+            top = idx[hi].view(top_k, 1).expand(top_k, self.n_kv).contiguous()
+            rk, rv = self._gather_kv(top)
+            out[hi] = K.decode_attn(q_post_rope[hi:hi + 1].float(), [(rk[:, kvh:kvh + 1], rv[:, kvh:kvh + 1])],
+                                    out_dtype=torch.float32, n_kv=1)[0]
         return out
 
     def _require_int4w(self, what):
@@ -526,10 +557,30 @@ class RetrievalIndex:
 
     @torch.no_grad()
     def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None):
-        """sd1 fast path: one fused decode step over the window buffer, the
-        pending tail and the selected tiles.  q (n_q, d); returns (n_q, d)."""
-        if self.codec != "sd1":
-            raise NotImplementedError("attend() is the sd1 fused path")
+        """One layer's retrieval + attention for the current step, q (n_q, d)
+        -> (n_q, d): exact softmax over the window buffer (if given) and the
+        retrieved rows — the hook's einsum over cat(window, retrieved)
+        (kvr_hook.py:274-282) without materialising the concatenation and with
+        no host synchronisation.  int4w: selection (token, chunk or attractor
+        branch) -> gather -> tensor-core V-predict -> decode attention (the
+        attractor branch's row count stays on the device).  sd1: one fused
+        decode step over the window, the pending tail and the selected tiles."""
+        if self.codec == "int4w":
+            nw = window.n if window is not None else 0
+            out_dtype = out_dtype or torch.float32
+            sel = self.select_device(q_post_rope.float(), exclude_start, exclude_end) if self.n_stored else None
+            if sel is None and not nw:
+                return torch.zeros(q_post_rope.shape[0], self.d_head, dtype=out_dtype, device=q_post_rope.device)
+            if nw:
+                win = (window.k[:nw], window.v[:nw])
+            else:
+                z = torch.zeros(0, self.n_kv, self.d_head, dtype=torch.float16, device=q_post_rope.device)
+                win = (z, z)
+            if sel is None:
+                return K.decode_attn(q_post_rope, [win], out_dtype=out_dtype, n_kv=self.n_kv)
+            top, count = sel
+            rk, rv = self._gather_kv(top, count)
+            return K.decode_attn(q_post_rope, [win, (rk, rv)], out_dtype=out_dtype, n_kv=self.n_kv, n1_count=count)
         if self.store is None:
             self._sd1_reset()
         t = self.tile

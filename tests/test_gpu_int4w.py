@@ -83,11 +83,16 @@ def test_retrieval_index_encode_matches_reference_store():
     assert ri.n_stored == ns
     assert np.array_equal(ri.k_packed[:ns].cpu().numpy(), G["k_packed"][:ns])
     # int2 residual codes depend on the V-predict GEMM (cuSOLVER pinv + cuBLAS vs
-    # the reference's CPU LAPACK/BLAS): mismatches must be rare
+    # the reference's CPU LAPACK/BLAS): each mismatch must sit at a rounding
+    # boundary of the residual (checked against the reference's own W)
+    from test_oracle_golden_ext import residual_boundary_check
     got = R.unpack_int2(ri.vr_packed[:ns].cpu().numpy())
     want = R.unpack_int2(G["vr_packed"][:ns])
-    assert (got != want).mean() < 2e-2
-    assert (np.abs(got.astype(int) - want.astype(int)) <= 1).all()
+    vpred = R.predict_v(k[:ns].reshape(ns, -1), G["W"], G["K_mean"], G["V_mean"]).reshape(ns, 2, 128)
+    mine = R.predict_v(k[:ns].reshape(ns, -1), ri.W.cpu().numpy(), ri.K_mean.cpu().numpy(),
+                       ri.V_mean.cpu().numpy()).reshape(ns, 2, 128)
+    n_bad = residual_boundary_check(v[:ns], vpred, G["vr_scales"], got, want, rel=1e-5, vpred_alt=mine)
+    print(f"int2 residual codes differing from the reference: {n_bad} of {got.size}")
 
 
 # ----------------------------------------------------------------- scoring --
@@ -116,6 +121,28 @@ def test_compute_scores_dropin_vs_restated_kernel():
     got = run_score_kernel_cuda(t(qa), t(kp), t(ks), t(ch), t(sh)).cpu().numpy()
     want = R.scores_interleaved(qa, kp, ks, ch, sh, 2000)
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-4 * np.abs(want).max())
+
+
+@pytest.mark.parametrize("n,n_kv,d", [(2000, 8, 128), (4096, 8, 128), (777, 4, 128), (33, 2, 64), (300, 1, 256)])
+def test_compute_scores_bit_exact_vs_reference_kernel(n, n_kv, d):
+    """kvr_compute_scores against the reference's own modules/kvr_cuda.cu,
+    built unmodified for sm_100a by oracle/build_ref.py: identical bits."""
+    from oracle import build_ref
+    ref = build_ref.load_module()
+    if ref is None:
+        pytest.fail("oracle/_ref/kvr_cuda_ref.so missing: run __graft_entry__.build() where the reference exists")
+    from kvr_b200.kvr_cuda import run_score_kernel_cuda
+    rng = np.random.default_rng(n + d)
+    k = (rng.standard_normal((n, n_kv, d)) * np.exp(rng.standard_normal((n_kv, d)))).astype(F32)
+    ks = np.maximum(np.abs(k).max(0), 1e-8).astype(F32)
+    kp = R.pack_int4(R.quantize_k(k, ks))
+    ang = np.arange(n)[:, None] * (1.0 / 500000 ** (np.arange(d // 2) / (d // 2)))[None]
+    ch, sh = np.cos(ang).astype(F32), np.sin(ang).astype(F32)
+    qa = rng.standard_normal((n_kv, d)).astype(F32)
+    got = run_score_kernel_cuda(t(qa), t(kp), t(ks), t(ch), t(sh))
+    want = ref.compute_scores(t(qa), t(kp), t(ks), t(ch), t(sh), n_kv, d, n)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
 
 
 # ------------------------------------------------------------------- top-k --

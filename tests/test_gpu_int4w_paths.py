@@ -1,0 +1,208 @@
+"""GPU parity of the int4w device paths that replace the reference's eager
+torch code: the tensor-core V-predict (modules/kvr_retrieval.py:131-134,
+394-402), the attractor branch (:248-263, 332-367) and the fused
+RetrievalIndex.attend (the hook's window + retrieved softmax,
+modules/kvr_hook.py:250-282) — against the CPU oracle and the
+reference-generated fixture.  Every call goes through the C ABI."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import int4w_ref as R
+
+pytestmark = pytest.mark.gpu
+
+G = np.load(os.path.join(os.path.dirname(__file__), "golden", "int4w_golden.npz"))
+F32 = np.float32
+DEV = "cuda"
+
+
+def t(x, dtype=None):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV, dtype=dtype)
+
+
+def _store(seed, n, n_kv=8, d=128, n_q=32, theta=500000.0):
+    """Config-0 K/V, calibrated and packed by the oracle."""
+    rng = np.random.default_rng(seed)
+    scale = np.exp(rng.standard_normal((n_kv, d))).astype(F32)
+    for h in range(n_kv):
+        scale[h, rng.permutation(d)[:4]] *= 20
+    k = (rng.standard_normal((n, n_kv, d)) * scale).astype(F32)
+    v = (rng.standard_normal((n, n_kv, d)) + 0.3 * k / scale).astype(F32)
+    cal = R.calibrate(k, v)
+    st = dict(cal)
+    st["k_packed"] = R.pack_int4(R.quantize_k(k, cal["k_scales"]))
+    vpred = R.predict_v(k.reshape(n, -1), cal["W"], cal["K_mean"], cal["V_mean"]).reshape(k.shape)
+    st["vr_packed"] = R.pack_int2(R.quantize_vres(v, vpred, cal["vr_scales"]))
+    st["n_stored"] = n
+    cos, sin = R.rope_tables(n, d, theta)
+    q = rng.standard_normal((n_q, d)).astype(F32)
+    return st, cos.astype(F32), sin.astype(F32), q
+
+
+def _index(st, cos, sin, top_k, chunk_size=0):
+    from kvr_b200 import RetrievalIndex
+    n_kv = st["k_packed"].shape[1]
+    ri = RetrievalIndex(n_kv, 128, top_k=top_k, device=DEV, chunk_size=chunk_size)
+    ri.set_rotary_tables(t(cos), t(sin))
+    for x in ("k_scales", "W", "K_mean", "V_mean", "vr_scales", "k_packed", "vr_packed"):
+        setattr(ri, x, t(st[x]))
+    ri.n_stored = st["n_stored"]
+    return ri
+
+
+def _v_exact(st, top):
+    """float64 W-predict + residual of the tokens top (k, n_kv), before the
+    fp16 rounding (kvr_retrieval.py:394-402)."""
+    n_kv = st["k_packed"].shape[1]
+    kpre = R.unpack_int4(st["k_packed"][top]).astype(np.float64) * R.k_step(st["k_scales"])[None, None]
+    out = np.empty(top.shape + (128,))
+    W, km, vm = st["W"].astype(np.float64), st["K_mean"].astype(np.float64), st["V_mean"].astype(np.float64)
+    vstep = R.vr_step(st["vr_scales"]).astype(np.float64)
+    for h in range(n_kv):
+        x = kpre[:, h].reshape(len(top), -1) - km
+        vb = (x @ W.T + vm).reshape(len(top), n_kv, 128)[:, h]
+        res = R.unpack_int2(st["vr_packed"][top[:, h]][:, h]).astype(np.float64) * vstep[h]
+        out[:, h] = vb + res
+    return out
+
+
+@pytest.mark.parametrize("n,k,n_kv", [(3000, 1024, 8), (700, 100, 8), (500, 77, 2), (300, 64, 1)])
+def test_vpredict_kernel_vs_exact(n, k, n_kv):
+    """Tensor-core V-predict: every fp16 output within half an fp16 ulp of the
+    float64 value (plus 1e-6 of the largest value for summation order)."""
+    from kvr_b200 import kernels as K
+    st, cos, sin, q = _store(n + k, n, n_kv=n_kv, n_q=4 * n_kv)
+    rng = np.random.default_rng(k)
+    top = rng.integers(0, n, size=(k, n_kv)).astype(np.int64)
+    prep = K.int4w_vpredict_prepare(t(st["W"]), t(st["K_mean"]), t(st["V_mean"]), t(st["k_scales"]), n_kv)
+    got = K.int4w_vpredict(t(st["k_packed"]), t(top), prep, t(st["vr_packed"]), t(st["vr_scales"]))
+    got = got.float().cpu().numpy().astype(np.float64)
+    want = _v_exact(st, top)
+    ulp = np.spacing(np.abs(want).astype(np.float16)).astype(np.float64)
+    err = np.abs(got - want)
+    assert np.all(err <= 0.5 * ulp + 1e-6 * np.abs(want).max()), err.max()
+    # and the fp16 values agree with the oracle's fp32 path except at rounding boundaries
+    _, ov = R.gather_selected(st, top, cos, sin)
+    assert (got != ov.astype(np.float64)).mean() < 5e-3
+
+
+def test_vpredict_count_bounds_rows():
+    from kvr_b200 import kernels as K
+    st, cos, sin, q = _store(9, 400, n_kv=8)
+    top = np.random.default_rng(1).integers(0, 400, size=(128, 8)).astype(np.int64)
+    prep = K.int4w_vpredict_prepare(t(st["W"]), t(st["K_mean"]), t(st["V_mean"]), t(st["k_scales"]), 8)
+    out = torch.full((128, 8, 128), 7.0, dtype=torch.float16, device=DEV)
+    cnt = torch.tensor([70], dtype=torch.int32, device=DEV)
+    K.int4w_vpredict(t(st["k_packed"]), t(top), prep, t(st["vr_packed"]), t(st["vr_scales"]), count=cnt, out=out)
+    full = K.int4w_vpredict(t(st["k_packed"]), t(top), prep, t(st["vr_packed"]), t(st["vr_scales"]))
+    assert torch.equal(out[:70], full[:70])
+    assert bool((out[70:] == 7.0).all())
+
+
+def test_retrieve_topk_vs_reference_fixture_with_vpredict_kernel():
+    """The reference's own retrieve_topk outputs (fixture) reproduced with the
+    tensor-core V-predict (ret_v within fp16 rounding)."""
+    ns = int(G["n_stored"])
+    st = {x: G[x] for x in ("k_scales", "W", "K_mean", "V_mean", "vr_scales", "k_packed", "vr_packed")}
+    st["n_stored"] = ns
+    ri = _index(st, G["cos"], G["sin"], int(G["top_k"]))
+    rk, rv = ri.retrieve_topk(t(G["q_post"]), n_q=8)
+    np.testing.assert_allclose(rk.cpu().numpy(), G["ret_k"], rtol=1e-5, atol=1e-5)
+    want = G["ret_v"].astype(np.float64)
+    got = rv.float().cpu().numpy().astype(np.float64)
+    ulp = np.spacing(np.abs(G["ret_v"])).astype(np.float64)
+    assert np.all(np.abs(got - want) <= ulp * 1.0001)           # at most one fp16 ulp apart
+    assert (got != want).mean() < 1e-2
+
+
+def _attractor_case(seed=4, n=4096, n_kv=8):
+    from kvr_b200 import kernels as K
+    st, cos, sin, q = _store(seed, n, n_kv=n_kv)
+    ri = _index(st, cos, sin, top_k=512)
+    ri.build_attractors()
+    labels = ri.labels.cpu().numpy()
+    cent = ri.attractors.cpu().numpy()
+    return st, cos, sin, q, ri, labels, cent, K
+
+
+@pytest.mark.parametrize("ex", [(0, 0), (1000, 3000), (0, 4000)])
+def test_attractor_branch_vs_oracle(ex):
+    """Device attractor selection = the oracle's restatement of
+    kvr_retrieval.py:332-367 on the same basins; differences only between
+    near-tied scores (rel 1e-6)."""
+    st, cos, sin, q, ri, labels, cent, K = _attractor_case()
+    got = ri.select_indices(t(q), *ex)
+    want, bs, tok = R.attractor_select(q, st, cos, sin, labels, cent, 48, 16, *ex)
+    if got is None:
+        assert len(want) == 0
+        return
+    got = got.cpu().numpy()
+    assert np.all(got == got[:, :1])                  # the same list for every head
+    g0 = got[:, 0]
+    assert np.all(np.diff(g0) > 0)                    # ascending, unique
+    if set(g0.tolist()) != set(want.tolist()):
+        # only tokens whose basin-local score ties the 16th best may differ
+        diff = set(g0.tolist()) ^ set(want.tolist())
+        for tkn in diff:
+            b = labels[tkn]
+            tidx, sc = tok[int(b)]
+            kth = np.sort(sc)[::-1][15]
+            assert abs(sc[list(tidx).index(tkn)] - kth) <= 1e-6 * abs(kth), tkn
+    ex0, ex1 = ex
+    if ex1 > ex0:
+        assert not np.any((g0 >= ex0) & (g0 < ex1))
+
+
+def test_attractor_branch_empty_after_exclusion():
+    st, cos, sin, q, ri, labels, cent, K = _attractor_case(seed=6, n=1024)
+    sel = ri.select_device(t(q), 0, 1023)
+    top, count = sel
+    want, _, _ = R.attractor_select(q, st, cos, sin, labels, cent, 48, 16, 0, 1023)
+    assert int(count.item()) == len(want)
+    assert ri.select_indices(t(q), 0, 1023) is None or len(want) > 0
+
+
+@pytest.mark.parametrize("branch", ["token", "attractor", "chunk"])
+def test_fused_attend_equals_retrieve_then_attend(branch):
+    """RetrievalIndex.attend (no host sync; the attractor row count stays on
+    the device) = retrieve_topk followed by the window + retrieved attention."""
+    from kvr_b200 import WindowBuffer
+    from kvr_b200 import kernels as K
+    st, cos, sin, q = _store(12, 4096)
+    ri = _index(st, cos, sin, top_k=512, chunk_size=64 if branch == "chunk" else 0)
+    if branch == "attractor":
+        ri.build_attractors()
+    rng = np.random.default_rng(2)
+    wb = WindowBuffer(8, 128, window_size=256, device=DEV)
+    wb.batch_append(t(rng.standard_normal((256, 8, 128)).astype(F32)), t(rng.standard_normal((256, 8, 128)).astype(F32)))
+    qt = t(q)
+    for ex in ((0, 0), (3900, 4096)):
+        got = ri.attend(qt, wb, *ex)
+        rk, rv = ri.retrieve_topk(qt, n_q=32, exclude_start=ex[0], exclude_end=ex[1])
+        want = K.decode_attn(qt, [(wb.k[:wb.n], wb.v[:wb.n]), (rk, rv)], out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert torch.allclose(got, want, rtol=1e-6, atol=1e-6), (got - want).abs().max()
+        # and against the oracle's softmax over the concatenation
+        kc = np.concatenate([wb.k.float().cpu().numpy(), rk.cpu().numpy()])
+        vc = np.concatenate([wb.v.float().cpu().numpy(), rv.float().cpu().numpy()])
+        ref = R.softmax_attention(q, kc, vc)
+        assert np.abs(got.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_fused_attend_vs_reference_hook_fixture():
+    """hook_attn of the fixture (the reference's own hook softmax over
+    cat(window, retrieve_topk)) through RetrievalIndex.attend."""
+    from kvr_b200 import WindowBuffer
+    ns = int(G["n_stored"])
+    st = {x: G[x] for x in ("k_scales", "W", "K_mean", "V_mean", "vr_scales", "k_packed", "vr_packed")}
+    st["n_stored"] = ns
+    ri = _index(st, G["cos"], G["sin"], int(G["top_k"]))
+    wb = WindowBuffer(2, 128, window_size=64, device=DEV)
+    wb.k.copy_(t(G["win_k"]))
+    wb.v.copy_(t(G["win_v"]))
+    wb.pos, wb.n = int(G["win_pos"]), int(G["win_n"])
+    out = ri.attend(t(G["q_post"]), wb).cpu().numpy()
+    np.testing.assert_allclose(out, G["hook_attn"], rtol=1e-5, atol=1e-5)

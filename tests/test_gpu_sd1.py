@@ -479,3 +479,21 @@ def test_retrieval_index_sd1_api():
     want = K().decode_attn(t(q), [(wb.k, wb.v), (rk, rv)], out_dtype=torch.float32)
     # the API returns V in fp16 (reference format), the fused path keeps it exact
     np.testing.assert_allclose(out.cpu().numpy(), want.cpu().numpy(), rtol=3e-3, atol=3e-3)
+
+
+def test_bounded_wait_runs_out_and_is_reported():
+    """The kernels' bounded mbarrier wait, made to run out on purpose (a
+    phase that never completes, a short poll limit): the kernel returns,
+    kvr_workspace_status reports KVR_ETIMEOUT once and clears it, and the
+    same context keeps working."""
+    from kvr_b200 import _native as N
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    N.call("kvr_selftest_bounded_wait", N.ptr(ws), 256, N.stream())
+    with pytest.raises(N.KvrError, match="KVR_ETIMEOUT"):
+        N.call("kvr_workspace_status", N.ptr(ws), N.stream())
+    N.call("kvr_workspace_status", N.ptr(ws), N.stream())  # cleared: no error now
+    q = torch.randn(8, 128, device="cuda")
+    k = torch.randn(100, 2, 128, device="cuda").half()
+    out = K().decode_attn(q, [(k, k)], out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
