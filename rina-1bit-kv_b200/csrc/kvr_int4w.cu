@@ -191,16 +191,26 @@ __device__ __forceinline__ void stage_qavg(const float *__restrict__ q, int n_q,
 }
 
 // --------------------------------------------------- cosine token scores ----
-// 8 lanes per (token, head); lane s of the group owns dims 16s..16s+15.
-// rotate_half partners (i, i +/- 64) sit in lanes s and s ^ 4.
+// compute_all_scores (kvr_retrieval.py:265-289).  A warp owns 8 consecutive
+// tokens and all (<= 8) KV heads of each: lane = (head lane/4, quarter lane%4
+// of the 128 channels), so one 16-byte load per lane fetches a token's whole
+// packed row (n_kv * 64 contiguous bytes) and the rotate_half partner of
+// channel c (c +/- 64) sits in lane ^ 2.  The dequantisation steps and the
+// group-mean queries live in shared memory; the cos/sin rows are read as
+// float4 (half rows when both halves of the table are equal).  Scores of the
+// warp's 8 tokens are written as contiguous runs per head.
+constexpr int kTsTok = 8;  // tokens per warp item
 __global__ void __launch_bounds__(256) token_scores_kernel(
     const float *__restrict__ q, int n_q, const uint8_t *__restrict__ kp, const float *__restrict__ sc,
     const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, int halves_equal, int n_kv,
     int64_t n_stored, float *__restrict__ scores, int64_t score_stride) {
   constexpr int d = 128;
-  __shared__ float qa[8 * d];  // n_kv <= 8
+  __shared__ __align__(16) float qa[8 * d];  // n_kv <= 8
+  __shared__ __align__(16) float stp[8 * d];
   __shared__ float qn_s[8];
+  __shared__ float outb[8][8][kTsTok];       // [warp][head][token]
   stage_qavg(q, n_q, n_kv, d, qa);
+  for (int i = threadIdx.x; i < n_kv * d; i += blockDim.x) stp[i] = __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + i)), 16.0f);
   __syncthreads();
   if (threadIdx.x < n_kv) {
     float s = 0.0f;
@@ -208,49 +218,62 @@ __global__ void __launch_bounds__(256) token_scores_kernel(
     qn_s[threadIdx.x] = sqrtf(s) + 1e-8f;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, sub = lane & 7;
-  const int64_t total = n_stored * n_kv;
-  const int64_t gwarp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  // each warp covers 4 (token, head) pairs per iteration; the loop bound is warp-uniform
-  for (int64_t base = gwarp * 4; base < total; base += nwarps * 4) {
-    const int64_t pair = base + (lane >> 3);
-    const bool valid = pair < total;
-    const int64_t pp = valid ? pair : total - 1;
-    const int h = (int)(pp % n_kv);
-    const int64_t t = pp / n_kv;
-    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(kp + pp * (d / 2) + sub * 8));
-    const uint32_t w[2] = {raw.x, raw.y};
-    float kx[16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = lane >> 2, qd = lane & 3;
+  const bool hv = h < n_kv;
+  const int hh = hv ? h : 0;
+  const int c0 = qd * 32;
+  const int coff = halves_equal ? (c0 & 63) : c0;
+  const int64_t row_bytes = (int64_t)n_kv * (d / 2);
+  const int64_t items = (n_stored + kTsTok - 1) / kTsTok;
+  const float4 *qa4 = reinterpret_cast<const float4 *>(qa + hh * d + c0);
+  const float4 *st4 = reinterpret_cast<const float4 *>(stp + hh * d + c0);
+  for (int64_t it = (int64_t)blockIdx.x * 8 + warp; it < items; it += (int64_t)gridDim.x * 8) {
+    const int64_t t0 = it * kTsTok;
+#pragma unroll 2
+    for (int j = 0; j < kTsTok; ++j) {
+      const int64_t t = t0 + j < n_stored ? t0 + j : n_stored - 1;
+      uint4 raw = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+      if (hv) raw = __ldg(reinterpret_cast<const uint4 *>(kp + t * row_bytes + hh * (d / 2) + qd * 16));
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      const float4 *cr = reinterpret_cast<const float4 *>(cs + t * rope_stride + coff);
+      const float4 *sr = reinterpret_cast<const float4 *>(sn + t * rope_stride + coff);
+      float dot = 0.0f, nk = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 16; e += 2) {
-      const uint32_t byte = (w[e / 8] >> (8 * ((e / 2) & 3))) & 0xffu;
-      const int c = sub * 16 + e;
-      kx[e] = (float)((int)(byte >> 4) - 8) * __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + h * d + c)), 16.0f);
-      kx[e + 1] = (float)((int)(byte & 15) - 8) * __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + h * d + c + 1)), 16.0f);
-    }
-    const float *cr = cs + t * rope_stride;
-    const float *sr = sn + t * rope_stride;
-    const int coff = halves_equal ? ((sub * 16) & 63) : sub * 16;
-    float dot = 0.0f, nk = 0.0f;
+      for (int g4 = 0; g4 < 8; ++g4) {  // channels c0 + 4*g4 .. +3
+        const float4 cv = __ldg(cr + g4), sv = __ldg(sr + g4), qv = qa4[g4], sp = st4[g4];
+        const uint32_t two = (w[g4 >> 1] >> (16 * (g4 & 1))) & 0xffffu;
+        const float kx[4] = {__fmul_rn((float)((int)((two >> 4) & 15u) - 8), sp.x),
+                             __fmul_rn((float)((int)(two & 15u) - 8), sp.y),
+                             __fmul_rn((float)((int)((two >> 12) & 15u) - 8), sp.z),
+                             __fmul_rn((float)((int)((two >> 8) & 15u) - 8), sp.w)};
+        const float cvv[4] = {cv.x, cv.y, cv.z, cv.w}, svv[4] = {sv.x, sv.y, sv.z, sv.w};
+        const float qvv[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, kx[e], 4);
-      const float rh = sub < 4 ? -partner : partner;
-      const float kr = __fadd_rn(__fmul_rn(kx[e], __ldg(cr + coff + e)), __fmul_rn(rh, __ldg(sr + coff + e)));
-      dot = fmaf(qa[h * d + sub * 16 + e], kr, dot);
-      nk = fmaf(kr, kr, nk);
+        for (int e = 0; e < 4; ++e) {
+          const float partner = __shfl_xor_sync(0xffffffffu, kx[e], 2);
+          const float rh = qd < 2 ? -partner : partner;
+          const float kr = __fadd_rn(__fmul_rn(kx[e], cvv[e]), __fmul_rn(rh, svv[e]));
+          dot = fmaf(qvv[e], kr, dot);
+          nk = fmaf(kr, kr, nk);
+        }
+      }
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      nk += __shfl_xor_sync(0xffffffffu, nk, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      nk += __shfl_xor_sync(0xffffffffu, nk, 2);
+      if (qd == 0 && hv) {
+        float s = dot / (qn_s[hh] * (sqrtf(nk) + 1e-8f));
+        if (s != s) s = -INFINITY;
+        outb[warp][hh][j] = s;
+      }
     }
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      nk += __shfl_xor_sync(0xffffffffu, nk, o);
+    __syncwarp();
+    for (int e = lane; e < n_kv * kTsTok; e += 32) {
+      const int hh2 = e / kTsTok, j = e - hh2 * kTsTok;
+      if (t0 + j < n_stored) scores[(int64_t)hh2 * score_stride + t0 + j] = outb[warp][hh2][j];
     }
-    if (valid && sub == 0) {
-      float s = dot / (qn_s[h] * (sqrtf(nk) + 1e-8f));
-      if (s != s) s = -INFINITY;
-      scores[(int64_t)h * score_stride + t] = s;
-    }
+    __syncwarp();
   }
 }
 
@@ -313,6 +336,10 @@ __global__ void __launch_bounds__(256) chunk_scores_kernel(
 
 // ----------------------------------------------------------------- top-k ----
 constexpr int kTopkThreads = 1024;
+// One CTA per row.  STAGE: the row is first copied into shared memory (one
+// coalesced pass, exclusions and NaN mapped to -inf there), so the radix
+// passes of block_topk re-read it on chip instead of from L2.
+template <bool STAGE>
 __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float *__restrict__ scores, int64_t n,
                                                                  int64_t row_stride, int k, int64_t ex0,
                                                                  int64_t ex1, int64_t *__restrict__ idx,
@@ -322,8 +349,20 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float *__
   TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn);
   unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn + align_up(sizeof(TopkSmem), 16));
   const float *row = scores + (int64_t)blockIdx.x * row_stride;
-  block_topk<kTopkThreads>([&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldg(row + i); },
-                           n, k, cand, tsm);
+  if constexpr (STAGE) {
+    int P = 1;
+    while (P < k) P <<= 1;
+    float *srow = reinterpret_cast<float *>(dyn + align_up(sizeof(TopkSmem), 16) + (size_t)P * 8);
+    for (int64_t i = threadIdx.x; i < n; i += kTopkThreads) {
+      const float v = __ldcs(row + i);
+      srow[i] = (i >= ex0 && i < ex1) ? -INFINITY : v;
+    }
+    __syncthreads();
+    block_topk<kTopkThreads>([&](int64_t i) -> float { return srow[i]; }, n, k, cand, tsm);
+  } else {
+    block_topk<kTopkThreads>(
+        [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldg(row + i); }, n, k, cand, tsm);
+  }
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
     const int64_t o = (int64_t)blockIdx.x * ors + (int64_t)j * oes;
     idx[o] = key_index(cand[j]);
@@ -496,8 +535,13 @@ extern "C" int kvr_int4w_token_scores(const float *q, int n_q, const uint8_t *k_
   KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && scores, "kvr_int4w_token_scores: null pointer");
   KVR_REQUIRE(score_stride >= n_stored && rope_stride >= (rope_halves_equal ? 64 : 128), "kvr_int4w_token_scores: bad strides");
   if (n_stored <= 0) return KVR_OK;
-  const int64_t pairs = n_stored * n_kv;
-  token_scores_kernel<<<blocks_for(pairs, 32), 256, 0, as_cuda(stream)>>>(
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(k_packed) & 15) == 0 && (reinterpret_cast<uintptr_t>(cos_tbl) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sin_tbl) & 15) == 0 && rope_stride % 4 == 0,
+              "kvr_int4w_token_scores: packed rows and rope tables must be 16-byte aligned");
+  const int64_t items = (n_stored + kTsTok - 1) / kTsTok;
+  int64_t blocks = (items + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  token_scores_kernel<<<(unsigned)blocks, 256, 0, as_cuda(stream)>>>(
       q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride, rope_halves_equal, n_kv, n_stored, scores,
       score_stride);
   return check_launch("kvr_int4w_token_scores");
@@ -530,10 +574,19 @@ extern "C" int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t r
   if (rows == 0 || k == 0) return KVR_OK;
   int P = 1;
   while (P < k) P <<= 1;
-  const size_t smem = align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  topk_rows_kernel<<<rows, kTopkThreads, smem, as_cuda(stream)>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
-                                                                   out_row_stride, out_elem_stride);
+  const size_t base = align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
+  const size_t staged = base + (size_t)n * 4;
+  cudaStream_t st = as_cuda(stream);
+  if (staged <= 200 * 1024) {
+    cudaFuncSetAttribute(topk_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
+    topk_rows_kernel<true><<<rows, kTopkThreads, staged, st>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
+                                                               out_row_stride, out_elem_stride);
+  } else {
+    if (base > 48 * 1024)
+      cudaFuncSetAttribute(topk_rows_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)base);
+    topk_rows_kernel<false><<<rows, kTopkThreads, base, st>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
+                                                              out_row_stride, out_elem_stride);
+  }
   return check_launch("kvr_topk_rows");
 }
 

@@ -98,9 +98,18 @@ def lib():
     return _lib
 
 
+_FN: dict = {}
+
+
 def call(name: str, *args) -> int:
-    rc = getattr(lib(), name)(*args)
-    if name.endswith("_bytes") or name in ("kvr_last_error", "kvr_abi_version"):
+    """Call an entry point; a non-zero status raises KvrError (functions that
+    return sizes or strings are returned as they are)."""
+    ent = _FN.get(name)
+    if ent is None:
+        ent = _FN[name] = (getattr(lib(), name), name.endswith("_bytes") or name in ("kvr_last_error",
+                                                                                    "kvr_abi_version"))
+    rc = ent[0](*args)
+    if ent[1]:
         return rc
     if rc != 0:
         raise KvrError(rc, lib().kvr_last_error().decode())
@@ -137,7 +146,7 @@ class Workspace:
 
     def get(self, nbytes: int, device) -> torch.Tensor:
         nbytes = max(int(nbytes), 256)
-        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
             self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
         return self.buf
 
@@ -146,5 +155,8 @@ _WS: dict = {}
 
 
 def workspace(tag: str, nbytes: int, device) -> torch.Tensor:
-    ws = _WS.setdefault((tag, str(device)), Workspace())
+    device = device if isinstance(device, torch.device) else torch.device(device)
+    ws = _WS.get((tag, device))
+    if ws is None:
+        ws = _WS[(tag, device)] = Workspace()
     return ws.get(nbytes, device)

@@ -389,6 +389,9 @@ def sd1_attend(store: Sd1Store, q, qprime, sel, win_k=None, win_v=None, n_win=0,
     return part if partial else out
 
 
+_STEP_WS: dict = {}
+
+
 def sd1_decode_step(store: Sd1Store, q, k_sel, win_k=None, win_v=None, n_win=0, tail_k=None, tail_v=None,
                     n_tail=0, ex_t0=0, ex_t1=0, scale=None, out=None, sel_out=None, ws=None):
     """Fused select + attend (two launches).  Returns out (B, n_q, d)."""
@@ -398,8 +401,13 @@ def sd1_decode_step(store: Sd1Store, q, k_sel, win_k=None, win_v=None, n_win=0, 
         out = torch.empty(B, n_q, D, dtype=q.dtype, device=q.device)
     wk, wv, wcap, nw = _win_args(win_k, win_v, n_win)
     tk, tv = (ptr(tail_k), ptr(tail_v)) if n_tail else (None, None)
-    need = call("kvr_sd1_workspace_bytes", B, n_q, store.n_kv, store.n_tiles, store.tile, k_sel, nw, n_tail)
     if ws is None:
+        key = (B, n_q, store.n_kv, store.n_tiles, store.tile, k_sel, nw, n_tail)
+        need = _STEP_WS.get(key)
+        if need is None:
+            need = _STEP_WS[key] = call("kvr_sd1_workspace_bytes", *key)
+            if len(_STEP_WS) > 4096:
+                _STEP_WS.clear()
         ws = N.workspace("sd1_step", need, q.device)
     call("kvr_sd1_decode_step", ptr(q), dtype_code(q), B, n_q, store.n_kv, wk, wv, wcap, nw, tk, tv, n_tail,
          ptr(store.kbits), ptr(store.kscale), ptr(store.vbits), ptr(store.vscale), store.nt_cap, store.n_tiles,

@@ -10,7 +10,7 @@ window 256, top 8 tiles of 64 (top_k = 512 tokens); 16 queries N(0,1), 4 of
 them planted at cosine 0.9 to a random past (evicted) key.
 
 tiny_llama: a small random-init fp16 Llama (head_dim 128) for the
-generator-level fixture.
+generator-level fixture (see TINY).
 """
 import math
 
@@ -60,9 +60,14 @@ def config0_case(seed=4242):
             "planted_pos": planted, "n_ret": n_ret, **c}
 
 
-TINY = dict(vocab_size=256, hidden_size=512, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
-            num_key_value_heads=2, head_dim=128, max_position_embeddings=512, rope_theta=500000.0,
-            window=32, top_k=16, n_prompt=96, n_steps=12)
+# one KV head (n_kv*d = 128) and a 320-token prompt, so that the V-predict
+# fit of calibrate (kvr_retrieval.py:105-112, pinv on the first half of the
+# prompt: 160 samples of 128 dims) is well conditioned and the W of different
+# LAPACK implementations agree; 224 evicted tokens stay below the 256 that
+# would trigger the reference's host k-means.
+TINY = dict(vocab_size=256, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=2,
+            num_key_value_heads=1, head_dim=128, max_position_embeddings=512, rope_theta=500000.0,
+            window=96, top_k=16, n_prompt=320, n_steps=12)
 
 
 def tiny_llama(seed=7):

@@ -14,7 +14,7 @@ Writes next to this script:
   sha256 of the packed K codes, the packed int2 residual codes, the indices
   and the attention outputs; the inputs are regenerated from the seed.
 * generator_golden.npz — KVRGenerator (modules/kvr_generator.py:41-161) on
-  the tiny fp16 Llama of inputs.tiny_llama: prefill of 96 tokens, window 32,
+  the tiny fp16 Llama of inputs.tiny_llama: prefill of 320 tokens, window 96,
   top_k 16, then 12 steps fed with fixed token ids (the window is full from
   the first step, so every step evicts into the index); the lm_head logits of
   every step.

@@ -24,7 +24,7 @@ def test_evicted_k_codes_bit_exact(reference_rope):
     from kvr_b200 import KVRHook
     model, prompt, _ = inputs.tiny_llama()
     model = model.to("cuda")
-    hook = KVRHook(model, window_size=32, top_k=16, device="cuda", chunk_size=0,
+    hook = KVRHook(model, window_size=inputs.TINY["window"], top_k=16, device="cuda", chunk_size=0,
                    reference_eviction_rope=reference_rope)
     hook.prefill(prompt.to("cuda"))
     cos, sin = hook.cos_tbl.cpu().numpy(), hook.sin_tbl.cpu().numpy()

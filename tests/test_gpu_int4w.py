@@ -89,9 +89,10 @@ def test_retrieval_index_encode_matches_reference_store():
     got = R.unpack_int2(ri.vr_packed[:ns].cpu().numpy())
     want = R.unpack_int2(G["vr_packed"][:ns])
     vpred = R.predict_v(k[:ns].reshape(ns, -1), G["W"], G["K_mean"], G["V_mean"]).reshape(ns, 2, 128)
-    mine = R.predict_v(k[:ns].reshape(ns, -1), ri.W.cpu().numpy(), ri.K_mean.cpu().numpy(),
-                       ri.V_mean.cpu().numpy()).reshape(ns, 2, 128)
-    n_bad = residual_boundary_check(v[:ns], vpred, G["vr_scales"], got, want, rel=1e-5, vpred_alt=mine)
+    # the V prediction the GPU encoder itself used (same library call as batch_append / append)
+    mine = ri._predict_v(t(k[:ns]).reshape(ns, -1)).reshape(ns, 2, 128).cpu().numpy()
+    n_bad = residual_boundary_check(v[:ns], vpred, G["vr_scales"], got, want, rel=1e-5, vpred_alt=mine,
+                                    vr_scales_alt=ri.vr_scales.cpu().numpy())
     print(f"int2 residual codes differing from the reference: {n_bad} of {got.size}")
 
 
