@@ -191,89 +191,145 @@ __device__ __forceinline__ void stage_qavg(const float *__restrict__ q, int n_q,
 }
 
 // --------------------------------------------------- cosine token scores ----
-// compute_all_scores (kvr_retrieval.py:265-289).  A warp owns 8 consecutive
-// tokens and all (<= 8) KV heads of each: lane = (head lane/4, quarter lane%4
-// of the 128 channels), so one 16-byte load per lane fetches a token's whole
-// packed row (n_kv * 64 contiguous bytes) and the rotate_half partner of
-// channel c (c +/- 64) sits in lane ^ 2.  The dequantisation steps and the
-// group-mean queries live in shared memory; the cos/sin rows are read as
-// float4 (half rows when both halves of the table are equal).  Scores of the
-// warp's 8 tokens are written as contiguous runs per head.
-constexpr int kTsTok = 8;  // tokens per warp item
+// compute_all_scores (kvr_retrieval.py:265-289).  Persistent CTAs walk tiles
+// of 32 tokens.  The tile's packed rows (32 * n_kv * 64 contiguous bytes) and
+// its cos/sin rows (half rows when both halves of the table are equal) are
+// brought into shared memory by cp.async, two tiles in flight, so the next
+// tile streams in while this one is scored.  Warp w scores tokens 4w..4w+3
+// of the tile, all (<= 8) heads at once: lane = (head lane/4, group lane%4);
+// group g covers channels [16g, 16g+16) and their rotate_half partners
+// [64+16g, 64+16g+16), so a lane rotates its own pairs with no shuffles.
+// The dequantisation steps and the group-mean queries sit in a padded
+// shared layout (the 8 lanes of a quarter-warp hit 8 distinct bank groups).
+// Each element's arithmetic is the reference's: k = code*step, k_rot =
+// k*cos + rotate_half(k)*sin (three roundings), then dot and norm.
+constexpr int kTsTile = 32;
+__device__ __forceinline__ int ts_idx(int h, int c) { return h * 176 + c + (c >> 4) * 4; }
 __global__ void __launch_bounds__(256) token_scores_kernel(
     const float *__restrict__ q, int n_q, const uint8_t *__restrict__ kp, const float *__restrict__ sc,
     const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, int halves_equal, int n_kv,
     int64_t n_stored, float *__restrict__ scores, int64_t score_stride) {
   constexpr int d = 128;
-  __shared__ __align__(16) float qa[8 * d];  // n_kv <= 8
-  __shared__ __align__(16) float stp[8 * d];
+  __shared__ __align__(16) float qa[8 * 176];  // n_kv <= 8
+  __shared__ __align__(16) float stp[8 * 176];
   __shared__ float qn_s[8];
-  __shared__ float outb[8][8][kTsTok];       // [warp][head][token]
-  stage_qavg(q, n_q, n_kv, d, qa);
-  for (int i = threadIdx.x; i < n_kv * d; i += blockDim.x) stp[i] = __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + i)), 16.0f);
-  __syncthreads();
-  if (threadIdx.x < n_kv) {
+  __shared__ float outb[8][kTsTile];           // [head][token]
+  extern __shared__ __align__(16) unsigned char dsm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row_bytes = n_kv * (d / 2);
+  const int cw = halves_equal ? 64 : 128;          // table floats kept per token
+  const int k_bytes = kTsTile * row_bytes;
+  const int t_bytes = kTsTile * cw * 4;
+  const int stage_bytes = k_bytes + 2 * t_bytes;
+  const int64_t tiles = (n_stored + kTsTile - 1) / kTsTile;
+
+  auto issue = [&](int64_t tile, int stage) {
+    unsigned char *base = dsm + stage * stage_bytes;
+    const int64_t t0 = tile * kTsTile;
+    const int nt = (int)(n_stored - t0 < kTsTile ? n_stored - t0 : kTsTile);
+    const unsigned char *ksrc = kp + t0 * row_bytes;
+    for (int p = tid; p < nt * row_bytes / 16; p += blockDim.x) cp_async16(base + p * 16, ksrc + p * 16);
+    const int per = cw / 4;  // 16-byte pieces per table row
+    for (int p = tid; p < nt * per; p += blockDim.x) {
+      const int j = p / per, o = p - j * per;
+      cp_async16(base + k_bytes + (j * cw + o * 4) * 4, cs + (t0 + j) * rope_stride + o * 4);
+      cp_async16(base + k_bytes + t_bytes + (j * cw + o * 4) * 4, sn + (t0 + j) * rope_stride + o * 4);
+    }
+    cp_async_commit();
+  };
+  int64_t tile = blockIdx.x;
+  if (tile < tiles) issue(tile, 0);
+  const int g = n_q / n_kv;
+  for (int i = tid; i < n_kv * d; i += blockDim.x) {
+    const int h = i / d, c = i - h * d;
     float s = 0.0f;
-    for (int c = 0; c < d; ++c) s += qa[threadIdx.x * d + c] * qa[threadIdx.x * d + c];
-    qn_s[threadIdx.x] = sqrtf(s) + 1e-8f;
+    for (int j = 0; j < g; ++j) s += __ldg(q + (int64_t)(h * g + j) * d + c);
+    qa[ts_idx(h, c)] = s / (float)g;
+    stp[ts_idx(h, c)] = __fdiv_rn(__fmul_rn(2.0f, __ldg(sc + i)), 16.0f);
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int h = lane >> 2, qd = lane & 3;
+  if (warp < n_kv) {
+    float s = 0.0f;
+    for (int c = lane; c < d; c += 32) s = fmaf(qa[ts_idx(warp, c)], qa[ts_idx(warp, c)], s);
+    s = warp_sum(s);
+    if (lane == 0) qn_s[warp] = sqrtf(s) + 1e-8f;
+  }
+  const int h = lane >> 2, gq = lane & 3;
   const bool hv = h < n_kv;
   const int hh = hv ? h : 0;
-  const int c0 = qd * 32;
-  const int coff = halves_equal ? (c0 & 63) : c0;
-  const int64_t row_bytes = (int64_t)n_kv * (d / 2);
-  const int64_t items = (n_stored + kTsTok - 1) / kTsTok;
-  const float4 *qa4 = reinterpret_cast<const float4 *>(qa + hh * d + c0);
-  const float4 *st4 = reinterpret_cast<const float4 *>(stp + hh * d + c0);
-  for (int64_t it = (int64_t)blockIdx.x * 8 + warp; it < items; it += (int64_t)gridDim.x * 8) {
-    const int64_t t0 = it * kTsTok;
-#pragma unroll 2
-    for (int j = 0; j < kTsTok; ++j) {
-      const int64_t t = t0 + j < n_stored ? t0 + j : n_stored - 1;
-      uint4 raw = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-      if (hv) raw = __ldg(reinterpret_cast<const uint4 *>(kp + t * row_bytes + hh * (d / 2) + qd * 16));
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-      const float4 *cr = reinterpret_cast<const float4 *>(cs + t * rope_stride + coff);
-      const float4 *sr = reinterpret_cast<const float4 *>(sn + t * rope_stride + coff);
+  const int c_lo = gq * 16, c_hi = 64 + gq * 16;
+  const int tc_hi = halves_equal ? c_lo : c_hi;
+  const float4 *qlo = reinterpret_cast<const float4 *>(qa + ts_idx(hh, c_lo));
+  const float4 *qhi = reinterpret_cast<const float4 *>(qa + ts_idx(hh, c_hi));
+  const float4 *slo = reinterpret_cast<const float4 *>(stp + ts_idx(hh, c_lo));
+  const float4 *shi = reinterpret_cast<const float4 *>(stp + ts_idx(hh, c_hi));
+  for (int it = 0; tile < tiles; ++it, tile += gridDim.x) {
+    const int st = it & 1;
+    if (tile + gridDim.x < tiles) {
+      issue(tile + gridDim.x, st ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const unsigned char *base = dsm + st * stage_bytes;
+    const float *cst = reinterpret_cast<const float *>(base + k_bytes);
+    const float *snt = reinterpret_cast<const float *>(base + k_bytes + t_bytes);
+    const int64_t t0 = tile * kTsTile;
+#pragma unroll 1
+    for (int jj = 0; jj < kTsTile / 8; ++jj) {
+      const int j = warp * (kTsTile / 8) + jj;
+      const uint8_t *row = base + j * row_bytes + hh * (d / 2);
+      const uint2 rlo = *reinterpret_cast<const uint2 *>(row + c_lo / 2);
+      const uint2 rhi = *reinterpret_cast<const uint2 *>(row + c_hi / 2);
+      const float4 *crl = reinterpret_cast<const float4 *>(cst + j * cw + c_lo);
+      const float4 *srl = reinterpret_cast<const float4 *>(snt + j * cw + c_lo);
+      const float4 *crh = reinterpret_cast<const float4 *>(cst + j * cw + tc_hi);
+      const float4 *srh = reinterpret_cast<const float4 *>(snt + j * cw + tc_hi);
       float dot = 0.0f, nk = 0.0f;
 #pragma unroll
-      for (int g4 = 0; g4 < 8; ++g4) {  // channels c0 + 4*g4 .. +3
-        const float4 cv = __ldg(cr + g4), sv = __ldg(sr + g4), qv = qa4[g4], sp = st4[g4];
-        const uint32_t two = (w[g4 >> 1] >> (16 * (g4 & 1))) & 0xffffu;
-        const float kx[4] = {__fmul_rn((float)((int)((two >> 4) & 15u) - 8), sp.x),
-                             __fmul_rn((float)((int)(two & 15u) - 8), sp.y),
-                             __fmul_rn((float)((int)((two >> 12) & 15u) - 8), sp.z),
-                             __fmul_rn((float)((int)((two >> 8) & 15u) - 8), sp.w)};
-        const float cvv[4] = {cv.x, cv.y, cv.z, cv.w}, svv[4] = {sv.x, sv.y, sv.z, sv.w};
-        const float qvv[4] = {qv.x, qv.y, qv.z, qv.w};
+      for (int g4 = 0; g4 < 4; ++g4) {  // channels c_lo + 4*g4 .. +3 and their partners c_hi + 4*g4 ..
+        const float4 cl = crl[g4], sl = srl[g4], ch = crh[g4], sh = srh[g4];
+        const float4 ql = qlo[g4], qh = qhi[g4], pl = slo[g4], ph = shi[g4];
+        const uint32_t wl = ((g4 < 2 ? rlo.x : rlo.y) >> (16 * (g4 & 1))) & 0xffffu;
+        const uint32_t wh = ((g4 < 2 ? rhi.x : rhi.y) >> (16 * (g4 & 1))) & 0xffffu;
+        const float al[4] = {__fmul_rn((float)((int)((wl >> 4) & 15u) - 8), pl.x),
+                             __fmul_rn((float)((int)(wl & 15u) - 8), pl.y),
+                             __fmul_rn((float)((int)((wl >> 12) & 15u) - 8), pl.z),
+                             __fmul_rn((float)((int)((wl >> 8) & 15u) - 8), pl.w)};
+        const float ah[4] = {__fmul_rn((float)((int)((wh >> 4) & 15u) - 8), ph.x),
+                             __fmul_rn((float)((int)(wh & 15u) - 8), ph.y),
+                             __fmul_rn((float)((int)((wh >> 12) & 15u) - 8), ph.z),
+                             __fmul_rn((float)((int)((wh >> 8) & 15u) - 8), ph.w)};
+        const float cvl[4] = {cl.x, cl.y, cl.z, cl.w}, svl[4] = {sl.x, sl.y, sl.z, sl.w};
+        const float cvh[4] = {ch.x, ch.y, ch.z, ch.w}, svh[4] = {sh.x, sh.y, sh.z, sh.w};
+        const float qvl[4] = {ql.x, ql.y, ql.z, ql.w}, qvh[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float partner = __shfl_xor_sync(0xffffffffu, kx[e], 2);
-          const float rh = qd < 2 ? -partner : partner;
-          const float kr = __fadd_rn(__fmul_rn(kx[e], cvv[e]), __fmul_rn(rh, svv[e]));
-          dot = fmaf(qvv[e], kr, dot);
-          nk = fmaf(kr, kr, nk);
+          // rotate_half: channel c < 64 pairs with -k[c+64], channel c+64 with +k[c]
+          const float kl = __fadd_rn(__fmul_rn(al[e], cvl[e]), __fmul_rn(-ah[e], svl[e]));
+          const float kh = __fadd_rn(__fmul_rn(ah[e], cvh[e]), __fmul_rn(al[e], svh[e]));
+          dot = fmaf(qvl[e], kl, dot);
+          nk = fmaf(kl, kl, nk);
+          dot = fmaf(qvh[e], kh, dot);
+          nk = fmaf(kh, kh, nk);
         }
       }
       dot += __shfl_xor_sync(0xffffffffu, dot, 1);
       nk += __shfl_xor_sync(0xffffffffu, nk, 1);
       dot += __shfl_xor_sync(0xffffffffu, dot, 2);
       nk += __shfl_xor_sync(0xffffffffu, nk, 2);
-      if (qd == 0 && hv) {
+      if (gq == 0 && hv) {
         float s = dot / (qn_s[hh] * (sqrtf(nk) + 1e-8f));
         if (s != s) s = -INFINITY;
-        outb[warp][hh][j] = s;
+        outb[hh][j] = s;
       }
     }
-    __syncwarp();
-    for (int e = lane; e < n_kv * kTsTok; e += 32) {
-      const int hh2 = e / kTsTok, j = e - hh2 * kTsTok;
-      if (t0 + j < n_stored) scores[(int64_t)hh2 * score_stride + t0 + j] = outb[warp][hh2][j];
+    __syncthreads();
+    for (int e = tid; e < n_kv * kTsTile; e += blockDim.x) {
+      const int h2 = e / kTsTile, j = e - h2 * kTsTile;
+      if (t0 + j < n_stored) scores[(int64_t)h2 * score_stride + t0 + j] = outb[h2][j];
     }
-    __syncwarp();
   }
 }
 
@@ -364,6 +420,194 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float *__
         [&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldg(row + i); }, n, k, cand, tsm);
   }
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const int64_t o = (int64_t)blockIdx.x * ors + (int64_t)j * oes;
+    idx[o] = key_index(cand[j]);
+    if (vals) vals[o] = key_score(cand[j]);
+  }
+}
+
+// Long rows (n in the tens of thousands, k up to ~1/8 of n): the row is staged
+// in shared memory, then a 4096-bin histogram over the linear map of the
+// finite scores' [min, max] range (a monotone map, so every key of a higher
+// bin beats every key of a lower one) locates the bin holding the k-th
+// largest score.  Keys of higher bins are taken outright; only that bin's
+// keys go through the exact radix selection, then the k keys are sorted
+// (score desc, index asc).  When the threshold bin is too crowded for the
+// candidate buffer, or fewer than k scores are finite, the CTA falls back to
+// the whole-row radix select.
+constexpr int kHistBins = 4096;
+constexpr int kHistCand = 4096;
+struct HistSmem {
+  int hist[kHistBins];
+  float mn[32], mx[32];
+  int thr_bin, above, n_cand, n_take, n_finite;
+  float lo, scale;
+};
+__global__ void __launch_bounds__(kTopkThreads) topk_rows_hist_kernel(const float *__restrict__ scores, int64_t n,
+                                                                      int64_t row_stride, int k, int64_t ex0,
+                                                                      int64_t ex1, int64_t *__restrict__ idx,
+                                                                      float *__restrict__ vals, int64_t ors,
+                                                                      int64_t oes) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn);
+  size_t off = align_up(sizeof(TopkSmem), 16);
+  HistSmem &hs = *reinterpret_cast<HistSmem *>(dyn + off);
+  off += align_up(sizeof(HistSmem), 16);
+  int P = 1;
+  while (P < k) P <<= 1;
+  unsigned long long *cand = reinterpret_cast<unsigned long long *>(dyn + off);   // P keys: the answer
+  off += (size_t)P * 8;
+  unsigned long long *cand2 = reinterpret_cast<unsigned long long *>(dyn + off);  // threshold-bin keys
+  off += (size_t)kHistCand * 8;
+  unsigned long long *cand3 = reinterpret_cast<unsigned long long *>(dyn + off);  // P keys: their top
+  off += (size_t)P * 8;
+  float *srow = reinterpret_cast<float *>(dyn + off);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float *row = scores + (int64_t)blockIdx.x * row_stride;
+  float mn = INFINITY, mx = -INFINITY;
+  int nf = 0;
+  for (int64_t r0 = 0; r0 < n; r0 += 8 * kTopkThreads) {  // 8 loads in flight per thread
+    float vv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t i = r0 + u * kTopkThreads + tid;
+      vv[u] = i < n ? __ldcs(row + i) : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t i = r0 + u * kTopkThreads + tid;
+      if (i >= n) continue;
+      float v = vv[u];
+      if ((i >= ex0 && i < ex1) || v != v) v = -INFINITY;
+      srow[i] = v;
+      if (v > -INFINITY && v < INFINITY) {
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+        ++nf;
+      }
+    }
+  }
+  for (int b = tid; b < kHistBins; b += kTopkThreads) hs.hist[b] = 0;
+  mn = -warp_max(-mn);
+  mx = warp_max(mx);
+  nf = warp_sum_int(nf);
+  if (lane == 0) {
+    hs.mn[warp] = mn;
+    hs.mx[warp] = mx;
+  }
+  if (tid == 0) {
+    hs.n_finite = 0;
+    hs.above = 0;
+    hs.n_cand = 0;
+  }
+  __syncthreads();
+  if (lane == 0) atomicAdd(&hs.n_finite, nf);
+  if (tid == 0) {
+    float a = INFINITY, b = -INFINITY;
+    for (int w = 0; w < kTopkThreads / 32; ++w) {
+      a = fminf(a, hs.mn[w]);
+      b = fmaxf(b, hs.mx[w]);
+    }
+    hs.lo = a;
+    hs.scale = (b > a) ? (float)(kHistBins - 1) / (b - a) : 0.0f;
+  }
+  __syncthreads();
+  const float lo = hs.lo, scale = hs.scale;
+  auto bin_of = [&](float v) -> int {
+    int b = (int)((v - lo) * scale);
+    return b < 0 ? 0 : (b >= kHistBins ? kHistBins - 1 : b);
+  };
+  bool fallback = hs.n_finite < k;
+  if (!fallback) {
+    for (int64_t i = tid; i < n; i += kTopkThreads) {
+      const float v = srow[i];
+      if (v > -INFINITY && v < INFINITY) atomicAdd(&hs.hist[bin_of(v)], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // suffix counts from the top bin down: lane l owns bins [128*(31-l), 128*(32-l))
+      int s = 0;
+      const int b_hi = kHistBins - 128 * lane;
+      for (int b = b_hi - 1; b >= b_hi - 128; --b) s += hs.hist[b];
+      int incl = s;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int excl = incl - s;
+      if (excl < k && k <= incl) {
+        int cum = excl;
+        for (int b = b_hi - 1; b >= b_hi - 128; --b) {
+          if (cum + hs.hist[b] >= k) {
+            hs.thr_bin = b;
+            hs.above = cum;
+            break;
+          }
+          cum += hs.hist[b];
+        }
+      }
+    }
+    __syncthreads();
+    fallback = hs.hist[hs.thr_bin] > kHistCand;
+  }
+  if (fallback) {  // (uniform across the block)
+    block_topk<kTopkThreads>([&](int64_t i) -> float { return srow[i]; }, n, k, cand, tsm);
+  } else {
+    const int thr = hs.thr_bin;
+    __shared__ int n_above;
+    __shared__ int wcount[kTopkThreads / 32];
+    if (tid == 0) n_above = 0;
+    __syncthreads();
+    // keys of higher bins in any order (they are sorted below); keys of the
+    // threshold bin in index order, so that block_topk's position tie-break
+    // over cand2 is the index tie-break of the row
+    int base_pos = 0;
+    for (int64_t r0 = 0; r0 < n; r0 += kTopkThreads) {
+      const int64_t i = r0 + tid;
+      float v = -INFINITY;
+      if (i < n) v = srow[i];
+      const bool fin = v > -INFINITY && v < INFINITY;
+      const int b = fin ? bin_of(v) : -1;
+      if (b > thr) cand[atomicAdd(&n_above, 1)] = make_key(v, i);
+      const bool in_thr = (b == thr);
+      const unsigned bal = __ballot_sync(0xffffffffu, in_thr);
+      if (lane == 0) wcount[warp] = __popc(bal);
+      __syncthreads();
+      int before = base_pos, total = 0;
+      for (int w = 0; w < kTopkThreads / 32; ++w) {
+        const int c = wcount[w];
+        if (w < warp) before += c;
+        total += c;
+      }
+      if (in_thr) cand2[before + __popc(bal & ((1u << lane) - 1u))] = make_key(v, i);
+      base_pos += total;
+      __syncthreads();
+    }
+    if (tid == 0) hs.n_cand = base_pos;
+    __syncthreads();
+    const int na = n_above, nc = hs.n_cand, need = k - na;
+    block_topk<kTopkThreads>([&](int64_t i) -> float { return key_score(cand2[i]); }, nc, need, cand3, tsm);
+    // cand3 holds positions in cand2 as its indices: map back to the row keys
+    for (int j = tid; j < need; j += kTopkThreads) cand[na + j] = cand2[key_index(cand3[j])];
+    for (int j = k + tid; j < P; j += kTopkThreads) cand[j] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < P / 2; i += kTopkThreads) {
+          const int a = 2 * i - (i & (stride - 1));
+          const int b = a + stride;
+          const bool desc = ((a & size) == 0);
+          const unsigned long long x = cand[a], y = cand[b];
+          if ((x < y) == desc) {
+            cand[a] = y;
+            cand[b] = x;
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+  for (int j = tid; j < k; j += blockDim.x) {
     const int64_t o = (int64_t)blockIdx.x * ors + (int64_t)j * oes;
     idx[o] = key_index(cand[j]);
     if (vals) vals[o] = key_score(cand[j]);
@@ -538,10 +782,19 @@ extern "C" int kvr_int4w_token_scores(const float *q, int n_q, const uint8_t *k_
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(k_packed) & 15) == 0 && (reinterpret_cast<uintptr_t>(cos_tbl) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(sin_tbl) & 15) == 0 && rope_stride % 4 == 0,
               "kvr_int4w_token_scores: packed rows and rope tables must be 16-byte aligned");
-  const int64_t items = (n_stored + kTsTok - 1) / kTsTok;
-  int64_t blocks = (items + 7) / 8;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  token_scores_kernel<<<(unsigned)blocks, 256, 0, as_cuda(stream)>>>(
+  KVR_REQUIRE(rope_stride >= (rope_halves_equal ? 64 : 128), "kvr_int4w_token_scores: rope rows too short");
+  const int cw = rope_halves_equal ? 64 : 128;
+  const size_t smem = 2 * ((size_t)kTsTile * n_kv * 64 + 2 * (size_t)kTsTile * cw * 4);
+  const int64_t tiles = (n_stored + kTsTile - 1) / kTsTile;
+  static thread_local int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    cudaFuncSetAttribute(token_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    attr_dev = dev;
+  }
+  int64_t blocks = tiles < 148 * 3 ? tiles : 148 * 3;
+  token_scores_kernel<<<(unsigned)blocks, 256, smem, as_cuda(stream)>>>(
       q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride, rope_halves_equal, n_kv, n_stored, scores,
       score_stride);
   return check_launch("kvr_int4w_token_scores");
@@ -576,8 +829,14 @@ extern "C" int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t r
   while (P < k) P <<= 1;
   const size_t base = align_up(sizeof(TopkSmem), 16) + (size_t)P * 8;
   const size_t staged = base + (size_t)n * 4;
+  const size_t hist = align_up(sizeof(TopkSmem), 16) + align_up(sizeof(HistSmem), 16) + (size_t)P * 16 +
+                      (size_t)kHistCand * 8 + (size_t)n * 4;
   cudaStream_t st = as_cuda(stream);
-  if (staged <= 200 * 1024) {
+  if (n >= 8192 && (int64_t)k * 4 <= n && hist <= 220 * 1024) {
+    cudaFuncSetAttribute(topk_rows_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist);
+    topk_rows_hist_kernel<<<rows, kTopkThreads, hist, st>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
+                                                             out_row_stride, out_elem_stride);
+  } else if (staged <= 200 * 1024) {
     cudaFuncSetAttribute(topk_rows_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
     topk_rows_kernel<true><<<rows, kTopkThreads, staged, st>>>(scores, n, row_stride, k, ex_start, ex_end, idx, vals,
                                                                out_row_stride, out_elem_stride);

@@ -160,10 +160,21 @@ __device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long lon
     if (sm.bin_count == sm.remaining) break;
   }
   const unsigned long long prefix = sm.prefix, mask = sm.mask;
-  for (int64_t i = tid; i < n; i += NT) {
-    const unsigned long long key = make_key(score_of(i), i);
-    if ((key & mask) >= prefix) {
-      const int slot = atomicAdd(&sm.n_out, 1);
+  for (int64_t base = 0; base < n; base += NT) {
+    const int64_t i = base + tid;
+    unsigned long long key = 0ull;
+    bool take = false;
+    if (i < n) {
+      key = make_key(score_of(i), i);
+      take = (key & mask) >= prefix;
+    }
+    // one atomic per warp for the slots of its selected keys
+    const unsigned ballot = __ballot_sync(0xffffffffu, take);
+    int first = 0;
+    if (ballot && lane == __ffs(ballot) - 1) first = atomicAdd(&sm.n_out, __popc(ballot));
+    first = __shfl_sync(0xffffffffu, first, __ffs(ballot ? ballot : 1u) - 1);
+    if (take) {
+      const int slot = first + __popc(ballot & ((1u << lane) - 1u));
       if (slot < k) cand[slot] = key;
     }
   }

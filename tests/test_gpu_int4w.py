@@ -164,6 +164,21 @@ def test_topk_rows_bit_exact(n, k):
     assert np.array_equal(idx.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("n,k,dec", [(32256, 1024, 3), (32256, 1024, 2), (20000, 16, 4), (9000, 2000, 2)])
+def test_topk_rows_long_rows_with_ties(n, k, dec):
+    """Long rows take the histogram path: ties inside the threshold bin (scores
+    rounded to `dec` decimals) must still come out index-ascending."""
+    rng = np.random.default_rng(n + k + dec)
+    s = np.round(rng.standard_normal((4, n)) * 0.2, dec).astype(F32)
+    s[3, ::5] = np.nan
+    ex = (n // 3, n // 3 + 100)
+    idx, vals = K().topk_rows(t(s), k, *ex)
+    sm = s.astype(np.float64)
+    sm[:, ex[0]:ex[1]] = -np.inf
+    want = R.topk_rule(sm.T, k).T
+    assert np.array_equal(idx.cpu().numpy(), want)
+
+
 def test_retrieve_topk_token_branch_vs_reference():
     from kvr_b200 import RetrievalIndex
     ns = int(G["n_stored"])
