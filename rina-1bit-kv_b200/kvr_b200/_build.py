@@ -34,12 +34,12 @@ def _headers():
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
-def _compile(src, verbose=False):
-    obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
+def _compile(src, verbose=False, objdir=None, extra=()):
+    obj = os.path.join(objdir or OBJDIR, os.path.basename(src) + ".o")
     newest = max([os.path.getmtime(src)] + [os.path.getmtime(h) for h in _headers()])
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest:
         return obj
-    cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
+    cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -50,19 +50,27 @@ def _compile(src, verbose=False):
     return obj
 
 
-def build(verbose: bool = False) -> str:
-    os.makedirs(OBJDIR, exist_ok=True)
+# variant -> (library file, extra nvcc flags).  "trace" compiles the
+# %globaltimer phase stamps (KVR_TRACE_POINT) into every kernel, for latency
+# studies only (phase_trace.py); the product library never has them.
+VARIANTS = {"": (LIB, ()), "trace": (os.path.join(LIBDIR, "libkvr_b200_trace.so"), ("-DKVR_TRACE",))}
+
+
+def build(verbose: bool = False, variant: str = "") -> str:
+    lib_path, extra = VARIANTS[variant]
+    objdir = OBJDIR if not variant else os.path.join(OBJDIR, variant)
+    os.makedirs(objdir, exist_ok=True)
     os.makedirs(LIBDIR, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        objs = list(ex.map(lambda s: _compile(s, verbose, objdir, extra), srcs))
+    if not os.path.exists(lib_path) or os.path.getmtime(lib_path) < max(os.path.getmtime(o) for o in objs):
+        cmd = [NVCC, *ARCH, "-shared", "-o", lib_path, *objs, "-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+    return lib_path
 
 
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    print(build(verbose="-v" in sys.argv, variant="trace" if "--trace" in sys.argv else ""))

@@ -1,0 +1,165 @@
+"""Phase breakdown of one batch-1 sd1 decode layer (BASELINE configs[1]
+shapes: 8 KV / 32 query heads, 32256 stored tokens in tiles of 64, window
+512, top 16 tiles, DCT), from %globaltimer stamps compiled into a separate
+trace build of the library (KVR_TRACE_POINT; python -m kvr_b200._build
+--trace).  The product library carries no stamps.
+
+    python rina-1bit-kv_b200/phase_trace.py [--layers 32] [--reps 30]
+
+A 32-layer step is captured in a CUDA graph as in bench.py and replayed;
+after each replay the stamps of the last layer's two kernels are read back
+(every launch overwrites the same slots) and expressed in microseconds from
+the first stamp of that layer's selection kernel.  Prints a markdown table of
+the medians over the replays.  Stamps are taken by thread 0 of each CTA;
+"first"/"last" are the minimum / maximum over the CTAs of a group.
+"""
+import argparse
+import ctypes
+import os
+import statistics
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+TRACE_LIB = os.path.join(HERE, "kvr_b200", "lib", "libkvr_b200_trace.so")
+os.environ["KVR_B200_LIB"] = TRACE_LIB
+sys.path.insert(0, HERE)
+
+import torch  # noqa: E402
+
+from kvr_b200 import _native as N  # noqa: E402
+from kvr_b200 import kernels as K  # noqa: E402
+
+D, HQ, HKV, CTX, WIN, TILE, KSEL = 128, 32, 8, 32768, 512, 64, 16
+NT = (CTX - WIN) // TILE
+SLOTS = 2048  # trace slots per kernel id
+
+
+def read(fn):
+    buf = (ctypes.c_ulonglong * (4 * SLOTS * 8))()
+    rc = fn(buf, 4 * SLOTS * 8)
+    if rc != 0:
+        raise RuntimeError("trace readback failed")
+    return buf
+
+
+def stamps(buf, kernel, blocks, point):
+    out = []
+    for b in blocks:
+        v = buf[(kernel * SLOTS + b) * 8 + point]
+        if v:
+            out.append(v)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--reps", type=int, default=30)
+    args = ap.parse_args()
+    if not os.path.exists(TRACE_LIB):
+        raise SystemExit(f"{TRACE_LIB} missing: python -m kvr_b200._build --trace (from rina-1bit-kv_b200/)")
+    lib = N.lib()
+    rd_sel = lib.kvr_debug_trace_sd1
+    rd_att = lib.kvr_debug_trace_attn
+    for f in (rd_sel, rd_att):
+        f.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        f.restype = ctypes.c_int
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    stores, wins = [], []
+    for _ in range(args.layers):
+        scale = torch.exp(torch.randn(HKV, D, device=dev, generator=g))
+        k = (torch.randn(1, NT * TILE, HKV, D, device=dev, generator=g) * scale).to(torch.bfloat16)
+        v = torch.randn(1, NT * TILE, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+        st = K.Sd1Store(1, HKV, NT, TILE, "dct", dev)
+        K.sd1_encode(st, k, v)
+        stores.append(st)
+        wins.append((torch.randn(1, WIN, HKV, D, device=dev, generator=g).half(),
+                     torch.randn(1, WIN, HKV, D, device=dev, generator=g).half()))
+        del k, v
+    qs = torch.randn(args.layers, 1, HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    outs = torch.empty_like(qs)
+    ws = torch.zeros(N.call("kvr_sd1_workspace_bytes", 1, HQ, HKV, NT, TILE, KSEL, WIN, 0) + 256, dtype=torch.uint8,
+                     device=dev)
+
+    def step():
+        for li in range(args.layers):
+            K.sd1_decode_step(stores[li], qs[li], KSEL, wins[li][0], wins[li][1], WIN, out=outs[li], ws=ws)
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        step()
+        step()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            gr.replay()
+        e0.record(stream)
+        for _ in range(20):
+            gr.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    layer_us = e0.elapsed_time(e1) / 20 / args.layers * 1e3
+
+    n_units_win = WIN // 64
+    att_blocks_win = [s + (n_units_win + KSEL) * h for h in range(HKV) for s in range(n_units_win)]
+    att_blocks_tile = [s + (n_units_win + KSEL) * h for h in range(HKV) for s in range(n_units_win, n_units_win + KSEL)]
+    rows = {}
+
+    def add(name, v):
+        rows.setdefault(name, []).append(v)
+
+    for _ in range(args.reps):
+        with torch.cuda.stream(stream):
+            gr.replay()
+        torch.cuda.synchronize()
+        bs, ba = read(rd_sel), read(rd_att)
+        sel_blocks = [b for b in range(SLOTS) if bs[(0 * SLOTS + b) * 8 + 0]]
+        t0 = min(stamps(bs, 0, sel_blocks, 0))
+        us = lambda x: (x - t0) / 1e3  # noqa: E731
+        add("select: first CTA starts", us(min(stamps(bs, 0, sel_blocks, 0))))
+        add("select: last CTA starts", us(max(stamps(bs, 0, sel_blocks, 0))))
+        add("select: q' formed (last CTA)", us(max(stamps(bs, 0, sel_blocks, 1))))
+        sc_end = stamps(bs, 0, sel_blocks, 2)
+        if sc_end:
+            add("select: tile scan done (last CTA)", us(max(sc_end)))
+        att_start = stamps(ba, 1, att_blocks_win + att_blocks_tile, 0)
+        add("attend: first CTA starts", us(min(att_start)))
+        add("attend: last CTA starts", us(max(att_start)))
+        add("attend: window units staged (last)", us(max(stamps(ba, 1, att_blocks_win, 1))))
+        add("attend: window units done (last)", us(max(stamps(ba, 1, att_blocks_win, 3))))
+        add("attend: tile units pass the grid wait (first)", us(min(stamps(ba, 3, att_blocks_tile, 6))))
+        add("attend: tile units pass the grid wait (last)", us(max(stamps(ba, 3, att_blocks_tile, 6))))
+        add("attend: tile rank select starts (last)", us(max(stamps(ba, 3, att_blocks_tile, 4))))
+        add("attend: tile rank select done (last)", us(max(stamps(ba, 3, att_blocks_tile, 5))))
+        add("attend: tile units staged (last)", us(max(stamps(ba, 1, att_blocks_tile, 1))))
+        add("attend: tile units done (last)", us(max(stamps(ba, 1, att_blocks_tile, 3))))
+        # merge stamps: only the CTA that arrives last for its head writes them;
+        # other slots hold older layers' stamps, so take the latest per head
+        allb = att_blocks_win + att_blocks_tile
+        per = n_units_win + KSEL
+        for pt, name in ((4, "merge starts"), (0, "merge: partial (m, l) loaded / weights formed"),
+                         (1, "merge: partial halves staged"), (6, "merge: slots combined"),
+                         (5, "merge done")):
+            kern = 3 if pt in (0, 1) else 1
+            heads = []
+            for h in range(HKV):
+                v = stamps(ba, kern, [b for b in allb if b // per == h], pt)
+                if v:
+                    heads.append(max(v))
+            if heads:
+                add(f"attend: {name} (first head)", us(min(heads)))
+                add(f"attend: {name} (last head)", us(max(heads)))
+    print(f"graph-replayed step: {layer_us:.2f} us per layer ({args.layers} layers)\n")
+    print("| phase (last layer of the step) | us from the layer's first selection stamp (median) |")
+    print("|---|---|")
+    for name, vals in rows.items():
+        print(f"| {name} | {statistics.median(vals):.2f} |")
+
+
+if __name__ == "__main__":
+    main()
