@@ -17,6 +17,8 @@ Secondary objects of the same JSON line:
   c4_seq_split      configs[4]: 70B attention shapes, 131072 context split by
                     tile range over the N ranks, NCCL candidate all-gather +
                     partial (m, l, o) all-gather, per-phase timing;
+  model_c1          configs[1] through KVRGenerator on a random-init
+                    Llama-3-8B-shaped model: prefill seconds, decode tokens/s;
   int4w_c1          the reference's own codec (int4 K + W-predicted V + int2
                     residual) at the configs[1] shapes the reference arm times,
                     through RetrievalIndex.retrieve_topk + decode attention;
@@ -661,6 +663,72 @@ def run_int4w(args, dist_, peak_hbm):
     return res
 
 
+# ------------------------------------------------ model line --
+
+def run_model(args, dist_, peak_hbm):
+    """configs[1] end to end: a random-init Llama-3-8B-shaped bf16 decoder
+    (32 layers, hidden 4096, 32 q / 8 KV heads, head_dim 128, MLP 14336,
+    vocab 128256) driven by KVRGenerator with the 1-bit codec: a 32768-token
+    prefill (the projection hooks write the window and encode the evicted
+    prefix) then 256 greedy decode steps through KVRGenerator.logits_step
+    (per layer: q/k/v projections, the fused RoPE + store update kernel,
+    RetrievalIndex.attend, o_proj and MLP in torch).  Synthetic uniform token
+    ids; random weights (no checkpoint here)."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from kvr_b200 import KVRGenerator
+
+    dev = dist_.dev
+    n_prompt, n_steps = CTX, args.model_steps
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=LAYERS,
+                      num_attention_heads=HQ, num_key_value_heads=HKV, head_dim=D,
+                      max_position_embeddings=n_prompt + n_steps + 64, rope_theta=500000.0,
+                      attn_implementation="sdpa")
+    torch.manual_seed(0)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(old)
+    gen = KVRGenerator(model, window_size=WIN, top_k=KSEL * TILE, device=dev, codec="sd1", tile=TILE,
+                       transform=KIND)
+    g = torch.Generator(device=dev).manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (1, n_prompt), device=dev, generator=g)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    gen.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_s = e0.elapsed_time(e1) / 1e3
+    tok = ids[0, -1]
+    warm = 4
+    for i in range(n_steps + warm):
+        if i == warm:
+            torch.cuda.synchronize()
+            e0.record()
+        logits = gen.logits_step(tok)
+        gen.kvr._context_len += 1
+        gen._is_first = False
+        tok = logits.argmax()
+    e1.record()
+    torch.cuda.synchronize()
+    dec_s = e0.elapsed_time(e1) / 1e3
+    res = {"workload": "configs[1]: random-init Llama-3-8B-shaped bf16 decoder, KVRGenerator, codec sd1 (dct, "
+                       "tile 64), window 512, top 16 tiles; 32768-token prefill then greedy decode",
+           "prefill_s": round(prefill_s, 3), "prefill_tokens_per_s": round(n_prompt / prefill_s, 1),
+           "decode_steps": n_steps, "decode_tokens_per_s": round(n_steps / dec_s, 2),
+           "decode_ms_per_token": round(dec_s * 1e3 / n_steps, 3),
+           "stored_tokens_layer0": gen.kvr.retrievals[0].n_tokens,
+           "launch": "eager (python per layer), fused RoPE + store update kernel per layer"}
+    del gen, model
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---------------------------------------------------------- encode sweep --
 
 def run_encode_sweep(args, dist_, peak_hbm):
@@ -775,9 +843,10 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default="", help="comma list of sections to run: headline,c2,c4,int4w,sweep")
+    ap.add_argument("--only", default="", help="comma list of sections: headline,c2,c4,int4w,sweep,model")
     ap.add_argument("--encode-sweep", default="short", choices=["short", "full", "off"])
     ap.add_argument("--c4-steps", type=int, default=10)
+    ap.add_argument("--model-steps", type=int, default=256)
     ap.add_argument("--cpu-sample", type=int, default=8, help="layers timed for the CPU baseline")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -824,7 +893,7 @@ def main():
     torch.cuda.set_device(local_rank)
     dist_ = Dist(world, rank, torch.device("cuda", local_rank))
     peak_hbm, _, _ = measured_peaks()
-    only = set(x for x in args.only.split(",") if x) or {"headline", "c2", "c4", "int4w", "sweep"}
+    only = set(x for x in args.only.split(",") if x) or {"headline", "c2", "c4", "int4w", "sweep", "model"}
 
     def section(name, fn):
         if name not in only:
@@ -841,6 +910,7 @@ def main():
     res["c4_seq_split"] = section("c4", run_c4)
     if world == 1:
         res["int4w_c1"] = section("int4w", run_int4w)
+        res["model_c1"] = section("model", run_model)
         if args.encode_sweep != "off":
             res["encode_sweep"] = section("sweep", run_encode_sweep)
     if rank == 0:

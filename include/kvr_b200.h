@@ -22,6 +22,7 @@
  *                                                         kvr_int4w_vres_add
  *   modules/kvr_retrieval.py:248-263, 332-367 (attractor branch) -> kvr_int4w_attractor_select
  *   modules/kvr_window.py:19-41      (ring append)     -> kvr_window_write
+ *   modules/kvr_generator.py:78-98   (RoPE + store update of a decode step) -> kvr_decode_store_update
  *   modules/kvr_window.py:43-69, kvr_hook.py:274-282,
  *   modules/kvr_triton.py:42-104     (attention)       -> kvr_decode_attn
  *   (no reference counterpart: the 1-bit sd1 codec)    -> kvr_sd1_*, kvr_transform, kvr_lse_merge
@@ -207,6 +208,20 @@ KVR_API int kvr_decode_attn_counted(const void *q, int q_dtype, int n_q, int n_k
                                     const void *k1, const void *v1, int kdt1, int vdt1, int64_t n1,
                                     int64_t tok_stride1, const int32_t *n1_count, float scale, void *out,
                                     int out_dtype, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
+/* One decode step's store update for a layer, fused (kvr_generator.py:78-98,
+ * kvr_hook.py:136-148, kvr_window.py:19-25): q_out = RoPE(q) and, when
+ * write_kv, window slot `slot` <- (fp16(RoPE(k)), fp16(v)), all at position
+ * `pos` with the rotate_half convention and every elementwise op rounded to
+ * `dtype` as the eager reference does.  If tail_k/tail_v are given, the slot's
+ * old K/V rows (post-RoPE fp16, the evicted token) are first copied to row
+ * tail_row of the 1-bit store's pending tail.  q, k, v: (n_q|n_kv, d) of
+ * dtype; tables (max_pos, d) fp32 with row stride rope_stride; d = 128. */
+KVR_API int kvr_decode_store_update(const void *q, const void *k, const void *v, int dtype, int n_q, int n_kv,
+                                    int d, const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                    int64_t pos, void *q_out, uint16_t *win_k, uint16_t *win_v, int64_t win_cap,
+                                    int64_t slot, uint16_t *tail_k, uint16_t *tail_v, int64_t tail_row,
+                                    int write_kv, kvr_stream_t stream);
 
 /* ------------------------------------------------------------------ sd1 ----
  * 1-bit codec (no reference counterpart).  head_dim d = 128, tile t in

@@ -53,6 +53,7 @@ SIGNATURES = {
                                     P]),
     "kvr_int4w_vres_add": (I, [P, P, P, P, I, I, I, P, P]),
     "kvr_window_write": (I, [P, P, I, I64, I, I, P, P, I64, I64, P]),
+    "kvr_decode_store_update": (I, [P, P, P, I, I, I, I, P, P, I64, I64, P, P, P, I64, I64, P, P, I64, I, P]),
     "kvr_decode_attn_workspace_bytes": (SZ, [I, I, I, I64]),
     "kvr_decode_attn": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, F, P, I, P, SZ, P]),
     "kvr_transform": (I, [P, P, I64, I, I, P]),

@@ -194,6 +194,23 @@ def window_write(k, v, ring_k, ring_v, pos: int):
          pos, stream())
 
 
+def decode_store_update(q, k, v, cos, sin, pos, ring_k, ring_v, slot, tail_k=None, tail_v=None, tail_row=0,
+                        write_kv=True, q_out=None):
+    """One decode step's RoPE + window write (+ eviction of the slot's old row
+    into the sd1 tail) in one launch.  q (n_q, d), k/v (n_kv, d) of the model
+    dtype -> q_out = RoPE(q) (same dtype)."""
+    q, k, v = _c(q), _c(k), _c(v)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k and v must share a dtype")
+    cos, sin, rs = _rope_args(cos, sin)
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    call("kvr_decode_store_update", ptr(q), ptr(k), ptr(v), dtype_code(q), q.shape[0], k.shape[0], D, ptr(cos),
+         ptr(sin), rs, pos, ptr(q_out), ptr(ring_k), ptr(ring_v), ring_k.shape[0], slot, ptr(tail_k), ptr(tail_v),
+         tail_row, int(write_kv), stream())
+    return q_out
+
+
 # -------------------------------------------------------------- attention --
 
 

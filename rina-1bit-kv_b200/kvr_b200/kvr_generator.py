@@ -5,9 +5,10 @@ step, generate).
 Per step and layer (modules/kvr_generator.py:78-126): input norm, q/k/v
 projections, RoPE at the step position, store update (eviction into the
 index), then attention over the window and the retrieved tokens — here one
-call into the B200 kernels (``kvr_decode_attn``, or the fused sd1 step when
-``codec='sd1'``) instead of ``torch.cat`` + the Triton kernel — then o_proj,
-residual and MLP.  Sampling uses the HF logits processors, as the reference
+call into the B200 kernels (RetrievalIndex.attend) instead of ``torch.cat``
++ the Triton kernel — then o_proj, residual and MLP.  With ``codec='sd1'`` the
+RoPE, the eviction and the window write are one kernel
+(kvr_decode_store_update).  Sampling uses the HF logits processors, as the reference
 does (modules/kvr_generator.py:129-154).
 """
 import torch
@@ -34,6 +35,9 @@ class KVRGenerator:
         self._step_count = 0
         self._generated_ids = []
         self._is_first = True
+        # codec='sd1': one fused kernel per layer for RoPE + store update
+        # (fused_store_update=False keeps the step-by-step torch path)
+        self.fused_store_update = kwargs.pop("fused_store_update", True)
         self.kvr = KVRHook(model, window_size=window_size, top_k=top_k, device=device, **kwargs)
         self.window_size = window_size
         self.top_k = top_k
@@ -81,10 +85,15 @@ class KVRGenerator:
             q = attn.q_proj(hn).view(self.n_q, self.d_head)
             k_pre = attn.k_proj(hn).view(self.n_kv, self.d_head)
             v = attn.v_proj(hn).view(self.n_kv, self.d_head)
-            q_rot = _apply_rotary(q, c, s)
-            k_rot = _apply_rotary(k_pre, c, s)
-            if not self._is_first:
-                self.kvr._update_stores(li, k_pre.to(torch.float16), v.to(torch.float16), k_rot.to(torch.float16))
+            if self.fused_store_update and self.kvr.fused_store_update_ok(li):
+                # RoPE + eviction + window write in one kernel (kvr_decode_store_update)
+                q_rot = self.kvr.decode_store_update(li, q, k_pre, v, pos, write_kv=not self._is_first)
+            else:
+                q_rot = _apply_rotary(q, c, s)
+                k_rot = _apply_rotary(k_pre, c, s)
+                if not self._is_first:
+                    self.kvr._update_stores(li, k_pre.to(torch.float16), v.to(torch.float16),
+                                            k_rot.to(torch.float16))
             out = self.kvr.attend(li, q_rot, out_dtype=q_rot.dtype)
             h = h + attn.o_proj(out.reshape(-1).to(h.dtype))
             h = h + layer.mlp(layer.post_attention_layernorm(h))

@@ -262,6 +262,46 @@ class KVRHook:
             self._build_all_retrievals()
         win.append(k_post, v_val)
 
+    def fused_store_update_ok(self, li):
+        """True when decode_store_update can stand for RoPE + _update_stores:
+        the 1-bit codec with eviction at the evicted token's own position, and
+        no lazy index build due at this step."""
+        if self.codec != "sd1" or self.reference_eviction_rope:
+            return False
+        win = self.windows[li]
+        if not self._retrieval_built:
+            return not (self._context_len >= self.window_size - 1 and li == 0) and win.n < win.cap
+        return self.retrievals[li].store is not None
+
+    def decode_store_update(self, li, q, k_pre, v, pos, write_kv=True):
+        """One launch (kvr_decode_store_update) for what a decode step does
+        between the projections and the attention (kvr_generator.py:91-98):
+        RoPE of q and k at `pos`, eviction of the window slot about to be
+        overwritten into the 1-bit index (its post-RoPE row goes to the pending
+        tail as it is; a full tail is encoded into a tile), and the window
+        write.  Returns the rotated q (model dtype)."""
+        win, ret = self.windows[li], self.retrievals[li]
+        evict = write_kv and self._retrieval_built and win.n >= win.cap
+        slot = win.pos % win.cap
+        tk = tv = None
+        if evict:
+            tk, tv = ret.tail_k[0], ret.tail_v[0]
+        q_rot = K.decode_store_update(q, k_pre, v, self.cos_tbl, self.sin_tbl, pos, win.k, win.v, slot, tk, tv,
+                                      ret.n_tail if evict else 0, write_kv)
+        if evict:
+            ret.n_tail += 1
+            if ret.n_tail == ret.tile:
+                st = ret.store
+                if st.n_tiles + 1 > st.nt_cap:
+                    st.grow(2 * st.nt_cap)
+                K.sd1_encode(st, ret.tail_k, ret.tail_v)
+                ret.n_stored += ret.tile
+                ret.n_tail = 0
+        if write_kv:
+            win.pos += 1
+            win.n = min(win.n + 1, win.cap)
+        return q_rot
+
     # ------------------------------------------------------- attention --
     def attend(self, li, q_post, out_dtype=torch.float32):
         """Window + retrieval attention of one layer for the current step:
