@@ -510,72 +510,80 @@ def run_c4(args, dist_, peak_hbm):
         torch.cuda.empty_cache()
         return res
 
-    comm = TorchDistComm()
-    decs = [SeqSplitDecoder(stores[li], base, comm, window=wins[li] if last else None, n_win=WIN4 if last else 0)
-            for li in range(L4)]
+    def measure(comm, phases):
+        decs = [SeqSplitDecoder(stores[li], base, comm, window=wins[li] if last else None,
+                                n_win=WIN4 if last else 0) for li in range(L4)]
 
-    def step(marks=None):
-        for li in range(L4):
-            o, _ = decs[li].step(q[li], K4, out_dtype=torch.bfloat16, marks=marks)
-            out[li].copy_(o)
+        def step(marks=None):
+            for li in range(L4):
+                o, _ = decs[li].step(q[li], K4, out_dtype=torch.bfloat16, marks=marks)
+                out[li].copy_(o)
 
-    # eager, per-phase CUDA events
-    phases = ["local_select", "candidate_allgather", "local_attend", "partial_allgather", "merge"]
-    acc = {p: 0.0 for p in phases}
-    n_meas = 3
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            step()
-    torch.cuda.synchronize()
-    dist_.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.c4_steps):
-            step()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    eager_ms = dist_.max(e0.elapsed_time(e1) / args.c4_steps)
-    for _ in range(n_meas):
-        evs = []
-
-        def mark(name):
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record(torch.cuda.current_stream())
-            evs.append((name, ev))
-
+        acc = {p: 0.0 for p in phases}
+        n_meas = 3
         with torch.cuda.stream(stream):
-            st0 = torch.cuda.Event(enable_timing=True)
-            st0.record(stream)
-            step(marks=mark)
+            for _ in range(2):
+                step()
         torch.cuda.synchronize()
-        prev = st0
-        for name, ev in evs:
-            acc[name] += prev.elapsed_time(ev) / n_meas
-            prev = ev
-    breakdown = {p: round(dist_.max(acc[p]), 4) for p in phases}
-    # graph-captured (NCCL collectives inside the graph)
-    graph_ms, graph_err = None, None
-    try:
         dist_.barrier()
-        gms = graph_time(torch, step, stream, args.c4_steps)
-        graph_ms = dist_.max(gms)
-    except Exception as e:  # noqa: BLE001 - reported in the line, eager number stands
-        graph_err = repr(e)[:200]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.c4_steps):
+                step()
+            e1.record(stream)
         torch.cuda.synchronize()
-    best = min(x for x in (eager_ms, graph_ms) if x is not None)
-    coll = breakdown["candidate_allgather"] + breakdown["partial_allgather"]
-    res.update({"mode": "sequence split, NCCL all-gathers", "ms_per_step": round(best, 4),
-                "value": round(1e3 / best, 2), "unit": "decode-steps/s (80 layers)",
-                "eager_ms_per_step": round(eager_ms, 4),
-                "graph_ms_per_step": None if graph_ms is None else round(graph_ms, 4),
-                "graph_error": graph_err,
-                "phase_ms_per_step_eager": breakdown,
-                "collective_share_eager": round(coll / max(sum(breakdown.values()), 1e-9), 4),
+        eager_ms = dist_.max(e0.elapsed_time(e1) / args.c4_steps)
+        for _ in range(n_meas):
+            evs = []
+
+            def mark(name):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(torch.cuda.current_stream())
+                evs.append((name, ev))
+
+            dist_.barrier()
+            with torch.cuda.stream(stream):
+                st0 = torch.cuda.Event(enable_timing=True)
+                st0.record(stream)
+                step(marks=mark)
+            torch.cuda.synchronize()
+            prev = st0
+            for name, ev in evs:
+                acc[name] += prev.elapsed_time(ev) / n_meas
+                prev = ev
+        breakdown = {p: round(dist_.max(acc[p]), 4) for p in phases}
+        graph_ms, graph_err = None, None
+        try:
+            dist_.barrier()
+            graph_ms = dist_.max(graph_time(torch, step, stream, args.c4_steps))
+        except Exception as e:  # noqa: BLE001 - reported in the line, the eager number stands
+            graph_err = repr(e)[:200]
+            torch.cuda.synchronize()
+        best = min(x for x in (eager_ms, graph_ms) if x is not None)
+        return {"ms_per_step": round(best, 4), "eager_ms_per_step": round(eager_ms, 4),
+                "graph_ms_per_step": None if graph_ms is None else round(graph_ms, 4), "graph_error": graph_err,
+                "phase_ms_per_step_eager": breakdown}
+
+    from kvr_b200.sharding import PeerComm
+    peer = PeerComm()
+    try:
+        r_peer = measure(peer, ["local_select", "candidate_exchange", "local_attend", "partial_exchange"])
+        peer.status()
+    finally:
+        dist_.barrier()
+        peer.close()
+    r_nccl = measure(TorchDistComm(), ["local_select", "candidate_allgather", "local_attend", "partial_allgather",
+                                       "merge"])
+    best = min(r_peer["ms_per_step"], r_nccl["ms_per_step"])
+    res.update({"mode": "sequence split; exchanges as NVLink peer-memory kernels (kvr_peer_*) and, for "
+                        "comparison, NCCL all-gathers",
+                "ms_per_step": round(best, 4), "value": round(1e3 / best, 2), "unit": "decode-steps/s (80 layers)",
+                "peer_exchange": r_peer, "nccl_allgather": r_nccl,
                 "bytes_crossing_nvlink_per_layer": {"candidates": world * HKV4 * K4 * 8,
                                                     "partials": world * HQ4 * (D + 2) * 4},
                 "job_hbm_gbs": round(L4 * (sel_b + att_b) / (best / 1e3) / 1e9, 1)})
-    del decs, stores, wins
+    del stores, wins
     torch.cuda.empty_cache()
     return res
 

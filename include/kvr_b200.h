@@ -339,6 +339,34 @@ KVR_API int kvr_merge_candidates(const float *scores, const int32_t *idx, int n_
                                  int k_sel, int64_t tile_base, int64_t n_local, int32_t *global_sel,
                                  int32_t *local_sel, kvr_stream_t stream);
 
+/* ----------------------------------------------- sequence split over NVLink ----
+ * No reference counterpart (the reference has no multi-GPU code).  In place of
+ * the NCCL all-gathers of a sequence split, each rank keeps one exchange
+ * buffer in its own HBM and maps the other ranks' buffers (CUDA IPC): an
+ * exchange is one kernel per rank that writes its data into every rank's
+ * buffer with plain stores over NVLink, raises release flags, waits
+ * (bounded; a timeout sets the buffer's error word, see
+ * kvr_workspace_status) for every rank's flags and merges locally.  bufs[r]
+ * is rank r's buffer as mapped in this process (bufs[rank] = its own).  All
+ * ranks must issue the same sequence of exchanges.  At most 8 ranks. */
+KVR_API size_t kvr_peer_buffer_bytes(void);
+KVR_API size_t kvr_peer_handle_bytes(void);
+KVR_API int kvr_peer_alloc(void **buf);            /* cudaMalloc + zero fill (set-up, not per step) */
+KVR_API int kvr_peer_free(void *buf);
+KVR_API int kvr_peer_handle(void *buf, void *handle_out);
+KVR_API int kvr_peer_open(const void *handle, void **buf);
+KVR_API int kvr_peer_close(void *buf);
+/* Candidate exchange + global top-k (same semantics as kvr_merge_candidates):
+ * scores/idx (rows, k_local) of this rank; rows <= 64, k_local <= 64. */
+KVR_API int kvr_peer_merge_candidates(void *const *bufs, int n_ranks, int rank, const float *scores,
+                                      const int32_t *idx, int rows, int k_local, int k_sel, int64_t tile_base,
+                                      int64_t n_local, int32_t *global_sel, int32_t *local_sel,
+                                      kvr_stream_t stream);
+/* Partial-row exchange + log-sum-exp merge (same arithmetic as kvr_lse_merge):
+ * partials (n_rows, d + 2) of this rank -> out (n_rows, d); n_rows <= 512. */
+KVR_API int kvr_peer_lse_merge(void *const *bufs, int n_ranks, int rank, const float *partials, int n_rows, int d,
+                               void *out, int out_dtype, kvr_stream_t stream);
+
 /* Allocation-free variant of kvr_decode_attn (no counterpart in the
  * reference).  For callers that cannot allocate device memory — a plugin
  * inside a host that owns the GPU heap, or a path where cudaMalloc would

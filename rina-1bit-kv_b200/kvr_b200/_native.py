@@ -70,6 +70,15 @@ SIGNATURES = {
                                 F, P, I, P, P, SZ, P]),
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),
     "kvr_merge_candidates": (I, [P, P, I, I, I, I, I64, I64, P, P, P]),
+    "kvr_peer_buffer_bytes": (SZ, []),
+    "kvr_peer_handle_bytes": (SZ, []),
+    "kvr_peer_alloc": (I, [P]),
+    "kvr_peer_free": (I, [P]),
+    "kvr_peer_handle": (I, [P, P]),
+    "kvr_peer_open": (I, [P, P]),
+    "kvr_peer_close": (I, [P]),
+    "kvr_peer_merge_candidates": (I, [P, I, I, P, P, I, I, I, I64, I64, P, P, P]),
+    "kvr_peer_lse_merge": (I, [P, I, I, P, I, I, P, I, P]),
     "kvr_sd1_prefill_workspace_bytes": (SZ, [I64, I]),
     "kvr_sd1_prefill_scores": (I, [P, I, I64, I, I, P, P, I64, I64, I, I, P, P, SZ, P]),
     "kvr_kmeans_workspace_bytes": (SZ, [I64, I]),

@@ -17,10 +17,12 @@ the window and the pending tail.  One decode step is
   4. all-gather of the partial rows and a local merge (kvr_lse_merge).
 The global top k of step 2 is one kernel (kvr_merge_candidates) that also
 writes the rank's own slice of the selection as local tile indices.
-Both exchanges use a communicator with ``all_gather(tensor) -> list``;
-``TorchDistComm`` wraps torch.distributed (NCCL over NVLink on the GPU box,
-gloo in the CPU tests); remote data lands in local memory before any kernel
-reads it.
+The exchanges use either a communicator with ``all_gather(tensor) -> list``
+(``TorchDistComm``: torch.distributed, NCCL on the GPU box, gloo in the CPU
+tests) or ``PeerComm``: one kernel per exchange that stores this rank's rows
+into every rank's buffer over NVLink and merges locally (kvr_peer_*).  Either
+way remote data lands in local memory before any kernel reads it; no kernel
+loads from a peer's memory.
 """
 from __future__ import annotations
 
@@ -96,6 +98,85 @@ class TorchDistComm:
         return torch.stack(self.all_gather(t))
 
 
+class PeerComm:
+    """The sequence-split exchanges over NVLink peer memory (kvr_peer_*): each
+    rank allocates one exchange buffer, the CUDA IPC handles travel once over
+    torch.distributed, and every later exchange is a single kernel per rank
+    that stores its rows into all ranks' buffers and merges locally — no NCCL
+    on the data path.  Build it collectively on every rank (after
+    torch.cuda.set_device), or with ``PeerComm.local()`` for one rank."""
+
+    def __init__(self, group=None, _local=False):
+        import ctypes
+
+        from . import _native as N
+
+        self.N = N
+        buf = ctypes.c_void_p()
+        N.call("kvr_peer_alloc", ctypes.byref(buf))
+        self.own = buf.value
+        self.opened = []
+        if _local:
+            self.world, self.rank, ptrs = 1, 0, [self.own]
+        else:
+            import torch.distributed as dist
+
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+            hb = N.call("kvr_peer_handle_bytes")
+            h = (ctypes.c_char * hb)()
+            N.call("kvr_peer_handle", self.own, h)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            ptrs = []
+            for r, hr in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.own)
+                    continue
+                p = ctypes.c_void_p()
+                N.call("kvr_peer_open", (ctypes.c_char * hb).from_buffer_copy(hr), ctypes.byref(p))
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+            dist.barrier(group=group)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+
+    @classmethod
+    def local(cls):
+        return cls(_local=True)
+
+    def merge_candidates(self, sc, sel, k_sel, tile_base, n_local):
+        """Local candidates (B, H, k_local) -> (global sel, local sel), both
+        (B, H, k_sel) int32, identical on every rank."""
+        B, H, kl = sel.shape
+        sc, sel = sc.float().contiguous(), sel.to(torch.int32).contiguous()
+        lsel = torch.empty(B, H, k_sel, dtype=torch.int32, device=sel.device)
+        gsel = torch.empty_like(lsel)
+        self.N.call("kvr_peer_merge_candidates", self.ptrs, self.world, self.rank, self.N.ptr(sc), self.N.ptr(sel),
+                    B * H, kl, k_sel, tile_base, n_local, self.N.ptr(gsel), self.N.ptr(lsel), self.N.stream())
+        return gsel, lsel
+
+    def merge_partials(self, part, out_dtype):
+        """This rank's partial rows (rows, d+2) -> the merged output (rows, d)."""
+        part = part.float().contiguous()
+        rows = part.shape[0]
+        out = torch.empty(rows, part.shape[1] - 2, dtype=out_dtype, device=part.device)
+        self.N.call("kvr_peer_lse_merge", self.ptrs, self.world, self.rank, self.N.ptr(part), rows,
+                    part.shape[1] - 2, self.N.ptr(out), self.N.dtype_code(out), self.N.stream())
+        return out
+
+    def status(self):
+        """Raises KvrError(KVR_ETIMEOUT) if an exchange wait gave up."""
+        import ctypes
+        self.N.call("kvr_workspace_status", ctypes.c_void_p(self.own), self.N.stream())
+
+    def close(self):
+        for p in self.opened:
+            self.N.call("kvr_peer_close", p)
+        self.opened = []
+        if self.own:
+            self.N.call("kvr_peer_free", self.own)
+            self.own = None
+
+
 class SeqSplitDecoder:
     """Per-rank state of a sequence-split layer: the local sd1 store (global
     tile indices [tile_base, tile_base + store.n_tiles)) and, on the last
@@ -144,6 +225,15 @@ class SeqSplitDecoder:
         mark = marks or (lambda name: None)
         sel, sc, qp = self.local_candidates(q, k_sel)
         mark("local_select")
+        if hasattr(self.comm, "merge_candidates"):
+            # NVLink peer-memory exchanges: one kernel each, no NCCL
+            gsel, local = self.comm.merge_candidates(sc, sel, k_sel, self.tile_base, self.n_local_tiles())
+            mark("candidate_exchange")
+            part = self.local_partial(q, qp, local)
+            mark("local_attend")
+            out = self.comm.merge_partials(part.reshape(B * n_q, d + 2), out_dtype or q.dtype)
+            mark("partial_exchange")
+            return out.view(B, n_q, d), gsel
         gather = getattr(self.comm, "all_gather_stacked", None) or (lambda t: torch.stack(self.comm.all_gather(t)))
         all_sc = gather(sc)
         all_idx = gather(sel.to(torch.int32))

@@ -132,24 +132,66 @@ def test_merge_candidates_matches_global_selection():
         assert torch.equal(lsel.cpu(), want_l)
 
 
-def _nccl_worker(rank, world, port, q_path):
+def test_peer_exchange_single_rank_and_graph_replay():
+    """PeerComm on one rank (the exchange kernels store into and read from
+    this GPU's buffer): the split decoder equals the single-store step, over
+    repeated exchanges (epochs advance) and from a replayed CUDA graph."""
+    from kvr_b200.sharding import PeerComm, SeqSplitDecoder
+    k, v, q, win, full = _setup("cuda")
+    want_sel, want = _ref(full, q, win)
+    comm = PeerComm.local()
+    try:
+        dec = SeqSplitDecoder(full, 0, comm, window=(win, win), n_win=200)
+        for _ in range(3):
+            out, gsel = dec.step(q, K_SEL, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.equal(gsel, want_sel)
+            assert float((out - want).abs().max() / want.abs().max()) < 1e-5
+        res = {}
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            dec.step(q, K_SEL, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            res["out"], res["sel"] = dec.step(q, K_SEL, out_dtype=torch.float32)
+        for _ in range(3):
+            gr.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(res["sel"], want_sel)
+            assert float((res["out"] - want).abs().max() / want.abs().max()) < 1e-5
+        comm.status()
+    finally:
+        comm.close()
+
+
+def _nccl_worker(rank, world, port, q_path, use_peer=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    from kvr_b200.sharding import SeqSplitDecoder, TorchDistComm
+    from kvr_b200.sharding import PeerComm, SeqSplitDecoder, TorchDistComm
     dev = f"cuda:{rank}"
     k, v, q, win, full = _setup(dev)
     st, base = _rank_store(k, v, rank, world, dev)
-    dec = SeqSplitDecoder(st, base, TorchDistComm(), window=(win, win) if rank == world - 1 else None,
+    comm = PeerComm() if use_peer else TorchDistComm()
+    dec = SeqSplitDecoder(st, base, comm, window=(win, win) if rank == world - 1 else None,
                           n_win=200 if rank == world - 1 else 0)
-    out, gsel = dec.step(q, K_SEL, out_dtype=torch.float32)
+    want_sel, want = _ref(full, q, win)
+    ok = True
+    for _ in range(3 if use_peer else 1):
+        out, gsel = dec.step(q, K_SEL, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(gsel.to(torch.int32), want_sel)
+        ok = ok and float((out - want).abs().max() / want.abs().max()) < 1e-5
+    if use_peer:
+        comm.status()
     if rank == 0:
-        want_sel, want = _ref(full, q, win)
-        ok = torch.equal(gsel.to(torch.int32), want_sel) and float((out - want).abs().max() / want.abs().max()) < 1e-5
         torch.save({"ok": ok}, q_path)
     dist.barrier()
+    if use_peer:
+        comm.close()
     dist.destroy_process_group()
 
 
@@ -162,4 +204,17 @@ def test_seq_split_nccl_two_gpus(tmp_path):
     s.close()
     path = str(tmp_path / "r.pt")
     mp.spawn(_nccl_worker, args=(2, port, path), nprocs=2, join=True)
+    assert torch.load(path)["ok"]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_seq_split_peer_exchange_two_gpus(tmp_path):
+    """The NVLink peer-memory exchanges (PeerComm) across two GPUs, three steps."""
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    path = str(tmp_path / "r.pt")
+    mp.spawn(_nccl_worker, args=(2, port, path, True), nprocs=2, join=True)
     assert torch.load(path)["ok"]
