@@ -160,19 +160,25 @@ KVR_API int kvr_int4w_vpredict(const uint8_t *k_packed, const int64_t *top, cons
 /* Attractor branch of retrieve_topk (kvr_retrieval.py:248-263, 332-367)
  * with no host sync: head-0 group-mean query vs the centroids (n_attractors,
  * d), the top_a basins, the top 16 tokens of each basin by head-0 cosine of
- * the re-rotated dequantised K (basins given as a CSR list: basin b's tokens
- * are basin_tokens[basin_start[b] .. basin_start[b+1]), ascending), the
- * ascending union minus [ex_start, ex_end).  Writes top (top_a*16, n_kv)
- * int64 (the same token in every column; rows past the count repeat a valid
- * token) and count (device int32).  Ties: score desc, then index asc.
- * Full-row (max_pos, d) rope tables; d = 128. */
+ * the re-rotated dequantised K (a basin's tokens: the t < n_labelled with
+ * labels[t] == basin), the ascending union minus [ex_start, ex_end).  Writes
+ * top (top_a*16, n_kv) int64 (the same token in every column; rows past the
+ * count repeat a valid token) and count (device int32).  Ties: score desc,
+ * then index asc.  Full-row (max_pos, d) rope tables; d = 128. */
 KVR_API size_t kvr_int4w_attractor_workspace_bytes(int64_t n_labelled, int top_a);
 KVR_API int kvr_int4w_attractor_select(const float *q, int n_q, int n_kv, const uint8_t *k_packed,
                                        const float *k_scales, const float *cos_tbl, const float *sin_tbl,
                                        int64_t rope_stride, const float *centroids, int n_attractors,
-                                       const int32_t *basin_start, const int32_t *basin_tokens, int64_t n_labelled,
-                                       int top_a, int64_t ex_start, int64_t ex_end, int64_t *top, int32_t *count,
-                                       void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+                                       const int32_t *labels, int64_t n_labelled, int top_a, int64_t ex_start,
+                                       int64_t ex_end, int64_t *top, int32_t *count, void *workspace,
+                                       size_t workspace_bytes, kvr_stream_t stream);
+
+/* Basins of tokens appended after the clustering (no reference counterpart:
+ * the reference never labels appended tokens): labels[t] for t in [t0, t1)
+ * = nearest centroid (argmin ||c||^2 - 2 x.c, lowest index on ties) of the
+ * token's head-0 K dequantised from its int4 codes. */
+KVR_API int kvr_int4w_assign_basins(const uint8_t *k_packed, const float *k_scales, int n_kv, int64_t t0, int64_t t1,
+                                    const float *centroids, int k, int32_t *labels, kvr_stream_t stream);
 
 /* ret_v[i, h, :] = fp16(v_base[h, i, :] + unpack2(vr_packed[top[i,h], h]) * (2*vr[h]/4))
  * with v_base (n_kv, k, d) fp32 (= x @ W_h^T + V_mean_h) (kvr_retrieval.py:399-402). */

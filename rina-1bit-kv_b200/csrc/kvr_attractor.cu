@@ -10,8 +10,9 @@
 // launches with no host sync:
 //   1. attractor_basins_kernel (1 CTA): centroid cosines, top basins;
 //   2. attractor_tokens_kernel (one CTA per chosen basin): the basin's tokens
-//      come from a CSR list built once at clustering time (token ids sorted
-//      within each basin); each warp scores tokens, then a block top-16;
+//      are gathered in ascending order from the label array (every labelled
+//      token, including tokens appended after the clustering); each warp
+//      scores tokens, then a block top-16;
 //   3. attractor_merge_kernel (1 CTA): drop empty slots and excluded tokens,
 //      sort ascending (basins are disjoint, so there are no duplicates), write
 //      the (rows, n_kv) index list and the device-side row count.
@@ -109,37 +110,54 @@ __device__ __forceinline__ float token_cosine_h0(const uint8_t *__restrict__ kp,
 
 __global__ void __launch_bounds__(256) attractor_tokens_kernel(
     const float *__restrict__ q, int g, const uint8_t *__restrict__ kp, int n_kv, const float *__restrict__ ks,
-    const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride,
-    const int32_t *__restrict__ basin_start, const int32_t *__restrict__ basin_tok,
-    const int32_t *__restrict__ basins, float *__restrict__ scratch, int32_t *__restrict__ sel_tok) {
+    const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, const int32_t *__restrict__ labels,
+    int64_t n_lab, const int32_t *__restrict__ basins, int32_t *__restrict__ scratch_tok,
+    float *__restrict__ scratch_sc, int32_t *__restrict__ sel_tok) {
   __shared__ float qa[attr::kD];
   __shared__ float red[1];
   __shared__ __align__(16) unsigned char tsm_raw[sizeof(TopkSmem)];
   __shared__ unsigned long long cand[attr::kPerBasin];
+  __shared__ int wcount[8];
   TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(tsm_raw);
   const float qn = stage_qavg0(q, g, qa, red);
   const int b = basins[blockIdx.x];
-  const int s0 = basin_start[b], s1 = basin_start[b + 1];
-  const int n = s1 - s0;
-  int32_t *out = sel_tok + blockIdx.x * attr::kPerBasin;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t *toks = scratch_tok + (int64_t)blockIdx.x * n_lab;
+  float *scs = scratch_sc + (int64_t)blockIdx.x * n_lab;
+  // the basin's tokens, ascending: ordered compaction of labels == b
+  int64_t n = 0;
+  for (int64_t r0 = 0; r0 < n_lab; r0 += blockDim.x) {
+    const int64_t i = r0 + threadIdx.x;
+    const bool m = i < n_lab && __ldg(labels + i) == b;
+    const unsigned bal = __ballot_sync(0xffffffffu, m);
+    if (lane == 0) wcount[warp] = __popc(bal);
+    __syncthreads();
+    int64_t before = n, total = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      if (w < warp) before += wcount[w];
+      total += wcount[w];
+    }
+    if (m) toks[before + __popc(bal & ((1u << lane) - 1u))] = (int32_t)i;
+    n += total;
+    __syncthreads();
+  }
+  int32_t *out = sel_tok + blockIdx.x * attr::kPerBasin;
   if (n <= attr::kPerBasin) {  // the whole basin (kvr_retrieval.py:345-346)
-    for (int r = threadIdx.x; r < attr::kPerBasin; r += blockDim.x) out[r] = r < n ? basin_tok[s0 + r] : -1;
+    for (int r = threadIdx.x; r < attr::kPerBasin; r += blockDim.x) out[r] = r < n ? toks[r] : -1;
     return;
   }
   float step4[4];
 #pragma unroll
   for (int r = 0; r < 4; ++r) step4[r] = __fdiv_rn(__fmul_rn(2.0f, __ldg(ks + lane * 4 + r)), 16.0f);
   const int64_t row_bytes = (int64_t)n_kv * (attr::kD / 2);
-  for (int p = warp; p < n; p += 8) {
-    const int64_t t = basin_tok[s0 + p];
+  for (int64_t p = warp; p < n; p += 8) {
+    const int64_t t = toks[p];
     const float s = token_cosine_h0(kp, row_bytes, step4, qa, qn, cs, sn, rope_stride, t, lane);
-    if (lane == 0) scratch[s0 + p] = s;
+    if (lane == 0) scs[p] = s;
   }
   __syncthreads();
-  const float *sl = scratch + s0;
-  block_topk<256>([&](int64_t i) -> float { return __ldcg(sl + i); }, n, attr::kPerBasin, cand, tsm);
-  for (int r = threadIdx.x; r < attr::kPerBasin; r += blockDim.x) out[r] = basin_tok[s0 + key_index(cand[r])];
+  block_topk<256>([&](int64_t i) -> float { return __ldcg(scs + i); }, n, attr::kPerBasin, cand, tsm);
+  for (int r = threadIdx.x; r < attr::kPerBasin; r += blockDim.x) out[r] = toks[key_index(cand[r])];
 }
 
 __global__ void __launch_bounds__(1024) attractor_merge_kernel(const int32_t *__restrict__ sel_tok, int n_slots,
@@ -188,25 +206,26 @@ __global__ void __launch_bounds__(1024) attractor_merge_kernel(const int32_t *__
 using namespace kvr;
 
 extern "C" size_t kvr_int4w_attractor_workspace_bytes(int64_t n_labelled, int top_a) {
-  return align_up((size_t)attr::kMaxTopA * 4, 256) + align_up((size_t)(top_a > 0 ? top_a : 1) * attr::kPerBasin * 4, 256) +
-         align_up((size_t)(n_labelled > 0 ? n_labelled : 1) * 4, 256);
+  const size_t ta = (size_t)(top_a > 0 ? top_a : 1);
+  const size_t nl = (size_t)(n_labelled > 0 ? n_labelled : 1);
+  return align_up((size_t)attr::kMaxTopA * 4, 256) + align_up(ta * attr::kPerBasin * 4, 256) +
+         2 * align_up(ta * nl * 4, 256);
 }
 
 extern "C" int kvr_int4w_attractor_select(const float *q, int n_q, int n_kv, const uint8_t *k_packed,
                                           const float *k_scales, const float *cos_tbl, const float *sin_tbl,
                                           int64_t rope_stride, const float *centroids, int n_attractors,
-                                          const int32_t *basin_start, const int32_t *basin_tokens,
-                                          int64_t n_labelled, int top_a, int64_t ex_start, int64_t ex_end,
-                                          int64_t *top, int32_t *count, void *workspace, size_t workspace_bytes,
-                                          kvr_stream_t stream) {
+                                          const int32_t *labels, int64_t n_labelled, int top_a, int64_t ex_start,
+                                          int64_t ex_end, int64_t *top, int32_t *count, void *workspace,
+                                          size_t workspace_bytes, kvr_stream_t stream) {
   clear_error();
-  KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && centroids && basin_start && basin_tokens && top &&
-                  count && workspace,
+  KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && centroids && labels && top && count && workspace,
               "kvr_int4w_attractor_select: null pointer");
   KVR_REQUIRE(n_kv > 0 && n_q % n_kv == 0 && n_q >= n_kv, "kvr_int4w_attractor_select: bad head counts");
   KVR_REQUIRE(n_attractors > 0 && n_attractors <= attr::kMaxBasins, "kvr_int4w_attractor_select: 1..%d basins",
               attr::kMaxBasins);
   KVR_REQUIRE(top_a > 0 && top_a <= n_attractors && top_a <= attr::kMaxTopA, "kvr_int4w_attractor_select: bad top_a");
+  KVR_REQUIRE(n_labelled > 0 && n_labelled < 0x7fffffffll, "kvr_int4w_attractor_select: bad n_labelled");
   KVR_REQUIRE(rope_stride >= attr::kD, "kvr_int4w_attractor_select: rope tables need full rows");
   KVR_REQUIRE(workspace_bytes >= kvr_int4w_attractor_workspace_bytes(n_labelled, top_a),
               "kvr_int4w_attractor_select: workspace too small");
@@ -216,12 +235,14 @@ extern "C" int kvr_int4w_attractor_select(const float *q, int n_q, int n_kv, con
   p += align_up((size_t)attr::kMaxTopA * 4, 256);
   int32_t *sel_tok = reinterpret_cast<int32_t *>(p);
   p += align_up((size_t)top_a * attr::kPerBasin * 4, 256);
-  float *scratch = reinterpret_cast<float *>(p);
+  int32_t *scratch_tok = reinterpret_cast<int32_t *>(p);
+  p += align_up((size_t)top_a * n_labelled * 4, 256);
+  float *scratch_sc = reinterpret_cast<float *>(p);
   cudaStream_t st = as_cuda(stream);
   const int g = n_q / n_kv;
   attractor_basins_kernel<<<1, 256, 0, st>>>(q, g, centroids, n_attractors, top_a, basins);
   attractor_tokens_kernel<<<top_a, 256, 0, st>>>(q, g, k_packed, n_kv, k_scales, cos_tbl, sin_tbl, rope_stride,
-                                                 basin_start, basin_tokens, basins, scratch, sel_tok);
+                                                 labels, n_labelled, basins, scratch_tok, scratch_sc, sel_tok);
   attractor_merge_kernel<<<1, 1024, 0, st>>>(sel_tok, top_a * attr::kPerBasin, ex_start, ex_end, n_kv,
                                              top_a * attr::kPerBasin, top, count);
   return check_launch("kvr_int4w_attractor_select");

@@ -105,9 +105,81 @@ __global__ void km_update_kernel(const float *__restrict__ part, const int32_t *
   if (m > 0) c[(int64_t)j * kKmD + t] = s / (float)m;
 }
 
+// Basin of tokens appended after clustering: head-0 K of tokens [t0, t1)
+// dequantised from the packed int4 codes (code * 2*s/16, as the clustering
+// input was formed) and assigned with the same rule as km_assign_kernel.
+__global__ void __launch_bounds__(kKmBlock) km_assign_packed_kernel(const uint8_t *__restrict__ kp, int n_kv,
+                                                                    const float *__restrict__ ks, int64_t t0,
+                                                                    int64_t t1, int k, const float *__restrict__ c,
+                                                                    int32_t *__restrict__ lab) {
+  extern __shared__ __align__(16) float cs[];  // [k][128] then norms[k]
+  float *cn = cs + (int64_t)k * kKmD;
+  for (int i = threadIdx.x; i < k * kKmD / 4; i += blockDim.x)
+    reinterpret_cast<float4 *>(cs)[i] = __ldg(reinterpret_cast<const float4 *>(c) + i);
+  __syncthreads();
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    float s = 0.0f;
+    for (int e = 0; e < kKmD; ++e) s = fmaf(cs[j * kKmD + e], cs[j * kKmD + e], s);
+    cn[j] = s;
+  }
+  __syncthreads();
+  const int64_t p = t0 + (int64_t)blockIdx.x * kKmBlock + threadIdx.x;
+  if (p >= t1) return;
+  float xv[kKmD];
+  const uint8_t *row = kp + p * (int64_t)n_kv * (kKmD / 2);  // head 0
+#pragma unroll
+  for (int e = 0; e < kKmD / 2; ++e) {
+    const uint32_t byte = __ldg(row + e);
+    xv[2 * e] = __fmul_rn((float)((int)(byte >> 4) - 8), __fdiv_rn(__fmul_rn(2.0f, __ldg(ks + 2 * e)), 16.0f));
+    xv[2 * e + 1] = __fmul_rn((float)((int)(byte & 15u) - 8), __fdiv_rn(__fmul_rn(2.0f, __ldg(ks + 2 * e + 1)), 16.0f));
+  }
+  float best = INFINITY;
+  int arg = 0;
+  for (int j = 0; j < k; ++j) {
+    const float4 *cj = reinterpret_cast<const float4 *>(cs + j * kKmD);
+    float acc = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kKmD / 4; ++e) {
+      const float4 v = cj[e];
+      acc = fmaf(xv[4 * e], v.x, acc);
+      acc = fmaf(xv[4 * e + 1], v.y, acc);
+      acc = fmaf(xv[4 * e + 2], v.z, acc);
+      acc = fmaf(xv[4 * e + 3], v.w, acc);
+    }
+    const float dist = fmaf(-2.0f, acc, cn[j]);
+    if (dist < best) {
+      best = dist;
+      arg = j;
+    }
+  }
+  lab[p] = arg;
+}
+
 }  // namespace kvr
 
 using namespace kvr;
+
+extern "C" int kvr_int4w_assign_basins(const uint8_t *k_packed, const float *k_scales, int n_kv, int64_t t0,
+                                       int64_t t1, const float *centroids, int k, int32_t *labels,
+                                       kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(k_packed && k_scales && centroids && labels, "kvr_int4w_assign_basins: null pointer");
+  KVR_REQUIRE(n_kv > 0 && k >= 1 && k <= kKmMaxK && t0 >= 0 && t1 >= t0, "kvr_int4w_assign_basins: bad sizes");
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(centroids) & 15) == 0, "kvr_int4w_assign_basins: centroids alignment");
+  if (t1 == t0) return KVR_OK;
+  static thread_local int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaFuncSetAttribute(km_assign_packed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kKmMaxK * (kKmD + 1) * 4);
+    set_dev = dev;
+  }
+  const int64_t blocks = (t1 - t0 + kKmBlock - 1) / kKmBlock;
+  km_assign_packed_kernel<<<(unsigned)blocks, kKmBlock, (size_t)k * (kKmD + 1) * 4, as_cuda(stream)>>>(
+      k_packed, n_kv, k_scales, t0, t1, k, centroids, labels);
+  return check_launch("kvr_int4w_assign_basins");
+}
 
 static int64_t km_ctas(int64_t n) { return (n + kKmBlock - 1) / kKmBlock; }
 

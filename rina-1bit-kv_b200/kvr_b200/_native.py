@@ -48,7 +48,8 @@ SIGNATURES = {
     "kvr_int4w_vpredict_prepare": (I, [P, P, P, P, I, I, P, P, P, P]),
     "kvr_int4w_vpredict": (I, [P, P, P, I, I, I, P, P, P, P, P, P, P]),
     "kvr_int4w_attractor_workspace_bytes": (SZ, [I64, I]),
-    "kvr_int4w_attractor_select": (I, [P, I, I, P, P, P, P, I64, P, I, P, P, I64, I, I64, I64, P, P, P, SZ, P]),
+    "kvr_int4w_attractor_select": (I, [P, I, I, P, P, P, P, I64, P, I, P, I64, I, I64, I64, P, P, P, SZ, P]),
+    "kvr_int4w_assign_basins": (I, [P, P, I, I64, I64, P, I, P, P]),
     "kvr_decode_attn_counted": (I, [P, I, I, I, I, P, P, I, I, I64, I64, P, P, I, I, I64, I64, P, F, P, I, P, SZ,
                                     P]),
     "kvr_int4w_vres_add": (I, [P, P, P, P, I, I, I, P, P]),

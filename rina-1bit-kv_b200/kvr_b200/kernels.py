@@ -153,31 +153,28 @@ def int4w_vpredict(k_packed, top, prep, vr_packed, vr_scales, count=None, out=No
     return out
 
 
-def int4w_attractor_select(q, n_kv, k_packed, k_scales, cos, sin, centroids, basin_start, basin_tokens, top_a=48,
+def int4w_attractor_select(q, n_kv, k_packed, k_scales, cos, sin, centroids, labels, n_labelled, top_a=48,
                            ex_start=0, ex_end=0):
     """Attractor branch selection (kvr_retrieval.py:332-367) on the device:
-    -> (top (top_a*16, n_kv) int64, count (1,) int32 device tensor)."""
+    labels int32 (>= n_labelled) -> (top (top_a*16, n_kv) int64, count (1,)
+    int32 device tensor)."""
     q = _c(q.float())
     n_q = q.shape[0]
     cos, sin, rs = _rope_args(cos.float(), sin.float())
     rows = top_a * 16
     top = torch.empty(rows, n_kv, dtype=torch.int64, device=q.device)
     count = torch.empty(1, dtype=torch.int32, device=q.device)
-    nl = basin_tokens.numel()
-    ws = N.workspace("attractor", call("kvr_int4w_attractor_workspace_bytes", nl, top_a), q.device)
+    ws = N.workspace("attractor", call("kvr_int4w_attractor_workspace_bytes", n_labelled, top_a), q.device)
     call("kvr_int4w_attractor_select", ptr(q), n_q, n_kv, ptr(_c(k_packed)), ptr(_c(k_scales.float())), ptr(cos),
-         ptr(sin), rs, ptr(_c(centroids.float())), centroids.shape[0], ptr(_c(basin_start)), ptr(_c(basin_tokens)),
-         nl, top_a, ex_start, ex_end, ptr(top), ptr(count), ptr(ws), ws.numel(), stream())
+         ptr(sin), rs, ptr(_c(centroids.float())), centroids.shape[0], ptr(_c(labels)), n_labelled, top_a, ex_start,
+         ex_end, ptr(top), ptr(count), ptr(ws), ws.numel(), stream())
     return top, count
 
 
-def int4w_vres_add(v_base, vr_packed, vr_scales, top):
-    """v_base (n_kv, k, d) fp32 -> ret_v (k, n_kv, d) fp16 (kvr_retrieval.py:399-402)."""
-    n_kv, k, d = v_base.shape
-    out = torch.empty(k, n_kv, d, dtype=torch.float16, device=v_base.device)
-    call("kvr_int4w_vres_add", ptr(_c(v_base)), ptr(_c(vr_packed)), ptr(_c(vr_scales.float().reshape(-1))),
-         ptr(_c(top)), k, n_kv, d, ptr(out), stream())
-    return out
+def int4w_assign_basins(k_packed, k_scales, t0, t1, centroids, labels):
+    """labels[t0:t1] (int32, in place) = nearest basin of each token's head-0 K."""
+    call("kvr_int4w_assign_basins", ptr(_c(k_packed)), ptr(_c(k_scales.float())), k_packed.shape[1], t0, t1,
+         ptr(_c(centroids.float())), centroids.shape[0], ptr(labels), stream())
 
 
 # ----------------------------------------------------------------- window --
@@ -460,14 +457,14 @@ def sd1_prefill_scores(store: Sd1Store, q):
 
 def kmeans(x, k=128, iters=10):
     """Deterministic Lloyd k-means on the device: x (n, 128) -> (labels (n,)
-    int64, centroids (k, 128) fp32)."""
+    int32, centroids (k, 128) fp32)."""
     x = _c(x.float())
     n = x.shape[0]
     c = torch.empty(k, D, dtype=torch.float32, device=x.device)
     lab = torch.empty(n, dtype=torch.int32, device=x.device)
     ws = N.workspace("kmeans", call("kvr_kmeans_workspace_bytes", n, k), x.device)
     call("kvr_kmeans", ptr(x), n, D, k, iters, ptr(c), ptr(lab), ptr(ws), ws.numel(), stream())
-    return lab.long(), c
+    return lab, c
 
 
 def workspace_status(ws: torch.Tensor):

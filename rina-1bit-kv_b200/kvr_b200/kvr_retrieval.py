@@ -71,7 +71,7 @@ class RetrievalIndex:
         self.attractors = None
         self.labels = None
         self._vp = None          # (key, prepared V-predict weights)
-        self._csr = None         # (key, basin_start, basin_tokens)
+        self._lab = None         # [int32 label buffer, labels view, labelled count]
         # sd1 state
         self.tile = tile
         self.transform = transform
@@ -256,6 +256,7 @@ class RetrievalIndex:
         if nr < self.n_attractors * 2:
             return
         self.labels, self.attractors = K.kmeans(self._deq_k(0).float(), self.n_attractors, iters)
+        self._lab = None
 
     @torch.no_grad()
     def compute_attractor_scores(self, q_post_rope):
@@ -277,19 +278,30 @@ class RetrievalIndex:
         z = torch.zeros(0, self.n_kv, self.d_head, device=self.device, dtype=torch.float16)
         return z, z
 
-    def _basins_csr(self):
-        """Basin membership as a CSR list (tokens sorted within each basin),
-        rebuilt when the labels change."""
+    def _labels_device(self):
+        """(int32 label buffer, labelled count): the clustering's basin labels,
+        and every token appended after it assigned to its nearest basin on the
+        device (kvr_int4w_assign_basins), so the attractor branch can return
+        it.  ``self.labels`` stays a view of the labelled prefix; a caller that
+        replaces it (or sets it to None) is followed."""
         lab = self.labels
-        key = (lab.data_ptr(), lab._version, lab.numel(), self.attractors.shape[0])
-        if self._csr is None or self._csr[0] != key:
-            lab = lab.to(self.device).long()
-            order = torch.argsort(lab, stable=True).to(torch.int32)
-            counts = torch.bincount(lab, minlength=self.attractors.shape[0])
-            start = torch.zeros(self.attractors.shape[0] + 1, dtype=torch.int32, device=self.device)
-            start[1:] = torch.cumsum(counts, 0).to(torch.int32)
-            self._csr = (key, start, order.contiguous())
-        return self._csr[1], self._csr[2]
+        if self._lab is None or self._lab[1] is not lab:
+            n0 = lab.numel()
+            buf = torch.empty(max(n0, self.n_stored, 1), dtype=torch.int32, device=self.device)
+            buf[:n0] = lab.to(device=self.device, dtype=torch.int32)
+            self._lab = [buf, buf[:n0], n0]
+            self.labels = self._lab[1]
+        buf, view, n0 = self._lab
+        nr = self.n_stored
+        if nr > n0:
+            if nr > buf.numel():
+                grown = torch.empty(max(nr, 2 * buf.numel()), dtype=torch.int32, device=self.device)
+                grown[:n0] = buf[:n0]
+                buf = grown
+            K.int4w_assign_basins(self.k_packed, self.k_scales, n0, nr, self.attractors, buf)
+            self._lab = [buf, buf[:nr], nr]
+            self.labels = self._lab[1]
+        return self._lab[0], self._lab[2]
 
     def _vpredict_weights(self):
         """W' = W * diag(step) split for the tensor-core V-predict, prepared
@@ -313,11 +325,11 @@ class RetrievalIndex:
         top_k = min(self.top_k, nr)
         if self.attractors is not None and self.labels is not None:
             # kvr_retrieval.py:332-367: top 48 basins x top 16 tokens, same list for every head
-            start, toks = self._basins_csr()
+            lab, n_lab = self._labels_device()
             cos, sin, _ = self._tables(nr)
             top_a = min(48, self.attractors.shape[0])
             return K.int4w_attractor_select(q_post_rope, self.n_kv, self.k_packed, self.k_scales, cos, sin,
-                                            self.attractors, start, toks, top_a, exclude_start, exclude_end)
+                                            self.attractors, lab, n_lab, top_a, exclude_start, exclude_end)
         cs = self.chunk_size
         if cs > 0 and nr >= cs * 2:
             # intended chunk branch (kvr_retrieval.py:370-388; the reference body is unreachable)

@@ -224,3 +224,30 @@ def test_fused_attend_vs_reference_hook_fixture():
     # fp16 last bits (this fixture's W comes from a rank-deficient fit, see
     # test_retrieve_topk_vs_reference_fixture_with_vpredict_kernel)
     np.testing.assert_allclose(out, G["hook_attn"], rtol=2e-3, atol=2e-3)
+
+
+def test_appended_tokens_join_their_nearest_basin():
+    """Tokens appended after build_attractors get the basin of their nearest
+    centroid on the device (head-0 K from the int4 codes, argmin ||c||^2 -
+    2 x.c), and the attractor branch can then return them."""
+    st, cos, sin, q, ri, labels, cent, K = _attractor_case(seed=8, n=3000)
+    rng = np.random.default_rng(9)
+    n_new = 300
+    cos_big, sin_big = R.rope_tables(3000 + n_new, 128, 500000.0)
+    ri.set_rotary_tables(t(cos_big.astype(F32)), t(sin_big.astype(F32)))
+    k_new = (rng.standard_normal((n_new, 8, 128)) * np.exp(rng.standard_normal((8, 128)))).astype(F32)
+    v_new = rng.standard_normal((n_new, 8, 128)).astype(F32)
+    for i in range(n_new):
+        ri.append(t(k_new[i]), t(v_new[i]))
+    got = ri.select_indices(t(q))
+    lab = ri.labels.cpu().numpy()
+    assert lab.shape[0] == 3000 + n_new and np.array_equal(lab[:3000], labels)
+    x = R.deq_k(ri.k_packed.cpu().numpy(), ri.k_scales.cpu().numpy(), 3000 + n_new)[3000:, 0].astype(np.float64)
+    c = cent.astype(np.float64)
+    want_lab = ((c * c).sum(1)[None] - 2.0 * x @ c.T).argmin(1)
+    assert (lab[3000:] == want_lab).mean() > 0.99          # fp32 vs float64 distances may flip a near tie
+    st2 = dict(st)
+    st2["k_packed"] = ri.k_packed.cpu().numpy()
+    want, _, _ = R.attractor_select(q, st2, cos_big.astype(F32), sin_big.astype(F32), lab, cent, 48, 16)
+    g0 = got.cpu().numpy()[:, 0]
+    assert len(set(g0.tolist()) ^ set(want.tolist())) <= 2
