@@ -286,7 +286,7 @@ def run_headline(args, dist_, peak_hbm):
                 e0.record(stream)
             q_dev.copy_(q_host, non_blocking=True)
             for li in range(LAYERS):
-                outs[li, 0].copy_(rets[li].attend(q_dev[li, 0], wbufs[li]))
+                rets[li].attend(q_dev[li, 0], wbufs[li], out=outs[li, 0])
             o_host.copy_(outs, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()

@@ -79,6 +79,7 @@ class RetrievalIndex:
         self.tail_k = None
         self.tail_v = None
         self.n_tail = 0
+        self._sd1_call = None    # cached pointer arguments of attend()
 
     # ------------------------------------------------------------ tables --
     def set_rotary_tables(self, cos, sin):
@@ -568,7 +569,7 @@ class RetrievalIndex:
         return torch.cat(parts_k, 0).contiguous(), torch.cat(parts_v, 0).contiguous()
 
     @torch.no_grad()
-    def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None):
+    def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None, out=None):
         """One layer's retrieval + attention for the current step, q (n_q, d)
         -> (n_q, d): exact softmax over the window buffer (if given) and the
         retrieved rows — the hook's einsum over cat(window, retrieved)
@@ -576,7 +577,9 @@ class RetrievalIndex:
         no host synchronisation.  int4w: selection (token, chunk or attractor
         branch) -> gather -> tensor-core V-predict -> decode attention (the
         attractor branch's row count stays on the device).  sd1: one fused
-        decode step over the window, the pending tail and the selected tiles."""
+        decode step over the window, the pending tail and the selected tiles.
+        ``out`` (sd1, optional): an (n_q, d) tensor of q's dtype to write the
+        result into instead of a new tensor."""
         if self.codec == "int4w":
             nw = window.n if window is not None else 0
             out_dtype = out_dtype or torch.float32
@@ -595,14 +598,42 @@ class RetrievalIndex:
             return K.decode_attn(q_post_rope, [win, (rk, rv)], out_dtype=out_dtype, n_kv=self.n_kv, n1_count=count)
         if self.store is None:
             self._sd1_reset()
+        st = self.store
         t = self.tile
-        k_sel = max(1, self.top_k // t) if self.store.n_tiles else 0
-        ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, self.store.n_tiles)
+        k_sel = max(1, self.top_k // t) if st.n_tiles else 0
+        ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, st.n_tiles)
         if ex0 >= ex1:
             ex0 = ex1 = 0
-        wk = window.k.unsqueeze(0) if window is not None else None
-        wv = window.v.unsqueeze(0) if window is not None else None
+        q = q_post_rope if q_post_rope.is_contiguous() else q_post_rope.contiguous()
+        if not q.is_cuda:
+            raise ValueError("kvr_b200 operators need CUDA tensors (this build has no CPU path)")
+        n_q = q.shape[0]
         nw = window.n if window is not None else 0
-        out = K.sd1_decode_step(self.store, q_post_rope.unsqueeze(0), k_sel, wk, wv, nw,
-                                self.tail_k, self.tail_v, self.n_tail, ex0, ex1)
-        return out[0] if out_dtype is None else out[0].to(out_dtype)
+        # the pointer arguments of this store / window / tail are cached (they
+        # change only when a buffer is reallocated); one ctypes call per layer
+        key = (st.kbits.data_ptr(), st.nt_cap, id(window), window.k.data_ptr() if window is not None else 0,
+               self.tail_k.data_ptr())
+        c = self._sd1_call
+        if c is None or c[0] != key:
+            P = K.ptr
+            wk = (P(window.k), P(window.v), window.cap) if window is not None else (None, None, 1)
+            c = self._sd1_call = (key, wk, (P(self.tail_k), P(self.tail_v)),
+                                  (P(st.kbits), P(st.kscale), P(st.vbits), P(st.vscale), st.nt_cap))
+        _, wk, tl, sp = c
+        N = K.N
+        if out is not None and (out.dtype != q.dtype or not out.is_contiguous() or out.numel() != n_q * self.d_head):
+            raise ValueError("out must be a contiguous (n_q, d) tensor of q's dtype")
+        res = out
+        out = torch.empty(1, n_q, self.d_head, dtype=q.dtype, device=q.device) if out is None else out
+        wkey = (1, n_q, self.n_kv, st.n_tiles, t, k_sel, nw, self.n_tail)
+        need = K._STEP_WS.get(wkey)
+        if need is None:
+            need = K._STEP_WS[wkey] = N.call("kvr_sd1_workspace_bytes", *wkey)
+        ws = N.workspace("sd1_step", need, q.device)
+        N.call("kvr_sd1_decode_step", q.data_ptr(), N.dtype_code(q), 1, n_q, self.n_kv, wk[0] if nw else None,
+               wk[1] if nw else None, wk[2], nw, tl[0] if self.n_tail else None, tl[1] if self.n_tail else None,
+               self.n_tail, sp[0], sp[1], sp[2], sp[3], sp[4], st.n_tiles, t, N.TRANSFORMS[st.kind], k_sel, ex0,
+               ex1, 0.0, out.data_ptr(), N.dtype_code(out), None, ws.data_ptr(), ws.numel(), N.stream())
+        if res is not None:
+            return res
+        return out[0] if out_dtype is None or out_dtype == q.dtype else out[0].to(out_dtype)
