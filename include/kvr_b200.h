@@ -127,6 +127,20 @@ KVR_API int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t row_
                   int64_t ex_start, int64_t ex_end, int64_t *idx, float *vals,
                   int64_t out_row_stride, int64_t out_elem_stride, kvr_stream_t stream);
 
+/* compute_all_scores + exclusion + torch.topk of the token branch
+ * (kvr_retrieval.py:265-289, 389-392) in one call: the cosine scores of
+ * kvr_int4w_token_scores, counted into a per-head histogram as they are
+ * produced, the rows split around the bin of the k-th largest score by many
+ * CTAs, and the exact top k (score desc, index asc; excluded tokens and NaN
+ * as -inf) per head.  idx (k, n_kv) int64, rows sorted by score.  The
+ * workspace (kvr_int4w_token_topk_workspace_bytes) must be zero-filled once;
+ * the call leaves it ready for the next one.  n_kv <= 8, d = 128, k <= 4096. */
+KVR_API size_t kvr_int4w_token_topk_workspace_bytes(int n_kv, int64_t n_stored, int k);
+KVR_API int kvr_int4w_token_topk(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                                 const float *cos_tbl, const float *sin_tbl, int64_t rope_stride, int rope_halves_equal,
+                                 int n_kv, int d, int64_t n_stored, int k, int64_t ex_start, int64_t ex_end,
+                                 int64_t *idx, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
 /* Gather for V reconstruction and K re-rotation (kvr_retrieval.py:394-412).
  * top (k, n_kv) int64 token indices.  Writes
  *   ret_k (k, n_kv, d) fp32 : RoPE(deq K[top[i,h], h]) at position top[i,h];

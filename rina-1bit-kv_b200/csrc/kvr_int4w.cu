@@ -204,11 +204,19 @@ __device__ __forceinline__ void stage_qavg(const float *__restrict__ q, int n_q,
 // Each element's arithmetic is the reference's: k = code*step, k_rot =
 // k*cos + rotate_half(k)*sin (three roundings), then dot and norm.
 constexpr int kTsTile = 32;
+// Bins of the cosine scores over [-1, 1] for the fused top-k: a monotone map,
+// so every score of a higher bin beats every score of a lower one.
+constexpr int kCosBins = 4096;
+__device__ __forceinline__ int cos_bin(float s) {
+  const int b = (int)floorf((s + 1.0f) * (0.5f * kCosBins));
+  return b < 0 ? 0 : (b >= kCosBins ? kCosBins - 1 : b);
+}
 __device__ __forceinline__ int ts_idx(int h, int c) { return h * 176 + c + (c >> 4) * 4; }
 __global__ void __launch_bounds__(256) token_scores_kernel(
     const float *__restrict__ q, int n_q, const uint8_t *__restrict__ kp, const float *__restrict__ sc,
     const float *__restrict__ cs, const float *__restrict__ sn, int64_t rope_stride, int halves_equal, int n_kv,
-    int64_t n_stored, float *__restrict__ scores, int64_t score_stride) {
+    int64_t n_stored, float *__restrict__ scores, int64_t score_stride, int *__restrict__ hist, int64_t ex0,
+    int64_t ex1) {
   constexpr int d = 128;
   __shared__ __align__(16) float qa[8 * 176];  // n_kv <= 8
   __shared__ __align__(16) float stp[8 * 176];
@@ -328,7 +336,13 @@ __global__ void __launch_bounds__(256) token_scores_kernel(
     __syncthreads();
     for (int e = tid; e < n_kv * kTsTile; e += blockDim.x) {
       const int h2 = e / kTsTile, j = e - h2 * kTsTile;
-      if (t0 + j < n_stored) scores[(int64_t)h2 * score_stride + t0 + j] = outb[h2][j];
+      if (t0 + j < n_stored) {
+        const float sv = outb[h2][j];
+        scores[(int64_t)h2 * score_stride + t0 + j] = sv;
+        const int64_t t = t0 + j;
+        if (hist != nullptr && !(t >= ex0 && t < ex1) && sv > -INFINITY)
+          atomicAdd(hist + h2 * kCosBins + cos_bin(sv), 1);
+      }
     }
   }
 }
@@ -614,6 +628,139 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_hist_kernel(const floa
   }
 }
 
+// ------------------------------------------- fused token top-k (int4w) ----
+// The score kernel counted every kept score of a head into kCosBins bins.
+// Split kernel: CTAs (segment, head) find the threshold bin (the bin holding
+// the k-th largest kept score, from the top) and route their segment's keys:
+// higher bins -> the head's "above" list (fewer than k), the threshold bin ->
+// its candidate list.  Finalize kernel (one CTA per head): exact top of the
+// candidates by key, joined with the above keys and sorted (score desc,
+// index asc); it clears the head's histogram and counters for the next call.
+// A head with fewer than k kept scores, or a threshold bin with more than
+// kTkCand keys, is finished by the whole-row radix select instead.
+constexpr int kTkCand = 4096;
+constexpr int kTkSegs = 16;
+struct TkRow {
+  int above, cand, overflow, thr;
+};
+
+__device__ __forceinline__ int tk_threshold(const int *__restrict__ hist, int k, int *above_out) {
+  // warp 0: lane l owns bins [kCosBins - 128(l+1), kCosBins - 128 l), descending
+  __shared__ int thr_s, above_s;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    thr_s = -1;
+    above_s = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int hi = kCosBins - 128 * lane;
+    int s = 0;
+    for (int b = hi - 1; b >= hi - 128; --b) s += hist[b];
+    int incl = s;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - s;
+    if (excl < k && k <= incl) {
+      int cum = excl;
+      for (int b = hi - 1; b >= hi - 128; --b) {
+        if (cum + hist[b] >= k) {
+          thr_s = b;
+          above_s = cum;
+          break;
+        }
+        cum += hist[b];
+      }
+    }
+  }
+  __syncthreads();
+  *above_out = above_s;
+  return thr_s;  // -1: fewer than k kept scores
+}
+
+__global__ void __launch_bounds__(256) tk_split_kernel(const float *__restrict__ scores, int64_t n, int k,
+                                                       int64_t ex0, int64_t ex1, const int *__restrict__ hist,
+                                                       TkRow *__restrict__ rows, unsigned long long *__restrict__ above,
+                                                       unsigned long long *__restrict__ cand) {
+  const int h = blockIdx.y;
+  int above_n;
+  const int thr = tk_threshold(hist + (int64_t)h * kCosBins, k, &above_n);
+  if (thr < 0) return;  // finalize falls back to the whole-row select
+  const float *row = scores + (int64_t)h * n;
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * per, i1 = min(n, i0 + per);
+  TkRow &r = rows[h];
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float v = __ldcg(row + i);
+    if ((i >= ex0 && i < ex1) || !(v > -INFINITY)) continue;
+    const int b = cos_bin(v);
+    if (b > thr) {
+      above[(int64_t)h * k + atomicAdd(&r.above, 1)] = make_key(v, i);
+    } else if (b == thr) {
+      const int slot = atomicAdd(&r.cand, 1);
+      if (slot < kTkCand) cand[(int64_t)h * kTkCand + slot] = make_key(v, i);
+      else r.overflow = 1;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kTopkThreads) tk_finalize_kernel(const float *__restrict__ scores, int64_t n,
+                                                                   int k, int64_t ex0, int64_t ex1,
+                                                                   int *__restrict__ hist, TkRow *__restrict__ rows,
+                                                                   const unsigned long long *__restrict__ above,
+                                                                   const unsigned long long *__restrict__ cand,
+                                                                   int64_t *__restrict__ idx, int n_kv) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn);
+  int P = 1;
+  while (P < k) P <<= 1;
+  unsigned long long *keys = reinterpret_cast<unsigned long long *>(dyn + align_up(sizeof(TopkSmem), 16));
+  unsigned long long *cand_s = keys + P;       // P keys: the candidates' top
+  unsigned long long *cbuf = cand_s + P;       // kTkCand keys staged
+  const int h = blockIdx.x, tid = threadIdx.x;
+  TkRow &r = rows[h];
+  int above_n;
+  const int thr = tk_threshold(hist + (int64_t)h * kCosBins, k, &above_n);
+  const int na = r.above, nc = r.cand;
+  const bool fallback = thr < 0 || r.overflow != 0 || na != above_n;
+  if (fallback) {
+    const float *row = scores + (int64_t)h * n;
+    block_topk<kTopkThreads>([&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(row + i); },
+                             n, k, keys, tsm);
+  } else {
+    for (int i = tid; i < nc; i += kTopkThreads) cbuf[i] = cand[(int64_t)h * kTkCand + i];
+    for (int i = tid; i < na; i += kTopkThreads) keys[i] = above[(int64_t)h * k + i];
+    __syncthreads();
+    const int need = k - na;
+    block_topk_keys<kTopkThreads>([&](int64_t i) -> unsigned long long { return cbuf[i]; }, nc, need, cand_s, tsm);
+    for (int j = tid; j < need; j += kTopkThreads) keys[na + j] = cand_s[j];
+    for (int j = k + tid; j < P; j += kTopkThreads) keys[j] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < P / 2; i += kTopkThreads) {
+          const int a = 2 * i - (i & (stride - 1));
+          const int b = a + stride;
+          const bool desc = ((a & size) == 0);
+          const unsigned long long x = keys[a], y = keys[b];
+          if ((x < y) == desc) {
+            keys[a] = y;
+            keys[b] = x;
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+  for (int j = tid; j < k; j += kTopkThreads) idx[(int64_t)j * n_kv + h] = key_index(keys[j]);
+  // leave the head's histogram and counters zeroed for the next call
+  __syncthreads();
+  for (int b = tid; b < kCosBins; b += kTopkThreads) hist[(int64_t)h * kCosBins + b] = 0;
+  if (tid == 0) r = TkRow{0, 0, 0, 0};
+}
+
 // ---------------------------------------------------------------- gather ----
 // One warp per (i, h): ret_k row (RoPE'd head h) and the all-heads x row.
 __global__ void __launch_bounds__(256) gather_kernel(const uint8_t *__restrict__ kp, const float *__restrict__ sc,
@@ -796,7 +943,7 @@ extern "C" int kvr_int4w_token_scores(const float *q, int n_q, const uint8_t *k_
   int64_t blocks = tiles < 148 * 3 ? tiles : 148 * 3;
   token_scores_kernel<<<(unsigned)blocks, 256, smem, as_cuda(stream)>>>(
       q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride, rope_halves_equal, n_kv, n_stored, scores,
-      score_stride);
+      score_stride, nullptr, 0, 0);
   return check_launch("kvr_int4w_token_scores");
 }
 
@@ -890,4 +1037,67 @@ extern "C" int kvr_window_write(const void *k, const void *v, int dtype, int64_t
   else if (dtype == KVR_F16) window_write_kernel<KVR_F16><<<blocks, 256, 0, st>>>(k, v, first, count, row, ring_k, ring_v, cap, pos);
   else window_write_kernel<KVR_BF16><<<blocks, 256, 0, st>>>(k, v, first, count, row, ring_k, ring_v, cap, pos);
   return check_launch("kvr_window_write");
+}
+
+extern "C" size_t kvr_int4w_token_topk_workspace_bytes(int n_kv, int64_t n_stored, int k) {
+  if (n_kv <= 0 || n_stored <= 0 || k <= 0) return 256;
+  return align_up((size_t)n_kv * kCosBins * 4, 256) + align_up((size_t)n_kv * sizeof(TkRow), 256) +
+         align_up((size_t)n_kv * k * 8, 256) + align_up((size_t)n_kv * kTkCand * 8, 256) +
+         align_up((size_t)n_kv * n_stored * 4, 256);
+}
+
+extern "C" int kvr_int4w_token_topk(const float *q, int n_q, const uint8_t *k_packed, const float *k_scales,
+                                    const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                    int rope_halves_equal, int n_kv, int d, int64_t n_stored, int k, int64_t ex_start,
+                                    int64_t ex_end, int64_t *idx, void *workspace, size_t workspace_bytes,
+                                    kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(d == 128, "kvr_int4w_token_topk: head_dim must be 128");
+  KVR_REQUIRE(n_kv > 0 && n_kv <= 8 && n_q % n_kv == 0, "kvr_int4w_token_topk: need n_kv <= 8, n_q %% n_kv == 0");
+  KVR_REQUIRE(q && k_packed && k_scales && cos_tbl && sin_tbl && idx && workspace, "kvr_int4w_token_topk: null pointer");
+  KVR_REQUIRE(n_stored > 0 && k > 0 && k <= n_stored && k <= 4096 && n_stored < 0xffffffffll,
+              "kvr_int4w_token_topk: need 0 < k <= min(n_stored, 4096)");
+  KVR_REQUIRE(workspace_bytes >= kvr_int4w_token_topk_workspace_bytes(n_kv, n_stored, k),
+              "kvr_int4w_token_topk: workspace too small");
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_int4w_token_topk: workspace alignment");
+  char *p = reinterpret_cast<char *>(workspace);
+  int *hist = reinterpret_cast<int *>(p);
+  p += align_up((size_t)n_kv * kCosBins * 4, 256);
+  TkRow *rows = reinterpret_cast<TkRow *>(p);
+  p += align_up((size_t)n_kv * sizeof(TkRow), 256);
+  unsigned long long *above = reinterpret_cast<unsigned long long *>(p);
+  p += align_up((size_t)n_kv * k * 8, 256);
+  unsigned long long *cand = reinterpret_cast<unsigned long long *>(p);
+  p += align_up((size_t)n_kv * kTkCand * 8, 256);
+  float *scores = reinterpret_cast<float *>(p);
+  // scores + histogram (the same launch as kvr_int4w_token_scores)
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(k_packed) & 15) == 0 && (reinterpret_cast<uintptr_t>(cos_tbl) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sin_tbl) & 15) == 0 && rope_stride % 4 == 0 &&
+                  rope_stride >= (rope_halves_equal ? 64 : 128),
+              "kvr_int4w_token_topk: packed rows and rope tables must be 16-byte aligned");
+  const int cw = rope_halves_equal ? 64 : 128;
+  const size_t smem = 2 * ((size_t)kTsTile * n_kv * 64 + 2 * (size_t)kTsTile * cw * 4);
+  const int64_t tiles = (n_stored + kTsTile - 1) / kTsTile;
+  cudaStream_t st = as_cuda(stream);
+  static thread_local int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int P = 1;
+  while (P < k) P <<= 1;
+  const size_t fin_smem = align_up(sizeof(TopkSmem), 16) + (size_t)P * 16 + (size_t)kTkCand * 8;
+  if (attr_dev != dev) {
+    cudaFuncSetAttribute(token_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(tk_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)(align_up(sizeof(TopkSmem), 16) + 4096 * 16 + kTkCand * 8));
+    attr_dev = dev;
+  }
+  const int64_t blocks = tiles < 148 * 3 ? tiles : 148 * 3;
+  token_scores_kernel<<<(unsigned)blocks, 256, smem, st>>>(q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride,
+                                                          rope_halves_equal, n_kv, n_stored, scores, n_stored, hist,
+                                                          ex_start, ex_end);
+  dim3 sg((unsigned)kTkSegs, (unsigned)n_kv);
+  tk_split_kernel<<<sg, 256, 0, st>>>(scores, n_stored, k, ex_start, ex_end, hist, rows, above, cand);
+  tk_finalize_kernel<<<n_kv, kTopkThreads, fin_smem, st>>>(scores, n_stored, k, ex_start, ex_end, hist, rows, above,
+                                                           cand, idx, n_kv);
+  return check_launch("kvr_int4w_token_topk");
 }

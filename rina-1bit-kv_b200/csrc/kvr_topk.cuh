@@ -99,12 +99,12 @@ __device__ unsigned long long block_kth_largest(ScoreFn score_of, int64_t n, int
   return sm.result;
 }
 
-// score_of(i) -> float for 0 <= i < n (exclusions already mapped to -inf).
-// cand: shared array of at least next_pow2(k) keys.  On return (after a
-// __syncthreads) cand[0..k) holds the selected keys in descending order.
+// key_of(i) -> the unique 64-bit key of entry i (0 <= i < n); the k largest
+// keys are selected.  cand: shared array of at least next_pow2(k) keys.  On
+// return (after a __syncthreads) cand[0..k) holds them in descending order.
 // Must be called by all NT threads of the block.
-template <int NT, typename ScoreFn>
-__device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long long *cand, TopkSmem &sm) {
+template <int NT, typename KeyFn>
+__device__ void block_topk_keys(KeyFn key_of, int64_t n, int k, unsigned long long *cand, TopkSmem &sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
     sm.prefix = 0ull;
@@ -120,7 +120,7 @@ __device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long lon
     __syncthreads();
     const unsigned long long prefix = sm.prefix, mask = sm.mask;
     for (int64_t i = tid; i < n; i += NT) {
-      const unsigned long long key = make_key(score_of(i), i);
+      const unsigned long long key = key_of(i);
       if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255], 1);
     }
     __syncthreads();
@@ -165,7 +165,7 @@ __device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long lon
     unsigned long long key = 0ull;
     bool take = false;
     if (i < n) {
-      key = make_key(score_of(i), i);
+      key = key_of(i);
       take = (key & mask) >= prefix;
     }
     // one atomic per warp for the slots of its selected keys
@@ -199,6 +199,13 @@ __device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long lon
       __syncthreads();
     }
   }
+}
+
+// score_of(i) -> float for 0 <= i < n (exclusions already mapped to -inf);
+// keys (score, ~index): score descending, then index ascending.
+template <int NT, typename ScoreFn>
+__device__ void block_topk(ScoreFn score_of, int64_t n, int k, unsigned long long *cand, TopkSmem &sm) {
+  block_topk_keys<NT>([&](int64_t i) -> unsigned long long { return make_key(score_of(i), i); }, n, k, cand, sm);
 }
 
 // Top-k (k <= 32) of a row held in shared memory by warp-level bitonic

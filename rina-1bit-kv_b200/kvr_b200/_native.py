@@ -43,6 +43,8 @@ SIGNATURES = {
     "kvr_int4w_token_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, P, I64, P]),
     "kvr_int4w_chunk_scores": (I, [P, I, P, P, P, P, I64, I, I, I, I64, I, P, I64, P]),
     "kvr_topk_rows": (I, [P, I, I64, I64, I, I64, I64, P, P, I64, I64, P]),
+    "kvr_int4w_token_topk_workspace_bytes": (SZ, [I, I64, I]),
+    "kvr_int4w_token_topk": (I, [P, I, P, P, P, P, I64, I, I, I, I64, I, I64, I64, P, P, SZ, P]),
     "kvr_int4w_gather": (I, [P, P, P, I, I, I, P, P, I64, P, P, P, P, P]),
     "kvr_int4w_vpredict_weights_bytes": (SZ, [I, I]),
     "kvr_int4w_vpredict_prepare": (I, [P, P, P, P, I, I, P, P, P, P]),

@@ -85,6 +85,20 @@ def int4w_token_scores(q_post, k_packed, k_scales, cos, sin, n_stored, halves_eq
     return out
 
 
+def int4w_token_topk(q_post, k_packed, k_scales, cos, sin, n_stored, k, halves_equal=False, ex_start=0, ex_end=0):
+    """Token branch of retrieve_topk in one call (scores + exclusion + top-k,
+    kvr_retrieval.py:265-289, 389-392) -> idx (k, n_kv) int64."""
+    n_kv = k_packed.shape[1]
+    q = _c(q_post.float())
+    cos, sin, rs = _rope_args(cos.float(), sin.float())
+    idx = torch.empty(k, n_kv, dtype=torch.int64, device=q.device)
+    ws = N.workspace("int4w_topk", call("kvr_int4w_token_topk_workspace_bytes", n_kv, n_stored, k), q.device)
+    call("kvr_int4w_token_topk", ptr(q), q.shape[0], ptr(_c(k_packed)), ptr(_c(k_scales.float())), ptr(cos),
+         ptr(sin), rs, int(halves_equal), n_kv, D, n_stored, k, ex_start, ex_end, ptr(idx), ptr(ws), ws.numel(),
+         stream())
+    return idx
+
+
 def int4w_chunk_scores(q_post, k_packed, k_scales, cos, sin, n_stored, chunk, halves_equal=False):
     """compute_chunk_scores (kvr_retrieval.py:291-315) -> HEAD-MAJOR (n_kv, n_stored // chunk)."""
     n_kv = k_packed.shape[1]

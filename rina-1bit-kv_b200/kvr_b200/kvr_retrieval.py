@@ -345,8 +345,8 @@ class RetrievalIndex:
             tok = cidx.unsqueeze(1) * cs + torch.arange(cs, device=self.device).view(1, cs, 1)
             return tok.reshape(top_chunks * cs, self.n_kv), None
         cos, sin, he = self._tables(nr)
-        sc = K.int4w_token_scores(q_post_rope, self.k_packed, self.k_scales, cos, sin, nr, he)
-        idx, _ = K.topk_rows(sc, top_k, exclude_start, exclude_end, transpose_out=True)
+        idx = K.int4w_token_topk(q_post_rope, self.k_packed, self.k_scales, cos, sin, nr, top_k, he, exclude_start,
+                                 exclude_end)
         return idx, None
 
     @torch.no_grad()

@@ -251,3 +251,20 @@ def test_appended_tokens_join_their_nearest_basin():
     want, _, _ = R.attractor_select(q, st2, cos_big.astype(F32), sin_big.astype(F32), lab, cent, 48, 16)
     g0 = got.cpu().numpy()[:, 0]
     assert len(set(g0.tolist()) ^ set(want.tolist())) <= 2
+
+
+@pytest.mark.parametrize("n,k,ex", [(32256, 1024, (0, 0)), (4096, 512, (1000, 2000)), (3000, 2900, (0, 500)),
+                                    (700, 64, (0, 0))])
+def test_fused_token_topk_vs_scores_then_topk(n, k, ex):
+    """kvr_int4w_token_topk = kvr_int4w_token_scores + exclusion +
+    kvr_topk_rows, index for index (including the fallback when fewer than
+    k scores survive the exclusion)."""
+    from kvr_b200 import kernels as K
+    st, cos, sin, q = _store(n + k, n)
+    kp, ks, ct, sn, qt = t(st["k_packed"]), t(st["k_scales"]), t(cos), t(sin), t(q)
+    for _ in range(2):  # the second call reuses the workspace the first left clean
+        got = K.int4w_token_topk(qt, kp, ks, ct, sn, n, k, True, *ex)
+        sc = K.int4w_token_scores(qt, kp, ks, ct, sn, n, True)
+        want, _ = K.topk_rows(sc, k, *ex, transpose_out=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
