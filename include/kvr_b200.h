@@ -129,9 +129,8 @@ KVR_API int kvr_topk_rows(const float *scores, int rows, int64_t n, int64_t row_
 
 /* compute_all_scores + exclusion + torch.topk of the token branch
  * (kvr_retrieval.py:265-289, 389-392) in one call: the cosine scores of
- * kvr_int4w_token_scores, counted into a per-head histogram as they are
- * produced, the rows split around the bin of the k-th largest score by many
- * CTAs, and the exact top k (score desc, index asc; excluded tokens and NaN
+ * kvr_int4w_token_scores, a per-head histogram of them, the rows split around
+ * the bin of the k-th largest score by many CTAs, and the exact top k (score desc, index asc; excluded tokens and NaN
  * as -inf) per head.  idx (k, n_kv) int64, rows sorted by score.  The
  * workspace (kvr_int4w_token_topk_workspace_bytes) must be zero-filled once;
  * the call leaves it ready for the next one.  n_kv <= 8, d = 128, k <= 4096. */

@@ -629,7 +629,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_hist_kernel(const floa
 }
 
 // ------------------------------------------- fused token top-k (int4w) ----
-// The score kernel counted every kept score of a head into kCosBins bins.
+// Histogram kernel: CTAs (segment, head) count the kept scores of a head into
+// kCosBins bins (shared-memory histograms added into a global one).
 // Split kernel: CTAs (segment, head) find the threshold bin (the bin holding
 // the k-th largest kept score, from the top) and route their segment's keys:
 // higher bins -> the head's "above" list (fewer than k), the threshold bin ->
@@ -678,6 +679,27 @@ __device__ __forceinline__ int tk_threshold(const int *__restrict__ hist, int k,
   __syncthreads();
   *above_out = above_s;
   return thr_s;  // -1: fewer than k kept scores
+}
+
+// Per-(segment, head) histogram of the kept scores in shared memory, added
+// into the head's global histogram bin by bin (only non-empty bins).
+__global__ void __launch_bounds__(256) tk_hist_kernel(const float *__restrict__ scores, int64_t n, int64_t ex0,
+                                                      int64_t ex1, int *__restrict__ hist) {
+  __shared__ int sh[kCosBins];
+  const int h = blockIdx.y;
+  for (int b = threadIdx.x; b < kCosBins; b += blockDim.x) sh[b] = 0;
+  __syncthreads();
+  const float *row = scores + (int64_t)h * n;
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * per, i1 = min(n, i0 + per);
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const float v = __ldcg(row + i);
+    if ((i >= ex0 && i < ex1) || !(v > -INFINITY)) continue;
+    atomicAdd(&sh[cos_bin(v)], 1);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < kCosBins; b += blockDim.x)
+    if (sh[b]) atomicAdd(hist + (int64_t)h * kCosBins + b, sh[b]);
 }
 
 __global__ void __launch_bounds__(256) tk_split_kernel(const float *__restrict__ scores, int64_t n, int k,
@@ -1039,10 +1061,17 @@ extern "C" int kvr_window_write(const void *k, const void *v, int dtype, int64_t
   return check_launch("kvr_window_write");
 }
 
+// Workspace: a fixed header (histograms and counters of up to 8 heads, which
+// must start at zero and are left at zero) at the same offsets whatever the
+// shapes, so one workspace can serve calls of different shapes; then the
+// per-call regions (rewritten before they are read).
+constexpr size_t kTkHdrHist = 0;
+constexpr size_t kTkHdrRows = (size_t)8 * kCosBins * 4;
+constexpr size_t kTkHdr = kTkHdrRows + 256;
+
 extern "C" size_t kvr_int4w_token_topk_workspace_bytes(int n_kv, int64_t n_stored, int k) {
-  if (n_kv <= 0 || n_stored <= 0 || k <= 0) return 256;
-  return align_up((size_t)n_kv * kCosBins * 4, 256) + align_up((size_t)n_kv * sizeof(TkRow), 256) +
-         align_up((size_t)n_kv * k * 8, 256) + align_up((size_t)n_kv * kTkCand * 8, 256) +
+  if (n_kv <= 0 || n_stored <= 0 || k <= 0) return kTkHdr;
+  return kTkHdr + align_up((size_t)n_kv * k * 8, 256) + align_up((size_t)n_kv * kTkCand * 8, 256) +
          align_up((size_t)n_kv * n_stored * 4, 256);
 }
 
@@ -1061,10 +1090,9 @@ extern "C" int kvr_int4w_token_topk(const float *q, int n_q, const uint8_t *k_pa
               "kvr_int4w_token_topk: workspace too small");
   KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "kvr_int4w_token_topk: workspace alignment");
   char *p = reinterpret_cast<char *>(workspace);
-  int *hist = reinterpret_cast<int *>(p);
-  p += align_up((size_t)n_kv * kCosBins * 4, 256);
-  TkRow *rows = reinterpret_cast<TkRow *>(p);
-  p += align_up((size_t)n_kv * sizeof(TkRow), 256);
+  int *hist = reinterpret_cast<int *>(p + kTkHdrHist);
+  TkRow *rows = reinterpret_cast<TkRow *>(p + kTkHdrRows);
+  p += kTkHdr;
   unsigned long long *above = reinterpret_cast<unsigned long long *>(p);
   p += align_up((size_t)n_kv * k * 8, 256);
   unsigned long long *cand = reinterpret_cast<unsigned long long *>(p);
@@ -1093,9 +1121,10 @@ extern "C" int kvr_int4w_token_topk(const float *q, int n_q, const uint8_t *k_pa
   }
   const int64_t blocks = tiles < 148 * 3 ? tiles : 148 * 3;
   token_scores_kernel<<<(unsigned)blocks, 256, smem, st>>>(q, n_q, k_packed, k_scales, cos_tbl, sin_tbl, rope_stride,
-                                                          rope_halves_equal, n_kv, n_stored, scores, n_stored, hist,
-                                                          ex_start, ex_end);
+                                                          rope_halves_equal, n_kv, n_stored, scores, n_stored, nullptr,
+                                                          0, 0);
   dim3 sg((unsigned)kTkSegs, (unsigned)n_kv);
+  tk_hist_kernel<<<sg, 256, 0, st>>>(scores, n_stored, ex_start, ex_end, hist);
   tk_split_kernel<<<sg, 256, 0, st>>>(scores, n_stored, k, ex_start, ex_end, hist, rows, above, cand);
   tk_finalize_kernel<<<n_kv, kTopkThreads, fin_smem, st>>>(scores, n_stored, k, ex_start, ex_end, hist, rows, above,
                                                            cand, idx, n_kv);
