@@ -16,11 +16,11 @@
 // relative (or 2^-25 of the row's largest entry), i.e. fp32-level: the
 // result differs from the reference's fp32 GEMM only by summation order.
 //
-// Work split: a CTA owns 64 selected tokens of one KV head and all 128
-// output channels; 8 warps = 4 (16-token rows) x 2 (64-channel halves), each
-// warp 8 n8-tiles of mma.sync m16n8k16 (fp16 in, fp32 accumulate).  The
-// contraction dimension (n_kv * d) advances in chunks of 64: the codes of
-// the CTA's 64 tokens are gathered from their packed rows and widened to
+// Work split: a CTA owns M (64, or 32 when that leaves SMs idle) selected
+// tokens of one KV head and all 128 output channels; its 8 warps tile
+// (M/16 token slabs) x (128 channels), mma.sync m16n8k16 (fp16 in, fp32
+// accumulate).  The contraction dimension (n_kv * d) advances in chunks of
+// 64: the codes of the CTA's tokens are gathered from their packed rows and widened to
 // fp16 in registers, W' hi/lo chunks (32 KB) arrive by cp.async; both are
 // double-buffered so the next chunk loads while the current one multiplies.
 #include "kvr_common.cuh"
@@ -29,13 +29,20 @@ namespace kvr {
 
 namespace vp {
 constexpr int kD = 128;
-constexpr int kM = 64;          // tokens per CTA
 constexpr int kK = 64;          // contraction chunk
 constexpr int kPitch = kK + 8;  // smem row pitch in halves (144 B: conflict-free ldmatrix)
-constexpr int kAHalves = kM * kPitch;
 constexpr int kBHalves = 2 * kD * kPitch;  // hi and lo parts
-constexpr int kStageHalves = kAHalves + kBHalves;
-constexpr size_t kSmem = 2 * kStageHalves * 2;  // two stages, bytes
+template <int M>
+struct Cfg {
+  static constexpr int kAHalves = M * kPitch;
+  static constexpr int kStageHalves = kAHalves + kBHalves;
+  static constexpr size_t kSmem = 2 * kStageHalves * 2;  // two stages, bytes
+  static constexpr int kWarpsM = M / 16;                  // 16-row slabs
+  static constexpr int kWarpsN = 8 / kWarpsM;             // column groups
+  static constexpr int kColsW = kD / kWarpsN;             // columns per warp
+  static constexpr int kNT = kColsW / 8;                  // n8 tiles per warp
+  static constexpr int kABytesT = M * (kK / 2) / 256;     // packed code bytes per thread per chunk
+};
 }  // namespace vp
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
@@ -52,43 +59,47 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// 16 int4 codes (8 packed bytes, even element in the high nibble) -> 16 fp16
-// values, in element order, as 8 half2 words.
-__device__ __forceinline__ void codes_to_half(uint2 raw, uint32_t (&h)[8]) {
-  const uint32_t w[2] = {raw.x, raw.y};
+// 2*NW int4 codes (NW packed words, even element in each byte's high nibble)
+// -> fp16 values in element order, as half2 words.
+template <int NW>
+__device__ __forceinline__ void codes_to_half(const uint32_t (&w)[NW], uint32_t (&h)[4 * NW]) {
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
+  for (int b = 0; b < 4 * NW; ++b) {
     const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xffu;
     const __half e = __int2half_rn((int)(byte >> 4) - 8), o = __int2half_rn((int)(byte & 15u) - 8);
     h[b] = (uint32_t)__half_as_ushort(e) | ((uint32_t)__half_as_ushort(o) << 16);
   }
 }
 
+template <int M>
 __global__ void __launch_bounds__(256) vpredict_kernel(const uint8_t *__restrict__ kp, const int64_t *__restrict__ top,
                                                        const int32_t *__restrict__ count, int k, int n_kv,
                                                        const __half *__restrict__ w3, const float *__restrict__ unscale,
                                                        const float *__restrict__ bias, const uint8_t *__restrict__ vr,
                                                        const float *__restrict__ vrs, __half *__restrict__ out) {
   using namespace vp;
+  using C = Cfg<M>;
+  constexpr int NWORD = C::kABytesT / 4;  // 32-bit code words per thread per chunk (2 or 1)
   extern __shared__ __align__(16) unsigned char smraw[];
   __half *sm = reinterpret_cast<__half *>(smraw);
   const int h = blockIdx.y;
-  const int i0 = blockIdx.x * kM;
+  const int i0 = blockIdx.x * M;
   const int n_valid = count ? min(k, __ldg(count)) : k;
   if (i0 >= n_valid) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int KD = n_kv * kD;
   const int64_t row_bytes = (int64_t)n_kv * (kD / 2);
   const int nch = KD / kK;
-  // A producer: thread -> (token row tid/4, 8-byte piece tid%4 of the chunk's 32 code bytes)
-  const int ar = tid >> 2, ap = tid & 3;
+  // A producer: thread -> (token row, piece of C::kABytesT bytes of the chunk's 32 code bytes)
+  constexpr int PPR = (kK / 2) / C::kABytesT;  // pieces per row
+  const int ar = tid / PPR, ap = tid % PPR;
   const bool a_ok = i0 + ar < n_valid;
   const int64_t tok = a_ok ? __ldg(top + (int64_t)(i0 + ar) * n_kv + h) : 0;
   const uint8_t *arow = kp + tok * row_bytes;
   const __half *wh = w3 + (int64_t)h * 2 * kD * KD;  // [part][c][j]
 
   auto issue_b = [&](int c, int stage) {
-    __half *Bs = sm + stage * kStageHalves + kAHalves;
+    __half *Bs = sm + stage * C::kStageHalves + C::kAHalves;
     const int j0 = c * kK;
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
@@ -98,39 +109,51 @@ __global__ void __launch_bounds__(256) vpredict_kernel(const uint8_t *__restrict
     }
     cp_async_commit();
   };
-  auto load_a = [&](int c) -> uint2 {
-    if (!a_ok) return make_uint2(0x88888888u, 0x88888888u);  // codes 0
-    return __ldg(reinterpret_cast<const uint2 *>(arow + c * (kK / 2) + ap * 8));
+  auto load_a = [&](int c, uint32_t (&w)[NWORD]) {
+#pragma unroll
+    for (int q = 0; q < NWORD; ++q) w[q] = 0x88888888u;  // codes 0
+    if (!a_ok) return;
+    if constexpr (NWORD == 2) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(arow + c * (kK / 2) + ap * 8));
+      w[0] = v.x;
+      w[NWORD - 1] = v.y;
+    } else {
+      w[0] = __ldg(reinterpret_cast<const uint32_t *>(arow + c * (kK / 2) + ap * 4));
+    }
   };
-  auto store_a = [&](uint2 raw, int stage) {
-    uint32_t hv[8];
-    codes_to_half(raw, hv);
-    __half *As = sm + stage * kStageHalves;
-    uint4 *dst = reinterpret_cast<uint4 *>(As + ar * kPitch + ap * 16);
-    dst[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-    dst[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+  auto store_a = [&](const uint32_t (&w)[NWORD], int stage) {
+    uint32_t hv[4 * NWORD];
+    codes_to_half<NWORD>(w, hv);
+    __half *As = sm + stage * C::kStageHalves;
+    uint4 *dst = reinterpret_cast<uint4 *>(As + ar * kPitch + ap * (8 * NWORD));
+#pragma unroll
+    for (int q = 0; q < NWORD; ++q) dst[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
   };
 
-  float acc[8][4];
+  float acc[C::kNT][4];
 #pragma unroll
-  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-  const int wm = (warp & 3) * 16, wn = (warp >> 2) * 64;
+  for (int n = 0; n < C::kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+  const int wm = (warp % C::kWarpsM) * 16, wn = (warp / C::kWarpsM) * C::kColsW;
 
   issue_b(0, 0);
-  store_a(load_a(0), 0);
+  {
+    uint32_t w0[NWORD];
+    load_a(0, w0);
+    store_a(w0, 0);
+  }
   for (int c = 0; c < nch; ++c) {
     const int st = c & 1;
-    uint2 nxt = make_uint2(0u, 0u);
+    uint32_t nxt[NWORD];
     if (c + 1 < nch) {
       issue_b(c + 1, st ^ 1);
-      nxt = load_a(c + 1);
+      load_a(c + 1, nxt);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const __half *As = sm + st * kStageHalves;
-    const __half *Bs = As + kAHalves;
+    const __half *As = sm + st * C::kStageHalves;
+    const __half *Bs = As + C::kAHalves;
 #pragma unroll
     for (int kk = 0; kk < kK; kk += 16) {
       uint32_t a[4];
@@ -138,7 +161,7 @@ __global__ void __launch_bounds__(256) vpredict_kernel(const uint8_t *__restrict
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {  // pairs of n8 tiles
+        for (int np = 0; np < C::kNT / 2; ++np) {  // pairs of n8 tiles
           uint32_t b[4];
           const int nrow = part * kD + wn + np * 16 + (lane & 7) + (lane >> 4) * 8;
           ldsm_x4(b, Bs + nrow * kPitch + kk + ((lane >> 3) & 1) * 8);
@@ -161,7 +184,7 @@ __global__ void __launch_bounds__(256) vpredict_kernel(const uint8_t *__restrict
     const int64_t t = __ldg(top + (int64_t)i * n_kv + h);
     const uint8_t *rrow = vr + (t * n_kv + h) * (kD / 4);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < C::kNT; ++n) {
       const int col = wn + n * 8 + 2 * t4;
       const int r = h * kD + col;
       float v2[2];
@@ -269,16 +292,27 @@ extern "C" int kvr_int4w_vpredict(const uint8_t *k_packed, const int64_t *top, c
   auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
   KVR_REQUIRE(al(k_packed, 8) && al(w3, 16) && al(ret_v, 4), "kvr_int4w_vpredict: misaligned buffers");
   if (k == 0) return KVR_OK;
+  // 32-token tiles (more CTAs in flight) unless the selection is large enough
+  // to fill the GPU with 64-token tiles
+  const bool small_m = (int64_t)((k + 63) / 64) * n_kv < 2 * 148;
   static thread_local int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaFuncSetAttribute(vpredict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vp::kSmem);
+    cudaFuncSetAttribute(vpredict_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vp::Cfg<64>::kSmem);
+    cudaFuncSetAttribute(vpredict_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vp::Cfg<32>::kSmem);
     attr_dev = dev;
   }
-  dim3 grid((unsigned)((k + vp::kM - 1) / vp::kM), (unsigned)n_kv);
-  vpredict_kernel<<<grid, 256, vp::kSmem, as_cuda(stream)>>>(k_packed, top, count, k, n_kv,
-                                                              reinterpret_cast<const __half *>(w3), unscale, bias,
-                                                              vr_packed, vr_scales, reinterpret_cast<__half *>(ret_v));
+  if (small_m) {
+    dim3 grid((unsigned)((k + 31) / 32), (unsigned)n_kv);
+    vpredict_kernel<32><<<grid, 256, vp::Cfg<32>::kSmem, as_cuda(stream)>>>(
+        k_packed, top, count, k, n_kv, reinterpret_cast<const __half *>(w3), unscale, bias, vr_packed, vr_scales,
+        reinterpret_cast<__half *>(ret_v));
+  } else {
+    dim3 grid((unsigned)((k + 63) / 64), (unsigned)n_kv);
+    vpredict_kernel<64><<<grid, 256, vp::Cfg<64>::kSmem, as_cuda(stream)>>>(
+        k_packed, top, count, k, n_kv, reinterpret_cast<const __half *>(w3), unscale, bias, vr_packed, vr_scales,
+        reinterpret_cast<__half *>(ret_v));
+  }
   return check_launch("kvr_int4w_vpredict");
 }
