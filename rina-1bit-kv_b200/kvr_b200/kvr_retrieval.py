@@ -540,6 +540,17 @@ class RetrievalIndex:
             self.n_stored += self.tile
             self.n_tail = 0
 
+    @torch.no_grad()
+    def prefill_tile_scores(self, q_block):
+        """sd1: tile scores of a block of prefill-position queries against the
+        encoded tiles on the tensor cores (kvr_sd1_prefill_scores, tcgen05):
+        q_block (nq, n_q, d) post-RoPE -> (nq, n_kv, n_tiles) fp32, the max over
+        each tile of q'.k-hat.  No reference counterpart (the reference only
+        retrieves at decode); for prefill-time retrieval over a long prompt."""
+        if self.codec != "sd1" or self.store is None:
+            raise NotImplementedError("prefill_tile_scores needs codec='sd1' with encoded tiles")
+        return K.sd1_prefill_scores(self.store, q_block)
+
     @property
     def n_tokens(self):
         """Tokens held: encoded + pending tail (sd1); n_stored (int4w)."""
