@@ -281,6 +281,7 @@ struct SelectArgs {
   const uint32_t *vbits;   // optional: V data of the scanned tiles is
   const uint16_t *vscale;  // prefetched into L2 for the attention kernel
   RowPrefetch rows;        // optional (k[s] null = none): exact rows prefetched into L2
+  unsigned *err;           // the workspace's error word (bounded waits that gave up)
 };
 
 
@@ -560,6 +561,13 @@ __device__ void warp_head_qprime(const void *__restrict__ q, int64_t qh, int kin
   reinterpret_cast<float4 *>(qprime + qh * kD)[lane] = make_float4(x[0], x[1], x[2], x[3]);
 }
 
+// Per-warp copy ring of the flat scan: kStages pairs of tiles in flight.
+template <int TILE>
+struct FlatRing {
+  static constexpr int kStages = TILE == 128 ? 2 : 4;
+  static constexpr size_t kBytes = (size_t)8 * kStages * 2 * (TILE * 16 + kD * 2);  // 8 warps
+};
+
 template <int DTQ, int TILE>
 __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
     const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
@@ -570,6 +578,7 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
   __shared__ __align__(16) float qp_s[2][kD];
   __shared__ int last_rows[2];
   __shared__ int n_last;
+  __shared__ uint64_t ring_bar[8][FlatRing<TILE>::kStages];
   extern __shared__ __align__(16) unsigned char dyn_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = n_q / n_kv;
@@ -582,6 +591,7 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
   const int n0 = (int)(min(f1, (r0 + 1) * n_tiles) - f0);
   const int n1 = nrows == 2 ? (int)(f1 - (r0 + 1) * n_tiles) : 0;
   const int pairs0 = (int)((n0 + 1) / 2), n_pairs = pairs0 + (int)((n1 + 1) / 2);
+  KVR_TRACE_POINT(2, 0);
   load_lee(lee_s);
   // the CTA holding tile 0 of a row streams that row's exact K/V rows into L2
   // for the attention kernel that follows (a hint: no ordering needed)
@@ -601,57 +611,80 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
     }
   }
   constexpr int TPL = TILE / 32;  // tokens per lane
+  constexpr int TB = TILE * 16, SB = kD * 2, PB = 2 * (TB + SB), NS = FlatRing<TILE>::kStages;
   // pair p -> (row slot, first tile, last tile of its segment)
   auto pair_at = [&](int p, int &sl, int &t_first, int &t_end) {
     sl = p < pairs0 ? 0 : 1;
     t_first = sl == 0 ? st0 + 2 * p : 2 * (p - pairs0);
     t_end = sl == 0 ? st0 + n0 : n1;
   };
-  uint4 kb[2][TPL];
-  uint16_t ks[2][4];
-  auto load_pair = [&](int sl, int t_first, int t_end, uint4 (&kbd)[2][TPL], uint16_t (&ksd)[2][4]) {
+  // Each warp streams its pairs (sign bits + scales of two tiles, PB bytes)
+  // through an NS-stage ring of bulk copies in shared memory, NS pairs ahead
+  // of the one it scores: enough bytes in flight per SM to cover DRAM latency.
+  unsigned char *ring = dyn_smem + (size_t)warp * NS * PB;
+  auto issue = [&](int p, int st) {  // lane 0
+    int sl, t_first, t_end;
+    pair_at(p, sl, t_first, t_end);
+    mbar_expect_tx(&ring_bar[warp][st], PB);
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int t = min(t_first + u, t_end - 1);  // a lone last tile is scored twice, stored once
       const int64_t tix = (r0 + sl) * nt_cap + t;
-      const uint4 *src = reinterpret_cast<const uint4 *>(kbits + tix * TILE * 4);
-#pragma unroll
-      for (int r = 0; r < TPL; ++r) kbd[u][r] = __ldg(src + lane + 32 * r);
-#pragma unroll
-      for (int m = 0; m < 4; ++m) ksd[u][m] = __ldg(kscale + tix * kD + lane + 32 * m);
+      bulk_g2s(ring + st * PB + u * TB, kbits + tix * TILE * 4, TB, &ring_bar[warp][st]);
+      bulk_g2s(ring + st * PB + 2 * TB + u * SB, kscale + tix * kD, SB, &ring_bar[warp][st]);
     }
   };
-  int p = warp, sl = 0, t_first = 0, t_end = 0;
-  if (p < n_pairs) {
-    pair_at(p, sl, t_first, t_end);
-    load_pair(sl, t_first, t_end, kb, ks);
-  }
+  int issued = 0;  // pairs issued by this warp (warp-uniform)
+  if (lane == 0)
+    for (int st = 0; st < NS; ++st) mbar_init(&ring_bar[warp][st], 1);
+  __syncwarp();
+  for (int st = 0; st < NS && warp + 8 * st < n_pairs; ++st, ++issued)
+    if (lane == 0) issue(warp + 8 * st, st);
+  KVR_TRACE_POINT(2, 6);
   // q is read, and anything written, after the previous kernel has finished
   griddep_wait();
+  KVR_TRACE_POINT(2, 7);
   asm volatile("griddepcontrol.launch_dependents;");
   __syncthreads();  // Lee factors
   if (warp < nrows) {
     const int64_t r = r0 + warp, b = r / n_kv;
     warp_group_qprime<DTQ>(q, n_q, g, b, (int)(r - b * n_kv), kind, lee_s, buf_s[warp], qp_s[warp]);
-  } else if (warp >= 2 && qprime != nullptr) {
-    // per-head T q for the attention kernel (warps 2..7), from the CTA holding
-    // the row's tile 0
-    for (int it = warp - 2; it < 2 * g; it += 6) {
-      const int s2 = it / g, i = it - s2 * g;
-      if (s2 >= nrows || (s2 == 0 && st0 != 0)) continue;
-      const int64_t r = r0 + s2, b = r / n_kv;
-      warp_head_qprime<DTQ>(q, (b * n_q + (r - b * n_kv) * g + i), kind, lee_s, buf_s[warp], qprime);
-    }
   }
   __syncthreads();
-  while (p < n_pairs) {  // warp-uniform
-    const int pn = p + 8;
-    uint4 kbn[2][TPL];
-    uint16_t ksn[2][4];
-    if (pn < n_pairs) {
-      int sln, tfn, ten;
-      pair_at(pn, sln, tfn, ten);
-      load_pair(sln, tfn, ten, kbn, ksn);
+  KVR_TRACE_POINT(2, 1);
+  int it = 0;
+  for (int p = warp; p < n_pairs; p += 8, ++it) {  // warp-uniform
+    const int st = it % NS;
+    if (!mbar_wait_bounded(&ring_bar[warp][st], (unsigned)(it / NS) & 1u)) {
+      // gave up: report, stop scoring, let the copies in flight land before
+      // the shared memory is reused by the selection
+      if (lane == 0 && sa.err) atomicOr(sa.err, 4u);
+      for (int j = it; j < issued; ++j) mbar_wait_bounded(&ring_bar[warp][j % NS], (unsigned)(j / NS) & 1u);
+      break;
+    }
+    int sl, t_first, t_end;
+    pair_at(p, sl, t_first, t_end);
+    uint4 kb[2][TPL];
+    uint16_t ks[2][4];
+    {
+      // token rows lane + 32 r of both tiles, channel scales lane + 32 m
+      const uint4 *bw = reinterpret_cast<const uint4 *>(ring + st * PB);
+      const uint16_t *sw = reinterpret_cast<const uint16_t *>(ring + st * PB + 2 * TB);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int r = 0; r < TPL; ++r) kb[u][r] = bw[u * TILE + lane + 32 * r];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) ks[u][m] = sw[u * kD + lane + 32 * m];
+      }
+    }
+    __syncwarp();
+    if (p + 8 * NS < n_pairs) {
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(p + 8 * NS, st);
+      }
+      ++issued;
     }
     float sc[2];
     sd1_score_tile2<TILE>(qp_s[sl], kb, ks, lane, sc);
@@ -660,20 +693,21 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
       scores[r * n_tiles + t_first] = sc[0];
       if (t_first + 1 < t_end) scores[r * n_tiles + t_first + 1] = sc[1];
     }
-    p = pn;
-    if (p < n_pairs) {
-      pair_at(p, sl, t_first, t_end);
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-#pragma unroll
-        for (int r = 0; r < TPL; ++r) kb[u][r] = kbn[u][r];
-#pragma unroll
-        for (int m = 0; m < 4; ++m) ks[u][m] = ksn[u][m];
-      }
+  }
+  // per-head T q for the attention kernel (which reads it after this grid
+  // has completed), from the CTA holding the row's tile 0: off the path to
+  // the first tile scores
+  if (qprime != nullptr) {
+    for (int it = warp; it < 2 * g; it += 8) {
+      const int s2 = it / g, i = it - s2 * g;
+      if (s2 >= nrows || (s2 == 0 && st0 != 0)) continue;
+      const int64_t r = r0 + s2, b = r / n_kv;
+      warp_head_qprime<DTQ>(q, (b * n_q + (r - b * n_kv) * g + i), kind, lee_s, buf_s[warp], qprime);
     }
   }
   // the CTA whose tiles complete a row selects it
   __syncthreads();
+  KVR_TRACE_POINT(2, 2);
   if (threadIdx.x == 0) {
     __threadfence();
     int nl = 0;
@@ -692,6 +726,7 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
     if (threadIdx.x == 0) sa.counters[r] = 0u;
     __syncthreads();
   }
+  KVR_TRACE_POINT(2, 3 + n_last);
 }
 
 // ---------------------------------------------------------- tile decode ----
@@ -834,7 +869,9 @@ template <int DTQ>
 static int launch_score_flat(int tile, int64_t rows, int64_t tpc, cudaStream_t st, const void *q, int n_q,
                              int n_kv, const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind,
                              float *scores, float *qprime, SelectArgs sa) {
-  const size_t smem = select_dyn_smem(sa.k_sel, nt);
+  const size_t sel_smem = select_dyn_smem(sa.k_sel, nt);
+  const size_t ring = tile == 32 ? FlatRing<32>::kBytes : tile == 64 ? FlatRing<64>::kBytes : FlatRing<128>::kBytes;
+  const size_t smem = sel_smem > ring ? sel_smem : ring;  // the selection reuses the ring after the scan
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)((rows * nt + tpc - 1) / tpc));
   cfg.blockDim = dim3(256);
@@ -990,6 +1027,8 @@ int sd1_select_scratch(const void *q, int q_dtype, int batch, int n_q, int n_kv,
   KVR_REQUIRE((int64_t)batch * n_kv <= kWsMaxRows, "kvr_sd1_select: batch*n_kv > %d", kWsMaxRows);
   SelectArgs sa{k_sel, ex_t0, ex_t1, tile_base, sel, sel_scores, counters, vbits, vscale, RowPrefetch{}};
   if (rows) sa.rows = *rows;
+  // every workspace that holds the selection counters starts with the error word
+  sa.err = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(counters) - kWsSelCounters);
   // With no full tile there is nothing to score; the kernel still forms q'
   // and writes an all-empty selection.
   return sd1_scores_impl(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, scores, qprime,

@@ -6,6 +6,29 @@
 
 namespace kvr {
 
+// P = sum_{p<7} 2^p popc(plane_p & x) - 2^7 popc(plane_7 & x) over the 4
+// words of one token row.  Planes 6 and 7 go through one carry-save full
+// adder each (three popcounts instead of four: popc(a)+popc(b)+popc(c) =
+// popc(a^b^c) + 2 popc(maj(a,b,c))), which moves work from the popcount unit
+// to the logic pipe where that pays: the scan is bound by the two together.
+__device__ __forceinline__ int sd1_plane_dot(const uint32_t (&plane)[8][4], const uint32_t (&bw)[4]) {
+  int P = 0;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    const uint32_t a = plane[p][0] & bw[0], b = plane[p][1] & bw[1], c = plane[p][2] & bw[2],
+                   d = plane[p][3] & bw[3];
+    int cnt;
+    if (p >= 6) {
+      const uint32_t sum = a ^ b ^ c, carry = (a & b) | (c & (a ^ b));
+      cnt = __popc(sum) + __popc(d) + 2 * __popc(carry);
+    } else {
+      cnt = __popc(a) + __popc(b) + __popc(c) + __popc(d);
+    }
+    P += p == 7 ? -(cnt << 7) : (cnt << p);
+  }
+  return P;
+}
+
 // qp: transformed group-mean query (128 fp32, shared memory); kb: this lane's
 // TILE/32 token rows (16 bytes = 4 words each, token lane + 32 r); ks: fp16
 // scales of channels lane + 32 m.  Lane c of the ballots owns channels
@@ -42,19 +65,7 @@ __device__ __forceinline__ float sd1_score_tile(const float *qp, const uint4 (&k
 #pragma unroll
   for (int r = 0; r < TPL; ++r) {
     const uint32_t bw[4] = {kb[r].x, kb[r].y, kb[r].z, kb[r].w};
-    int P = 0;
-#pragma unroll
-    for (int p = 0; p < 7; ++p) {
-      int cnt = 0;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) cnt += __popc(plane[p][m] & bw[m]);
-      P += cnt << p;
-    }
-    int c7 = 0;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) c7 += __popc(plane[7][m] & bw[m]);
-    P -= c7 << 7;
-    best = max(best, 2 * P - wsum);
+    best = max(best, 2 * sd1_plane_dot(plane, bw) - wsum);
   }
   best = warp_max_int(best);
   return __fmul_rn((float)best, __fdiv_rn(mx, 127.0f));
@@ -106,19 +117,7 @@ __device__ __forceinline__ void sd1_score_tile2(const float *qp, const uint4 (&k
 #pragma unroll
     for (int r = 0; r < TPL; ++r) {
       const uint32_t bw[4] = {kb[u][r].x, kb[u][r].y, kb[u][r].z, kb[u][r].w};
-      int P = 0;
-#pragma unroll
-      for (int p = 0; p < 7; ++p) {
-        int cnt = 0;
-#pragma unroll
-        for (int m = 0; m < 4; ++m) cnt += __popc(plane[p][m] & bw[m]);
-        P += cnt << p;
-      }
-      int c7 = 0;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) c7 += __popc(plane[7][m] & bw[m]);
-      P -= c7 << 7;
-      best[u] = max(best[u], 2 * P - wsum[u]);
+      best[u] = max(best[u], 2 * sd1_plane_dot(plane, bw) - wsum[u]);
     }
   }
 #pragma unroll
