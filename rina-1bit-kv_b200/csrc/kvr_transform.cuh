@@ -50,7 +50,7 @@ __device__ __forceinline__ void wht128(float (&x)[4], int lane) {
 // Loads the Lee factors into shared memory (call by all threads of a block,
 // followed by a __syncthreads before first use).
 __device__ __forceinline__ void load_lee(float *lee_s) {
-  for (int i = threadIdx.x; i < kD - 1; i += blockDim.x) lee_s[i] = __uint_as_float(kLeeBits[i]);
+  for (int i = threadIdx.x; i < kD - 1; i += blockDim.x) lee_s[i] = __uint_as_float(__ldg(kLeeBitsGlobal + i));
 }
 
 // Lee levels as compile-time steps (block size M is a template constant, so

@@ -5,6 +5,7 @@ trace build of the library (KVR_TRACE_POINT; python -m kvr_b200._build
 --trace).  The product library carries no stamps.
 
     python rina-1bit-kv_b200/phase_trace.py [--layers 32] [--reps 30]
+    python rina-1bit-kv_b200/phase_trace.py --batched   # configs[2] flat tile scan
 
 A 32-layer step is captured in a CUDA graph as in bench.py and replayed;
 after each replay the stamps of the last layer's two kernels are read back
@@ -51,13 +52,70 @@ def stamps(buf, kernel, blocks, point):
     return out
 
 
+def batched_scan(reps):
+    """Phases of sd1_score_flat_kernel (trace kernel id 2) at configs[2]
+    shapes: 32 sequences x 8 KV heads x 252 tiles of 64 (16384 context less a
+    256 window), top 16, DCT, bf16 q.  Each replay is one standalone
+    selection call after a 256 MiB memset (cold L2); stamps are per CTA."""
+    B, NT2 = 32, 252
+    lib = N.lib()
+    rd = lib.kvr_debug_trace_sd1
+    rd.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    rd.restype = ctypes.c_int
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    scale = torch.exp(torch.randn(HKV, D, device=dev, generator=g))
+    k = (torch.randn(B, NT2 * TILE, HKV, D, device=dev, generator=g) * scale).to(torch.bfloat16)
+    v = torch.randn(B, NT2 * TILE, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    st = K.Sd1Store(B, HKV, NT2, TILE, "dct", dev)
+    K.sd1_encode(st, k, v)
+    del k, v
+    q = torch.randn(B, HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rows = {}
+    for _ in range(reps):
+        flush.zero_()
+        K.sd1_select(st, q, KSEL)
+        torch.cuda.synchronize()
+        buf = read(rd)
+        T = lambda b, p: buf[(2 * SLOTS + b) * 8 + p]  # noqa: E731
+        blocks = [b for b in range(SLOTS) if T(b, 0)]
+        t0 = min(T(b, 0) for b in blocks)
+        V = lambda b, p: T(b, p) if T(b, p) >= t0 else 0  # noqa: E731  (older launches' stamps)
+        med = lambda xs: statistics.median(list(xs)) / 1e3  # noqa: E731
+
+        def add(name, val):
+            rows.setdefault(name, []).append(val)
+
+        add("CTAs", len(blocks))
+        add("start -> copy ring issued (median CTA)", med(T(b, 6) - T(b, 0) for b in blocks))
+        add("grid dependency wait (median CTA)", med(T(b, 7) - T(b, 6) for b in blocks))
+        add("q' of the CTA's rows formed (median CTA)", med(T(b, 1) - T(b, 7) for b in blocks))
+        add("tile scan (median CTA)", med(T(b, 2) - T(b, 1) for b in blocks))
+        add("tile scan (slowest CTA)", max(T(b, 2) - T(b, 1) for b in blocks) / 1e3)
+        sel = [max(V(b, 4), V(b, 5)) - T(b, 2) for b in blocks if max(V(b, 4), V(b, 5))]
+        add("row selection by the completing CTA (median)", med(sel))
+        add("row selection (slowest)", max(sel) / 1e3)
+        add("last CTA done (from first start)",
+            max(max(V(b, 3), V(b, 4), V(b, 5)) for b in blocks) / 1e3 - t0 / 1e3)
+    print("| phase (configs[2] flat tile scan) | us (median over replays) |")
+    print("|---|---|")
+    for name, vals in rows.items():
+        val = statistics.median(vals)
+        print(f"| {name} | {val:.0f} |" if name == "CTAs" else f"| {name} | {val:.2f} |")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--reps", type=int, default=30)
+    ap.add_argument("--batched", action="store_true", help="configs[2] flat tile scan phases instead")
     args = ap.parse_args()
     if not os.path.exists(TRACE_LIB):
         raise SystemExit(f"{TRACE_LIB} missing: python -m kvr_b200._build --trace (from rina-1bit-kv_b200/)")
+    if args.batched:
+        batched_scan(args.reps)
+        return
     lib = N.lib()
     rd_sel = lib.kvr_debug_trace_sd1
     rd_att = lib.kvr_debug_trace_attn
