@@ -1049,55 +1049,52 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   const int64_t row = b * a.n_kv + h;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const int n_exact = a.nchunk[0] + a.nchunk[1];
+  KVR_TRACE_POINT(1, 0);
   asm volatile("griddepcontrol.launch_dependents;");
   if (a.kind == KVR_DCT) load_lee(reinterpret_cast<float *>(sm + AttnSmem::kLee));
   if (tid == 0) reinterpret_cast<int *>(sm + AttnSmem::kFlag)[2] = 0;
-  // q and q' of the group (q' and the selection come from the preceding
-  // kernel) staged as fp32 rows, rows of heads >= g zero
-  griddep_wait();
+  // q of the group staged as fp32 rows (rows of heads >= g zero).  q is
+  // ready before the preceding selection kernel started, so the window /
+  // tail pieces run while that kernel finishes; q' and the selection are
+  // read after the grid dependency wait below.
   float *Qs = reinterpret_cast<float *>(sm + AttnSmem::kQ);   // fp32 [8][128]
   float *Qps = reinterpret_cast<float *>(sm + AttnSmem::kS);  // fp32 [8][128]
   float *red = reinterpret_cast<float *>(sm + RowSmem::kRed);
   const bool any_tiles = a.units > n_exact;
-  float amx = 0.0f, amt = 0.0f;
-  for (int i = tid; i < kMaxG * 32; i += blockDim.x) {
-    const int hq = i >> 5, qd = i & 31;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
-    if (hq < a.g) {
-      const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
-      x = cvt4(raw4(a.q, qh * kD + qd * 4, a.q_dt), a.q_dt);
-      if (any_tiles) y = __ldcg(reinterpret_cast<const float4 *>(a.qprime + qh * kD) + qd);
+  // stage the group's rows of q (sd1 = false) or q' (sd1 = true) as B
+  // fragments, multiplied by the power of two that brings max |.| near 2^12
+  auto stage_bfrags = [&](bool sd1, float *rows, uint4 *QB) -> float {
+    float amx = 0.0f;
+    for (int i = tid; i < kMaxG * 32; i += blockDim.x) {
+      const int hq = i >> 5, qd = i & 31;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (hq < a.g) {
+        const int64_t qh = b * a.n_q + (int64_t)h * a.g + hq;
+        x = sd1 ? __ldcg(reinterpret_cast<const float4 *>(a.qprime + qh * kD) + qd)
+                : cvt4(raw4(a.q, qh * kD + qd * 4, a.q_dt), a.q_dt);
+      }
+      amx = fmaxf(amx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      reinterpret_cast<float4 *>(rows + hq * kD)[qd] = x;
     }
-    amx = fmaxf(amx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-    amt = fmaxf(amt, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
-    reinterpret_cast<float4 *>(Qs + hq * kD)[qd] = x;
-    reinterpret_cast<float4 *>(Qps + hq * kD)[qd] = y;
-  }
-  amx = warp_max(amx);
-  amt = warp_max(amt);
-  if (lane == 0) {
-    red[warp] = amx;
-    red[8 + warp] = amt;
-  }
-  __syncthreads();
-  float qsx = 0.0f, qst = 0.0f;
+    amx = warp_max(amx);
+    if (lane == 0) red[(sd1 ? 8 : 0) + warp] = amx;
+    __syncthreads();
+    float qs = 0.0f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    qsx = fmaxf(qsx, red[w]);
-    qst = fmaxf(qst, red[8 + w]);
-  }
-  qsx = pow2_scale(qsx);
-  qst = pow2_scale(qst);
+    for (int w = 0; w < 8; ++w) qs = fmaxf(qs, red[(sd1 ? 8 : 0) + w]);
+    qs = pow2_scale(qs);
+    const int kk = tid >> 5;  // 8 k-steps x 32 lanes = 256 threads
+    QB[kk * 32 + lane] = q_bfrag(rows + g * kD, kk, lane, sd1, qs);
+    __syncthreads();
+    return qs;
+  };
   uint4 *QBx = reinterpret_cast<uint4 *>(sm + RowSmem::kQBx);
   uint4 *QBt = reinterpret_cast<uint4 *>(sm + RowSmem::kQBt);
-  {
-    const int kk = tid >> 5;  // 8 k-steps x 32 lanes = 256 threads
-    QBx[kk * 32 + lane] = q_bfrag(Qs + g * kD, kk, lane, false, qsx);
-    if (any_tiles) QBt[kk * 32 + lane] = q_bfrag(Qps + g * kD, kk, lane, true, qst);
-  }
-  __syncthreads();
+  const float qsx = stage_bfrags(false, Qs, QBx);
+  KVR_TRACE_POINT(1, 1);
   constexpr float kLog2e = 1.4426950408889634f;
-  const float sx = a.inv_scale * kLog2e / qsx, stl = a.inv_scale * kLog2e / qst;
+  const float sx = a.inv_scale * kLog2e / qsx;
+  float stl = 0.0f;
 
   RowState st;
   st.m[0] = st.m[1] = -INFINITY;
@@ -1139,58 +1136,71 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   const int n_pieces = 2 * ex_units + PPT * max(0, u1 - u0 - ex_units);
   // Every piece of this warp is requested into L2 first (no registers held):
   // the loads of the pieces then wait for L2 instead of a DRAM round trip each.
-  for (int pc = warp; pc < n_pieces; pc += 8) {
-    if (pc < 2 * ex_units) {
-      const int u = u0 + pc / 2;
-      const int seg = u < a.nchunk[0] ? 0 : 1;
-      const int64_t t0 = (int64_t)(seg == 0 ? u : u - a.nchunk[0]) * kChunk + (pc & 1) * kPiece;
-      if (t0 + lane < a.n[seg]) {
-        const int64_t off = b * a.batch_stride[seg] + (int64_t)h * kD + (t0 + lane) * a.tok_stride[seg];
-        prefetch_l2(reinterpret_cast<const __half *>(a.k[seg]) + off, kD * 2);
-        prefetch_l2(reinterpret_cast<const __half *>(a.v[seg]) + off, kD * 2);
-      }
-    } else if (lane < 4) {
-      const int r = pc - 2 * ex_units;
-      const int u = u0 + ex_units + r / PPT, sub = r % PPT;
-      const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
-      if (tsel >= 0) {
-        const int64_t tix = row * a.nt_cap + tsel;
-        const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
-        if (lane == 0) prefetch_l2(a.kbits + w0, kPiece * 16);
-        if (lane == 1) prefetch_l2(a.vbits + w0, kPiece * 16);
-        if (lane == 2) prefetch_l2(a.kscale + tix * kD, kD * 2);
-        if (lane == 3) prefetch_l2(a.vscale + tix * kD, kD * 2);
+  // Exact pieces (pc < 2 * ex_units) come first in every warp's sequence.
+  auto prefetch_pieces = [&](int pc0, int pc1) {
+    for (int pc = pc0; pc < pc1; pc += 8) {
+      if (pc < 2 * ex_units) {
+        const int u = u0 + pc / 2;
+        const int seg = u < a.nchunk[0] ? 0 : 1;
+        const int64_t t0 = (int64_t)(seg == 0 ? u : u - a.nchunk[0]) * kChunk + (pc & 1) * kPiece;
+        if (t0 + lane < a.n[seg]) {
+          const int64_t off = b * a.batch_stride[seg] + (int64_t)h * kD + (t0 + lane) * a.tok_stride[seg];
+          prefetch_l2(reinterpret_cast<const __half *>(a.k[seg]) + off, kD * 2);
+          prefetch_l2(reinterpret_cast<const __half *>(a.v[seg]) + off, kD * 2);
+        }
+      } else if (lane < 4) {
+        const int r = pc - 2 * ex_units;
+        const int u = u0 + ex_units + r / PPT, sub = r % PPT;
+        const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+        if (tsel >= 0) {
+          const int64_t tix = row * a.nt_cap + tsel;
+          const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
+          if (lane == 0) prefetch_l2(a.kbits + w0, kPiece * 16);
+          if (lane == 1) prefetch_l2(a.vbits + w0, kPiece * 16);
+          if (lane == 2) prefetch_l2(a.kscale + tix * kD, kD * 2);
+          if (lane == 3) prefetch_l2(a.vscale + tix * kD, kD * 2);
+        }
       }
     }
+  };
+  // first sd1 piece of this warp's sequence
+  const int pc_t = warp >= 2 * ex_units ? warp : warp + (2 * ex_units - warp + 7) / 8 * 8;
+  prefetch_pieces(warp, min(n_pieces, 2 * ex_units));
+  for (int pc = warp; pc < min(n_pieces, 2 * ex_units); pc += 8) {
+    const int u = u0 + pc / 2;
+    const int seg = u < a.nchunk[0] ? 0 : 1;
+    const int chunk = seg == 0 ? u : u - a.nchunk[0];
+    const int64_t t0 = (int64_t)chunk * kChunk + (pc & 1) * kPiece;
+    const int64_t left = a.n[seg] - t0;
+    if (left <= 0) continue;
+    const int nt = (int)(left < kPiece ? left : kPiece);
+    const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD + t0 * a.tok_stride[seg];
+    row_piece_exact<PLO>(st, QBx, Ph, nt, reinterpret_cast<const __half *>(a.k[seg]) + base,
+                         reinterpret_cast<const __half *>(a.v[seg]) + base, a.tok_stride[seg], sx, a.g);
   }
-  for (int pc = warp; pc < n_pieces; pc += 8) {
-    if (pc < 2 * ex_units) {
-      const int u = u0 + pc / 2;
-      const int seg = u < a.nchunk[0] ? 0 : 1;
-      const int chunk = seg == 0 ? u : u - a.nchunk[0];
-      const int64_t t0 = (int64_t)chunk * kChunk + (pc & 1) * kPiece;
-      const int64_t left = a.n[seg] - t0;
-      if (left <= 0) continue;
-      const int nt = (int)(left < kPiece ? left : kPiece);
-      const int64_t base = b * a.batch_stride[seg] + (int64_t)h * kD + t0 * a.tok_stride[seg];
-      row_piece_exact<PLO>(st, QBx, Ph, nt, reinterpret_cast<const __half *>(a.k[seg]) + base,
-                      reinterpret_cast<const __half *>(a.v[seg]) + base, a.tok_stride[seg], sx, a.g);
-    } else {
-      if (!parked) park();
-      const int r = pc - 2 * ex_units;
-      const int u = u0 + ex_units + r / PPT, sub = r % PPT;
-      const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
-      if (tsel < 0) continue;
-      const int64_t tix = row * a.nt_cap + tsel;
-      const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
-      row_piece_sd1<PLO>(st, QBt, Ph, a.kbits + w0, a.vbits + w0, a.kscale + tix * kD, a.vscale + tix * kD, SC,
-                         stl, a.g);
-    }
+  // q' and the selection come from the preceding kernel
+  griddep_wait();
+  if (any_tiles) {
+    const float qst = stage_bfrags(true, Qps, QBt);  // block-wide: every warp arrives here
+    stl = a.inv_scale * kLog2e / qst;
+    prefetch_pieces(pc_t, n_pieces);
+  }
+  for (int pc = pc_t; pc < n_pieces; pc += 8) {
+    if (!parked) park();
+    const int r = pc - 2 * ex_units;
+    const int u = u0 + ex_units + r / PPT, sub = r % PPT;
+    const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+    if (tsel < 0) continue;
+    const int64_t tix = row * a.nt_cap + tsel;
+    const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
+    row_piece_sd1<PLO>(st, QBt, Ph, a.kbits + w0, a.vbits + w0, a.kscale + tix * kD, a.vscale + tix * kD, SC,
+                       stl, a.g);
   }
   if (!parked) park();  // only exact pieces (or none): the sd1 sum is zero
 
   // fold the 8 warp states into the CTA accumulators (warp order)
   __syncthreads();  // the B fragments and P staging are dead from here on
+  KVR_TRACE_POINT(1, 2);
   float *Ftr = reinterpret_cast<float *>(sm + RowSmem::kFtr);
   float *Fm = reinterpret_cast<float *>(sm + RowSmem::kFm);
   float *Fl = reinterpret_cast<float *>(sm + RowSmem::kFl);
@@ -1237,6 +1247,7 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   __syncthreads();
   KVR_TRACE_POINT(1, 3);
   attn_finish(a, sm, b, h);
+  KVR_TRACE_POINT(1, 6);
 }
 
 // Merge kernel for sequence-split partials: one warp per query row.

@@ -98,11 +98,41 @@ def batched_scan(reps):
         add("row selection (slowest)", max(sel) / 1e3)
         add("last CTA done (from first start)",
             max(max(V(b, 3), V(b, 4), V(b, 5)) for b in blocks) / 1e3 - t0 / 1e3)
+    # the batched attention kernel (attn_rows_kernel, trace kernel id 1) on
+    # the selection above: window of 256 fp16 rows + 16 tiles per row
+    WIN2 = 256
+    wk = torch.randn(B, WIN2, HKV, D, device=dev, generator=g).half()
+    wv = torch.randn(B, WIN2, HKV, D, device=dev, generator=g).half()
+    rd_att = lib.kvr_debug_trace_attn
+    rd_att.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    rd_att.restype = ctypes.c_int
+    sel, _, qp = K.sd1_select(st, q, KSEL)
+    for _ in range(reps):
+        flush.zero_()
+        K.sd1_attend(st, q, qp, sel, wk, wv, WIN2, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        buf = read(rd_att)
+        T = lambda b, p: buf[(1 * SLOTS + b) * 8 + p]  # noqa: E731
+        blocks = [b for b in range(SLOTS) if T(b, 0) and T(b, 6) >= T(b, 0)]
+        t0 = min(T(b, 0) for b in blocks)
+        med = lambda xs: statistics.median(list(xs)) / 1e3  # noqa: E731
+
+        def add(name, val):
+            rows.setdefault(name, []).append(val)
+
+        add("attend: CTAs", len(blocks))
+        add("attend: last CTA start", max(T(b, 0) for b in blocks) / 1e3 - t0 / 1e3)
+        add("attend: q staged as B fragments (median CTA)", med(T(b, 1) - T(b, 0) for b in blocks))
+        add("attend: 32-token pieces, all warps (median CTA)", med(T(b, 2) - T(b, 1) for b in blocks))
+        add("attend: pieces (slowest CTA)", max(T(b, 2) - T(b, 1) for b in blocks) / 1e3)
+        add("attend: fold of the 8 warp states (median CTA)", med(T(b, 3) - T(b, 2) for b in blocks))
+        add("attend: finish, inverse transform + output (median CTA)", med(T(b, 6) - T(b, 3) for b in blocks))
+        add("attend: last CTA done (from first start)", max(T(b, 6) for b in blocks) / 1e3 - t0 / 1e3)
     print("| phase (configs[2] flat tile scan) | us (median over replays) |")
     print("|---|---|")
     for name, vals in rows.items():
         val = statistics.median(vals)
-        print(f"| {name} | {val:.0f} |" if name == "CTAs" else f"| {name} | {val:.2f} |")
+        print(f"| {name} | {val:.0f} |" if name.endswith("CTAs") else f"| {name} | {val:.2f} |")
 
 
 def main():
