@@ -756,6 +756,14 @@ struct RowSmem {
 };
 static_assert(RowSmem::kEnd <= AttnSmem::kQ && RowSmem::kFEnd + 64 <= AttnSmem::kQ,
               "batched decode staging must stay inside the unit region");
+// In-kernel selection of the batched path: scores (<= kRowsRankMax), the
+// warp lists and the candidates in the parked-sum region, the chosen tiles
+// (<= 32) after the piece staging.
+constexpr int64_t kRowsRankMax = 4096;
+constexpr int kRowsRankMaxK = 32;
+static_assert(4 * kRowsRankMax + 8 * 32 * 8 + kRowsRankMaxK * 8 <= RowSmem::kQBx - RowSmem::kFex &&
+                  RowSmem::kEnd + 4 * kRowsRankMaxK <= AttnSmem::kQ,
+              "batched in-kernel selection must fit the free staging");
 
 __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -1134,6 +1142,13 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   const int ex_units = max(0, min(u1, n_exact) - u0);
   constexpr int PPT = TILE / kPiece;  // pieces per tile
   const int n_pieces = 2 * ex_units + PPT * max(0, u1 - u0 - ex_units);
+  // The row's selected tiles: from the selection kernel (a.sel), or, with
+  // rank scores given, the top k_sel of the row's tile scores picked here
+  // after the grid dependency wait (the same keys and order as the selection
+  // kernel's pick), into RS.
+  const bool rank_rows = a.rank_scores != nullptr && any_tiles;
+  int32_t *RS = reinterpret_cast<int32_t *>(sm + RowSmem::kEnd);
+  auto tile_of = [&](int j) -> int32_t { return rank_rows ? RS[j] : __ldcg(a.sel + row * a.k_sel + j); };
   // Every piece of this warp is requested into L2 first (no registers held):
   // the loads of the pieces then wait for L2 instead of a DRAM round trip each.
   // Exact pieces (pc < 2 * ex_units) come first in every warp's sequence.
@@ -1151,7 +1166,7 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
       } else if (lane < 4) {
         const int r = pc - 2 * ex_units;
         const int u = u0 + ex_units + r / PPT, sub = r % PPT;
-        const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+        const int32_t tsel = tile_of(u - n_exact);
         if (tsel >= 0) {
           const int64_t tix = row * a.nt_cap + tsel;
           const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
@@ -1180,6 +1195,25 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
   }
   // q' and the selection come from the preceding kernel
   griddep_wait();
+  if (rank_rows) {
+    // the parked-sum region is free until the first tile piece
+    float *sc = reinterpret_cast<float *>(sm + RowSmem::kFex);
+    unsigned long long *lists = reinterpret_cast<unsigned long long *>(sm + RowSmem::kFex + 4 * kRowsRankMax);
+    unsigned long long *cand = lists + 8 * 32;
+    const int64_t n = a.rank_n;
+    const int kk = (int)(n < a.k_sel ? n : a.k_sel);
+    const float *src = a.rank_scores + row * n;
+    for (int64_t i = tid; i < n; i += blockDim.x)
+      sc[i] = (i >= a.rank_ex0 && i < a.rank_ex1) ? -INFINITY : __ldcg(src + i);
+    __syncthreads();
+    if (kk > 0) block_topk_warp32<256>(sc, n, kk, lists, cand);
+    if (tid < a.k_sel) {
+      const int32_t v = tid < kk ? (int32_t)key_index(cand[tid]) : -1;
+      RS[tid] = v;
+      if (slot == 0 && a.sel_out != nullptr) a.sel_out[row * a.k_sel + tid] = v;
+    }
+    __syncthreads();
+  }
   if (any_tiles) {
     const float qst = stage_bfrags(true, Qps, QBt);  // block-wide: every warp arrives here
     stl = a.inv_scale * kLog2e / qst;
@@ -1189,7 +1223,7 @@ __global__ void __launch_bounds__(256, 2) attn_rows_kernel(AttnArgs a) {
     if (!parked) park();
     const int r = pc - 2 * ex_units;
     const int u = u0 + ex_units + r / PPT, sub = r % PPT;
-    const int32_t tsel = __ldcg(a.sel + row * a.k_sel + (u - n_exact));
+    const int32_t tsel = tile_of(u - n_exact);
     if (tsel < 0) continue;
     const int64_t tix = row * a.nt_cap + tsel;
     const int64_t w0 = (tix * TILE + sub * kPiece) * 4;
@@ -1318,7 +1352,7 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
   if (a.units <= 0) return set_error(KVR_EINVAL, "%s: nothing to attend", what);
   size_t smem = AttnSmem::kTotal;
   const int upc = attn_upc(a.units, (int64_t)batch * a.n_kv);
-  KVR_REQUIRE(a.rank_scores == nullptr || upc == 1, "%s: in-unit selection needs one unit per CTA", what);
+
   a.slots = (a.units + upc - 1) / upc;
   if (upc > 1) {
     // batched rows: one CTA per row once the rows fill every SM (one wave,
@@ -1338,6 +1372,9 @@ int launch_attn(AttnArgs &a, int batch, cudaStream_t st, const char *what, bool 
           (reinterpret_cast<uintptr_t>(a.v[s]) % 16) == 0;
   }
   a.pipelined = (f16 && a.n1_dev == nullptr) ? 1 : 0;
+  KVR_REQUIRE(a.rank_scores == nullptr || upc == 1 ||
+                  (a.pipelined && a.k_sel <= kRowsRankMaxK && a.rank_n <= kRowsRankMax),
+              "%s: in-kernel selection needs one unit per CTA or the batched fp16 path", what);
   const size_t ms = merge_smem_bytes(a.slots);
   if (ms > (size_t)AttnSmem::kML) return set_error(KVR_ENOTSUP, "%s: too many units (%d)", what, a.units);
   dim3 grid(a.slots, a.n_kv, batch);
@@ -1587,17 +1624,23 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   rows.tok_stride = tokw;
   const bool rows_ok = (reinterpret_cast<uintptr_t>(win_k) | reinterpret_cast<uintptr_t>(win_v) |
                         reinterpret_cast<uintptr_t>(tail_k) | reinterpret_cast<uintptr_t>(tail_v)) % 16 == 0;
+  // Batched steps on the fp16 rows path: the scan only scores and every
+  // attention CTA picks its row's top k_sel itself (no per-row counter and
+  // no selection tail at the end of the scan).
+  const bool rows_rank = !rank && rows_ok && k_sel > 0 && k_sel <= kRowsRankMaxK && n_tiles > 0 &&
+                         n_tiles <= kRowsRankMax;
+  const bool self_select = rank || rows_rank;
   int rc = sd1_select_scratch(q, q_dtype, batch, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0,
                               ex_t1, 0, sel, nullptr, qprime, reinterpret_cast<unsigned *>(p + kWsSelCounters), scores,
-                              as_cuda(stream), rank ? vbits : nullptr, rank ? vscale : nullptr, rank ? 0 : 1,
+                              as_cuda(stream), rank ? vbits : nullptr, rank ? vscale : nullptr, self_select ? 0 : 1,
                               !rank && rows_ok ? &rows : nullptr);
   if (rc) return rc;
   // the attention kernel is a programmatic dependent of the selection
   // kernel: its window/tail units overlap the tile scan, its tile units wait
   return sd1_attend_impl(q, q_dtype, qprime, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
                          kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
-                         workspace, a_bytes, stream, true, rank ? scores : nullptr, n_tiles, ex_t0, ex_t1,
-                         rank ? sel : nullptr);
+                         workspace, a_bytes, stream, true, self_select ? scores : nullptr, n_tiles, ex_t0, ex_t1,
+                         self_select ? sel : nullptr);
 }
 
 #ifdef KVR_TRACE

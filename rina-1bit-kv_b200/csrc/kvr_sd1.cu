@@ -572,7 +572,7 @@ template <int DTQ, int TILE>
 __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
     const void *__restrict__ q, int n_q, int n_kv, const uint32_t *__restrict__ kbits,
     const uint16_t *__restrict__ kscale, int64_t nt_cap, int64_t n_tiles, int kind, int64_t rows,
-    float *__restrict__ scores, float *__restrict__ qprime, SelectArgs sa, int64_t tpc) {
+    float *__restrict__ scores, float *__restrict__ qprime, SelectArgs sa, int do_select, int64_t tpc) {
   __shared__ float lee_s[kD];
   __shared__ __align__(16) float buf_s[8][2 * kD];
   __shared__ __align__(16) float qp_s[2][kD];
@@ -705,9 +705,10 @@ __global__ void __launch_bounds__(256, 2) sd1_score_flat_kernel(
       warp_head_qprime<DTQ>(q, (b * n_q + (r - b * n_kv) * g + i), kind, lee_s, buf_s[warp], qprime);
     }
   }
+  KVR_TRACE_POINT(2, 2);
+  if (!do_select) return;  // the consumer selects from the scores
   // the CTA whose tiles complete a row selects it
   __syncthreads();
-  KVR_TRACE_POINT(2, 2);
   if (threadIdx.x == 0) {
     __threadfence();
     int nl = 0;
@@ -868,8 +869,8 @@ static int launch_score(int tile, dim3 grid, int64_t tpc, cudaStream_t st, const
 template <int DTQ>
 static int launch_score_flat(int tile, int64_t rows, int64_t tpc, cudaStream_t st, const void *q, int n_q,
                              int n_kv, const uint32_t *kb, const uint16_t *ks, int64_t cap, int64_t nt, int kind,
-                             float *scores, float *qprime, SelectArgs sa) {
-  const size_t sel_smem = select_dyn_smem(sa.k_sel, nt);
+                             float *scores, float *qprime, SelectArgs sa, int do_select) {
+  const size_t sel_smem = do_select ? select_dyn_smem(sa.k_sel, nt) : 0;
   const size_t ring = tile == 32 ? FlatRing<32>::kBytes : tile == 64 ? FlatRing<64>::kBytes : FlatRing<128>::kBytes;
   const size_t smem = sel_smem > ring ? sel_smem : ring;  // the selection reuses the ring after the scan
   cudaLaunchConfig_t cfg{};
@@ -887,7 +888,7 @@ static int launch_score_flat(int tile, int64_t rows, int64_t tpc, cudaStream_t s
   case T:                                                                                               \
     ensure_dyn_smem(sd1_score_flat_kernel<DTQ, T>, smem);                                               \
     cudaLaunchKernelEx(&cfg, sd1_score_flat_kernel<DTQ, T>, q, n_q, n_kv, kb, ks, cap, nt, kind, rows,  \
-                       scores, qprime, sa, tpc);                                                        \
+                       scores, qprime, sa, do_select, tpc);                                             \
     break;
     KVR_SF(32)
     KVR_SF(64)
@@ -903,7 +904,7 @@ int sd1_scores_impl(const void *q, int q_dtype, int batch, int n_q, int n_kv, co
                     const uint16_t *kscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind, float *scores,
                     float *qprime, SelectArgs sa, int do_select, cudaStream_t st) {
   const int64_t rows = (int64_t)batch * n_kv;
-  // Batched steps with selection: equal flat ranges of the (row, tile) space,
+  // Batched steps: equal flat ranges of the (row, tile) space,
   // two CTAs per SM, once that gives every CTA at least 16 tiles and at most
   // one row's worth (KVR_SD1_SCAN=flat / warps forces a path where valid).
   {
@@ -911,13 +912,13 @@ int sd1_scores_impl(const void *q, int q_dtype, int batch, int n_q, int n_kv, co
     const bool force_flat = scan && strcmp(scan, "flat") == 0, force_warps = scan && strcmp(scan, "warps") == 0;
     const int64_t total = rows * n_tiles;
     const int64_t ftpc = (total + 295) / 296;
-    if (do_select && sa.vbits == nullptr && n_tiles >= 16 && !force_warps &&
+    if (sa.vbits == nullptr && n_tiles >= 16 && !force_warps &&
         (force_flat ? (total > 0 && ftpc <= n_tiles) : (ftpc >= 16 && ftpc <= n_tiles && rows > 1))) {
       const int64_t t = force_flat && ftpc < 16 ? (n_tiles < 16 ? n_tiles : 16) : ftpc;
       switch (q_dtype) {
-        case KVR_F32: return launch_score_flat<KVR_F32>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
-        case KVR_F16: return launch_score_flat<KVR_F16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
-        default: return launch_score_flat<KVR_BF16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa);
+        case KVR_F32: return launch_score_flat<KVR_F32>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+        case KVR_F16: return launch_score_flat<KVR_F16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
+        default: return launch_score_flat<KVR_BF16>(tile, rows, t, st, q, n_q, n_kv, kbits, kscale, nt_cap, n_tiles, kind, scores, qprime, sa, do_select);
       }
     }
   }
