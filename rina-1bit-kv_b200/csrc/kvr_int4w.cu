@@ -645,40 +645,54 @@ struct TkRow {
   int above, cand, overflow, thr;
 };
 
-__device__ __forceinline__ int tk_threshold(const int *__restrict__ hist, int k, int *above_out) {
-  // warp 0: lane l owns bins [kCosBins - 128(l+1), kCosBins - 128 l), descending
-  __shared__ int thr_s, above_s;
-  const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
+// The threshold bin of a head (the bin holding its k-th largest kept score,
+// counting from the top) by a block scan of the histogram: thread t owns
+// kCosBins / NT consecutive bins, thread 0 the highest.  Optionally leaves
+// each bin's count (cnt_s) and the number of kept scores in higher bins
+// (pos_s) in shared memory.  Returns -1 when fewer than k scores are kept.
+template <int NT>
+__device__ int tk_threshold_block(const int *__restrict__ hist, int k, int *above_out, int *pos_s = nullptr,
+                                  int *cnt_s = nullptr) {
+  constexpr int PER = kCosBins / NT;
+  __shared__ int thr_s, above_s, wsum[NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hi = kCosBins - PER * tid;  // bins [hi - PER, hi), visited downwards
+  int v[PER], sum = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    v[j] = __ldcg(hist + hi - 1 - j);
+    sum += v[j];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  if (tid == 0) {
     thr_s = -1;
     above_s = 0;
   }
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const int hi = kCosBins - 128 * lane;
-    int s = 0;
-    for (int b = hi - 1; b >= hi - 128; --b) s += hist[b];
-    int incl = s;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
+  int cum = incl - sum;
+  for (int w = 0; w < warp; ++w) cum += wsum[w];
+  const bool mine = cum < k && k <= cum + sum;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    if (pos_s) {
+      pos_s[hi - 1 - j] = cum;
+      cnt_s[hi - 1 - j] = v[j];
     }
-    const int excl = incl - s;
-    if (excl < k && k <= incl) {
-      int cum = excl;
-      for (int b = hi - 1; b >= hi - 128; --b) {
-        if (cum + hist[b] >= k) {
-          thr_s = b;
-          above_s = cum;
-          break;
-        }
-        cum += hist[b];
-      }
+    if (mine && cum < k && k <= cum + v[j]) {
+      thr_s = hi - 1 - j;
+      above_s = cum;
     }
+    cum += v[j];
   }
   __syncthreads();
   *above_out = above_s;
-  return thr_s;  // -1: fewer than k kept scores
+  return thr_s;
 }
 
 // Per-(segment, head) histogram of the kept scores in shared memory, added
@@ -706,27 +720,54 @@ __global__ void __launch_bounds__(256) tk_split_kernel(const float *__restrict__
                                                        int64_t ex0, int64_t ex1, const int *__restrict__ hist,
                                                        TkRow *__restrict__ rows, unsigned long long *__restrict__ above,
                                                        unsigned long long *__restrict__ cand) {
-  const int h = blockIdx.y;
+  const int h = blockIdx.y, lane = threadIdx.x & 31;
   int above_n;
-  const int thr = tk_threshold(hist + (int64_t)h * kCosBins, k, &above_n);
+  const int thr = tk_threshold_block<256>(hist + (int64_t)h * kCosBins, k, &above_n);
   if (thr < 0) return;  // finalize falls back to the whole-row select
   const float *row = scores + (int64_t)h * n;
   const int64_t per = (n + gridDim.x - 1) / gridDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * per, i1 = min(n, i0 + per);
   TkRow &r = rows[h];
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    const float v = __ldcg(row + i);
-    if ((i >= ex0 && i < ex1) || !(v > -INFINITY)) continue;
-    const int b = cos_bin(v);
-    if (b > thr) {
-      above[(int64_t)h * k + atomicAdd(&r.above, 1)] = make_key(v, i);
-    } else if (b == thr) {
-      const int slot = atomicAdd(&r.cand, 1);
+  // one atomic per warp and list: lanes take consecutive slots
+  const int64_t i_end = i0 + (i1 - i0 + 31) / 32 * 32;
+  for (int64_t i = i0 + threadIdx.x; i < i_end; i += blockDim.x) {
+    float v = -INFINITY;
+    if (i < i1 && !(i >= ex0 && i < ex1)) v = __ldcg(row + i);
+    const bool kept = v > -INFINITY;
+    const int b = kept ? cos_bin(v) : -1;
+    const unsigned ma = __ballot_sync(0xffffffffu, kept && b > thr);
+    const unsigned mc = __ballot_sync(0xffffffffu, kept && b == thr);
+    const unsigned below = (1u << lane) - 1u;
+    int base_a = 0, base_c = 0;
+    if (lane == 0) {
+      if (ma) base_a = atomicAdd(&r.above, __popc(ma));
+      if (mc) base_c = atomicAdd(&r.cand, __popc(mc));
+    }
+    base_a = __shfl_sync(0xffffffffu, base_a, 0);
+    base_c = __shfl_sync(0xffffffffu, base_c, 0);
+    if (ma >> lane & 1u) above[(int64_t)h * k + base_a + __popc(ma & below)] = make_key(v, i);
+    if (mc >> lane & 1u) {
+      const int slot = base_c + __popc(mc & below);
       if (slot < kTkCand) cand[(int64_t)h * kTkCand + slot] = make_key(v, i);
       else r.overflow = 1;
     }
   }
 }
+
+// Shared-memory layout of the finalize kernel for top k (P = k rounded up to
+// a power of two).
+struct TkFinSmem {
+  size_t keys, cand_s, cbuf, pos, cnt, fill, total;
+  __host__ __device__ explicit TkFinSmem(int P) {
+    keys = align_up(sizeof(TopkSmem), 16);
+    cand_s = keys + (size_t)P * 8;
+    cbuf = cand_s + (size_t)P * 8;
+    pos = cbuf + (size_t)kTkCand * 8;
+    cnt = pos + (size_t)kCosBins * 4;
+    fill = cnt + (size_t)kCosBins * 4;
+    total = fill + (size_t)kCosBins * 4;
+  }
+};
 
 __global__ void __launch_bounds__(kTopkThreads) tk_finalize_kernel(const float *__restrict__ scores, int64_t n,
                                                                    int k, int64_t ex0, int64_t ex1,
@@ -738,45 +779,63 @@ __global__ void __launch_bounds__(kTopkThreads) tk_finalize_kernel(const float *
   TopkSmem &tsm = *reinterpret_cast<TopkSmem *>(dyn);
   int P = 1;
   while (P < k) P <<= 1;
-  unsigned long long *keys = reinterpret_cast<unsigned long long *>(dyn + align_up(sizeof(TopkSmem), 16));
-  unsigned long long *cand_s = keys + P;       // P keys: the candidates' top
-  unsigned long long *cbuf = cand_s + P;       // kTkCand keys staged
+  const TkFinSmem L(P);
+  unsigned long long *keys = reinterpret_cast<unsigned long long *>(dyn + L.keys);
+  unsigned long long *cand_s = reinterpret_cast<unsigned long long *>(dyn + L.cand_s);  // the candidates' top
+  unsigned long long *cbuf = reinterpret_cast<unsigned long long *>(dyn + L.cbuf);      // candidates staged
+  int *pos_s = reinterpret_cast<int *>(dyn + L.pos);    // kept scores in higher bins
+  int *cnt_s = reinterpret_cast<int *>(dyn + L.cnt);    // the bin's count
+  int *fill_s = reinterpret_cast<int *>(dyn + L.fill);  // keys placed per bin
   const int h = blockIdx.x, tid = threadIdx.x;
   TkRow &r = rows[h];
   int above_n;
-  const int thr = tk_threshold(hist + (int64_t)h * kCosBins, k, &above_n);
+  const int thr = tk_threshold_block<kTopkThreads>(hist + (int64_t)h * kCosBins, k, &above_n, pos_s, cnt_s);
   const int na = r.above, nc = r.cand;
   const bool fallback = thr < 0 || r.overflow != 0 || na != above_n;
   if (fallback) {
     const float *row = scores + (int64_t)h * n;
     block_topk<kTopkThreads>([&](int64_t i) -> float { return (i >= ex0 && i < ex1) ? -INFINITY : __ldcg(row + i); },
                              n, k, keys, tsm);
+    for (int j = tid; j < k; j += kTopkThreads) idx[(int64_t)j * n_kv + h] = key_index(keys[j]);
   } else {
+    // The keys above the threshold bin, counting-sorted by bin (bins are
+    // monotone in the score, pos_s gives each bin's first output slot), then
+    // ranked inside their bin; the threshold bin's candidates ranked among
+    // themselves fill the last k - na slots.  Keys are unique, so the ranks
+    // give exactly the order (score desc, index asc).
+    for (int b = tid; b < kCosBins; b += kTopkThreads) fill_s[b] = 0;
     for (int i = tid; i < nc; i += kTopkThreads) cbuf[i] = cand[(int64_t)h * kTkCand + i];
-    for (int i = tid; i < na; i += kTopkThreads) keys[i] = above[(int64_t)h * k + i];
     __syncthreads();
+    for (int i = tid; i < na; i += kTopkThreads) {
+      const unsigned long long key = above[(int64_t)h * k + i];
+      const int b = cos_bin(key_float((uint32_t)(key >> 32)));
+      keys[pos_s[b] + atomicAdd(&fill_s[b], 1)] = key;
+    }
+    __syncthreads();
+    for (int i = tid; i < na; i += kTopkThreads) {
+      const unsigned long long key = keys[i];
+      const int b = cos_bin(key_float((uint32_t)(key >> 32)));
+      const int g0 = pos_s[b], g1 = g0 + cnt_s[b];
+      int rk = 0;
+      for (int j = g0; j < g1; ++j) rk += keys[j] > key ? 1 : 0;
+      idx[(int64_t)(g0 + rk) * n_kv + h] = key_index(key);
+    }
     const int need = k - na;
-    block_topk_keys<kTopkThreads>([&](int64_t i) -> unsigned long long { return cbuf[i]; }, nc, need, cand_s, tsm);
-    for (int j = tid; j < need; j += kTopkThreads) keys[na + j] = cand_s[j];
-    for (int j = k + tid; j < P; j += kTopkThreads) keys[j] = 0ull;
-    __syncthreads();
-    for (int size = 2; size <= P; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = tid; i < P / 2; i += kTopkThreads) {
-          const int a = 2 * i - (i & (stride - 1));
-          const int b = a + stride;
-          const bool desc = ((a & size) == 0);
-          const unsigned long long x = keys[a], y = keys[b];
-          if ((x < y) == desc) {
-            keys[a] = y;
-            keys[b] = x;
-          }
-        }
-        __syncthreads();
-      }
+    const unsigned long long *pool = cbuf;
+    int np = nc;
+    if (nc > kTopkThreads) {
+      // many ties in one bin: exact top `need` of the candidates first
+      block_topk_keys<kTopkThreads>([&](int64_t i) -> unsigned long long { return cbuf[i]; }, nc, need, cand_s, tsm);
+      pool = cand_s;
+      np = need;
+    }
+    for (int i = tid; i < np; i += kTopkThreads) {
+      const unsigned long long key = pool[i];
+      int rk = 0;
+      for (int j = 0; j < np; ++j) rk += pool[j] > key ? 1 : 0;
+      if (rk < need) idx[(int64_t)(na + rk) * n_kv + h] = key_index(key);
     }
   }
-  for (int j = tid; j < k; j += kTopkThreads) idx[(int64_t)j * n_kv + h] = key_index(keys[j]);
   // leave the head's histogram and counters zeroed for the next call
   __syncthreads();
   for (int b = tid; b < kCosBins; b += kTopkThreads) hist[(int64_t)h * kCosBins + b] = 0;
@@ -1112,11 +1171,10 @@ extern "C" int kvr_int4w_token_topk(const float *q, int n_q, const uint8_t *k_pa
   cudaGetDevice(&dev);
   int P = 1;
   while (P < k) P <<= 1;
-  const size_t fin_smem = align_up(sizeof(TopkSmem), 16) + (size_t)P * 16 + (size_t)kTkCand * 8;
+  const size_t fin_smem = TkFinSmem(P).total;
   if (attr_dev != dev) {
     cudaFuncSetAttribute(token_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    cudaFuncSetAttribute(tk_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)(align_up(sizeof(TopkSmem), 16) + 4096 * 16 + kTkCand * 8));
+    cudaFuncSetAttribute(tk_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TkFinSmem(4096).total);
     attr_dev = dev;
   }
   const int64_t blocks = tiles < 148 * 3 ? tiles : 148 * 3;

@@ -268,3 +268,33 @@ def test_fused_token_topk_vs_scores_then_topk(n, k, ex):
         want, _ = K.topk_rows(sc, k, *ex, transpose_out=True)
         torch.cuda.synchronize()
         assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("n_mid,n_top", [(3000, 300), (800, 900), (6000, 0)])
+def test_fused_token_topk_with_duplicated_rows(n_mid, n_top):
+    """Many equal scores: with position-free RoPE tables (cos 1, sin 0) copies
+    of one packed row score the same, so one histogram bin can hold hundreds
+    of keys above the threshold (n_top copies of the best row) or thousands
+    of candidates at it (n_mid copies of the row ranked 500th; 6000 copies
+    overflow the candidate list and take the whole-row select).  The order is
+    still index for index that of kvr_topk_rows (score desc, index asc)."""
+    from kvr_b200 import kernels as K
+    n, k = 16384, 1024
+    st, cos, sin, q = _store(23, n)
+    cos, sin = np.ones_like(cos), np.zeros_like(sin)
+    kp, ks, ct, sn, qt = t(st["k_packed"]), t(st["k_scales"]), t(cos), t(sin), t(q)
+    sc = K.int4w_token_scores(qt, kp, ks, ct, sn, n, True)
+    order = torch.argsort(sc[0], descending=True).cpu().numpy()
+    rng = np.random.default_rng(5)
+    pos = rng.permutation(n)
+    kp_np = st["k_packed"].copy()
+    kp_np[pos[:n_mid]] = kp_np[order[500]]
+    if n_top:
+        kp_np[pos[n_mid:n_mid + n_top]] = kp_np[order[0]]
+    kp = t(kp_np)
+    for _ in range(2):
+        got = K.int4w_token_topk(qt, kp, ks, ct, sn, n, k, True, 0, 0)
+        sc = K.int4w_token_scores(qt, kp, ks, ct, sn, n, True)
+        want, _ = K.topk_rows(sc, k, 0, 0, transpose_out=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
