@@ -82,12 +82,12 @@ def test_kernel_constants_match_spec():
     """The DCT constants baked into the CUDA sources equal the spec's."""
     src = open(os.path.join(ROOT, "rina-1bit-kv_b200", "csrc", "kvr_lee_table.h")).read()
     words = [int(w, 16) for w in re.findall(r"0x([0-9a-f]{8})u", src)]
-    c0, c1, table = words[0], words[1], words[2:]
+    c0, c1, table, table_global = words[0], words[1], words[2:129], words[129:]
     f = S.lee_factors()
     flat = np.zeros(127, F32)
     for M, vals in f.items():
         flat[M // 2 - 1: M - 1] = vals
-    assert table == flat.view(np.uint32).tolist()
+    assert table == flat.view(np.uint32).tolist() and table_global == table
     cc0, cc1 = S.dct_consts()
     assert c0 == np.array([cc0]).view(np.uint32)[0] and c1 == np.array([cc1]).view(np.uint32)[0]
     tsrc = open(os.path.join(ROOT, "rina-1bit-kv_b200", "csrc", "kvr_transform.cuh")).read()
