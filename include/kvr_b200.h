@@ -158,8 +158,10 @@ KVR_API int kvr_int4w_gather(const uint8_t *k_packed, const float *k_scales, con
  * t = top[i, h], contracting over all n_kv*d channels of token t straight from
  * its packed int4 codes.  w3/unscale/bias come from kvr_int4w_vpredict_prepare
  * (once per calibration): W' = W * diag(step) split into fp16 hi + lo parts
- * with a power-of-two scale per output row (fp32-level accuracy).
- * count (optional, device int32): only rows i < *count are written.  d = 128. */
+ * with a power-of-two scale per output row (fp32-level accuracy), stored in
+ * the kernel's tensor-core operand layout (opaque to callers).
+ * count (optional, device int32): only rows i < *count are written.  d = 128,
+ * n_kv <= 8; k_packed, w3, vr_packed and ret_v 16-byte aligned. */
 KVR_API size_t kvr_int4w_vpredict_weights_bytes(int n_kv, int d);
 KVR_API int kvr_int4w_vpredict_prepare(const float *W /* (n_kv*d, n_kv*d) */, const float *k_mean,
                                        const float *v_mean, const float *k_scales, int n_kv, int d, void *w3,
@@ -169,6 +171,9 @@ KVR_API int kvr_int4w_vpredict(const uint8_t *k_packed, const int64_t *top, cons
                                int d, const void *w3, const float *unscale, const float *bias,
                                const uint8_t *vr_packed, const float *vr_scales, uint16_t *ret_v /* fp16 */,
                                kvr_stream_t stream);
+/* Synchronises `stream`, then reads and clears the V-predict kernel's error
+ * word: KVR_ETIMEOUT if a bounded device-side wait gave up since the last call. */
+KVR_API int kvr_int4w_vpredict_status(kvr_stream_t stream);
 
 /* Attractor branch of retrieve_topk (kvr_retrieval.py:248-263, 332-367)
  * with no host sync: head-0 group-mean query vs the centroids (n_attractors,

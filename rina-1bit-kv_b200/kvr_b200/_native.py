@@ -86,6 +86,7 @@ SIGNATURES = {
     "kvr_sd1_prefill_scores": (I, [P, I, I64, I, I, P, P, I64, I64, I, I, P, P, SZ, P]),
     "kvr_kmeans_workspace_bytes": (SZ, [I64, I]),
     "kvr_kmeans": (I, [P, I64, I, I, I, P, P, P, SZ, P]),
+    "kvr_int4w_vpredict_status": (I, [P]),
     "kvr_workspace_status": (I, [P, P]),
     "kvr_selftest_bounded_wait": (I, [P, C.c_uint32, P]),
     "kvr_decode_attn_noalloc_max_scratch_bytes": (SZ, []),

@@ -142,8 +142,9 @@ def int4w_gather(k_packed, k_scales, top, cos, sin, k_mean=None, want_x=True, co
 
 
 def int4w_vpredict_prepare(W, k_mean, v_mean, k_scales, n_kv):
-    """Once per calibration: (w3 fp16 (n_kv, 2, d, n_kv*d), unscale fp32
-    (n_kv*d), bias fp32 (n_kv*d)) for int4w_vpredict."""
+    """Once per calibration: (w3, unscale fp32 (n_kv*d), bias fp32 (n_kv*d))
+    for int4w_vpredict; w3 holds the fp16 hi/lo parts of W' = W diag(step) in
+    the kernel's tensor-core operand layout (n_kv*2*d*n_kv*d halves)."""
     dev = W.device
     KD = n_kv * D
     w3 = torch.empty(n_kv, 2, D, KD, dtype=torch.float16, device=dev)
@@ -165,6 +166,12 @@ def int4w_vpredict(k_packed, top, prep, vr_packed, vr_scales, count=None, out=No
     call("kvr_int4w_vpredict", ptr(_c(k_packed)), ptr(_c(top)), ptr(count), k, n_kv, D, ptr(w3), ptr(unscale),
          ptr(bias), ptr(_c(vr_packed)), ptr(_c(vr_scales.float().reshape(-1))), ptr(out), stream())
     return out
+
+
+def int4w_vpredict_status():
+    """Raises if a bounded device-side wait of the V-predict kernel gave up
+    since the last check (synchronises the current stream)."""
+    call("kvr_int4w_vpredict_status", stream())
 
 
 def int4w_attractor_select(q, n_kv, k_packed, k_scales, cos, sin, centroids, labels, n_labelled, top_a=48,
