@@ -18,15 +18,17 @@
 // result differs from the reference's fp32 GEMM only by summation order.
 //
 // Work split: a CTA owns 128 selected tokens of one KV head (MMA M = 128)
-// and all 128 output channels (N = 128); the contraction (n_kv * d) advances
-// in chunks of 64.  Roles: warps 0-3 (one thread per token row) copy their
-// packed rows into shared memory once (cp.async), then widen each chunk's
-// codes to fp16 into the A stage and finally run the epilogue from tensor
-// memory; warp 4 streams the W' chunks (hi + lo, 32 KB, laid out by the
-// prepare kernel as the MMA's shared-memory image) with one bulk copy each;
-// warp 5 issues tcgen05.mma (8 per chunk: 4 K-steps x 2 parts).  Operands
-// are K-major, no swizzle: 8-row x 16-byte core matrices, SBO = 128 B between
-// 8-row groups, LBO = 2048 B between 8-element K chunks.  Every wait is
+// and half of its 128 output channels (N = 64: twice the CTAs and half the
+// W' bytes each, since the bytes in flight per SM bound the W' stream); the
+// contraction (n_kv * d) advances in chunks of 64.  Roles: warps 0-7 (two
+// threads per token row) copy their packed rows into shared memory once
+// (cp.async), then widen each chunk's codes to fp16 into the A stage and
+// finally run the epilogue from tensor memory (32 channels each); warp 8
+// streams the W' chunks (hi + lo, 16 KB, laid out by the prepare kernel as
+// the MMA's shared-memory image) with one bulk copy each; warp 9 issues
+// tcgen05.mma (8 per chunk: 4 K-steps x 2 parts).  Operands are K-major, no
+// swizzle: 8-row x 16-byte core matrices, SBO = 128 B between 8-row groups,
+// LBO = (rows / 8) * 128 B between 8-element K chunks.  Every wait is
 // bounded; a timeout sets the error word read by kvr_int4w_vpredict_status,
 // lets copies and MMAs in flight finish and frees the tensor memory.
 #include "kvr_common.cuh"
@@ -37,19 +39,20 @@ namespace vp {
 constexpr int kD = 128;
 constexpr int kK = 64;                          // contraction chunk
 constexpr int kM = 128;                         // tokens per CTA (MMA M)
-constexpr int kN = 128;                         // output channels (MMA N)
-constexpr int kStages = 3;
-constexpr uint32_t kLbo = (kM / 8) * 128;       // 2048 B between 8-element K chunks (128-row operands)
+constexpr int kN = 64;                          // output channels per CTA (MMA N): half a head
+constexpr int kStages = 4;
+constexpr uint32_t kLboA = (kM / 8) * 128;      // 2048 B between 8-element K chunks of A (128 rows)
+constexpr uint32_t kLboB = (kN / 8) * 128;      // 1024 B between 8-element K chunks of B (64 rows)
 constexpr int kABytes = kM * kK * 2;            // 16 KB
-constexpr int kPartBytes = kN * kK * 2;         // 16 KB
+constexpr int kPartBytes = kN * kK * 2;         // 8 KB
 constexpr int kBBytes = 2 * kPartBytes;         // hi + lo
-constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr int kStageBytes = kABytes + kBBytes;  // 32 KB
 constexpr int kRawPitch = 8 * 64 + 16;          // packed row (n_kv <= 8) + 16 B: conflict-free 16-byte reads
 constexpr int kOffRaw = kStages * kStageBytes;
 constexpr int kOffConst = kOffRaw + kM * kRawPitch;  // unscale, bias of the head: 2 x 128 fp32
 constexpr int kOffBar = kOffConst + 2 * kN * 4;
 constexpr int kSmem = kOffBar + 8 * (3 * kStages + 1) + 16;
-constexpr int kThreads = 192;  // warps 0-3 A + epilogue, warp 4 W' copies, warp 5 MMA
+constexpr int kThreads = 320;  // warps 0-7 A + epilogue, warp 8 W' copies, warp 9 MMA
 constexpr uint32_t kTmemCols = kN;
 // kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, N, M.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kN >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
@@ -77,14 +80,16 @@ __device__ __forceinline__ bool vp_wait(uint64_t *bar, unsigned phase, volatile 
 
 // 8 int4 codes (one 32-bit word, even element in each byte's high nibble) ->
 // 8 fp16 values in element order: fp16(1024 + nibble) has the nibble as its
-// mantissa, and subtracting 1032 leaves nibble - 8 exactly.
+// mantissa, and subtracting 1032 leaves nibble - 8 exactly.  Byte q's two
+// nibbles are placed by one byte permute into the low bytes of the halves.
 __device__ __forceinline__ uint4 vp_codes8(uint32_t w) {
-  uint32_t r[4];
+  const uint32_t hi = (w >> 4) & 0x0f0f0f0fu, lo = w & 0x0f0f0f0fu;
   const __half2 off = __halves2half2(__ushort_as_half(0x6408u), __ushort_as_half(0x6408u));  // 1032
+  uint32_t r[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const uint32_t e = (w >> (8 * q + 4)) & 15u, o = (w >> (8 * q)) & 15u;
-    const uint32_t x = 0x64006400u | e | (o << 16);
+    const uint32_t x = (__byte_perm(hi, lo, (uint32_t)(q | ((q + 4) << 8) | (q << 16) | ((q + 4) << 24))) &
+                        0x00ff00ffu) | 0x64006400u;
     const __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&x), off);
     r[q] = *reinterpret_cast<const uint32_t *>(&v);
   }
@@ -105,40 +110,42 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
   float *us_s = reinterpret_cast<float *>(sm + kOffConst);
   float *bs_s = us_s + kN;
-  const int h = blockIdx.y, i0 = blockIdx.x * kM;
+  const int h = blockIdx.y >> 1, ch0 = (blockIdx.y & 1) * kN, i0 = blockIdx.x * kM;
   const int n_valid = count ? min(k, __ldg(count)) : k;
   if (i0 >= n_valid) return;  // uniform: before any allocation or barrier
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nch = n_kv * kD / kK;
   const int row_bytes = n_kv * (kD / 2);
 
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  if (tid == 4 * 32) {
+  if (tid == 8 * 32) {
     *abort_s = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_a[s], 4);  // one arrive per producer warp
+      mbar_init(&full_a[s], 8);  // one arrive per producer warp
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
   }
   if (tid < kN) {
-    us_s[tid] = __ldg(unscale + h * kD + tid);
-    bs_s[tid] = __ldg(bias + h * kD + tid);
+    us_s[tid] = __ldg(unscale + h * kD + ch0 + tid);
+    bs_s[tid] = __ldg(bias + h * kD + ch0 + tid);
   }
-  // warps 0-3: the packed row of token i0 + tid, all heads, into shared memory
-  const int m = tid;
-  const bool row_ok = warp < 4 && i0 + m < n_valid;
+  // warps 0-7: thread (m, hf) = (token row i0 + m, half hf of each chunk's
+  // 32 code bytes); it copies the 16-byte pieces of the packed row (all
+  // heads) that it widens later into shared memory
+  const int m = tid & (kM - 1), hf = (tid >> 7) & 1;
+  const bool row_ok = warp < 8 && i0 + m < n_valid;
   int64_t t = 0;
   unsigned char *raw = sm + kOffRaw + m * kRawPitch;
   if (row_ok) {
     t = __ldg(top + (int64_t)(i0 + m) * n_kv + h);
     const uint8_t *src = kp + t * row_bytes;
-    for (int o = 0; o < row_bytes; o += 16) cp_async16(raw + o, src + o);
+    for (int o = 16 * hf; o < row_bytes; o += 32) cp_async16(raw + o, src + o);
   }
   cp_async_commit();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -146,8 +153,8 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ---- A: chunk c's 64 codes of row m widened to fp16 in the MMA layout
+  if (warp < 8) {
+    // ---- A: half hf of chunk c's 64 codes of row m widened to fp16 in the MMA layout
     cp_async_wait<0>();
     bool stop = false;
     for (int c = 0; c < nch; ++c) {
@@ -160,19 +167,18 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
         stop = true;
         break;
       }
-      const uint4 *src = reinterpret_cast<const uint4 *>(raw + c * (kK / 2));
-      const uint4 w0 = src[0], w1 = src[1];  // rows past the selection: any codes (their output is not stored)
-      const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      unsigned char *As = sm + s * kStageBytes;
+      // rows past the selection: any codes (their output is not stored)
+      const uint4 w4 = *reinterpret_cast<const uint4 *>(raw + c * (kK / 2) + 16 * hf);
+      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+      unsigned char *As = sm + s * kStageBytes + 4 * hf * kLboA + (m >> 3) * 128 + (m & 7) * 16;
 #pragma unroll
-      for (int kc = 0; kc < 8; ++kc)
-        *reinterpret_cast<uint4 *>(As + kc * kLbo + (m >> 3) * 128 + (m & 7) * 16) = vp_codes8(ww[kc]);
+      for (int kc = 0; kc < 4; ++kc) *reinterpret_cast<uint4 *>(As + kc * kLboA) = vp_codes8(ww[kc]);
       // generic-proxy writes -> visible to the tensor core (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&full_a[s])) : "memory");
     }
-    // ---- epilogue: row m of the accumulator (TMEM lane m), 128 channels
+    // ---- epilogue: row m of the accumulator (TMEM lane m), channels ch0 + [32 hf, 32 hf + 32)
     bool ok = !stop && __all_sync(0xffffffffu, vp_wait(done, 0u, abort_s));
     if (!stop && !ok && lane == 0) {
       atomicOr(&g_vp_err, 1u);
@@ -189,9 +195,9 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
       }
       const uint32_t rcw[8] = {rc[0].x, rc[0].y, rc[0].z, rc[0].w, rc[1].x, rc[1].y, rc[1].z, rc[1].w};
 #pragma unroll
-      for (int cb = 0; cb < kN / 32; ++cb) {
+      for (int cb = hf; cb < hf + 1; ++cb) {
         uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cb * 32);
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(cb * 32);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
             "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -211,14 +217,15 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
             for (int u = 0; u < 2; ++u) {
               const int col = cb * 32 + e + u;
               const float pred = __fadd_rn(__fmul_rn(__uint_as_float(r[e + u]), us_s[col]), bs_s[col]);
-              const uint32_t byte = (rcw[col >> 4] >> (8 * ((col >> 2) & 3))) & 0xffu;
-              const int code = (int)((byte >> (6 - 2 * (col & 3))) & 3u) - 2;
+              const int gc = ch0 + col;  // channel of the head
+              const uint32_t byte = (rcw[gc >> 4] >> (8 * ((gc >> 2) & 3))) & 0xffu;
+              const int code = (int)((byte >> (6 - 2 * (gc & 3))) & 3u) - 2;
               v2[u] = __fadd_rn(pred, __fmul_rn((float)code, step));
             }
             const __half2 hv = __floats2half2_rn(v2[0], v2[1]);
             packed[e / 2] = *reinterpret_cast<const uint32_t *>(&hv);
           }
-          uint4 *dst = reinterpret_cast<uint4 *>(out + ((int64_t)(i0 + m) * n_kv + h) * kD + cb * 32);
+          uint4 *dst = reinterpret_cast<uint4 *>(out + ((int64_t)(i0 + m) * n_kv + h) * kD + ch0 + cb * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
@@ -226,13 +233,13 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
       }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---- W' chunks of head h (hi + lo, the MMA's shared-memory image)
     int last[kStages];
 #pragma unroll
     for (int s = 0; s < kStages; ++s) last[s] = -1;
     if (lane == 0) {
-      const unsigned char *wh = w3 + (int64_t)h * nch * kBBytes;
+      const unsigned char *wh = w3 + (int64_t)(2 * h + ch0 / kN) * nch * kBBytes;
       for (int c = 0; c < nch; ++c) {
         const int s = c % kStages;
         if (c >= kStages && !vp_wait(&empty[s], (unsigned)((c / kStages - 1) & 1), abort_s)) {
@@ -269,8 +276,8 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
         for (int ks = 0; ks < kK / 16; ++ks) {
 #pragma unroll
           for (int part = 0; part < 2; ++part) {
-            const uint64_t da = vp_desc(a_base + ks * 2 * kLbo, kLbo, 128);
-            const uint64_t db = vp_desc(b_base + part * kPartBytes + ks * 2 * kLbo, kLbo, 128);
+            const uint64_t da = vp_desc(a_base + ks * 2 * kLboA, kLboA, 128);
+            const uint64_t db = vp_desc(b_base + part * kPartBytes + ks * 2 * kLboB, kLboB, 128);
             const uint32_t acc = (c > 0 || ks > 0 || part > 0) ? 1u : 0u;
             asm volatile(
                 "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
     __syncwarp();
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -304,8 +311,8 @@ __global__ void __launch_bounds__(vp::kThreads, 1) vpredict_kernel(
 // One CTA per output row r: W'[r, j] = W[r, j] * step[j], the row's power-of-two
 // scale, the fp16 hi/lo split and the bias V_mean[r] - sum_j W[r, j] K_mean[j]
 // (accumulated in fp64).  hi/lo are stored as the V-predict kernel's shared-
-// memory image: per (head h, 64-wide chunk c) 32 KB = [part][8-element K
-// chunk kc][channel n 0..127][8 halves].
+// memory image: per (head h, channel half, 64-wide chunk c) 16 KB =
+// [part][8-element K chunk kc][channel n 0..63][8 halves].
 __global__ void __launch_bounds__(256) vpredict_prepare_kernel(const float *__restrict__ W,
                                                                const float *__restrict__ kmean,
                                                                const float *__restrict__ vmean,
@@ -355,7 +362,8 @@ __global__ void __launch_bounds__(256) vpredict_prepare_kernel(const float *__re
     const float x = __fmul_rn(__fmul_rn(__ldg(wr + j), step), sc);
     const __half xh = __float2half_rn(x);
     const int c = j / vp::kK, kc = (j % vp::kK) / 8, el = j % 8;
-    const int64_t base = ((int64_t)(h * nch + c) * 2 * 8 + kc) * (vp::kN * 8) + n * 8 + el;  // part 0
+    const int nh = n / vp::kN, nl = n % vp::kN;
+    const int64_t base = (((int64_t)((h * 2 + nh) * nch + c) * 2 * 8 + kc) * vp::kN + nl) * 8 + el;  // part 0
     w3[base] = xh;
     w3[base + 8 * vp::kN * 8] = __float2half_rn(__fsub_rn(x, __half2float(xh)));  // part 1
   }
@@ -403,7 +411,7 @@ extern "C" int kvr_int4w_vpredict(const uint8_t *k_packed, const int64_t *top, c
     cudaFuncSetAttribute(vpredict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vp::kSmem);
     attr_dev = dev;
   }
-  dim3 grid((unsigned)((k + vp::kM - 1) / vp::kM), (unsigned)n_kv);
+  dim3 grid((unsigned)((k + vp::kM - 1) / vp::kM), (unsigned)(2 * n_kv));
   vpredict_kernel<<<grid, vp::kThreads, vp::kSmem, as_cuda(stream)>>>(
       k_packed, top, count, k, n_kv, reinterpret_cast<const unsigned char *>(w3), unscale, bias, vr_packed,
       vr_scales, reinterpret_cast<__half *>(ret_v));
