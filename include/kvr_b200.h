@@ -311,8 +311,21 @@ KVR_API int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int 
                    int tile, int kind, const int32_t *sel, int k_sel, float scale, void *out, int out_dtype,
                    float *partial_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
-/* kvr_sd1_select followed by kvr_sd1_attend on one stream (sel/qprime live in
- * the workspace; sel_out may be NULL). */
+/* One sd1 decode step: tile selection + attention over window, tail and the
+ * selected tiles (sel/qprime live in the workspace; sel_out may be NULL).
+ * Few rows (batch * n_kv <= 16): one kernel, a thread-block cluster per row
+ * (see kvr_set_sd1_step_path); otherwise kvr_sd1_select followed by
+ * kvr_sd1_attend on one stream. */
+/* Which kernels kvr_sd1_decode_step runs (no reference counterpart; a
+ * tuning and test switch, process-wide): 0 (default) = one kernel per step,
+ * a thread-block cluster per (b, h) row, wherever batch * n_kv <= 16 and the
+ * shapes fit its limits (k_sel <= 32, at most 96 window + tail rows and 1024
+ * tiles per CTA of the cluster); otherwise, and with 1, the selection kernel
+ * followed by the attention kernel.  Both give the same selection; outputs
+ * agree to fp32 rounding (the partials are merged in a different order).
+ * Returns the previous value.  The initial value comes from the environment
+ * variable KVR_SD1_STEP ("split" = 1). */
+KVR_API int kvr_set_sd1_step_path(int path);
 KVR_API size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,
                                int64_t n_win, int64_t n_tail);
 KVR_API int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, int n_kv,

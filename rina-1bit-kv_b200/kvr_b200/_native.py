@@ -69,6 +69,7 @@ SIGNATURES = {
     "kvr_sd1_attend": (I, [P, I, P, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I, I, P, I, F, P, I, P,
                            P, SZ, P]),
     "kvr_sd1_workspace_bytes": (SZ, [I, I, I, I64, I, I, I64, I64]),
+    "kvr_set_sd1_step_path": (I, [I]),
     "kvr_sd1_decode_step": (I, [P, I, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I64, I, I, I, I64, I64,
                                 F, P, I, P, P, SZ, P]),
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),

@@ -6,6 +6,7 @@ All tensors must live on a CUDA device; outputs are allocated here with torch
 """
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -427,9 +428,23 @@ def sd1_attend(store: Sd1Store, q, qprime, sel, win_k=None, win_v=None, n_win=0,
 _STEP_WS: dict = {}
 
 
+@contextlib.contextmanager
+def sd1_step_path(path):
+    """Within the block, kvr_sd1_decode_step runs the one-kernel cluster path
+    where shapes allow ("cluster", the default) or always the selection +
+    attention kernels ("split").  Process-wide; restores the previous value."""
+    fn = N.lib().kvr_set_sd1_step_path  # returns the previous value, not a status
+    prev = fn({"cluster": 0, "split": 1}[path])
+    try:
+        yield
+    finally:
+        fn(prev)
+
+
 def sd1_decode_step(store: Sd1Store, q, k_sel, win_k=None, win_v=None, n_win=0, tail_k=None, tail_v=None,
                     n_tail=0, ex_t0=0, ex_t1=0, scale=None, out=None, sel_out=None, ws=None):
-    """Fused select + attend (two launches).  Returns out (B, n_q, d)."""
+    """Tile selection + attention in one call: one cluster kernel for few rows,
+    else the selection and attention kernels.  Returns out (B, n_q, d)."""
     q = _c(q if q.dim() == 3 else q.unsqueeze(0))
     B, n_q, _ = q.shape
     if out is None:

@@ -6,6 +6,7 @@ trace build of the library (KVR_TRACE_POINT; python -m kvr_b200._build
 
     python rina-1bit-kv_b200/phase_trace.py [--layers 32] [--reps 30]
     python rina-1bit-kv_b200/phase_trace.py --batched   # configs[2] flat tile scan
+    python rina-1bit-kv_b200/phase_trace.py --split     # the two-kernel batch-1 step
 
 A 32-layer step is captured in a CUDA graph as in bench.py and replayed;
 after each replay the stamps of the last layer's two kernels are read back
@@ -135,11 +136,62 @@ def batched_scan(reps):
         print(f"| {name} | {val:.0f} |" if name.endswith("CTAs") else f"| {name} | {val:.2f} |")
 
 
+def cluster_phases(lib, gr, stream, reps, layer_us, layers):
+    """Phases of the one-kernel step (sd1_dsmem_step_kernel, trace kernel id 0
+    of its translation unit): one cluster of C CTAs per KV head; times are
+    from the first CTA start of the last layer."""
+    rd = lib.kvr_debug_trace_dsmem
+    rd.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    rd.restype = ctypes.c_int
+    rows = {}
+    names = {1: "grid dependency wait passed", 2: "q' formed", 3: "store staged + tile scan done",
+             4: "list built + cluster barrier 1", 5: "lists exchanged + rank selection done",
+             6: "tiles attended, warp states ready", 7: "rows pushed + cluster barrier 2"}
+    names1 = {0: "  store staged (scan may start)", 1: "  selection done, tile copies issued (warps 0-3)",
+              2: "  exact rows attended (warps 4-7)", 3: "  selected tiles landed",
+              4: "  selected tiles attended (warp 0)", 5: "  merge: weights formed (merging CTAs)",
+              6: "  merge: rows combined", 7: "  merge: inverse transform + output written"}
+    for _ in range(reps):
+        with torch.cuda.stream(stream):
+            gr.replay()
+        torch.cuda.synchronize()
+        buf = read(rd)
+        blocks = [b for b in range(SLOTS) if buf[b * 8]]
+        t0 = min(stamps(buf, 0, blocks, 0))
+        us = lambda x: (x - t0) / 1e3  # noqa: E731
+
+        def add(name, v):
+            rows.setdefault(name, []).append(v)
+
+        add("CTAs", len(blocks))
+        sms = [buf[(2 * SLOTS + b) * 8] for b in blocks]
+        add("distinct SMs", len(set(sms)))
+        add("first CTA starts", 0.0)
+        add("last CTA starts", us(max(stamps(buf, 0, blocks, 0))))
+        for p, name in names.items():
+            v = stamps(buf, 0, blocks, p)
+            add(f"{name} (first CTA)", us(min(v)))
+            add(f"{name} (last CTA)", us(max(v)))
+        for p, name in names1.items():
+            v = [x for x in stamps(buf, 1, blocks, p) if x >= t0]
+            if v:
+                add(f"{name} (first CTA)", us(min(v)))
+                add(f"{name} (last CTA)", us(max(v)))
+    print(f"graph-replayed step: {layer_us:.2f} us per layer ({layers} layers)\n")
+    print("| phase (last layer of the step, one-kernel cluster step) | us from the layer's first CTA start (median) |")
+    print("|---|---|")
+    for name, vals in rows.items():
+        val = statistics.median(vals)
+        print(f"| {name} | {val:.0f} |" if name in ("CTAs", "distinct SMs") else f"| {name} | {val:.2f} |")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--reps", type=int, default=30)
     ap.add_argument("--batched", action="store_true", help="configs[2] flat tile scan phases instead")
+    ap.add_argument("--split", action="store_true", help="the two-kernel step (select + attend) instead of "
+                    "the one-kernel cluster step")
     args = ap.parse_args()
     if not os.path.exists(TRACE_LIB):
         raise SystemExit(f"{TRACE_LIB} missing: python -m kvr_b200._build --trace (from rina-1bit-kv_b200/)")
@@ -147,6 +199,8 @@ def main():
         batched_scan(args.reps)
         return
     lib = N.lib()
+    if args.split:
+        lib.kvr_set_sd1_step_path(1)
     rd_sel = lib.kvr_debug_trace_sd1
     rd_att = lib.kvr_debug_trace_attn
     for f in (rd_sel, rd_att):
@@ -201,6 +255,9 @@ def main():
     def add(name, v):
         rows.setdefault(name, []).append(v)
 
+    if not args.split:
+        cluster_phases(lib, gr, stream, args.reps, layer_us, args.layers)
+        return
     for _ in range(args.reps):
         with torch.cuda.stream(stream):
             gr.replay()

@@ -235,11 +235,17 @@ def test_decode_step_in_unit_selection_matches_select(nt, k_sel, ex):
     q = t(rng.standard_normal((B, n_kv * g, 128)).astype(F32))
     win = t(rng.standard_normal((B, 70, n_kv, 128)).astype(np.float16))
     sel, _, qp = K().sd1_select(st, q, k_sel, ex_t0=ex[0], ex_t1=ex[1])
-    sel_f = torch.full_like(sel, -7)
-    step = K().sd1_decode_step(st, q, k_sel, win, win, 70, ex_t0=ex[0], ex_t1=ex[1], sel_out=sel_f)
-    assert torch.equal(sel_f, sel)
     want = K().sd1_attend(st, q, qp, sel, win, win, 70)
-    assert torch.equal(step, want)
+    for path in ("split", "cluster"):
+        sel_f = torch.full_like(sel, -7)
+        with K().sd1_step_path(path):
+            step = K().sd1_decode_step(st, q, k_sel, win, win, 70, ex_t0=ex[0], ex_t1=ex[1], sel_out=sel_f)
+        assert torch.equal(sel_f, sel), path
+        if path == "split":
+            assert torch.equal(step, want)
+        else:  # same rows, partials merged in another order
+            err = (step.float() - want.float()).abs().max() / want.float().abs().max()
+            assert err < 1e-5, err
 
 
 def _oracle_attend(q, st, b, h, sel_row, win_k, win_v, nw, tail_k, tail_v, ntl, kind, g):
@@ -271,20 +277,17 @@ def test_attend_vs_oracle(kind, tile, nw, ntl, g, B):
     sel, _, qp = K().sd1_select(st, qt, k_sel)
     out = K().sd1_attend(st, qt, qp, sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
                          out_dtype=torch.float32).cpu().numpy()
-    # decode_step selects the same tiles as select (both variants)
-    sel_f = torch.empty_like(sel)
-    step = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
-                               sel_out=sel_f).cpu().numpy()
-    assert torch.equal(sel_f, sel)
-    assert np.array_equal(step, out)  # default: the select + attend kernels
-    os.environ["KVR_SD1_PATH"] = "fused"  # clustered single-kernel variant
-    try:
-        sel_c = torch.empty_like(sel)
-        fused = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
-                                    sel_out=sel_c).cpu().numpy()
-    finally:
-        del os.environ["KVR_SD1_PATH"]
-    assert torch.equal(sel_c, sel)
+    # decode_step selects the same tiles as select, on both of its paths; the
+    # split path is the select + attend kernels, bit for bit
+    steps = {}
+    for path in ("split", "cluster"):
+        sel_f = torch.empty_like(sel)
+        with K().sd1_step_path(path):
+            steps[path] = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                                              sel_out=sel_f).cpu().numpy()
+        assert torch.equal(sel_f, sel), path
+    assert np.array_equal(steps["split"], out)
+    fused = steps["cluster"]
     s = sel.cpu().numpy()
     for b in range(B):
         for h in range(n_kv):
@@ -450,6 +453,47 @@ def test_full_size_config1_layer_sampled_parity():
     for h in range(n_kv):
         want = S.tile_scores(qp[h], st.kbits[0, h].cpu().numpy().view(np.uint32), st.kscale[0, h].cpu().numpy())
         assert np.array_equal(sel[0, h].cpu().numpy(), S.select_tiles(want, 16))
+
+
+@pytest.mark.parametrize("g,k_sel,nw,ntl,ex", [(4, 16, 512, 0, (0, 0)), (4, 32, 512, 40, (500, 504)),
+                                               (8, 16, 1024, 63, (0, 3)), (2, 8, 256, 1, (0, 0)),
+                                               (1, 1, 96, 0, (0, 0))])
+def test_cluster_step_config1_layer(g, k_sel, nw, ntl, ex):
+    """Config-1 layer (504 tiles of 64 per head, 8 KV heads, DCT, bf16 q):
+    the one-kernel cluster step selects exactly the oracle's tiles and its
+    output matches the split path (select + attend kernels) and the exact
+    softmax over the same rows."""
+    n_kv, tile, T = 8, 64, 504 * 64
+    k, v, q = cfg0(77 + g, T, n_kv=n_kv, n_q=n_kv * g)
+    st = K().Sd1Store(1, n_kv, T // tile, tile, "dct", DEV)
+    K().sd1_encode(st, t(k).to(torch.bfloat16), t(v).to(torch.bfloat16))
+    rng = np.random.default_rng(g)
+    win_k = rng.standard_normal((1, nw, n_kv, 128)).astype(np.float16)
+    win_v = rng.standard_normal((1, nw, n_kv, 128)).astype(np.float16)
+    tail_k = rng.standard_normal((1, tile, n_kv, 128)).astype(np.float16)
+    tail_v = rng.standard_normal((1, tile, n_kv, 128)).astype(np.float16)
+    qb = t(q[None]).to(torch.bfloat16)
+    outs, sels = {}, {}
+    for path in ("split", "cluster"):
+        sels[path] = torch.full((1, n_kv, k_sel), -7, dtype=torch.int32, device=DEV)
+        with K().sd1_step_path(path):
+            outs[path] = K().sd1_decode_step(st, qb, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
+                                             ex_t0=ex[0], ex_t1=ex[1], sel_out=sels[path]).float().cpu().numpy()
+    assert torch.equal(sels["split"], sels["cluster"])
+    qa = S.q_group_mean_f32(qb.float().cpu().numpy()[0], n_kv)
+    qp = S.transform(qa, "dct")
+    s = sels["cluster"].cpu().numpy()
+    for h in range(n_kv):
+        sc = S.tile_scores(qp[h], st.kbits[0, h].cpu().numpy().view(np.uint32), st.kscale[0, h].cpu().numpy())
+        sc[ex[0]:ex[1]] = -np.inf
+        assert np.array_equal(s[0, h], S.select_tiles(sc, k_sel)), h
+    qf = qb.float().cpu().numpy()
+    for h in range(n_kv):
+        want = _oracle_attend(qf, st, 0, h, s[0, h], win_k, win_v, nw, tail_k, tail_v, ntl, "dct", g)
+        for path in ("split", "cluster"):
+            got = outs[path][0, h * g:(h + 1) * g]
+            err = np.linalg.norm(got - want) / np.linalg.norm(want)
+            assert err < 2e-3, (path, h, err)  # bf16 output: norm-relative, as the batched 16-bit test
 
 
 def test_retrieval_index_sd1_api():
