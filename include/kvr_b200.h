@@ -323,7 +323,8 @@ KVR_API int kvr_sd1_attend(const void *q, int q_dtype, const float *qprime, int 
  * tiles per CTA of the cluster); otherwise, and with 1, the selection kernel
  * followed by the attention kernel.  Both give the same selection; outputs
  * agree to fp32 rounding (the partials are merged in a different order).
- * Returns the previous value.  The initial value comes from the environment
+ * 2 = the one-kernel path with 8-CTA clusters only (its fallback where
+ * 16-CTA clusters cannot be placed).  Returns the previous value.  The initial value comes from the environment
  * variable KVR_SD1_STEP ("split" = 1). */
 KVR_API int kvr_set_sd1_step_path(int path);
 KVR_API size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,

@@ -1439,7 +1439,8 @@ int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, con
                    const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits, const uint16_t *kscale,
                    const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
                    int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
-                   float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl);
+                   float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl,
+                   int force_c);
 }
 
 extern "C" size_t kvr_decode_attn_workspace_bytes(int n_q, int n_kv, int d, int64_t n_tok_total) {
@@ -1592,7 +1593,9 @@ static std::atomic<int> g_sd1_step_path{[] {
   return (e != nullptr && strcmp(e, "split") == 0) ? 1 : 0;
 }()};
 
-extern "C" int kvr_set_sd1_step_path(int path) { return g_sd1_step_path.exchange(path ? 1 : 0); }
+extern "C" int kvr_set_sd1_step_path(int path) {
+  return g_sd1_step_path.exchange(path == 1 || path == 2 ? path : 0);
+}
 
 // decode_step layout: [header | attention partials | tile scores | sel | qprime]
 extern "C" size_t kvr_sd1_workspace_bytes(int batch, int n_q, int n_kv, int64_t n_tiles, int tile, int k_sel,
@@ -1626,11 +1629,12 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
   float *qprime = reinterpret_cast<float *>(p + a_bytes + s_bytes + sel_bytes);
   // Few rows (batch-1 decode): one kernel, a thread-block cluster per row
   // (kvr_dsmem_step.cu).  KVR_SD1_STEP=split keeps the two-kernel path.
-  if (g_sd1_step_path.load(std::memory_order_relaxed) == 0 && (int64_t)batch * n_kv <= 16) {
+  const int path = g_sd1_step_path.load(std::memory_order_relaxed);
+  if (path != 1 && (int64_t)batch * n_kv <= 16) {
     const int rc = sd1_dsmem_step(q, q_dtype, batch, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail,
                                   kbits, kscale, vbits, vscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0, ex_t1,
                                   scale, out, out_dtype, nullptr, sel_out, reinterpret_cast<unsigned *>(p),
-                                  as_cuda(stream), true);
+                                  as_cuda(stream), true, path == 2 ? 8 : 0);
     if (rc != KVR_ENOTSUP) return rc;
   }
   // One unit per attention CTA (batch-1, latency-bound): the selection

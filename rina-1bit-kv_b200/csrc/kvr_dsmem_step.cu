@@ -54,7 +54,8 @@ constexpr int kDsExStride = 272;    // bytes per staged fp16 row (256 + 16: conf
 constexpr int kDsPart = 4 + 2 * kD; // floats per partial row: m, l, pad, pad, o_exact[128], o_tr[128]
 constexpr int kDsStageMaxBytes = 48 * 1024;
 constexpr int kDsMaxExact = 96;     // exact rows per CTA
-constexpr int kDsMaxTpc = 1024;     // tiles per CTA (beyond the staged ones they are read from global)
+constexpr int kDsMaxTpc = 1024;
+     // tiles per CTA (beyond the staged ones they are read from global)
 
 struct DsArgs {
   const void *q;
@@ -138,6 +139,9 @@ __device__ __forceinline__ int count_greater(const unsigned long long *list, int
 #define DS_TRACE(id, point, owner) ((void)0)
 #endif
 
+#define DS_FN __device__ __forceinline__
+DS_FN void ds_dct_fwd(float (&x)[4], int lane, const float *lee) { dct128_fwd_shfl(x, lane, lee); }
+
 // Named barrier of the first 128 threads (warps 0-3: the selection group).
 __device__ __forceinline__ void sel_group_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -149,7 +153,7 @@ __device__ __forceinline__ unsigned long long merge_top32(unsigned long long a, 
 
 // Exact softmax partial of query head hq over the CTA's staged rows [0, n):
 // (m, l) and o (channels 4 lane .. 4 lane + 3), scores q.k * inv_scale.
-__device__ __forceinline__ void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, float &m_out,
+DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, float &m_out,
                                            float &l_out, float (&o)[4], int lane) {
   const float4 *q4 = reinterpret_cast<const float4 *>(qn);
   constexpr int R = kDsMaxExact / 32;
@@ -207,12 +211,12 @@ __device__ __forceinline__ void exact_rows(const unsigned char *ex, int epc, int
 }
 
 // Transformed query head: T q (DCT strided lanes or Hadamard lane*4) * inv_scale.
-__device__ __forceinline__ void head_qprime(const DsArgs &a, int64_t qh, const float *lee, float *dst, int lane) {
+DS_FN void head_qprime(const DsArgs &a, int64_t qh, const float *lee, float *dst, int lane) {
   float x[4];
   if (a.kind == KVR_DCT) {
 #pragma unroll
     for (int s = 0; s < 4; ++s) x[s] = load_q1(a.q, qh + lane + 32 * s, a.q_dt);
-    dct128_fwd_shfl(x, lane, lee);
+    ds_dct_fwd(x, lane, lee);
 #pragma unroll
     for (int s = 0; s < 4; ++s) dst[lane + 32 * s] = x[s] * a.inv_scale;
   } else {
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
     if (blk < 2048) g_kvr_trace[(2 * 2048 + blk) * 8] = smid + 1;
   }
 #endif
-  // ---- 0. stage this CTA's store range and exact rows; V of the range into L2
+  // ---- 0. stage this CTA's store range and exact rows
   const int64_t t0 = (int64_t)my * a.tpc;
   const int n_mine = (int)max((int64_t)0, min(a.n_tiles, t0 + a.tpc) - t0);
   const int n_staged = min(n_mine, a.staged);
@@ -282,13 +286,6 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
       bulk_g2s(region, a.kbits + tix * TILE * 4, (unsigned)n_staged * kTileBits, &bars[0]);
       bulk_g2s(region + a.staged * kTileBits, a.kscale + tix * kD, (unsigned)n_staged * kD * 2, &bars[0]);
     }
-  } else if (tid == 32 && n_mine > 0) {
-    // the one or two tiles this cluster's CTAs will attend come from L2
-    const int64_t tix = row * a.nt_cap + t0;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vbits + tix * TILE * 4),
-                 "r"((unsigned)n_mine * kTileBits) : "memory");
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vscale + tix * kD),
-                 "r"((unsigned)n_mine * kD * 2) : "memory");
   }
   for (int i = tid; i < ex_mine * 32; i += 256) {
     const int j = i >> 5, kv = (i >> 4) & 1, c = i & 15;
@@ -322,7 +319,7 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
         for (int s = 0; s < 4; ++s) x[s] = __fadd_rn(x[s], load_q1(a.q, qb + (int64_t)i * kD + lane + 32 * s, a.q_dt));
 #pragma unroll
       for (int s = 0; s < 4; ++s) x[s] = __fdiv_rn(x[s], (float)g);
-      dct128_fwd_shfl(x, lane, lee);
+      ds_dct_fwd(x, lane, lee);
 #pragma unroll
       for (int s = 0; s < 4; ++s) qp[lane + 32 * s] = x[s];
     } else {
@@ -704,7 +701,9 @@ int ds_plan(DsArgs &a, int C) {
   const int tile_bits = a.tile * 16;
   a.tpc = (int)((a.n_tiles + C - 1) / C);
   const int per_tile = tile_bits + kD * 2;
-  a.staged = min(a.tpc, kDsStageMaxBytes / per_tile);
+  // 16-CTA clusters: two CTAs per SM (this layer's and the next one's);
+  // 8-CTA clusters use half the SMs per layer and may fill an SM alone
+  a.staged = min(a.tpc, (C == 8 ? 2 : 1) * kDsStageMaxBytes / per_tile);
   a.epc = (int)((a.n_win + a.n_tail + C - 1) / C);
   if (a.tpc > kDsMaxTpc || a.epc > kDsMaxExact) return -1;
   size_t o = 576 + 512 + 2 * kDsMaxG * kD * 4;
@@ -731,7 +730,6 @@ int ds_plan(DsArgs &a, int C) {
   a.o_wpart = (int)o;
   o += (size_t)8 * kDsPart * 4 + (size_t)kDsMaxG * (4 + kD) * 4;
   a.smem = (int)align_up(o, 128);
-  if (const char *e = getenv("KVR_DS_MIN_SMEM")) a.smem = std::max(a.smem, atoi(e));
   return a.smem <= 227 * 1024 ? 0 : -1;
 }
 
@@ -789,13 +787,14 @@ int ds_dispatch(DsArgs &a, int batch, cudaStream_t st, bool pdl, bool query_only
 
 // Cluster size usable on this device for this plan (cached per device,
 // tile and C): 16 where a 16-CTA cluster can be placed, else 8, else 0.
-int ds_pick_cluster(DsArgs &a, int batch, cudaStream_t st) {
+int ds_pick_cluster(DsArgs &a, int batch, cudaStream_t st, int force_c) {
   static std::mutex mu;
   static int cache[64][3][2];  // [dev][tile][C16?]: 0 unknown, 1 yes, 2 no
   int dev = 0;
   cudaGetDevice(&dev);
   const int ti = a.tile == 32 ? 0 : a.tile == 64 ? 1 : 2;
   for (int C : {16, 8}) {
+    if (force_c && C != force_c) continue;
     DsArgs t = a;
     if (ds_plan(t, C) != 0) continue;
     if (a.k_sel > 2 * C) continue;
@@ -827,13 +826,15 @@ int ds_pick_cluster(DsArgs &a, int batch, cudaStream_t st) {
 }  // namespace
 
 // Used by kvr_sd1_decode_step: returns KVR_ENOTSUP (without launching) when
-// the shape is outside this path's limits.
+// the shape is outside this path's limits.  force_c = 8 or 16 restricts the
+// cluster size (tests of the 8-CTA fallback), 0 picks it.
 int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, const uint16_t *win_k,
                    const uint16_t *win_v, int64_t win_cap, int64_t n_win, const uint16_t *tail_k,
                    const uint16_t *tail_v, int64_t n_tail, const uint32_t *kbits, const uint16_t *kscale,
                    const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
                    int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
-                   float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl) {
+                   float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl,
+                   int force_c) {
   const int g = n_kv > 0 ? n_q / n_kv : 0;
   if (!(g == 1 || g == 2 || g == 4 || g == 8) || n_q != g * n_kv) return KVR_ENOTSUP;
   if (k_sel < 0 || k_sel > kDsList) return KVR_ENOTSUP;
@@ -854,7 +855,7 @@ int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, con
   a.nt_cap = nt_cap; a.n_tiles = n_tiles; a.tile = tile; a.kind = kind; a.k_sel = k_sel;
   a.ex0 = ex_t0; a.ex1 = ex_t1;
   a.out = out; a.out_dt = out_dtype; a.partial_out = partial_out; a.sel_out = sel_out; a.err = err;
-  const int C = ds_pick_cluster(a, batch, st);
+  const int C = ds_pick_cluster(a, batch, st, force_c);
   if (C == 16) return ds_dispatch<16>(a, batch, st, pdl, false, nullptr);
   if (C == 8) return ds_dispatch<8>(a, batch, st, pdl, false, nullptr);
   return KVR_ENOTSUP;

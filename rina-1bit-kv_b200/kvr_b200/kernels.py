@@ -431,10 +431,11 @@ _STEP_WS: dict = {}
 @contextlib.contextmanager
 def sd1_step_path(path):
     """Within the block, kvr_sd1_decode_step runs the one-kernel cluster path
-    where shapes allow ("cluster", the default) or always the selection +
-    attention kernels ("split").  Process-wide; restores the previous value."""
+    where shapes allow ("cluster", the default; "cluster8": 8-CTA clusters
+    only) or always the selection + attention kernels ("split").
+    Process-wide; restores the previous value."""
     fn = N.lib().kvr_set_sd1_step_path  # returns the previous value, not a status
-    prev = fn({"cluster": 0, "split": 1}[path])
+    prev = fn({"cluster": 0, "split": 1, "cluster8": 2}[path])
     try:
         yield
     finally:

@@ -280,19 +280,19 @@ def test_attend_vs_oracle(kind, tile, nw, ntl, g, B):
     # decode_step selects the same tiles as select, on both of its paths; the
     # split path is the select + attend kernels, bit for bit
     steps = {}
-    for path in ("split", "cluster"):
+    for path in ("split", "cluster", "cluster8"):
         sel_f = torch.empty_like(sel)
         with K().sd1_step_path(path):
             steps[path] = K().sd1_decode_step(st, qt, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
                                               sel_out=sel_f).cpu().numpy()
         assert torch.equal(sel_f, sel), path
     assert np.array_equal(steps["split"], out)
-    fused = steps["cluster"]
     s = sel.cpu().numpy()
     for b in range(B):
         for h in range(n_kv):
             want = _oracle_attend(q, st, b, h, s[b, h], win_k, win_v, nw, tail_k, tail_v, ntl, kind, g)
-            for got in (out[b, h * g:(h + 1) * g], fused[b, h * g:(h + 1) * g]):
+            for got in (out[b, h * g:(h + 1) * g], steps["cluster"][b, h * g:(h + 1) * g],
+                        steps["cluster8"][b, h * g:(h + 1) * g]):
                 err = np.abs(got - want).max() / np.abs(want).max()
                 assert err < 1e-5, (b, h, err)
 
@@ -474,12 +474,12 @@ def test_cluster_step_config1_layer(g, k_sel, nw, ntl, ex):
     tail_v = rng.standard_normal((1, tile, n_kv, 128)).astype(np.float16)
     qb = t(q[None]).to(torch.bfloat16)
     outs, sels = {}, {}
-    for path in ("split", "cluster"):
+    for path in ("split", "cluster", "cluster8"):
         sels[path] = torch.full((1, n_kv, k_sel), -7, dtype=torch.int32, device=DEV)
         with K().sd1_step_path(path):
             outs[path] = K().sd1_decode_step(st, qb, k_sel, t(win_k), t(win_v), nw, t(tail_k), t(tail_v), ntl,
                                              ex_t0=ex[0], ex_t1=ex[1], sel_out=sels[path]).float().cpu().numpy()
-    assert torch.equal(sels["split"], sels["cluster"])
+    assert torch.equal(sels["split"], sels["cluster"]) and torch.equal(sels["split"], sels["cluster8"])
     qa = S.q_group_mean_f32(qb.float().cpu().numpy()[0], n_kv)
     qp = S.transform(qa, "dct")
     s = sels["cluster"].cpu().numpy()
@@ -490,7 +490,7 @@ def test_cluster_step_config1_layer(g, k_sel, nw, ntl, ex):
     qf = qb.float().cpu().numpy()
     for h in range(n_kv):
         want = _oracle_attend(qf, st, 0, h, s[0, h], win_k, win_v, nw, tail_k, tail_v, ntl, "dct", g)
-        for path in ("split", "cluster"):
+        for path in ("split", "cluster", "cluster8"):
             got = outs[path][0, h * g:(h + 1) * g]
             err = np.linalg.norm(got - want) / np.linalg.norm(want)
             assert err < 2e-3, (path, h, err)  # bf16 output: norm-relative, as the batched 16-bit test
