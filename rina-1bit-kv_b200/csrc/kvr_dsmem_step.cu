@@ -140,7 +140,6 @@ __device__ __forceinline__ int count_greater(const unsigned long long *list, int
 #endif
 
 #define DS_FN __device__ __forceinline__
-DS_FN void ds_dct_fwd(float (&x)[4], int lane, const float *lee) { dct128_fwd_shfl(x, lane, lee); }
 
 // Named barrier of the first 128 threads (warps 0-3: the selection group).
 __device__ __forceinline__ void sel_group_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -166,7 +165,7 @@ DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, 
     if (j < n) {
       const uint4 *kr = reinterpret_cast<const uint4 *>(ex + j * kDsExStride);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+#pragma unroll 2
       for (int c = 0; c < 16; ++c) {
         const uint4 w = kr[c];
         const float4 qa = q4[2 * c], qb4 = q4[2 * c + 1];
@@ -207,24 +206,6 @@ DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, 
       o[0] = fmaf(pj, v0.x, o[0]); o[1] = fmaf(pj, v0.y, o[1]);
       o[2] = fmaf(pj, v1.x, o[2]); o[3] = fmaf(pj, v1.y, o[3]);
     }
-  }
-}
-
-// Transformed query head: T q (DCT strided lanes or Hadamard lane*4) * inv_scale.
-DS_FN void head_qprime(const DsArgs &a, int64_t qh, const float *lee, float *dst, int lane) {
-  float x[4];
-  if (a.kind == KVR_DCT) {
-#pragma unroll
-    for (int s = 0; s < 4; ++s) x[s] = load_q1(a.q, qh + lane + 32 * s, a.q_dt);
-    ds_dct_fwd(x, lane, lee);
-#pragma unroll
-    for (int s = 0; s < 4; ++s) dst[lane + 32 * s] = x[s] * a.inv_scale;
-  } else {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) x[r] = load_q1(a.q, qh + lane * 4 + r, a.q_dt);
-    wht128(x, lane);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) dst[lane * 4 + r] = x[r] * a.inv_scale;
   }
 }
 
@@ -307,35 +288,34 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
   KVR_TRACE_POINT(0, 1);
   __syncthreads();  // Lee factors, barrier init
   const int64_t qb = (b * a.n_q + (int64_t)h * g) * kD;
-  // warp 0: group mean (ordered sum) -> q' for the scan; warps 1..7: T q of
-  // heads 0..6 for the tile attention (head 7 later, by the exact group)
-  if (warp == 0) {
-    float x[4];
-    if (a.kind == KVR_DCT) {
+  // task 0 (warp 0): group mean (ordered sum) -> q' for the scan; task 1 + i:
+  // T q of head i for the tile attention (warp 0 also takes head 7 when
+  // g = 8).  One transform call site keeps the kernel's code small (every
+  // layer's launch fetches it again).
+  {
+    const bool dct = a.kind == KVR_DCT;
+    for (int task = warp; task <= g; task += 8) {
+      float x[4];
+      const int64_t src = task == 0 ? qb : qb + (int64_t)(task - 1) * kD;
 #pragma unroll
-      for (int s = 0; s < 4; ++s) x[s] = load_q1(a.q, qb + lane + 32 * s, a.q_dt);
-      for (int i = 1; i < g; ++i)
+      for (int s = 0; s < 4; ++s) x[s] = load_q1(a.q, src + (dct ? lane + 32 * s : lane * 4 + s), a.q_dt);
+      if (task == 0) {
+        for (int i = 1; i < g; ++i)
 #pragma unroll
-        for (int s = 0; s < 4; ++s) x[s] = __fadd_rn(x[s], load_q1(a.q, qb + (int64_t)i * kD + lane + 32 * s, a.q_dt));
+          for (int s = 0; s < 4; ++s)
+            x[s] = __fadd_rn(x[s], load_q1(a.q, qb + (int64_t)i * kD + (dct ? lane + 32 * s : lane * 4 + s), a.q_dt));
 #pragma unroll
-      for (int s = 0; s < 4; ++s) x[s] = __fdiv_rn(x[s], (float)g);
-      ds_dct_fwd(x, lane, lee);
+        for (int s = 0; s < 4; ++s) x[s] = __fdiv_rn(x[s], (float)g);
+      }
+      if (dct) dct128_fwd_shfl(x, lane, lee);
+      else wht128(x, lane);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) qp[lane + 32 * s] = x[s];
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) x[r] = load_q1(a.q, qb + lane * 4 + r, a.q_dt);
-      for (int i = 1; i < g; ++i)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) x[r] = __fadd_rn(x[r], load_q1(a.q, qb + (int64_t)i * kD + lane * 4 + r, a.q_dt));
-#pragma unroll
-      for (int r = 0; r < 4; ++r) x[r] = __fdiv_rn(x[r], (float)g);
-      wht128(x, lane);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) qp[lane * 4 + r] = x[r];
+      for (int s = 0; s < 4; ++s) {
+        const int c = dct ? lane + 32 * s : lane * 4 + s;
+        if (task == 0) qp[c] = x[s];
+        else Qt[(task - 1) * kD + c] = x[s] * a.inv_scale;
+      }
     }
-  } else if (warp - 1 < g) {
-    head_qprime(a, qb + (int64_t)(warp - 1) * kD, lee, Qt + (warp - 1) * kD, lane);
   }
   for (int i = tid; i < g * kD; i += 256) Qn[i] = load_q1(a.q, qb + i, a.q_dt) * a.inv_scale;
   __syncthreads();
@@ -455,9 +435,8 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
     }
     DS_TRACE(1, 1, 0);
   } else {
-    // exact group: T q of head 7 (g = 8), then the exact rows of every head
+    // exact group: the exact rows of every head
     const int wi = warp - 4;
-    if (g == 8 && wi == 0) head_qprime(a, qb + 7 * kD, lee, Qt + 7 * kD, lane);
     for (int hh = wi; hh < g; hh += 4) {
       float m, l, o[4];
       exact_rows(ex, a.epc, ex_mine, Qn + hh * kD, m, l, o, lane);
