@@ -60,6 +60,19 @@ def sd1_bytes(batch, hkv, hq, nt, ksel, win, tile=TILE):
     return select, attend
 
 
+def sd1_maint_bytes(hkv, hq, tile=TILE):
+    """Algorithmic bytes of one layer's per-step store maintenance, averaged
+    over the tile period: q in/out (bf16), new k/v in (bf16), the evicted
+    window slot read and written to the tail, the new slot written (fp16),
+    the pending tail rows attended as exact rows (on average (tile - 1) / 2
+    rows), and 1/tile of one tile encode (tail read, bits + scales written)."""
+    row = hkv * D * 2
+    upd = 2 * hq * D * 2 + 2 * row + 2 * row + 2 * row + 2 * row
+    tail_read = (tile - 1) / 2 * 2 * row
+    enc = (2 * tile * row + 2 * hkv * (tile * D // 8 + 2 * D)) / tile
+    return int(upd + tail_read + enc)
+
+
 def int4w_bytes(n_stored, top_k, win, hkv=HKV, hq=HQ):
     """Algorithmic bytes of one int4w layer-step: every stored token's packed
     K (d/2 B per head), the selected tokens' packed K of all heads (the V
@@ -106,6 +119,22 @@ def clocks_summary(proc, dev_index):
     if not sm:
         return None
     return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def preroll_steps(torch, replay, stream, seconds=1.5):
+    """Untimed replays for about `seconds` (GPU time), queued without a host
+    synchronisation at the end so the timed region follows them with the GPU
+    still busy.  Returns how many ran."""
+    t0 = time.perf_counter()
+    n = 0
+    with torch.cuda.stream(stream):
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(16):
+                replay(n)
+                n += 1
+            if n % 256 == 0:
+                stream.synchronize()
+    return n
 
 
 def measured_peaks():
@@ -188,7 +217,7 @@ def run_headline(args, dist_, peak_hbm):
     st_ev, en_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for li in range(LAYERS):
         k, v = cfg0_kv(torch, dev, g, B, CTX, hkv, torch.bfloat16)
-        st = K.Sd1Store(B, hkv, NT, TILE, KIND, dev)
+        st = K.Sd1Store(B, hkv, NT + 4, TILE, KIND, dev)   # room for tiles encoded during decode
         for r in range(3 if li == 0 else 1):
             st.n_tiles = 0
             torch.cuda._sleep(100000)  # the GPU is busy while the host enqueues: events bracket the kernel
@@ -204,43 +233,85 @@ def run_headline(args, dist_, peak_hbm):
     enc_s = statistics.median(enc_ms) / 1e3
     enc_bytes = B * T_STORED * hkv * (2 * D * 2 + 2 * D // 8) + B * hkv * NT * 2 * 2 * D
 
-    # ---- decode step: all layers, q per layer, CUDA graph
-    qs = torch.randn(LAYERS, B, hq, D, device=dev, generator=g).to(torch.bfloat16)
+    # ---- decode step: all layers, CUDA graphs.  Every step does per layer
+    # what a decode step of the hook does (kvr_hook.py:136-148 with
+    # kvr_generator.py:78-98): RoPE of the new token's q and k at its
+    # position, eviction of the window slot it overwrites into the pending
+    # tail, the window write (one kvr_decode_store_update launch), then tile
+    # selection + attention over window + tail + selected tiles; every TILE-th
+    # step the full tail is encoded into a new tile.  The 64 phases of that
+    # period are 64 graphs; step s replays graph s % TILE.
+    qs = torch.randn(LAYERS, B, hq, D, device=dev, generator=g).to(torch.bfloat16)   # pre-RoPE q
+    knew = torch.randn(LAYERS, hkv, D, device=dev, generator=g).to(torch.bfloat16)   # pre-RoPE k
+    vnew = torch.randn(LAYERS, hkv, D, device=dev, generator=g).to(torch.bfloat16)
+    qrot = torch.empty_like(qs)
     outs = torch.empty_like(qs)
-    need = N.call("kvr_sd1_workspace_bytes", B, hq, hkv, NT, TILE, KSEL, WIN, 0)
+    inv_freq = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    ang = torch.arange(CTX + 256, device=dev, dtype=torch.float32)[:, None] * inv_freq[None]
+    ang = torch.cat([ang, ang], 1)
+    cos_t, sin_t = ang.cos().contiguous(), ang.sin().contiguous()
+    tails = [(torch.zeros(1, TILE, hkv, D, dtype=torch.float16, device=dev),
+              torch.zeros(1, TILE, hkv, D, dtype=torch.float16, device=dev)) for _ in range(LAYERS)]
+    need = max(N.call("kvr_sd1_workspace_bytes", B, hq, hkv, NT + 1, TILE, KSEL, WIN, nt_) for nt_ in (0, TILE))
     ws = torch.zeros(need + 256, dtype=torch.uint8, device=dev)
 
-    def step(q_all, o_all):
+    def step(q_all, o_all, phase=0, maint=True):
+        """One decode step at tail phase `phase` (0 .. TILE-1)."""
         for li in range(LAYERS):
             wk, wv = wins[li]
-            K.sd1_decode_step(stores[li], q_all[li], KSEL, wk, wv, WIN, out=o_all[li], ws=ws)
+            st = stores[li]
+            n_tail = 0
+            if maint:
+                tk, tv = tails[li]
+                K.decode_store_update(q_all[li, 0], knew[li], vnew[li], cos_t, sin_t, CTX + phase, wk[0], wv[0],
+                                      phase % WIN, tk[0], tv[0], phase, True, q_out=qrot[li, 0])
+                n_tail = phase + 1
+                if n_tail == TILE:
+                    K.sd1_encode(st, tk, tv, tile0=NT)
+                    n_tail = 0
+                st.n_tiles = NT + (1 if maint and phase == TILE - 1 else 0)
+                K.sd1_decode_step(st, qrot[li], KSEL, wk, wv, WIN, tails[li][0], tails[li][1], n_tail,
+                                  out=o_all[li], ws=ws)
+                st.n_tiles = NT
+            else:
+                K.sd1_decode_step(st, q_all[li], KSEL, wk, wv, WIN, out=o_all[li], ws=ws)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
-        for _ in range(2):
-            step(qs, outs)
+        for ph in range(TILE):
+            step(qs, outs, ph)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-        step(qs, outs)
+    graphs = []
+    for ph in range(TILE):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream, capture_error_mode="thread_local"):
+            step(qs, outs, ph)
+        graphs.append(gr)
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph.replay()
+        for i in range(max(args.warmup, 1)):
+            graphs[i % TILE].replay()
     torch.cuda.synchronize()
     dist_.barrier()
+    # nvidia-smi samples every 200 ms, far longer than a few timed steps: the
+    # sampler runs through ~1 s of untimed replays that lead straight into
+    # the timed region, so the clocks it reports are those of the loaded GPU
     clk = clocks_sampler() if rank == 0 else None
+    preroll = preroll_steps(torch, lambda i: graphs[i % TILE].replay(), stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
+        for i in range(args.steps):
+            graphs[i % TILE].replay()
         e1.record(stream)
     torch.cuda.synchronize()
     t_ms = dist_.max(e0.elapsed_time(e1))
     dist_.barrier()
     clocks = clocks_summary(clk, torch.cuda.current_device()) if rank == 0 else None
     ms_per_step = t_ms / args.steps
+    n_encodes = sum(1 for i in range(args.steps) if i % TILE == TILE - 1)
+    del graphs
+    # the attention-only step (no store maintenance), for comparison
+    attn_step_ms = graph_time(torch, lambda: step(qs, outs, 0, maint=False), stream, 50)
 
     # ---- which kernels the step ran: one cluster kernel per layer
     # (kvr_dsmem_step.cu) unless KVR_SD1_STEP=split; the split path (selection
@@ -251,7 +322,7 @@ def run_headline(args, dist_, peak_hbm):
     cluster_path = prev == 0
     sel_b, att_b = sd1_bytes(B, hkv, hq, NT, KSEL, WIN)
     with K.sd1_step_path("split"):
-        split_step_ms = graph_time(torch, lambda: step(qs, outs), stream, 50)
+        split_step_ms = graph_time(torch, lambda: step(qs, outs, 0, maint=False), stream, 50)
 
     # ---- the split path's kernels alone: a graph of each kernel's 32 launches
     sels = [K.sd1_select(stores[li], qs[li], KSEL) for li in range(LAYERS)]
@@ -271,9 +342,13 @@ def run_headline(args, dist_, peak_hbm):
     del sels
 
     # ---- end to end through the reference-facing API: every step copies the
-    # step's queries (all layers) from pinned host memory, runs
-    # RetrievalIndex.attend(q, window) layer by layer (eager launches, as a
-    # caller of the drop-in makes them) and reads the outputs back
+    # new token's q, k, v (all layers, pre-RoPE, as the projections give
+    # them) from pinned host memory, then per layer does what KVRHook's decode
+    # step does over the drop-in objects -- kernels.decode_store_update (RoPE,
+    # eviction of the overwritten window slot into the RetrievalIndex tail,
+    # window write), a tail encode when the tail fills, and
+    # RetrievalIndex.attend(q, window) -- as eager launches, and reads the
+    # outputs back
     rets, wbufs = [], []
     for li in range(LAYERS):
         r = RetrievalIndex(hkv, D, top_k=KSEL * TILE, device=dev, codec="sd1", tile=TILE, transform=KIND)
@@ -286,21 +361,38 @@ def run_headline(args, dist_, peak_hbm):
         wb.pos = wb.n = WIN
         rets.append(r)
         wbufs.append(wb)
-    q_host = qs.cpu().pin_memory()
+    qkv_host = [t.cpu().pin_memory() for t in (qs, knew, vnew)]
     o_host = torch.empty(outs.shape, dtype=outs.dtype).pin_memory()
-    q_dev = torch.empty_like(qs)
+    q_dev, k_dev, v_dev = torch.empty_like(qs), torch.empty_like(knew), torch.empty_like(vnew)
     e2e_steps = max(3, min(args.steps, 100))
+
+    def hook_layer(li, pos):
+        r, wb = rets[li], wbufs[li]
+        q_rot = K.decode_store_update(q_dev[li, 0], k_dev[li], v_dev[li], cos_t, sin_t, pos, wb.k, wb.v,
+                                      wb.pos % wb.cap, r.tail_k[0], r.tail_v[0], r.n_tail, True, q_out=qrot[li, 0])
+        r.n_tail += 1
+        if r.n_tail == TILE:
+            K.sd1_encode(r.store, r.tail_k, r.tail_v)
+            r.n_stored += TILE
+            r.n_tail = 0
+        wb.pos += 1
+        r.attend(q_rot, wb, out=outs[li, 0])
+
     with torch.cuda.stream(stream):
         for i in range(e2e_steps + 2):
             if i == 2:
                 e0.record(stream)
-            q_dev.copy_(q_host, non_blocking=True)
+            for hst, dst in zip(qkv_host, (q_dev, k_dev, v_dev)):
+                dst.copy_(hst, non_blocking=True)
             for li in range(LAYERS):
-                rets[li].attend(q_dev[li, 0], wbufs[li], out=outs[li, 0])
+                hook_layer(li, CTX + i)
             o_host.copy_(outs, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = dist_.max(e0.elapsed_time(e1) / e2e_steps)
+    e2e_h2d = sum(t.numel() * t.element_size() for t in qkv_host)
+    for st in stores:
+        st.n_tiles = NT
 
     # ---- tcgen05 prefill tile scoring (secondary): a 4096-query chunk of
     # prefill positions scored against layer 0's store
@@ -333,16 +425,18 @@ def run_headline(args, dist_, peak_hbm):
     except (OSError, KeyError, ValueError):
         tj = {}
     layer_bytes = sel_b + att_b
+    maint_b = sd1_maint_bytes(hkv, hq)
     if cluster_path:
-        # one launch per layer: the kernel's time is the step's time per layer
-        dom, dom_bytes, dom_ms = "dsmem_step", layer_bytes, ms_per_step / LAYERS
+        # one launch per layer: the kernel's time is the attention-only step's
+        # time per layer (a graph of its 32 launches, gaps included)
+        dom, dom_bytes, dom_ms = "dsmem_step", layer_bytes, attn_step_ms / LAYERS
         traffic = tj.get("sd1_dsmem_step_kernel")
     else:
         dom = "select" if ms_sel >= ms_att else "attend"
         dom_bytes, dom_ms = (sel_b, ms_sel) if dom == "select" else (att_b, ms_att)
         traffic = tj.get("sd1_score_kernel" if dom == "select" else "attn_kernel")
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    step_gbs = LAYERS * layer_bytes / (ms_per_step / 1e3) / 1e9
+    step_gbs = LAYERS * (layer_bytes + maint_b) / (ms_per_step / 1e3) / 1e9
     res = {
         "metric": METRIC,
         "value": round(world * 1e3 / ms_per_step, 3),
@@ -360,11 +454,14 @@ def run_headline(args, dist_, peak_hbm):
                    "layers": LAYERS, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
                    "window": WIN, "tile": TILE, "top_k_tiles": KSEL, "transform": KIND,
                    "batch_per_rank": B, "parallelism": f"one sequence per rank x{world} (weak)",
-                   "l2": "inputs larger than L2 (~395 MB of stores+windows per step)", "launch": "cuda_graph"},
+                   "l2": "inputs larger than L2 (~395 MB of stores+windows per step)", "launch": "cuda_graph",
+                   "step": "per layer: store update (RoPE, eviction, window write) + selection + attention; "
+                           "tail encode every 64 steps"},
         "hbm_gbs": round(step_gbs * world, 1),
-        "roofline_step": {"bound": "hbm", "what": "whole decode step (32 x (select + attend)), per GPU",
+        "roofline_step": {"bound": "hbm", "what": "whole decode step (32 x (store update + select + attend), tail encode every 64 steps), per GPU",
                           "achieved": round(step_gbs, 1), "peak": peak_hbm, "unit": "GB/s",
-                          "frac": round(step_gbs / peak_hbm, 4), "bytes_per_step": LAYERS * layer_bytes},
+                          "frac": round(step_gbs / peak_hbm, 4), "bytes_per_step": LAYERS * (layer_bytes + maint_b),
+                          "maintenance_bytes_per_layer": maint_b},
         "encode": {"layer_tokens_per_s": round(B * T_STORED / enc_s * world, 1),
                    "prefill_tokens_per_s": round(B * T_STORED / enc_s * world / LAYERS, 1),
                    "hbm_gbs": round(enc_bytes / enc_s / 1e9, 1), "ms_per_layer": round(enc_s * 1e3, 4),
@@ -373,18 +470,22 @@ def run_headline(args, dist_, peak_hbm):
                      "unit": "GB/s", "frac": round(achieved / peak_hbm, 4), "traffic": traffic,
                      "traffic_source": "profiles/traffic_config1.json (ncu)",
                      "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5),
-                     "timing": "CUDA events around a graph of the kernel's 32 launches (one per layer)",
+                     "timing": "CUDA events around a graph of the kernel's 32 launches (one per layer, no store "
+                               "maintenance)",
+                     "attention_only_step_ms": round(attn_step_ms, 5),
                      "split_path": {"step_ms": round(split_step_ms, 5), "select_ms": round(ms_sel, 5),
                                     "attend_ms": round(ms_att, 5), "select_bytes": sel_b,
                                     "attend_bytes": att_b}},
         "e2e": {"value": round(world * 1e3 / e2e_ms, 3), "unit": UNIT,
-                "h2d_bytes_per_step": q_host.numel() * q_host.element_size(),
+                "h2d_bytes_per_step": e2e_h2d,
                 "d2h_bytes_per_step": o_host.numel() * o_host.element_size(),
-                "path": "per step: q of all layers H2D from pinned memory, RetrievalIndex.attend(q, window) per "
-                        "layer (kvr_b200, codec='sd1', eager launches), outputs D2H"},
+                "path": "per step: new-token q/k/v of all layers H2D from pinned memory; per layer "
+                        "kernels.decode_store_update (RoPE, eviction into the tail, window write), tail encode "
+                        "every 64 steps, RetrievalIndex.attend(q, window) (codec='sd1', eager launches); outputs D2H"},
         "prefill_scores": prefill,
-        "gpu_launches": args.steps * LAYERS * (1 if cluster_path else 2),
+        "gpu_launches": args.steps * LAYERS * (2 if cluster_path else 3) + n_encodes * LAYERS,
         "clocks": clocks,
+        "clock_preroll_steps": preroll,
     }
     del stores, wins
     torch.cuda.empty_cache()

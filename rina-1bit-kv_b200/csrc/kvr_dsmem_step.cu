@@ -9,10 +9,11 @@
 //
 //  0. before the grid dependency wait (overlapping the previous kernel):
 //     CTA r bulk-copies its range of the row's tiles (K bits + K scales, one
-//     contiguous copy each) and cp.async-stages its share of the exact rows
-//     (window ring + pending tail, fp16) into shared memory;
-//  1. q is read; warp 0 forms q' = T(group mean), warps 1..g the per-head
-//     T q_h, the rest the scaled natural q;
+//     contiguous copy each) into shared memory;
+//  1. after the wait, CTA r cp.async-stages its share of the exact rows
+//     (window ring + pending tail, fp16; consumed after the scan) and reads
+//     q; warp 0 forms q' = T(group mean), warps 1..g the per-head T q_h, the
+//     rest the scaled natural q;
 //  2. scan: the CTA's tiles are scored from shared memory with the
 //     selection kernel's arithmetic (sd1_score_tile2: identical scores);
 //     warp 0 keeps the CTA's top-32 keys (score desc, index asc) in a list;
@@ -268,6 +269,16 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
       bulk_g2s(region + a.staged * kTileBits, a.kscale + tix * kD, (unsigned)n_staged * kD * 2, &bars[0]);
     }
   }
+  if (a.kind == KVR_DCT) load_lee(lee);
+
+  // ---- 1. queries and exact rows (the previous kernel may write both: the
+  // per-layer store update writes q, the window slot and the tail).
+  // Everything above reads only the store's tiles: a kernel that lets this
+  // one start early (griddepcontrol.launch_dependents) must not write those
+  // -- in this library the attention kernels and the store update do not.
+  griddep_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
+  // the exact rows are consumed after the scan: their copies overlap it
   for (int i = tid; i < ex_mine * 32; i += 256) {
     const int j = i >> 5, kv = (i >> 4) & 1, c = i & 15;
     const int64_t e = e0 + j;
@@ -277,14 +288,6 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
     cp_async16(ex + (kv * a.epc + j) * kDsExStride + c * 16, src + (int64_t)h * kD + c * 8);
   }
   cp_async_commit();
-  if (a.kind == KVR_DCT) load_lee(lee);
-
-  // ---- 1. queries (written by the previous kernel).  Everything above reads
-  // only the store and the window/tail rows: a kernel that lets this one
-  // start early (griddepcontrol.launch_dependents) must not write those --
-  // in this library only the attention kernels do, and they write neither.
-  griddep_wait();
-  asm volatile("griddepcontrol.launch_dependents;");
   KVR_TRACE_POINT(0, 1);
   __syncthreads();  // Lee factors, barrier init
   const int64_t qb = (b * a.n_q + (int64_t)h * g) * kD;

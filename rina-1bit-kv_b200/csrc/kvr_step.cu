@@ -12,7 +12,15 @@
 //     rotates it back at the same position);
 //   * the window ring write of the new post-RoPE K and V (kvr_window.py:19-25),
 //     in fp16.
-// One CTA; the evicted row is read before the new row overwrites its slot.
+// One thread per 8-channel chunk of a head row (n_q x 16 chunks of q, then
+// n_kv x 16 chunks of k/v), so every thread makes one round trip to memory:
+// its vector loads are issued together.  The thread that owns a window-slot
+// chunk reads the old (evicted) chunk before it writes the new one.
+// Launched as a programmatic dependent: it waits for the previous kernel
+// (griddepcontrol.wait) before touching memory, then lets the next kernel
+// start.  The next kernel may only read, before its own wait, what this
+// kernel does not write: the 1-bit store's tiles (the one-kernel decode step
+// stages those early, and the window rows and q only after its wait).
 // write_kv = 0 only rotates q (the generator's first step, whose token is
 // already in the window from the prefill).
 #include "kvr_common.cuh"
@@ -37,41 +45,110 @@ __device__ __forceinline__ float rope_elem(float x, float partner, bool low_half
   return round_dt<DT>(__fadd_rn(a, b));
 }
 
+constexpr int kChunk = 8;
+
 template <int DT>
-__global__ void __launch_bounds__(256) decode_store_update_kernel(
+__device__ __forceinline__ void load8(const void *base, int64_t i, float (&x)[kChunk]) {
+  if constexpr (DT == KVR_F32) {
+    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
+    const float4 u = p[0], w = p[1];
+    x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+    x[4] = w.x; x[5] = w.y; x[6] = w.z; x[7] = w.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + i);
+    const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint16_t lo = (uint16_t)(wd[j] & 0xffffu), hi = (uint16_t)(wd[j] >> 16);
+      if constexpr (DT == KVR_F16) {
+        x[2 * j] = __half2float(__ushort_as_half(lo));
+        x[2 * j + 1] = __half2float(__ushort_as_half(hi));
+      } else {
+        x[2 * j] = __bfloat162float(__ushort_as_bfloat16(lo));
+        x[2 * j + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+      }
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t bits_dt(float x) {
+  if constexpr (DT == KVR_F16) return __half_as_ushort(__float2half_rn(x));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+template <int DT>
+__device__ __forceinline__ void store8(void *base, int64_t i, const float (&x)[kChunk]) {
+  if constexpr (DT == KVR_F32) {
+    float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(base) + i);
+    p[0] = make_float4(x[0], x[1], x[2], x[3]);
+    p[1] = make_float4(x[4], x[5], x[6], x[7]);
+  } else {
+    uint32_t wd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wd[j] = (uint32_t)bits_dt<DT>(x[2 * j]) | ((uint32_t)bits_dt<DT>(x[2 * j + 1]) << 16);
+    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(base) + i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_f16x8(const float (&x)[kChunk]) {
+  uint32_t wd[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    wd[j] = (uint32_t)bits_dt<KVR_F16>(x[2 * j]) | ((uint32_t)bits_dt<KVR_F16>(x[2 * j + 1]) << 16);
+  return make_uint4(wd[0], wd[1], wd[2], wd[3]);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(128) decode_store_update_kernel(
     const void *__restrict__ q, const void *__restrict__ k, const void *__restrict__ v, int n_q, int n_kv,
     const float *__restrict__ cos_row, const float *__restrict__ sin_row, void *__restrict__ q_out,
     uint16_t *__restrict__ win_k, uint16_t *__restrict__ win_v, int64_t slot, uint16_t *__restrict__ tail_k,
     uint16_t *__restrict__ tail_v, int64_t tail_row, int write_kv) {
-  constexpr int d = 128, h2 = d / 2;
-  const int row_elems = n_kv * d;
-  // 1. eviction: the slot's fp16 K/V rows move to the tail
-  if (tail_k != nullptr) {
-    const uint4 *sk = reinterpret_cast<const uint4 *>(win_k + slot * row_elems);
-    const uint4 *sv = reinterpret_cast<const uint4 *>(win_v + slot * row_elems);
-    uint4 *dk = reinterpret_cast<uint4 *>(tail_k + tail_row * row_elems);
-    uint4 *dv = reinterpret_cast<uint4 *>(tail_v + tail_row * row_elems);
-    for (int i = threadIdx.x; i < row_elems / 8; i += blockDim.x) {
-      dk[i] = sk[i];
-      dv[i] = sv[i];
+  constexpr int d = 128, cpr = d / kChunk;  // 16 chunks per head row
+  griddep_wait();
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool is_q = t < n_q * cpr;
+  if (!is_q && (t >= (n_q + n_kv) * cpr || (!write_kv && tail_k == nullptr))) return;
+  const int u = is_q ? t : t - n_q * cpr;  // chunk index within q or within the k/v row
+  const int head = u / cpr, cc = u % cpr;
+  const int pc = (cc + cpr / 2) % cpr;     // the rotate_half partner chunk
+  const bool lo = cc < cpr / 2;
+  const int64_t off = (int64_t)head * d + cc * kChunk, poff = (int64_t)head * d + pc * kChunk;
+  const void *src = is_q ? q : k;
+  float x[kChunk], p[kChunk], c[kChunk], s[kChunk], vv[kChunk];
+  load8<DT>(src, off, x);
+  load8<DT>(src, poff, p);
+  load8<KVR_F32>(cos_row, cc * kChunk, c);
+  load8<KVR_F32>(sin_row, cc * kChunk, s);
+  uint4 old_k, old_v;
+  const int64_t row_elems = (int64_t)n_kv * d;
+  uint4 *wk = nullptr, *wv = nullptr;
+  if (!is_q) {
+    load8<DT>(v, off, vv);
+    wk = reinterpret_cast<uint4 *>(win_k + slot * row_elems + off);
+    wv = reinterpret_cast<uint4 *>(win_v + slot * row_elems + off);
+    if (tail_k != nullptr) {
+      old_k = *wk;
+      old_v = *wv;
     }
-    __syncthreads();
   }
-  // 2. q: RoPE in the model dtype
-  for (int i = threadIdx.x; i < n_q * d; i += blockDim.x) {
-    const int c = i & (d - 1);
-    const bool lo = c < h2;
-    const float x = load1<DT>(q, i), p = load1<DT>(q, lo ? i + h2 : i - h2);
-    store_elem<DT>(q_out, i, rope_elem<DT>(x, p, lo, __ldg(cos_row + c), __ldg(sin_row + c)));
+  float r[kChunk];
+#pragma unroll
+  for (int e = 0; e < kChunk; ++e) r[e] = rope_elem<DT>(x[e], p[e], lo, c[e], s[e]);
+  if (is_q) {
+    store8<DT>(q_out, off, r);
+    return;
   }
-  // 3. k, v: RoPE'd K and V into the window slot, as fp16
-  for (int i = threadIdx.x; write_kv && i < row_elems; i += blockDim.x) {
-    const int c = i & (d - 1);
-    const bool lo = c < h2;
-    const float x = load1<DT>(k, i), p = load1<DT>(k, lo ? i + h2 : i - h2);
-    const float kr = rope_elem<DT>(x, p, lo, __ldg(cos_row + c), __ldg(sin_row + c));
-    win_k[slot * row_elems + i] = __half_as_ushort(__float2half_rn(kr));
-    win_v[slot * row_elems + i] = __half_as_ushort(__float2half_rn(load1<DT>(v, i)));
+  // eviction: the slot's fp16 K/V chunk moves to the tail, then the new one lands
+  if (tail_k != nullptr) {
+    *reinterpret_cast<uint4 *>(tail_k + tail_row * row_elems + off) = old_k;
+    *reinterpret_cast<uint4 *>(tail_v + tail_row * row_elems + off) = old_v;
+  }
+  if (write_kv) {
+    *wk = pack_f16x8(r);
+    *wv = pack_f16x8(vv);
   }
 }
 
@@ -93,18 +170,30 @@ extern "C" int kvr_decode_store_update(const void *q, const void *k, const void 
   KVR_REQUIRE((tail_k == nullptr) == (tail_v == nullptr) && (tail_k == nullptr || tail_row >= 0),
               "kvr_decode_store_update: bad tail");
   KVR_REQUIRE(((reinterpret_cast<uintptr_t>(win_k) | reinterpret_cast<uintptr_t>(win_v) |
-                reinterpret_cast<uintptr_t>(tail_k) | reinterpret_cast<uintptr_t>(tail_v)) & 15) == 0,
-              "kvr_decode_store_update: window/tail buffers must be 16-byte aligned");
+                reinterpret_cast<uintptr_t>(tail_k) | reinterpret_cast<uintptr_t>(tail_v) |
+                reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(cos_tbl) |
+                reinterpret_cast<uintptr_t>(sin_tbl)) & 15) == 0 && rope_stride % 4 == 0,
+              "kvr_decode_store_update: buffers must be 16-byte aligned (and the table row stride a multiple of 4)");
   const float *cr = cos_tbl + pos * rope_stride, *sr = sin_tbl + pos * rope_stride;
   cudaStream_t st = as_cuda(stream);
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)(((n_q + n_kv) * (d / kChunk) + 127) / 128));
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (dtype == KVR_F32)
-    decode_store_update_kernel<KVR_F32><<<1, 256, 0, st>>>(q, k, v, n_q, n_kv, cr, sr, q_out, win_k, win_v, slot,
-                                                           tail_k, tail_v, tail_row, write_kv);
+    cudaLaunchKernelEx(&cfg, decode_store_update_kernel<KVR_F32>, q, k, v, n_q, n_kv, cr, sr, q_out, win_k,
+                       win_v, slot, tail_k, tail_v, tail_row, write_kv);
   else if (dtype == KVR_F16)
-    decode_store_update_kernel<KVR_F16><<<1, 256, 0, st>>>(q, k, v, n_q, n_kv, cr, sr, q_out, win_k, win_v, slot,
-                                                           tail_k, tail_v, tail_row, write_kv);
+    cudaLaunchKernelEx(&cfg, decode_store_update_kernel<KVR_F16>, q, k, v, n_q, n_kv, cr, sr, q_out, win_k,
+                       win_v, slot, tail_k, tail_v, tail_row, write_kv);
   else
-    decode_store_update_kernel<KVR_BF16><<<1, 256, 0, st>>>(q, k, v, n_q, n_kv, cr, sr, q_out, win_k, win_v, slot,
-                                                            tail_k, tail_v, tail_row, write_kv);
+    cudaLaunchKernelEx(&cfg, decode_store_update_kernel<KVR_BF16>, q, k, v, n_q, n_kv, cr, sr, q_out, win_k,
+                       win_v, slot, tail_k, tail_v, tail_row, write_kv);
   return check_launch("kvr_decode_store_update");
 }

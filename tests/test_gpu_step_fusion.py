@@ -17,19 +17,22 @@ sys.path.insert(0, os.path.join(HERE, "golden"))
 import inputs  # noqa: E402
 
 
+@pytest.mark.parametrize("heads", [(32, 8), (64, 8), (4, 1)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
-def test_rope_and_window_write_bit_exact(dtype):
+def test_rope_and_window_write_bit_exact(dtype, heads):
+    n_q, n_kv = heads
     from kvr_b200 import kernels as K
     from kvr_b200.kvr_retrieval import _apply_rotary
     g = torch.Generator(device="cuda").manual_seed(0)
     cos, sin = inputs.rope_tables(1000, 128, 500000.0)
     cos, sin = cos.cuda(), sin.cuda()
-    q = (torch.randn(32, 128, device="cuda", generator=g) * 3).to(dtype)
-    k = (torch.randn(8, 128, device="cuda", generator=g) * 3).to(dtype)
-    v = torch.randn(8, 128, device="cuda", generator=g).to(dtype)
-    ring_k = torch.randn(16, 8, 128, device="cuda", generator=g).half()
-    ring_v = torch.randn(16, 8, 128, device="cuda", generator=g).half()
-    tail_k = torch.zeros(64, 8, 128, device="cuda", dtype=torch.float16)
+    q = (torch.randn(n_q, 128, device="cuda", generator=g) * 3).to(dtype)
+    k = (torch.randn(n_kv, 128, device="cuda", generator=g) * 3).to(dtype)
+    v = torch.randn(n_kv, 128, device="cuda", generator=g).to(dtype)
+    ring_k = torch.randn(16, n_kv, 128, device="cuda", generator=g).half()
+    ring_v = torch.randn(16, n_kv, 128, device="cuda", generator=g).half()
+    ring_k0, ring_v0 = ring_k.clone(), ring_v.clone()
+    tail_k = torch.zeros(64, n_kv, 128, device="cuda", dtype=torch.float16)
     tail_v = torch.zeros_like(tail_k)
     old_k, old_v = ring_k[5].clone(), ring_v[5].clone()
     pos = 777
@@ -41,6 +44,8 @@ def test_rope_and_window_write_bit_exact(dtype):
     assert torch.equal(ring_v[5], v.to(torch.float16))
     assert torch.equal(tail_k[9], old_k) and torch.equal(tail_v[9], old_v)
     assert int((tail_k.abs().sum(dim=(1, 2)) > 0).sum()) == 1
+    others = [i for i in range(16) if i != 5]
+    assert torch.equal(ring_k[others], ring_k0[others]) and torch.equal(ring_v[others], ring_v0[others])
     # q only (the first decode step)
     before = ring_k.clone()
     q2 = K.decode_store_update(q, k, v, cos, sin, pos + 1, ring_k, ring_v, 6, write_kv=False)
