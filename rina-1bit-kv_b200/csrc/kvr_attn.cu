@@ -777,11 +777,6 @@ __device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
-// bulk prefetch of `bytes` (multiple of 16) at a 16-byte aligned address into L2
-__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // x -> fp16 hi + lo (x = hi + lo to about 22 bits for |x| in fp16 range)
 __device__ __forceinline__ void split_f16(float x0, float x1, uint32_t &hi, uint32_t &lo) {
   const __half2 h = __floats2half2_rn(x0, x1);

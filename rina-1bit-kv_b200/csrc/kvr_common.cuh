@@ -181,6 +181,13 @@ struct RowPrefetch {
   int64_t n[2], batch_stride[2], tok_stride;
 };
 
+// L2 prefetch of `bytes` (a multiple of 16) at a 16-byte aligned address: a
+// hint only, nothing is read into the CTA, so it may run before a grid
+// dependency wait on data the previous kernel still writes.
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---- mbarrier + bulk copy (PTX)

@@ -9,7 +9,8 @@
 //
 //  0. before the grid dependency wait (overlapping the previous kernel):
 //     CTA r bulk-copies its range of the row's tiles (K bits + K scales, one
-//     contiguous copy each) into shared memory;
+//     contiguous copy each) into shared memory as far as the staging buffer
+//     holds them, and prefetches the rest and its exact rows into L2;
 //  1. after the wait, CTA r cp.async-stages its share of the exact rows
 //     (window ring + pending tail, fp16; consumed after the scan) and reads
 //     q; warp 0 forms q' = T(group mean), warps 1..g the per-head T q_h, the
@@ -268,6 +269,21 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
       bulk_g2s(region, a.kbits + tix * TILE * 4, (unsigned)n_staged * kTileBits, &bars[0]);
       bulk_g2s(region + a.staged * kTileBits, a.kscale + tix * kD, (unsigned)n_staged * kD * 2, &bars[0]);
     }
+  }
+  // L2 prefetch of what this CTA later reads from global memory: the tiles
+  // beyond the staging buffer (read by the scan) and its window/tail row
+  // slices (staged after the wait).  Hints only, so they may precede the wait.
+  if (tid == 32 && n_mine > n_staged) {
+    const int64_t tix = row * a.nt_cap + t0 + n_staged;
+    prefetch_l2(a.kbits + tix * TILE * 4, (unsigned)(n_mine - n_staged) * kTileBits);
+    prefetch_l2(a.kscale + tix * kD, (unsigned)(n_mine - n_staged) * kD * 2);
+  }
+  for (int i = tid; i < ex_mine * 2; i += 256) {
+    const int j = i >> 1, kv = i & 1;
+    const int64_t e = e0 + j;
+    const uint16_t *src = e < a.n_win ? (kv ? a.win_v : a.win_k) + (b * a.win_cap + e) * tokw
+                                      : (kv ? a.tail_v : a.tail_k) + (b * TILE + (e - a.n_win)) * tokw;
+    prefetch_l2(src + (int64_t)h * kD, kD * 2);
   }
   if (a.kind == KVR_DCT) load_lee(lee);
 
