@@ -237,9 +237,11 @@ def run_headline(args, dist_, peak_hbm):
     # what a decode step of the hook does (kvr_hook.py:136-148 with
     # kvr_generator.py:78-98): RoPE of the new token's q and k at its
     # position, eviction of the window slot it overwrites into the pending
-    # tail, the window write (one kvr_decode_store_update launch), then tile
-    # selection + attention over window + tail + selected tiles; every TILE-th
-    # step the full tail is encoded into a new tile.  The 64 phases of that
+    # tail, the window write, then tile selection + attention over window +
+    # tail + selected tiles, all in one cluster launch per layer
+    # (kvr_sd1_decode_step_update); every TILE-th step the eviction fills the
+    # tail, which is encoded into a new tile before that step's selection
+    # (store update, encode and step as three launches).  The 64 phases of that
     # period are 64 graphs; step s replays graph s % TILE.
     qs = torch.randn(LAYERS, B, hq, D, device=dev, generator=g).to(torch.bfloat16)   # pre-RoPE q
     knew = torch.randn(LAYERS, hkv, D, device=dev, generator=g).to(torch.bfloat16)   # pre-RoPE k
@@ -261,17 +263,21 @@ def run_headline(args, dist_, peak_hbm):
             wk, wv = wins[li]
             st = stores[li]
             n_tail = 0
-            if maint:
+            if maint and phase < TILE - 1:
+                # one launch: store update fused into the cluster step
+                tk, tv = tails[li]
+                K.sd1_decode_step_update(st, q_all[li, 0], knew[li], vnew[li], cos_t, sin_t, CTX + phase, KSEL, wk,
+                                         wv, WIN, phase % WIN, tk, tv, phase + 1, True, out=o_all[li],
+                                         q_out=qrot[li, 0], ws=ws)
+            elif maint:
+                # the eviction fills the tail: store update, tile encode, then
+                # the step over the grown store
                 tk, tv = tails[li]
                 K.decode_store_update(q_all[li, 0], knew[li], vnew[li], cos_t, sin_t, CTX + phase, wk[0], wv[0],
                                       phase % WIN, tk[0], tv[0], phase, True, q_out=qrot[li, 0])
-                n_tail = phase + 1
-                if n_tail == TILE:
-                    K.sd1_encode(st, tk, tv, tile0=NT)
-                    n_tail = 0
-                st.n_tiles = NT + (1 if maint and phase == TILE - 1 else 0)
-                K.sd1_decode_step(st, qrot[li], KSEL, wk, wv, WIN, tails[li][0], tails[li][1], n_tail,
-                                  out=o_all[li], ws=ws)
+                K.sd1_encode(st, tk, tv, tile0=NT)
+                st.n_tiles = NT + 1
+                K.sd1_decode_step(st, qrot[li], KSEL, wk, wv, WIN, out=o_all[li], ws=ws)
                 st.n_tiles = NT
             else:
                 K.sd1_decode_step(st, q_all[li], KSEL, wk, wv, WIN, out=o_all[li], ws=ws)
@@ -344,11 +350,10 @@ def run_headline(args, dist_, peak_hbm):
     # ---- end to end through the reference-facing API: every step copies the
     # new token's q, k, v (all layers, pre-RoPE, as the projections give
     # them) from pinned host memory, then per layer does what KVRHook's decode
-    # step does over the drop-in objects -- kernels.decode_store_update (RoPE,
-    # eviction of the overwritten window slot into the RetrievalIndex tail,
-    # window write), a tail encode when the tail fills, and
-    # RetrievalIndex.attend(q, window) -- as eager launches, and reads the
-    # outputs back
+    # step does over the drop-in objects -- RetrievalIndex.decode_step (RoPE,
+    # eviction of the overwritten window slot into the index's tail, window
+    # write, selection and attention: one launch, three when the tail fills
+    # and is encoded) -- as eager calls, and reads the outputs back
     rets, wbufs = [], []
     for li in range(LAYERS):
         r = RetrievalIndex(hkv, D, top_k=KSEL * TILE, device=dev, codec="sd1", tile=TILE, transform=KIND)
@@ -367,16 +372,7 @@ def run_headline(args, dist_, peak_hbm):
     e2e_steps = max(3, min(args.steps, 100))
 
     def hook_layer(li, pos):
-        r, wb = rets[li], wbufs[li]
-        q_rot = K.decode_store_update(q_dev[li, 0], k_dev[li], v_dev[li], cos_t, sin_t, pos, wb.k, wb.v,
-                                      wb.pos % wb.cap, r.tail_k[0], r.tail_v[0], r.n_tail, True, q_out=qrot[li, 0])
-        r.n_tail += 1
-        if r.n_tail == TILE:
-            K.sd1_encode(r.store, r.tail_k, r.tail_v)
-            r.n_stored += TILE
-            r.n_tail = 0
-        wb.pos += 1
-        r.attend(q_rot, wb, out=outs[li, 0])
+        rets[li].decode_step(q_dev[li, 0], k_dev[li], v_dev[li], wbufs[li], pos, cos_t, sin_t, out=outs[li, 0])
 
     with torch.cuda.stream(stream):
         for i in range(e2e_steps + 2):
@@ -480,10 +476,11 @@ def run_headline(args, dist_, peak_hbm):
                 "h2d_bytes_per_step": e2e_h2d,
                 "d2h_bytes_per_step": o_host.numel() * o_host.element_size(),
                 "path": "per step: new-token q/k/v of all layers H2D from pinned memory; per layer "
-                        "kernels.decode_store_update (RoPE, eviction into the tail, window write), tail encode "
-                        "every 64 steps, RetrievalIndex.attend(q, window) (codec='sd1', eager launches); outputs D2H"},
+                        "RetrievalIndex.decode_step (RoPE, eviction into the tail, window write, selection, "
+                        "attention; codec='sd1', eager calls; tail encode every 64 steps); outputs D2H"},
         "prefill_scores": prefill,
-        "gpu_launches": args.steps * LAYERS * (2 if cluster_path else 3) + n_encodes * LAYERS,
+        "gpu_launches": (args.steps * LAYERS + n_encodes * LAYERS * 2 if cluster_path
+                         else args.steps * LAYERS * 3 + n_encodes * LAYERS),
         "clocks": clocks,
         "clock_preroll_steps": preroll,
     }

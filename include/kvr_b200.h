@@ -22,7 +22,8 @@
  *                                                         kvr_int4w_vres_add
  *   modules/kvr_retrieval.py:248-263, 332-367 (attractor branch) -> kvr_int4w_attractor_select
  *   modules/kvr_window.py:19-41      (ring append)     -> kvr_window_write
- *   modules/kvr_generator.py:78-98   (RoPE + store update of a decode step) -> kvr_decode_store_update
+ *   modules/kvr_generator.py:78-98   (RoPE + store update of a decode step) -> kvr_decode_store_update,
+ *                                                         kvr_sd1_decode_step_update (fused with the step)
  *   modules/kvr_window.py:43-69, kvr_hook.py:274-282,
  *   modules/kvr_triton.py:42-104     (attention)       -> kvr_decode_attn
  *   (no reference counterpart: the 1-bit sd1 codec)    -> kvr_sd1_*, kvr_transform, kvr_lse_merge
@@ -336,6 +337,28 @@ KVR_API int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_q, 
                         const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
                         int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
                         int32_t *sel_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
+
+/* One batch-1 decode step of a layer with its store update fused in
+ * (modules/kvr_generator.py:78-98 + kvr_hook.py:136-148 + the retrieval and
+ * attention of kvr_hook.py:274-282, with the 1-bit codec): q, k, v are the
+ * new token's PRE-RoPE rows ((n_q | n_kv, 128) of dtype); RoPE at `pos` as
+ * in kvr_decode_store_update; q_out receives the rotated q.  The new K (fp16,
+ * rotated) and V land in window slot `slot`, which must be one of the n_win
+ * rows attended (n_win counts the new row).  With `evict`, the slot's old row
+ * first moves to tail row n_tail - 1 (n_tail counts it; at most `tile`).
+ * Then the step runs as kvr_sd1_decode_step over window, tail and store.  One
+ * cluster kernel where kvr_sd1_decode_step would run one; otherwise
+ * kvr_decode_store_update followed by kvr_sd1_decode_step (same results).
+ * Workspace: kvr_sd1_workspace_bytes(1, n_q, n_kv, n_tiles, tile, k_sel,
+ * n_win, n_tail). */
+KVR_API int kvr_sd1_decode_step_update(const void *q, const void *k, const void *v, int dtype, int n_q, int n_kv,
+                               const float *cos_tbl, const float *sin_tbl, int64_t rope_stride, int64_t pos,
+                               void *q_out, uint16_t *win_k, uint16_t *win_v, int64_t win_cap, int64_t n_win,
+                               int64_t slot, uint16_t *tail_k, uint16_t *tail_v, int64_t n_tail, int evict,
+                               const uint32_t *kbits, const uint16_t *kscale, const uint32_t *vbits,
+                               const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile, int kind,
+                               int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
+                               int32_t *sel_out, void *workspace, size_t workspace_bytes, kvr_stream_t stream);
 
 /* Prefill-sized tile scoring on the tensor cores (tcgen05, kind::f16):
  * q (nq, n_q, d) post-RoPE queries of a prefill block (batch 1); for every

@@ -1435,7 +1435,7 @@ int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, con
                    const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
                    int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
                    float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl,
-                   int force_c);
+                   int force_c, const Sd1StepUpdate *upd = nullptr);
 }
 
 extern "C" size_t kvr_decode_attn_workspace_bytes(int n_q, int n_kv, int d, int64_t n_tok_total) {
@@ -1666,6 +1666,58 @@ extern "C" int kvr_sd1_decode_step(const void *q, int q_dtype, int batch, int n_
                          kbits, kscale, vbits, vscale, nt_cap, tile, kind, sel, k_sel, scale, out, out_dtype, nullptr,
                          workspace, a_bytes, stream, true, self_select ? scores : nullptr, n_tiles, ex_t0, ex_t1,
                          self_select ? sel : nullptr);
+}
+
+// The decode step with the layer's store update fused in (batch 1): one
+// cluster launch rotates q and the new k, builds the new window row in place
+// of the slot's old one, moves the old row to the tail and attends; where the
+// cluster path does not apply, the store-update kernel and the step run back
+// to back, with identical results.
+extern "C" int kvr_sd1_decode_step_update(const void *q, const void *k, const void *v, int dtype, int n_q, int n_kv,
+                                          const float *cos_tbl, const float *sin_tbl, int64_t rope_stride,
+                                          int64_t pos, void *q_out, uint16_t *win_k, uint16_t *win_v,
+                                          int64_t win_cap, int64_t n_win, int64_t slot, uint16_t *tail_k,
+                                          uint16_t *tail_v, int64_t n_tail, int evict, const uint32_t *kbits,
+                                          const uint16_t *kscale, const uint32_t *vbits, const uint16_t *vscale,
+                                          int64_t nt_cap, int64_t n_tiles, int tile, int kind, int k_sel,
+                                          int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
+                                          int32_t *sel_out, void *workspace, size_t workspace_bytes,
+                                          kvr_stream_t stream) {
+  clear_error();
+  KVR_REQUIRE(valid_dtype(dtype) && q && k && v && cos_tbl && sin_tbl && q_out && win_k && win_v,
+              "kvr_sd1_decode_step_update: bad dtype or null pointer");
+  KVR_REQUIRE(n_kv > 0 && n_q > 0 && n_q % n_kv == 0, "kvr_sd1_decode_step_update: bad head counts");
+  KVR_REQUIRE(n_win >= 1 && n_win <= win_cap && slot >= 0 && slot < n_win,
+              "kvr_sd1_decode_step_update: the slot must lie in the window's valid rows");
+  KVR_REQUIRE(pos >= 0 && rope_stride >= kD && rope_stride % 4 == 0, "kvr_sd1_decode_step_update: bad RoPE position");
+  KVR_REQUIRE(!evict || (tail_k && tail_v && n_tail >= 1 && n_tail <= tile),
+              "kvr_sd1_decode_step_update: an eviction needs a tail with room (n_tail counts the evicted row)");
+  KVR_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(cos_tbl) |
+                reinterpret_cast<uintptr_t>(sin_tbl)) & 15) == 0,
+              "kvr_sd1_decode_step_update: q, k, v, q_out and the tables must be 16-byte aligned");
+  const size_t need = kvr_sd1_workspace_bytes(1, n_q, n_kv, n_tiles, tile, k_sel, n_win, n_tail);
+  KVR_REQUIRE(workspace && workspace_bytes >= need, "kvr_sd1_decode_step_update: workspace %zu < %zu bytes",
+              workspace_bytes, need);
+  KVR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+              "kvr_sd1_decode_step_update: workspace must be 256-byte aligned");
+  const float *cr = cos_tbl + pos * rope_stride, *sr = sin_tbl + pos * rope_stride;
+  const int path = g_sd1_step_path.load(std::memory_order_relaxed);
+  if (path != 1 && n_kv <= 16) {
+    const Sd1StepUpdate u{k, v, cr, sr, q_out, slot, evict ? n_tail - 1 : -1};
+    const int rc = sd1_dsmem_step(q, dtype, 1, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail, kbits,
+                                  kscale, vbits, vscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0, ex_t1, scale, out,
+                                  out_dtype, nullptr, sel_out, reinterpret_cast<unsigned *>(workspace),
+                                  as_cuda(stream), true, path == 2 ? 8 : 0, &u);
+    if (rc != KVR_ENOTSUP) return rc;
+  }
+  int rc = kvr_decode_store_update(q, k, v, dtype, n_q, n_kv, kD, cos_tbl, sin_tbl, rope_stride, pos, q_out, win_k,
+                                   win_v, win_cap, slot, evict ? tail_k : nullptr, evict ? tail_v : nullptr,
+                                   evict ? n_tail - 1 : 0, 1, stream);
+  if (rc) return rc;
+  return kvr_sd1_decode_step(q_out, dtype, 1, n_q, n_kv, win_k, win_v, win_cap, n_win, tail_k, tail_v, n_tail, kbits,
+                             kscale, vbits, vscale, nt_cap, n_tiles, tile, kind, k_sel, ex_t0, ex_t1, scale, out,
+                             out_dtype, sel_out, workspace, workspace_bytes, stream);
 }
 
 #ifdef KVR_TRACE

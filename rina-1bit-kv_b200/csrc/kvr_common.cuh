@@ -181,6 +181,93 @@ struct RowPrefetch {
   int64_t n[2], batch_stride[2], tok_stride;
 };
 
+// RoPE with the rotate_half convention in the arithmetic of an eager model
+// in dtype DT (modules/kvr_generator.py:91-94).
+template <int DT>
+__device__ __forceinline__ float round_dt(float x) {
+  if constexpr (DT == KVR_F32) return x;
+  else if constexpr (DT == KVR_F16) return __half2float(__float2half_rn(x));
+  else return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// x * c + rotate_half(x) * s with each op rounded to DT; x_i and its partner
+// x_p (i +/- d/2) are the DT values, c and s the table entries rounded to DT.
+template <int DT>
+__device__ __forceinline__ float rope_elem(float x, float partner, bool low_half, float c, float s) {
+  const float cr = round_dt<DT>(c), sr = round_dt<DT>(s);
+  const float rh = low_half ? -partner : partner;
+  const float a = round_dt<DT>(__fmul_rn(x, cr));
+  const float b = round_dt<DT>(__fmul_rn(rh, sr));
+  return round_dt<DT>(__fadd_rn(a, b));
+}
+
+// Eight consecutive elements of a row in dtype DT, as fp32 (16-byte loads and
+// stores; the address must be 16-byte aligned).
+constexpr int kChunk8 = 8;
+
+template <int DT>
+__device__ __forceinline__ void load8(const void *base, int64_t i, float (&x)[kChunk8]) {
+  if constexpr (DT == KVR_F32) {
+    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
+    const float4 u = p[0], w = p[1];
+    x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+    x[4] = w.x; x[5] = w.y; x[6] = w.z; x[7] = w.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + i);
+    const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint16_t lo = (uint16_t)(wd[j] & 0xffffu), hi = (uint16_t)(wd[j] >> 16);
+      if constexpr (DT == KVR_F16) {
+        x[2 * j] = __half2float(__ushort_as_half(lo));
+        x[2 * j + 1] = __half2float(__ushort_as_half(hi));
+      } else {
+        x[2 * j] = __bfloat162float(__ushort_as_bfloat16(lo));
+        x[2 * j + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+      }
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t bits_dt(float x) {
+  if constexpr (DT == KVR_F16) return __half_as_ushort(__float2half_rn(x));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+template <int DT>
+__device__ __forceinline__ void store8(void *base, int64_t i, const float (&x)[kChunk8]) {
+  if constexpr (DT == KVR_F32) {
+    float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(base) + i);
+    p[0] = make_float4(x[0], x[1], x[2], x[3]);
+    p[1] = make_float4(x[4], x[5], x[6], x[7]);
+  } else {
+    uint32_t wd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wd[j] = (uint32_t)bits_dt<DT>(x[2 * j]) | ((uint32_t)bits_dt<DT>(x[2 * j + 1]) << 16);
+    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(base) + i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_f16x8(const float (&x)[kChunk8]) {
+  uint32_t wd[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    wd[j] = (uint32_t)bits_dt<KVR_F16>(x[2 * j]) | ((uint32_t)bits_dt<KVR_F16>(x[2 * j + 1]) << 16);
+  return make_uint4(wd[0], wd[1], wd[2], wd[3]);
+}
+
+// The per-layer store update fused into the batch-1 decode step (host side):
+// the new token's pre-RoPE k and v rows (n_kv x 128, q's dtype), the RoPE
+// table rows of its position, the window slot it lands in, the tail row the
+// slot's old row moves to (-1: none) and an optional output for rotated q.
+struct Sd1StepUpdate {
+  const void *k_new, *v_new;
+  const float *cos_row, *sin_row;
+  void *q_out;
+  int64_t slot, evict_row;
+};
+
 // L2 prefetch of `bytes` (a multiple of 16) at a 16-byte aligned address: a
 // hint only, nothing is read into the CTA, so it may run before a grid
 // dependency wait on data the previous kernel still writes.

@@ -79,6 +79,15 @@ struct DsArgs {
   float *partial_out;
   int32_t *sel_out;
   unsigned *err;
+  // fused store update (upd != 0, batch 1): q is pre-RoPE; the new token's
+  // pre-RoPE k and v (n_kv x 128, q's dtype) go to window slot `slot`; the
+  // slot's old row becomes tail row `evict_row` (-1: nothing is evicted);
+  // q_out (optional) receives the rotated q
+  int upd;
+  const void *k_new, *v_new;
+  const float *cos_row, *sin_row;
+  void *q_out;
+  int64_t slot, evict_row;
   int tpc, staged, epc;
   // shared-memory plan (bytes, set by the host)
   int o_lists, o_sc, o_region, o_lut, o_p, o_ex, o_tiles, o_wpart, smem;
@@ -113,6 +122,68 @@ __device__ __forceinline__ float load_q1(const void *p, int64_t i, int dt) {
   if (dt == KVR_F32) return load1<KVR_F32>(p, i);
   if (dt == KVR_F16) return load1<KVR_F16>(p, i);
   return load1<KVR_BF16>(p, i);
+}
+
+// q rows of the cluster's g heads into Qn (rotated when the store update is
+// fused; CTA 0 also writes them to q_out).  Every load of a thread is
+// issued before any of them is used: one round trip.
+template <int DT>
+__device__ __forceinline__ void stage_q_rows(const DsArgs &a, int64_t qb, int g, int tid, unsigned my, float *Qn) {
+  constexpr int kMaxPer = kDsMaxG * kD / 256;  // q elements per thread, at most
+  float x[kMaxPer], p[kMaxPer], cs[kMaxPer], sn[kMaxPer];
+  const int n = g * kD;
+#pragma unroll
+  for (int u = 0; u < kMaxPer; ++u) {
+    const int i = tid + 256 * u;
+    if (i < n) {
+      const int c = i & (kD - 1);
+      x[u] = load1<DT>(a.q, qb + i);
+      if (a.upd) {
+        p[u] = load1<DT>(a.q, qb + (c < kD / 2 ? i + kD / 2 : i - kD / 2));
+        cs[u] = __ldg(a.cos_row + c);
+        sn[u] = __ldg(a.sin_row + c);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxPer; ++u) {
+    const int i = tid + 256 * u;
+    if (i < n) {
+      const int c = i & (kD - 1);
+      const float v = a.upd ? rope_elem<DT>(x[u], p[u], c < kD / 2, cs[u], sn[u]) : x[u];
+      Qn[i] = v;
+      if (a.q_out != nullptr && my == 0) store_elem<DT>(a.q_out, qb + i, v);
+    }
+  }
+}
+
+// The new token's window row (head h) from the raw rows staged in shared
+// memory (raw: [k (128 of DT)][v][cos row fp32][sin row fp32], 512 B each):
+// lanes 0-15 rotate 8 K channels each, lanes 16-31 convert 8 V channels; the
+// fp16 chunks go to the staged K / V rows and to the window slot in global
+// memory.
+template <int DT>
+__device__ __forceinline__ void build_new_row(const unsigned char *raw, unsigned char *k_row, unsigned char *v_row,
+                                              uint16_t *g_k, uint16_t *g_v, int lane) {
+  const int kv = lane >> 4, c8 = (lane & 15) * 8;
+  float x[kChunk8];
+  uint4 out;
+  if (kv) {
+    load8<DT>(raw + 512, c8, x);
+    out = pack_f16x8(x);
+  } else {
+    float p[kChunk8], cs[kChunk8], sn[kChunk8], r[kChunk8];
+    load8<DT>(raw, c8, x);
+    load8<DT>(raw, (c8 + kD / 2) % kD, p);
+    load8<KVR_F32>(raw + 1024, c8, cs);
+    load8<KVR_F32>(raw + 1536, c8, sn);
+    const bool lo = c8 < kD / 2;
+#pragma unroll
+    for (int e = 0; e < kChunk8; ++e) r[e] = rope_elem<DT>(x[e], p[e], lo, cs[e], sn[e]);
+    out = pack_f16x8(r);
+  }
+  *reinterpret_cast<uint4 *>((kv ? v_row : k_row) + c8 * 2) = out;
+  *reinterpret_cast<uint4 *>((kv ? g_v : g_k) + c8) = out;
 }
 
 // number of keys > x in a descending list of n keys
@@ -212,7 +283,7 @@ DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, 
 }
 
 template <int TILE, int C>
-__global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
+__global__ void __launch_bounds__(256, 2) sd1_dsmem_step_kernel(DsArgs a) {
   extern __shared__ __align__(128) unsigned char sm[];
   constexpr int TPL = TILE / 32;
   constexpr unsigned kTileBits = TILE * 16;
@@ -295,18 +366,45 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
   griddep_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   // the exact rows are consumed after the scan: their copies overlap it
+  // (fused store update: the slot's row is the new token's, built by the
+  // exact-row warps after the first cluster barrier; the evicted tail row is
+  // read from the slot, and its CTA waits for that copy before the barrier,
+  // so the slot may be overwritten after it)
+  const bool slot_here = a.upd && a.slot >= e0 && a.slot < e0 + ex_mine;
+  const bool evict_here = a.upd && a.evict_row >= 0 && a.n_win + a.evict_row >= e0 &&
+                          a.n_win + a.evict_row < e0 + ex_mine;
+  unsigned char *raw = reinterpret_cast<unsigned char *>(wpart);  // free until the warp fold
+  if (slot_here && tid < 128) {
+    // the new row's raw inputs (k, v of q's dtype; the RoPE table rows)
+    const int part = tid >> 5, c = tid & 31;
+    const int esz = a.q_dt == KVR_F32 ? 4 : 2;
+    const unsigned char *src = part == 0   ? static_cast<const unsigned char *>(a.k_new) + (int64_t)h * kD * esz
+                               : part == 1 ? static_cast<const unsigned char *>(a.v_new) + (int64_t)h * kD * esz
+                               : part == 2 ? reinterpret_cast<const unsigned char *>(a.cos_row)
+                                           : reinterpret_cast<const unsigned char *>(a.sin_row);
+    if (part >= 2 || c * 16 < kD * esz) cp_async16(raw + part * 512 + c * 16, src + c * 16);
+  }
   for (int i = tid; i < ex_mine * 32; i += 256) {
     const int j = i >> 5, kv = (i >> 4) & 1, c = i & 15;
     const int64_t e = e0 + j;
-    const uint16_t *src = e < a.n_win
-                              ? (kv ? a.win_v : a.win_k) + (b * a.win_cap + e) * tokw
+    unsigned char *dst = ex + (kv * a.epc + j) * kDsExStride + c * 16;
+    if (a.upd && e == a.slot) continue;  // built by the exact-row warps
+    const bool evicted = a.upd && e - a.n_win == a.evict_row;
+    const uint16_t *src = e < a.n_win || evicted
+                              ? (kv ? a.win_v : a.win_k) + (b * a.win_cap + (evicted ? a.slot : e)) * tokw
                               : (kv ? a.tail_v : a.tail_k) + (b * TILE + (e - a.n_win)) * tokw;
-    cp_async16(ex + (kv * a.epc + j) * kDsExStride + c * 16, src + (int64_t)h * kD + c * 8);
+    cp_async16(dst, src + (int64_t)h * kD + c * 8);
   }
   cp_async_commit();
   KVR_TRACE_POINT(0, 1);
-  __syncthreads();  // Lee factors, barrier init
   const int64_t qb = (b * a.n_q + (int64_t)h * g) * kD;
+  // the row's g query heads, read (and rotated, when the store update is
+  // fused) once, in one round trip: Qn holds them unscaled until the
+  // transforms below have read them
+  if (a.q_dt == KVR_F32) stage_q_rows<KVR_F32>(a, qb, g, tid, my, Qn);
+  else if (a.q_dt == KVR_F16) stage_q_rows<KVR_F16>(a, qb, g, tid, my, Qn);
+  else stage_q_rows<KVR_BF16>(a, qb, g, tid, my, Qn);
+  __syncthreads();  // q rows, Lee factors, barrier init
   // task 0 (warp 0): group mean (ordered sum) -> q' for the scan; task 1 + i:
   // T q of head i for the tile attention (warp 0 also takes head 7 when
   // g = 8).  One transform call site keeps the kernel's code small (every
@@ -315,14 +413,13 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
     const bool dct = a.kind == KVR_DCT;
     for (int task = warp; task <= g; task += 8) {
       float x[4];
-      const int64_t src = task == 0 ? qb : qb + (int64_t)(task - 1) * kD;
+      const int src = task == 0 ? 0 : (task - 1) * kD;
 #pragma unroll
-      for (int s = 0; s < 4; ++s) x[s] = load_q1(a.q, src + (dct ? lane + 32 * s : lane * 4 + s), a.q_dt);
+      for (int s = 0; s < 4; ++s) x[s] = Qn[src + (dct ? lane + 32 * s : lane * 4 + s)];
       if (task == 0) {
         for (int i = 1; i < g; ++i)
 #pragma unroll
-          for (int s = 0; s < 4; ++s)
-            x[s] = __fadd_rn(x[s], load_q1(a.q, qb + (int64_t)i * kD + (dct ? lane + 32 * s : lane * 4 + s), a.q_dt));
+          for (int s = 0; s < 4; ++s) x[s] = __fadd_rn(x[s], Qn[i * kD + (dct ? lane + 32 * s : lane * 4 + s)]);
 #pragma unroll
         for (int s = 0; s < 4; ++s) x[s] = __fdiv_rn(x[s], (float)g);
       }
@@ -336,7 +433,8 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
       }
     }
   }
-  for (int i = tid; i < g * kD; i += 256) Qn[i] = load_q1(a.q, qb + i, a.q_dt) * a.inv_scale;
+  __syncthreads();  // the transforms have read the unscaled rows
+  for (int i = tid; i < g * kD; i += 256) Qn[i] *= a.inv_scale;
   __syncthreads();
   KVR_TRACE_POINT(0, 2);
 
@@ -397,6 +495,9 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
 
   // ---- 3. global top-k: tree merge of the C lists (level 1 straight from
   // the owners' shared memory); meanwhile warps 4-7 attend the exact rows
+  // the CTA that staged the evicted row (a copy of the slot's old row) has
+  // it before the barrier; after it the slot may be overwritten
+  if (evict_here) cp_async_wait<0>();
   cluster_sync_all();
   KVR_TRACE_POINT(0, 4);
   if (warp < C / 2) {
@@ -454,7 +555,27 @@ __global__ void __launch_bounds__(256) sd1_dsmem_step_kernel(DsArgs a) {
     }
     DS_TRACE(1, 1, 0);
   } else {
-    // exact group: the exact rows of every head
+    // exact group: the exact rows of every head (fused store update: first
+    // the new window row, and the evicted row goes to the tail)
+    if (slot_here) {
+      if (warp == 7) {
+        unsigned char *kr = ex + (a.slot - e0) * kDsExStride, *vr = ex + (a.epc + a.slot - e0) * kDsExStride;
+        // the fused entry point passes writable window and tail buffers
+        uint16_t *gk = const_cast<uint16_t *>(a.win_k) + (b * a.win_cap + a.slot) * tokw + (int64_t)h * kD;
+        uint16_t *gv = const_cast<uint16_t *>(a.win_v) + (b * a.win_cap + a.slot) * tokw + (int64_t)h * kD;
+        if (a.q_dt == KVR_F32) build_new_row<KVR_F32>(raw, kr, vr, gk, gv, lane);
+        else if (a.q_dt == KVR_F16) build_new_row<KVR_F16>(raw, kr, vr, gk, gv, lane);
+        else build_new_row<KVR_BF16>(raw, kr, vr, gk, gv, lane);
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");  // warps 4-7
+    }
+    if (evict_here && warp == 6) {
+      const int kv = lane >> 4, c = lane & 15;
+      const int64_t j = a.n_win + a.evict_row - e0;
+      uint16_t *dst = const_cast<uint16_t *>(kv ? a.tail_v : a.tail_k) + (b * TILE + a.evict_row) * tokw +
+                      (int64_t)h * kD + c * 8;
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(ex + (kv * a.epc + j) * kDsExStride + c * 16);
+    }
     const int wi = warp - 4;
     for (int hh = wi; hh < g; hh += 4) {
       float m, l, o[4];
@@ -832,7 +953,7 @@ int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, con
                    const uint32_t *vbits, const uint16_t *vscale, int64_t nt_cap, int64_t n_tiles, int tile,
                    int kind, int k_sel, int64_t ex_t0, int64_t ex_t1, float scale, void *out, int out_dtype,
                    float *partial_out, int32_t *sel_out, unsigned *err, cudaStream_t st, bool pdl,
-                   int force_c) {
+                   int force_c, const Sd1StepUpdate *upd) {
   const int g = n_kv > 0 ? n_q / n_kv : 0;
   if (!(g == 1 || g == 2 || g == 4 || g == 8) || n_q != g * n_kv) return KVR_ENOTSUP;
   if (k_sel < 0 || k_sel > kDsList) return KVR_ENOTSUP;
@@ -853,6 +974,14 @@ int sd1_dsmem_step(const void *q, int q_dtype, int batch, int n_q, int n_kv, con
   a.nt_cap = nt_cap; a.n_tiles = n_tiles; a.tile = tile; a.kind = kind; a.k_sel = k_sel;
   a.ex0 = ex_t0; a.ex1 = ex_t1;
   a.out = out; a.out_dt = out_dtype; a.partial_out = partial_out; a.sel_out = sel_out; a.err = err;
+  if (upd != nullptr) {
+    if (batch != 1) return KVR_ENOTSUP;
+    a.upd = 1;
+    a.k_new = upd->k_new; a.v_new = upd->v_new; a.cos_row = upd->cos_row; a.sin_row = upd->sin_row;
+    a.q_out = upd->q_out; a.slot = upd->slot; a.evict_row = upd->evict_row;
+  } else {
+    a.slot = a.evict_row = -1;
+  }
   const int C = ds_pick_cluster(a, batch, st, force_c);
   if (C == 16) return ds_dispatch<16>(a, batch, st, pdl, false, nullptr);
   if (C == 8) return ds_dispatch<8>(a, batch, st, pdl, false, nullptr);

@@ -28,84 +28,12 @@
 namespace kvr {
 
 template <int DT>
-__device__ __forceinline__ float round_dt(float x) {
-  if constexpr (DT == KVR_F32) return x;
-  else if constexpr (DT == KVR_F16) return __half2float(__float2half_rn(x));
-  else return __bfloat162float(__float2bfloat16_rn(x));
-}
-
-// x * c + rotate_half(x) * s with each op rounded to DT; x_i and its partner
-// x_p (i +/- d/2) are the DT values, c and s the table entries rounded to DT.
-template <int DT>
-__device__ __forceinline__ float rope_elem(float x, float partner, bool low_half, float c, float s) {
-  const float cr = round_dt<DT>(c), sr = round_dt<DT>(s);
-  const float rh = low_half ? -partner : partner;
-  const float a = round_dt<DT>(__fmul_rn(x, cr));
-  const float b = round_dt<DT>(__fmul_rn(rh, sr));
-  return round_dt<DT>(__fadd_rn(a, b));
-}
-
-constexpr int kChunk = 8;
-
-template <int DT>
-__device__ __forceinline__ void load8(const void *base, int64_t i, float (&x)[kChunk]) {
-  if constexpr (DT == KVR_F32) {
-    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
-    const float4 u = p[0], w = p[1];
-    x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
-    x[4] = w.x; x[5] = w.y; x[6] = w.z; x[7] = w.w;
-  } else {
-    const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + i);
-    const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint16_t lo = (uint16_t)(wd[j] & 0xffffu), hi = (uint16_t)(wd[j] >> 16);
-      if constexpr (DT == KVR_F16) {
-        x[2 * j] = __half2float(__ushort_as_half(lo));
-        x[2 * j + 1] = __half2float(__ushort_as_half(hi));
-      } else {
-        x[2 * j] = __bfloat162float(__ushort_as_bfloat16(lo));
-        x[2 * j + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
-      }
-    }
-  }
-}
-
-template <int DT>
-__device__ __forceinline__ uint16_t bits_dt(float x) {
-  if constexpr (DT == KVR_F16) return __half_as_ushort(__float2half_rn(x));
-  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
-
-template <int DT>
-__device__ __forceinline__ void store8(void *base, int64_t i, const float (&x)[kChunk]) {
-  if constexpr (DT == KVR_F32) {
-    float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(base) + i);
-    p[0] = make_float4(x[0], x[1], x[2], x[3]);
-    p[1] = make_float4(x[4], x[5], x[6], x[7]);
-  } else {
-    uint32_t wd[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) wd[j] = (uint32_t)bits_dt<DT>(x[2 * j]) | ((uint32_t)bits_dt<DT>(x[2 * j + 1]) << 16);
-    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(base) + i) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-  }
-}
-
-__device__ __forceinline__ uint4 pack_f16x8(const float (&x)[kChunk]) {
-  uint32_t wd[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    wd[j] = (uint32_t)bits_dt<KVR_F16>(x[2 * j]) | ((uint32_t)bits_dt<KVR_F16>(x[2 * j + 1]) << 16);
-  return make_uint4(wd[0], wd[1], wd[2], wd[3]);
-}
-
-template <int DT>
 __global__ void __launch_bounds__(128) decode_store_update_kernel(
     const void *__restrict__ q, const void *__restrict__ k, const void *__restrict__ v, int n_q, int n_kv,
     const float *__restrict__ cos_row, const float *__restrict__ sin_row, void *__restrict__ q_out,
     uint16_t *__restrict__ win_k, uint16_t *__restrict__ win_v, int64_t slot, uint16_t *__restrict__ tail_k,
     uint16_t *__restrict__ tail_v, int64_t tail_row, int write_kv) {
-  constexpr int d = 128, cpr = d / kChunk;  // 16 chunks per head row
+  constexpr int d = 128, cpr = d / kChunk8;  // 16 chunks per head row
   griddep_wait();
   asm volatile("griddepcontrol.launch_dependents;");
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -115,13 +43,13 @@ __global__ void __launch_bounds__(128) decode_store_update_kernel(
   const int head = u / cpr, cc = u % cpr;
   const int pc = (cc + cpr / 2) % cpr;     // the rotate_half partner chunk
   const bool lo = cc < cpr / 2;
-  const int64_t off = (int64_t)head * d + cc * kChunk, poff = (int64_t)head * d + pc * kChunk;
+  const int64_t off = (int64_t)head * d + cc * kChunk8, poff = (int64_t)head * d + pc * kChunk8;
   const void *src = is_q ? q : k;
-  float x[kChunk], p[kChunk], c[kChunk], s[kChunk], vv[kChunk];
+  float x[kChunk8], p[kChunk8], c[kChunk8], s[kChunk8], vv[kChunk8];
   load8<DT>(src, off, x);
   load8<DT>(src, poff, p);
-  load8<KVR_F32>(cos_row, cc * kChunk, c);
-  load8<KVR_F32>(sin_row, cc * kChunk, s);
+  load8<KVR_F32>(cos_row, cc * kChunk8, c);
+  load8<KVR_F32>(sin_row, cc * kChunk8, s);
   uint4 old_k, old_v;
   const int64_t row_elems = (int64_t)n_kv * d;
   uint4 *wk = nullptr, *wv = nullptr;
@@ -134,9 +62,9 @@ __global__ void __launch_bounds__(128) decode_store_update_kernel(
       old_v = *wv;
     }
   }
-  float r[kChunk];
+  float r[kChunk8];
 #pragma unroll
-  for (int e = 0; e < kChunk; ++e) r[e] = rope_elem<DT>(x[e], p[e], lo, c[e], s[e]);
+  for (int e = 0; e < kChunk8; ++e) r[e] = rope_elem<DT>(x[e], p[e], lo, c[e], s[e]);
   if (is_q) {
     store8<DT>(q_out, off, r);
     return;
@@ -181,7 +109,7 @@ extern "C" int kvr_decode_store_update(const void *q, const void *k, const void 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3((unsigned)(((n_q + n_kv) * (d / kChunk) + 127) / 128));
+  cfg.gridDim = dim3((unsigned)(((n_q + n_kv) * (d / kChunk8) + 127) / 128));
   cfg.blockDim = dim3(128);
   cfg.stream = st;
   cfg.attrs = attr;

@@ -70,6 +70,8 @@ SIGNATURES = {
                            P, SZ, P]),
     "kvr_sd1_workspace_bytes": (SZ, [I, I, I, I64, I, I, I64, I64]),
     "kvr_set_sd1_step_path": (I, [I]),
+    "kvr_sd1_decode_step_update": (I, [P, P, P, I, I, I, P, P, I64, I64, P, P, P, I64, I64, I64, P, P, I64, I,
+                                       P, P, P, P, I64, I64, I, I, I, I64, I64, F, P, I, P, P, SZ, P]),
     "kvr_sd1_decode_step": (I, [P, I, I, I, I, P, P, I64, I64, P, P, I64, P, P, P, P, I64, I64, I, I, I, I64, I64,
                                 F, P, I, P, P, SZ, P]),
     "kvr_lse_merge": (I, [P, I, I, I, P, I, P]),

@@ -467,6 +467,41 @@ def sd1_decode_step(store: Sd1Store, q, k_sel, win_k=None, win_v=None, n_win=0, 
     return out
 
 
+def sd1_decode_step_update(store: Sd1Store, q, k, v, cos, sin, pos, k_sel, win_k, win_v, n_win, slot,
+                           tail_k=None, tail_v=None, n_tail=0, evict=False, ex_t0=0, ex_t1=0, scale=None,
+                           out=None, q_out=None, sel_out=None, ws=None):
+    """The layer's store update fused with its decode step (batch 1).
+
+    q (n_q, d), k and v (n_kv, d): the new token's pre-RoPE rows, one dtype.
+    The rotated K / V land in window slot `slot` (one of the n_win rows
+    attended, n_win counting the new row); with `evict` the slot's old row
+    first moves to tail row n_tail - 1.  Returns (out (1, n_q, d) of q's
+    dtype, q_out = RoPE(q))."""
+    q, k, v = _c(q), _c(k), _c(v)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k and v must share a dtype")
+    n_q, n_kv = q.shape[0], k.shape[0]
+    cos, sin, rs = _rope_args(cos, sin)
+    if out is None:
+        out = torch.empty(1, n_q, D, dtype=q.dtype, device=q.device)
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    if ws is None:
+        key = (1, n_q, n_kv, store.n_tiles, store.tile, k_sel, n_win, n_tail)
+        need = _STEP_WS.get(key)
+        if need is None:
+            need = _STEP_WS[key] = call("kvr_sd1_workspace_bytes", *key)
+            if len(_STEP_WS) > 4096:
+                _STEP_WS.clear()
+        ws = N.workspace("sd1_step", need, q.device)
+    call("kvr_sd1_decode_step_update", ptr(q), ptr(k), ptr(v), dtype_code(q), n_q, n_kv, ptr(cos), ptr(sin), rs,
+         pos, ptr(q_out), ptr(win_k), ptr(win_v), win_k.shape[-3], n_win, slot, ptr(tail_k), ptr(tail_v), n_tail,
+         int(evict), ptr(store.kbits), ptr(store.kscale), ptr(store.vbits), ptr(store.vscale), store.nt_cap,
+         store.n_tiles, store.tile, N.TRANSFORMS[store.kind], k_sel, ex_t0, ex_t1, float(scale or 0.0), ptr(out),
+         dtype_code(out), ptr(sel_out), ptr(ws), ws.numel(), stream())
+    return out, q_out
+
+
 def sd1_decode_tiles(store: Sd1Store, sel):
     """sel (B, n_kv, k) int64 -> (K (B, k*t, n_kv, d) fp32, V fp16)."""
     sel = _c(sel.long())

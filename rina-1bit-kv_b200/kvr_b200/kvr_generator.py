@@ -6,8 +6,10 @@ Per step and layer (modules/kvr_generator.py:78-126): input norm, q/k/v
 projections, RoPE at the step position, store update (eviction into the
 index), then attention over the window and the retrieved tokens — here one
 call into the B200 kernels (RetrievalIndex.attend) instead of ``torch.cat``
-+ the Triton kernel — then o_proj, residual and MLP.  With ``codec='sd1'`` the
-RoPE, the eviction and the window write are one kernel
++ the Triton kernel — then o_proj, residual and MLP.  With ``codec='sd1'``,
+once the 1-bit index is active, RoPE, eviction, window write, selection and
+attention are one kernel per layer (RetrievalIndex.decode_step); before that
+the RoPE, the eviction and the window write are one kernel
 (kvr_decode_store_update).  Sampling uses the HF logits processors, as the reference
 does (modules/kvr_generator.py:129-154).
 """
@@ -85,16 +87,21 @@ class KVRGenerator:
             q = attn.q_proj(hn).view(self.n_q, self.d_head)
             k_pre = attn.k_proj(hn).view(self.n_kv, self.d_head)
             v = attn.v_proj(hn).view(self.n_kv, self.d_head)
-            if self.fused_store_update and self.kvr.fused_store_update_ok(li):
-                # RoPE + eviction + window write in one kernel (kvr_decode_store_update)
-                q_rot = self.kvr.decode_store_update(li, q, k_pre, v, pos, write_kv=not self._is_first)
-            else:
-                q_rot = _apply_rotary(q, c, s)
-                k_rot = _apply_rotary(k_pre, c, s)
-                if not self._is_first:
-                    self.kvr._update_stores(li, k_pre.to(torch.float16), v.to(torch.float16),
-                                            k_rot.to(torch.float16))
-            out = self.kvr.attend(li, q_rot, out_dtype=q_rot.dtype)
+            out = None
+            if self.fused_store_update and not self._is_first:
+                # store update + selection + attention in one kernel
+                out = self.kvr.decode_step_fused(li, q, k_pre, v, pos)
+            if out is None:
+                if self.fused_store_update and self.kvr.fused_store_update_ok(li):
+                    # RoPE + eviction + window write in one kernel (kvr_decode_store_update)
+                    q_rot = self.kvr.decode_store_update(li, q, k_pre, v, pos, write_kv=not self._is_first)
+                else:
+                    q_rot = _apply_rotary(q, c, s)
+                    k_rot = _apply_rotary(k_pre, c, s)
+                    if not self._is_first:
+                        self.kvr._update_stores(li, k_pre.to(torch.float16), v.to(torch.float16),
+                                                k_rot.to(torch.float16))
+                out = self.kvr.attend(li, q_rot, out_dtype=q_rot.dtype)
             h = h + attn.o_proj(out.reshape(-1).to(h.dtype))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         return self.lm_head(self.final_norm(h)).float()

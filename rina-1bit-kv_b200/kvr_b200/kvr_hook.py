@@ -302,6 +302,22 @@ class KVRHook:
             win.n = min(win.n + 1, win.cap)
         return q_rot
 
+    def decode_step_fused(self, li, q, k_pre, v, pos):
+        """The whole decode step of layer li after the projections in one
+        launch where that applies (sd1 index built and active, eviction at
+        the evicted token's own position): RoPE, eviction into the tail,
+        window write, selection and attention
+        (RetrievalIndex.decode_step).  Returns the (n_q, d) output in q's
+        dtype, or None when the step must take the separate calls."""
+        win, ret = self.windows[li], self.retrievals[li]
+        if (self.codec != "sd1" or self.reference_eviction_rope or not self._retrieval_built or ret.store is None
+                or self._ret_weight <= 0 or ret.n_tokens == 0):
+            return None
+        fills = win.n >= win.cap and ret.n_tail + 1 == ret.tile
+        ex = exclusion_range(self._context_len, min(win.n + 1, win.cap), ret.n_stored + (ret.tile if fills else 0))
+        out, _ = ret.decode_step(q, k_pre, v, win, pos, self.cos_tbl, self.sin_tbl, ex[0], ex[1])
+        return out
+
     # ------------------------------------------------------- attention --
     def attend(self, li, q_post, out_dtype=torch.float32):
         """Window + retrieval attention of one layer for the current step:

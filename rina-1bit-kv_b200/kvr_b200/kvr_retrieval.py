@@ -580,6 +580,52 @@ class RetrievalIndex:
         return torch.cat(parts_k, 0).contiguous(), torch.cat(parts_v, 0).contiguous()
 
     @torch.no_grad()
+    def decode_step(self, q_pre, k_pre, v, window, pos, cos, sin, exclude_start=0, exclude_end=0, out=None):
+        """sd1, batch 1: one layer's decode step with its store update fused in
+        (kvr_generator.py:78-98, kvr_hook.py:136-148 and :274-282 in one
+        call).  q_pre (n_q, d), k_pre and v (n_kv, d): the new token's
+        pre-RoPE rows in the model dtype; RoPE at `pos` from the (max_pos, d)
+        tables cos/sin.  The new K/V take the window's next ring slot; when the
+        window is full the slot's old row first moves to the pending tail.
+        Then window + tail + selected tiles are attended (exclusion range in
+        tokens, as for ``attend``).  One cluster launch; when the eviction
+        fills the tail, the store update, the tile encode and the step run as
+        separate launches so the new tile is in the store before the step, as
+        in the step-by-step path.  Returns (out (n_q, d) of q's dtype, RoPE(q))."""
+        if self.codec != "sd1":
+            raise NotImplementedError("decode_step is the sd1 codec's fused path")
+        if self.store is None:
+            self._sd1_reset()
+        slot = window.pos % window.cap
+        evict = window.n >= window.cap
+        if evict and self.n_tail + 1 == self.tile:
+            q_rot = K.decode_store_update(q_pre, k_pre, v, cos, sin, pos, window.k, window.v, slot, self.tail_k[0],
+                                          self.tail_v[0], self.n_tail, True)
+            self.n_tail += 1
+            st = self.store
+            if st.n_tiles + 1 > st.nt_cap:
+                st.grow(2 * st.nt_cap)
+            K.sd1_encode(st, self.tail_k, self.tail_v)
+            self.n_stored += self.tile
+            self.n_tail = 0
+            window.pos += 1
+            window.n = min(window.n + 1, window.cap)
+            return self.attend(q_rot, window, exclude_start, exclude_end, out=out), q_rot
+        if evict:
+            self.n_tail += 1
+        window.pos += 1
+        window.n = min(window.n + 1, window.cap)
+        st = self.store
+        t = self.tile
+        k_sel = max(1, self.top_k // t) if st.n_tiles else 0
+        ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, st.n_tiles)
+        if ex0 >= ex1:
+            ex0 = ex1 = 0
+        o, q_rot = K.sd1_decode_step_update(st, q_pre, k_pre, v, cos, sin, pos, k_sel, window.k, window.v, window.n,
+                                            slot, self.tail_k, self.tail_v, self.n_tail, evict, ex0, ex1,
+                                            out=None if out is None else out.view(1, *out.shape))
+        return (o[0] if out is None else out), q_rot
+
     def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None, out=None):
         """One layer's retrieval + attention for the current step, q (n_q, d)
         -> (n_q, d): exact softmax over the window buffer (if given) and the

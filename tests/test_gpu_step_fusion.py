@@ -88,3 +88,94 @@ def test_generator_fused_store_update_matches_step_by_step():
         a, b = r0.tail_k[0, :r0.n_tail].float(), r1.tail_k[0, :r1.n_tail].float()
         assert torch.all((a - b).abs() <= 2 * torch.finfo(torch.float16).eps * b.abs() + 1e-6)
         assert torch.equal(r0.tail_v[0, :r0.n_tail], r1.tail_v[0, :r1.n_tail])
+
+
+def _sd1_layer(g, nt, n_kv=8, cap=128, tile=64, kind="dct"):
+    from kvr_b200 import kernels as K
+    st = K.Sd1Store(1, n_kv, nt + 2, tile, kind, "cuda")
+    scale = torch.exp(torch.randn(n_kv, 128, device="cuda", generator=g))
+    k = torch.randn(1, nt * tile, n_kv, 128, device="cuda", generator=g) * scale
+    v = torch.randn(1, nt * tile, n_kv, 128, device="cuda", generator=g)
+    K.sd1_encode(st, k.to(torch.bfloat16), v.to(torch.bfloat16))
+    win_k = torch.randn(cap, n_kv, 128, device="cuda", generator=g).half()
+    win_v = torch.randn(cap, n_kv, 128, device="cuda", generator=g).half()
+    tail_k = torch.randn(1, tile, n_kv, 128, device="cuda", generator=g).half()
+    tail_v = torch.randn(1, tile, n_kv, 128, device="cuda", generator=g).half()
+    return st, win_k, win_v, tail_k, tail_v
+
+
+@pytest.mark.parametrize("dtype,full,tile,kind", [
+    (torch.bfloat16, True, 64, "dct"), (torch.bfloat16, False, 64, "dct"), (torch.float16, True, 64, "dct"),
+    (torch.float16, False, 64, "dct"), (torch.float32, True, 64, "dct"), (torch.float32, False, 64, "dct"),
+    (torch.bfloat16, True, 32, "hadamard"), (torch.bfloat16, True, 128, "dct")])
+def test_fused_step_update_matches_store_update_then_step(dtype, full, tile, kind):
+    """kvr_sd1_decode_step_update (one cluster launch) leaves the same window,
+    tail and rotated q as kvr_decode_store_update, and gives the same tile
+    selection and outputs as kvr_sd1_decode_step after it, bit for bit, over
+    three consecutive steps (with and without eviction)."""
+    from kvr_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(3)
+    cos, sin = inputs.rope_tables(4096, 128, 500000.0)
+    cos, sin = cos.cuda(), sin.cuda()
+    st, wk, wv, tk, tv = _sd1_layer(g, 40 * 64 // tile, tile=tile, kind=kind)
+    wk2, wv2, tk2, tv2 = wk.clone(), wv.clone(), tk.clone(), tv.clone()
+    cap, n_kv, k_sel = wk.shape[0], 8, 16 * 64 // tile
+    n_win = cap if full else 100
+    n_tail = 5
+    for step in range(3):
+        pos = 3000 + step
+        q = (torch.randn(32, 128, device="cuda", generator=g) * 2).to(dtype)
+        k = (torch.randn(n_kv, 128, device="cuda", generator=g) * 2).to(dtype)
+        v = torch.randn(n_kv, 128, device="cuda", generator=g).to(dtype)
+        if full:
+            slot, evict = (17 + step) % cap, True
+            n_tail += 1
+        else:
+            slot, evict = n_win, False
+            n_win += 1
+        q_rot = K.decode_store_update(q, k, v, cos, sin, pos, wk, wv, slot, tk[0] if evict else None,
+                                      tv[0] if evict else None, n_tail - 1, True)
+        sel1 = torch.empty(1, n_kv, k_sel, dtype=torch.int32, device="cuda")
+        out1 = K.sd1_decode_step(st, q_rot, k_sel, wk.unsqueeze(0), wv.unsqueeze(0), n_win, tk, tv, n_tail,
+                                 sel_out=sel1)
+        sel2 = torch.empty_like(sel1)
+        out2, q_out = K.sd1_decode_step_update(st, q, k, v, cos, sin, pos, k_sel, wk2.unsqueeze(0), wv2.unsqueeze(0),
+                                               n_win, slot, tk2, tv2, n_tail, evict, sel_out=sel2)
+        torch.cuda.synchronize()
+        assert torch.equal(q_out, q_rot), step
+        assert torch.equal(wk2, wk) and torch.equal(wv2, wv), step
+        assert torch.equal(tk2[:, :n_tail], tk[:, :n_tail]) and torch.equal(tv2[:, :n_tail], tv[:, :n_tail]), step
+        assert torch.equal(sel2, sel1), step
+        assert torch.equal(out2, out1), step
+
+
+def test_fused_step_update_split_fallback():
+    """With the two-kernel step selected, the fused entry point runs the
+    store-update kernel and the split step: same stores and selection, outputs
+    within fp32 rounding of the cluster kernel's."""
+    from kvr_b200 import kernels as K
+    from kvr_b200 import _native as N
+    g = torch.Generator(device="cuda").manual_seed(4)
+    cos, sin = inputs.rope_tables(4096, 128, 500000.0)
+    cos, sin = cos.cuda(), sin.cuda()
+    st, wk, wv, tk, tv = _sd1_layer(g, 24)
+    wk2, wv2, tk2, tv2 = wk.clone(), wv.clone(), tk.clone(), tv.clone()
+    q = torch.randn(32, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(8, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(8, 128, device="cuda", generator=g).to(torch.bfloat16)
+    sel1 = torch.empty(1, 8, 16, dtype=torch.int32, device="cuda")
+    sel2 = torch.empty_like(sel1)
+    out1, q1 = K.sd1_decode_step_update(st, q, k, v, cos, sin, 1234, 16, wk.unsqueeze(0), wv.unsqueeze(0), 128, 9,
+                                        tk, tv, 3, True, sel_out=sel1)
+    lib = N.lib()
+    prev = lib.kvr_set_sd1_step_path(1)
+    try:
+        out2, q2 = K.sd1_decode_step_update(st, q, k, v, cos, sin, 1234, 16, wk2.unsqueeze(0), wv2.unsqueeze(0), 128,
+                                            9, tk2, tv2, 3, True, sel_out=sel2)
+        torch.cuda.synchronize()
+    finally:
+        lib.kvr_set_sd1_step_path(prev)
+    assert torch.equal(q1, q2) and torch.equal(sel1, sel2)
+    assert torch.equal(wk, wk2) and torch.equal(wv, wv2) and torch.equal(tk[:, :3], tk2[:, :3])
+    err = (out1.float() - out2.float()).abs().max() / out1.float().abs().max()
+    assert err < 1e-2, err  # bf16 outputs: one rounding step apart at most
