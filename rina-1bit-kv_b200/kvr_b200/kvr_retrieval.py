@@ -80,6 +80,7 @@ class RetrievalIndex:
         self.tail_v = None
         self.n_tail = 0
         self._sd1_call = None    # cached pointer arguments of attend()
+        self._sd1_upd_call = None  # cached pointer arguments of decode_step()
 
     # ------------------------------------------------------------ tables --
     def set_rotary_tables(self, cos, sin):
@@ -591,7 +592,8 @@ class RetrievalIndex:
         tokens, as for ``attend``).  One cluster launch; when the eviction
         fills the tail, the store update, the tile encode and the step run as
         separate launches so the new tile is in the store before the step, as
-        in the step-by-step path.  Returns (out (n_q, d) of q's dtype, RoPE(q))."""
+        in the step-by-step path.  Returns (out (n_q, d) of q's dtype, RoPE(q));
+        the RoPE(q) buffer belongs to the index and the next call overwrites it."""
         if self.codec != "sd1":
             raise NotImplementedError("decode_step is the sd1 codec's fused path")
         if self.store is None:
@@ -621,10 +623,41 @@ class RetrievalIndex:
         ex0, ex1 = exclude_start // t, min((exclude_end + t - 1) // t, st.n_tiles)
         if ex0 >= ex1:
             ex0 = ex1 = 0
-        o, q_rot = K.sd1_decode_step_update(st, q_pre, k_pre, v, cos, sin, pos, k_sel, window.k, window.v, window.n,
-                                            slot, self.tail_k, self.tail_v, self.n_tail, evict, ex0, ex1,
-                                            out=None if out is None else out.view(1, *out.shape))
-        return (o[0] if out is None else out), q_rot
+        for x in (q_pre, k_pre, v):
+            if not x.is_cuda or not x.is_contiguous() or x.dtype != q_pre.dtype:
+                raise ValueError("q, k and v must be contiguous CUDA tensors of one dtype")
+        N = K.N
+        n_q = q_pre.shape[0]
+        # pointer arguments of the tables, window, tail and store are cached
+        # (they change only when a buffer is reallocated): one ctypes call
+        key = (st.kbits.data_ptr(), st.nt_cap, id(window), window.k.data_ptr(), self.tail_k.data_ptr(),
+               cos.data_ptr(), sin.data_ptr(), q_pre.dtype, n_q)
+        c = self._sd1_upd_call
+        if c is None or c[0] != key:
+            cos_c, sin_c, rs = K._rope_args(cos.float(), sin.float())
+            c = self._sd1_upd_call = (
+                key, (cos_c.data_ptr(), sin_c.data_ptr(), rs),
+                (window.k.data_ptr(), window.v.data_ptr(), window.cap), (self.tail_k.data_ptr(), self.tail_v.data_ptr()),
+                (st.kbits.data_ptr(), st.kscale.data_ptr(), st.vbits.data_ptr(), st.vscale.data_ptr(), st.nt_cap),
+                torch.empty_like(q_pre), N.dtype_code(q_pre), N.TRANSFORMS[st.kind], (cos_c, sin_c))
+        _, tb, wk, tl, sp, q_rot, dt, kind, _ = c
+        if out is None:
+            res = None
+            out = torch.empty(n_q, self.d_head, dtype=q_pre.dtype, device=q_pre.device)
+        else:
+            if out.dtype != q_pre.dtype or not out.is_contiguous() or out.numel() != n_q * self.d_head:
+                raise ValueError("out must be a contiguous (n_q, d) tensor of q's dtype")
+            res = out
+        wkey = (1, n_q, self.n_kv, st.n_tiles, t, k_sel, window.n, self.n_tail)
+        need = K._STEP_WS.get(wkey)
+        if need is None:
+            need = K._STEP_WS[wkey] = N.call("kvr_sd1_workspace_bytes", *wkey)
+        ws = N.workspace("sd1_step", need, q_pre.device)
+        N.call("kvr_sd1_decode_step_update", q_pre.data_ptr(), k_pre.data_ptr(), v.data_ptr(), dt, n_q, self.n_kv,
+               tb[0], tb[1], tb[2], pos, q_rot.data_ptr(), wk[0], wk[1], wk[2], window.n, slot, tl[0], tl[1],
+               self.n_tail, int(evict), sp[0], sp[1], sp[2], sp[3], sp[4], st.n_tiles, t, kind, k_sel, ex0, ex1, 0.0,
+               out.data_ptr(), dt, None, ws.data_ptr(), ws.numel(), N.stream())
+        return (out if res is None else res), q_rot
 
     def attend(self, q_post_rope, window=None, exclude_start=0, exclude_end=0, out_dtype=None, out=None):
         """One layer's retrieval + attention for the current step, q (n_q, d)

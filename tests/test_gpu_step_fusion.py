@@ -179,3 +179,59 @@ def test_fused_step_update_split_fallback():
     assert torch.equal(wk, wk2) and torch.equal(wv, wv2) and torch.equal(tk[:, :3], tk2[:, :3])
     err = (out1.float() - out2.float()).abs().max() / out1.float().abs().max()
     assert err < 1e-2, err  # bf16 outputs: one rounding step apart at most
+
+
+def test_retrieval_index_decode_step_over_a_tile_period():
+    """RetrievalIndex.decode_step against the separate calls (store update
+    kernel, tail encode when full, RetrievalIndex.attend) on two copies of one
+    index: 70 steps with a full window, so one step fills the tail and encodes
+    it; outputs, rotated q, windows, tails and stores bit-identical."""
+    from kvr_b200 import RetrievalIndex, WindowBuffer
+    from kvr_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(11)
+    n_kv, n_q, tile, cap = 8, 32, 64, 128
+    cos, sin = inputs.rope_tables(4096, 128, 500000.0)
+    cos, sin = cos.cuda(), sin.cuda()
+    k0 = torch.randn(40 * tile + 7, n_kv, 128, device="cuda", generator=g) * 3
+    v0 = torch.randn(40 * tile + 7, n_kv, 128, device="cuda", generator=g)
+    wk0 = torch.randn(cap, n_kv, 128, device="cuda", generator=g).half()
+    wv0 = torch.randn(cap, n_kv, 128, device="cuda", generator=g).half()
+    pairs = []
+    for _ in range(2):
+        ri = RetrievalIndex(n_kv, 128, top_k=16 * tile, device="cuda", codec="sd1", tile=tile, transform="dct")
+        ri.set_rotary_tables(cos, sin)
+        ri.calibrate(k0, v0)
+        ri.batch_append(k0, v0)
+        wb = WindowBuffer(n_kv, 128, cap, "cuda")
+        wb.k.copy_(wk0)
+        wb.v.copy_(wv0)
+        wb.pos, wb.n = 5, cap
+        pairs.append((ri, wb))
+    (r1, w1), (r2, w2) = pairs
+    assert r1.n_tail == 7
+    for step in range(70):
+        pos = 3000 + step
+        q = torch.randn(n_q, 128, device="cuda", generator=g).to(torch.bfloat16)
+        k = torch.randn(n_kv, 128, device="cuda", generator=g).to(torch.bfloat16)
+        v = torch.randn(n_kv, 128, device="cuda", generator=g).to(torch.bfloat16)
+        # separate calls, as KVRHook.decode_store_update + RetrievalIndex.attend
+        slot = w1.pos % w1.cap
+        q_rot = K.decode_store_update(q, k, v, cos, sin, pos, w1.k, w1.v, slot, r1.tail_k[0], r1.tail_v[0],
+                                      r1.n_tail, True)
+        r1.n_tail += 1
+        if r1.n_tail == tile:
+            K.sd1_encode(r1.store, r1.tail_k, r1.tail_v)
+            r1.n_stored += tile
+            r1.n_tail = 0
+        w1.pos += 1
+        out1 = r1.attend(q_rot, w1)
+        out2, q2 = r2.decode_step(q, k, v, w2, pos, cos, sin)
+        torch.cuda.synchronize()
+        assert torch.equal(q2, q_rot), step
+        assert torch.equal(out2, out1), step
+        assert (r1.n_stored, r1.n_tail, w1.pos, w1.n) == (r2.n_stored, r2.n_tail, w2.pos, w2.n), step
+    assert r2.store.n_tiles == r1.store.n_tiles == 41
+    assert torch.equal(w1.k, w2.k) and torch.equal(w1.v, w2.v)
+    assert torch.equal(r1.tail_k[:, :r1.n_tail], r2.tail_k[:, :r2.n_tail])
+    for name in ("kbits", "kscale", "vbits", "vscale"):
+        assert torch.equal(getattr(r1.store, name)[:, :, :41], getattr(r2.store, name)[:, :, :41]), name
