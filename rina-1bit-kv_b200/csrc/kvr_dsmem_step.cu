@@ -233,13 +233,20 @@ DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, 
   float mx = -INFINITY;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int j = lane + 32 * r;
+    const int rows = n - 32 * r;  // rows of this pass (warp-uniform)
     sj[r] = -INFINITY;
-    if (j < n) {
-      const uint4 *kr = reinterpret_cast<const uint4 *>(ex + j * kDsExStride);
+    if (rows <= 0) continue;
+    // a full pass gives each lane a row; a short one (fewer than 16 rows,
+    // e.g. the few pending-tail rows past 32) splits each row's 16 chunks
+    // over a group of lanes and reduces them, so it costs a fraction of a pass
+    const int lpr = rows >= 16 ? 1 : rows > 8 ? 2 : rows > 4 ? 4 : rows > 2 ? 8 : 16;
+    const int row = lane / lpr, part = lane - row * lpr, nch = 16 / lpr;
+    float v = -INFINITY;
+    if (row < rows) {
+      const uint4 *kr = reinterpret_cast<const uint4 *>(ex + (32 * r + row) * kDsExStride);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-      for (int c = 0; c < 16; ++c) {
+      for (int c = part * nch; c < (part + 1) * nch; ++c) {
         const uint4 w = kr[c];
         const float4 qa = q4[2 * c], qb4 = q4[2 * c + 1];
         const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
@@ -251,9 +258,15 @@ DS_FN void exact_rows(const unsigned char *ex, int epc, int n, const float *qn, 
         acc[0] = fmaf(qb4.x, f2.x, acc[0]); acc[1] = fmaf(qb4.y, f2.y, acc[1]);
         acc[2] = fmaf(qb4.z, f3.x, acc[2]); acc[3] = fmaf(qb4.w, f3.y, acc[3]);
       }
-      sj[r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      mx = fmaxf(mx, sj[r]);
+      v = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
+    if (lpr > 1) {
+      for (int o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      v = __shfl_sync(0xffffffffu, v, (lane * lpr) & 31);  // row `lane`'s sum, from its group
+      if (lane >= rows) v = -INFINITY;
+    }
+    sj[r] = v;
+    mx = fmaxf(mx, v);
   }
   mx = warp_max(mx);
   o[0] = o[1] = o[2] = o[3] = 0.0f;
